@@ -1,0 +1,163 @@
+/*
+ * ltx25_cuda.h -- C ABI of the B200 (sm_100a) implementation of LTX-2.5's
+ * quantized-linear hot path and the joint audio-video DiT block.
+ *
+ * It replaces, for this path, the reference plugin's ltx25-metal-ops,
+ * ltx25-block-metal and ltx25-kernels.metal (tgo-app-dev/vpipe-ltx-2.5).
+ * Every entry point names the reference interface it stands in for.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Activations, outputs and biases are
+ *     DEVICE pointers to bf16 (uint16 bit patterns), caller-owned, row-major.
+ *     `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *   - Every call returns LTX_OK (0) or a negative LTX_E_* code; the message
+ *     for the last failure on a context is ltx_ctx_last_error().
+ *   - Calls on one context are serialized by the caller (the reference's
+ *     one-encoder-per-stack discipline, src/ltx25-block-metal.h:162-163).
+ *   - Nothing is computed on the CPU: without a usable sm_100a device the
+ *     context cannot be created and every op fails with LTX_E_CUDA.
+ */
+#ifndef LTX25_CUDA_H
+#define LTX25_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LTX25_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define LTX_API __attribute__((visibility("default")))
+#else
+#define LTX_API
+#endif
+
+enum {
+  LTX_OK = 0,
+  LTX_E_NULL = -1,        /* a required pointer was NULL */
+  LTX_E_SHAPE = -2,       /* sizes disagree with the weight or the layout */
+  LTX_E_UNSUPPORTED = -3, /* a pack this build does not run (not w8g64) */
+  LTX_E_CUDA = -4,        /* a CUDA runtime call or launch failed */
+  LTX_E_OOM = -5,         /* device allocation failed */
+  LTX_E_KERNEL = -6,      /* a kernel gave up on a bounded wait */
+  LTX_E_STATE = -7,       /* call out of order (e.g. block not loaded) */
+  LTX_E_ALIGN = -8        /* a pointer is not 16-byte aligned */
+};
+
+/* Data types of a pack's scales / zero-points as they arrive. */
+enum { LTX_SB_F16 = 0, LTX_SB_BF16 = 1, LTX_SB_F32 = 2 };
+
+/* qlinear routes for a quantized weight (the reference's
+ * VPIPE_LTX25_NO_DEQUANT_MMA A/B, src/ltx25-metal-ops.cc:532-569). */
+enum {
+  LTX_ROUTE_FUSED = 0,         /* w8g64 dequant-fused tcgen05 GEMM */
+  LTX_ROUTE_DEQUANT_ONCE = 1   /* expand to bf16 scratch, dense GEMM */
+};
+
+/* Fused epilogues of ltx_qlinear_ex. */
+enum {
+  LTX_EPI_STORE = 0,     /* y = x W^T + b */
+  LTX_EPI_GELU = 1,      /* y = gelu_tanh(x W^T + b) */
+  LTX_EPI_GATED_RES = 2  /* y += gate[n] * (x W^T + b), y is the residual */
+};
+
+typedef struct ltx_ctx ltx_ctx;
+typedef struct ltx_qweight ltx_qweight;
+
+/* ---- context ----------------------------------------------------------
+ * Replaces MetalOps::init (src/ltx25-metal-ops.h:68-70): selects the
+ * device, checks it is sm_100, and creates the scratch arena. */
+LTX_API int ltx_ctx_create(int device, ltx_ctx** out);
+LTX_API void ltx_ctx_destroy(ltx_ctx* ctx);
+LTX_API const char* ltx_ctx_last_error(const ltx_ctx* ctx);
+LTX_API int ltx_abi_version(void);
+
+/* Size the shared scratch once for the largest call that will follow, so
+ * the hot calls allocate nothing (BlockScratch / reserve,
+ * src/ltx25-block-metal.h:140-240 and 296-299).  A later call that needs
+ * more grows the arena outside any graph capture. */
+LTX_API int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k);
+
+/* Reads and clears the device-side error word that a kernel sets when one
+ * of its bounded waits gave up.  LTX_OK when clean, LTX_E_KERNEL when not
+ * (the reference's wait_ok(), src/ltx25-dit.cc:1920-1931). */
+LTX_API int ltx_ctx_check(ltx_ctx* ctx, void* stream);
+
+/* ---- weights ----------------------------------------------------------
+ * Replaces QWeight + bind_qlinear / need_q_ (src/ltx25-metal-ops.h:45-57,
+ * src/ltx25-dit-weights.h:170-175, src/ltx25-dit-weights.cc:352-403).
+ *
+ * codes:   u32 words holding unsigned codes LOW BITS FIRST, [N][K*bits/32]
+ * scales:  one per (row, group), [N][K/group], dtype sb_dtype
+ * biases:  the group ZERO-POINT (the group minimum), same layout
+ * Uploaded once into HBM (scales/zero-points converted to bf16 with RNE,
+ * as get_as_bf16_ does, src/ltx25-dit-weights.cc:230-277).
+ * `on_device` != 0 means the three pointers are already device memory.
+ * Only bits == 8, group == 64 (the w8g64 pack) is accepted; anything else
+ * returns LTX_E_UNSUPPORTED.  N must be a multiple of 8, K of 64. */
+LTX_API int ltx_qweight_upload(ltx_ctx* ctx, const uint32_t* codes,
+                       const void* scales, const void* biases, int sb_dtype,
+                       int N, int K, int bits, int group, int on_device,
+                       ltx_qweight** out);
+
+/* A dense bf16 weight [N][K] (gate logits and any tensor a pack leaves
+ * dense; QWeight with quantized == false). */
+LTX_API int ltx_dweight_upload(ltx_ctx* ctx, const uint16_t* w_bf16, int N, int K,
+                       int on_device, ltx_qweight** out);
+
+LTX_API void ltx_qweight_free(ltx_qweight* w);
+
+LTX_API int ltx_qweight_info(const ltx_qweight* w, int* N, int* K, int* bits,
+                     int* group, int* quantized);
+
+/* ---- the quantized linear --------------------------------------------
+ * Replaces MetalOps::linear(enc, x, QWeight, bias*, y, M, K, N)
+ * (src/ltx25-metal-ops.h:100-105, src/ltx25-metal-ops.cc:532-569):
+ * y[M][N] = x[M][K] . W[N][K]^T (+ bias[N]).  W is PyTorch's [out][in].
+ * bias may be NULL.  x, y, bias: device bf16.  Unlike the reference the
+ * bias is fused into the GEMM epilogue instead of a second pass. */
+LTX_API int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
+                const void* bias, void* y, int M, int K, int N, void* stream);
+
+/* The same with explicit row strides and a fused epilogue (LTX_EPI_*).
+ * `gate` is [N] bf16 for LTX_EPI_GATED_RES (y += gate * (xW^T + b)), the
+ * reference's linear + gated_residual pair (src/ltx25-metal-ops.cc:
+ * 1047-1059) and linear + gelu (src/ltx25-metal-ops.cc:1062-1070). */
+LTX_API int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
+                   int ldx, const void* bias, void* y, int ldy, int M, int K,
+                   int N, int epilogue, const void* gate, void* stream);
+
+/* Route for quantized weights (LTX_ROUTE_*).  Default FUSED. */
+LTX_API int ltx_set_route(ltx_ctx* ctx, int route);
+
+/* ---- acceleration tiers ------------------------------------------------
+ * Replaces MetalOps::set_i8_gemm / set_sage (src/ltx25-metal-ops.h:151,
+ * 265) fed from the accel bag keys i8_gemm, sage_attn, sage_dense_layers
+ * (src/ltx25-generator.cc:297-375). */
+LTX_API int ltx_set_tiers(ltx_ctx* ctx, int i8_gemm, int sage_attn,
+                  int sage_dense_layers);
+
+/* Will ltx_qlinear take the int8 tier for this shape?  1 / 0.
+ * Replaces MetalOps::i8_takes (src/ltx25-metal-ops.cc:761-768). */
+LTX_API int ltx_i8_takes(const ltx_ctx* ctx, int M, int K, int N);
+
+/* ---- pieces exposed for parity tests -----------------------------------
+ * The dequantized weight exactly as the GEMMs see it: out[N][K] bf16 =
+ * s*q + z rounded once (the M5 dequant-once expansion,
+ * src/ltx25-metal-ops.cc:468-502). */
+LTX_API int ltx_dequant(ltx_ctx* ctx, const ltx_qweight* w, void* out, void* stream);
+
+/* Symmetric int8 quantization per (row, group): scale = absmax/127,
+ * q = rint(x/scale) in [-127, 127].  group == K is per-token.  q is
+ * [rows][K] int8, scale [rows][K/group] f32, both device. */
+LTX_API int ltx_quant_rows_i8(ltx_ctx* ctx, const void* x, int rows, int K,
+                      int group, void* q, void* scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTX25_CUDA_H */

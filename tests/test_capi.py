@@ -1,0 +1,54 @@
+"""The C-ABI library: it is built, it loads, and it exports exactly what
+include/ltx25_cuda.h declares (CPU only; no compute calls)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "ltx25_cuda.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"LTX_API\s+[\w\s\*]+?\b(ltx_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_boundary():
+    syms = declared_symbols()
+    for must in ("ltx_ctx_create", "ltx_qweight_upload", "ltx_qlinear",
+                 "ltx_qlinear_ex", "ltx_set_tiers", "ltx_i8_takes",
+                 "ltx_ctx_check"):
+        assert must in syms
+
+
+def test_library_loads_and_exports_every_symbol():
+    import ltx25_b200 as L
+    lib = L.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.ltx_abi_version() == 1
+
+
+def test_binding_covers_the_header():
+    import ltx25_b200 as L
+    assert sorted(L.SIGNATURES) == declared_symbols()
+
+
+def test_null_arguments_rejected_without_a_device():
+    import ltx25_b200 as L
+    lib = L.load()
+    assert lib.ltx_ctx_create(0, None) == -1                 # LTX_E_NULL
+    assert lib.ltx_qlinear(None, None, None, None, None, 1, 64, 8, None) == -1
+    assert lib.ltx_set_tiers(None, 1, 0, 0) == -1
+    assert lib.ltx_i8_takes(None, 8160, 4096, 4096) == 0
+
+
+def test_context_creation_fails_loudly_without_an_sm100_device():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the gpu tests")
+    import ltx25_b200 as L
+    with pytest.raises(L.LtxError):
+        L.Context(0)

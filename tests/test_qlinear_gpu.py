@@ -1,0 +1,220 @@
+"""The w8g64 quantized linear on the GPU, against the CPU oracle.
+
+Mirrors tests/ltx25-qlinear-test.cc of the reference: pack by the restated
+(reference-pinned) packer, run ltx_qlinear, compare with a dense f64 GEMM
+over the dequantized weight; a negative control (one flipped code must move
+the result); the bias; plus the shapes BASELINE configs 1-2 dispatch, the
+split-K small-M path, both routes and the fused epilogues.
+"""
+import numpy as np
+import pytest
+
+from oracle import block_np, lib
+
+pytestmark = pytest.mark.gpu
+
+# Bar for a bf16-output GEMM vs an f64 reference over the same bf16
+# operands: the reference test's 3e-3 (qlinear-test.cc:188-197).
+TOL = 3e-3
+
+
+def make(M, N, K, seed, wstd=0.05, xstd=1.0):
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((M, K)) * xstd).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * wstd).astype(np.float32)
+    codes, scales, biases, deq = lib.pack_affine(w, 8, 64)
+    xb = lib.f32_to_bf16(x)
+    return xb, codes, scales, biases, deq
+
+
+def to_dev(a_u16):
+    import torch
+    return torch.from_numpy(a_u16.view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def from_dev(t):
+    return lib.bf16_to_f32(t.view(__import__("torch").int16).cpu().numpy().view(np.uint16))
+
+
+def oracle_y(xb, codes, scales, biases, K, bias=None):
+    wq = lib.bf16_to_f32(lib.dequant_bf16(codes, scales, biases, K))
+    return lib.linear_f64(lib.bf16_to_f32(xb), wq, bias, threads=8)
+
+
+CASES = [
+    # the reference test's w8g64 shapes (qlinear-test.cc:188-194)
+    (16, 128, 256), (192, 128, 256), (192, 256, 512),
+    # ragged tokens / features, tiny M
+    (1, 128, 64), (130, 200, 256), (300, 384, 1024), (8, 136, 128),
+    # audio stream (split-K), text K/V rows, a2v/v2a cross projections
+    (126, 2048, 2048), (126, 8192, 2048), (126, 2048, 8192), (256, 4096, 4096),
+    (126, 2048, 4096),
+    # BASELINE config 1 (scaled on N to keep the f64 oracle quick)
+    (1024, 512, 4096),
+]
+
+
+@pytest.mark.parametrize("M,N,K", CASES)
+def test_qlinear_matches_dequant_then_dense(ctx, M, N, K):
+    import ltx25_b200 as L
+    xb, codes, scales, biases, _ = make(M, N, K, seed=M * 7 + N + K)
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    y = from_dev(L.qlinear(ctx, w, to_dev(xb)))
+    ctx.check()
+    want = oracle_y(xb, codes, scales, biases, K)
+    r = lib.rel_l2(y, want)
+    assert r < TOL, f"rel-L2 {r:.3e}"
+    assert np.abs(y).sum() > 0
+
+
+def test_dequant_is_bit_exact(ctx, golden):
+    import ltx25_b200 as L
+    g = golden("pack.npz")
+    for name in ("case0", "case1", "case6", "edge"):
+        codes, s, b = g[f"{name}__codes"], g[f"{name}__scales"], g[f"{name}__biases"]
+        N, K = g[f"{name}__w"].shape
+        w = L.QWeight.upload(ctx, codes, s, b, N, K)
+        got = L.dequant(ctx, w).view(__import__("torch").int16).cpu().numpy().view(np.uint16)
+        assert np.array_equal(got, lib.dequant_bf16(codes, s, b, K)), name
+
+
+def test_negative_control_one_code_moves_the_result(ctx):
+    import ltx25_b200 as L
+    M, N, K = 64, 128, 256
+    xb, codes, scales, biases, _ = make(M, N, K, seed=1)
+    bad = codes.copy()
+    bad[0, 0] ^= np.uint32(0xFF)
+    wa = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    wb = L.QWeight.upload(ctx, bad, scales, biases, N, K)
+    xd = to_dev(xb)
+    ya, yb = from_dev(L.qlinear(ctx, wa, xd)), from_dev(L.qlinear(ctx, wb, xd))
+    assert lib.rel_l2(yb, ya) > 0.0
+    # only output feature 0 may change
+    assert np.array_equal(ya[:, 1:], yb[:, 1:])
+
+
+@pytest.mark.parametrize("M", [64, 126, 2048])
+def test_bias_is_fused(ctx, M):
+    import ltx25_b200 as L
+    N, K = 256, 512
+    xb, codes, scales, biases, _ = make(M, N, K, seed=2)
+    rng = np.random.default_rng(3)
+    bias = (rng.standard_normal(N) * 0.2).astype(np.float32)
+    bb = lib.f32_to_bf16(bias)
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    y = from_dev(L.qlinear(ctx, w, to_dev(xb), bias=to_dev(bb)))
+    want = oracle_y(xb, codes, scales, biases, K, lib.bf16_to_f32(bb))
+    assert lib.rel_l2(y, want) < TOL
+    nob = oracle_y(xb, codes, scales, biases, K)
+    assert lib.rel_l2(want, nob) > 10 * TOL   # the bias is visible
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 384, 1024), (126, 2048, 2048)])
+def test_routes_agree(ctx, M, N, K):
+    import ltx25_b200 as L
+    xb, codes, scales, biases, _ = make(M, N, K, seed=4)
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    xd = to_dev(xb)
+    ctx.set_route(L.ROUTE_DEQUANT_ONCE)
+    try:
+        y1 = from_dev(L.qlinear(ctx, w, xd))
+    finally:
+        ctx.set_route(L.ROUTE_FUSED)
+    y0 = from_dev(L.qlinear(ctx, w, xd))
+    want = oracle_y(xb, codes, scales, biases, K)
+    assert lib.rel_l2(y0, want) < TOL and lib.rel_l2(y1, want) < TOL
+    assert lib.rel_l2(y0, y1) < 1e-3
+
+
+def test_dense_weight_path(ctx):
+    import ltx25_b200 as L
+    rng = np.random.default_rng(8)
+    M, N, K = 300, 32 + 8, 256
+    x = lib.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    wd = lib.f32_to_bf16((rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+    w = L.QWeight.upload_dense(ctx, wd, N, K)
+    y = from_dev(L.qlinear(ctx, w, to_dev(x)))
+    want = lib.linear_f64(lib.bf16_to_f32(x), lib.bf16_to_f32(wd))
+    assert lib.rel_l2(y, want) < TOL
+
+
+@pytest.mark.parametrize("M", [126, 600])
+def test_gelu_epilogue(ctx, M):
+    import ltx25_b200 as L
+    N, K = 512, 256
+    xb, codes, scales, biases, _ = make(M, N, K, seed=5, wstd=0.1)
+    bias = lib.f32_to_bf16((np.random.default_rng(1).standard_normal(N) * 0.1).astype(np.float32))
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    y = from_dev(L.qlinear(ctx, w, to_dev(xb), bias=to_dev(bias),
+                           epilogue=L.EPI_GELU))
+    pre = oracle_y(xb, codes, scales, biases, K, lib.bf16_to_f32(bias))
+    want = block_np.gelu_tanh(pre)
+    assert lib.rel_l2(y, want) < TOL
+
+
+@pytest.mark.parametrize("M", [126, 600])
+def test_gated_residual_epilogue(ctx, M):
+    import ltx25_b200 as L
+    N, K = 256, 512
+    xb, codes, scales, biases, _ = make(M, N, K, seed=6)
+    rng = np.random.default_rng(2)
+    h = lib.f32_to_bf16(rng.standard_normal((M, N)).astype(np.float32))
+    gate = lib.f32_to_bf16((rng.standard_normal(N) * 0.5).astype(np.float32))
+    bias = lib.f32_to_bf16((rng.standard_normal(N) * 0.1).astype(np.float32))
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    hd = to_dev(h)
+    L.qlinear(ctx, w, to_dev(xb), bias=to_dev(bias), out=hd,
+              epilogue=L.EPI_GATED_RES, gate=to_dev(gate))
+    y = from_dev(hd)
+    sub = oracle_y(xb, codes, scales, biases, K, lib.bf16_to_f32(bias))
+    want = lib.bf16_to_f32(h) + sub * lib.bf16_to_f32(gate)[None, :]
+    assert lib.rel_l2(y, want) < TOL
+
+
+def test_repeat_calls_are_deterministic(ctx):
+    """Split-K reduces in a fixed order: bitwise identical across calls."""
+    import ltx25_b200 as L
+    M, N, K = 126, 2048, 4096
+    xb, codes, scales, biases, _ = make(M, N, K, seed=9)
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    xd = to_dev(xb)
+    a = L.qlinear(ctx, w, xd).clone()
+    for _ in range(3):
+        assert bool((L.qlinear(ctx, w, xd).view(__import__("torch").int16) ==
+                     a.view(__import__("torch").int16)).all())
+    ctx.check()
+
+
+def test_shape_and_pack_errors(ctx):
+    import ltx25_b200 as L
+    xb, codes, scales, biases, _ = make(8, 128, 256, seed=10)
+    with pytest.raises(L.LtxError) as e:
+        L.QWeight.upload(ctx, codes, scales, biases, 128, 256, bits=4)
+    assert e.value.code == -3
+    with pytest.raises(L.LtxError) as e:
+        L.QWeight.upload(ctx, codes, scales, biases, 128, 250)
+    assert e.value.code == -2
+    w = L.QWeight.upload(ctx, codes, scales, biases, 128, 256)
+    import torch
+    x = torch.zeros((8, 512), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(L.LtxError) as e:
+        out = torch.empty((8, 128), dtype=torch.bfloat16, device="cuda")
+        rc = ctx.lib.ltx_qlinear(ctx.h, w.h, L._ptr(x), None, L._ptr(out), 8,
+                                 512, 128, None)
+        ctx._ok(rc, "qlinear")
+    assert e.value.code == -2
+
+
+def test_f16_scales_are_converted_rne(ctx):
+    """A checkpoint's F16 scales/zero-points load through the RNE conversion
+    of get_as_bf16_ (src/ltx25-dit-weights.cc:230-277)."""
+    import ltx25_b200 as L
+    N, K = 64, 256
+    _, codes, scales, biases, _ = make(4, N, K, seed=11)
+    s16 = lib.bf16_to_f32(scales).astype(np.float16)
+    b16 = lib.bf16_to_f32(biases).astype(np.float16)
+    w = L.QWeight.upload(ctx, codes, s16, b16, N, K, sb_dtype=L.SB_F16)
+    got = L.dequant(ctx, w).view(__import__("torch").int16).cpu().numpy().view(np.uint16)
+    want = lib.dequant_bf16(codes, lib.f32_to_bf16(s16.astype(np.float32)),
+                            lib.f32_to_bf16(b16.astype(np.float32)), K)
+    assert np.array_equal(got, want)

@@ -1,0 +1,94 @@
+// gemm_tc.cuh -- the tcgen05 GEMM behind every projection of the LTX-2.5
+// block:  y[M][N] = x[M][K] . W[N][K]^T (+ bias) with a fused epilogue.
+//
+// One persistent kernel per (mode, token-tile, epilogue):
+//
+//   MODE_W8G64  W is the group-affine u8 pack (4 codes per u32 word, low
+//               bits first; one bf16 scale and zero-point per 64 K).  The
+//               codes are TMA-staged into shared memory and DEQUANTIZED BY
+//               FOUR WARPS STRAIGHT INTO TENSOR MEMORY, where tcgen05.mma
+//               reads them as its A operand.  The dequantized weight never
+//               touches shared memory, so the only smem operand stream is the
+//               activation tile.
+//   MODE_BF16   W is dense bf16 (the dequant-once arm, the gate logits).
+//   MODE_I8     x and W are int8 (the i8_gemm tier), s32 accumulate,
+//               per-token x scale and per-channel W scale in the epilogue.
+//
+// The MMA is issued TRANSPOSED: its M dimension (128 lanes of TMEM) is the
+// weight's output-feature tile and its N dimension is the TOKEN tile (TN).
+// Small token counts (the 126-token audio stream) therefore cost a 128-wide
+// MMA instead of padding 126 rows up to a 128-row M tile, and the epilogue
+// thread that owns TMEM lane n owns output feature n for every token.
+//
+// Warp roles (320 threads):
+//   warp 0     TMA producer (one elected lane)
+//   warp 1     TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5  dequant (MODE_W8G64 only): TMEM lane quarter warp%4
+//   warps 6-9  epilogue: TMEM -> registers -> bias/act/residual -> global
+//
+// K is split across CTAs (`splits` > 1) for the small-M, bandwidth-bound
+// shapes; partial tiles are reduced in L2 by the last CTA to finish each
+// tile (a counter per tile, no spin-waits), in a fixed order, so results
+// are deterministic.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace ltx {
+
+enum GemmMode : int { MODE_W8G64 = 0, MODE_BF16 = 1, MODE_I8 = 2 };
+enum EpiMode : int { EPI_STORE = 0, EPI_GELU = 1, EPI_GATED_RES = 2 };
+
+// Error codes written into GemmParams::err by a kernel that gave up.
+enum KernelErr : int {
+  KERR_NONE = 0,
+  KERR_WAIT_PRODUCER = 1,
+  KERR_WAIT_MMA = 2,
+  KERR_WAIT_DEQUANT = 3,
+  KERR_WAIT_EPILOGUE = 4,
+  KERR_DRAIN = 5,
+};
+
+struct GemmParams {
+  int M, N, K;             // tokens, output features, input features
+  int m_tiles, n_tiles;    // ceil(M/TN), ceil(N/128)
+  int splits;              // K splits (1 = no split)
+  int kblocks;             // K / bytes-per-stage
+  int num_tiles;           // m_tiles * n_tiles * splits
+  int ldy;                 // row stride of y, elements
+  const __nv_bfloat16* bias;   // [N] or null
+  const __nv_bfloat16* gate;   // [N], EPI_GATED_RES only
+  __nv_bfloat16* y;            // [M][ldy]
+  float* ws;                   // [splits][m_tiles*TN][N] partials
+  int* counters;               // [m_tiles*n_tiles], zero between calls
+  const float* sx;             // MODE_I8: [M] token scales
+  const float* sw;             // MODE_I8: [N] channel scales
+  int* err;                    // device error word (0 = ok)
+};
+
+template <int MODE, int TN>
+struct GemmCfg {
+  static constexpr int kBM = 128;                       // weight rows / tile
+  static constexpr int kXStage = TN * 128;               // 128 B of K per row
+  static constexpr int kWStage = MODE == MODE_W8G64 ? kBM * 64 : kBM * 128;
+  static constexpr int kSZStage = MODE == MODE_W8G64 ? kBM * 4 : 0;
+  static constexpr int kStageBytes = kXStage + kWStage + kSZStage;
+  static constexpr int kStages =
+      (220 * 1024) / kStageBytes > 8 ? 8 : (220 * 1024) / kStageBytes;
+  static constexpr int kNAcc =
+      MODE == MODE_W8G64 ? (2 * TN + 4 * 32 <= 512 ? 2 : 1) : 2;
+  static constexpr int kASlotsRaw = (512 - kNAcc * TN) / 32;
+  static constexpr int kASlots =
+      MODE == MODE_W8G64 ? (kASlotsRaw > 8 ? 8 : kASlotsRaw) : 0;
+  static constexpr int kACol0 = kNAcc * TN;              // first A column
+  static constexpr int kKPerStage = MODE == MODE_I8 ? 128 : 64;  // elements
+  static constexpr int kThreads = 320;
+  static constexpr int kNumBars = 2 * kStages + 2 * (kASlots > 0 ? kASlots : 1) + 2 * 2 + 1;
+  static constexpr int kSmemBytes =
+      1024 + kStages * kStageBytes + kNumBars * 8 + 64;
+  static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "MMA N");
+  static_assert(kNAcc * TN + kASlots * 32 <= 512, "TMEM budget");
+  static_assert(MODE != MODE_W8G64 || kASlots >= 2, "A pipeline depth");
+};
+
+}  // namespace ltx

@@ -1,0 +1,410 @@
+// ltx25-cuda-ops.cc -- CudaOps: routing, tile planning and the scratch
+// arena around the tcgen05 GEMM (see ltx25-cuda-ops.h).
+#include "ltx25-cuda-ops.h"
+
+#include <algorithm>
+#include <cstring>
+
+#include "../csrc/kernels.h"
+
+namespace ltx25 {
+
+namespace {
+
+bool cuda_ok(cudaError_t e, const char* what, std::string* err)
+{
+  if (e == cudaSuccess) return true;
+  if (err) *err = std::string(what) + ": " + cudaGetErrorString(e);
+  return false;
+}
+
+bool aligned(const void* p, size_t a)
+{
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+struct Plan {
+  int tn = 256;
+  int splits = 1;
+  int m_tiles = 1, n_tiles = 1, kblocks = 1;
+};
+
+// Token tile and K split for one GEMM.  Large token counts take the
+// 256-token tile (the widest MMA N, least dequant per FLOP); the audio and
+// text shapes (M <= 128 / small tile counts) split K until the grid covers
+// the SMs, because those shapes are bound by reading the weight, not by
+// the tensor pipe.
+Plan plan_gemm(int mode, int M, int N, int K, int sms)
+{
+  Plan p;
+  const int kpb = mode == ltx::MODE_I8 ? 128 : 64;
+  p.kblocks = K / kpb;
+  p.n_tiles = (N + 127) / 128;
+  p.tn = M <= 128 ? 128 : 256;
+  p.m_tiles = (M + p.tn - 1) / p.tn;
+  const int tiles = p.m_tiles * p.n_tiles;
+  p.splits = 1;
+  if (tiles * 2 <= sms && p.kblocks >= 4) {
+    p.splits = std::min(std::min(sms / tiles, p.kblocks / 2), 16);
+    if (p.splits < 1) p.splits = 1;
+  }
+  return p;
+}
+
+}  // namespace
+
+CudaOps::~CudaOps()
+{
+  if (_dev < 0) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(_dev);
+  cudaFree(_ws);
+  cudaFree(_counters);
+  cudaFree(_xq);
+  cudaFree(_sx);
+  cudaFree(_deq);
+  cudaFree(_err_word);
+  cudaSetDevice(prev);
+}
+
+bool CudaOps::init(int device, std::string* err)
+{
+  int n = 0;
+  if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount", err)) return false;
+  if (device < 0 || device >= n) {
+    if (err) *err = "no CUDA device " + std::to_string(device);
+    return false;
+  }
+  cudaDeviceProp prop;
+  if (!cuda_ok(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties", err))
+    return false;
+  if (prop.major != 10 || prop.minor != 0) {
+    if (err)
+      *err = std::string("device ") + prop.name + " is sm_" +
+             std::to_string(prop.major) + std::to_string(prop.minor) +
+             "; this library is built for sm_100a (B200) only";
+    return false;
+  }
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice", err)) return false;
+  _dev = device;
+  _sms = prop.multiProcessorCount;
+  if (!cuda_ok(cudaMalloc(&_err_word, sizeof(int)), "cudaMalloc(err)", err))
+    return false;
+  return cuda_ok(cudaMemset(_err_word, 0, sizeof(int)), "cudaMemset", err);
+}
+
+bool CudaOps::ensure_(size_t ws_bytes, size_t i8_bytes, size_t deq_bytes,
+                      std::string* err)
+{
+  const size_t n_counters = 64 * 1024;
+  if (_counters == nullptr) {
+    if (!cuda_ok(cudaMalloc(&_counters, n_counters * sizeof(int)), "cudaMalloc(counters)", err))
+      return false;
+    if (!cuda_ok(cudaMemset(_counters, 0, n_counters * sizeof(int)), "cudaMemset", err))
+      return false;
+    _n_counters = n_counters;
+  }
+  if (ws_bytes > _ws_bytes) {
+    cudaFree(_ws);
+    _ws = nullptr;
+    _ws_bytes = 0;
+    if (!cuda_ok(cudaMalloc(&_ws, ws_bytes), "cudaMalloc(split-K scratch)", err))
+      return false;
+    _ws_bytes = ws_bytes;
+  }
+  if (i8_bytes > _xq_bytes) {
+    cudaFree(_xq);
+    cudaFree(_sx);
+    _xq = nullptr;
+    _sx = nullptr;
+    _xq_bytes = 0;
+    if (!cuda_ok(cudaMalloc(&_xq, i8_bytes), "cudaMalloc(int8 activations)", err))
+      return false;
+    if (!cuda_ok(cudaMalloc(&_sx, i8_bytes / 64 * sizeof(float) + 1024), "cudaMalloc(int8 scales)", err))
+      return false;
+    _xq_bytes = i8_bytes;
+  }
+  if (deq_bytes > _deq_bytes) {
+    cudaFree(_deq);
+    _deq = nullptr;
+    _deq_bytes = 0;
+    if (!cuda_ok(cudaMalloc(&_deq, deq_bytes), "cudaMalloc(dequant scratch)", err))
+      return false;
+    _deq_bytes = deq_bytes;
+  }
+  return true;
+}
+
+bool CudaOps::reserve(int max_tokens, int max_n, int max_k, std::string* err)
+{
+  if (max_tokens <= 0 || max_n <= 0 || max_k <= 0) {
+    if (err) *err = "reserve: sizes must be positive";
+    return false;
+  }
+  // Split-K only runs on small tile counts; bound it by the planner.
+  size_t ws = 0;
+  for (int mode : {(int)ltx::MODE_W8G64, (int)ltx::MODE_I8}) {
+    for (int m : {std::min(max_tokens, 128), std::min(max_tokens, 256), max_tokens}) {
+      const Plan p = plan_gemm(mode, m, max_n, max_k, _sms);
+      if (p.splits > 1)
+        ws = std::max(ws, (size_t)p.splits * p.m_tiles * p.tn * max_n * sizeof(float));
+    }
+  }
+  return ensure_(ws, 0, 0, err);
+}
+
+bool CudaOps::i8_takes(int M, int K, int N) const
+{
+  // The reference's gates (src/ltx25-metal-ops.cc:381-391): the int8 tier
+  // pays back its quantize passes only on tall, deep GEMMs.  K must fill
+  // whole 128-byte int8 K tiles here.
+  return _i8 && M >= 1024 && K >= 1024 && K % 128 == 0 && N % 8 == 0;
+}
+
+bool CudaOps::prepare_i8(QWeight& w, cudaStream_t s, std::string* err) const
+{
+  if (w.wq != nullptr) return true;
+  if (!w.quantized) {
+    if (err) *err = "int8 tier: weight is not quantized";
+    return false;
+  }
+  const size_t nk = (size_t)w.N * w.K;
+  __nv_bfloat16* tmp = nullptr;
+  if (!cuda_ok(cudaMalloc(&tmp, nk * 2), "cudaMalloc(i8 prep)", err)) return false;
+  if (!cuda_ok(cudaMalloc(&w.wq, nk), "cudaMalloc(i8 weight)", err)) {
+    cudaFree(tmp);
+    return false;
+  }
+  if (!cuda_ok(cudaMalloc(&w.sw, (size_t)w.N * sizeof(float)), "cudaMalloc(i8 scales)", err)) {
+    cudaFree(tmp);
+    return false;
+  }
+  bool ok = ltx::launch_dequant_w8(w.codes, w.sz, w.N, w.K, tmp, s) == 0 &&
+            ltx::launch_quant_rows_i8(tmp, w.N, w.K, w.K, w.K, w.wq, w.sw, s) == 0;
+  ok = ok && cuda_ok(cudaStreamSynchronize(s), "i8 weight prep", err);
+  cudaFree(tmp);
+  if (!ok && err && err->empty()) *err = "i8 weight prep launch failed";
+  return ok;
+}
+
+bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
+                    const void* wptr, const uint32_t* sz,
+                    const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy,
+                    int M, int K, int N, int epi, const __nv_bfloat16* gate,
+                    const float* sx, const float* sw, std::string* err)
+{
+  const Plan pl = plan_gemm(mode, M, N, K, _sms);
+  if (pl.splits > 1) {
+    const size_t need = (size_t)pl.splits * pl.m_tiles * pl.tn * N * sizeof(float);
+    if (!ensure_(need, 0, 0, err)) return false;
+    if ((size_t)pl.m_tiles * pl.n_tiles > _n_counters) {
+      if (err) *err = "split-K: too many tiles for the counter array";
+      return false;
+    }
+  }
+  ltx::GemmLaunch L;
+  L.mode = mode;
+  L.tn = pl.tn;
+  L.epi = epi;
+  L.num_sms = _sms;
+  L.x = x;
+  L.ldx = ldx;
+  L.w = wptr;
+  L.sz = sz;
+  ltx::GemmParams& p = L.p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = pl.m_tiles;
+  p.n_tiles = pl.n_tiles;
+  p.splits = pl.splits;
+  p.kblocks = pl.kblocks;
+  p.num_tiles = pl.m_tiles * pl.n_tiles * pl.splits;
+  p.ldy = ldy;
+  p.bias = bias;
+  p.gate = gate;
+  p.y = y;
+  p.ws = _ws;
+  p.counters = _counters;
+  p.sx = sx;
+  p.sw = sw;
+  p.err = _err_word;
+  const int rc = ltx::gemm_launch(L, s);
+  if (rc != 0) {
+    if (err)
+      *err = "gemm launch failed (" + std::to_string(rc) + "): " +
+             cudaGetErrorString(cudaGetLastError());
+    return false;
+  }
+  return true;
+}
+
+bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
+                     const QWeight& w, const __nv_bfloat16* bias,
+                     __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
+                     const __nv_bfloat16* gate, std::string* err)
+{
+  if (x == nullptr || y == nullptr) {
+    if (err) *err = "linear: null x or y";
+    return false;
+  }
+  if (M <= 0 || K != w.K || N != w.N) {
+    if (err)
+      *err = "linear: shape (M=" + std::to_string(M) + ", K=" + std::to_string(K) +
+             ", N=" + std::to_string(N) + ") disagrees with the weight [" +
+             std::to_string(w.N) + "][" + std::to_string(w.K) + "]";
+    return false;
+  }
+  if (!aligned(x, 16) || ldx % 8 != 0 || ldx < K || !aligned(y, 4) ||
+      ldy % 2 != 0 || ldy < N || (bias && !aligned(bias, 4)) ||
+      (gate && !aligned(gate, 4))) {
+    if (err) *err = "linear: x must be 16-byte aligned with ldx % 8 == 0; y, bias, gate 4-byte aligned";
+    return false;
+  }
+  if (epi == ltx::EPI_GATED_RES && gate == nullptr) {
+    if (err) *err = "linear: gated residual needs a gate";
+    return false;
+  }
+  if (!w.quantized) {
+    return gemm_(s, ltx::MODE_BF16, x, ldx, w.w, nullptr, bias, y, ldy, M, K,
+                 N, epi, gate, nullptr, nullptr, err);
+  }
+  if (i8_takes(M, K, N)) {
+    if (!prepare_i8(const_cast<QWeight&>(w), s, err)) return false;
+    if (!ensure_(0, (size_t)M * K, 0, err)) return false;
+    if (ltx::launch_quant_rows_i8(x, M, K, ldx, K, _xq, _sx, s) != 0) {
+      if (err) *err = "int8 activation quantize launch failed";
+      return false;
+    }
+    return gemm_(s, ltx::MODE_I8, _xq, K, w.wq, nullptr, bias, y, ldy, M, K,
+                 N, epi, gate, _sx, w.sw, err);
+  }
+  if (_route == Route::DequantOnce) {
+    if (!ensure_(0, 0, (size_t)N * K * 2, err)) return false;
+    if (ltx::launch_dequant_w8(w.codes, w.sz, N, K, _deq, s) != 0) {
+      if (err) *err = "dequant launch failed";
+      return false;
+    }
+    return gemm_(s, ltx::MODE_BF16, x, ldx, _deq, nullptr, bias, y, ldy, M,
+                 K, N, epi, gate, nullptr, nullptr, err);
+  }
+  return gemm_(s, ltx::MODE_W8G64, x, ldx, w.codes, w.sz, bias, y, ldy, M, K,
+               N, epi, gate, nullptr, nullptr, err);
+}
+
+int CudaOps::check(cudaStream_t s, std::string* err) const
+{
+  int h = 0;
+  if (!cuda_ok(cudaMemcpyAsync(&h, _err_word, sizeof(int), cudaMemcpyDeviceToHost, s), "check", err))
+    return -1;
+  if (!cuda_ok(cudaStreamSynchronize(s), "check", err)) return -1;
+  if (h != 0) {
+    cudaMemsetAsync(_err_word, 0, sizeof(int), s);
+    if (_counters) cudaMemsetAsync(_counters, 0, _n_counters * sizeof(int), s);
+    cudaStreamSynchronize(s);
+    if (err) *err = "a kernel gave up on a bounded wait (code " + std::to_string(h) + ")";
+  }
+  return h;
+}
+
+// ---- upload ---------------------------------------------------------------
+
+bool upload_qweight(const CudaOps& ops, const uint32_t* codes,
+                    const void* scales, const void* biases, int sb_dtype,
+                    int N, int K, int bits, int group, bool on_device,
+                    QWeight* out, std::string* err)
+{
+  if (codes == nullptr || scales == nullptr || biases == nullptr || out == nullptr) {
+    if (err) *err = "upload: null tensor";
+    return false;
+  }
+  if (bits != 8 || group != 64) {
+    if (err)
+      *err = "upload: w" + std::to_string(bits) + "g" + std::to_string(group) +
+             " is not run by this build (only the w8g64 pack)";
+    return false;
+  }
+  if (N <= 0 || K <= 0 || K % 64 != 0 || N % 8 != 0) {
+    if (err) *err = "upload: need K % 64 == 0 and N % 8 == 0, got N=" +
+                    std::to_string(N) + " K=" + std::to_string(K);
+    return false;
+  }
+  if (sb_dtype < 0 || sb_dtype > 2) {
+    if (err) *err = "upload: unknown scale dtype";
+    return false;
+  }
+  const int G = K / 64;
+  const size_t sb_elt = sb_dtype == 2 ? 4 : 2;
+  QWeight w;
+  w.N = N;
+  w.K = K;
+  w.bits = 8;
+  w.group = 64;
+  w.quantized = true;
+  w.device = ops.device();
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  void* d_s = nullptr;
+  void* d_b = nullptr;
+  bool ok = cuda_ok(cudaMalloc(&w.codes, (size_t)N * K), "cudaMalloc(codes)", err) &&
+            cuda_ok(cudaMalloc(&w.sz, (size_t)N * G * 4), "cudaMalloc(sz)", err) &&
+            cuda_ok(cudaMemcpy(w.codes, codes, (size_t)N * K, kind), "upload codes", err);
+  if (ok && !on_device) {
+    ok = cuda_ok(cudaMalloc(&d_s, (size_t)N * G * sb_elt), "cudaMalloc", err) &&
+         cuda_ok(cudaMalloc(&d_b, (size_t)N * G * sb_elt), "cudaMalloc", err) &&
+         cuda_ok(cudaMemcpy(d_s, scales, (size_t)N * G * sb_elt, kind), "upload scales", err) &&
+         cuda_ok(cudaMemcpy(d_b, biases, (size_t)N * G * sb_elt, kind), "upload zero-points", err);
+  }
+  if (ok) {
+    ok = ltx::launch_pack_sz(on_device ? scales : d_s, on_device ? biases : d_b,
+                             sb_dtype, N, G, w.sz, nullptr) == 0 &&
+         cuda_ok(cudaDeviceSynchronize(), "pack scales", err);
+  }
+  cudaFree(d_s);
+  cudaFree(d_b);
+  if (!ok) {
+    free_qweight(&w);
+    return false;
+  }
+  *out = w;
+  return true;
+}
+
+bool upload_dweight(const CudaOps& ops, const uint16_t* wsrc, int N, int K,
+                    bool on_device, QWeight* out, std::string* err)
+{
+  if (wsrc == nullptr || out == nullptr) {
+    if (err) *err = "upload: null tensor";
+    return false;
+  }
+  if (N <= 0 || K <= 0 || K % 64 != 0 || N % 8 != 0) {
+    if (err) *err = "upload: dense weight needs K % 64 == 0 and N % 8 == 0";
+    return false;
+  }
+  QWeight w;
+  w.N = N;
+  w.K = K;
+  w.quantized = false;
+  w.device = ops.device();
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  if (!cuda_ok(cudaMalloc(&w.w, (size_t)N * K * 2), "cudaMalloc(w)", err) ||
+      !cuda_ok(cudaMemcpy(w.w, wsrc, (size_t)N * K * 2, kind), "upload w", err)) {
+    free_qweight(&w);
+    return false;
+  }
+  *out = w;
+  return true;
+}
+
+void free_qweight(QWeight* w)
+{
+  if (w == nullptr) return;
+  cudaFree(w->codes);
+  cudaFree(w->sz);
+  cudaFree(w->w);
+  cudaFree(w->wq);
+  cudaFree(w->sw);
+  *w = QWeight{};
+}
+
+}  // namespace ltx25

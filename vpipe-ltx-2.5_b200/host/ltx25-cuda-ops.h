@@ -1,0 +1,118 @@
+// ltx25-cuda-ops.h -- the op vocabulary of the LTX-2.5 block on B200.
+//
+// The CUDA counterpart of the reference's MetalOps (src/ltx25-metal-ops.h):
+// one object per device, owning the scratch arena and the tier switches,
+// with each op one (or a few) kernel launches on a caller-supplied stream.
+// Buffers are caller-owned device memory; nothing here allocates on a hot
+// call once reserve() has sized the arena.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace ltx25 {
+
+// One linear's weights, dense or w8g64 group-affine (src/ltx25-metal-ops.h:
+// 45-57).  The pack stays bit-exact: `codes` is the reference's u32 words
+// viewed as bytes (little-endian, so code k of a row is byte k).  The
+// scale/zero-point pairs are stored per K group as one u32 each, bf16
+// scale low / bf16 zero-point high, [K/64][N].
+struct QWeight {
+  uint8_t* codes = nullptr;        // [N][K]
+  uint32_t* sz = nullptr;          // [K/64][N]
+  __nv_bfloat16* w = nullptr;      // dense [N][K] when !quantized
+  int8_t* wq = nullptr;            // int8 tier: per-channel requantized
+  float* sw = nullptr;             // int8 tier: [N] channel scales
+  int N = 0, K = 0, bits = 0, group = 0;
+  bool quantized = false;
+  int device = 0;
+};
+
+enum class Route { Fused = 0, DequantOnce = 1 };
+
+class CudaOps {
+public:
+  ~CudaOps();
+
+  // False (with `err`) when the device is missing or not sm_100.
+  bool init(int device, std::string* err);
+
+  // Grow the shared scratch to cover calls up to these sizes.
+  bool reserve(int max_tokens, int max_n, int max_k, std::string* err);
+
+  // y[M][N] = x[M][K] . W^T (+ bias), epilogue per ltx::EpiMode.
+  bool linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
+              const QWeight& w, const __nv_bfloat16* bias, __nv_bfloat16* y,
+              int ldy, int M, int K, int N, int epi,
+              const __nv_bfloat16* gate, std::string* err);
+
+  void set_route(Route r) { _route = r; }
+  Route route() const { return _route; }
+
+  void set_i8_gemm(bool on) { _i8 = on; }
+  bool i8_on() const { return _i8; }
+  bool i8_takes(int M, int K, int N) const;
+
+  void set_sage(bool on, int dense_layers)
+  {
+    _sage = on;
+    _sage_dense = dense_layers;
+  }
+  bool sage_on() const { return _sage; }
+  int sage_dense_layers() const { return _sage_dense; }
+
+  // Per-channel int8 copy of a quantized weight for the int8 tier; made
+  // once per weight, on first use or here.
+  bool prepare_i8(QWeight& w, cudaStream_t s, std::string* err) const;
+
+  int device() const { return _dev; }
+  int num_sms() const { return _sms; }
+  int* err_word() const { return _err_word; }
+
+  // Reads and clears the device error word.  0 when clean.
+  int check(cudaStream_t s, std::string* err) const;
+
+private:
+  bool ensure_(size_t ws_bytes, size_t i8_bytes, size_t deq_bytes,
+               std::string* err);
+  bool gemm_(cudaStream_t s, int mode, const void* x, int ldx,
+             const void* wptr, const uint32_t* sz, const __nv_bfloat16* bias,
+             __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
+             const __nv_bfloat16* gate, const float* sx, const float* sw,
+             std::string* err);
+
+  int _dev = -1;
+  int _sms = 148;
+  Route _route = Route::Fused;
+  bool _i8 = false;
+  bool _sage = false;
+  int _sage_dense = 0;
+
+  // Scratch arena: split-K partials + tile counters, the int8 tier's
+  // quantized activations, the dequant-once expansion.
+  float* _ws = nullptr;
+  size_t _ws_bytes = 0;
+  int* _counters = nullptr;
+  size_t _n_counters = 0;
+  int8_t* _xq = nullptr;
+  float* _sx = nullptr;
+  size_t _xq_bytes = 0;
+  __nv_bfloat16* _deq = nullptr;
+  size_t _deq_bytes = 0;
+  int* _err_word = nullptr;
+};
+
+// Upload helpers (the ltx25-dit-weights bind path, src/ltx25-dit-weights.cc:
+// 352-403): validate, copy once into HBM, relayout scale/zero-point pairs.
+bool upload_qweight(const CudaOps& ops, const uint32_t* codes,
+                    const void* scales, const void* biases, int sb_dtype,
+                    int N, int K, int bits, int group, bool on_device,
+                    QWeight* out, std::string* err);
+bool upload_dweight(const CudaOps& ops, const uint16_t* w, int N, int K,
+                    bool on_device, QWeight* out, std::string* err);
+void free_qweight(QWeight* w);
+
+}  // namespace ltx25
