@@ -1,0 +1,454 @@
+#!/usr/bin/env python
+"""bench.py -- the w8g64 qlinear sweep of BASELINE config 2 on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the DiT linear-shape sweep:
+nine w8g64 quantized linears at the shapes one LTX-2.5 block dispatches at
+960x544x121 -- video stream M=8160 (4096->4096 attention out, 4096->12288
+fused QKV, 4096->16384 FFN-up, 16384->4096 FFN-down), audio stream M=126
+(2048->2048, 2048->8192, 8192->2048), audio<->video cross projections
+(2048->4096, 4096->2048 at M=8160) -- each through the library's C ABI
+(ltx_qlinear).  Weights are N(0, 0.02) packed by the library's own w8g64
+quantizer (bit-identical to the reference packer), activations N(0, 1) bf16,
+all seeded.
+
+value   whole-job TFLOP/s (algorithmic 2*M*N*K), inputs resident in HBM.
+e2e     the same through the C ABI with HOST buffers: each step copies every
+        activation in from pinned host memory and every output back out.
+roofline  tensor-bound: the w8g64 GEMM over the six M=8160 shapes, achieved
+        = their algorithmic FLOPs / their CUDA-event time inside the timed
+        region, against MEASURED_PEAKS.json bf16_tflops.  roofline_hbm: the
+        three M=126 audio shapes, algorithmic bytes (N*K codes + 4*N*K/64
+        scale/zero-point bytes + 2*M*(K+N) activations) / time, against
+        MEASURED_PEAKS.json hbm_gbs.
+cpu_baseline  the reference's own CPU dequantise-then-dense linear_
+        (oracle/_ref, compiled from the reference sources) on a bounded
+        sample, 1 core, rank 0 at N=1.
+
+--impl reference  times that reference CPU path alone on all host cores
+        (the reference has no GPU path that runs here: it is Apple Metal).
+
+Multi-GPU: one process per GPU, each running the sweep on its own copy of
+the workload (weak scaling, no data-path collective); the time is the max
+over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "vpipe-ltx-2.5_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+SHAPES = [  # (name, M, K, N)
+    ("video attn-out 4096->4096", 8160, 4096, 4096),
+    ("video fused-QKV 4096->12288", 8160, 4096, 12288),
+    ("video FFN-up 4096->16384", 8160, 4096, 16384),
+    ("video FFN-down 16384->4096", 8160, 16384, 4096),
+    ("audio 2048->2048", 126, 2048, 2048),
+    ("audio FFN-up 2048->8192", 126, 2048, 8192),
+    ("audio FFN-down 8192->2048", 126, 8192, 2048),
+    ("a2v out 2048->4096", 8160, 2048, 4096),
+    ("v2a k/v 4096->2048", 8160, 4096, 2048),
+]
+METRIC = "w8g64 qlinear TFLOP/s, DiT linear-shape sweep (BASELINE config 2)"
+UNIT = "TFLOP/s"
+CPU_ROWS = 64        # cpu sample: first 64 tokens ...
+CPU_FEATURES = 1024  # ... x first 1024 output features of every shape
+
+
+def flops(M, K, N):
+    return 2.0 * M * N * K
+
+
+def hbm_bytes(M, K, N):
+    return N * K * (1.0 + 4.0 / 64.0) + 2.0 * M * (K + N)
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100", "-i",
+                 str(self.gpu_id)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.t.join(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_weights(L, ctx, torch, dev, K, N, gen):
+    w = torch.randn((N, K), generator=gen, device=dev, dtype=torch.float32) * 0.02
+    codes, scales, biases = L.pack_w8g64(ctx, w)
+    del w
+    qw = L.QWeight.upload(ctx, codes, scales, biases, N, K, sb_dtype=L.SB_BF16,
+                          on_device=True)
+    del codes, scales, biases
+    return qw
+
+
+def cpu_reference_sample(threads):
+    """The reference CPU qlinear (dequantise-then-dense, linear_ with f64
+    accumulation) on the bounded sample.  Returns (flops, seconds, kind)."""
+    import concurrent.futures as cf
+    import numpy as np
+    from oracle import lib as olib
+    from oracle import ref as oref
+    kind = "reference" if oref.available() else "port"
+    rng = np.random.default_rng(7)
+    jobs = []
+    for _, M, K, N in SHAPES:
+        m, n = min(M, CPU_ROWS), min(N, CPU_FEATURES)
+        x = olib.bf16_to_f32(olib.f32_to_bf16(rng.standard_normal((m, K)).astype(np.float32)))
+        w = (rng.standard_normal((n, K)) * 0.02).astype(np.float32)
+        _, _, _, deq = (oref.pack(w, 8, 64) if kind == "reference"
+                        else olib.pack_affine(w, 8, 64))
+        jobs.append((x, deq))
+    linear = oref.linear if kind == "reference" else (
+        lambda x, w: olib.linear_f64(x, w, None, 1))
+
+    def run_one(x, w):
+        return linear(x, w)
+
+    total = sum(flops(x.shape[0], x.shape[1], w.shape[0]) for x, w in jobs)
+    t0 = time.perf_counter()
+    if threads <= 1:
+        for x, w in jobs:
+            run_one(x, w)
+    else:
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            futs = []
+            for x, w in jobs:
+                step = max(1, (x.shape[0] + threads - 1) // threads)
+                for r in range(0, x.shape[0], step):
+                    futs.append(ex.submit(run_one, x[r:r + step], w))
+            for f in futs:
+                f.result()
+    return total, time.perf_counter() - t0, kind
+
+
+def sample_desc():
+    return (f"first {CPU_ROWS} tokens x first {CPU_FEATURES} output features of "
+            "each of the 9 sweep shapes (full K), weights dequantized once "
+            "outside the timing")
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_reference_sample(threads)
+    fl = 0.0
+    sec = 0.0
+    kind = "port"
+    for _ in range(args.steps):
+        f, s, kind = cpu_reference_sample(threads)
+        fl += f
+        sec += s
+    value = fl / sec / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32/f64-accumulate",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": "BASELINE config 2 sweep, bounded CPU sample",
+                   "sample": sample_desc()},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
+                         "kind": kind, "sample": sample_desc()},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's GPU path is Apple Metal (unavailable on this "
+                "box); this arm is its CPU dequantise-then-dense qlinear",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", type=int, default=None,
+                    help="profile one sweep shape (index into SHAPES)")
+    args = ap.parse_args()
+    if args.only is not None:
+        SHAPES[:] = [SHAPES[args.only]]
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import ltx25_b200 as L
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+
+    ctx = L.Context(local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    weights, xs, ys = [], [], []
+    for _, M, K, N in SHAPES:
+        weights.append(make_weights(L, ctx, torch, dev, K, N, gen))
+        xs.append(torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16))
+        ys.append(torch.empty((M, N), device=dev, dtype=torch.bfloat16))
+    ctx.reserve(max(s[1] for s in SHAPES), max(s[3] for s in SHAPES),
+                max(s[2] for s in SHAPES))
+    stream = torch.cuda.current_stream()
+    ctx.check()
+
+    def step(evs=None):
+        for i, (w, x, y) in enumerate(zip(weights, xs, ys)):
+            if evs is not None:
+                evs[i][0].record(stream)
+            L.qlinear(ctx, w, x, out=y, stream=stream)
+            if evs is not None:
+                evs[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.check()
+
+    # ---------------------------------------------------------- timed region
+    evs = [[[torch.cuda.Event(enable_timing=True),
+             torch.cuda.Event(enable_timing=True)] for _ in SHAPES]
+           for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    with ClockSampler(gpu_id) as clk:
+        t_start.record(stream)
+        for s in range(args.steps):
+            step(evs[s])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    ctx.check()
+    ms_total = t_start.elapsed_time(t_end)
+    per_shape_ms = [0.0] * len(SHAPES)
+    for s in range(args.steps):
+        for i in range(len(SHAPES)):
+            per_shape_ms[i] += evs[s][i][0].elapsed_time(evs[s][i][1])
+    if pg is not None:
+        t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms_total = float(t.item())
+
+    step_flops = sum(flops(M, K, N) for _, M, K, N in SHAPES)
+    ms_per_step = ms_total / args.steps
+    value = world * step_flops / (ms_per_step * 1e-3) / 1e12
+
+    # ------------------------------------------------------------- e2e leg
+    xh = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs]
+    yh = [torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for y in ys]
+    for a, b in zip(xh, xs):
+        a.copy_(b)
+    h2d = sum(x.numel() * 2 for x in xs)
+    d2h = sum(y.numel() * 2 for y in ys)
+
+    def e2e_step():
+        for w, x, y, a, b in zip(weights, xs, ys, xh, yh):
+            x.copy_(a, non_blocking=True)
+            L.qlinear(ctx, w, x, out=y, stream=stream)
+            b.copy_(y, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    ctx.check()
+    e2e_value = world * step_flops / (e2e_ms * 1e-3) / 1e12
+
+    # ------------------------------------------------------------- rooflines
+    bf16_peak, hbm_peak, peak_kind = peaks()
+    vid = [i for i, s in enumerate(SHAPES) if s[1] > 1024]
+    aud = [i for i, s in enumerate(SHAPES) if s[1] <= 1024]
+    vid_fl = sum(flops(*SHAPES[i][1:]) for i in vid) * args.steps
+    vid_s = sum(per_shape_ms[i] for i in vid) * 1e-3
+    aud_b = sum(hbm_bytes(*SHAPES[i][1:]) for i in aud) * args.steps
+    aud_s = sum(per_shape_ms[i] for i in aud) * 1e-3
+    achieved = vid_fl / vid_s / 1e12 if vid_s > 0 else 0.0
+    achieved_hbm = aud_b / aud_s / 1e9 if aud_s > 0 else 0.0
+    prof = traffic_from_profile() or {}
+
+    per_shape = []
+    for i, (name, M, K, N) in enumerate(SHAPES):
+        t = per_shape_ms[i] / args.steps * 1e-3
+        per_shape.append({"shape": name, "M": M, "K": K, "N": N,
+                          "us": round(t * 1e6, 2),
+                          "tflops": round(flops(M, K, N) / t / 1e12, 1),
+                          "gbs": round(hbm_bytes(M, K, N) / t / 1e9, 1)})
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        f, s, kind = cpu_reference_sample(1)
+        cpu = {"value": f / s / 1e12, "unit": UNIT, "cores": 1, "kind": kind,
+               "sample": sample_desc(), "seconds": round(s, 2)}
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 activations; N(0,0.02) weights "
+                "w8g64-packed on device, bit-identical to the reference packer)",
+        "config": {
+            "workload": "BASELINE config 2: DiT linear-shape sweep, all w8g64",
+            "shapes": [f"{n}: M={M} K={K} N={N}" for n, M, K, N in SHAPES],
+            "l2": "inputs larger than L2: the sweep's operands total ~1.5 GB "
+                  "and each shape's are evicted by the others between repeats",
+            "parallelism": f"replicas x{world} (no data-path collective)",
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3),
+                "api": "ltx_qlinear via ctypes, pinned host buffers"},
+        "gpu_launches": len(SHAPES) * args.steps,
+        "clocks": clk.summary(),
+        "roofline": {
+            "bound": "tensor", "achieved": round(achieved, 1),
+            "peak": bf16_peak, "unit": "TFLOP/s",
+            "frac": round(achieved / bf16_peak, 4),
+            "peak_source": f"{peak_kind} bf16_tflops (burst)",
+            "kernel": "gemm_tc_kernel<MODE_W8G64,TN=256> over the 6 M=8160 shapes",
+            "traffic": prof.get("video_bytes_per_launch"),
+        },
+        "roofline_hbm": {
+            "bound": "hbm", "achieved": round(achieved_hbm, 1),
+            "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved_hbm / hbm_peak, 4),
+            "kernel": "gemm_tc_kernel<MODE_W8G64,TN=128> split-K, 3 M=126 shapes",
+            "traffic": prof.get("audio_bytes_per_launch"),
+        },
+        "per_shape": per_shape,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for w in weights:
+        w.free()
+    ctx.close()
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -156,6 +156,16 @@ LTX_API int ltx_dequant(ltx_ctx* ctx, const ltx_qweight* w, void* out, void* str
 LTX_API int ltx_quant_rows_i8(ltx_ctx* ctx, const void* x, int rows, int K,
                       int group, void* q, void* scale, void* stream);
 
+/* The w8g64 quantizer itself, on the device: w f32 [N][K] -> codes u32
+ * [N][K/4] (low bits first), scales and zero-points bf16 [N][K/64], with
+ * the arithmetic of the reference's packer (tests/ltx25-qlinear-test.cc:
+ * 94-141) so the pack is bit-identical.  What vpipe's model-quantize
+ * writes for a w8g64 tensor, before its F16 storage.  All device pointers;
+ * K % 64 == 0. */
+LTX_API int ltx_pack_w8g64(ltx_ctx* ctx, const float* w, int N, int K,
+                           uint32_t* codes, uint16_t* scales,
+                           uint16_t* biases, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -218,3 +218,23 @@ def test_f16_scales_are_converted_rne(ctx):
     want = lib.dequant_bf16(codes, lib.f32_to_bf16(s16.astype(np.float32)),
                             lib.f32_to_bf16(b16.astype(np.float32)), K)
     assert np.array_equal(got, want)
+
+
+def test_device_packer_is_bit_exact(ctx, golden):
+    """ltx_pack_w8g64 against the reference packer's golden output."""
+    import torch
+    import ltx25_b200 as L
+    g = golden("pack.npz")
+    for name in ("case0", "case1", "case6", "edge"):
+        w = g[f"{name}__w"]
+        c, s, b = L.pack_w8g64(ctx, torch.from_numpy(w).cuda())
+        assert np.array_equal(c.cpu().numpy().view(np.uint32), g[f"{name}__codes"]), name
+        assert np.array_equal(s.cpu().numpy().view(np.uint16), g[f"{name}__scales"]), name
+        assert np.array_equal(b.cpu().numpy().view(np.uint16), g[f"{name}__biases"]), name
+    rng = np.random.default_rng(12)
+    w = (rng.standard_normal((384, 4096)) * 0.02).astype(np.float32)
+    c, s, b = L.pack_w8g64(ctx, torch.from_numpy(w).cuda())
+    want = lib.pack_affine(w, 8, 64)
+    assert np.array_equal(c.cpu().numpy().view(np.uint32), want[0])
+    assert np.array_equal(s.cpu().numpy().view(np.uint16), want[1])
+    assert np.array_equal(b.cpu().numpy().view(np.uint16), want[2])

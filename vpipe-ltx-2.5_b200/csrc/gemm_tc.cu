@@ -108,7 +108,6 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* drain = accempty + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-  volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem + 2);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
@@ -128,7 +127,6 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(drain, 1);
     *s_abort = 0;
-    *s_last = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -316,13 +314,11 @@ __global__ void __launch_bounds__(320, 1)
     // ----------------------------------------------------------- epilogue
     const int q = warp & 3;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const int ep_tid = threadIdx.x - 192;   // 0..127
     int acc = 0;
     uint32_t accphase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int mt, nt, kb0, kb1;
       decode_tile(p, t, mt, nt, kb0, kb1);
-      const int split = t % p.splits;
       if (!mbar_wait(&accfull[acc], accphase, s_abort, p.err,
                      KERR_WAIT_EPILOGUE))
         goto epi_done;
@@ -356,6 +352,23 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         const int j0 = mt * TN + c * 32;
+        if (p.splits > 1) {
+          // K-split partial: park it in this CTA's shared memory as
+          // red[token][feature] f32 (the pipeline buffers are idle now);
+          // the cluster reduces it after the role loops.
+          float* red = reinterpret_cast<float*>(s_x);
+          const int nl = q * 32 + (int)lane;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float val = f[i];
+            if constexpr (MODE == MODE_I8) {
+              const int j = j0 + i;
+              val *= j < p.M ? p.sx[j] : 0.0f;
+            }
+            red[(c * 32 + i) * C::kBM + nl] = val;
+          }
+          continue;
+        }
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           // even lane keeps token 2k, odd lane keeps token 2k+1
@@ -369,50 +382,11 @@ __global__ void __launch_bounds__(320, 1)
             a *= s;
             b *= s;
           }
-          if (p.splits == 1) {
-            if (j < p.M && n_pair < p.N) {
-              __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
-              const uint32_t o = epi_pair<EPI>(a, b, n_pair, p, yrow);
-              *reinterpret_cast<uint32_t*>(yrow + n_pair) = o;
-            }
-          } else if (n_pair < p.N) {
-            float* wrow =
-                p.ws + ((size_t)split * p.m_tiles * TN + j) * p.N + n_pair;
-            __stcg(reinterpret_cast<float2*>(wrow), make_float2(a, b));
+          if (j < p.M && n_pair < p.N) {
+            __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
+            const uint32_t o = epi_pair<EPI>(a, b, n_pair, p, yrow);
+            *reinterpret_cast<uint32_t*>(yrow + n_pair) = o;
           }
-        }
-      }
-      if (p.splits > 1) {
-        // Last CTA of this (m, n) tile reduces the partials in split order.
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (ep_tid == 0) {
-          const int prev = atomicAdd(&p.counters[mt * p.n_tiles + nt], 1);
-          *s_last = (prev == p.splits - 1) ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        if (*s_last) {
-          __threadfence();
-#pragma unroll 1
-          for (int c = 0; c < TN / 32; ++c) {
-#pragma unroll 1
-            for (int k = 0; k < 16; ++k) {
-              const int j = mt * TN + c * 32 + 2 * k + odd;
-              if (j >= p.M || n_pair >= p.N) continue;
-              float a = 0.0f, b = 0.0f;
-              for (int sp = 0; sp < p.splits; ++sp) {
-                const float2 w2 = __ldcg(reinterpret_cast<const float2*>(
-                    p.ws + ((size_t)sp * p.m_tiles * TN + j) * p.N + n_pair));
-                a += w2.x;
-                b += w2.y;
-              }
-              __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
-              const uint32_t o = epi_pair<EPI>(a, b, n_pair, p, yrow);
-              *reinterpret_cast<uint32_t*>(yrow + n_pair) = o;
-            }
-          }
-          named_bar_sync(1, 128);
-          if (ep_tid == 0) p.counters[mt * p.n_tiles + nt] = 0;
         }
       }
       if (++acc == C::kNAcc) {
@@ -425,7 +399,46 @@ __global__ void __launch_bounds__(320, 1)
 
   tc_fence_before();
   __syncthreads();
+
+  if (p.splits > 1) {
+    // One cluster per output tile, one CTA per K split (cluster rank ==
+    // split).  Each CTA reduces a band of token rows across the cluster's
+    // partials through DSMEM, in rank order, and stores the bf16 result.
+    cluster_sync_all();
+    int mt, nt, kb0, kb1;
+    decode_tile(p, blockIdx.x, mt, nt, kb0, kb1);
+    const int rank = (int)cluster_ctarank();
+    const int per = (TN + p.splits - 1) / p.splits;
+    const int r0 = rank * per;
+    const int r1 = min(TN, r0 + per);
+    const uint32_t red = smem_u32(s_x);
+    for (int idx = threadIdx.x; idx < (r1 - r0) * (C::kBM / 4); idx += blockDim.x) {
+      const int jl = r0 + idx / (C::kBM / 4);
+      const int c4 = (idx % (C::kBM / 4)) * 4;
+      const int j = mt * TN + jl;
+      const int n = nt * C::kBM + c4;
+      if (j >= p.M || n >= p.N) continue;
+      const uint32_t off = (uint32_t)((jl * C::kBM + c4) * 4);
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < p.splits; ++sp) {
+        const float4 v = ld_dsmem_f4(mapa_shared(red + off, (uint32_t)sp));
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
+      const uint32_t o0 = epi_pair<EPI>(s.x, s.y, n, p, yrow);
+      const uint32_t o1 = epi_pair<EPI>(s.z, s.w, n + 2, p, yrow);
+      *reinterpret_cast<uint32_t*>(yrow + n) = o0;
+      *reinterpret_cast<uint32_t*>(yrow + n + 2) = o1;
+    }
+    // Peers may still be reading this CTA's partial: leave together.
+    cluster_sync_all();
+  }
+
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -501,6 +514,24 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
                              C::kSmemBytes) != cudaSuccess)
       return -2;
     attr_done = true;
+  }
+  if (p.splits > 1) {
+    // One cluster of `splits` CTAs per output tile, one unit per CTA.
+    if (p.num_tiles > L.num_sms || p.splits > 8) return -5;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p.num_tiles, 1, 1);
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tx, tw, tsz, p) != cudaSuccess) return -3;
+    return 0;
   }
   const int grid = p.num_tiles < L.num_sms ? p.num_tiles : L.num_sms;
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, tsz, p);

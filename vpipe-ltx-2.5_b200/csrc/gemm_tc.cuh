@@ -26,10 +26,12 @@
 //   warps 2-5  dequant (MODE_W8G64 only): TMEM lane quarter warp%4
 //   warps 6-9  epilogue: TMEM -> registers -> bias/act/residual -> global
 //
-// K is split across CTAs (`splits` > 1) for the small-M, bandwidth-bound
-// shapes; partial tiles are reduced in L2 by the last CTA to finish each
-// tile (a counter per tile, no spin-waits), in a fixed order, so results
-// are deterministic.
+// K is split across CTAs (`splits` > 1, at most 8) for the small-M,
+// bandwidth-bound shapes.  The splits of one output tile are launched as
+// one thread-block cluster; each parks its f32 partial in its own shared
+// memory and the cluster reduces them through distributed shared memory in
+// rank order, so the result is deterministic and never leaves the SMs
+// before it is final.
 #pragma once
 
 #include "ptx.cuh"
@@ -59,8 +61,6 @@ struct GemmParams {
   const __nv_bfloat16* bias;   // [N] or null
   const __nv_bfloat16* gate;   // [N], EPI_GATED_RES only
   __nv_bfloat16* y;            // [M][ldy]
-  float* ws;                   // [splits][m_tiles*TN][N] partials
-  int* counters;               // [m_tiles*n_tiles], zero between calls
   const float* sx;             // MODE_I8: [M] token scales
   const float* sw;             // MODE_I8: [N] channel scales
   int* err;                    // device error word (0 = ok)

@@ -40,6 +40,10 @@ int gemm_smem_bytes(int mode, int tn);
 // the bf16 scale in the low half and the bf16 zero-point in the high half.
 int launch_pack_sz(const void* scales, const void* biases, int dtype, int N,
                    int G, uint32_t* sz, cudaStream_t stream);
+// The reference w8g64 quantizer on the device: w f32 [N][K] -> codes u32
+// [N][K/4], scales / zero-points bf16 [N][K/64].
+int launch_pack_w8g64(const float* w, int N, int K, uint32_t* codes,
+                      uint16_t* scales, uint16_t* biases, cudaStream_t stream);
 // codes u8 [N][K] + sz -> bf16 [N][K] (s*q + z, one rounding).
 int launch_dequant_w8(const uint8_t* codes, const uint32_t* sz, int N, int K,
                       __nv_bfloat16* out, cudaStream_t stream);

@@ -283,4 +283,44 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads)
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ---- thread-block clusters (distributed shared memory) -------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA in the cluster arrives, then waits.  Writes to
+// shared memory before the barrier are visible to peers after it.
+__device__ __forceinline__ void cluster_sync_all()
+{
+  asm volatile(
+      "barrier.cluster.arrive.release;\n\t"
+      "barrier.cluster.wait.acquire;" ::
+          : "memory");
+}
+
+// The shared::cluster address of `saddr` (a shared::cta address) in CTA
+// `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank)
+{
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(r)
+               : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t caddr)
+{
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(caddr)
+               : "memory");
+  return v;
+}
+
 }  // namespace ltx

@@ -133,6 +133,50 @@ __global__ void quant_rows_i8_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// The w8g64 quantizer, one warp per (row, 64-group).  The arithmetic of the
+// reference's packer (tests/ltx25-qlinear-test.cc:94-141) -- min/max, scale
+// = (hi - lo) / 255 and both rounded to bf16, q = lround((w - lo) / scale)
+// clamped to [0, 255], 0 when the scale is 0 -- done in IEEE single
+// operations, so the pack is bit-identical.
+__global__ void pack_w8g64_kernel(const float* __restrict__ w, int N, int K,
+                                  uint32_t* __restrict__ codes,
+                                  uint16_t* __restrict__ scales,
+                                  uint16_t* __restrict__ biases)
+{
+  const int G = K / 64;
+  const long long warp_id =
+      (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_id >= (long long)N * G) return;
+  const int n = (int)(warp_id / G), g = (int)(warp_id % G);
+  const float2 v =
+      *reinterpret_cast<const float2*>(w + (size_t)n * K + g * 64 + lane * 2);
+  float lo = fminf(v.x, v.y), hi = fmaxf(v.x, v.y);
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  const float sc = __fdiv_rn(__fsub_rn(hi, lo), 255.0f);
+  const uint16_t sc_b = to_bf16_bits(sc), lo_b = to_bf16_bits(lo);
+  const float scr = __uint_as_float((uint32_t)sc_b << 16);
+  const float lor = __uint_as_float((uint32_t)lo_b << 16);
+  int q0 = 0, q1 = 0;
+  if (scr > 0.0f) {
+    q0 = (int)lroundf(__fdiv_rn(__fsub_rn(v.x, lor), scr));
+    q1 = (int)lroundf(__fdiv_rn(__fsub_rn(v.y, lor), scr));
+    q0 = min(max(q0, 0), 255);
+    q1 = min(max(q1, 0), 255);
+  }
+  const uint32_t half = (uint32_t)q0 | ((uint32_t)q1 << 8);
+  const uint32_t other = __shfl_down_sync(0xffffffffu, half, 1);
+  if ((lane & 1) == 0)
+    codes[(size_t)n * (K / 4) + g * 16 + lane / 2] = half | (other << 16);
+  if (lane == 0) {
+    scales[(size_t)n * G + g] = sc_b;
+    biases[(size_t)n * G + g] = lo_b;
+  }
+}
+
 int grid_for(long long work, int threads)
 {
   long long g = (work + threads - 1) / threads;
@@ -148,6 +192,18 @@ int launch_pack_sz(const void* scales, const void* biases, int dtype, int N,
 {
   pack_sz_kernel<<<grid_for((long long)N * G, 256), 256, 0, stream>>>(
       scales, biases, dtype, N, G, sz);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_pack_w8g64(const float* w, int N, int K, uint32_t* codes,
+                      uint16_t* scales, uint16_t* biases, cudaStream_t stream)
+{
+  if (K % 64 != 0 || N <= 0) return -1;
+  const long long threads = (long long)N * (K / 64) * 32;
+  const int block = 256;
+  const long long grid = (threads + block - 1) / block;
+  pack_w8g64_kernel<<<(unsigned)grid, block, 0, stream>>>(w, N, K, codes,
+                                                          scales, biases);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -214,4 +214,17 @@ int ltx_quant_rows_i8(ltx_ctx* ctx, const void* x, int rows, int K, int group,
   return LTX_OK;
 }
 
+int ltx_pack_w8g64(ltx_ctx* ctx, const float* w, int N, int K, uint32_t* codes,
+                   uint16_t* scales, uint16_t* biases, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (w == nullptr || codes == nullptr || scales == nullptr || biases == nullptr)
+    return fail(ctx, LTX_E_NULL, "pack_w8g64: null");
+  if (N <= 0 || K <= 0 || K % 64 != 0)
+    return fail(ctx, LTX_E_SHAPE, "pack_w8g64: need K % 64 == 0");
+  if (ltx::launch_pack_w8g64(w, N, K, codes, scales, biases, S(stream)) != 0)
+    return fail(ctx, LTX_E_CUDA, "pack_w8g64 launch failed");
+  return LTX_OK;
+}
+
 }  // extern "C"

@@ -45,7 +45,7 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
   const int tiles = p.m_tiles * p.n_tiles;
   p.splits = 1;
   if (tiles * 2 <= sms && p.kblocks >= 4) {
-    p.splits = std::min(std::min(sms / tiles, p.kblocks / 2), 16);
+    p.splits = std::min(std::min(sms / tiles, p.kblocks / 2), 8);
     if (p.splits < 1) p.splits = 1;
   }
   return p;
@@ -59,8 +59,6 @@ CudaOps::~CudaOps()
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(_dev);
-  cudaFree(_ws);
-  cudaFree(_counters);
   cudaFree(_xq);
   cudaFree(_sx);
   cudaFree(_deq);
@@ -94,25 +92,8 @@ bool CudaOps::init(int device, std::string* err)
   return cuda_ok(cudaMemset(_err_word, 0, sizeof(int)), "cudaMemset", err);
 }
 
-bool CudaOps::ensure_(size_t ws_bytes, size_t i8_bytes, size_t deq_bytes,
-                      std::string* err)
+bool CudaOps::ensure_(size_t i8_bytes, size_t deq_bytes, std::string* err)
 {
-  const size_t n_counters = 64 * 1024;
-  if (_counters == nullptr) {
-    if (!cuda_ok(cudaMalloc(&_counters, n_counters * sizeof(int)), "cudaMalloc(counters)", err))
-      return false;
-    if (!cuda_ok(cudaMemset(_counters, 0, n_counters * sizeof(int)), "cudaMemset", err))
-      return false;
-    _n_counters = n_counters;
-  }
-  if (ws_bytes > _ws_bytes) {
-    cudaFree(_ws);
-    _ws = nullptr;
-    _ws_bytes = 0;
-    if (!cuda_ok(cudaMalloc(&_ws, ws_bytes), "cudaMalloc(split-K scratch)", err))
-      return false;
-    _ws_bytes = ws_bytes;
-  }
   if (i8_bytes > _xq_bytes) {
     cudaFree(_xq);
     cudaFree(_sx);
@@ -142,16 +123,11 @@ bool CudaOps::reserve(int max_tokens, int max_n, int max_k, std::string* err)
     if (err) *err = "reserve: sizes must be positive";
     return false;
   }
-  // Split-K only runs on small tile counts; bound it by the planner.
-  size_t ws = 0;
-  for (int mode : {(int)ltx::MODE_W8G64, (int)ltx::MODE_I8}) {
-    for (int m : {std::min(max_tokens, 128), std::min(max_tokens, 256), max_tokens}) {
-      const Plan p = plan_gemm(mode, m, max_n, max_k, _sms);
-      if (p.splits > 1)
-        ws = std::max(ws, (size_t)p.splits * p.m_tiles * p.tn * max_n * sizeof(float));
-    }
-  }
-  return ensure_(ws, 0, 0, err);
+  // The split-K partials live in shared memory; only the int8 tier's
+  // quantized activations and the dequant-once expansion need HBM scratch.
+  const size_t i8 = _i8 ? (size_t)max_tokens * max_k : 0;
+  const size_t deq = _route == Route::DequantOnce ? (size_t)max_n * max_k * 2 : 0;
+  return ensure_(i8, deq, err);
 }
 
 bool CudaOps::i8_takes(int M, int K, int N) const
@@ -195,14 +171,6 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
                     const float* sx, const float* sw, std::string* err)
 {
   const Plan pl = plan_gemm(mode, M, N, K, _sms);
-  if (pl.splits > 1) {
-    const size_t need = (size_t)pl.splits * pl.m_tiles * pl.tn * N * sizeof(float);
-    if (!ensure_(need, 0, 0, err)) return false;
-    if ((size_t)pl.m_tiles * pl.n_tiles > _n_counters) {
-      if (err) *err = "split-K: too many tiles for the counter array";
-      return false;
-    }
-  }
   ltx::GemmLaunch L;
   L.mode = mode;
   L.tn = pl.tn;
@@ -225,8 +193,6 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.bias = bias;
   p.gate = gate;
   p.y = y;
-  p.ws = _ws;
-  p.counters = _counters;
   p.sx = sx;
   p.sw = sw;
   p.err = _err_word;
@@ -272,7 +238,7 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
   }
   if (i8_takes(M, K, N)) {
     if (!prepare_i8(const_cast<QWeight&>(w), s, err)) return false;
-    if (!ensure_(0, (size_t)M * K, 0, err)) return false;
+    if (!ensure_((size_t)M * K, 0, err)) return false;
     if (ltx::launch_quant_rows_i8(x, M, K, ldx, K, _xq, _sx, s) != 0) {
       if (err) *err = "int8 activation quantize launch failed";
       return false;
@@ -281,7 +247,7 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
                  N, epi, gate, _sx, w.sw, err);
   }
   if (_route == Route::DequantOnce) {
-    if (!ensure_(0, 0, (size_t)N * K * 2, err)) return false;
+    if (!ensure_(0, (size_t)N * K * 2, err)) return false;
     if (ltx::launch_dequant_w8(w.codes, w.sz, N, K, _deq, s) != 0) {
       if (err) *err = "dequant launch failed";
       return false;
@@ -301,7 +267,6 @@ int CudaOps::check(cudaStream_t s, std::string* err) const
   if (!cuda_ok(cudaStreamSynchronize(s), "check", err)) return -1;
   if (h != 0) {
     cudaMemsetAsync(_err_word, 0, sizeof(int), s);
-    if (_counters) cudaMemsetAsync(_counters, 0, _n_counters * sizeof(int), s);
     cudaStreamSynchronize(s);
     if (err) *err = "a kernel gave up on a bounded wait (code " + std::to_string(h) + ")";
   }

@@ -76,8 +76,7 @@ public:
   int check(cudaStream_t s, std::string* err) const;
 
 private:
-  bool ensure_(size_t ws_bytes, size_t i8_bytes, size_t deq_bytes,
-               std::string* err);
+  bool ensure_(size_t i8_bytes, size_t deq_bytes, std::string* err);
   bool gemm_(cudaStream_t s, int mode, const void* x, int ldx,
              const void* wptr, const uint32_t* sz, const __nv_bfloat16* bias,
              __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
@@ -91,12 +90,8 @@ private:
   bool _sage = false;
   int _sage_dense = 0;
 
-  // Scratch arena: split-K partials + tile counters, the int8 tier's
-  // quantized activations, the dequant-once expansion.
-  float* _ws = nullptr;
-  size_t _ws_bytes = 0;
-  int* _counters = nullptr;
-  size_t _n_counters = 0;
+  // Scratch arena: the int8 tier's quantized activations and the
+  // dequant-once expansion.
   int8_t* _xq = nullptr;
   float* _sx = nullptr;
   size_t _xq_bytes = 0;

@@ -48,6 +48,7 @@ SIGNATURES = {
     "ltx_i8_takes": (_I, [_P, _I, _I, _I]),
     "ltx_dequant": (_I, [_P, _P, _P, _P]),
     "ltx_quant_rows_i8": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
+    "ltx_pack_w8g64": (_I, [_P, _P, _I, _I, _P, _P, _P, _P]),
 }
 
 
@@ -218,3 +219,18 @@ def quant_rows_i8(ctx, x, group, stream=None):
     ctx._ok(ctx.lib.ltx_quant_rows_i8(ctx.h, _ptr(x), rows, K, group, _ptr(q),
                                       _ptr(s), _stream(stream)), "quant_rows_i8")
     return q, s
+
+
+def pack_w8g64(ctx, w, stream=None):
+    """w8g64-pack a device f32 [N][K] weight on the GPU.  Returns device
+    tensors (codes int32 [N][K/4] holding the u32 words, scales and
+    zero-points as bf16-bit int16 [N][K/64])."""
+    import torch
+    N, K = w.shape
+    codes = torch.empty((N, K // 4), dtype=torch.int32, device=w.device)
+    scales = torch.empty((N, K // 64), dtype=torch.int16, device=w.device)
+    biases = torch.empty((N, K // 64), dtype=torch.int16, device=w.device)
+    ctx._ok(ctx.lib.ltx_pack_w8g64(ctx.h, _ptr(w.contiguous()), N, K, _ptr(codes),
+                                   _ptr(scales), _ptr(biases), _stream(stream)),
+            "pack_w8g64")
+    return codes, scales, biases
