@@ -86,6 +86,15 @@ LTX_API int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k);
  * (the reference's wait_ok(), src/ltx25-dit.cc:1920-1931). */
 LTX_API int ltx_ctx_check(ltx_ctx* ctx, void* stream);
 
+/* Diagnostics (the reference's VPIPE_LTX25_BLOCK_PROFILE role, src/
+ * ltx25-dit.cc:1597-1598): every following GEMM launch writes 16 u64 per
+ * CTA for its first `max_ctas` CTAs into the device buffer `buf` -- SM
+ * clock64 stamps of its phases (entry, setup, first/last TMA, first
+ * dequant, first/last MMA, epilogue, end) and the MMA issuer's cumulative
+ * wait cycles on loads, on dequantized operands and on the accumulator.
+ * NULL turns it off. */
+LTX_API int ltx_ctx_set_trace(ltx_ctx* ctx, void* buf, int max_ctas);
+
 /* ---- weights ----------------------------------------------------------
  * Replaces QWeight + bind_qlinear / need_q_ (src/ltx25-metal-ops.h:45-57,
  * src/ltx25-dit-weights.h:170-175, src/ltx25-dit-weights.cc:352-403).

@@ -81,15 +81,18 @@ __device__ __forceinline__ uint32_t epi_pair(float a, float b, int n,
 
 }  // namespace
 
-template <int MODE, int TN, int EPI>
-__global__ void __launch_bounds__(320, 1)
+template <int MODE, int TN, int EPI, bool PAIR>
+__global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_sz, GemmParams p)
 {
-  using C = GemmCfg<MODE, TN>;
+  using C = GemmCfg<MODE, TN, PAIR>;
   constexpr int S = C::kStages;
   constexpr int A = C::kASlots > 0 ? C::kASlots : 1;
+  constexpr int kDeqWarps = 8;
+  constexpr int kWT = PAIR ? 2 * C::kBM : C::kBM;   // weight rows per tile
+  static_assert(!PAIR || MODE == MODE_W8G64, "pairs run the w8g64 path");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -99,8 +102,9 @@ __global__ void __launch_bounds__(320, 1)
   uint32_t* s_sz = reinterpret_cast<uint32_t*>(s_w + S * C::kWStage);
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       reinterpret_cast<uint8_t*>(s_sz) + S * C::kSZStage);
-  uint64_t* full = bars;
-  uint64_t* empty = full + S;
+  uint64_t* full = bars;            // X (+ codes, scales when !PAIR)
+  uint64_t* cfull = full + S;       // PAIR: this CTA's codes + scales
+  uint64_t* empty = cfull + S;
   uint64_t* afull = empty + S;
   uint64_t* aempty = afull + A;
   uint64_t* accfull = aempty + A;
@@ -111,19 +115,28 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const int unit0 = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+  const int unit_step = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+  unsigned long long* tr = (p.trace != nullptr && (int)blockIdx.x < p.trace_ctas)
+                               ? p.trace + (size_t)blockIdx.x * kTraceSlots
+                               : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[TR_ENTRY] = clock64();
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
+      mbar_init(&cfull[i], 1);
       mbar_init(&empty[i], MODE == MODE_W8G64 ? 5 : 1);
     }
     for (int i = 0; i < A; ++i) {
-      mbar_init(&afull[i], 4);
+      mbar_init(&afull[i], PAIR ? 8 : 4);
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
-      mbar_init(&accempty[i], 4);
+      mbar_init(&accempty[i], PAIR ? 16 : 8);
     }
     mbar_init(drain, 1);
     *s_abort = 0;
@@ -135,13 +148,20 @@ __global__ void __launch_bounds__(320, 1)
     if constexpr (MODE == MODE_W8G64) tma_prefetch_desc(&tm_sz);
   }
   if (warp == 1) {
-    tmem_alloc(s_tmem, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(s_tmem, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(s_tmem, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();   // peer barriers live before use
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  if (tr != nullptr && threadIdx.x == 0) tr[TR_SETUP] = clock64();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
@@ -149,24 +169,42 @@ __global__ void __launch_bounds__(320, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_par = 0;   // per-stage: armed once / parity
-      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      unsigned long long w_empty = 0;
+      bool first = true;
+      for (int t = unit0; t < p.num_tiles; t += unit_step) {
         int mt, nt, kb0, kb1;
         decode_tile(p, t, mt, nt, kb0, kb1);
+        const int wrow0 = nt * kWT + rank * C::kBM;
+        const int xrow0 = mt * TN + rank * C::kXRows;
         for (int kb = kb0; kb < kb1; ++kb) {
+          const unsigned long long c0 = tr ? clock64() : 0ull;
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, p.err,
                          KERR_WAIT_PRODUCER))
             goto producer_done;
-          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          if (tr) w_empty += clock64() - c0;
           armed |= 1u << stage;
           armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
           const int kx = kb * C::kKPerStage;
-          tma_load_2d(&tm_x, &full[stage], s_x + stage * C::kXStage, kx,
-                      mt * TN);
-          tma_load_2d(&tm_w, &full[stage], s_w + stage * C::kWStage, kx,
-                      nt * C::kBM);
-          if constexpr (MODE == MODE_W8G64) {
-            tma_load_2d(&tm_sz, &full[stage], s_sz + stage * C::kBM,
-                        nt * C::kBM, kb);
+          if constexpr (PAIR) {
+            // Both halves of the activation tile complete on the leader's
+            // barrier (it arms them); the codes on this CTA's own.
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kXStage);
+            mbar_arrive_expect_tx(&cfull[stage], C::kWStage + C::kSZStage);
+            tma_load_2d_pair(&tm_x, mapa_shared(smem_u32(&full[stage]), 0),
+                             s_x + stage * C::kXStage, kx, xrow0);
+            tma_load_2d(&tm_w, &cfull[stage], s_w + stage * C::kWStage, kx, wrow0);
+            tma_load_2d(&tm_sz, &cfull[stage], s_sz + stage * C::kBM, wrow0, kb);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+            tma_load_2d(&tm_x, &full[stage], s_x + stage * C::kXStage, kx, xrow0);
+            tma_load_2d(&tm_w, &full[stage], s_w + stage * C::kWStage, kx, wrow0);
+            if constexpr (MODE == MODE_W8G64) {
+              tma_load_2d(&tm_sz, &full[stage], s_sz + stage * C::kBM, wrow0, kb);
+            }
+          }
+          if (tr && first) {
+            tr[TR_FIRST_TMA] = clock64();
+            first = false;
           }
           if (++stage == S) {
             stage = 0;
@@ -175,37 +213,61 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     producer_done:
-      // Let every load this CTA issued land before the CTA can exit.
+      if (tr) {
+        tr[TR_LAST_TMA] = clock64();
+        tr[TR_PROD_WAIT_EMPTY] = w_empty;
+      }
+      // Let every load this CTA tracks land before the CTA can exit (in a
+      // pair, the activation halves are tracked by the leader's MMA).
       for (int s = 0; s < S; ++s) {
         if (armed & (1u << s)) {
           volatile int no_abort = 0;
-          mbar_wait(&full[s], (armed_par >> s) & 1u, &no_abort, p.err,
-                    KERR_DRAIN);
+          mbar_wait(PAIR ? &cfull[s] : &full[s], (armed_par >> s) & 1u,
+                    &no_abort, p.err, KERR_DRAIN);
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
-    if (lane == 0) {
-      constexpr uint32_t idesc =
-          MODE == MODE_I8 ? idesc_s8(C::kBM, TN) : idesc_bf16(C::kBM, TN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = MODE == MODE_I8
+                                     ? idesc_s8(C::kBM, TN)
+                                     : idesc_bf16(PAIR ? 2 * C::kBM : C::kBM, TN);
       int stage = 0, aslot = 0, acc = 0;
       uint32_t phase = 0, aphase = 0, accphase = 0;
-      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      unsigned long long w_full = 0, w_a = 0, w_acc = 0, n_tiles = 0;
+      bool first = true;
+      for (int t = unit0; t < p.num_tiles; t += unit_step) {
         int mt, nt, kb0, kb1;
         decode_tile(p, t, mt, nt, kb0, kb1);
+        ++n_tiles;
+        unsigned long long c0 = tr ? clock64() : 0ull;
         if (!mbar_wait(&accempty[acc], accphase ^ 1, s_abort, p.err,
                        KERR_WAIT_MMA))
           goto mma_done;
+        if (tr) w_acc += clock64() - c0;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * TN);
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (tr) c0 = clock64();
           if (!mbar_wait(&full[stage], phase, s_abort, p.err, KERR_WAIT_MMA))
             goto mma_done;
+          if (tr) {
+            const unsigned long long c1 = clock64();
+            w_full += c1 - c0;
+            c0 = c1;
+          }
           if constexpr (MODE == MODE_W8G64) {
             if (!mbar_wait(&afull[aslot], aphase, s_abort, p.err,
                            KERR_WAIT_MMA))
               goto mma_done;
+          }
+          if (tr) {
+            w_a += clock64() - c0;
+            if (first) {
+              tr[TR_FIRST_MMA] = clock64();
+              first = false;
+            }
           }
           tc_fence_after();
           const uint64_t bdesc =
@@ -213,7 +275,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
-            if constexpr (MODE == MODE_W8G64) {
+            if constexpr (PAIR) {
+              umma_f16_ts_pair(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
+                               bdesc + (uint64_t)(2 * kk), idesc, accum);
+            } else if constexpr (MODE == MODE_W8G64) {
               umma_f16_ts(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
                           bdesc + (uint64_t)(2 * kk), idesc, accum);
             } else {
@@ -228,9 +293,16 @@ __global__ void __launch_bounds__(320, 1)
               }
             }
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) {
+            umma_commit_pair(smem_u32(&empty[stage]));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+            umma_commit_pair(smem_u32(&aempty[aslot]));
+            umma_commit_pair(mapa_shared(smem_u32(&aempty[aslot]), 1));
+          } else {
+            umma_commit(&empty[stage]);
+            if constexpr (MODE == MODE_W8G64) umma_commit(&aempty[aslot]);
+          }
           if constexpr (MODE == MODE_W8G64) {
-            umma_commit(&aempty[aslot]);
             if (++aslot == C::kASlots) {
               aslot = 0;
               aphase ^= 1;
@@ -241,34 +313,68 @@ __global__ void __launch_bounds__(320, 1)
             phase ^= 1;
           }
         }
-        umma_commit(&accfull[acc]);
+        if constexpr (PAIR) {
+          umma_commit_pair(smem_u32(&accfull[acc]));
+          umma_commit_pair(mapa_shared(smem_u32(&accfull[acc]), 1));
+        } else {
+          umma_commit(&accfull[acc]);
+        }
         if (++acc == C::kNAcc) {
           acc = 0;
           accphase ^= 1;
         }
       }
     mma_done:
+      if (tr) {
+        tr[TR_LAST_COMMIT] = clock64();
+        tr[TR_MMA_WAIT_FULL] = w_full;
+        tr[TR_MMA_WAIT_A] = w_a;
+        tr[TR_MMA_WAIT_ACC] = w_acc;
+        tr[TR_TILES] = n_tiles;
+      }
       // Every MMA issued above has completed once `drain` flips.
-      umma_commit(drain);
+      if constexpr (PAIR) {
+        umma_commit_pair(smem_u32(drain));
+      } else {
+        umma_commit(drain);
+      }
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, p.err, KERR_DRAIN);
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + kDeqWarps) {
     // ------------------------------------------------------------ dequant
+    // Two groups of four warps (one warp per TMEM lane quarter each) take
+    // alternate k-blocks: codes from shared memory -> bf16 -> TMEM A slot.
     if constexpr (MODE == MODE_W8G64) {
       const int q = warp & 3;                 // TMEM lane quarter
+      const int grp = (warp - 2) >> 2;        // 0: even blocks, 1: odd
       const int r = q * 32 + (int)lane;       // weight row within the tile
       const int sw = (r >> 1) & 3;            // TMA SWIZZLE_64B chunk xor
       const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-      int stage = 0, aslot = 0;
-      uint32_t phase = 0, aphase = 0;
-      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      uint64_t* cbar = PAIR ? cfull : full;
+      int seq = 0;                            // CTA-wide k-block sequence
+      const bool tw = tr != nullptr && warp == 2 && lane == 0;
+      unsigned long long d_full = 0, d_load = 0, d_math = 0, d_st = 0,
+                         d_ae = 0, d_blocks = 0;
+      for (int t = unit0; t < p.num_tiles; t += unit_step) {
         int mt, nt, kb0, kb1;
         decode_tile(p, t, mt, nt, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, s_abort, p.err,
+        for (int kb = kb0; kb < kb1; ++kb, ++seq) {
+          if ((seq & 1) != grp) continue;
+          const int stage = seq % S;
+          const uint32_t phase = (uint32_t)(seq / S) & 1u;
+          const int aslot = seq % C::kASlots;
+          const uint32_t aphase = (uint32_t)(seq / C::kASlots) & 1u;
+          unsigned long long c0 = tw ? clock64() : 0ull;
+          if (!mbar_wait(&cbar[stage], phase, s_abort, p.err,
                          KERR_WAIT_DEQUANT))
             goto deq_done;
+          if (tr && warp == 2 && lane == 0 && seq == 0) tr[TR_FIRST_FULL_DEQ] = clock64();
+          if (tw) {
+            const unsigned long long c1 = clock64();
+            d_full += c1 - c0;
+            c0 = c1;
+          }
           const uint8_t* rowp = s_w + stage * C::kWStage + r * 64;
           uint4 c[4];
 #pragma unroll
@@ -277,6 +383,11 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t sz = s_sz[stage * C::kBM + r];
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[stage]);
+          if (tw) {
+            const unsigned long long c1 = clock64();
+            d_load += c1 - c0;
+            c0 = c1;
+          }
           const uint32_t s2 = __byte_perm(sz, 0, 0x1010);
           const uint32_t z2 = __byte_perm(sz, 0, 0x3232);
           uint32_t out[32];
@@ -289,58 +400,100 @@ __global__ void __launch_bounds__(320, 1)
               out[j * 8 + u * 2 + 1] = deq_pair(w4[u], 2, 3, s2, z2);
             }
           }
+          if (tw) {
+            const unsigned long long c1 = clock64();
+            d_math += c1 - c0;
+            c0 = c1;
+          }
           if (!mbar_wait(&aempty[aslot], aphase ^ 1, s_abort, p.err,
                          KERR_WAIT_DEQUANT))
             goto deq_done;
+          if (tw) {
+            const unsigned long long c1 = clock64();
+            d_ae += c1 - c0;
+            c0 = c1;
+          }
           tc_fence_after();
           tmem_st32(tmem + lane_base + (uint32_t)(C::kACol0 + aslot * 32), out);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[aslot]);
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1;
+          if (lane == 0) {
+            if constexpr (PAIR) {
+              mbar_arrive_cluster(mapa_shared(smem_u32(&afull[aslot]), 0));
+            } else {
+              mbar_arrive(&afull[aslot]);
+            }
           }
-          if (++aslot == C::kASlots) {
-            aslot = 0;
-            aphase ^= 1;
+          if (tw) {
+            d_st += clock64() - c0;
+            ++d_blocks;
           }
         }
       }
-    deq_done:;
+    deq_done:
+      if (tw) {
+        tr[TR_DEQ_WAIT_FULL] = d_full;
+        tr[TR_DEQ_LOAD] = d_load;
+        tr[TR_DEQ_MATH] = d_math;
+        tr[TR_DEQ_WAIT_ST] = d_st;
+        tr[TR_DEQ_WAIT_AEMPTY] = d_ae;
+        tr[TR_DEQ_BLOCKS] = d_blocks;
+      }
     }
   } else {
     // ----------------------------------------------------------- epilogue
+    // Two groups of four warps (one per lane quarter) drain alternate
+    // 32-column chunks, halving the time the accumulator is held.
     const int q = warp & 3;
+    const int egrp = (warp - 2 - kDeqWarps) >> 2;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     int acc = 0;
     uint32_t accphase = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+    const bool te = tr != nullptr && warp == 2 + kDeqWarps && lane == 0;
+    unsigned long long e_wait = 0, e_work = 0;
+    for (int t = unit0; t < p.num_tiles; t += unit_step) {
       int mt, nt, kb0, kb1;
       decode_tile(p, t, mt, nt, kb0, kb1);
+      unsigned long long ce = te ? clock64() : 0ull;
       if (!mbar_wait(&accfull[acc], accphase, s_abort, p.err,
                      KERR_WAIT_EPILOGUE))
         goto epi_done;
+      if (te) {
+        const unsigned long long c1 = clock64();
+        e_wait += c1 - ce;
+        ce = c1;
+      }
+      if (tr && warp == 2 + kDeqWarps && lane == 0 && t == unit0)
+        tr[TR_FIRST_ACC] = clock64();
       tc_fence_after();
       // Pair layout: lanes (2i, 2i+1) own features (n, n+1); the even lane
       // writes even tokens, the odd lane odd tokens.
-      const int n_pair = nt * C::kBM + q * 32 + (int)(lane & ~1u);
+      const int nrow = nt * kWT + rank * C::kBM + q * 32;
+      const int n_pair = nrow + (int)(lane & ~1u);
       const int odd = (int)(lane & 1u);
       float csx = 1.0f;
       if constexpr (MODE == MODE_I8) {
-        const int nn = nt * C::kBM + q * 32 + (int)lane;
+        const int nn = nrow + (int)lane;
         csx = nn < p.N ? p.sw[nn] : 0.0f;
       }
+      constexpr int kChunks = TN / 32;
+      const int c_last = ((kChunks - 1 - egrp) / 2) * 2 + egrp;
 #pragma unroll 1
-      for (int c = 0; c < TN / 32; ++c) {
+      for (int c = egrp; c < kChunks; c += 2) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + (uint32_t)(acc * TN + c * 32), v);
         tmem_wait_ld();
-        if (c == TN / 32 - 1) {
+        if (c == c_last) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&accempty[acc]);
+          if (lane == 0) {
+            if constexpr (PAIR) {
+              mbar_arrive_cluster(mapa_shared(smem_u32(&accempty[acc]), 0));
+            } else {
+              mbar_arrive(&accempty[acc]);
+            }
+          }
         }
         float f[32];
 #pragma unroll
@@ -352,7 +505,7 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         const int j0 = mt * TN + c * 32;
-        if (p.splits > 1) {
+        if (!PAIR && p.splits > 1) {
           // K-split partial: park it in this CTA's shared memory as
           // red[token][feature] f32 (the pipeline buffers are idle now);
           // the cluster reduces it after the role loops.
@@ -378,9 +531,9 @@ __global__ void __launch_bounds__(320, 1)
           float b = odd ? f[2 * k + 1] : recv;       // feature n_pair + 1
           const int j = j0 + 2 * k + odd;
           if constexpr (MODE == MODE_I8) {
-            const float s = j < p.M ? p.sx[j] : 0.0f;
-            a *= s;
-            b *= s;
+            const float sj = j < p.M ? p.sx[j] : 0.0f;
+            a *= sj;
+            b *= sj;
           }
           if (j < p.M && n_pair < p.N) {
             __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
@@ -389,27 +542,33 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
+      if (te) e_work += clock64() - ce;
       if (++acc == C::kNAcc) {
         acc = 0;
         accphase ^= 1;
       }
     }
-  epi_done:;
+  epi_done:
+    if (te) {
+      tr[TR_EPI_WAIT] = e_wait;
+      tr[TR_EPI_WORK] = e_work;
+      tr[TR_EPI_DONE] = clock64();
+    }
   }
 
   tc_fence_before();
   __syncthreads();
 
-  if (p.splits > 1) {
+  if (!PAIR && p.splits > 1) {
     // One cluster per output tile, one CTA per K split (cluster rank ==
     // split).  Each CTA reduces a band of token rows across the cluster's
     // partials through DSMEM, in rank order, and stores the bf16 result.
     cluster_sync_all();
     int mt, nt, kb0, kb1;
     decode_tile(p, blockIdx.x, mt, nt, kb0, kb1);
-    const int rank = (int)cluster_ctarank();
+    const int crank = (int)cluster_ctarank();
     const int per = (TN + p.splits - 1) / p.splits;
-    const int r0 = rank * per;
+    const int r0 = crank * per;
     const int r1 = min(TN, r0 + per);
     const uint32_t red = smem_u32(s_x);
     for (int idx = threadIdx.x; idx < (r1 - r0) * (C::kBM / 4); idx += blockDim.x) {
@@ -419,28 +578,44 @@ __global__ void __launch_bounds__(320, 1)
       const int n = nt * C::kBM + c4;
       if (j >= p.M || n >= p.N) continue;
       const uint32_t off = (uint32_t)((jl * C::kBM + c4) * 4);
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp = 0; sp < p.splits; ++sp) {
-        const float4 v = ld_dsmem_f4(mapa_shared(red + off, (uint32_t)sp));
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
+      float4 v[8];
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp)
+        if (sp < p.splits) v[sp] = ld_dsmem_f4(mapa_shared(red + off, (uint32_t)sp));
+      float4 sum = v[0];
+#pragma unroll
+      for (int sp = 1; sp < 8; ++sp) {
+        if (sp < p.splits) {
+          sum.x += v[sp].x;
+          sum.y += v[sp].y;
+          sum.z += v[sp].z;
+          sum.w += v[sp].w;
+        }
       }
       __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
-      const uint32_t o0 = epi_pair<EPI>(s.x, s.y, n, p, yrow);
-      const uint32_t o1 = epi_pair<EPI>(s.z, s.w, n + 2, p, yrow);
+      const uint32_t o0 = epi_pair<EPI>(sum.x, sum.y, n, p, yrow);
+      const uint32_t o1 = epi_pair<EPI>(sum.z, sum.w, n + 2, p, yrow);
       *reinterpret_cast<uint32_t*>(yrow + n) = o0;
       *reinterpret_cast<uint32_t*>(yrow + n + 2) = o1;
     }
     // Peers may still be reading this CTA's partial: leave together.
     cluster_sync_all();
   }
-
+  if constexpr (PAIR) {
+    // The leader's MMAs read this CTA's shared memory and write its TMEM;
+    // they have drained, and no remote arrive is left in flight after this.
+    cluster_sync_all();
+  }
+  if (tr != nullptr && threadIdx.x == 0) tr[TR_REDUCED] = clock64();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem, 512);
+    } else {
+      tmem_dealloc(tmem, 512);
+    }
+    if (tr != nullptr && lane == 0) tr[TR_END] = clock64();
   }
 }
 
@@ -475,23 +650,23 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* gaddr,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MODE, int TN, int EPI>
+template <int MODE, int TN, int EPI, bool PAIR>
 int launch_t(const GemmLaunch& L, cudaStream_t stream)
 {
-  using C = GemmCfg<MODE, TN>;
+  using C = GemmCfg<MODE, TN, PAIR>;
   CUtensorMap tx, tw, tsz;
   memset(&tsz, 0, sizeof(tsz));
   const GemmParams& p = L.p;
   if (MODE == MODE_I8) {
     if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.x, p.K, p.M, L.ldx,
-                   128, TN, CU_TENSOR_MAP_SWIZZLE_128B))
+                   128, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
     if (!encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.w, p.K, p.N, p.K,
                    128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
   } else {
     if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, L.x, p.K, p.M,
-                   (uint64_t)L.ldx * 2, 64, TN, CU_TENSOR_MAP_SWIZZLE_128B))
+                   (uint64_t)L.ldx * 2, 64, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
     if (MODE == MODE_W8G64) {
       if (!encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.w, p.K, p.N, p.K,
@@ -507,7 +682,7 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
         return -1;
     }
   }
-  auto kern = gemm_tc_kernel<MODE, TN, EPI>;
+  auto kern = gemm_tc_kernel<MODE, TN, EPI, PAIR>;
   static bool attr_done = false;
   if (!attr_done) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -515,17 +690,29 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
       return -2;
     attr_done = true;
   }
-  if (p.splits > 1) {
+  int cluster = 1;
+  int grid = p.num_tiles < L.num_sms ? p.num_tiles : L.num_sms;
+  if (PAIR) {
+    // One cluster of two CTAs per output tile, persistent over tiles.
+    if (p.splits != 1) return -5;
+    const int pairs = p.num_tiles < L.num_sms / 2 ? p.num_tiles : L.num_sms / 2;
+    grid = 2 * pairs;
+    cluster = 2;
+  } else if (p.splits > 1) {
     // One cluster of `splits` CTAs per output tile, one unit per CTA.
     if (p.num_tiles > L.num_sms || p.splits > 8) return -5;
+    grid = p.num_tiles;
+    cluster = p.splits;
+  }
+  if (cluster > 1) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)p.num_tiles, 1, 1);
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
     cfg.blockDim = dim3(C::kThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)p.splits;
+    attr[0].val.clusterDim.x = (unsigned)cluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
@@ -533,18 +720,17 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
     if (cudaLaunchKernelEx(&cfg, kern, tx, tw, tsz, p) != cudaSuccess) return -3;
     return 0;
   }
-  const int grid = p.num_tiles < L.num_sms ? p.num_tiles : L.num_sms;
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, tsz, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-template <int MODE, int TN>
+template <int MODE, int TN, bool PAIR>
 int launch_epi(const GemmLaunch& L, cudaStream_t stream)
 {
   switch (L.epi) {
-    case EPI_STORE: return launch_t<MODE, TN, EPI_STORE>(L, stream);
-    case EPI_GELU: return launch_t<MODE, TN, EPI_GELU>(L, stream);
-    case EPI_GATED_RES: return launch_t<MODE, TN, EPI_GATED_RES>(L, stream);
+    case EPI_STORE: return launch_t<MODE, TN, EPI_STORE, PAIR>(L, stream);
+    case EPI_GELU: return launch_t<MODE, TN, EPI_GELU, PAIR>(L, stream);
+    case EPI_GATED_RES: return launch_t<MODE, TN, EPI_GATED_RES, PAIR>(L, stream);
   }
   return -4;
 }
@@ -552,10 +738,14 @@ int launch_epi(const GemmLaunch& L, cudaStream_t stream)
 template <int MODE>
 int launch_tn(const GemmLaunch& L, cudaStream_t stream)
 {
+  if constexpr (MODE == MODE_W8G64) {
+    if (L.pair) return L.tn == 256 ? launch_epi<MODE, 256, true>(L, stream) : -4;
+  } else {
+    if (L.pair) return -4;
+  }
   switch (L.tn) {
-    case 128: return launch_epi<MODE, 128>(L, stream);
-    case 192: return launch_epi<MODE, 192>(L, stream);
-    case 256: return launch_epi<MODE, 256>(L, stream);
+    case 128: return launch_epi<MODE, 128, false>(L, stream);
+    case 256: return launch_epi<MODE, 256, false>(L, stream);
   }
   return -4;
 }
@@ -566,13 +756,10 @@ int gemm_smem_bytes(int mode, int tn)
 {
   switch (mode * 1000 + tn) {
     case MODE_W8G64 * 1000 + 128: return GemmCfg<MODE_W8G64, 128>::kSmemBytes;
-    case MODE_W8G64 * 1000 + 192: return GemmCfg<MODE_W8G64, 192>::kSmemBytes;
     case MODE_W8G64 * 1000 + 256: return GemmCfg<MODE_W8G64, 256>::kSmemBytes;
     case MODE_BF16 * 1000 + 128: return GemmCfg<MODE_BF16, 128>::kSmemBytes;
-    case MODE_BF16 * 1000 + 192: return GemmCfg<MODE_BF16, 192>::kSmemBytes;
     case MODE_BF16 * 1000 + 256: return GemmCfg<MODE_BF16, 256>::kSmemBytes;
     case MODE_I8 * 1000 + 128: return GemmCfg<MODE_I8, 128>::kSmemBytes;
-    case MODE_I8 * 1000 + 192: return GemmCfg<MODE_I8, 192>::kSmemBytes;
     case MODE_I8 * 1000 + 256: return GemmCfg<MODE_I8, 256>::kSmemBytes;
   }
   return -1;

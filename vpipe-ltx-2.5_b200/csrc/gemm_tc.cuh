@@ -20,11 +20,18 @@
 // MMA instead of padding 126 rows up to a 128-row M tile, and the epilogue
 // thread that owns TMEM lane n owns output feature n for every token.
 //
-// Warp roles (320 threads):
-//   warp 0     TMA producer (one elected lane)
-//   warp 1     TMEM allocator + MMA issuer (one elected lane)
-//   warps 2-5  dequant (MODE_W8G64 only): TMEM lane quarter warp%4
-//   warps 6-9  epilogue: TMEM -> registers -> bias/act/residual -> global
+// Warp roles (576 threads):
+//   warp 0       TMA producer (one elected lane)
+//   warp 1       TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-9    dequant (MODE_W8G64 only): two groups of four, one warp per
+//                TMEM lane quarter (warp % 4), alternating k-blocks
+//   warps 10-17  epilogue: two groups of four, alternating 32-column chunks;
+//                TMEM -> registers -> bias/act/residual -> global
+//
+// Large token counts run as CTA PAIRS (cta_group::2, a cluster of two):
+// one M = 256 MMA spans 256 weight rows, each CTA dequantizing its 128 into
+// its own TMEM and holding half of the 256-token activation tile, so each
+// SM streams half the activation bytes per FLOP of a single-CTA tile.
 //
 // K is split across CTAs (`splits` > 1, at most 8) for the small-M,
 // bandwidth-bound shapes.  The splits of one output tile are launched as
@@ -64,12 +71,33 @@ struct GemmParams {
   const float* sx;             // MODE_I8: [M] token scales
   const float* sw;             // MODE_I8: [N] channel scales
   int* err;                    // device error word (0 = ok)
+  // Diagnostics (null = off): kTraceSlots u64 per CTA for the first
+  // `trace_ctas` CTAs -- phase timestamps (clock64) and the MMA issuer's
+  // cumulative wait cycles per barrier kind.
+  unsigned long long* trace;
+  int trace_ctas;
 };
 
-template <int MODE, int TN>
+constexpr int kTraceSlots = 24;
+enum TraceSlot : int {
+  TR_ENTRY = 0, TR_SETUP, TR_FIRST_TMA, TR_LAST_TMA, TR_FIRST_FULL_DEQ,
+  TR_FIRST_MMA, TR_LAST_COMMIT, TR_FIRST_ACC, TR_EPI_DONE, TR_REDUCED,
+  TR_END, TR_TILES, TR_MMA_WAIT_FULL, TR_MMA_WAIT_A, TR_MMA_WAIT_ACC,
+  TR_PROD_WAIT_EMPTY,
+  // dequant warp 2, lane 0: cumulative cycles
+  TR_DEQ_WAIT_FULL, TR_DEQ_LOAD, TR_DEQ_MATH, TR_DEQ_WAIT_ST,
+  TR_DEQ_WAIT_AEMPTY, TR_DEQ_BLOCKS,
+  // first epilogue warp, lane 0: cumulative cycles waiting / working
+  TR_EPI_WAIT, TR_EPI_WORK
+};
+
+template <int MODE, int TN, bool PAIR = false>
 struct GemmCfg {
-  static constexpr int kBM = 128;                       // weight rows / tile
-  static constexpr int kXStage = TN * 128;               // 128 B of K per row
+  static constexpr int kBM = 128;                       // weight rows / CTA
+  // Activation rows per CTA: a pair splits the TN-token tile between its
+  // two CTAs (each holds half of the MMA's B operand).
+  static constexpr int kXRows = PAIR ? TN / 2 : TN;
+  static constexpr int kXStage = kXRows * 128;           // 128 B of K per row
   static constexpr int kWStage = MODE == MODE_W8G64 ? kBM * 64 : kBM * 128;
   static constexpr int kSZStage = MODE == MODE_W8G64 ? kBM * 4 : 0;
   static constexpr int kStageBytes = kXStage + kWStage + kSZStage;
@@ -82,13 +110,15 @@ struct GemmCfg {
       MODE == MODE_W8G64 ? (kASlotsRaw > 8 ? 8 : kASlotsRaw) : 0;
   static constexpr int kACol0 = kNAcc * TN;              // first A column
   static constexpr int kKPerStage = MODE == MODE_I8 ? 128 : 64;  // elements
-  static constexpr int kThreads = 320;
-  static constexpr int kNumBars = 2 * kStages + 2 * (kASlots > 0 ? kASlots : 1) + 2 * 2 + 1;
+  static constexpr int kThreads = 576;   // 18 warps, see the role table
+  static constexpr int kNumBars =
+      3 * kStages + 2 * (kASlots > 0 ? kASlots : 1) + 2 * 2 + 1;
   static constexpr int kSmemBytes =
       1024 + kStages * kStageBytes + kNumBars * 8 + 64;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "MMA N");
   static_assert(kNAcc * TN + kASlots * 32 <= 512, "TMEM budget");
   static_assert(MODE != MODE_W8G64 || kASlots >= 2, "A pipeline depth");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 }  // namespace ltx

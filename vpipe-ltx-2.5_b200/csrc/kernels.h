@@ -22,7 +22,8 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType,
 
 struct GemmLaunch {
   int mode = MODE_W8G64;   // GemmMode
-  int tn = 256;            // token tile: 128, 192 or 256
+  int tn = 256;            // token tile: 128 or 256
+  bool pair = false;       // cta_group::2 pairs (MODE_W8G64, tn 256)
   int epi = EPI_STORE;     // EpiMode
   int num_sms = 148;
   const void* x = nullptr; // bf16 [M][ldx] (int8 for MODE_I8)

@@ -283,6 +283,74 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads)
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ---- cta_group::2 (two SMs per MMA) -----------------------------------------
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols)
+{
+  asm volatile(
+      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst)),
+      "r"(ncols)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+// D (+)= A(tmem) * B(smem), M = 256 across the CTA pair: each CTA's TMEM
+// holds its 128 rows of A and D, each CTA's shared memory its half of B at
+// the same offset.  Issued by the leader CTA only.
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d, uint32_t a_tmem,
+                                                 uint64_t b, uint32_t idesc,
+                                                 uint32_t acc)
+{
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at shared::cluster address `caddr` (this CTA's
+// or the peer's) when the pair MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t caddr)
+{
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(caddr)
+      : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on the mbarrier at shared::cluster address `cbar` -- the leader CTA's.
+__device__ __forceinline__ void tma_load_2d_pair(const void* map, uint32_t cbar,
+                                                 void* dst, int x, int y)
+{
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::"
+      "complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(cbar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Arrive on an mbarrier in another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr)
+{
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
+}
+
 // ---- thread-block clusters (distributed shared memory) -------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank()

@@ -85,6 +85,14 @@ int ltx_ctx_check(ltx_ctx* ctx, void* stream)
   return LTX_OK;
 }
 
+int ltx_ctx_set_trace(ltx_ctx* ctx, void* buf, int max_ctas)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  ctx->ops.set_trace(static_cast<unsigned long long*>(buf),
+                     buf == nullptr ? 0 : max_ctas);
+  return LTX_OK;
+}
+
 int ltx_qweight_upload(ltx_ctx* ctx, const uint32_t* codes, const void* scales,
                        const void* biases, int sb_dtype, int N, int K, int bits,
                        int group, int on_device, ltx_qweight** out)

@@ -3,6 +3,7 @@
 #include "ltx25-cuda-ops.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "../csrc/kernels.h"
@@ -25,6 +26,7 @@ bool aligned(const void* p, size_t a)
 
 struct Plan {
   int tn = 256;
+  bool pair = false;
   int splits = 1;
   int m_tiles = 1, n_tiles = 1, kblocks = 1;
 };
@@ -39,14 +41,33 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
   Plan p;
   const int kpb = mode == ltx::MODE_I8 ? 128 : 64;
   p.kblocks = K / kpb;
-  p.n_tiles = (N + 127) / 128;
   p.tn = M <= 128 ? 128 : 256;
+  // CTA pairs (M = 256 MMA over two SMs) halve the activation bytes each SM
+  // streams per FLOP; measured slower than single CTAs so far (the
+  // cross-CTA hand-off of dequantized A slots), so opt-in for A/B.
+  p.pair = false;
+  if (const char* e = std::getenv("LTX25_FORCE_PAIR")) {
+    p.pair = mode == ltx::MODE_W8G64 && std::atoi(e) != 0 && M > 128;
+  }
+  if (p.pair) p.tn = 256;
+  if (const char* e = std::getenv("LTX25_FORCE_TN")) {
+    const int tn = std::atoi(e);
+    if (!p.pair && (tn == 128 || tn == 256)) p.tn = tn;
+  }
+  p.n_tiles = (N + (p.pair ? 255 : 127)) / (p.pair ? 256 : 128);
   p.m_tiles = (M + p.tn - 1) / p.tn;
   const int tiles = p.m_tiles * p.n_tiles;
   p.splits = 1;
-  if (tiles * 2 <= sms && p.kblocks >= 4) {
+  if (!p.pair && tiles * 2 <= sms && p.kblocks >= 4) {
     p.splits = std::min(std::min(sms / tiles, p.kblocks / 2), 8);
     if (p.splits < 1) p.splits = 1;
+  }
+  // A/B override of the K split (the reference's tile knobs,
+  // src/ltx25-metal-ops.cc:164-231).  Ignored when out of range.
+  if (const char* e = std::getenv("LTX25_FORCE_SPLITS")) {
+    const int sp = std::atoi(e);
+    if (!p.pair && sp >= 1 && sp <= 8 && sp <= p.kblocks && (sp == 1 || tiles * sp <= sms))
+      p.splits = sp;
   }
   return p;
 }
@@ -174,6 +195,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   ltx::GemmLaunch L;
   L.mode = mode;
   L.tn = pl.tn;
+  L.pair = pl.pair;
   L.epi = epi;
   L.num_sms = _sms;
   L.x = x;
@@ -196,6 +218,8 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.sx = sx;
   p.sw = sw;
   p.err = _err_word;
+  p.trace = _trace;
+  p.trace_ctas = _trace_ctas;
   const int rc = ltx::gemm_launch(L, s);
   if (rc != 0) {
     if (err)

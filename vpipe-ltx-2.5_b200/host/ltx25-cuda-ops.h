@@ -72,6 +72,14 @@ public:
   int num_sms() const { return _sms; }
   int* err_word() const { return _err_word; }
 
+  // Diagnostics: every following GEMM writes per-CTA phase timestamps into
+  // `buf` (16 u64 per CTA, first `ctas` CTAs); null turns it off.
+  void set_trace(unsigned long long* buf, int ctas)
+  {
+    _trace = buf;
+    _trace_ctas = ctas;
+  }
+
   // Reads and clears the device error word.  0 when clean.
   int check(cudaStream_t s, std::string* err) const;
 
@@ -98,6 +106,8 @@ private:
   __nv_bfloat16* _deq = nullptr;
   size_t _deq_bytes = 0;
   int* _err_word = nullptr;
+  unsigned long long* _trace = nullptr;
+  int _trace_ctas = 0;
 };
 
 // Upload helpers (the ltx25-dit-weights bind path, src/ltx25-dit-weights.cc:

@@ -35,6 +35,7 @@ SIGNATURES = {
     "ltx_ctx_last_error": (ctypes.c_char_p, [_P]),
     "ltx_ctx_reserve": (_I, [_P, _I, _I, _I]),
     "ltx_ctx_check": (_I, [_P, _P]),
+    "ltx_ctx_set_trace": (_I, [_P, _P, _I]),
     "ltx_qweight_upload": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                                 ctypes.POINTER(_P)]),
     "ltx_dweight_upload": (_I, [_P, _P, _I, _I, _I, ctypes.POINTER(_P)]),
@@ -125,6 +126,12 @@ class Context:
 
     def check(self, stream=None):
         self._ok(self.lib.ltx_ctx_check(self.h, _stream(stream)), "check")
+
+    def set_trace(self, buf=None, max_ctas=0):
+        """Diagnostics: per-CTA phase stamps of every following GEMM into a
+        device int64 tensor [max_ctas][16] (None turns it off)."""
+        self._ok(self.lib.ltx_ctx_set_trace(self.h, _ptr(buf), max_ctas),
+                 "set_trace")
 
     def set_route(self, route):
         self._ok(self.lib.ltx_set_route(self.h, route), "set_route")
