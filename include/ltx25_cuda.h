@@ -106,14 +106,14 @@ LTX_API int ltx_ctx_set_trace(ltx_ctx* ctx, void* buf, int max_ctas);
  * as get_as_bf16_ does, src/ltx25-dit-weights.cc:230-277).
  * `on_device` != 0 means the three pointers are already device memory.
  * Only bits == 8, group == 64 (the w8g64 pack) is accepted; anything else
- * returns LTX_E_UNSUPPORTED.  N must be a multiple of 8, K of 64. */
+ * returns LTX_E_UNSUPPORTED.  N must be a multiple of 4, K of 64. */
 LTX_API int ltx_qweight_upload(ltx_ctx* ctx, const uint32_t* codes,
                        const void* scales, const void* biases, int sb_dtype,
                        int N, int K, int bits, int group, int on_device,
                        ltx_qweight** out);
 
 /* A dense bf16 weight [N][K] (gate logits and any tensor a pack leaves
- * dense; QWeight with quantized == false). */
+ * dense; QWeight with quantized == false).  N even, K a multiple of 64. */
 LTX_API int ltx_dweight_upload(ltx_ctx* ctx, const uint16_t* w_bf16, int N, int K,
                        int on_device, ltx_qweight** out);
 
@@ -132,7 +132,7 @@ LTX_API int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                 const void* bias, void* y, int M, int K, int N, void* stream);
 
 /* The same with explicit row strides and a fused epilogue (LTX_EPI_*).
- * `gate` is [N] bf16 for LTX_EPI_GATED_RES (y += gate * (xW^T + b)), the
+ * `gate` is [N] f32 for LTX_EPI_GATED_RES (y += gate * (xW^T + b)), the
  * reference's linear + gated_residual pair (src/ltx25-metal-ops.cc:
  * 1047-1059) and linear + gelu (src/ltx25-metal-ops.cc:1062-1070). */
 LTX_API int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
@@ -174,6 +174,89 @@ LTX_API int ltx_quant_rows_i8(ltx_ctx* ctx, const void* x, int rows, int K,
 LTX_API int ltx_pack_w8g64(ltx_ctx* ctx, const float* w, int N, int K,
                            uint32_t* codes, uint16_t* scales,
                            uint16_t* biases, void* stream);
+
+/* ---- block op vocabulary ---------------------------------------------
+ * The row ops and attention of the block, exposed one by one (MetalOps::
+ * ada_zero / rms_norm_gain + rope / sdpa_steel + gate_heads,
+ * src/ltx25-metal-ops.h:330-560).  bf16 device tensors, f32 vectors. */
+
+/* out = rms_norm(x) * (1 + scale) + shift (normalize != 0) or
+ * x * (1 + scale) + shift (normalize == 0); scale, shift f32 [dim] or NULL;
+ * eps 1e-6 (src/ltx25-block-ref.cc:134-165). */
+LTX_API int ltx_ada_zero(ltx_ctx* ctx, const void* x, void* out, int rows,
+                         int dim, const float* scale, const float* shift,
+                         int normalize, void* stream);
+
+/* RMSNorm over the whole heads*head_dim row with an f32 gain, then the
+ * split-half RoPE per head with f32 tables [heads][rows][head_dim/2] (NULL:
+ * no rotation).  in has row stride ld_in; out is compact
+ * (src/ltx25-block-ref.cc:31-45, src/ltx25-rope.cc:325-352). */
+LTX_API int ltx_qk_norm_rope(ltx_ctx* ctx, const void* in, int ld_in,
+                             void* out, int rows, int heads, int head_dim,
+                             const float* gain, const float* cos_tab,
+                             const float* sin_tab, void* stream);
+
+/* o = softmax(q k^T / sqrt(D)) v per head, times 2 sigmoid(gate[t][h]) when
+ * gate_logits != NULL.  Token-major: head h at columns [h*D, (h+1)*D).
+ * head_dim 64 or 128 (src/ltx25-block-ref.cc:49-127). */
+LTX_API int ltx_attention(ltx_ctx* ctx, const void* q, int ldq, const void* k,
+                          int ldk, const void* v, int ldv, void* o, int ldo,
+                          const void* gate_logits, int ldg, int tq, int tk,
+                          int heads, int head_dim, void* stream);
+
+/* ---- the joint audio-video block ---------------------------------------
+ * Replaces MetalBlock (src/ltx25-block-metal.h:245-371) with the math of
+ * block_forward (src/ltx25-block-ref.cc:308-389). */
+typedef struct ltx_block ltx_block;
+
+/* One stream's inputs for a forward (GpuStreamInput,
+ * src/ltx25-block-metal.h:70-118).  Device pointers; bf16 unless noted. */
+typedef struct {
+  void* x;                        /* [tokens][dim], UPDATED in place */
+  const void* context;            /* [text_tokens][dim] */
+  const void* timesteps;          /* 9 * dim adaLN driver */
+  const void* cross_scale_shift;  /* 4 * dim */
+  const void* cross_gate;         /* dim */
+  const void* prompt_timestep;    /* 2 * dim, or NULL (static table alone) */
+  const float* pe_cos;            /* self RoPE [heads][tokens][head_dim/2] */
+  const float* pe_sin;
+  const float* cross_pe_cos;      /* a2v/v2a RoPE at the AUDIO width */
+  const float* cross_pe_sin;
+  int tokens;
+  int text_tokens;
+  int present;                    /* 0: stream absent this forward */
+} ltx_stream_io;
+
+LTX_API int ltx_block_create(ltx_ctx* ctx, int video_dim, int video_heads,
+                             int audio_dim, int audio_heads, ltx_block** out);
+LTX_API void ltx_block_destroy(ltx_block* b);
+LTX_API const char* ltx_block_last_error(const ltx_block* b);
+
+/* Stage a tensor under the reference's parameter name
+ * (load_block_weights, src/ltx25-block-ref.cc:424-523): the 28 quantized
+ * linears (`attn1.to_q.weight`, `audio_ff.net.2.weight`, ...) as w8g64
+ * packs (bind_qlinear); every other tensor (biases, q/k norms, gate
+ * logits, adaLN tables) as f32 [rows][cols] (cols 0 for a vector). */
+LTX_API int ltx_block_set_qlinear(ltx_block* b, const char* name,
+                                  const uint32_t* codes, const void* scales,
+                                  const void* biases, int sb_dtype, int N,
+                                  int K, int on_device);
+LTX_API int ltx_block_set_tensor(ltx_block* b, const char* name,
+                                 const float* data, int rows, int cols,
+                                 int on_device);
+
+/* Check every required tensor is present (naming the first missing one,
+ * as load_block_weights does), fuse the q/k/v and k/v packs, upload. */
+LTX_API int ltx_block_finalize(ltx_block* b);
+
+/* Size the block's scratch arena once (MetalBlock::reserve). */
+LTX_API int ltx_block_reserve(ltx_block* b, int max_video_tokens,
+                              int max_audio_tokens, int max_text_tokens);
+
+/* Run the block on `stream`; video->x and audio->x are updated in place
+ * (MetalBlock::forward, src/ltx25-block-metal.h:307-311). */
+LTX_API int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
+                              const ltx_stream_io* audio, void* stream);
 
 #ifdef __cplusplus
 }

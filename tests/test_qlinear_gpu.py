@@ -159,15 +159,16 @@ def test_gated_residual_epilogue(ctx, M):
     xb, codes, scales, biases, _ = make(M, N, K, seed=6)
     rng = np.random.default_rng(2)
     h = lib.f32_to_bf16(rng.standard_normal((M, N)).astype(np.float32))
-    gate = lib.f32_to_bf16((rng.standard_normal(N) * 0.5).astype(np.float32))
+    gate = (rng.standard_normal(N) * 0.5).astype(np.float32)
     bias = lib.f32_to_bf16((rng.standard_normal(N) * 0.1).astype(np.float32))
     w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
     hd = to_dev(h)
+    import torch
     L.qlinear(ctx, w, to_dev(xb), bias=to_dev(bias), out=hd,
-              epilogue=L.EPI_GATED_RES, gate=to_dev(gate))
+              epilogue=L.EPI_GATED_RES, gate=torch.from_numpy(gate).cuda())
     y = from_dev(hd)
     sub = oracle_y(xb, codes, scales, biases, K, lib.bf16_to_f32(bias))
-    want = lib.bf16_to_f32(h) + sub * lib.bf16_to_f32(gate)[None, :]
+    want = lib.bf16_to_f32(h) + sub * gate[None, :]
     assert lib.rel_l2(y, want) < TOL
 
 
@@ -238,3 +239,22 @@ def test_device_packer_is_bit_exact(ctx, golden):
     assert np.array_equal(c.cpu().numpy().view(np.uint32), want[0])
     assert np.array_equal(s.cpu().numpy().view(np.uint16), want[1])
     assert np.array_equal(b.cpu().numpy().view(np.uint16), want[2])
+
+
+@pytest.mark.parametrize("M,N", [(24, 2), (8160, 2), (126, 6)])
+def test_dense_narrow_outputs(ctx, M, N):
+    """Gate-logit shaped GEMMs (N = heads, not a multiple of 4), including
+    the split-K path: nothing may be written past column N."""
+    import torch
+    import ltx25_b200 as L
+    rng = np.random.default_rng(M + N)
+    K = 256
+    x = lib.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    wd = lib.f32_to_bf16((rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+    w = L.QWeight.upload_dense(ctx, wd, N, K)
+    out = torch.full((M + 1, N), 7.0, dtype=torch.bfloat16, device="cuda")
+    L.qlinear(ctx, w, to_dev(x), out=out[:M], M=M)
+    y = from_dev(out)
+    assert np.all(y[M] == 7.0)       # the guard row is untouched
+    want = lib.linear_f64(lib.bf16_to_f32(x), lib.bf16_to_f32(wd))
+    assert lib.rel_l2(y[:M], want) < TOL

@@ -1,0 +1,232 @@
+// block_ops.cu -- the bandwidth-bound row ops of the LTX-2.5 AV block.
+//
+// Each replaces a plugin Metal kernel of the reference (src/ltx25-kernels
+// .metal) and follows the CPU reference's math (src/ltx25-block-ref.cc):
+//
+//   vec_add          adaLN rows: table[i] + timesteps[i]   (ada_values, av_ada_)
+//   ada_zero         rms_norm(x) * (1 + scale) + shift     (ltx_ada_zero)
+//                    with scale = shift = 0 it is ltx_rms_norm_out
+//   modulate         x * (1 + scale) + shift               (adaln_modulate)
+//   qk_norm_rope     RMSNorm over the WHOLE inner width with a gain, then the
+//                    split-half rotation per head          (ltx_rms_norm_gain
+//                                                           + ltx_rope_half_perhead)
+//
+// bf16 storage, f32 arithmetic, one CTA per row, 16-byte vector accesses.
+#include "block_ops.h"
+
+namespace ltx {
+
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red)
+{
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8])
+{
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8])
+{
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+__global__ void vec_add_kernel(const float* __restrict__ a,
+                               const __nv_bfloat16* __restrict__ b,
+                               float* __restrict__ out, int n)
+{
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += gridDim.x * blockDim.x) {
+    out[i] = a[i] + (b != nullptr ? __bfloat162float(b[i]) : 0.0f);
+  }
+}
+
+// out = (rms_norm(x) if norm) * (1 + scale) + shift.  scale/shift may be
+// null (0).  dim % 8 == 0; a thread owns 8-element chunks.
+template <bool NORM>
+__global__ void __launch_bounds__(kRowThreads)
+    row_mod_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                   __nv_bfloat16* __restrict__ out, int ldo, int dim,
+                   const float* __restrict__ scale,
+                   const float* __restrict__ shift, float eps)
+{
+  __shared__ float red[33];
+  const __nv_bfloat16* xr = x + (size_t)blockIdx.x * ldx;
+  __nv_bfloat16* orow = out + (size_t)blockIdx.x * ldo;
+  constexpr int kMaxChunks = 4;   // dim <= 256 * 8 * 4 = 8192
+  float v[kMaxChunks][8];
+  int nch = 0;
+  float ss = 0.0f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int k = (c * kRowThreads + threadIdx.x) * 8;
+    if (k < dim) {
+      load8(xr + k, v[c]);
+      if (NORM) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+      }
+      nch = c + 1;
+    }
+  }
+  float inv = 1.0f;
+  if (NORM) inv = rsqrtf(block_sum(ss, red) / (float)dim + eps);
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    if (c >= nch) break;
+    const int k = (c * kRowThreads + threadIdx.x) * 8;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float sc = scale != nullptr ? scale[k + i] : 0.0f;
+      const float sh = shift != nullptr ? shift[k + i] : 0.0f;
+      o[i] = fmaf(v[c][i] * inv, 1.0f + sc, sh);
+    }
+    store8(orow + k, o);
+  }
+}
+
+// q/k normalization over the whole inner width, gain, then RoPE (optional).
+// in: row stride ldi (the fused-QKV output), out: compact [rows][inner].
+// cos/sin: [heads][tokens][half] f32.
+__global__ void __launch_bounds__(kRowThreads)
+    qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ in, int ldi,
+                        __nv_bfloat16* __restrict__ out, int ldo, int heads,
+                        int head_dim, const float* __restrict__ gain,
+                        const float* __restrict__ cosb,
+                        const float* __restrict__ sinb, int tokens, float eps)
+{
+  extern __shared__ float srow[];   // the normalized row, f32 [inner]
+  __shared__ float red[33];
+  const int inner = heads * head_dim;
+  const int t = blockIdx.x;
+  const __nv_bfloat16* xr = in + (size_t)t * ldi;
+  float ss = 0.0f;
+  for (int k = threadIdx.x * 8; k < inner; k += kRowThreads * 8) {
+    float v[8];
+    load8(xr + k, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(v[i], v[i], ss);
+      srow[k + i] = v[i];
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / (float)inner + eps);
+  // (block_sum's barriers also publish srow.)
+  const int half = head_dim / 2;
+  __nv_bfloat16* orow = out + (size_t)t * ldo;
+  for (int idx = threadIdx.x; idx < heads * half; idx += kRowThreads) {
+    const int h = idx / half, j = idx % half;
+    const int ia = h * head_dim + j, ib = ia + half;
+    float a = srow[ia] * inv * (gain != nullptr ? gain[ia] : 1.0f);
+    float b = srow[ib] * inv * (gain != nullptr ? gain[ib] : 1.0f);
+    if (cosb != nullptr) {
+      const size_t o = ((size_t)h * tokens + t) * half + j;
+      const float c = cosb[o], s = sinb[o];
+      const float ra = a * c - b * s;
+      const float rb = b * c + a * s;
+      a = ra;
+      b = rb;
+    }
+    orow[ia] = __float2bfloat16_rn(a);
+    orow[ib] = __float2bfloat16_rn(b);
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ a,
+                                   __nv_bfloat16* __restrict__ out, size_t n)
+{
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __float2bfloat16_rn(a[i]);
+}
+
+}  // namespace
+
+int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
+                       cudaStream_t s)
+{
+  if (n == 0) return 0;
+  size_t grid = (n + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  f32_to_bf16_kernel<<<(unsigned)grid, 256, 0, s>>>(a, out, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,
+                   cudaStream_t s)
+{
+  if (n <= 0) return 0;
+  const int threads = 256;
+  int grid = (n + threads - 1) / threads;
+  if (grid > 1024) grid = 1024;
+  vec_add_kernel<<<grid, threads, 0, s>>>(a, b, out, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
+                    int ldo, int rows, int dim, const float* scale,
+                    const float* shift, float eps, bool norm, cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  if (dim % 8 != 0 || dim > kRowThreads * 8 * 4) return -2;
+  if (norm) {
+    row_mod_kernel<true><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, dim,
+                                                      scale, shift, eps);
+  } else {
+    row_mod_kernel<false><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, dim,
+                                                       scale, shift, eps);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
+                        int ldo, int rows, int heads, int head_dim,
+                        const float* gain, const float* cosb,
+                        const float* sinb, float eps, cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  const int inner = heads * head_dim;
+  if (inner % 8 != 0 || head_dim % 2 != 0) return -2;
+  const size_t smem = (size_t)inner * sizeof(float);
+  if (smem > 48 * 1024) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(qk_norm_rope_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           96 * 1024);
+      attr = true;
+    }
+  }
+  qk_norm_rope_kernel<<<rows, kRowThreads, smem, s>>>(
+      in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace ltx

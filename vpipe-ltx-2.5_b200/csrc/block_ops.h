@@ -1,0 +1,42 @@
+// block_ops.h -- launchers for the block's row ops and attention (internal).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace ltx {
+
+int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
+                       cudaStream_t s);
+
+// out[i] = a[i] + b[i] (b bf16, may be null), f32.
+int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,
+                   cudaStream_t s);
+
+// out = (norm ? rms_norm(x) : x) * (1 + scale) + shift; scale/shift f32 [dim]
+// or null.  dim % 8 == 0, dim <= 8192.
+int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
+                    int ldo, int rows, int dim, const float* scale,
+                    const float* shift, float eps, bool norm, cudaStream_t s);
+
+// RMSNorm over the whole heads*head_dim row with gain (f32, may be null),
+// then split-half RoPE with [heads][rows][head_dim/2] f32 tables (may be
+// null).  in: row stride ldi; out: row stride ldo.
+int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
+                        int ldo, int rows, int heads, int head_dim,
+                        const float* gain, const float* cosb,
+                        const float* sinb, float eps, cudaStream_t s);
+
+// Non-causal attention, token-major q [tq][ldq], k/v [tk][ld], head h at
+// columns [h*D, (h+1)*D); o [tq][ldo]; optional gate logits [tq][ldg]
+// (o *= 2 sigmoid(gate[t][h])).  head_dim 64 or 128.
+int launch_attention(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
+                     int ldk, const __nv_bfloat16* v, int ldv,
+                     __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate,
+                     int ldg, int tq, int tk, int heads, int head_dim,
+                     cudaStream_t s);
+
+}  // namespace ltx

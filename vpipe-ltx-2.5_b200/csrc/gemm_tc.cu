@@ -70,10 +70,10 @@ __device__ __forceinline__ uint32_t epi_pair(float a, float b, int n,
     a = gelu_tanh(a);
     b = gelu_tanh(b);
   } else if constexpr (EPI == EPI_GATED_RES) {
-    const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(p.gate + n);
+    const float2 g = *reinterpret_cast<const float2*>(p.gate + n);
     const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(yrow + n);
-    a = fmaf(__bfloat162float(g.x), a, __bfloat162float(h.x));
-    b = fmaf(__bfloat162float(g.y), b, __bfloat162float(h.y));
+    a = fmaf(g.x, a, __bfloat162float(h.x));
+    b = fmaf(g.y, b, __bfloat162float(h.y));
   }
   const __nv_bfloat162 o = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&o);
@@ -594,9 +594,11 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
       }
       __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
       const uint32_t o0 = epi_pair<EPI>(sum.x, sum.y, n, p, yrow);
-      const uint32_t o1 = epi_pair<EPI>(sum.z, sum.w, n + 2, p, yrow);
       *reinterpret_cast<uint32_t*>(yrow + n) = o0;
-      *reinterpret_cast<uint32_t*>(yrow + n + 2) = o1;
+      if (n + 2 < p.N) {   // N is even but need not be a multiple of 4
+        const uint32_t o1 = epi_pair<EPI>(sum.z, sum.w, n + 2, p, yrow);
+        *reinterpret_cast<uint32_t*>(yrow + n + 2) = o1;
+      }
     }
     // Peers may still be reading this CTA's partial: leave together.
     cluster_sync_all();

@@ -66,7 +66,7 @@ struct GemmParams {
   int num_tiles;           // m_tiles * n_tiles * splits
   int ldy;                 // row stride of y, elements
   const __nv_bfloat16* bias;   // [N] or null
-  const __nv_bfloat16* gate;   // [N], EPI_GATED_RES only
+  const float* gate;           // [N] f32, EPI_GATED_RES only
   __nv_bfloat16* y;            // [M][ldy]
   const float* sx;             // MODE_I8: [M] token scales
   const float* sw;             // MODE_I8: [N] channel scales

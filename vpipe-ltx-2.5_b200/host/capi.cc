@@ -6,6 +6,8 @@
 
 #include "../../include/ltx25_cuda.h"
 #include "../csrc/kernels.h"
+#include "../csrc/block_ops.h"
+#include "ltx25-block-cuda.h"
 #include "ltx25-cuda-ops.h"
 
 struct ltx_ctx {
@@ -159,7 +161,7 @@ int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x, int ldx,
   if (!ctx->ops.linear(S(stream), static_cast<const __nv_bfloat16*>(x), ldx, w->w,
                        static_cast<const __nv_bfloat16*>(bias),
                        static_cast<__nv_bfloat16*>(y), ldy, M, K, N, epilogue,
-                       static_cast<const __nv_bfloat16*>(gate), &e))
+                       static_cast<const float*>(gate), &e))
     return fail(ctx, code_for(e), e);
   return LTX_OK;
 }
@@ -232,6 +234,193 @@ int ltx_pack_w8g64(ltx_ctx* ctx, const float* w, int N, int K, uint32_t* codes,
     return fail(ctx, LTX_E_SHAPE, "pack_w8g64: need K % 64 == 0");
   if (ltx::launch_pack_w8g64(w, N, K, codes, scales, biases, S(stream)) != 0)
     return fail(ctx, LTX_E_CUDA, "pack_w8g64 launch failed");
+  return LTX_OK;
+}
+
+int ltx_ada_zero(ltx_ctx* ctx, const void* x, void* out, int rows, int dim,
+                 const float* scale, const float* shift, int normalize,
+                 void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (x == nullptr || out == nullptr) return fail(ctx, LTX_E_NULL, "ada_zero: null");
+  const int rc = ltx::launch_ada_zero(static_cast<const __nv_bfloat16*>(x), dim,
+                                      static_cast<__nv_bfloat16*>(out), dim, rows,
+                                      dim, scale, shift, 1e-6f, normalize != 0,
+                                      S(stream));
+  if (rc == -2) return fail(ctx, LTX_E_SHAPE, "ada_zero: dim % 8 != 0 or > 8192");
+  if (rc != 0) return fail(ctx, LTX_E_CUDA, "ada_zero launch failed");
+  return LTX_OK;
+}
+
+int ltx_qk_norm_rope(ltx_ctx* ctx, const void* in, int ld_in, void* out,
+                     int rows, int heads, int head_dim, const float* gain,
+                     const float* cos_tab, const float* sin_tab, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (in == nullptr || out == nullptr) return fail(ctx, LTX_E_NULL, "qk_norm_rope: null");
+  if ((cos_tab == nullptr) != (sin_tab == nullptr))
+    return fail(ctx, LTX_E_NULL, "qk_norm_rope: cos and sin go together");
+  const int rc = ltx::launch_qk_norm_rope(
+      static_cast<const __nv_bfloat16*>(in), ld_in, static_cast<__nv_bfloat16*>(out),
+      heads * head_dim, rows, heads, head_dim, gain, cos_tab, sin_tab, 1e-6f, S(stream));
+  if (rc == -2) return fail(ctx, LTX_E_SHAPE, "qk_norm_rope: bad head geometry");
+  if (rc != 0) return fail(ctx, LTX_E_CUDA, "qk_norm_rope launch failed");
+  return LTX_OK;
+}
+
+int ltx_attention(ltx_ctx* ctx, const void* q, int ldq, const void* k, int ldk,
+                  const void* v, int ldv, void* o, int ldo,
+                  const void* gate_logits, int ldg, int tq, int tk, int heads,
+                  int head_dim, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
+    return fail(ctx, LTX_E_NULL, "attention: null");
+  const int rc = ltx::launch_attention(
+      static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k),
+      ldk, static_cast<const __nv_bfloat16*>(v), ldv, static_cast<__nv_bfloat16*>(o),
+      ldo, static_cast<const __nv_bfloat16*>(gate_logits), ldg, tq, tk, heads,
+      head_dim, S(stream));
+  if (rc == -2) return fail(ctx, LTX_E_SHAPE, "attention: head_dim must be 64 or 128, strides % 8");
+  if (rc != 0) return fail(ctx, LTX_E_CUDA, "attention launch failed");
+  return LTX_OK;
+}
+
+}  // extern "C"
+
+struct ltx_block {
+  ltx_ctx* ctx = nullptr;
+  ltx25::CudaBlock* blk = nullptr;
+  std::string err;
+};
+
+namespace {
+
+int bfail(ltx_block* b, int code, const std::string& m)
+{
+  if (b != nullptr) b->err = m;
+  return code;
+}
+
+ltx25::StreamIO to_io(const ltx_stream_io* s)
+{
+  ltx25::StreamIO io;
+  if (s == nullptr) {
+    io.present = false;
+    return io;
+  }
+  io.x = static_cast<__nv_bfloat16*>(s->x);
+  io.context = static_cast<const __nv_bfloat16*>(s->context);
+  io.timesteps = static_cast<const __nv_bfloat16*>(s->timesteps);
+  io.cross_scale_shift = static_cast<const __nv_bfloat16*>(s->cross_scale_shift);
+  io.cross_gate = static_cast<const __nv_bfloat16*>(s->cross_gate);
+  io.prompt_timestep = static_cast<const __nv_bfloat16*>(s->prompt_timestep);
+  io.pe_cos = s->pe_cos;
+  io.pe_sin = s->pe_sin;
+  io.cpe_cos = s->cross_pe_cos;
+  io.cpe_sin = s->cross_pe_sin;
+  io.tokens = s->tokens;
+  io.text_tokens = s->text_tokens;
+  io.present = s->present != 0;
+  return io;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltx_block_create(ltx_ctx* ctx, int video_dim, int video_heads,
+                     int audio_dim, int audio_heads, ltx_block** out)
+{
+  if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  if (video_dim <= 0 || video_heads <= 0 || audio_dim <= 0 || audio_heads <= 0 ||
+      video_dim % video_heads != 0 || audio_dim % audio_heads != 0)
+    return fail(ctx, LTX_E_SHAPE, "block: widths must be positive multiples of the heads");
+  ltx_block* b = new (std::nothrow) ltx_block();
+  if (b == nullptr) return fail(ctx, LTX_E_OOM, "host allocation failed");
+  b->ctx = ctx;
+  b->blk = new (std::nothrow) ltx25::CudaBlock(&ctx->ops, video_dim, video_heads,
+                                               audio_dim, audio_heads);
+  if (b->blk == nullptr) {
+    delete b;
+    return fail(ctx, LTX_E_OOM, "host allocation failed");
+  }
+  *out = b;
+  return LTX_OK;
+}
+
+void ltx_block_destroy(ltx_block* b)
+{
+  if (b == nullptr) return;
+  delete b->blk;
+  delete b;
+}
+
+const char* ltx_block_last_error(const ltx_block* b)
+{
+  return b == nullptr ? "null block" : b->err.c_str();
+}
+
+int ltx_block_set_qlinear(ltx_block* b, const char* name, const uint32_t* codes,
+                          const void* scales, const void* biases, int sb_dtype,
+                          int N, int K, int on_device)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  if (name == nullptr) return bfail(b, LTX_E_NULL, "set_qlinear: null name");
+  std::string e;
+  if (!b->blk->set_qlinear(name, codes, scales, biases, sb_dtype, N, K,
+                           on_device != 0, &e))
+    return bfail(b, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_block_set_tensor(ltx_block* b, const char* name, const float* data,
+                         int rows, int cols, int on_device)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  if (name == nullptr || data == nullptr) return bfail(b, LTX_E_NULL, "set_tensor: null");
+  std::string e;
+  if (!b->blk->set_tensor(name, data, rows, cols, on_device != 0, &e))
+    return bfail(b, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_block_finalize(ltx_block* b)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  std::string e;
+  if (!b->blk->finalize(&e)) {
+    const int code = e.find("missing") != std::string::npos ? LTX_E_STATE : code_for(e);
+    return bfail(b, code, e);
+  }
+  return LTX_OK;
+}
+
+int ltx_block_reserve(ltx_block* b, int max_video_tokens, int max_audio_tokens,
+                      int max_text_tokens)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  std::string e;
+  if (!b->blk->reserve(max_video_tokens, max_audio_tokens, max_text_tokens, &e))
+    return bfail(b, b->blk->finalized() ? code_for(e) : LTX_E_STATE, e);
+  return LTX_OK;
+}
+
+int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
+                      const ltx_stream_io* audio, void* stream)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  ltx25::StreamIO v = to_io(video), a = to_io(audio);
+  std::string e;
+  if (!b->blk->forward(S(stream), v, a, &e)) {
+    int code = code_for(e);
+    if (e.find("before finalize") != std::string::npos || e.find("arena") != std::string::npos)
+      code = LTX_E_STATE;
+    if (e.find("neither stream") != std::string::npos || e.find("missing") != std::string::npos)
+      code = LTX_E_NULL;
+    return bfail(b, code, e);
+  }
   return LTX_OK;
 }
 

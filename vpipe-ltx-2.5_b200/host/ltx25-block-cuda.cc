@@ -1,0 +1,546 @@
+// ltx25-block-cuda.cc -- CudaBlock (see ltx25-block-cuda.h).
+#include "ltx25-block-cuda.h"
+
+#include <algorithm>
+#include <cstring>
+
+#include "../csrc/block_ops.h"
+#include "../csrc/kernels.h"
+
+namespace ltx25 {
+
+namespace {
+
+constexpr float kEps = 1e-6f;   // norm_eps, src/ltx25-block-ref.h:74
+
+bool cuda_ok(cudaError_t e, const char* what, std::string* err)
+{
+  if (e == cudaSuccess) return true;
+  if (err) *err = std::string(what) + ": " + cudaGetErrorString(e);
+  return false;
+}
+
+bool fail(std::string* err, const std::string& m)
+{
+  if (err) *err = m;
+  return false;
+}
+
+// Offsets (in units of the stream width) of the f32 adaLN rows in a stream's
+// region of the modulation scratch.
+enum ModRow : int {
+  MOD_MSA = 0,      // self-attn shift, scale, gate   (table rows 0..2)
+  MOD_CA = 3,       // text cross shift, scale, gate   (rows 6..8)
+  MOD_PROMPT = 6,   // K/V shift, scale                 (prompt table)
+  MOD_MLP = 8,      // ff shift, scale, gate            (rows 3..5)
+  MOD_AV = 11,      // a2v/v2a scale, shift, scale, shift (cross rows 0..3)
+  MOD_AVG = 15,     // a2v/v2a gate                      (cross row 4)
+  MOD_ROWS = 16
+};
+
+}  // namespace
+
+CudaBlock::~CudaBlock()
+{
+  for (auto& kv : _staged)
+    if (kv.second.quant) free_qweight(&kv.second.q);
+  for (CudaAttn* a : {&_video.attn1, &_video.attn2, &_audio.attn1,
+                      &_audio.attn2, &_a2v, &_v2a}) {
+    free_qweight(&a->qkv);
+    free_qweight(&a->q);
+    free_qweight(&a->kv);
+    free_qweight(&a->o);
+    free_qweight(&a->gate);
+  }
+  for (CudaStreamW* w : {&_video, &_audio}) {
+    free_qweight(&w->ff_in);
+    free_qweight(&w->ff_out);
+  }
+  for (void* p : _owned) cudaFree(p);
+  for (void* p : {(void*)_ar.normed, (void*)_ar.qkv, (void*)_ar.qn,
+                  (void*)_ar.kn, (void*)_ar.att, (void*)_ar.glog,
+                  (void*)_ar.ctxmod, (void*)_ar.kvp, (void*)_ar.ff,
+                  (void*)_ar.qv, (void*)_ar.kva, (void*)_ar.qa,
+                  (void*)_ar.kvv, (void*)_ar.mods})
+    cudaFree(p);
+}
+
+bool CudaBlock::set_qlinear(const std::string& name, const uint32_t* codes,
+                            const void* scales, const void* biases,
+                            int sb_dtype, int N, int K, bool on_device,
+                            std::string* err)
+{
+  if (_final) return fail(err, "block already finalized");
+  Staged st;
+  st.quant = true;
+  if (!upload_qweight(*_ops, codes, scales, biases, sb_dtype, N, K, 8, 64,
+                      on_device, &st.q, err))
+    return false;
+  st.rows = N;
+  st.cols = K;
+  auto it = _staged.find(name);
+  if (it != _staged.end() && it->second.quant) free_qweight(&it->second.q);
+  _staged[name] = std::move(st);
+  return true;
+}
+
+bool CudaBlock::set_tensor(const std::string& name, const float* data,
+                           int rows, int cols, bool on_device,
+                           std::string* err)
+{
+  if (_final) return fail(err, "block already finalized");
+  if (data == nullptr || rows <= 0) return fail(err, "set_tensor: null or empty " + name);
+  Staged st;
+  st.rows = rows;
+  st.cols = cols > 0 ? cols : 1;
+  const size_t n = (size_t)st.rows * st.cols;
+  if (on_device) {
+    st.dev_f32 = const_cast<float*>(data);
+  } else {
+    st.host.assign(data, data + n);
+  }
+  auto it = _staged.find(name);
+  if (it != _staged.end() && it->second.quant) free_qweight(&it->second.q);
+  _staged[name] = std::move(st);
+  return true;
+}
+
+bool CudaBlock::take_f32_(const std::string& name, size_t count, float** out,
+                          std::string* err, bool required)
+{
+  *out = nullptr;
+  auto it = _staged.find(name);
+  if (it == _staged.end() || it->second.quant) {
+    if (!required) return true;
+    return fail(err, "missing tensor '" + name + "'");
+  }
+  const Staged& st = it->second;
+  if ((size_t)st.rows * st.cols != count)
+    return fail(err, "tensor '" + name + "' has " +
+                         std::to_string((size_t)st.rows * st.cols) +
+                         " elements, want " + std::to_string(count));
+  float* d = nullptr;
+  if (!cuda_ok(cudaMalloc(&d, count * sizeof(float)), "cudaMalloc", err)) return false;
+  _owned.push_back(d);
+  const cudaError_t e =
+      st.dev_f32 ? cudaMemcpy(d, st.dev_f32, count * 4, cudaMemcpyDeviceToDevice)
+                 : cudaMemcpy(d, st.host.data(), count * 4, cudaMemcpyHostToDevice);
+  if (!cuda_ok(e, "upload", err)) return false;
+  *out = d;
+  return true;
+}
+
+bool CudaBlock::take_bf16_(const std::string& name, size_t count,
+                           __nv_bfloat16** out, std::string* err,
+                           bool required)
+{
+  *out = nullptr;
+  float* f = nullptr;
+  if (!take_f32_(name, count, &f, err, required)) return false;
+  if (f == nullptr) return true;
+  __nv_bfloat16* d = nullptr;
+  if (!cuda_ok(cudaMalloc(&d, count * 2), "cudaMalloc", err)) return false;
+  _owned.push_back(d);
+  if (ltx::launch_f32_to_bf16(f, d, count, nullptr) != 0 ||
+      !cuda_ok(cudaDeviceSynchronize(), "convert", err))
+    return fail(err, "f32 -> bf16 conversion failed for " + name);
+  *out = d;
+  return true;
+}
+
+// Concatenate quantized linears along N (rows of the weight): codes row
+// blocks back to back, scale/zero-point pairs side by side per K group.
+bool CudaBlock::fuse_(const std::vector<const QWeight*>& parts, QWeight* out,
+                      std::string* err)
+{
+  const int K = parts[0]->K;
+  int N = 0;
+  for (const QWeight* q : parts) {
+    if (!q->quantized || q->K != K) return fail(err, "fuse: mismatched parts");
+    N += q->N;
+  }
+  QWeight f;
+  f.N = N;
+  f.K = K;
+  f.bits = 8;
+  f.group = 64;
+  f.quantized = true;
+  f.device = _ops->device();
+  const int G = K / 64;
+  if (!cuda_ok(cudaMalloc(&f.codes, (size_t)N * K), "cudaMalloc(fused codes)", err) ||
+      !cuda_ok(cudaMalloc(&f.sz, (size_t)N * G * 4), "cudaMalloc(fused sz)", err)) {
+    free_qweight(&f);
+    return false;
+  }
+  int n0 = 0;
+  for (const QWeight* q : parts) {
+    if (!cuda_ok(cudaMemcpy(f.codes + (size_t)n0 * K, q->codes, (size_t)q->N * K,
+                            cudaMemcpyDeviceToDevice), "fuse codes", err) ||
+        !cuda_ok(cudaMemcpy2D(f.sz + n0, (size_t)N * 4, q->sz, (size_t)q->N * 4,
+                              (size_t)q->N * 4, G, cudaMemcpyDeviceToDevice),
+                 "fuse sz", err)) {
+      free_qweight(&f);
+      return false;
+    }
+    n0 += q->N;
+  }
+  *out = f;
+  return true;
+}
+
+bool CudaBlock::build_attn_(const std::string& p, bool self, int qdim,
+                            int kvdim, int heads, int head_dim, int odim,
+                            CudaAttn& a, std::string* err)
+{
+  const int inner = heads * head_dim;
+  a.self = self;
+  a.heads = heads;
+  a.head_dim = head_dim;
+  a.inner = inner;
+  a.qdim = qdim;
+  a.kvdim = kvdim;
+  a.odim = odim;
+  auto qlin = [&](const std::string& n, int N, int K) -> const QWeight* {
+    auto it = _staged.find(p + n);
+    if (it == _staged.end() || !it->second.quant) {
+      fail(err, "missing quantized tensor '" + p + n + "'");
+      return nullptr;
+    }
+    if (it->second.q.N != N || it->second.q.K != K) {
+      fail(err, "tensor '" + p + n + "' is [" + std::to_string(it->second.q.N) +
+                    "][" + std::to_string(it->second.q.K) + "], want [" +
+                    std::to_string(N) + "][" + std::to_string(K) + "]");
+      return nullptr;
+    }
+    return &it->second.q;
+  };
+  const QWeight* wq = qlin(".to_q.weight", inner, qdim);
+  if (!wq) return false;
+  const QWeight* wk = qlin(".to_k.weight", inner, kvdim);
+  if (!wk) return false;
+  const QWeight* wv = qlin(".to_v.weight", inner, kvdim);
+  if (!wv) return false;
+  const QWeight* wo = qlin(".to_out.0.weight", odim, inner);
+  if (!wo) return false;
+
+  // Biases: q/k/v concatenated to match the fused GEMM's output columns.
+  std::vector<float> bcat;
+  for (const char* bn : {".to_q.bias", ".to_k.bias", ".to_v.bias"}) {
+    auto it = _staged.find(p + bn);
+    if (it == _staged.end() || it->second.quant || (size_t)it->second.rows * it->second.cols != (size_t)inner)
+      return fail(err, "missing tensor '" + p + bn + "'");
+    std::vector<float> h(inner);
+    if (it->second.dev_f32) {
+      if (!cuda_ok(cudaMemcpy(h.data(), it->second.dev_f32, inner * 4, cudaMemcpyDeviceToHost), "bias", err))
+        return false;
+    } else {
+      h = it->second.host;
+    }
+    bcat.insert(bcat.end(), h.begin(), h.end());
+  }
+  const std::string tmpq = p + ".__qkv_bias", tmpkv = p + ".__kv_bias";
+  if (self) {
+    if (!fuse_({wq, wk, wv}, &a.qkv, err)) return false;
+    if (!set_tensor(tmpq, bcat.data(), 3 * inner, 0, false, err) ||
+        !take_bf16_(tmpq, (size_t)3 * inner, &a.qkv_b, err))
+      return false;
+  } else {
+    if (!fuse_({wq}, &a.q, err) || !fuse_({wk, wv}, &a.kv, err)) return false;
+    if (!set_tensor(tmpq, bcat.data(), inner, 0, false, err) ||
+        !take_bf16_(tmpq, (size_t)inner, &a.qkv_b, err))
+      return false;
+    if (!set_tensor(tmpkv, bcat.data() + inner, 2 * inner, 0, false, err) ||
+        !take_bf16_(tmpkv, (size_t)2 * inner, &a.kv_b, err))
+      return false;
+  }
+  _staged.erase(tmpq);
+  _staged.erase(tmpkv);
+  if (!fuse_({wo}, &a.o, err)) return false;
+  if (!take_bf16_(p + ".to_out.0.bias", odim, &a.o_b, err) ||
+      !take_f32_(p + ".q_norm.weight", inner, &a.q_norm, err) ||
+      !take_f32_(p + ".k_norm.weight", inner, &a.k_norm, err))
+    return false;
+  // Gate logits: dense (excluded from quantization), [heads][qdim].
+  float* gw = nullptr;
+  if (!take_f32_(p + ".to_gate_logits.weight", (size_t)heads * qdim, &gw, err, false))
+    return false;
+  if (gw != nullptr) {
+    __nv_bfloat16* gwb = nullptr;
+    if (!cuda_ok(cudaMalloc(&gwb, (size_t)heads * qdim * 2), "cudaMalloc", err)) return false;
+    if (ltx::launch_f32_to_bf16(gw, gwb, (size_t)heads * qdim, nullptr) != 0 ||
+        !cuda_ok(cudaDeviceSynchronize(), "convert", err))
+      return false;
+    const bool ok = upload_dweight(*_ops, reinterpret_cast<const uint16_t*>(gwb),
+                                   heads, qdim, true, &a.gate, err);
+    cudaFree(gwb);
+    if (!ok) return false;
+    if (!take_bf16_(p + ".to_gate_logits.bias", heads, &a.gate_b, err, false))
+      return false;
+  }
+  return true;
+}
+
+bool CudaBlock::build_stream_(bool audio, CudaStreamW& w, std::string* err)
+{
+  const std::string pre = audio ? "audio_" : "";
+  const int d = audio ? _adim : _vdim;
+  const int h = audio ? _aheads : _vheads;
+  w.dim = d;
+  w.heads = h;
+  if (d % h != 0) return fail(err, "stream width is not a multiple of the heads");
+  if (!build_attn_(pre + "attn1", true, d, d, h, d / h, d, w.attn1, err) ||
+      !build_attn_(pre + "attn2", false, d, d, h, d / h, d, w.attn2, err))
+    return false;
+  auto fi = _staged.find(pre + "ff.net.0.proj.weight");
+  auto fo = _staged.find(pre + "ff.net.2.weight");
+  if (fi == _staged.end() || !fi->second.quant)
+    return fail(err, "missing quantized tensor '" + pre + "ff.net.0.proj.weight'");
+  if (fo == _staged.end() || !fo->second.quant)
+    return fail(err, "missing quantized tensor '" + pre + "ff.net.2.weight'");
+  w.ff_hidden = fi->second.q.N;
+  if (fi->second.q.K != d || fo->second.q.N != d || fo->second.q.K != w.ff_hidden)
+    return fail(err, "feed-forward shapes disagree with the stream width");
+  if (!fuse_({&fi->second.q}, &w.ff_in, err) || !fuse_({&fo->second.q}, &w.ff_out, err))
+    return false;
+  // Video ff has no bias, audio ff does (src/ltx25-dit-weights.cc:482-486).
+  if (!take_bf16_(pre + "ff.net.0.proj.bias", w.ff_hidden, &w.ff_in_b, err, false) ||
+      !take_bf16_(pre + "ff.net.2.bias", d, &w.ff_out_b, err, false))
+    return false;
+  if (!take_f32_(pre + "scale_shift_table", (size_t)9 * d, &w.scale_shift, err) ||
+      !take_f32_(pre + "prompt_scale_shift_table", (size_t)2 * d,
+                 &w.prompt_scale_shift, err) ||
+      !take_f32_(audio ? "scale_shift_table_a2v_ca_audio"
+                       : "scale_shift_table_a2v_ca_video",
+                 (size_t)5 * d, &w.cross_table, err))
+    return false;
+  return true;
+}
+
+bool CudaBlock::finalize(std::string* err)
+{
+  if (_final) return true;
+  if (!build_stream_(false, _video, err) || !build_stream_(true, _audio, err))
+    return false;
+  // Both cross-attentions run at the AUDIO head count and head width
+  // (src/ltx25-block-ref.cc:510-519).
+  const int ahd = _adim / _aheads;
+  if (!build_attn_("audio_to_video_attn", false, _vdim, _adim, _aheads, ahd,
+                   _vdim, _a2v, err) ||
+      !build_attn_("video_to_audio_attn", false, _adim, _vdim, _aheads, ahd,
+                   _adim, _v2a, err))
+    return false;
+  for (auto& kv : _staged)
+    if (kv.second.quant) free_qweight(&kv.second.q);
+  _staged.clear();
+  _final = true;
+  return true;
+}
+
+bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
+                        std::string* err)
+{
+  if (!_final) return fail(err, "reserve before finalize");
+  const size_t vt = std::max(max_video, 0), at = std::max(max_audio, 0),
+               tt = std::max(max_text, 0);
+  const size_t vd = _vdim, ad = _adim;
+  const size_t ai = ad;   // audio inner (the cross attentions' width too)
+  auto mx = [](std::initializer_list<size_t> l) { return std::max(l); };
+  const size_t n_normed = mx({vt * vd, at * ad});
+  const size_t n_qkv = mx({vt * 3 * vd, at * 3 * ad, vt * vd, vt * ai, at * ai});
+  const size_t n_kvp = mx({tt * 2 * vd, tt * 2 * ad, at * 2 * ai, vt * 2 * ai});
+  const size_t n_qn = mx({vt * vd, at * ad, vt * ai});
+  const size_t n_kn = mx({vt * vd, at * ad, tt * vd, tt * ad, vt * ai, at * ai});
+  const size_t n_att = mx({vt * vd, at * ad, vt * ai});
+  const size_t n_glog = mx({vt, at}) * (size_t)std::max(_vheads, _aheads);
+  const size_t n_ctx = tt * std::max(vd, ad);
+  const size_t n_ff = mx({vt * (size_t)_video.ff_hidden, at * (size_t)_audio.ff_hidden});
+  struct B { __nv_bfloat16** p; size_t n; };
+  const B bufs[] = {{&_ar.normed, n_normed}, {&_ar.qkv, n_qkv}, {&_ar.kvp, n_kvp},
+                    {&_ar.qn, n_qn}, {&_ar.kn, n_kn}, {&_ar.att, n_att},
+                    {&_ar.glog, n_glog}, {&_ar.ctxmod, n_ctx}, {&_ar.ff, n_ff},
+                    {&_ar.qv, vt * vd}, {&_ar.kva, at * ad}, {&_ar.qa, at * ad},
+                    {&_ar.kvv, vt * vd}};
+  for (const B& b : bufs) {
+    cudaFree(*b.p);
+    *b.p = nullptr;
+    if (b.n > 0 &&
+        !cuda_ok(cudaMalloc(b.p, (b.n + 64) * sizeof(__nv_bfloat16)), "cudaMalloc(block arena)", err))
+      return false;
+  }
+  cudaFree(_ar.mods);
+  _ar.mods = nullptr;
+  if (!cuda_ok(cudaMalloc(&_ar.mods, (size_t)MOD_ROWS * (vd + ad) * sizeof(float)),
+               "cudaMalloc(block arena)", err))
+    return false;
+  _ar.tokens = mx({vt, at, tt});
+  // The GEMMs' own scratch (int8 tier) follows the largest projection.
+  return _ops->reserve((int)mx({vt, at, tt}), (int)mx({3 * vd, (size_t)_video.ff_hidden}),
+                       (int)mx({vd, (size_t)_video.ff_hidden}), err);
+}
+
+bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
+                        const __nv_bfloat16* xq, int tq,
+                        const __nv_bfloat16* xkv, int tkv, const float* qcos,
+                        const float* qsin, const float* kcos,
+                        const float* ksin, __nv_bfloat16* out,
+                        std::string* err)
+{
+  const int I = a.inner;
+  const __nv_bfloat16 *qraw, *kraw, *vraw;
+  int ldq, ldkv;
+  if (a.self) {
+    if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _ar.qkv, 3 * I, tq, a.qdim,
+                      3 * I, ltx::EPI_STORE, nullptr, err))
+      return false;
+    qraw = _ar.qkv;
+    kraw = _ar.qkv + I;
+    vraw = _ar.qkv + 2 * I;
+    ldq = ldkv = 3 * I;
+  } else {
+    if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _ar.qkv, I, tq, a.qdim, I,
+                      ltx::EPI_STORE, nullptr, err) ||
+        !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _ar.kvp, 2 * I, tkv,
+                      a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err))
+      return false;
+    qraw = _ar.qkv;
+    kraw = _ar.kvp;
+    vraw = _ar.kvp + I;
+    ldq = I;
+    ldkv = 2 * I;
+  }
+  if (ltx::launch_qk_norm_rope(qraw, ldq, _ar.qn, I, tq, a.heads, a.head_dim,
+                               a.q_norm, qcos, qsin, kEps, s) != 0 ||
+      ltx::launch_qk_norm_rope(kraw, ldkv, _ar.kn, I, tkv, a.heads,
+                               a.head_dim, a.k_norm, kcos, ksin, kEps, s) != 0)
+    return fail(err, "q/k norm + rope launch failed");
+  const __nv_bfloat16* glog = nullptr;
+  if (a.gate.N > 0) {
+    if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _ar.glog, a.heads, tq,
+                      a.qdim, a.heads, ltx::EPI_STORE, nullptr, err))
+      return false;
+    glog = _ar.glog;
+  }
+  if (ltx::launch_attention(_ar.qn, I, _ar.kn, I, vraw, ldkv, out, I, glog,
+                            a.heads, tq, tkv, a.heads, a.head_dim, s) != 0)
+    return fail(err, "attention launch failed");
+  return true;
+}
+
+bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
+                            std::string* err)
+{
+  // src/ltx25-block-ref.cc:196-262
+  const int n = io.tokens, d = w.dim;
+  float* mods = _ar.mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
+  if (ltx::launch_vec_add(w.scale_shift, io.timesteps, mods + MOD_MSA * d, 3 * d, s) ||
+      ltx::launch_vec_add(w.scale_shift + 6 * d, io.timesteps ? io.timesteps + 6 * d : nullptr,
+                          mods + MOD_CA * d, 3 * d, s) ||
+      ltx::launch_vec_add(w.prompt_scale_shift, io.prompt_timestep,
+                          mods + MOD_PROMPT * d, 2 * d, s))
+    return fail(err, "adaLN rows launch failed");
+  // normed = rms_norm(x) * (1 + scale) + shift;  x += gate * attn1(normed)
+  if (ltx::launch_ada_zero(io.x, d, _ar.normed, d, n, d, mods + (MOD_MSA + 1) * d,
+                           mods + MOD_MSA * d, kEps, true, s))
+    return fail(err, "ada_zero launch failed");
+  if (!attend_(s, w.attn1, _ar.normed, n, _ar.normed, n, io.pe_cos, io.pe_sin,
+               io.pe_cos, io.pe_sin, _ar.att, err))
+    return false;
+  if (!_ops->linear(s, _ar.att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, d,
+                    n, w.attn1.inner, d, ltx::EPI_GATED_RES,
+                    mods + (MOD_MSA + 2) * d, err))
+    return false;
+  // Text cross-attention: query = mod(rms_norm(x)) (= ada_zero with the
+  // cross rows), key/value = context modulated by the prompt table + driver.
+  if (ltx::launch_ada_zero(io.x, d, _ar.normed, d, n, d, mods + (MOD_CA + 1) * d,
+                           mods + MOD_CA * d, kEps, true, s) ||
+      ltx::launch_ada_zero(io.context, d, _ar.ctxmod, d, io.text_tokens, d,
+                           mods + (MOD_PROMPT + 1) * d, mods + MOD_PROMPT * d,
+                           kEps, false, s))
+    return fail(err, "modulation launch failed");
+  if (!attend_(s, w.attn2, _ar.normed, n, _ar.ctxmod, io.text_tokens, nullptr,
+               nullptr, nullptr, nullptr, _ar.att, err))
+    return false;
+  return _ops->linear(s, _ar.att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x,
+                      d, n, w.attn2.inner, d, ltx::EPI_GATED_RES,
+                      mods + (MOD_CA + 2) * d, err);
+}
+
+bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
+                    std::string* err)
+{
+  // src/ltx25-block-ref.cc:264-281
+  const int n = io.tokens, d = w.dim;
+  float* mods = _ar.mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
+  if (ltx::launch_vec_add(w.scale_shift + 3 * d, io.timesteps ? io.timesteps + 3 * d : nullptr,
+                          mods + MOD_MLP * d, 3 * d, s) ||
+      ltx::launch_ada_zero(io.x, d, _ar.normed, d, n, d, mods + (MOD_MLP + 1) * d,
+                           mods + MOD_MLP * d, kEps, true, s))
+    return fail(err, "ff pre-norm launch failed");
+  return _ops->linear(s, _ar.normed, d, w.ff_in, w.ff_in_b, _ar.ff, w.ff_hidden, n,
+                      d, w.ff_hidden, ltx::EPI_GELU, nullptr, err) &&
+         _ops->linear(s, _ar.ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, d, n,
+                      w.ff_hidden, d, ltx::EPI_GATED_RES, mods + (MOD_MLP + 2) * d,
+                      err);
+}
+
+bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
+                        std::string* err)
+{
+  if (!_final) return fail(err, "forward before finalize");
+  const bool rv = v.present && v.tokens > 0;
+  const bool ra = a.present && a.tokens > 0;
+  if (!rv && !ra) return fail(err, "neither stream is present");
+  auto too_big = [&](const StreamIO& io) {
+    return (size_t)io.tokens > _ar.tokens || (size_t)io.text_tokens > _ar.tokens;
+  };
+  if ((rv && too_big(v)) || (ra && too_big(a)))
+    return fail(err, "geometry exceeds the reserved arena");
+  for (const StreamIO* io : {&v, &a}) {
+    const bool on = io == &v ? rv : ra;
+    if (on && (io->x == nullptr || io->context == nullptr || io->timesteps == nullptr))
+      return fail(err, "stream input missing x, context or timesteps");
+  }
+  if (rv && !first_half_(s, _video, v, err)) return false;
+  if (ra && !first_half_(s, _audio, a, err)) return false;
+
+  if (rv && ra) {
+    // src/ltx25-block-ref.cc:336-385.  Both directions read the PRE-cross
+    // state: all four ada_zero operands are formed before either update.
+    const int vd = _vdim, ad = _adim;
+    float* vm = _ar.mods;
+    float* am = _ar.mods + (size_t)MOD_ROWS * _vdim;
+    if (ltx::launch_vec_add(_video.cross_table, v.cross_scale_shift, vm + MOD_AV * vd, 4 * vd, s) ||
+        ltx::launch_vec_add(_video.cross_table + 4 * vd, v.cross_gate, vm + MOD_AVG * vd, vd, s) ||
+        ltx::launch_vec_add(_audio.cross_table, a.cross_scale_shift, am + MOD_AV * ad, 4 * ad, s) ||
+        ltx::launch_vec_add(_audio.cross_table + 4 * ad, a.cross_gate, am + MOD_AVG * ad, ad, s))
+      return fail(err, "cross adaLN launch failed");
+    // av rows: [scale(lo=0), shift(lo=0), scale(lo=2), shift(lo=2)]
+    if (ltx::launch_ada_zero(v.x, vd, _ar.qv, vd, v.tokens, vd, vm + (MOD_AV + 0) * vd,
+                             vm + (MOD_AV + 1) * vd, kEps, true, s) ||
+        ltx::launch_ada_zero(a.x, ad, _ar.kva, ad, a.tokens, ad, am + (MOD_AV + 0) * ad,
+                             am + (MOD_AV + 1) * ad, kEps, true, s) ||
+        ltx::launch_ada_zero(a.x, ad, _ar.qa, ad, a.tokens, ad, am + (MOD_AV + 2) * ad,
+                             am + (MOD_AV + 3) * ad, kEps, true, s) ||
+        ltx::launch_ada_zero(v.x, vd, _ar.kvv, vd, v.tokens, vd, vm + (MOD_AV + 2) * vd,
+                             vm + (MOD_AV + 3) * vd, kEps, true, s))
+      return fail(err, "cross ada_zero launch failed");
+    // a2v: video queries, audio keys/values
+    if (!attend_(s, _a2v, _ar.qv, v.tokens, _ar.kva, a.tokens, v.cpe_cos,
+                 v.cpe_sin, a.cpe_cos, a.cpe_sin, _ar.att, err) ||
+        !_ops->linear(s, _ar.att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, vd, v.tokens,
+                      _a2v.inner, vd, ltx::EPI_GATED_RES, vm + MOD_AVG * vd, err))
+      return false;
+    // v2a: audio queries, video keys/values
+    if (!attend_(s, _v2a, _ar.qa, a.tokens, _ar.kvv, v.tokens, a.cpe_cos,
+                 a.cpe_sin, v.cpe_cos, v.cpe_sin, _ar.att, err) ||
+        !_ops->linear(s, _ar.att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, ad, a.tokens,
+                      _v2a.inner, ad, ltx::EPI_GATED_RES, am + MOD_AVG * ad, err))
+      return false;
+  }
+
+  if (rv && !ff_(s, _video, v, err)) return false;
+  if (ra && !ff_(s, _audio, a, err)) return false;
+  return true;
+}
+
+}  // namespace ltx25

@@ -1,0 +1,148 @@
+// ltx25-block-cuda.h -- one BasicAVTransformerBlock on B200.
+//
+// The CUDA counterpart of the reference's MetalBlock (src/ltx25-block-metal.h)
+// with the math of its CPU reference block_forward (src/ltx25-block-ref.cc:
+// 308-389): the same order, adaLN row slices and pre-cross semantics.  Where
+// the two differ it is by fusion, never by result:
+//   * q/k/v of a self-attention are ONE GEMM over a fused [3*inner][dim]
+//     pack, k/v of a cross-attention one GEMM over [2*inner][dim];
+//   * bias, GELU and the gated residual ride in the GEMM epilogues;
+//   * the a2v/v2a "pre-cross snapshot" is realised by computing all four
+//     ada_zero operands before either residual update, so nothing is copied;
+//   * the per-head gate is applied in the attention's output step.
+// Weights come in under the reference's parameter names (load_block_weights,
+// src/ltx25-block-ref.cc:424-523); the 28 block linears are w8g64 packs, the
+// gate logits stay dense (the quant recipe's exclusion list,
+// src/ltx25-quant-family.cc:50-71).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "ltx25-cuda-ops.h"
+
+namespace ltx25 {
+
+struct CudaAttn {
+  QWeight qkv;        // fused [q; k; v] (self-attention)
+  QWeight q, kv;      // q and fused [k; v] (cross-attentions)
+  QWeight o;
+  QWeight gate;       // dense bf16 [heads][query_dim]
+  __nv_bfloat16* qkv_b = nullptr;   // [3*inner] (self) or q_b [inner]
+  __nv_bfloat16* kv_b = nullptr;    // [2*inner] (cross)
+  __nv_bfloat16* o_b = nullptr;
+  __nv_bfloat16* gate_b = nullptr;
+  float* q_norm = nullptr;
+  float* k_norm = nullptr;
+  bool self = false;
+  int heads = 0, head_dim = 0, inner = 0, qdim = 0, kvdim = 0, odim = 0;
+};
+
+struct CudaStreamW {
+  CudaAttn attn1, attn2;
+  QWeight ff_in, ff_out;
+  __nv_bfloat16* ff_in_b = nullptr;
+  __nv_bfloat16* ff_out_b = nullptr;
+  float* scale_shift = nullptr;         // 9 * dim
+  float* prompt_scale_shift = nullptr;  // 2 * dim
+  float* cross_table = nullptr;         // 5 * dim
+  int dim = 0, heads = 0, ff_hidden = 0;
+};
+
+// One stream's per-forward inputs (device pointers; see ltx_stream_io).
+struct StreamIO {
+  __nv_bfloat16* x = nullptr;
+  const __nv_bfloat16* context = nullptr;
+  const __nv_bfloat16* timesteps = nullptr;
+  const __nv_bfloat16* cross_scale_shift = nullptr;
+  const __nv_bfloat16* cross_gate = nullptr;
+  const __nv_bfloat16* prompt_timestep = nullptr;
+  const float* pe_cos = nullptr;
+  const float* pe_sin = nullptr;
+  const float* cpe_cos = nullptr;
+  const float* cpe_sin = nullptr;
+  int tokens = 0, text_tokens = 0;
+  bool present = true;
+};
+
+class CudaBlock {
+public:
+  CudaBlock(CudaOps* ops, int vdim, int vheads, int adim, int aheads)
+      : _ops(ops), _vdim(vdim), _vheads(vheads), _adim(adim), _aheads(aheads)
+  {
+  }
+  ~CudaBlock();
+
+  // Stage one tensor under its reference name.  Quantized linears arrive as
+  // w8g64 packs; every other tensor as f32 (host or device).
+  bool set_qlinear(const std::string& name, const uint32_t* codes,
+                   const void* scales, const void* biases, int sb_dtype, int N,
+                   int K, bool on_device, std::string* err);
+  bool set_tensor(const std::string& name, const float* data, int rows,
+                  int cols, bool on_device, std::string* err);
+
+  // Assemble the block: every required tensor must be present (the
+  // reference refuses a partial map, src/ltx25-block-ref.cc:424-432), fuse
+  // the q/k/v and k/v packs, upload the rest.  Frees the staged parts.
+  bool finalize(std::string* err);
+
+  // Size the scratch arena once for the largest geometry.
+  bool reserve(int max_video, int max_audio, int max_text, std::string* err);
+
+  // Run the block; video.x / audio.x are updated in place.
+  bool forward(cudaStream_t s, StreamIO& video, StreamIO& audio,
+               std::string* err);
+
+  bool finalized() const { return _final; }
+
+private:
+  struct Staged {
+    QWeight q;          // quantized linear
+    std::vector<float> host;
+    float* dev_f32 = nullptr;   // caller's device pointer (on_device)
+    int rows = 0, cols = 0;
+    bool quant = false;
+  };
+  bool build_attn_(const std::string& prefix, bool self, int qdim, int kvdim,
+                   int heads, int head_dim, int odim, CudaAttn& a,
+                   std::string* err);
+  bool build_stream_(bool audio, CudaStreamW& w, std::string* err);
+  bool attend_(cudaStream_t s, const CudaAttn& a, const __nv_bfloat16* xq,
+               int tq, const __nv_bfloat16* xkv, int tkv, const float* qcos,
+               const float* qsin, const float* kcos, const float* ksin,
+               __nv_bfloat16* out, std::string* err);
+  bool first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
+                   std::string* err);
+  bool ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
+           std::string* err);
+  bool take_f32_(const std::string& name, size_t count, float** out,
+                 std::string* err, bool required = true);
+  bool take_bf16_(const std::string& name, size_t count, __nv_bfloat16** out,
+                  std::string* err, bool required = true);
+  bool fuse_(const std::vector<const QWeight*>& parts, QWeight* out,
+             std::string* err);
+
+  CudaOps* _ops;
+  int _vdim, _vheads, _adim, _aheads;
+  std::map<std::string, Staged> _staged;
+  std::vector<void*> _owned;   // device buffers this block frees
+  CudaStreamW _video, _audio;
+  CudaAttn _a2v, _v2a;
+  bool _final = false;
+
+  // scratch arena
+  struct Arena {
+    __nv_bfloat16 *normed = nullptr, *qkv = nullptr, *qn = nullptr,
+                  *kn = nullptr, *att = nullptr, *glog = nullptr,
+                  *ctxmod = nullptr, *kvp = nullptr, *ff = nullptr,
+                  *qv = nullptr, *kva = nullptr, *qa = nullptr, *kvv = nullptr;
+    float* mods = nullptr;   // adaLN rows, f32
+    size_t tokens = 0;
+  } _ar;
+};
+
+}  // namespace ltx25

@@ -156,7 +156,7 @@ bool CudaOps::i8_takes(int M, int K, int N) const
   // The reference's gates (src/ltx25-metal-ops.cc:381-391): the int8 tier
   // pays back its quantize passes only on tall, deep GEMMs.  K must fill
   // whole 128-byte int8 K tiles here.
-  return _i8 && M >= 1024 && K >= 1024 && K % 128 == 0 && N % 8 == 0;
+  return _i8 && M >= 1024 && K >= 1024 && K % 128 == 0 && N % 4 == 0;
 }
 
 bool CudaOps::prepare_i8(QWeight& w, cudaStream_t s, std::string* err) const
@@ -188,7 +188,7 @@ bool CudaOps::prepare_i8(QWeight& w, cudaStream_t s, std::string* err) const
 bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
                     const void* wptr, const uint32_t* sz,
                     const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy,
-                    int M, int K, int N, int epi, const __nv_bfloat16* gate,
+                    int M, int K, int N, int epi, const float* gate,
                     const float* sx, const float* sw, std::string* err)
 {
   const Plan pl = plan_gemm(mode, M, N, K, _sms);
@@ -233,7 +233,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
 bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
                      const QWeight& w, const __nv_bfloat16* bias,
                      __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
-                     const __nv_bfloat16* gate, std::string* err)
+                     const float* gate, std::string* err)
 {
   if (x == nullptr || y == nullptr) {
     if (err) *err = "linear: null x or y";
@@ -248,8 +248,8 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
   }
   if (!aligned(x, 16) || ldx % 8 != 0 || ldx < K || !aligned(y, 4) ||
       ldy % 2 != 0 || ldy < N || (bias && !aligned(bias, 4)) ||
-      (gate && !aligned(gate, 4))) {
-    if (err) *err = "linear: x must be 16-byte aligned with ldx % 8 == 0; y, bias, gate 4-byte aligned";
+      (gate && !aligned(gate, 8))) {
+    if (err) *err = "linear: x must be 16-byte aligned with ldx % 8 == 0; y, bias 4-byte, gate 8-byte aligned";
     return false;
   }
   if (epi == ltx::EPI_GATED_RES && gate == nullptr) {
@@ -314,8 +314,8 @@ bool upload_qweight(const CudaOps& ops, const uint32_t* codes,
              " is not run by this build (only the w8g64 pack)";
     return false;
   }
-  if (N <= 0 || K <= 0 || K % 64 != 0 || N % 8 != 0) {
-    if (err) *err = "upload: need K % 64 == 0 and N % 8 == 0, got N=" +
+  if (N <= 0 || K <= 0 || K % 64 != 0 || N % 4 != 0) {
+    if (err) *err = "upload: need K % 64 == 0 and N % 4 == 0, got N=" +
                     std::to_string(N) + " K=" + std::to_string(K);
     return false;
   }
@@ -366,8 +366,8 @@ bool upload_dweight(const CudaOps& ops, const uint16_t* wsrc, int N, int K,
     if (err) *err = "upload: null tensor";
     return false;
   }
-  if (N <= 0 || K <= 0 || K % 64 != 0 || N % 8 != 0) {
-    if (err) *err = "upload: dense weight needs K % 64 == 0 and N % 8 == 0";
+  if (N <= 0 || K <= 0 || K % 64 != 0 || N % 2 != 0) {
+    if (err) *err = "upload: dense weight needs K % 64 == 0 and N % 2 == 0";
     return false;
   }
   QWeight w;

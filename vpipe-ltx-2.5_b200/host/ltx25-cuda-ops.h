@@ -47,7 +47,7 @@ public:
   bool linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
               const QWeight& w, const __nv_bfloat16* bias, __nv_bfloat16* y,
               int ldy, int M, int K, int N, int epi,
-              const __nv_bfloat16* gate, std::string* err);
+              const float* gate, std::string* err);
 
   void set_route(Route r) { _route = r; }
   Route route() const { return _route; }
@@ -88,7 +88,7 @@ private:
   bool gemm_(cudaStream_t s, int mode, const void* x, int ldx,
              const void* wptr, const uint32_t* sz, const __nv_bfloat16* bias,
              __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
-             const __nv_bfloat16* gate, const float* sx, const float* sw,
+             const float* gate, const float* sx, const float* sw,
              std::string* err);
 
   int _dev = -1;

@@ -50,7 +50,31 @@ SIGNATURES = {
     "ltx_dequant": (_I, [_P, _P, _P, _P]),
     "ltx_quant_rows_i8": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "ltx_pack_w8g64": (_I, [_P, _P, _I, _I, _P, _P, _P, _P]),
+    "ltx_ada_zero": (_I, [_P, _P, _P, _I, _I, _P, _P, _I, _P]),
+    "ltx_qk_norm_rope": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "ltx_attention": (_I, [_P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _I,
+                           _I, _I, _P]),
+    "ltx_block_create": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_P)]),
+    "ltx_block_destroy": (None, [_P]),
+    "ltx_block_last_error": (ctypes.c_char_p, [_P]),
+    "ltx_block_set_qlinear": (_I, [_P, ctypes.c_char_p, _P, _P, _P, _I, _I, _I,
+                                   _I]),
+    "ltx_block_set_tensor": (_I, [_P, ctypes.c_char_p, _P, _I, _I, _I]),
+    "ltx_block_finalize": (_I, [_P]),
+    "ltx_block_reserve": (_I, [_P, _I, _I, _I]),
+    "ltx_block_forward": (_I, [_P, _P, _P, _P]),
 }
+
+
+class StreamIO(ctypes.Structure):
+    """ltx_stream_io (include/ltx25_cuda.h)."""
+    _fields_ = [
+        ("x", _P), ("context", _P), ("timesteps", _P),
+        ("cross_scale_shift", _P), ("cross_gate", _P),
+        ("prompt_timestep", _P), ("pe_cos", _P), ("pe_sin", _P),
+        ("cross_pe_cos", _P), ("cross_pe_sin", _P), ("tokens", _I),
+        ("text_tokens", _I), ("present", _I),
+    ]
 
 
 class LtxError(RuntimeError):
@@ -241,3 +265,161 @@ def pack_w8g64(ctx, w, stream=None):
                                    _ptr(scales), _ptr(biases), _stream(stream)),
             "pack_w8g64")
     return codes, scales, biases
+
+
+def ada_zero(ctx, x, scale=None, shift=None, normalize=True, out=None,
+             stream=None):
+    import torch
+    rows, dim = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    ctx._ok(ctx.lib.ltx_ada_zero(ctx.h, _ptr(x), _ptr(out), rows, dim,
+                                 _ptr(scale), _ptr(shift), int(normalize),
+                                 _stream(stream)), "ada_zero")
+    return out
+
+
+def qk_norm_rope(ctx, x, heads, head_dim, gain=None, cos=None, sin=None,
+                 rows=None, stream=None):
+    import torch
+    rows = x.shape[0] if rows is None else rows
+    out = torch.empty((rows, heads * head_dim), dtype=torch.bfloat16,
+                      device=x.device)
+    ctx._ok(ctx.lib.ltx_qk_norm_rope(ctx.h, _ptr(x), x.stride(0), _ptr(out),
+                                     rows, heads, head_dim, _ptr(gain),
+                                     _ptr(cos), _ptr(sin), _stream(stream)),
+            "qk_norm_rope")
+    return out
+
+
+def attention(ctx, q, k, v, heads, head_dim, gate=None, tq=None, tk=None,
+              stream=None):
+    import torch
+    tq = q.shape[0] if tq is None else tq
+    tk = k.shape[0] if tk is None else tk
+    o = torch.empty((tq, heads * head_dim), dtype=torch.bfloat16,
+                    device=q.device)
+    ctx._ok(ctx.lib.ltx_attention(
+        ctx.h, _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v),
+        v.stride(0), _ptr(o), o.stride(0), _ptr(gate),
+        0 if gate is None else gate.stride(0), tq, tk, heads, head_dim,
+        _stream(stream)), "attention")
+    return o
+
+
+def is_quantized_name(name, ndim):
+    """The w8g64 recipe's choice for a block tensor: every 2-D linear in the
+    blocks except the gate logits and the adaLN tables
+    (src/ltx25-quant-family.cc:50-71)."""
+    return ndim == 2 and "to_gate_logits" not in name and "scale_shift" not in name
+
+
+class Block:
+    """ltx_block: one joint audio-video DiT block on the GPU."""
+
+    def __init__(self, ctx, vdim, vheads, adim, aheads):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        ctx._ok(ctx.lib.ltx_block_create(ctx.h, vdim, vheads, adim, aheads,
+                                         ctypes.byref(h)), "block_create")
+        self.h = h
+        self._keep = []
+
+    def err(self):
+        return self.ctx.lib.ltx_block_last_error(self.h).decode()
+
+    def _ok(self, rc, what):
+        if rc != LTX_OK:
+            raise LtxError(rc, f"{what}: {self.err()}")
+
+    def set_qlinear(self, name, codes, scales, biases, N, K, on_device=True,
+                    sb_dtype=SB_BF16):
+        self._ok(self.ctx.lib.ltx_block_set_qlinear(
+            self.h, name.encode(), _ptr(codes), _ptr(scales), _ptr(biases),
+            sb_dtype, N, K, int(on_device)), f"set_qlinear({name})")
+
+    def set_tensor(self, name, t):
+        """t: device f32 torch tensor (1-D or 2-D)."""
+        t = t.contiguous()
+        self._keep.append(t)
+        rows, cols = (t.shape[0], t.shape[1]) if t.dim() == 2 else (t.numel(), 0)
+        self._ok(self.ctx.lib.ltx_block_set_tensor(
+            self.h, name.encode(), _ptr(t), rows, cols, 1),
+            f"set_tensor({name})")
+
+    def load(self, tensors, device="cuda"):
+        """Stage a name -> f32 array map: 2-D linears are w8g64-packed on the
+        device (bit-identical to the reference packer), the rest as is.
+        Returns the dequantized f32 weights the GPU will use, as numpy (for
+        an oracle run on the same weights)."""
+        import numpy as np
+        import torch
+        deq = {}
+        for name, arr in tensors.items():
+            t = torch.as_tensor(np.ascontiguousarray(arr, dtype=np.float32)).to(device)
+            if is_quantized_name(name, t.dim()):
+                N, K = t.shape
+                c, s, b = pack_w8g64(self.ctx, t)
+                self.set_qlinear(name, c, s, b, N, K)
+                q = QWeight.upload(self.ctx, c, s, b, N, K, on_device=True)
+                deq[name] = dequant(self.ctx, q).float().cpu().numpy()
+                q.free()
+            else:
+                self.set_tensor(name, t)
+                deq[name] = np.asarray(arr, dtype=np.float32)
+        torch.cuda.synchronize()
+        return deq
+
+    def finalize(self):
+        # Staged device tensors are read here; they may be dropped after.
+        self._ok(self.ctx.lib.ltx_block_finalize(self.h), "block_finalize")
+        self._keep = []
+
+    def reserve(self, max_video, max_audio, max_text):
+        self._ok(self.ctx.lib.ltx_block_reserve(self.h, max_video, max_audio,
+                                                max_text), "block_reserve")
+
+    @staticmethod
+    def make_io(s):
+        """s: dict of device tensors (x, context, timesteps, cross_scale_shift,
+        cross_gate, prompt_timestep, pe=(cos, sin), cross_pe=(cos, sin),
+        present)."""
+        io = StreamIO()
+        if s is None:
+            io.present = 0
+            return io
+        io.x = _ptr(s["x"])
+        io.context = _ptr(s.get("context"))
+        io.timesteps = _ptr(s.get("timesteps"))
+        io.cross_scale_shift = _ptr(s.get("cross_scale_shift"))
+        io.cross_gate = _ptr(s.get("cross_gate"))
+        io.prompt_timestep = _ptr(s.get("prompt_timestep"))
+        pe = s.get("pe")
+        if pe is not None:
+            io.pe_cos, io.pe_sin = _ptr(pe[0]), _ptr(pe[1])
+        cpe = s.get("cross_pe")
+        if cpe is not None:
+            io.cross_pe_cos, io.cross_pe_sin = _ptr(cpe[0]), _ptr(cpe[1])
+        io.tokens = s["x"].shape[0]
+        io.text_tokens = 0 if s.get("context") is None else s["context"].shape[0]
+        io.present = int(s.get("present", True))
+        return io
+
+    def forward(self, video, audio, stream=None):
+        v = self.make_io(video)
+        a = self.make_io(audio)
+        self._ok(self.ctx.lib.ltx_block_forward(self.h, ctypes.byref(v),
+                                                ctypes.byref(a),
+                                                _stream(stream)),
+                 "block_forward")
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            self.ctx.lib.ltx_block_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
