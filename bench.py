@@ -218,6 +218,72 @@ def sample_desc():
             "outside the timing")
 
 
+def run_block(args):
+    """one joint AV block, 8160 video + 126 audio + 256
+    text tokens at the real widths, synthetic w8g64 weights."""
+    import torch
+    import ltx25_b200 as L
+    from ltx25_b200 import synth
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    vdim, vh, adim, ah = 4096, 32, 2048, 32
+    frames, hh, ww, at, tt = 16, 17, 30, 126, 256
+    vt = frames * hh * ww
+    blk = synth.load_random_block(ctx, vdim, vh, adim, ah, seed=7)
+    blk.reserve(vt, at, tt)
+    v_self, a_self, v_cross, a_cross = L.geometry_tables(frames, hh, ww, at, vdim, vh, adim, ah)
+    dt = lambda t: (torch.from_numpy(t[0]).to(dev), torch.from_numpy(t[1]).to(dev))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    v = synth.random_stream_inputs(vdim, vt, tt, vh, gen, pe=dt(v_self), cross_pe=dt(v_cross))
+    a = synth.random_stream_inputs(adim, at, tt, ah, gen, pe=dt(a_self), cross_pe=dt(a_cross))
+    x0v, x0a = v["x"].clone(), a["x"].clone()
+    for _ in range(args.warmup):
+        blk.forward(v, a)
+    torch.cuda.synchronize()
+    ctx.check()
+    times = []
+    for _ in range(args.steps):
+        v["x"].copy_(x0v)
+        a["x"].copy_(x0a)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        blk.forward(v, a)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ctx.check()
+    ms = statistics.median(times)
+    gemm_flops = 0.0
+    for (M, K, N) in [(vt, vdim, 3 * vdim), (vt, vdim, vdim), (vt, vdim, vdim), (tt, vdim, 2 * vdim),
+                      (vt, vdim, vdim), (vt, vdim, 4 * vdim), (vt, 4 * vdim, vdim),
+                      (at, adim, 3 * adim), (at, adim, adim), (at, adim, adim), (tt, adim, 2 * adim),
+                      (at, adim, adim), (at, adim, 4 * adim), (at, 4 * adim, adim),
+                      (vt, vdim, adim), (at, adim, 2 * adim), (vt, adim, vdim),
+                      (at, adim, adim), (vt, vdim, 2 * adim), (at, adim, adim)]:
+        gemm_flops += flops(M, K, N)
+    attn_flops = 4.0 * (vt * vt * vdim + vt * tt * vdim + at * at * adim + at * tt * adim
+                        + vt * at * adim + at * vt * adim)
+    line = {
+        "metric": "DiT joint AV block forward ms @960x544x121 (BASELINE config 4)",
+        "value": round(ms, 3), "unit": "ms", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": False,
+        "dtype": "bf16", "data": "synthetic (seeded device-generated weights, w8g64)",
+        "config": {"workload": "one block: video 8160x4096 (16x17x30), audio 126x2048, "
+                               "text 256, 3-axis video RoPE, 1-D audio RoPE"},
+        "algorithmic_tflop": round((gemm_flops + attn_flops) / 1e12, 3),
+        "tflops": round((gemm_flops + attn_flops) / (ms * 1e-3) / 1e12, 1),
+        "gemm_tflop": round(gemm_flops / 1e12, 3), "attention_tflop": round(attn_flops / 1e12, 3),
+    }
+    print(json.dumps(line), flush=True)
+    blk.close()
+    ctx.close()
+    return 0
+
+
 def run_reference(args):
     world, rank, _ = dist_setup()
     if rank != 0:
@@ -262,7 +328,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", type=int, default=None,
                     help="profile one sweep shape (index into SHAPES)")
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "block"],
+                    help="sweep: BASELINE config 2 (the headline); block: one "
+                         "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
+    if args.workload == "block" and args.impl == "ours":
+        return run_block(args)
     if args.only is not None:
         SHAPES[:] = [SHAPES[args.only]]
     args.warmup = max(args.warmup, 3)

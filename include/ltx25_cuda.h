@@ -204,6 +204,29 @@ LTX_API int ltx_attention(ltx_ctx* ctx, const void* q, int ldq, const void* k,
                           const void* gate_logits, int ldg, int tq, int tk,
                           int heads, int head_dim, void* stream);
 
+/* ---- RoPE tables (host, once per generation) ----------------------------
+ * The reference's build_rope / video_spans / audio_time_seconds
+ * (src/ltx25-rope.cc:74-296), computed on the host into caller buffers; no
+ * device or context needed.  starts/ends are [n_axes][tokens] doubles, the
+ * tables [heads][tokens][inner_dim/heads/2] f32.  theta 10000 and
+ * f64_precision 1 are LTX-2.5's values. */
+LTX_API int ltx_rope_table(const double* starts, const double* ends,
+                           int n_axes, int tokens, const int* max_pos,
+                           int inner_dim, int heads, double theta,
+                           int f64_precision, float* cos_out, float* sin_out);
+
+/* Per-token (start, end) of a [frames][height][width] latent in pixels (h,
+ * w) and seconds (t), w fastest, causal first frame (video_spans,
+ * src/ltx25-rope.cc:180-247).  starts/ends: [3][frames*height*width]. */
+LTX_API int ltx_rope_video_spans(int frames, int height, int width,
+                                 int scale_t, int scale_h, int scale_w,
+                                 double fps, int causal_fix, double* starts,
+                                 double* ends);
+
+/* Audio latent token spans in seconds (audio_time_seconds,
+ * src/ltx25-rope.cc:262-276): tokens of 4 mel frames, hop 160 at 16 kHz. */
+LTX_API int ltx_rope_audio_seconds(int tokens, double* starts, double* ends);
+
 /* ---- the joint audio-video block ---------------------------------------
  * Replaces MetalBlock (src/ltx25-block-metal.h:245-371) with the math of
  * block_forward (src/ltx25-block-ref.cc:308-389). */

@@ -112,7 +112,12 @@ def _attn_params(t, prefix):
     return {k: t.get(f"{prefix}.{k}") for k in keys}
 
 
-def stream_first_half(t, pre, s, dim, heads, eps):
+def _upd(x, sub, gate, x_round):
+    y = (x + sub * gate).astype(F32)
+    return x_round(y) if x_round is not None else y
+
+
+def stream_first_half(t, pre, s, dim, heads, eps, x_round=None):
     """src/ltx25-block-ref.cc:196-262."""
     hd = dim // heads
     table = t[f"{pre}scale_shift_table"]
@@ -120,7 +125,7 @@ def stream_first_half(t, pre, s, dim, heads, eps):
     normed = ada_zero(s["x"], eps, msa[1], msa[0])
     sa = attention(_attn_params(t, f"{pre}attn1"), normed, normed, s.get("pe"),
                    None, heads, hd)
-    s["x"] = (s["x"] + sa * msa[2]).astype(F32)
+    s["x"] = _upd(s["x"], sa, msa[2], x_round)
     xn = rms_norm(s["x"], eps)
     ca = ada_values(table, s["timesteps"], dim, 6, 9)
     qin = mod(xn, ca[1], ca[0])
@@ -134,7 +139,7 @@ def stream_first_half(t, pre, s, dim, heads, eps):
         scale = (scale + pts[dim:2 * dim]).astype(F32)
     kv = mod(s["context"], scale, shift)
     co = attention(_attn_params(t, f"{pre}attn2"), qin, kv, None, None, heads, hd)
-    s["x"] = (s["x"] + co * ca[2]).astype(F32)
+    s["x"] = _upd(s["x"], co, ca[2], x_round)
 
 
 def gelu_tanh(h):
@@ -144,7 +149,7 @@ def gelu_tanh(h):
     return (0.5 * x * (1.0 + np.tanh(u))).astype(F32)
 
 
-def stream_ff(t, pre, s, dim, eps):
+def stream_ff(t, pre, s, dim, eps, x_round=None):
     """src/ltx25-block-ref.cc:264-281."""
     table = t[f"{pre}scale_shift_table"]
     mlp = ada_values(table, s["timesteps"], dim, 3, 6)
@@ -153,7 +158,7 @@ def stream_ff(t, pre, s, dim, eps):
                t.get(f"{pre}ff.net.0.proj.bias"))
     h = gelu_tanh(h)
     o = linear(h, t[f"{pre}ff.net.2.weight"], t.get(f"{pre}ff.net.2.bias"))
-    s["x"] = (s["x"] + o * mlp[2]).astype(F32)
+    s["x"] = _upd(s["x"], o, mlp[2], x_round)
 
 
 def av_ada(table, css, cg, dim, lo):
@@ -165,9 +170,12 @@ def av_ada(table, css, cg, dim, lo):
     return ss[0], ss[1], gate
 
 
-def block_forward(t, video, audio, vdim, vheads, adim, aheads, eps=EPS):
+def block_forward(t, video, audio, vdim, vheads, adim, aheads, eps=EPS,
+                  x_round=None):
     """src/ltx25-block-ref.cc:308-389.  Returns (video_x, audio_x); the
-    input dicts are not modified."""
+    input dicts are not modified.  `x_round`, when given, is applied to the
+    residual stream after every update -- to model a device that stores x
+    in bf16 (the reference's GPU block does); None is the reference's f32."""
     v = dict(video)
     a = dict(audio)
     v["x"] = np.asarray(v["x"], F32).copy()
@@ -177,9 +185,9 @@ def block_forward(t, video, audio, vdim, vheads, adim, aheads, eps=EPS):
     if not rv and not ra:
         raise ValueError("neither stream is present")
     if rv:
-        stream_first_half(t, "", v, vdim, vheads, eps)
+        stream_first_half(t, "", v, vdim, vheads, eps, x_round)
     if ra:
-        stream_first_half(t, "audio_", a, adim, aheads, eps)
+        stream_first_half(t, "audio_", a, adim, aheads, eps, x_round)
     if rv and ra:
         vx_pre = v["x"].copy()
         ax_pre = a["x"].copy()
@@ -192,18 +200,18 @@ def block_forward(t, video, audio, vdim, vheads, adim, aheads, eps=EPS):
         kv = ada_zero(ax_pre, eps, asc, ash)
         o = attention(_attn_params(t, "audio_to_video_attn"), qv, kv,
                       v.get("cross_pe"), a.get("cross_pe"), aheads, ahd)
-        v["x"] = (v["x"] + o * vg).astype(F32)
+        v["x"] = _upd(v["x"], o, vg, x_round)
         asc, ash, ag = av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 2)
         vsc, vsh, _ = av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 2)
         qa = ada_zero(ax_pre, eps, asc, ash)
         kvv = ada_zero(vx_pre, eps, vsc, vsh)
         o = attention(_attn_params(t, "video_to_audio_attn"), qa, kvv,
                       a.get("cross_pe"), v.get("cross_pe"), aheads, ahd)
-        a["x"] = (a["x"] + o * ag).astype(F32)
+        a["x"] = _upd(a["x"], o, ag, x_round)
     if rv:
-        stream_ff(t, "", v, vdim, eps)
+        stream_ff(t, "", v, vdim, eps, x_round)
     if ra:
-        stream_ff(t, "audio_", a, adim, eps)
+        stream_ff(t, "audio_", a, adim, eps, x_round)
     return v["x"], a["x"]
 
 

@@ -9,8 +9,12 @@ the GPU uses: the w8g64-dequantized linears and bf16-rounded biases / gate
 weights / inputs.
 
 Bars: the reference's per-block bf16 figure is ~6e-3 rel-L2 on the output
-(README.md:85); the block's own contribution (output - input) is checked at
-3e-2 so that a broken sub-layer cannot hide behind the residual stream.
+(README.md:85).  The block's own contribution (output - input) is checked
+too, so that a broken sub-layer cannot hide behind the residual stream: at
+2e-2 against an oracle that stores the residual stream in bf16 after every
+update, as the device does (measured 1.2-1.3 %, the bf16 activations, q/k
+and attention probabilities of four gated sub-layers; against the f32-stream
+oracle it is 2-3 %, the difference being the stream's own bf16 storage).
 """
 import numpy as np
 import pytest
@@ -20,7 +24,7 @@ from oracle import block_np, lib, rope_np
 pytestmark = pytest.mark.gpu
 
 OUT_BAR = 6e-3
-DELTA_BAR = 3e-2
+DELTA_BAR = 2e-2
 
 
 def bf16r(a):
@@ -147,16 +151,18 @@ def run_and_compare(blk, ow, ins, cfg, mode):
     torch.cuda.synchronize()
     wv, wa = block_np.block_forward(ow, v, a, cfg["vdim"], cfg["vheads"],
                                     cfg["adim"], cfg["aheads"])
+    bv, ba = block_np.block_forward(ow, v, a, cfg["vdim"], cfg["vheads"],
+                                    cfg["adim"], cfg["aheads"], x_round=bf16r)
     res = {}
-    for name, d, want, present in (("video", dv, wv, v["present"]),
-                                   ("audio", da, wa, a["present"])):
+    for name, d, want, wantb, present in (("video", dv, wv, bv, v["present"]),
+                                          ("audio", da, wa, ba, a["present"])):
         got = host(d["x"])
         x0 = ins[name]["x"]
         if not present:
             assert np.array_equal(got, x0), f"{name} absent but modified"
             continue
         out_r = lib.rel_l2(got, want)
-        delta_r = lib.rel_l2(got - x0, want - x0)
+        delta_r = lib.rel_l2(got - x0, wantb - x0)
         res[name] = (out_r, delta_r)
         assert out_r < OUT_BAR, f"{mode}/{name}: output rel-L2 {out_r:.3e}"
         assert delta_r < DELTA_BAR, f"{mode}/{name}: delta rel-L2 {delta_r:.3e}"

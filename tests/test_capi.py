@@ -52,3 +52,23 @@ def test_context_creation_fails_loudly_without_an_sm100_device():
     import ltx25_b200 as L
     with pytest.raises(L.LtxError):
         L.Context(0)
+
+
+def test_rope_tables_match_reference_golden(golden):
+    """The product's host RoPE builder against the reference's own tables
+    (src/ltx25-rope.cc, frozen in tests/golden/rope.npz)."""
+    import numpy as np
+    import ltx25_b200 as L
+    g = golden("rope.npz")
+    s, e = L.video_spans(2, 3, 4)
+    c, sn = L.rope_table(s, e, [20, 2048, 2048], 96, 4)
+    np.testing.assert_allclose(c, g["video__cos"], atol=1.2e-7)
+    np.testing.assert_allclose(sn, g["video__sin"], atol=1.2e-7)
+    a_s, a_e = L.audio_seconds(7)
+    c, sn = L.rope_table(a_s, a_e, [20], 64, 4)
+    np.testing.assert_allclose(c, g["audio__cos"], atol=1.2e-7)
+    np.testing.assert_array_equal(a_s[:9 if len(a_s) >= 9 else len(a_s)], g["atime"][:len(a_s)])
+    c, sn = L.rope_table(g["cross__starts"], g["cross__ends"], [20], 32, 4)
+    np.testing.assert_allclose(c, g["cross__cos"], atol=1.2e-7)
+    # spans: the time axis equals the reference's video_time_seconds
+    np.testing.assert_array_equal(np.unique(s[0]), g["vtime"][:2])

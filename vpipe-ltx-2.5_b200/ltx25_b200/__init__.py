@@ -63,6 +63,11 @@ SIGNATURES = {
     "ltx_block_finalize": (_I, [_P]),
     "ltx_block_reserve": (_I, [_P, _I, _I, _I]),
     "ltx_block_forward": (_I, [_P, _P, _P, _P]),
+    "ltx_rope_table": (_I, [_P, _P, _I, _I, _P, _I, _I, ctypes.c_double, _I,
+                            _P, _P]),
+    "ltx_rope_video_spans": (_I, [_I, _I, _I, _I, _I, _I, ctypes.c_double, _I,
+                                  _P, _P]),
+    "ltx_rope_audio_seconds": (_I, [_I, _P, _P]),
 }
 
 
@@ -423,3 +428,64 @@ class Block:
             self.close()
         except Exception:
             pass
+
+
+# ---- RoPE tables (host) --------------------------------------------------
+
+def _np_ptr(a):
+    return a.ctypes.data_as(_P)
+
+
+def rope_table(starts, ends, max_pos, inner_dim, heads, theta=10000.0,
+               f64_precision=True):
+    """cos, sin [heads][tokens][half] f32 numpy (ltx_rope_table)."""
+    import numpy as np
+    starts = np.ascontiguousarray(np.atleast_2d(starts), dtype=np.float64)
+    ends = np.ascontiguousarray(np.atleast_2d(ends), dtype=np.float64)
+    n_axes, tokens = starts.shape
+    mp = np.ascontiguousarray(np.atleast_1d(max_pos), dtype=np.int32)
+    half = inner_dim // heads // 2
+    cos = np.empty((heads, tokens, half), np.float32)
+    sin = np.empty((heads, tokens, half), np.float32)
+    rc = load().ltx_rope_table(_np_ptr(starts), _np_ptr(ends), n_axes, tokens,
+                               _np_ptr(mp), inner_dim, heads, theta,
+                               int(f64_precision), _np_ptr(cos), _np_ptr(sin))
+    if rc != LTX_OK:
+        raise LtxError(rc, "rope_table")
+    return cos, sin
+
+
+def video_spans(frames, height, width, scale=(8, 32, 32), fps=24.0,
+                causal_fix=True):
+    import numpy as np
+    T = frames * height * width
+    s = np.empty((3, T), np.float64)
+    e = np.empty((3, T), np.float64)
+    rc = load().ltx_rope_video_spans(frames, height, width, scale[0], scale[1],
+                                     scale[2], fps, int(causal_fix),
+                                     _np_ptr(s), _np_ptr(e))
+    if rc != LTX_OK:
+        raise LtxError(rc, "video_spans")
+    return s, e
+
+
+def audio_seconds(tokens):
+    import numpy as np
+    s = np.empty(tokens, np.float64)
+    e = np.empty(tokens, np.float64)
+    rc = load().ltx_rope_audio_seconds(tokens, _np_ptr(s), _np_ptr(e))
+    if rc != LTX_OK:
+        raise LtxError(rc, "audio_seconds")
+    return s, e
+
+
+def geometry_tables(frames, height, width, audio_tokens, vdim, vheads, adim,
+                    aheads, max_pos_v=(20, 2048, 2048), max_pos_a=20):
+    """The four tables one generation needs: video self (3 axes), audio self
+    (seconds), and the two time-only cross tables at the audio width."""
+    s, e = video_spans(frames, height, width)
+    v_self = rope_table(s, e, list(max_pos_v), vdim, vheads)
+    v_cross = rope_table(s[0:1], e[0:1], [max_pos_a], adim, aheads)
+    a_s, a_e = audio_seconds(audio_tokens)
+    a_self = rope_table(a_s, a_e, [max_pos_a], adim, aheads)
+    return v_self, a_self, v_cross, a_self
