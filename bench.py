@@ -218,6 +218,106 @@ def sample_desc():
             "outside the timing")
 
 
+def block_flops(vt, at, tt, vdim, adim):
+    """Algorithmic FLOPs of one joint block: its 20 GEMMs (fused q/k/v and
+    k/v counted as one) and the six attentions' QK^T and PV."""
+    gemm = 0.0
+    for (M, K, N) in [(vt, vdim, 3 * vdim), (vt, vdim, vdim), (vt, vdim, vdim), (tt, vdim, 2 * vdim),
+                      (vt, vdim, vdim), (vt, vdim, 4 * vdim), (vt, 4 * vdim, vdim),
+                      (at, adim, 3 * adim), (at, adim, adim), (at, adim, adim), (tt, adim, 2 * adim),
+                      (at, adim, adim), (at, adim, 4 * adim), (at, 4 * adim, adim),
+                      (vt, vdim, adim), (at, adim, 2 * adim), (vt, adim, vdim),
+                      (at, adim, adim), (vt, vdim, 2 * adim), (at, adim, adim)]:
+        gemm += flops(M, K, N)
+    attn = 4.0 * (vt * vt * vdim + vt * tt * vdim + at * at * adim + at * tt * adim
+                  + vt * at * adim + at * vt * adim)
+    return gemm, attn
+
+
+def run_stack(args):
+    """BASELINE config 5 on one GPU: one denoise step = the 48-block stack
+    over 8160 video + 126 audio + 256 text tokens, synthetic w8g64 weights,
+    one shared scratch arena."""
+    import torch
+    import ltx25_b200 as L
+    from ltx25_b200 import synth
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    vdim, vh, adim, ah = 4096, 32, 2048, 32
+    frames, hh, ww, at, tt = 16, 17, 30, 126, 256
+    vt = frames * hh * ww
+    nblk = args.blocks
+    st = L.Stack(ctx)
+    for i in range(nblk):
+        st.add(synth.load_random_block(ctx, vdim, vh, adim, ah, seed=7 + i))
+    st.reserve(vt, at, tt)
+    v_self, a_self, v_cross, a_cross = L.geometry_tables(frames, hh, ww, at, vdim, vh, adim, ah)
+    dt = lambda t: (torch.from_numpy(t[0]).to(dev), torch.from_numpy(t[1]).to(dev))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    v = synth.random_stream_inputs(vdim, vt, tt, vh, gen, pe=dt(v_self), cross_pe=dt(v_cross))
+    a = synth.random_stream_inputs(adim, at, tt, ah, gen, pe=dt(a_self), cross_pe=dt(a_cross))
+    x0v, x0a = v["x"].clone(), a["x"].clone()
+    for _ in range(args.warmup):
+        v["x"].copy_(x0v)
+        a["x"].copy_(x0a)
+        st.forward(v, a)
+    torch.cuda.synchronize()
+    ctx.check()
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    times = []
+    with ClockSampler(gpu_id) as clk:
+        for _ in range(args.steps):
+            v["x"].copy_(x0v)
+            a["x"].copy_(x0a)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            st.forward(v, a)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+    ctx.check()
+    peak_tf, _, peak_kind = peaks()
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak_tf = float(json.load(f)["bf16_tflops_sustained"])
+            peak_kind = "measured (sustained)"
+    except Exception:
+        pass
+    ok = bool(torch.isfinite(v["x"].float()).all() and torch.isfinite(a["x"].float()).all())
+    ms = statistics.median(times)
+    g, at_fl = block_flops(vt, at, tt, vdim, adim)
+    step_flops = nblk * (g + at_fl)
+    line = {
+        "metric": "DiT s/denoise-step @960x544x121 (BASELINE config 5, 48-block stack)",
+        "value": round(ms / 1e3, 4), "unit": "s/step", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded device-generated weights, w8g64)",
+        "config": {"workload": f"{nblk}-block joint AV stack: video 8160x4096 (16x17x30), "
+                               "audio 126x2048, text 256; inputs > L2 every step",
+                   "parallelism": "tp1"},
+        "algorithmic_tflop": round(step_flops / 1e12, 2),
+        "tflops": round(step_flops / (ms * 1e-3) / 1e12, 1),
+        "roofline": {"bound": "tensor", "achieved": round(step_flops / (ms * 1e-3) / 1e12, 1),
+                     "peak": peak_tf, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                     "frac": round(step_flops / (ms * 1e-3) / 1e12 / peak_tf, 3),
+                     "traffic": None},
+        "finite": ok, "clocks": clk.summary(),
+        "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+    st.close()
+    for b in st.blocks:
+        b.close()
+    ctx.close()
+    return 0
+
+
 def run_block(args):
     """one joint AV block, 8160 video + 126 audio + 256
     text tokens at the real widths, synthetic w8g64 weights."""
@@ -257,16 +357,7 @@ def run_block(args):
         times.append(e0.elapsed_time(e1))
     ctx.check()
     ms = statistics.median(times)
-    gemm_flops = 0.0
-    for (M, K, N) in [(vt, vdim, 3 * vdim), (vt, vdim, vdim), (vt, vdim, vdim), (tt, vdim, 2 * vdim),
-                      (vt, vdim, vdim), (vt, vdim, 4 * vdim), (vt, 4 * vdim, vdim),
-                      (at, adim, 3 * adim), (at, adim, adim), (at, adim, adim), (tt, adim, 2 * adim),
-                      (at, adim, adim), (at, adim, 4 * adim), (at, 4 * adim, adim),
-                      (vt, vdim, adim), (at, adim, 2 * adim), (vt, adim, vdim),
-                      (at, adim, adim), (vt, vdim, 2 * adim), (at, adim, adim)]:
-        gemm_flops += flops(M, K, N)
-    attn_flops = 4.0 * (vt * vt * vdim + vt * tt * vdim + at * at * adim + at * tt * adim
-                        + vt * at * adim + at * vt * adim)
+    gemm_flops, attn_flops = block_flops(vt, at, tt, vdim, adim)
     line = {
         "metric": "DiT joint AV block forward ms @960x544x121 (BASELINE config 4)",
         "value": round(ms, 3), "unit": "ms", "n_gpus": 1, "steps": args.steps,
@@ -328,12 +419,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", type=int, default=None,
                     help="profile one sweep shape (index into SHAPES)")
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "block"],
+    ap.add_argument("--blocks", type=int, default=48, help="stack depth (--workload stack)")
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "block", "stack"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
     if args.workload == "block" and args.impl == "ours":
         return run_block(args)
+    if args.workload == "stack" and args.impl == "ours":
+        args.warmup = max(args.warmup, 3)
+        return run_stack(args)
     if args.only is not None:
         SHAPES[:] = [SHAPES[args.only]]
     args.warmup = max(args.warmup, 3)

@@ -44,7 +44,8 @@ enum {
   LTX_E_OOM = -5,         /* device allocation failed */
   LTX_E_KERNEL = -6,      /* a kernel gave up on a bounded wait */
   LTX_E_STATE = -7,       /* call out of order (e.g. block not loaded) */
-  LTX_E_ALIGN = -8        /* a pointer is not 16-byte aligned */
+  LTX_E_ALIGN = -8,       /* a pointer is not 16-byte aligned */
+  LTX_E_ABORTED = -9      /* a progress callback asked to stop */
 };
 
 /* Data types of a pack's scales / zero-points as they arrive. */
@@ -280,6 +281,40 @@ LTX_API int ltx_block_reserve(ltx_block* b, int max_video_tokens,
  * (MetalBlock::forward, src/ltx25-block-metal.h:307-311). */
 LTX_API int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
                               const ltx_stream_io* audio, void* stream);
+
+/* ---- the block stack ----------------------------------------------------
+ * The block loop of Ltx25Dit::forward (src/ltx25-dit.cc:1716-1931): blocks
+ * run in order on the same stream inputs, x updated in place, and share ONE
+ * scratch arena (the reference's BlockScratch, src/ltx25-block-metal.h:
+ * 140-240).  The stack references its blocks without owning them: destroy
+ * the stack first. */
+typedef struct ltx_stack ltx_stack;
+
+/* Host-side progress hook, called before block `block` of `blocks` is
+ * enqueued (the reference's in.progress, src/ltx25-dit.cc:1718-1720).
+ * Return 0 to stop: the forward returns LTX_E_ABORTED with the blocks
+ * before it enqueued. */
+typedef int (*ltx_progress_fn)(int block, int blocks, void* user);
+
+LTX_API int ltx_stack_create(ltx_ctx* ctx, ltx_stack** out);
+LTX_API void ltx_stack_destroy(ltx_stack* s);
+LTX_API const char* ltx_stack_last_error(const ltx_stack* s);
+
+/* Append a finalized block of the same context and widths. */
+LTX_API int ltx_stack_add_block(ltx_stack* s, ltx_block* b);
+LTX_API int ltx_stack_size(const ltx_stack* s);
+
+/* Size the shared arena for the largest geometry; call after the last
+ * add_block (Ltx25Dit::set_geometry's reserve, src/ltx25-dit.cc:984-1204). */
+LTX_API int ltx_stack_reserve(ltx_stack* s, int max_video_tokens,
+                              int max_audio_tokens, int max_text_tokens);
+
+/* Run blocks [begin, end) (end < 0: to the last block) on `stream`.
+ * progress may be NULL. */
+LTX_API int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
+                              const ltx_stream_io* audio, int begin, int end,
+                              ltx_progress_fn progress, void* user,
+                              void* stream);
 
 #ifdef __cplusplus
 }

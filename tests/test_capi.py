@@ -43,6 +43,12 @@ def test_null_arguments_rejected_without_a_device():
     assert lib.ltx_qlinear(None, None, None, None, None, 1, 64, 8, None) == -1
     assert lib.ltx_set_tiers(None, 1, 0, 0) == -1
     assert lib.ltx_i8_takes(None, 8160, 4096, 4096) == 0
+    assert lib.ltx_stack_create(None, None) == -1
+    assert lib.ltx_stack_add_block(None, None) == -1
+    assert lib.ltx_stack_reserve(None, 1, 1, 1) == -1
+    assert lib.ltx_stack_forward(None, None, None, 0, -1, None, None, None) == -1
+    assert lib.ltx_stack_size(None) == 0
+    assert lib.ltx_stack_last_error(None) == b"null stack"
 
 
 def test_context_creation_fails_loudly_without_an_sm100_device():

@@ -1,8 +1,10 @@
 // capi.cc -- the extern "C" boundary declared in include/ltx25_cuda.h, over
 // the C++ host mirror (CudaOps and friends).
 #include <cstring>
+#include <memory>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/ltx25_cuda.h"
 #include "../csrc/kernels.h"
@@ -420,6 +422,106 @@ int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
     if (e.find("neither stream") != std::string::npos || e.find("missing") != std::string::npos)
       code = LTX_E_NULL;
     return bfail(b, code, e);
+  }
+  return LTX_OK;
+}
+
+}  // extern "C"
+
+struct ltx_stack {
+  ltx_ctx* ctx = nullptr;
+  std::vector<ltx_block*> blocks;
+  std::shared_ptr<ltx25::BlockArena> arena;
+  bool reserved = false;
+  std::string err;
+};
+
+namespace {
+
+int sfail(ltx_stack* s, int code, const std::string& m)
+{
+  if (s != nullptr) s->err = m;
+  return code;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltx_stack_create(ltx_ctx* ctx, ltx_stack** out)
+{
+  if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  ltx_stack* s = new (std::nothrow) ltx_stack();
+  if (s == nullptr) return fail(ctx, LTX_E_OOM, "host allocation failed");
+  s->ctx = ctx;
+  *out = s;
+  return LTX_OK;
+}
+
+void ltx_stack_destroy(ltx_stack* s) { delete s; }
+
+const char* ltx_stack_last_error(const ltx_stack* s)
+{
+  return s == nullptr ? "null stack" : s->err.c_str();
+}
+
+int ltx_stack_add_block(ltx_stack* s, ltx_block* b)
+{
+  if (s == nullptr) return LTX_E_NULL;
+  if (b == nullptr) return sfail(s, LTX_E_NULL, "add_block: null block");
+  if (b->ctx != s->ctx) return sfail(s, LTX_E_STATE, "add_block: block of another context");
+  if (!b->blk->finalized()) return sfail(s, LTX_E_STATE, "add_block: block not finalized");
+  if (!s->blocks.empty() && !s->blocks[0]->blk->same_widths(*b->blk))
+    return sfail(s, LTX_E_SHAPE, "add_block: widths differ from block 0");
+  s->blocks.push_back(b);
+  s->reserved = false;
+  return LTX_OK;
+}
+
+int ltx_stack_size(const ltx_stack* s) { return s == nullptr ? 0 : (int)s->blocks.size(); }
+
+int ltx_stack_reserve(ltx_stack* s, int max_video_tokens, int max_audio_tokens,
+                      int max_text_tokens)
+{
+  if (s == nullptr) return LTX_E_NULL;
+  if (s->blocks.empty()) return sfail(s, LTX_E_STATE, "reserve: empty stack");
+  if (!s->arena) s->arena = std::make_shared<ltx25::BlockArena>();
+  std::string e;
+  for (ltx_block* b : s->blocks)
+    if (!b->blk->reserve(max_video_tokens, max_audio_tokens, max_text_tokens, &e,
+                         s->arena))
+      return sfail(s, code_for(e), e);
+  s->reserved = true;
+  return LTX_OK;
+}
+
+int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
+                      const ltx_stream_io* audio, int begin, int end,
+                      ltx_progress_fn progress, void* user, void* stream)
+{
+  if (s == nullptr) return LTX_E_NULL;
+  const int n = (int)s->blocks.size();
+  if (end < 0) end = n;
+  if (begin < 0 || begin > end || end > n)
+    return sfail(s, LTX_E_SHAPE, "forward: block range outside the stack");
+  if (!s->reserved) return sfail(s, LTX_E_STATE, "forward before reserve");
+  ltx25::StreamIO v = to_io(video), a = to_io(audio);
+  for (int i = begin; i < end; ++i) {
+    if (progress != nullptr && progress(i, n, user) == 0)
+      return sfail(s, LTX_E_ABORTED, "aborted at block " + std::to_string(i));
+    ltx25::CudaBlock* blk = s->blocks[(size_t)i]->blk;
+    if (blk->arena() != s->arena)
+      return sfail(s, LTX_E_STATE, "block " + std::to_string(i) +
+                                       " was reserved outside the stack");
+    std::string e;
+    if (!blk->forward(S(stream), v, a, &e)) {
+      int code = code_for(e);
+      if (e.find("arena") != std::string::npos) code = LTX_E_STATE;
+      if (e.find("neither stream") != std::string::npos || e.find("missing") != std::string::npos)
+        code = LTX_E_NULL;
+      return sfail(s, code, "block " + std::to_string(i) + ": " + e);
+    }
   }
   return LTX_OK;
 }

@@ -57,12 +57,6 @@ CudaBlock::~CudaBlock()
     free_qweight(&w->ff_out);
   }
   for (void* p : _owned) cudaFree(p);
-  for (void* p : {(void*)_ar.normed, (void*)_ar.qkv, (void*)_ar.qn,
-                  (void*)_ar.kn, (void*)_ar.att, (void*)_ar.glog,
-                  (void*)_ar.ctxmod, (void*)_ar.kvp, (void*)_ar.ff,
-                  (void*)_ar.qv, (void*)_ar.kva, (void*)_ar.qa,
-                  (void*)_ar.kvv, (void*)_ar.mods})
-    cudaFree(p);
 }
 
 bool CudaBlock::set_qlinear(const std::string& name, const uint32_t* codes,
@@ -336,8 +330,33 @@ bool CudaBlock::finalize(std::string* err)
   return true;
 }
 
+BlockArena::~BlockArena()
+{
+  for (void* p : {(void*)normed, (void*)qkv, (void*)qn, (void*)kn, (void*)att,
+                  (void*)glog, (void*)ctxmod, (void*)kvp, (void*)ff, (void*)qv,
+                  (void*)kva, (void*)qa, (void*)kvv, (void*)mods})
+    cudaFree(p);
+}
+
+bool BlockArena::ensure(int i, size_t n, std::string* err)
+{
+  void** slots[14] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
+                      (void**)&att, (void**)&glog, (void**)&ctxmod, (void**)&kvp,
+                      (void**)&ff, (void**)&qv, (void**)&kva, (void**)&qa,
+                      (void**)&kvv, (void**)&mods};
+  if (n <= cap[i]) return true;
+  const size_t elt = i == 13 ? sizeof(float) : sizeof(__nv_bfloat16);
+  cudaFree(*slots[i]);
+  *slots[i] = nullptr;
+  cap[i] = 0;
+  if (!cuda_ok(cudaMalloc(slots[i], (n + 64) * elt), "cudaMalloc(block arena)", err))
+    return false;
+  cap[i] = n;
+  return true;
+}
+
 bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
-                        std::string* err)
+                        std::string* err, std::shared_ptr<BlockArena> share)
 {
   if (!_final) return fail(err, "reserve before finalize");
   const size_t vt = std::max(max_video, 0), at = std::max(max_audio, 0),
@@ -345,34 +364,24 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   const size_t vd = _vdim, ad = _adim;
   const size_t ai = ad;   // audio inner (the cross attentions' width too)
   auto mx = [](std::initializer_list<size_t> l) { return std::max(l); };
-  const size_t n_normed = mx({vt * vd, at * ad});
-  const size_t n_qkv = mx({vt * 3 * vd, at * 3 * ad, vt * vd, vt * ai, at * ai});
-  const size_t n_kvp = mx({tt * 2 * vd, tt * 2 * ad, at * 2 * ai, vt * 2 * ai});
-  const size_t n_qn = mx({vt * vd, at * ad, vt * ai});
-  const size_t n_kn = mx({vt * vd, at * ad, tt * vd, tt * ad, vt * ai, at * ai});
-  const size_t n_att = mx({vt * vd, at * ad, vt * ai});
-  const size_t n_glog = mx({vt, at}) * (size_t)std::max(_vheads, _aheads);
-  const size_t n_ctx = tt * std::max(vd, ad);
-  const size_t n_ff = mx({vt * (size_t)_video.ff_hidden, at * (size_t)_audio.ff_hidden});
-  struct B { __nv_bfloat16** p; size_t n; };
-  const B bufs[] = {{&_ar.normed, n_normed}, {&_ar.qkv, n_qkv}, {&_ar.kvp, n_kvp},
-                    {&_ar.qn, n_qn}, {&_ar.kn, n_kn}, {&_ar.att, n_att},
-                    {&_ar.glog, n_glog}, {&_ar.ctxmod, n_ctx}, {&_ar.ff, n_ff},
-                    {&_ar.qv, vt * vd}, {&_ar.kva, at * ad}, {&_ar.qa, at * ad},
-                    {&_ar.kvv, vt * vd}};
-  for (const B& b : bufs) {
-    cudaFree(*b.p);
-    *b.p = nullptr;
-    if (b.n > 0 &&
-        !cuda_ok(cudaMalloc(b.p, (b.n + 64) * sizeof(__nv_bfloat16)), "cudaMalloc(block arena)", err))
-      return false;
-  }
-  cudaFree(_ar.mods);
-  _ar.mods = nullptr;
-  if (!cuda_ok(cudaMalloc(&_ar.mods, (size_t)MOD_ROWS * (vd + ad) * sizeof(float)),
-               "cudaMalloc(block arena)", err))
-    return false;
-  _ar.tokens = mx({vt, at, tt});
+  const size_t need[14] = {
+      mx({vt * vd, at * ad}),                                        // normed
+      mx({vt * 3 * vd, at * 3 * ad, vt * vd, vt * ai, at * ai}),     // qkv / q
+      mx({vt * vd, at * ad, vt * ai}),                               // qn
+      mx({vt * vd, at * ad, tt * vd, tt * ad, vt * ai, at * ai}),    // kn
+      mx({vt * vd, at * ad, vt * ai}),                               // att
+      mx({vt, at}) * (size_t)std::max(_vheads, _aheads),             // glog
+      tt * std::max(vd, ad),                                         // ctxmod
+      mx({tt * 2 * vd, tt * 2 * ad, at * 2 * ai, vt * 2 * ai}),      // kv proj
+      mx({vt * (size_t)_video.ff_hidden, at * (size_t)_audio.ff_hidden}),  // ff
+      vt * vd, at * ad, at * ad, vt * vd,                            // qv kva qa kvv
+      (size_t)MOD_ROWS * (vd + ad)};                                 // mods
+  _arp = share ? share : std::make_shared<BlockArena>();
+  for (int i = 0; i < 14; ++i)
+    if (!_arp->ensure(i, need[i], err)) return false;
+  _arp->video = std::max(_arp->video, vt);
+  _arp->audio = std::max(_arp->audio, at);
+  _arp->text = std::max(_arp->text, tt);
   // The GEMMs' own scratch (int8 tier) follows the largest projection.
   return _ops->reserve((int)mx({vt, at, tt}), (int)mx({3 * vd, (size_t)_video.ff_hidden}),
                        (int)mx({vd, (size_t)_video.ff_hidden}), err);
@@ -389,38 +398,38 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   const __nv_bfloat16 *qraw, *kraw, *vraw;
   int ldq, ldkv;
   if (a.self) {
-    if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _ar.qkv, 3 * I, tq, a.qdim,
+    if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _arp->qkv, 3 * I, tq, a.qdim,
                       3 * I, ltx::EPI_STORE, nullptr, err))
       return false;
-    qraw = _ar.qkv;
-    kraw = _ar.qkv + I;
-    vraw = _ar.qkv + 2 * I;
+    qraw = _arp->qkv;
+    kraw = _arp->qkv + I;
+    vraw = _arp->qkv + 2 * I;
     ldq = ldkv = 3 * I;
   } else {
-    if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _ar.qkv, I, tq, a.qdim, I,
+    if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _arp->qkv, I, tq, a.qdim, I,
                       ltx::EPI_STORE, nullptr, err) ||
-        !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _ar.kvp, 2 * I, tkv,
+        !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _arp->kvp, 2 * I, tkv,
                       a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err))
       return false;
-    qraw = _ar.qkv;
-    kraw = _ar.kvp;
-    vraw = _ar.kvp + I;
+    qraw = _arp->qkv;
+    kraw = _arp->kvp;
+    vraw = _arp->kvp + I;
     ldq = I;
     ldkv = 2 * I;
   }
-  if (ltx::launch_qk_norm_rope(qraw, ldq, _ar.qn, I, tq, a.heads, a.head_dim,
+  if (ltx::launch_qk_norm_rope(qraw, ldq, _arp->qn, I, tq, a.heads, a.head_dim,
                                a.q_norm, qcos, qsin, kEps, s) != 0 ||
-      ltx::launch_qk_norm_rope(kraw, ldkv, _ar.kn, I, tkv, a.heads,
+      ltx::launch_qk_norm_rope(kraw, ldkv, _arp->kn, I, tkv, a.heads,
                                a.head_dim, a.k_norm, kcos, ksin, kEps, s) != 0)
     return fail(err, "q/k norm + rope launch failed");
   const __nv_bfloat16* glog = nullptr;
   if (a.gate.N > 0) {
-    if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _ar.glog, a.heads, tq,
+    if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _arp->glog, a.heads, tq,
                       a.qdim, a.heads, ltx::EPI_STORE, nullptr, err))
       return false;
-    glog = _ar.glog;
+    glog = _arp->glog;
   }
-  if (ltx::launch_attention(_ar.qn, I, _ar.kn, I, vraw, ldkv, out, I, glog,
+  if (ltx::launch_attention(_arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog,
                             a.heads, tq, tkv, a.heads, a.head_dim, s) != 0)
     return fail(err, "attention launch failed");
   return true;
@@ -431,7 +440,7 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
 {
   // src/ltx25-block-ref.cc:196-262
   const int n = io.tokens, d = w.dim;
-  float* mods = _ar.mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
+  float* mods = _arp->mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
   if (ltx::launch_vec_add(w.scale_shift, io.timesteps, mods + MOD_MSA * d, 3 * d, s) ||
       ltx::launch_vec_add(w.scale_shift + 6 * d, io.timesteps ? io.timesteps + 6 * d : nullptr,
                           mods + MOD_CA * d, 3 * d, s) ||
@@ -439,28 +448,28 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                           mods + MOD_PROMPT * d, 2 * d, s))
     return fail(err, "adaLN rows launch failed");
   // normed = rms_norm(x) * (1 + scale) + shift;  x += gate * attn1(normed)
-  if (ltx::launch_ada_zero(io.x, d, _ar.normed, d, n, d, mods + (MOD_MSA + 1) * d,
+  if (ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_MSA + 1) * d,
                            mods + MOD_MSA * d, kEps, true, s))
     return fail(err, "ada_zero launch failed");
-  if (!attend_(s, w.attn1, _ar.normed, n, _ar.normed, n, io.pe_cos, io.pe_sin,
-               io.pe_cos, io.pe_sin, _ar.att, err))
+  if (!attend_(s, w.attn1, _arp->normed, n, _arp->normed, n, io.pe_cos, io.pe_sin,
+               io.pe_cos, io.pe_sin, _arp->att, err))
     return false;
-  if (!_ops->linear(s, _ar.att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, d,
+  if (!_ops->linear(s, _arp->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, d,
                     n, w.attn1.inner, d, ltx::EPI_GATED_RES,
                     mods + (MOD_MSA + 2) * d, err))
     return false;
   // Text cross-attention: query = mod(rms_norm(x)) (= ada_zero with the
   // cross rows), key/value = context modulated by the prompt table + driver.
-  if (ltx::launch_ada_zero(io.x, d, _ar.normed, d, n, d, mods + (MOD_CA + 1) * d,
+  if (ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_CA + 1) * d,
                            mods + MOD_CA * d, kEps, true, s) ||
-      ltx::launch_ada_zero(io.context, d, _ar.ctxmod, d, io.text_tokens, d,
+      ltx::launch_ada_zero(io.context, d, _arp->ctxmod, d, io.text_tokens, d,
                            mods + (MOD_PROMPT + 1) * d, mods + MOD_PROMPT * d,
                            kEps, false, s))
     return fail(err, "modulation launch failed");
-  if (!attend_(s, w.attn2, _ar.normed, n, _ar.ctxmod, io.text_tokens, nullptr,
-               nullptr, nullptr, nullptr, _ar.att, err))
+  if (!attend_(s, w.attn2, _arp->normed, n, _arp->ctxmod, io.text_tokens, nullptr,
+               nullptr, nullptr, nullptr, _arp->att, err))
     return false;
-  return _ops->linear(s, _ar.att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x,
+  return _ops->linear(s, _arp->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x,
                       d, n, w.attn2.inner, d, ltx::EPI_GATED_RES,
                       mods + (MOD_CA + 2) * d, err);
 }
@@ -470,15 +479,15 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
 {
   // src/ltx25-block-ref.cc:264-281
   const int n = io.tokens, d = w.dim;
-  float* mods = _ar.mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
+  float* mods = _arp->mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
   if (ltx::launch_vec_add(w.scale_shift + 3 * d, io.timesteps ? io.timesteps + 3 * d : nullptr,
                           mods + MOD_MLP * d, 3 * d, s) ||
-      ltx::launch_ada_zero(io.x, d, _ar.normed, d, n, d, mods + (MOD_MLP + 1) * d,
+      ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_MLP + 1) * d,
                            mods + MOD_MLP * d, kEps, true, s))
     return fail(err, "ff pre-norm launch failed");
-  return _ops->linear(s, _ar.normed, d, w.ff_in, w.ff_in_b, _ar.ff, w.ff_hidden, n,
+  return _ops->linear(s, _arp->normed, d, w.ff_in, w.ff_in_b, _arp->ff, w.ff_hidden, n,
                       d, w.ff_hidden, ltx::EPI_GELU, nullptr, err) &&
-         _ops->linear(s, _ar.ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, d, n,
+         _ops->linear(s, _arp->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, d, n,
                       w.ff_hidden, d, ltx::EPI_GATED_RES, mods + (MOD_MLP + 2) * d,
                       err);
 }
@@ -487,13 +496,14 @@ bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
                         std::string* err)
 {
   if (!_final) return fail(err, "forward before finalize");
+  if (!_arp) return fail(err, "forward before reserve");
   const bool rv = v.present && v.tokens > 0;
   const bool ra = a.present && a.tokens > 0;
   if (!rv && !ra) return fail(err, "neither stream is present");
-  auto too_big = [&](const StreamIO& io) {
-    return (size_t)io.tokens > _ar.tokens || (size_t)io.text_tokens > _ar.tokens;
-  };
-  if ((rv && too_big(v)) || (ra && too_big(a)))
+  const bool too_big =
+      (rv && ((size_t)v.tokens > _arp->video || (size_t)v.text_tokens > _arp->text)) ||
+      (ra && ((size_t)a.tokens > _arp->audio || (size_t)a.text_tokens > _arp->text));
+  if (too_big)
     return fail(err, "geometry exceeds the reserved arena");
   for (const StreamIO* io : {&v, &a}) {
     const bool on = io == &v ? rv : ra;
@@ -507,33 +517,33 @@ bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
     // src/ltx25-block-ref.cc:336-385.  Both directions read the PRE-cross
     // state: all four ada_zero operands are formed before either update.
     const int vd = _vdim, ad = _adim;
-    float* vm = _ar.mods;
-    float* am = _ar.mods + (size_t)MOD_ROWS * _vdim;
+    float* vm = _arp->mods;
+    float* am = _arp->mods + (size_t)MOD_ROWS * _vdim;
     if (ltx::launch_vec_add(_video.cross_table, v.cross_scale_shift, vm + MOD_AV * vd, 4 * vd, s) ||
         ltx::launch_vec_add(_video.cross_table + 4 * vd, v.cross_gate, vm + MOD_AVG * vd, vd, s) ||
         ltx::launch_vec_add(_audio.cross_table, a.cross_scale_shift, am + MOD_AV * ad, 4 * ad, s) ||
         ltx::launch_vec_add(_audio.cross_table + 4 * ad, a.cross_gate, am + MOD_AVG * ad, ad, s))
       return fail(err, "cross adaLN launch failed");
     // av rows: [scale(lo=0), shift(lo=0), scale(lo=2), shift(lo=2)]
-    if (ltx::launch_ada_zero(v.x, vd, _ar.qv, vd, v.tokens, vd, vm + (MOD_AV + 0) * vd,
+    if (ltx::launch_ada_zero(v.x, vd, _arp->qv, vd, v.tokens, vd, vm + (MOD_AV + 0) * vd,
                              vm + (MOD_AV + 1) * vd, kEps, true, s) ||
-        ltx::launch_ada_zero(a.x, ad, _ar.kva, ad, a.tokens, ad, am + (MOD_AV + 0) * ad,
+        ltx::launch_ada_zero(a.x, ad, _arp->kva, ad, a.tokens, ad, am + (MOD_AV + 0) * ad,
                              am + (MOD_AV + 1) * ad, kEps, true, s) ||
-        ltx::launch_ada_zero(a.x, ad, _ar.qa, ad, a.tokens, ad, am + (MOD_AV + 2) * ad,
+        ltx::launch_ada_zero(a.x, ad, _arp->qa, ad, a.tokens, ad, am + (MOD_AV + 2) * ad,
                              am + (MOD_AV + 3) * ad, kEps, true, s) ||
-        ltx::launch_ada_zero(v.x, vd, _ar.kvv, vd, v.tokens, vd, vm + (MOD_AV + 2) * vd,
+        ltx::launch_ada_zero(v.x, vd, _arp->kvv, vd, v.tokens, vd, vm + (MOD_AV + 2) * vd,
                              vm + (MOD_AV + 3) * vd, kEps, true, s))
       return fail(err, "cross ada_zero launch failed");
     // a2v: video queries, audio keys/values
-    if (!attend_(s, _a2v, _ar.qv, v.tokens, _ar.kva, a.tokens, v.cpe_cos,
-                 v.cpe_sin, a.cpe_cos, a.cpe_sin, _ar.att, err) ||
-        !_ops->linear(s, _ar.att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, vd, v.tokens,
+    if (!attend_(s, _a2v, _arp->qv, v.tokens, _arp->kva, a.tokens, v.cpe_cos,
+                 v.cpe_sin, a.cpe_cos, a.cpe_sin, _arp->att, err) ||
+        !_ops->linear(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, vd, v.tokens,
                       _a2v.inner, vd, ltx::EPI_GATED_RES, vm + MOD_AVG * vd, err))
       return false;
     // v2a: audio queries, video keys/values
-    if (!attend_(s, _v2a, _ar.qa, a.tokens, _ar.kvv, v.tokens, a.cpe_cos,
-                 a.cpe_sin, v.cpe_cos, v.cpe_sin, _ar.att, err) ||
-        !_ops->linear(s, _ar.att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, ad, a.tokens,
+    if (!attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, v.tokens, a.cpe_cos,
+                 a.cpe_sin, v.cpe_cos, v.cpe_sin, _arp->att, err) ||
+        !_ops->linear(s, _arp->att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, ad, a.tokens,
                       _v2a.inner, ad, ltx::EPI_GATED_RES, am + MOD_AVG * ad, err))
       return false;
   }

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <map>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -69,6 +70,22 @@ struct StreamIO {
   bool present = true;
 };
 
+// The scratch ONE block forward needs, shared by every block of a stack
+// (the reference's BlockScratch, src/ltx25-block-metal.h:140-240): the stack
+// runs strictly in sequence, so 48 private arenas would only cost memory.
+struct BlockArena {
+  __nv_bfloat16 *normed = nullptr, *qkv = nullptr, *qn = nullptr,
+                *kn = nullptr, *att = nullptr, *glog = nullptr,
+                *ctxmod = nullptr, *kvp = nullptr, *ff = nullptr,
+                *qv = nullptr, *kva = nullptr, *qa = nullptr, *kvv = nullptr;
+  float* mods = nullptr;      // adaLN rows, f32
+  size_t cap[14] = {};        // element capacity of each buffer above
+  size_t video = 0, audio = 0, text = 0;   // reserved token maxima
+  ~BlockArena();
+  // Grow buffer i (in the order declared) to at least n elements.
+  bool ensure(int i, size_t n, std::string* err);
+};
+
 class CudaBlock {
 public:
   CudaBlock(CudaOps* ops, int vdim, int vheads, int adim, int aheads)
@@ -90,14 +107,25 @@ public:
   // the q/k/v and k/v packs, upload the rest.  Frees the staged parts.
   bool finalize(std::string* err);
 
-  // Size the scratch arena once for the largest geometry.
-  bool reserve(int max_video, int max_audio, int max_text, std::string* err);
+  // Size the scratch arena once for the largest geometry.  `share`, when
+  // given, is adopted (and grown if this block needs more): every block of
+  // a stack uses the same arena.
+  bool reserve(int max_video, int max_audio, int max_text, std::string* err,
+               std::shared_ptr<BlockArena> share = nullptr);
+  const std::shared_ptr<BlockArena>& arena() const { return _arp; }
 
   // Run the block; video.x / audio.x are updated in place.
   bool forward(cudaStream_t s, StreamIO& video, StreamIO& audio,
                std::string* err);
 
   bool finalized() const { return _final; }
+  CudaOps* ops() const { return _ops; }
+  bool same_widths(const CudaBlock& o) const
+  {
+    return _vdim == o._vdim && _vheads == o._vheads && _adim == o._adim &&
+           _aheads == o._aheads && _video.ff_hidden == o._video.ff_hidden &&
+           _audio.ff_hidden == o._audio.ff_hidden;
+  }
 
 private:
   struct Staged {
@@ -134,15 +162,7 @@ private:
   CudaAttn _a2v, _v2a;
   bool _final = false;
 
-  // scratch arena
-  struct Arena {
-    __nv_bfloat16 *normed = nullptr, *qkv = nullptr, *qn = nullptr,
-                  *kn = nullptr, *att = nullptr, *glog = nullptr,
-                  *ctxmod = nullptr, *kvp = nullptr, *ff = nullptr,
-                  *qv = nullptr, *kva = nullptr, *qa = nullptr, *kvv = nullptr;
-    float* mods = nullptr;   // adaLN rows, f32
-    size_t tokens = 0;
-  } _ar;
+  std::shared_ptr<BlockArena> _arp;
 };
 
 }  // namespace ltx25

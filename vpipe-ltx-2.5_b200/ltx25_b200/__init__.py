@@ -16,7 +16,7 @@ LTX_OK = 0
 ERRORS = {
     -1: "LTX_E_NULL", -2: "LTX_E_SHAPE", -3: "LTX_E_UNSUPPORTED",
     -4: "LTX_E_CUDA", -5: "LTX_E_OOM", -6: "LTX_E_KERNEL", -7: "LTX_E_STATE",
-    -8: "LTX_E_ALIGN",
+    -8: "LTX_E_ALIGN", -9: "LTX_E_ABORTED",
 }
 SB_F16, SB_BF16, SB_F32 = 0, 1, 2
 ROUTE_FUSED, ROUTE_DEQUANT_ONCE = 0, 1
@@ -63,6 +63,13 @@ SIGNATURES = {
     "ltx_block_finalize": (_I, [_P]),
     "ltx_block_reserve": (_I, [_P, _I, _I, _I]),
     "ltx_block_forward": (_I, [_P, _P, _P, _P]),
+    "ltx_stack_create": (_I, [_P, ctypes.POINTER(_P)]),
+    "ltx_stack_destroy": (None, [_P]),
+    "ltx_stack_last_error": (ctypes.c_char_p, [_P]),
+    "ltx_stack_add_block": (_I, [_P, _P]),
+    "ltx_stack_size": (_I, [_P]),
+    "ltx_stack_reserve": (_I, [_P, _I, _I, _I]),
+    "ltx_stack_forward": (_I, [_P, _P, _P, _I, _I, _P, _P, _P]),
     "ltx_rope_table": (_I, [_P, _P, _I, _I, _P, _I, _I, ctypes.c_double, _I,
                             _P, _P]),
     "ltx_rope_video_spans": (_I, [_I, _I, _I, _I, _I, _I, ctypes.c_double, _I,
@@ -421,6 +428,64 @@ class Block:
     def close(self):
         if getattr(self, "h", None) is not None and self.h.value:
             self.ctx.lib.ltx_block_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+PROGRESS_FN = ctypes.CFUNCTYPE(_I, _I, _I, _P)
+
+
+class Stack:
+    """ltx_stack: blocks run in order over one shared scratch arena.  Holds
+    Python references to its blocks so they outlive it."""
+
+    def __init__(self, ctx, blocks=()):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        ctx._ok(ctx.lib.ltx_stack_create(ctx.h, ctypes.byref(h)), "stack_create")
+        self.h = h
+        self.blocks = []
+        for b in blocks:
+            self.add(b)
+
+    def err(self):
+        return self.ctx.lib.ltx_stack_last_error(self.h).decode()
+
+    def _ok(self, rc, what):
+        if rc != LTX_OK:
+            raise LtxError(rc, f"{what}: {self.err()}")
+
+    def add(self, block):
+        self._ok(self.ctx.lib.ltx_stack_add_block(self.h, block.h), "stack_add_block")
+        self.blocks.append(block)
+
+    def __len__(self):
+        return self.ctx.lib.ltx_stack_size(self.h)
+
+    def reserve(self, max_video, max_audio, max_text):
+        self._ok(self.ctx.lib.ltx_stack_reserve(self.h, max_video, max_audio,
+                                                max_text), "stack_reserve")
+
+    def forward(self, video, audio, begin=0, end=-1, progress=None, stream=None):
+        """progress(block, blocks) -> bool; False stops (LTX_E_ABORTED)."""
+        v = Block.make_io(video)
+        a = Block.make_io(audio)
+        cb = None
+        if progress is not None:
+            cb = PROGRESS_FN(lambda i, n, _u: 1 if progress(i, n) else 0)
+        self._ok(self.ctx.lib.ltx_stack_forward(
+            self.h, ctypes.byref(v), ctypes.byref(a), begin, end,
+            ctypes.cast(cb, _P) if cb is not None else None, None,
+            _stream(stream)), "stack_forward")
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            self.ctx.lib.ltx_stack_destroy(self.h)
             self.h = None
 
     def __del__(self):

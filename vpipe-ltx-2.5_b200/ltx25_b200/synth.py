@@ -43,13 +43,19 @@ def tensor_specs(vdim, vheads, adim, aheads, ff_mult=4):
     return specs
 
 
-def load_random_block(ctx, vdim, vheads, adim, aheads, seed, device="cuda"):
-    """A finalized ltx25_b200.Block with random weights made on the device."""
+def load_random_block(ctx, vdim, vheads, adim, aheads, seed, device="cuda",
+                      effective=False):
+    """A finalized ltx25_b200.Block with random weights made on the device.
+
+    effective=True also returns the weights the device computes with, as
+    host f32 numpy under the same names: the dequantized linears, the bf16
+    biases and gate weights, the f32 gains and tables."""
     import torch
-    from . import Block, QWeight, is_quantized_name, pack_w8g64  # noqa: F401
+    from . import Block, QWeight, dequant, is_quantized_name, pack_w8g64
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     blk = Block(ctx, vdim, vheads, adim, aheads)
+    eff = {}
     for name, (shape, kind) in tensor_specs(vdim, vheads, adim, aheads).items():
         t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
         if kind in ("mat", "gate"):
@@ -65,12 +71,19 @@ def load_random_block(ctx, vdim, vheads, adim, aheads, seed, device="cuda"):
         if is_quantized_name(name, t.dim()):
             c, s, b = pack_w8g64(ctx, t)
             blk.set_qlinear(name, c, s, b, shape[0], shape[1])
+            if effective:
+                q = QWeight.upload(ctx, c, s, b, shape[0], shape[1], on_device=True)
+                eff[name] = dequant(ctx, q).float().cpu().numpy()
+                q.free()
             del c, s, b
         else:
             blk.set_tensor(name, t)
+            if effective:
+                bf16 = kind in ("bias", "gate", "gate_b")
+                eff[name] = (t.to(torch.bfloat16).float() if bf16 else t).cpu().numpy()
         del t
     blk.finalize()
-    return blk
+    return (blk, eff) if effective else blk
 
 
 def video_grid(frames=16, height=17, width=30):
