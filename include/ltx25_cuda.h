@@ -132,6 +132,28 @@ LTX_API int ltx_qweight_info(const ltx_qweight* w, int* N, int* K, int* bits,
 LTX_API int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                 const void* bias, void* y, int M, int K, int N, void* stream);
 
+/* The int8 tier's qlinear (per-token int8 activation codes, kind::i8 GEMM)
+ * with its activation scratch in one fixed device array of the library
+ * instead of context memory: the call allocates nothing, for callers that
+ * may not allocate device memory while they run (a runtime that owns HBM
+ * through its own pool and plans every byte ahead).  No counterpart in the
+ * reference.
+ *   - M*K <= LTX_I8_STATIC_MAX_CODES and M <= LTX_I8_STATIC_MAX_ROWS, else
+ *     LTX_E_SHAPE; K a multiple of 128, N of 4.  ldx = K, ldy = N.
+ *   - The weight must already hold its int8 copy, which the first int8-tier
+ *     ltx_qlinear on it makes (ltx_set_tiers(ctx, 1, ...)); else LTX_E_STATE.
+ *   - The array (32 MiB + 64 KiB) is held by every GPU that loads the
+ *     library until the process exits.  The first call on a device looks up
+ *     its address (cudaGetSymbolAddress, with that device current); make
+ *     that first call before any stream capture.
+ *   - All calls on a device share the array and it keeps the last call's
+ *     contents; calls whose kernels overlap on the GPU race on it. */
+#define LTX_I8_STATIC_MAX_CODES 33554432
+#define LTX_I8_STATIC_MAX_ROWS 16384
+LTX_API int ltx_qlinear_i8_static(ltx_ctx* ctx, const ltx_qweight* w,
+                                  const void* x, const void* bias, void* y,
+                                  int M, int K, int N, void* stream);
+
 /* The same with explicit row strides and a fused epilogue (LTX_EPI_*).
  * `gate` is [N] f32 for LTX_EPI_GATED_RES (y += gate * (xW^T + b)), the
  * reference's linear + gated_residual pair (src/ltx25-metal-ops.cc:

@@ -8,6 +8,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <string>
+
 #include "gemm_tc.cuh"
 
 namespace ltx {
@@ -52,5 +54,10 @@ int launch_dequant_w8(const uint8_t* codes, const uint32_t* sz, int N, int K,
 int launch_quant_rows_i8(const __nv_bfloat16* x, int rows, int K, int ldx,
                          int group, int8_t* q, float* scale,
                          cudaStream_t stream);
+
+// Device address of the fixed int8-tier scratch array on `device`
+// (i8_static.cu): LTX_I8_STATIC_MAX_CODES codes, then LTX_I8_STATIC_MAX_ROWS
+// f32 scales.
+bool i8_static_scratch(int device, int8_t** codes, float** scales, std::string* err);
 
 }  // namespace ltx

@@ -175,6 +175,37 @@ int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                         nullptr, stream);
 }
 
+int ltx_qlinear_i8_static(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
+                          const void* bias, void* y, int M, int K, int N,
+                          void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (w == nullptr || x == nullptr || y == nullptr)
+    return fail(ctx, LTX_E_NULL, "qlinear_i8_static: null weight, x or y");
+  if (M <= 0 || K <= 0 || (size_t)M * (size_t)K > (size_t)LTX_I8_STATIC_MAX_CODES ||
+      M > LTX_I8_STATIC_MAX_ROWS)
+    return fail(ctx, LTX_E_SHAPE,
+                "qlinear_i8_static: M*K = " + std::to_string((long long)M * K) +
+                    " codes, M = " + std::to_string(M) + "; the fixed scratch holds " +
+                    std::to_string(LTX_I8_STATIC_MAX_CODES) + " codes and " +
+                    std::to_string(LTX_I8_STATIC_MAX_ROWS) + " rows");
+  if (!w->w.quantized)
+    return fail(ctx, LTX_E_UNSUPPORTED, "qlinear_i8_static: weight is dense");
+  int8_t* xq = nullptr;
+  float* sx = nullptr;
+  std::string e;
+  if (!ltx::i8_static_scratch(ctx->ops.device(), &xq, &sx, &e))
+    return fail(ctx, LTX_E_CUDA, e);
+  if (!ctx->ops.linear_i8_scratch(S(stream), static_cast<const __nv_bfloat16*>(x), w->w,
+                                  static_cast<const __nv_bfloat16*>(bias),
+                                  static_cast<__nv_bfloat16*>(y), M, K, N, xq, sx, &e)) {
+    int code = code_for(e);
+    if (e.find("int8 tier state") != std::string::npos) code = LTX_E_STATE;
+    return fail(ctx, code, e);
+  }
+  return LTX_OK;
+}
+
 int ltx_set_route(ltx_ctx* ctx, int route)
 {
   if (ctx == nullptr) return LTX_E_NULL;

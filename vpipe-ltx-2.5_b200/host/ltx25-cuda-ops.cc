@@ -283,6 +283,42 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
                N, epi, gate, nullptr, nullptr, err);
 }
 
+bool CudaOps::linear_i8_scratch(cudaStream_t s, const __nv_bfloat16* x,
+                                const QWeight& w, const __nv_bfloat16* bias,
+                                __nv_bfloat16* y, int M, int K, int N,
+                                int8_t* xq, float* sx, std::string* err)
+{
+  if (x == nullptr || y == nullptr) {
+    if (err) *err = "linear: null x or y";
+    return false;
+  }
+  if (M <= 0 || K != w.K || N != w.N) {
+    if (err)
+      *err = "linear: shape (M=" + std::to_string(M) + ", K=" + std::to_string(K) +
+             ", N=" + std::to_string(N) + ") disagrees with the weight [" +
+             std::to_string(w.N) + "][" + std::to_string(w.K) + "]";
+    return false;
+  }
+  if (K % 128 != 0 || N % 4 != 0) {
+    if (err) *err = "int8 tier shape: K must be a multiple of 128, N of 4";
+    return false;
+  }
+  if (!w.quantized || w.wq == nullptr) {
+    if (err) *err = "int8 tier state: the weight has no int8 copy yet";
+    return false;
+  }
+  if (!aligned(x, 16) || !aligned(y, 4) || (bias && !aligned(bias, 4))) {
+    if (err) *err = "linear: x must be 16-byte aligned; y, bias 4-byte aligned";
+    return false;
+  }
+  if (ltx::launch_quant_rows_i8(x, M, K, K, K, xq, sx, s) != 0) {
+    if (err) *err = "int8 activation quantize launch failed";
+    return false;
+  }
+  return gemm_(s, ltx::MODE_I8, xq, K, w.wq, nullptr, bias, y, N, M, K, N,
+               ltx::EPI_STORE, nullptr, sx, w.sw, err);
+}
+
 int CudaOps::check(cudaStream_t s, std::string* err) const
 {
   int h = 0;

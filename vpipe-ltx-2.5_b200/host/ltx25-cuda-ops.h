@@ -68,6 +68,14 @@ public:
   // once per weight, on first use or here.
   bool prepare_i8(QWeight& w, cudaStream_t s, std::string* err) const;
 
+  // The int8 tier's quantize + kind::i8 GEMM on caller-given scratch (xq:
+  // M*K codes, sx: M scales) and allocating nothing: the weight must
+  // already hold its int8 copy (made by the tier's first linear on it).
+  bool linear_i8_scratch(cudaStream_t s, const __nv_bfloat16* x, const QWeight& w,
+                         const __nv_bfloat16* bias, __nv_bfloat16* y, int M,
+                         int K, int N, int8_t* xq, float* sx,
+                         std::string* err);
+
   int device() const { return _dev; }
   int num_sms() const { return _sms; }
   int* err_word() const { return _err_word; }

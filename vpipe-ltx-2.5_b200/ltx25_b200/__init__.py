@@ -44,6 +44,7 @@ SIGNATURES = {
     "ltx_qlinear": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "ltx_qlinear_ex": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P,
                             _P]),
+    "ltx_qlinear_i8_static": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "ltx_set_route": (_I, [_P, _I]),
     "ltx_set_tiers": (_I, [_P, _I, _I, _I]),
     "ltx_i8_takes": (_I, [_P, _I, _I, _I]),
@@ -242,6 +243,19 @@ def qlinear(ctx, w, x, bias=None, out=None, epilogue=EPI_STORE, gate=None,
                                 _ptr(out), out.stride(0), M, w.K, w.N, epilogue,
                                 _ptr(gate), _stream(stream))
     ctx._ok(rc, "qlinear")
+    return out
+
+
+def qlinear_i8_static(ctx, w, x, bias=None, out=None, stream=None):
+    """ltx_qlinear_i8_static: the int8 tier on the library's fixed scratch
+    array (no device allocation in the call).  x: contiguous [M][K] bf16."""
+    import torch
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, w.N), dtype=torch.bfloat16, device=x.device)
+    ctx._ok(ctx.lib.ltx_qlinear_i8_static(ctx.h, w.h, _ptr(x), _ptr(bias), _ptr(out),
+                                          M, w.K, w.N, _stream(stream)),
+            "qlinear_i8_static")
     return out
 
 
