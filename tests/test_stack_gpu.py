@@ -2,11 +2,19 @@
 
 Mirrors the reference's ltx25-dit-stack-golden-test (tests/ltx25-dit-stack-
 golden-test.cc:1-21, 166-170): the stack's hidden state is compared with the
-CPU block_forward chained over the same weights, at the taps {0, 1, 3, 7,
-15, 31, 47}, against the reference's stated bf16 bar for 48 blocks (~2e-2,
-README.md:86).  The full 48 blocks run at the model's real widths on a short
-clip (the oracle at 8160 tokens would take hours per block); the token count
-does not change any GEMM's K or N, only M.
+CPU block_forward chained over the same weights at the taps {0, 1, 3, 7, 15,
+31, 47}.  The full 48 blocks run at the model's real widths on a short clip
+(the oracle at 8160 tokens would take hours per block); the token count does
+not change any GEMM's K or N, only M.
+
+Bars.  Against the f32-stream oracle the reference's own bar is 0.25 (a
+48-deep bf16 chain "accumulates", only its shape is diagnostic; it measured
+6.7e-3 -> 1.8e-2 on the real checkpoint, README.md:86); the taps must also
+grow smoothly (no tap more than 2.5x the previous one, which a defect in one
+block would break).  Against an oracle that stores the residual stream in
+bf16 after every update, as the interface's bf16 x does on the device, the
+chain must stay under 2e-2 at every tap: that isolates the kernels' own
+error from the stream's storage.
 
 Also pinned here: the stack's shared arena gives the same bits as private
 per-block arenas, ranges compose, the progress hook stops between blocks,
@@ -21,7 +29,8 @@ from test_block_gpu import SMALL, bf16r, build, host, to_dev
 
 pytestmark = pytest.mark.gpu
 
-STACK_BAR = 2e-2
+STACK_BAR = 2e-2          # small stack / bf16-stream oracle
+REF_BAR = 2.5e-1          # tests/ltx25-dit-stack-golden-test.cc:166-170
 
 
 def chain_oracle(weights, ins, cfg, x_round=None):
@@ -157,22 +166,26 @@ def test_stack_48_blocks_real_widths(ctx):
         for key in ("x", "context", "timesteps", "cross_scale_shift", "cross_gate",
                     "prompt_timestep"):
             ins[s][key] = bf16r(ins[s][key])
-    v = {k: (np.array(x) if k == "x" else x) for k, x in ins["video"].items()}
-    a = {k: (np.array(x) if k == "x" else x) for k, x in ins["audio"].items()}
+    fresh = lambda d: {k: (np.array(x) if k == "x" else x) for k, x in d.items()}
+    v, a = fresh(ins["video"]), fresh(ins["audio"])
+    vb, ab = fresh(ins["video"]), fresh(ins["audio"])
     st = L.Stack(ctx)
-    taps = {}
+    taps, taps_b = {}, {}
     for i in range(48):
         blk, ow = synth.load_random_block(ctx, 4096, 32, 2048, 32, seed=9000 + i,
                                           effective=True)
         st.add(blk)
         v["x"], a["x"] = block_np.block_forward(ow, v, a, 4096, 32, 2048, 32)
+        vb["x"], ab["x"] = block_np.block_forward(ow, vb, ab, 4096, 32, 2048, 32,
+                                                  x_round=bf16r)
         if i in TAPS:
             taps[i] = (v["x"].copy(), a["x"].copy())
+            taps_b[i] = (vb["x"].copy(), ab["x"].copy())
         del ow
     st.reserve(cfg["vt"], cfg["at"], cfg["tt"])
     dv, da = to_dev(ins["video"]), to_dev(ins["audio"])
     prev = 0
-    errs = {}
+    errs, errs_b = {}, {}
     for t in TAPS:
         st.forward(dv, da, prev, t + 1)
         torch.cuda.synchronize()
@@ -181,9 +194,18 @@ def test_stack_48_blocks_real_widths(ctx):
         gv, ga = host(dv["x"]), host(da["x"])
         assert np.isfinite(gv).all() and np.isfinite(ga).all()
         errs[t] = (lib.rel_l2(gv, taps[t][0]), lib.rel_l2(ga, taps[t][1]))
-    print({t: (f"{e[0]:.2e}", f"{e[1]:.2e}") for t, e in errs.items()})
-    for t, (ev, ea) in errs.items():
-        assert ev < STACK_BAR and ea < STACK_BAR, (t, ev, ea)
+        errs_b[t] = (lib.rel_l2(gv, taps_b[t][0]), lib.rel_l2(ga, taps_b[t][1]))
+    print("f32-stream oracle", {t: (f"{e[0]:.2e}", f"{e[1]:.2e}") for t, e in errs.items()})
+    print("bf16-stream oracle", {t: (f"{e[0]:.2e}", f"{e[1]:.2e}") for t, e in errs_b.items()})
+    last = None
+    for t in TAPS:
+        ev, ea = errs[t]
+        assert ev < REF_BAR and ea < REF_BAR, (t, ev, ea)
+        if last is not None:
+            assert ev < 2.5 * last[0] and ea < 2.5 * last[1], ("jump", t, ev, ea, last)
+        last = (ev, ea)
+        bv, ba = errs_b[t]
+        assert bv < STACK_BAR and ba < STACK_BAR, ("bf16-stream", t, bv, ba)
     st.close()
     for b in st.blocks:
         b.close()
