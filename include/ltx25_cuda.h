@@ -304,6 +304,28 @@ LTX_API int ltx_block_reserve(ltx_block* b, int max_video_tokens,
 LTX_API int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
                               const ltx_stream_io* audio, void* stream);
 
+/* Kernels this library has launched in the process so far (all contexts,
+ * all devices): bracket a region with two reads to count its launches. */
+LTX_API unsigned long long ltx_launch_count(void);
+
+/* ---- tensor parallelism (no reference counterpart) --
+ * One process per GPU, one context each.  Rank 0 makes a rendezvous id,
+ * the caller ships its LTX_TP_ID_BYTES to every rank by any channel, and
+ * every rank joins with ltx_ctx_set_tp before creating blocks.  Blocks
+ * finalized on a TP context keep only their rank's shard of the weights
+ * they are given in full: q/k/v, the gate logits and ff.net.0 split by
+ * heads / hidden columns, the output projections and ff.net.2 by K, with
+ * the partial products summed over the group (NCCL all-reduce) before the
+ * bias and the gated residual.  Every rank then calls the same forwards
+ * with the same (replicated) stream inputs, and each ends with the same x.
+ * NCCL is loaded at run time (libnccl.so.2). */
+#define LTX_TP_ID_BYTES 128
+LTX_API int ltx_tp_unique_id(void* id, int bytes);
+LTX_API int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id);
+/* In-place sum over the group on `stream`; dtype 0 = f32, 1 = bf16. */
+LTX_API int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype,
+                             void* stream);
+
 /* ---- the block stack ----------------------------------------------------
  * The block loop of Ltx25Dit::forward (src/ltx25-dit.cc:1716-1931): blocks
  * run in order on the same stream inputs, x updated in place, and share ONE

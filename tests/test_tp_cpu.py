@@ -1,0 +1,87 @@
+"""The tensor-parallel plan on CPU, over gloo ranks.
+
+tests/tp_np.py restates the CUDA block's Megatron sharding (heads split for
+q/k/v and the gates, K split for the output projections and ff.net.2, the
+q/k RMSNorm's sums of squares and the partial products reduced over ranks).
+Run as 2 and 4 gloo processes, every rank must end with the same x, equal to
+the unsharded oracle block up to summation order.  This is the host-side
+logic the GPU tensor-parallel path follows; tests/test_tp_gpu.py runs the
+device path itself on 2 GPUs.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from oracle import block_np, lib
+
+CFG = dict(vdim=512, vheads=4, adim=256, aheads=4, vt=24, at=7, tt=5)
+SEED = 41
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    t = block_np.random_block_tensors(CFG["vdim"], CFG["vheads"], CFG["adim"],
+                                      CFG["aheads"], seed=SEED)
+    ins = block_np.random_block_inputs(CFG, seed=SEED + 1, video_grid=(2, 3, 4))
+    return t, ins
+
+
+def _worker(rank, world, port, out_dir):
+    import torch
+    import torch.distributed as dist
+    import tp_np
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        t, ins = _inputs()
+
+        def allreduce(arr):
+            dist.all_reduce(torch.from_numpy(arr))
+
+        vx, ax = tp_np.block_forward_tp(t, ins["video"], ins["audio"], CFG["vdim"],
+                                        CFG["vheads"], CFG["adim"], CFG["aheads"],
+                                        rank, world, allreduce)
+        np.save(os.path.join(out_dir, f"v{rank}.npy"), vx)
+        np.save(os.path.join(out_dir, f"a{rank}.npy"), ax)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_block_equals_the_oracle(tmp_path, world):
+    import torch.multiprocessing as mp
+    mp.start_processes(_worker, args=(world, _port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    t, ins = _inputs()
+    wv, wa = block_np.block_forward(t, ins["video"], ins["audio"], CFG["vdim"],
+                                    CFG["vheads"], CFG["adim"], CFG["aheads"])
+    v0 = np.load(tmp_path / "v0.npy")
+    a0 = np.load(tmp_path / "a0.npy")
+    for r in range(1, world):
+        assert np.array_equal(np.load(tmp_path / f"v{r}.npy"), v0)
+        assert np.array_equal(np.load(tmp_path / f"a{r}.npy"), a0)
+    assert lib.rel_l2(v0, wv) < 1e-5
+    assert lib.rel_l2(a0, wa) < 1e-5
+    # and the sharding is not vacuous: the block moved x
+    assert lib.rel_l2(v0, ins["video"]["x"]) > 1e-2
+
+
+def test_one_rank_plan_is_the_oracle():
+    import tp_np
+    t, ins = _inputs()
+    vx, ax = tp_np.block_forward_tp(t, ins["video"], ins["audio"], CFG["vdim"],
+                                    CFG["vheads"], CFG["adim"], CFG["aheads"], 0, 1,
+                                    lambda a: None)
+    wv, wa = block_np.block_forward(t, ins["video"], ins["audio"], CFG["vdim"],
+                                    CFG["vheads"], CFG["adim"], CFG["aheads"])
+    assert lib.rel_l2(vx, wv) < 1e-6 and lib.rel_l2(ax, wa) < 1e-6

@@ -1,0 +1,143 @@
+"""The tensor-parallel plan of the CUDA block, restated in numpy (test helper).
+
+Megatron-style sharding over `world` ranks, as host/ltx25-block-cuda.cc
+implements it:
+  * q/k/v projections, their biases, the q/k RMSNorm gains and the per-head
+    gate logits keep this rank's heads [rank*H/W, (rank+1)*H/W);
+  * the RMSNorm over the WHOLE inner width needs the per-token sum of
+    squares of all heads: each rank sums its columns, the sums are reduced;
+  * the output projection keeps its K columns of this rank's heads; the
+    partial products are reduced, then the bias and the gated residual are
+    applied once;
+  * ff.net.0 keeps hidden columns [rank*F/W, ...) (GELU is per column),
+    ff.net.2 the same K columns, reduced like the output projections;
+  * everything else (adaLN rows, modulation, norms of x) is replicated.
+
+`block_forward_tp` with world == 1 is block_np.block_forward; with world > 1
+it must equal it up to summation order, which tests/test_tp_cpu.py checks
+over gloo ranks.
+"""
+import numpy as np
+
+from oracle import block_np, rope_np
+from oracle.block_np import F32, F64
+
+EPS = 1e-6
+
+
+def _attn_tp(t, prefix, x, ctx, pe, k_pe, heads, head_dim, rank, world, allreduce):
+    hl = heads // world
+    il = hl * head_dim
+    c0 = rank * il
+    inner = heads * head_dim
+    cols = slice(c0, c0 + il)
+    w = lambda n: t.get(f"{prefix}.{n}")
+
+    def lin(inp, name, rows=True):
+        wt = w(f"{name}.weight")
+        b = w(f"{name}.bias")
+        return block_np.linear(inp, wt[cols] if rows else wt, None if b is None else b[cols])
+
+    q = lin(x, "to_q")
+    k = lin(ctx, "to_k")
+    v = lin(ctx, "to_v")
+    ss = np.concatenate([(q.astype(F64) ** 2).sum(axis=1), (k.astype(F64) ** 2).sum(axis=1)])
+    allreduce(ss)
+    sq, sk = ss[:q.shape[0]], ss[q.shape[0]:]
+
+    def norm(m, s, gain):
+        out = m.astype(F64) / np.sqrt(s / inner + EPS)[:, None]
+        return (out * np.asarray(gain, F32)[cols].astype(F64)[None, :]).astype(F32)
+
+    q = norm(q, sq, w("q_norm.weight"))
+    k = norm(k, sk, w("k_norm.weight"))
+    hs = slice(rank * hl, (rank + 1) * hl)
+    if pe is not None:
+        rope_np.apply_rope(pe[0][hs], pe[1][hs], q, hl, head_dim)
+        kt = k_pe if k_pe is not None else pe
+        rope_np.apply_rope(kt[0][hs], kt[1][hs], k, hl, head_dim)
+    att = block_np.sdpa(q, k, v, hl, head_dim)
+    gw = w("to_gate_logits.weight")
+    if gw is not None:
+        gb = w("to_gate_logits.bias")
+        g = block_np.linear(x, gw[hs], None if gb is None else gb[hs])
+        gate = (F32(2.0) / (F32(1.0) + np.exp(-g))).astype(F32)
+        att = (att.reshape(att.shape[0], hl, head_dim) * gate[:, :, None]).astype(F32) \
+            .reshape(att.shape)
+    part = block_np.linear(att, w("to_out.0.weight")[:, cols]).astype(F64)
+    allreduce(part)
+    b = w("to_out.0.bias")
+    return (part + (0.0 if b is None else np.asarray(b, F32).astype(F64))).astype(F32)
+
+
+def _ff_tp(t, pre, xin, rank, world, allreduce):
+    wi = t[f"{pre}ff.net.0.proj.weight"]
+    fl = wi.shape[0] // world
+    cols = slice(rank * fl, (rank + 1) * fl)
+    bi = t.get(f"{pre}ff.net.0.proj.bias")
+    h = block_np.gelu_tanh(block_np.linear(xin, wi[cols], None if bi is None else bi[cols]))
+    part = block_np.linear(h, t[f"{pre}ff.net.2.weight"][:, cols]).astype(F64)
+    allreduce(part)
+    bo = t.get(f"{pre}ff.net.2.bias")
+    return (part + (0.0 if bo is None else np.asarray(bo, F32).astype(F64))).astype(F32)
+
+
+def _first_half(t, pre, s, dim, heads, tp):
+    hd = dim // heads
+    table = t[f"{pre}scale_shift_table"]
+    msa = block_np.ada_values(table, s["timesteps"], dim, 0, 3)
+    normed = block_np.ada_zero(s["x"], EPS, msa[1], msa[0])
+    sa = _attn_tp(t, f"{pre}attn1", normed, normed, s.get("pe"), None, heads, hd, *tp)
+    s["x"] = (s["x"] + sa * msa[2]).astype(F32)
+    xn = block_np.rms_norm(s["x"], EPS)
+    ca = block_np.ada_values(table, s["timesteps"], dim, 6, 9)
+    qin = block_np.mod(xn, ca[1], ca[0])
+    pst = np.asarray(t[f"{pre}prompt_scale_shift_table"], F32).ravel()
+    shift, scale = pst[:dim].copy(), pst[dim:2 * dim].copy()
+    pts = s.get("prompt_timestep")
+    if pts is not None and np.asarray(pts).size >= 2 * dim:
+        pts = np.asarray(pts, F32).ravel()
+        shift = (shift + pts[:dim]).astype(F32)
+        scale = (scale + pts[dim:2 * dim]).astype(F32)
+    kv = block_np.mod(s["context"], scale, shift)
+    co = _attn_tp(t, f"{pre}attn2", qin, kv, None, None, heads, hd, *tp)
+    s["x"] = (s["x"] + co * ca[2]).astype(F32)
+
+
+def _ff(t, pre, s, dim, tp):
+    mlp = block_np.ada_values(t[f"{pre}scale_shift_table"], s["timesteps"], dim, 3, 6)
+    scaled = block_np.ada_zero(s["x"], EPS, mlp[1], mlp[0])
+    s["x"] = (s["x"] + _ff_tp(t, pre, scaled, *tp) * mlp[2]).astype(F32)
+
+
+def block_forward_tp(t, video, audio, vdim, vheads, adim, aheads, rank, world, allreduce):
+    """block_np.block_forward (src/ltx25-block-ref.cc:308-389) on one rank's
+    shard; `allreduce(arr)` sums a float64 numpy array in place over ranks."""
+    tp = (rank, world, allreduce)
+    v = dict(video)
+    a = dict(audio)
+    v["x"] = np.asarray(v["x"], F32).copy()
+    a["x"] = np.asarray(a["x"], F32).copy()
+    _first_half(t, "", v, vdim, vheads, tp)
+    _first_half(t, "audio_", a, adim, aheads, tp)
+    vx_pre, ax_pre = v["x"].copy(), a["x"].copy()
+    ahd = adim // aheads
+    vtab = t["scale_shift_table_a2v_ca_video"]
+    atab = t["scale_shift_table_a2v_ca_audio"]
+    vsc, vsh, vg = block_np.av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 0)
+    asc, ash, _ = block_np.av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 0)
+    qv = block_np.ada_zero(vx_pre, EPS, vsc, vsh)
+    kv = block_np.ada_zero(ax_pre, EPS, asc, ash)
+    o = _attn_tp(t, "audio_to_video_attn", qv, kv, v.get("cross_pe"), a.get("cross_pe"),
+                 aheads, ahd, *tp)
+    v["x"] = (v["x"] + o * vg).astype(F32)
+    asc, ash, ag = block_np.av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 2)
+    vsc, vsh, _ = block_np.av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 2)
+    qa = block_np.ada_zero(ax_pre, EPS, asc, ash)
+    kvv = block_np.ada_zero(vx_pre, EPS, vsc, vsh)
+    o = _attn_tp(t, "video_to_audio_attn", qa, kvv, a.get("cross_pe"), v.get("cross_pe"),
+                 aheads, ahd, *tp)
+    a["x"] = (a["x"] + o * ag).astype(F32)
+    _ff(t, "", v, vdim, tp)
+    _ff(t, "audio_", a, adim, tp)
+    return v["x"], a["x"]

@@ -286,7 +286,7 @@ int launch_attention(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
   } else {
     return -2;
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 }  // namespace ltx

@@ -14,7 +14,22 @@
 // bf16 storage, f32 arithmetic, one CTA per row, 16-byte vector accesses.
 #include "block_ops.h"
 
+#include <atomic>
+
 namespace ltx {
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}  // namespace
+
+int launched()
+{
+  if (cudaGetLastError() != cudaSuccess) return -1;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return 0;
+}
+
+unsigned long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 namespace {
 
@@ -120,7 +135,9 @@ __global__ void __launch_bounds__(kRowThreads)
                         __nv_bfloat16* __restrict__ out, int ldo, int heads,
                         int head_dim, const float* __restrict__ gain,
                         const float* __restrict__ cosb,
-                        const float* __restrict__ sinb, int tokens, float eps)
+                        const float* __restrict__ sinb, int tokens, float eps,
+                        const float* __restrict__ sumsq, int norm_width,
+                        int head0)
 {
   extern __shared__ float srow[];   // the normalized row, f32 [inner]
   __shared__ float red[33];
@@ -137,8 +154,16 @@ __global__ void __launch_bounds__(kRowThreads)
       srow[k + i] = v[i];
     }
   }
-  const float inv = rsqrtf(block_sum(ss, red) / (float)inner + eps);
-  // (block_sum's barriers also publish srow.)
+  // A tensor-parallel rank holds only its heads' columns: the row's sum of
+  // squares over the whole width then comes in already reduced.
+  float total;
+  if (sumsq != nullptr) {
+    __syncthreads();   // publish srow
+    total = sumsq[t];
+  } else {
+    total = block_sum(ss, red);   // (its barriers also publish srow)
+  }
+  const float inv = rsqrtf(total / (float)norm_width + eps);
   const int half = head_dim / 2;
   __nv_bfloat16* orow = out + (size_t)t * ldo;
   for (int idx = threadIdx.x; idx < heads * half; idx += kRowThreads) {
@@ -147,7 +172,7 @@ __global__ void __launch_bounds__(kRowThreads)
     float a = srow[ia] * inv * (gain != nullptr ? gain[ia] : 1.0f);
     float b = srow[ib] * inv * (gain != nullptr ? gain[ib] : 1.0f);
     if (cosb != nullptr) {
-      const size_t o = ((size_t)h * tokens + t) * half + j;
+      const size_t o = ((size_t)(head0 + h) * tokens + t) * half + j;
       const float c = cosb[o], s = sinb[o];
       const float ra = a * c - b * s;
       const float rb = b * c + a * s;
@@ -156,6 +181,55 @@ __global__ void __launch_bounds__(kRowThreads)
     }
     orow[ia] = __float2bfloat16_rn(a);
     orow[ib] = __float2bfloat16_rn(b);
+  }
+}
+
+// out[t] = sum of squares of row t's `cols` values (f32).
+__global__ void __launch_bounds__(kRowThreads)
+    row_sumsq_kernel(const __nv_bfloat16* __restrict__ in, int ldi, int cols,
+                     float* __restrict__ out)
+{
+  __shared__ float red[33];
+  const __nv_bfloat16* xr = in + (size_t)blockIdx.x * ldi;
+  float ss = 0.0f;
+  for (int k = threadIdx.x * 8; k < cols; k += kRowThreads * 8) {
+    float v[8];
+    load8(xr + k, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+  }
+  const float tot = block_sum(ss, red);
+  if (threadIdx.x == 0) out[blockIdx.x] = tot;
+}
+
+// x = x + gate * (part + bias): the gated residual of a row-split output
+// projection once its partial sums are reduced (the GEMM epilogue's
+// EPI_GATED_RES arithmetic: a = acc + bias; x = fma(gate, a, x)).
+__global__ void gated_residual_kernel(__nv_bfloat16* __restrict__ x, int ldx,
+                                      const __nv_bfloat16* __restrict__ part,
+                                      const __nv_bfloat16* __restrict__ bias,
+                                      const float* __restrict__ gate, int rows,
+                                      int dim)
+{
+  const int chunks = dim / 8;
+  const size_t total = (size_t)rows * chunks;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / chunks);
+    const int k = (int)(i % chunks) * 8;
+    float xv[8], pv[8];
+    load8(x + (size_t)r * ldx + k, xv);
+    load8(part + (size_t)r * dim + k, pv);
+    float bv[8];
+    if (bias != nullptr) {
+      load8(bias + k, bv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bv[j] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xv[j] = fmaf(gate[k + j], pv[j] + bv[j], xv[j]);
+    store8(x + (size_t)r * ldx + k, xv);
   }
 }
 
@@ -176,7 +250,7 @@ int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
   size_t grid = (n + 255) / 256;
   if (grid > 4096) grid = 4096;
   f32_to_bf16_kernel<<<(unsigned)grid, 256, 0, s>>>(a, out, n);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,
@@ -187,7 +261,7 @@ int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,
   int grid = (n + threads - 1) / threads;
   if (grid > 1024) grid = 1024;
   vec_add_kernel<<<grid, threads, 0, s>>>(a, b, out, n);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
@@ -203,13 +277,14 @@ int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
     row_mod_kernel<false><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, dim,
                                                        scale, shift, eps);
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
                         int ldo, int rows, int heads, int head_dim,
                         const float* gain, const float* cosb,
-                        const float* sinb, float eps, cudaStream_t s)
+                        const float* sinb, float eps, cudaStream_t s,
+                        const float* sumsq, int norm_width, int head0)
 {
   if (rows <= 0) return 0;
   const int inner = heads * head_dim;
@@ -225,8 +300,32 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
     }
   }
   qk_norm_rope_kernel<<<rows, kRowThreads, smem, s>>>(
-      in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+      in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq,
+      norm_width > 0 ? norm_width : inner, head0);
+  return launched();
+}
+
+int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,
+                     float* out, cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  if (cols % 8 != 0 || ldi % 8 != 0) return -2;
+  row_sumsq_kernel<<<rows, kRowThreads, 0, s>>>(in, ldi, cols, out);
+  return launched();
+}
+
+int launch_gated_residual(__nv_bfloat16* x, int ldx, const __nv_bfloat16* part,
+                          const __nv_bfloat16* bias, const float* gate, int rows,
+                          int dim, cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  if (dim % 8 != 0 || ldx % 8 != 0) return -2;
+  const size_t total = (size_t)rows * (dim / 8);
+  size_t grid = (total + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  gated_residual_kernel<<<(unsigned)grid, 256, 0, s>>>(x, ldx, part, bias, gate,
+                                                      rows, dim);
+  return launched();
 }
 
 }  // namespace ltx

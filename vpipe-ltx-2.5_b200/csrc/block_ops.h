@@ -9,6 +9,11 @@
 
 namespace ltx {
 
+// Status of the kernel launch just issued (0 or -1), counting it when it
+// went in: the library's launch tally, read by ltx_launch_count.
+int launched();
+unsigned long long launch_count();
+
 int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
                        cudaStream_t s);
 
@@ -24,11 +29,24 @@ int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
 
 // RMSNorm over the whole heads*head_dim row with gain (f32, may be null),
 // then split-half RoPE with [heads][rows][head_dim/2] f32 tables (may be
-// null).  in: row stride ldi; out: row stride ldo.
+// null).  in: row stride ldi; out: row stride ldo.  Tensor-parallel form:
+// the row holds heads [head0, head0 + heads) of a wider row whose per-token
+// sum of squares (over norm_width columns) is given in sumsq.
 int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
                         int ldo, int rows, int heads, int head_dim,
                         const float* gain, const float* cosb,
-                        const float* sinb, float eps, cudaStream_t s);
+                        const float* sinb, float eps, cudaStream_t s,
+                        const float* sumsq = nullptr, int norm_width = 0,
+                        int head0 = 0);
+
+// out[r] = sum of squares of row r's first `cols` values, f32.
+int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,
+                     float* out, cudaStream_t s);
+
+// x[r] += gate * (part[r] + bias) (part [rows][dim] dense, bias may be null).
+int launch_gated_residual(__nv_bfloat16* x, int ldx, const __nv_bfloat16* part,
+                          const __nv_bfloat16* bias, const float* gate, int rows,
+                          int dim, cudaStream_t s);
 
 // Non-causal attention, token-major q [tq][ldq], k/v [tk][ld], head h at
 // columns [h*D, (h+1)*D); o [tq][ldo]; optional gate logits [tq][ldg]

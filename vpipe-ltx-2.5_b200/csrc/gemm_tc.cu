@@ -3,6 +3,7 @@
 #include <cstdio>
 
 #include "gemm_tc.cuh"
+#include "block_ops.h"
 #include "kernels.h"
 
 namespace ltx {
@@ -720,10 +721,10 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (cudaLaunchKernelEx(&cfg, kern, tx, tw, tsz, p) != cudaSuccess) return -3;
-    return 0;
+    return launched() == 0 ? 0 : -3;
   }
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, tsz, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  return launched() == 0 ? 0 : -3;
 }
 
 template <int MODE, int TN, bool PAIR>

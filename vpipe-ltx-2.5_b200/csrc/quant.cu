@@ -3,6 +3,7 @@
 // symmetric int8 row quantization.  All HBM-bound.
 #include <cuda_fp16.h>
 
+#include "block_ops.h"
 #include "kernels.h"
 
 namespace ltx {
@@ -192,7 +193,7 @@ int launch_pack_sz(const void* scales, const void* biases, int dtype, int N,
 {
   pack_sz_kernel<<<grid_for((long long)N * G, 256), 256, 0, stream>>>(
       scales, biases, dtype, N, G, sz);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 int launch_pack_w8g64(const float* w, int N, int K, uint32_t* codes,
@@ -204,7 +205,7 @@ int launch_pack_w8g64(const float* w, int N, int K, uint32_t* codes,
   const long long grid = (threads + block - 1) / block;
   pack_w8g64_kernel<<<(unsigned)grid, block, 0, stream>>>(w, N, K, codes,
                                                           scales, biases);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 int launch_dequant_w8(const uint8_t* codes, const uint32_t* sz, int N, int K,
@@ -212,7 +213,7 @@ int launch_dequant_w8(const uint8_t* codes, const uint32_t* sz, int N, int K,
 {
   dequant_w8_kernel<<<grid_for((long long)N * (K / 16), 256), 256, 0,
                       stream>>>(codes, sz, N, K, out);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 int launch_quant_rows_i8(const __nv_bfloat16* x, int rows, int K, int ldx,
@@ -226,7 +227,7 @@ int launch_quant_rows_i8(const __nv_bfloat16* x, int rows, int K, int ldx,
   dim3 grid(K / group, rows);
   quant_rows_i8_kernel<<<grid, threads, 0, stream>>>(x, K, ldx, group, q,
                                                      scale);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launched();
 }
 
 }  // namespace ltx

@@ -206,6 +206,43 @@ int ltx_qlinear_i8_static(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
   return LTX_OK;
 }
 
+unsigned long long ltx_launch_count(void) { return ltx::launch_count(); }
+
+int ltx_tp_unique_id(void* id, int bytes)
+{
+  if (id == nullptr) return LTX_E_NULL;
+  if (bytes < LTX_TP_ID_BYTES) return LTX_E_SHAPE;
+  std::string e;
+  return ltx25::Comm::unique_id(id, &e) ? LTX_OK : LTX_E_CUDA;
+}
+
+int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, LTX_E_SHAPE, "set_tp: rank outside [0, world)");
+  if (ctx->ops.comm() != nullptr) return fail(ctx, LTX_E_STATE, "set_tp: already set");
+  if (world == 1) return LTX_OK;
+  if (id == nullptr) return fail(ctx, LTX_E_NULL, "set_tp: null id");
+  auto c = std::make_unique<ltx25::Comm>();
+  std::string e;
+  if (!c->init(ctx->ops.device(), rank, world, id, &e)) return fail(ctx, LTX_E_CUDA, e);
+  ctx->ops.set_comm(std::move(c));
+  return LTX_OK;
+}
+
+int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (buf == nullptr && count > 0) return fail(ctx, LTX_E_NULL, "tp_allreduce: null buffer");
+  if (dtype != 0 && dtype != 1) return fail(ctx, LTX_E_SHAPE, "tp_allreduce: dtype 0 or 1");
+  if (ctx->ops.comm() == nullptr) return LTX_OK;   // one rank: the sum is itself
+  std::string e;
+  if (!ctx->ops.comm()->allreduce_sum(buf, count, dtype, S(stream), &e))
+    return fail(ctx, LTX_E_CUDA, e);
+  return LTX_OK;
+}
+
 int ltx_set_route(ltx_ctx* ctx, int route)
 {
   if (ctx == nullptr) return LTX_E_NULL;

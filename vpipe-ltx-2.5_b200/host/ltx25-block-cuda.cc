@@ -100,7 +100,7 @@ bool CudaBlock::set_tensor(const std::string& name, const float* data,
 }
 
 bool CudaBlock::take_f32_(const std::string& name, size_t count, float** out,
-                          std::string* err, bool required)
+                          std::string* err, bool required, size_t off, size_t n)
 {
   *out = nullptr;
   auto it = _staged.find(name);
@@ -113,12 +113,14 @@ bool CudaBlock::take_f32_(const std::string& name, size_t count, float** out,
     return fail(err, "tensor '" + name + "' has " +
                          std::to_string((size_t)st.rows * st.cols) +
                          " elements, want " + std::to_string(count));
+  if (n == 0) n = count - off;
+  if (off + n > count) return fail(err, "tensor '" + name + "': slice outside the tensor");
   float* d = nullptr;
-  if (!cuda_ok(cudaMalloc(&d, count * sizeof(float)), "cudaMalloc", err)) return false;
+  if (!cuda_ok(cudaMalloc(&d, n * sizeof(float)), "cudaMalloc", err)) return false;
   _owned.push_back(d);
   const cudaError_t e =
-      st.dev_f32 ? cudaMemcpy(d, st.dev_f32, count * 4, cudaMemcpyDeviceToDevice)
-                 : cudaMemcpy(d, st.host.data(), count * 4, cudaMemcpyHostToDevice);
+      st.dev_f32 ? cudaMemcpy(d, st.dev_f32 + off, n * 4, cudaMemcpyDeviceToDevice)
+                 : cudaMemcpy(d, st.host.data() + off, n * 4, cudaMemcpyHostToDevice);
   if (!cuda_ok(e, "upload", err)) return false;
   *out = d;
   return true;
@@ -126,32 +128,38 @@ bool CudaBlock::take_f32_(const std::string& name, size_t count, float** out,
 
 bool CudaBlock::take_bf16_(const std::string& name, size_t count,
                            __nv_bfloat16** out, std::string* err,
-                           bool required)
+                           bool required, size_t off, size_t n)
 {
   *out = nullptr;
   float* f = nullptr;
-  if (!take_f32_(name, count, &f, err, required)) return false;
+  if (!take_f32_(name, count, &f, err, required, off, n)) return false;
   if (f == nullptr) return true;
+  if (n == 0) n = count - off;
   __nv_bfloat16* d = nullptr;
-  if (!cuda_ok(cudaMalloc(&d, count * 2), "cudaMalloc", err)) return false;
+  if (!cuda_ok(cudaMalloc(&d, n * 2), "cudaMalloc", err)) return false;
   _owned.push_back(d);
-  if (ltx::launch_f32_to_bf16(f, d, count, nullptr) != 0 ||
+  if (ltx::launch_f32_to_bf16(f, d, n, nullptr) != 0 ||
       !cuda_ok(cudaDeviceSynchronize(), "convert", err))
     return fail(err, "f32 -> bf16 conversion failed for " + name);
   *out = d;
   return true;
 }
 
-// Concatenate quantized linears along N (rows of the weight): codes row
-// blocks back to back, scale/zero-point pairs side by side per K group.
-bool CudaBlock::fuse_(const std::vector<const QWeight*>& parts, QWeight* out,
+// Concatenate blocks of quantized linears along N (rows of the weight):
+// codes row blocks back to back, scale/zero-point pairs side by side per K
+// group.  Each part may also keep only a K range (a row-split shard): its
+// codes columns and the matching scale groups.
+bool CudaBlock::fuse_(const std::vector<Part>& parts, QWeight* out,
                       std::string* err)
 {
-  const int K = parts[0]->K;
+  const int K = parts[0].kcols > 0 ? parts[0].kcols : parts[0].q->K;
   int N = 0;
-  for (const QWeight* q : parts) {
-    if (!q->quantized || q->K != K) return fail(err, "fuse: mismatched parts");
-    N += q->N;
+  for (const Part& pt : parts) {
+    const int kc = pt.kcols > 0 ? pt.kcols : pt.q->K;
+    if (!pt.q->quantized || kc != K || pt.k0 % 64 != 0 || kc % 64 != 0 ||
+        pt.k0 + kc > pt.q->K || pt.r0 < 0 || pt.r0 + pt.rows > pt.q->N)
+      return fail(err, "fuse: mismatched parts");
+    N += pt.rows;
   }
   QWeight f;
   f.N = N;
@@ -167,16 +175,19 @@ bool CudaBlock::fuse_(const std::vector<const QWeight*>& parts, QWeight* out,
     return false;
   }
   int n0 = 0;
-  for (const QWeight* q : parts) {
-    if (!cuda_ok(cudaMemcpy(f.codes + (size_t)n0 * K, q->codes, (size_t)q->N * K,
-                            cudaMemcpyDeviceToDevice), "fuse codes", err) ||
-        !cuda_ok(cudaMemcpy2D(f.sz + n0, (size_t)N * 4, q->sz, (size_t)q->N * 4,
-                              (size_t)q->N * 4, G, cudaMemcpyDeviceToDevice),
+  for (const Part& pt : parts) {
+    const QWeight* q = pt.q;
+    const uint8_t* src_codes = q->codes + (size_t)pt.r0 * q->K + pt.k0;
+    const uint32_t* src_sz = q->sz + (size_t)(pt.k0 / 64) * q->N + pt.r0;
+    if (!cuda_ok(cudaMemcpy2D(f.codes + (size_t)n0 * K, K, src_codes, q->K, K,
+                              pt.rows, cudaMemcpyDeviceToDevice), "fuse codes", err) ||
+        !cuda_ok(cudaMemcpy2D(f.sz + n0, (size_t)N * 4, src_sz, (size_t)q->N * 4,
+                              (size_t)pt.rows * 4, G, cudaMemcpyDeviceToDevice),
                  "fuse sz", err)) {
       free_qweight(&f);
       return false;
     }
-    n0 += q->N;
+    n0 += pt.rows;
   }
   *out = f;
   return true;
@@ -187,13 +198,26 @@ bool CudaBlock::build_attn_(const std::string& p, bool self, int qdim,
                             CudaAttn& a, std::string* err)
 {
   const int inner = heads * head_dim;
+  // Tensor parallelism (Megatron): q/k/v and the gate logits are split by
+  // heads (column split), the output projection by its K columns (row
+  // split); the out bias is added once, after the partial sums are reduced.
+  const int W = _tp_world, R = _tp_rank;
+  if (heads % W != 0)
+    return fail(err, p + ": " + std::to_string(heads) + " heads do not split over " +
+                         std::to_string(W) + " ranks (shape)");
+  const int hl = heads / W, il = hl * head_dim, c0 = R * il;
+  if (W > 1 && il % 64 != 0)
+    return fail(err, p + ": per-rank width " + std::to_string(il) +
+                         " is not a multiple of 64 (shape)");
   a.self = self;
-  a.heads = heads;
+  a.heads = hl;
   a.head_dim = head_dim;
-  a.inner = inner;
+  a.inner = il;
   a.qdim = qdim;
   a.kvdim = kvdim;
   a.odim = odim;
+  a.head0 = R * hl;
+  a.norm_width = inner;
   auto qlin = [&](const std::string& n, int N, int K) -> const QWeight* {
     auto it = _staged.find(p + n);
     if (it == _staged.end() || !it->second.quant) {
@@ -217,7 +241,8 @@ bool CudaBlock::build_attn_(const std::string& p, bool self, int qdim,
   const QWeight* wo = qlin(".to_out.0.weight", odim, inner);
   if (!wo) return false;
 
-  // Biases: q/k/v concatenated to match the fused GEMM's output columns.
+  // Biases: this rank's q/k/v columns, concatenated to match the fused
+  // GEMM's output columns.
   std::vector<float> bcat;
   for (const char* bn : {".to_q.bias", ".to_k.bias", ".to_v.bias"}) {
     auto it = _staged.find(p + bn);
@@ -230,45 +255,51 @@ bool CudaBlock::build_attn_(const std::string& p, bool self, int qdim,
     } else {
       h = it->second.host;
     }
-    bcat.insert(bcat.end(), h.begin(), h.end());
+    bcat.insert(bcat.end(), h.begin() + c0, h.begin() + c0 + il);
   }
   const std::string tmpq = p + ".__qkv_bias", tmpkv = p + ".__kv_bias";
   if (self) {
-    if (!fuse_({wq, wk, wv}, &a.qkv, err)) return false;
-    if (!set_tensor(tmpq, bcat.data(), 3 * inner, 0, false, err) ||
-        !take_bf16_(tmpq, (size_t)3 * inner, &a.qkv_b, err))
+    if (!fuse_({{wq, c0, il, 0, 0}, {wk, c0, il, 0, 0}, {wv, c0, il, 0, 0}}, &a.qkv, err))
+      return false;
+    if (!set_tensor(tmpq, bcat.data(), 3 * il, 0, false, err) ||
+        !take_bf16_(tmpq, (size_t)3 * il, &a.qkv_b, err))
       return false;
   } else {
-    if (!fuse_({wq}, &a.q, err) || !fuse_({wk, wv}, &a.kv, err)) return false;
-    if (!set_tensor(tmpq, bcat.data(), inner, 0, false, err) ||
-        !take_bf16_(tmpq, (size_t)inner, &a.qkv_b, err))
+    if (!fuse_({{wq, c0, il, 0, 0}}, &a.q, err) ||
+        !fuse_({{wk, c0, il, 0, 0}, {wv, c0, il, 0, 0}}, &a.kv, err))
       return false;
-    if (!set_tensor(tmpkv, bcat.data() + inner, 2 * inner, 0, false, err) ||
-        !take_bf16_(tmpkv, (size_t)2 * inner, &a.kv_b, err))
+    if (!set_tensor(tmpq, bcat.data(), il, 0, false, err) ||
+        !take_bf16_(tmpq, (size_t)il, &a.qkv_b, err))
+      return false;
+    if (!set_tensor(tmpkv, bcat.data() + il, 2 * il, 0, false, err) ||
+        !take_bf16_(tmpkv, (size_t)2 * il, &a.kv_b, err))
       return false;
   }
   _staged.erase(tmpq);
   _staged.erase(tmpkv);
-  if (!fuse_({wo}, &a.o, err)) return false;
+  if (!fuse_({{wo, 0, odim, W > 1 ? c0 : 0, W > 1 ? il : 0}}, &a.o, err)) return false;
   if (!take_bf16_(p + ".to_out.0.bias", odim, &a.o_b, err) ||
-      !take_f32_(p + ".q_norm.weight", inner, &a.q_norm, err) ||
-      !take_f32_(p + ".k_norm.weight", inner, &a.k_norm, err))
+      !take_f32_(p + ".q_norm.weight", inner, &a.q_norm, err, true, c0, il) ||
+      !take_f32_(p + ".k_norm.weight", inner, &a.k_norm, err, true, c0, il))
     return false;
-  // Gate logits: dense (excluded from quantization), [heads][qdim].
+  // Gate logits: dense (excluded from quantization), [heads][qdim]; this
+  // rank's rows.
   float* gw = nullptr;
-  if (!take_f32_(p + ".to_gate_logits.weight", (size_t)heads * qdim, &gw, err, false))
+  if (!take_f32_(p + ".to_gate_logits.weight", (size_t)heads * qdim, &gw, err, false,
+                 (size_t)R * hl * qdim, (size_t)hl * qdim))
     return false;
   if (gw != nullptr) {
     __nv_bfloat16* gwb = nullptr;
-    if (!cuda_ok(cudaMalloc(&gwb, (size_t)heads * qdim * 2), "cudaMalloc", err)) return false;
-    if (ltx::launch_f32_to_bf16(gw, gwb, (size_t)heads * qdim, nullptr) != 0 ||
+    if (!cuda_ok(cudaMalloc(&gwb, (size_t)hl * qdim * 2), "cudaMalloc", err)) return false;
+    if (ltx::launch_f32_to_bf16(gw, gwb, (size_t)hl * qdim, nullptr) != 0 ||
         !cuda_ok(cudaDeviceSynchronize(), "convert", err))
       return false;
     const bool ok = upload_dweight(*_ops, reinterpret_cast<const uint16_t*>(gwb),
-                                   heads, qdim, true, &a.gate, err);
+                                   hl, qdim, true, &a.gate, err);
     cudaFree(gwb);
     if (!ok) return false;
-    if (!take_bf16_(p + ".to_gate_logits.bias", heads, &a.gate_b, err, false))
+    if (!take_bf16_(p + ".to_gate_logits.bias", heads, &a.gate_b, err, false,
+                    (size_t)R * hl, (size_t)hl))
       return false;
   }
   return true;
@@ -291,13 +322,21 @@ bool CudaBlock::build_stream_(bool audio, CudaStreamW& w, std::string* err)
     return fail(err, "missing quantized tensor '" + pre + "ff.net.0.proj.weight'");
   if (fo == _staged.end() || !fo->second.quant)
     return fail(err, "missing quantized tensor '" + pre + "ff.net.2.weight'");
-  w.ff_hidden = fi->second.q.N;
-  if (fi->second.q.K != d || fo->second.q.N != d || fo->second.q.K != w.ff_hidden)
+  const int hidden = fi->second.q.N;
+  if (fi->second.q.K != d || fo->second.q.N != d || fo->second.q.K != hidden)
     return fail(err, "feed-forward shapes disagree with the stream width");
-  if (!fuse_({&fi->second.q}, &w.ff_in, err) || !fuse_({&fo->second.q}, &w.ff_out, err))
+  // Column-split ff.net.0 (GELU is per column), row-split ff.net.2.
+  const int W = _tp_world, R = _tp_rank;
+  if (hidden % (64 * W) != 0)
+    return fail(err, pre + "ff: hidden width " + std::to_string(hidden) +
+                         " does not split over " + std::to_string(W) + " ranks (shape)");
+  const int fl = hidden / W, f0 = R * fl;
+  w.ff_hidden = fl;
+  if (!fuse_({{&fi->second.q, f0, fl, 0, 0}}, &w.ff_in, err) ||
+      !fuse_({{&fo->second.q, 0, d, W > 1 ? f0 : 0, W > 1 ? fl : 0}}, &w.ff_out, err))
     return false;
   // Video ff has no bias, audio ff does (src/ltx25-dit-weights.cc:482-486).
-  if (!take_bf16_(pre + "ff.net.0.proj.bias", w.ff_hidden, &w.ff_in_b, err, false) ||
+  if (!take_bf16_(pre + "ff.net.0.proj.bias", hidden, &w.ff_in_b, err, false, f0, fl) ||
       !take_bf16_(pre + "ff.net.2.bias", d, &w.ff_out_b, err, false))
     return false;
   if (!take_f32_(pre + "scale_shift_table", (size_t)9 * d, &w.scale_shift, err) ||
@@ -313,6 +352,9 @@ bool CudaBlock::build_stream_(bool audio, CudaStreamW& w, std::string* err)
 bool CudaBlock::finalize(std::string* err)
 {
   if (_final) return true;
+  _comm = _ops->comm();
+  _tp_world = _comm ? _comm->world() : 1;
+  _tp_rank = _comm ? _comm->rank() : 0;
   if (!build_stream_(false, _video, err) || !build_stream_(true, _audio, err))
     return false;
   // Both cross-attentions run at the AUDIO head count and head width
@@ -334,18 +376,19 @@ BlockArena::~BlockArena()
 {
   for (void* p : {(void*)normed, (void*)qkv, (void*)qn, (void*)kn, (void*)att,
                   (void*)glog, (void*)ctxmod, (void*)kvp, (void*)ff, (void*)qv,
-                  (void*)kva, (void*)qa, (void*)kvv, (void*)mods})
+                  (void*)kva, (void*)qa, (void*)kvv, (void*)mods, (void*)part,
+                  (void*)ssq})
     cudaFree(p);
 }
 
 bool BlockArena::ensure(int i, size_t n, std::string* err)
 {
-  void** slots[14] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
+  void** slots[16] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
                       (void**)&att, (void**)&glog, (void**)&ctxmod, (void**)&kvp,
                       (void**)&ff, (void**)&qv, (void**)&kva, (void**)&qa,
-                      (void**)&kvv, (void**)&mods};
+                      (void**)&kvv, (void**)&mods, (void**)&part, (void**)&ssq};
   if (n <= cap[i]) return true;
-  const size_t elt = i == 13 ? sizeof(float) : sizeof(__nv_bfloat16);
+  const size_t elt = (i == 13 || i == 15) ? sizeof(float) : sizeof(__nv_bfloat16);
   cudaFree(*slots[i]);
   *slots[i] = nullptr;
   cap[i] = 0;
@@ -364,7 +407,7 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   const size_t vd = _vdim, ad = _adim;
   const size_t ai = ad;   // audio inner (the cross attentions' width too)
   auto mx = [](std::initializer_list<size_t> l) { return std::max(l); };
-  const size_t need[14] = {
+  const size_t need[16] = {
       mx({vt * vd, at * ad}),                                        // normed
       mx({vt * 3 * vd, at * 3 * ad, vt * vd, vt * ai, at * ai}),     // qkv / q
       mx({vt * vd, at * ad, vt * ai}),                               // qn
@@ -375,9 +418,11 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
       mx({tt * 2 * vd, tt * 2 * ad, at * 2 * ai, vt * 2 * ai}),      // kv proj
       mx({vt * (size_t)_video.ff_hidden, at * (size_t)_audio.ff_hidden}),  // ff
       vt * vd, at * ad, at * ad, vt * vd,                            // qv kva qa kvv
-      (size_t)MOD_ROWS * (vd + ad)};                                 // mods
+      (size_t)MOD_ROWS * (vd + ad),                                  // mods
+      _tp_world > 1 ? mx({vt * vd, at * ad}) : 0,                    // part
+      _tp_world > 1 ? 2 * (vt + at + tt) : 0};                       // ssq
   _arp = share ? share : std::make_shared<BlockArena>();
-  for (int i = 0; i < 14; ++i)
+  for (int i = 0; i < 16; ++i)
     if (!_arp->ensure(i, need[i], err)) return false;
   _arp->video = std::max(_arp->video, vt);
   _arp->audio = std::max(_arp->audio, at);
@@ -417,10 +462,23 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     ldq = I;
     ldkv = 2 * I;
   }
+  // RMSNorm spans the whole inner width: a rank that holds only some heads
+  // reduces the per-token sums of squares (q rows then k rows) first.
+  const float *qss = nullptr, *kss = nullptr;
+  if (a.norm_width != I) {
+    if (ltx::launch_row_sumsq(qraw, ldq, tq, I, _arp->ssq, s) != 0 ||
+        ltx::launch_row_sumsq(kraw, ldkv, tkv, I, _arp->ssq + tq, s) != 0)
+      return fail(err, "q/k sum-of-squares launch failed");
+    if (!_comm->allreduce_sum(_arp->ssq, (size_t)tq + tkv, 0, s, err)) return false;
+    qss = _arp->ssq;
+    kss = _arp->ssq + tq;
+  }
   if (ltx::launch_qk_norm_rope(qraw, ldq, _arp->qn, I, tq, a.heads, a.head_dim,
-                               a.q_norm, qcos, qsin, kEps, s) != 0 ||
+                               a.q_norm, qcos, qsin, kEps, s, qss, a.norm_width,
+                               a.head0) != 0 ||
       ltx::launch_qk_norm_rope(kraw, ldkv, _arp->kn, I, tkv, a.heads,
-                               a.head_dim, a.k_norm, kcos, ksin, kEps, s) != 0)
+                               a.head_dim, a.k_norm, kcos, ksin, kEps, s, kss,
+                               a.norm_width, a.head0) != 0)
     return fail(err, "q/k norm + rope launch failed");
   const __nv_bfloat16* glog = nullptr;
   if (a.gate.N > 0) {
@@ -432,6 +490,24 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   if (ltx::launch_attention(_arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog,
                             a.heads, tq, tkv, a.heads, a.head_dim, s) != 0)
     return fail(err, "attention launch failed");
+  return true;
+}
+
+bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
+                          const QWeight& w, const __nv_bfloat16* bias,
+                          __nv_bfloat16* x, int n, int d, const float* gate,
+                          std::string* err)
+{
+  if (_tp_world == 1)
+    return _ops->linear(s, in, k, w, bias, x, d, n, k, d, ltx::EPI_GATED_RES, gate, err);
+  // Row split: this rank's K columns give a partial product; the sum over
+  // ranks, then the bias and the gated residual, once.
+  if (!_ops->linear(s, in, k, w, nullptr, _arp->part, d, n, k, d, ltx::EPI_STORE,
+                    nullptr, err) ||
+      !_comm->allreduce_sum(_arp->part, (size_t)n * d, 1, s, err))
+    return false;
+  if (ltx::launch_gated_residual(x, d, _arp->part, bias, gate, n, d, s) != 0)
+    return fail(err, "gated residual launch failed");
   return true;
 }
 
@@ -454,9 +530,8 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
   if (!attend_(s, w.attn1, _arp->normed, n, _arp->normed, n, io.pe_cos, io.pe_sin,
                io.pe_cos, io.pe_sin, _arp->att, err))
     return false;
-  if (!_ops->linear(s, _arp->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, d,
-                    n, w.attn1.inner, d, ltx::EPI_GATED_RES,
-                    mods + (MOD_MSA + 2) * d, err))
+  if (!out_proj_(s, _arp->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, n, d,
+                 mods + (MOD_MSA + 2) * d, err))
     return false;
   // Text cross-attention: query = mod(rms_norm(x)) (= ada_zero with the
   // cross rows), key/value = context modulated by the prompt table + driver.
@@ -469,9 +544,8 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
   if (!attend_(s, w.attn2, _arp->normed, n, _arp->ctxmod, io.text_tokens, nullptr,
                nullptr, nullptr, nullptr, _arp->att, err))
     return false;
-  return _ops->linear(s, _arp->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x,
-                      d, n, w.attn2.inner, d, ltx::EPI_GATED_RES,
-                      mods + (MOD_CA + 2) * d, err);
+  return out_proj_(s, _arp->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x, n, d,
+                   mods + (MOD_CA + 2) * d, err);
 }
 
 bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
@@ -487,9 +561,8 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
     return fail(err, "ff pre-norm launch failed");
   return _ops->linear(s, _arp->normed, d, w.ff_in, w.ff_in_b, _arp->ff, w.ff_hidden, n,
                       d, w.ff_hidden, ltx::EPI_GELU, nullptr, err) &&
-         _ops->linear(s, _arp->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, d, n,
-                      w.ff_hidden, d, ltx::EPI_GATED_RES, mods + (MOD_MLP + 2) * d,
-                      err);
+         out_proj_(s, _arp->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, n, d,
+                   mods + (MOD_MLP + 2) * d, err);
 }
 
 bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
@@ -537,14 +610,14 @@ bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
     // a2v: video queries, audio keys/values
     if (!attend_(s, _a2v, _arp->qv, v.tokens, _arp->kva, a.tokens, v.cpe_cos,
                  v.cpe_sin, a.cpe_cos, a.cpe_sin, _arp->att, err) ||
-        !_ops->linear(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, vd, v.tokens,
-                      _a2v.inner, vd, ltx::EPI_GATED_RES, vm + MOD_AVG * vd, err))
+        !out_proj_(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, v.tokens, vd,
+                   vm + MOD_AVG * vd, err))
       return false;
     // v2a: audio queries, video keys/values
     if (!attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, v.tokens, a.cpe_cos,
                  a.cpe_sin, v.cpe_cos, v.cpe_sin, _arp->att, err) ||
-        !_ops->linear(s, _arp->att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, ad, a.tokens,
-                      _v2a.inner, ad, ltx::EPI_GATED_RES, am + MOD_AVG * ad, err))
+        !out_proj_(s, _arp->att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, a.tokens, ad,
+                   am + MOD_AVG * ad, err))
       return false;
   }
 

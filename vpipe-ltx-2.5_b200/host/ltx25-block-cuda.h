@@ -40,7 +40,11 @@ struct CudaAttn {
   float* q_norm = nullptr;
   float* k_norm = nullptr;
   bool self = false;
+  // heads/inner are this rank's share under tensor parallelism; head0 is
+  // its first head and norm_width the full inner width the q/k RMSNorm
+  // spans (== inner on one GPU).
   int heads = 0, head_dim = 0, inner = 0, qdim = 0, kvdim = 0, odim = 0;
+  int head0 = 0, norm_width = 0;
 };
 
 struct CudaStreamW {
@@ -79,7 +83,9 @@ struct BlockArena {
                 *ctxmod = nullptr, *kvp = nullptr, *ff = nullptr,
                 *qv = nullptr, *kva = nullptr, *qa = nullptr, *kvv = nullptr;
   float* mods = nullptr;      // adaLN rows, f32
-  size_t cap[14] = {};        // element capacity of each buffer above
+  __nv_bfloat16* part = nullptr;   // row-split partial sums (tensor parallel)
+  float* ssq = nullptr;            // per-token q/k sums of squares (tensor parallel)
+  size_t cap[16] = {};        // element capacity of each buffer above
   size_t video = 0, audio = 0, text = 0;   // reserved token maxima
   ~BlockArena();
   // Grow buffer i (in the order declared) to at least n elements.
@@ -147,15 +153,31 @@ private:
                    std::string* err);
   bool ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
            std::string* err);
+  // Upload tensor `name` (count elements in all) as f32 / bf16, keeping
+  // elements [off, off + n) (n = 0: all).
   bool take_f32_(const std::string& name, size_t count, float** out,
-                 std::string* err, bool required = true);
+                 std::string* err, bool required = true, size_t off = 0,
+                 size_t n = 0);
   bool take_bf16_(const std::string& name, size_t count, __nv_bfloat16** out,
-                  std::string* err, bool required = true);
-  bool fuse_(const std::vector<const QWeight*>& parts, QWeight* out,
-             std::string* err);
+                  std::string* err, bool required = true, size_t off = 0,
+                  size_t n = 0);
+  // A block of a w8g64 pack: rows [r0, r0 + rows) and K columns
+  // [k0, k0 + kcols) (kcols = 0: all of K).
+  struct Part {
+    const QWeight* q;
+    int r0, rows, k0, kcols;
+  };
+  bool fuse_(const std::vector<Part>& parts, QWeight* out, std::string* err);
+  // x += gate * (att . Wo^T + bias), row-split and reduced under tensor
+  // parallelism.
+  bool out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k, const QWeight& w,
+                 const __nv_bfloat16* bias, __nv_bfloat16* x, int n, int d,
+                 const float* gate, std::string* err);
 
   CudaOps* _ops;
   int _vdim, _vheads, _adim, _aheads;
+  const Comm* _comm = nullptr;   // set at finalize when the context is sharded
+  int _tp_rank = 0, _tp_world = 1;
   std::map<std::string, Staged> _staged;
   std::vector<void*> _owned;   // device buffers this block frees
   CudaStreamW _video, _audio;

@@ -1,0 +1,114 @@
+// ltx25-comm.cc -- Comm (see ltx25-comm.h).
+#include "ltx25-comm.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+namespace ltx25 {
+
+namespace {
+
+struct Nccl {
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclCommDestroy) comm_destroy = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  bool ok = false;
+  std::string why;
+};
+
+const Nccl& nccl()
+{
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = nullptr;
+    for (const char* name : {"libnccl.so.2", "libnccl.so"}) {
+      h = dlopen(name, RTLD_NOW | RTLD_GLOBAL);
+      if (h != nullptr) break;
+    }
+    if (h == nullptr) {
+      const char* e = dlerror();
+      n.why = std::string("NCCL not found: ") + (e ? e : "dlopen failed");
+      return;
+    }
+    n.get_unique_id = reinterpret_cast<decltype(n.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    n.comm_init_rank = reinterpret_cast<decltype(n.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    n.all_reduce = reinterpret_cast<decltype(n.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
+    n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce &&
+           n.error_string;
+    if (!n.ok) n.why = "NCCL library lacks a required symbol";
+  });
+  return n;
+}
+
+bool nccl_ok(ncclResult_t r, const char* what, std::string* err)
+{
+  if (r == ncclSuccess) return true;
+  if (err) *err = std::string(what) + ": " + nccl().error_string(r);
+  return false;
+}
+
+}  // namespace
+
+bool Comm::unique_id(void* out, std::string* err)
+{
+  const Nccl& n = nccl();
+  if (!n.ok) {
+    if (err) *err = n.why;
+    return false;
+  }
+  ncclUniqueId id;
+  if (!nccl_ok(n.get_unique_id(&id), "ncclGetUniqueId", err)) return false;
+  static_assert(sizeof(id) == kIdBytes, "unique id size");
+  memcpy(out, &id, sizeof(id));
+  return true;
+}
+
+Comm::~Comm()
+{
+  if (_comm != nullptr && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(_comm));
+}
+
+bool Comm::init(int device, int rank, int world, const void* id, std::string* err)
+{
+  const Nccl& n = nccl();
+  if (!n.ok) {
+    if (err) *err = n.why;
+    return false;
+  }
+  if (world < 1 || rank < 0 || rank >= world) {
+    if (err) *err = "tp: rank outside [0, world)";
+    return false;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    if (err) *err = "tp: cudaSetDevice failed";
+    return false;
+  }
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclComm_t c = nullptr;
+  if (!nccl_ok(n.comm_init_rank(&c, world, uid, rank), "ncclCommInitRank", err)) return false;
+  _comm = c;
+  _rank = rank;
+  _world = world;
+  return true;
+}
+
+bool Comm::allreduce_sum(void* buf, size_t count, int dtype, cudaStream_t s,
+                         std::string* err) const
+{
+  if (_comm == nullptr || count == 0) return true;
+  const ncclDataType_t t = dtype == 0 ? ncclFloat32 : ncclBfloat16;
+  return nccl_ok(nccl().all_reduce(buf, buf, count, t, ncclSum,
+                                   static_cast<ncclComm_t>(_comm), s),
+                 "ncclAllReduce", err);
+}
+
+}  // namespace ltx25

@@ -1,0 +1,38 @@
+// ltx25-comm.h -- the tensor-parallel communicator: one NCCL communicator per
+// context, reached through dlopen so the library has no link-time NCCL
+// dependency (a process that already loaded NCCL, e.g. through PyTorch, shares
+// that copy).  The reference has no counterpart: it runs on one Apple GPU.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <string>
+
+namespace ltx25 {
+
+class Comm {
+public:
+  static constexpr int kIdBytes = 128;   // NCCL_UNIQUE_ID_BYTES
+
+  // A fresh rendezvous id (rank 0 makes it; the caller ships it to the
+  // other ranks by any channel).
+  static bool unique_id(void* out, std::string* err);
+
+  ~Comm();
+  // Join the group: every rank calls this with the same id and world.
+  bool init(int device, int rank, int world, const void* id, std::string* err);
+
+  // In-place sum over the group on `s`.  dtype: 0 = f32, 1 = bf16.
+  bool allreduce_sum(void* buf, size_t count, int dtype, cudaStream_t s,
+                     std::string* err) const;
+
+  int rank() const { return _rank; }
+  int world() const { return _world; }
+
+private:
+  void* _comm = nullptr;
+  int _rank = 0, _world = 1;
+};
+
+}  // namespace ltx25

@@ -11,7 +11,10 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
 #include <string>
+
+#include "ltx25-comm.h"
 
 namespace ltx25 {
 
@@ -80,6 +83,11 @@ public:
   int num_sms() const { return _sms; }
   int* err_word() const { return _err_word; }
 
+  // Tensor parallelism: blocks finalized after this shard their weights
+  // over the group (rank, world); null comm = one GPU.
+  void set_comm(std::unique_ptr<Comm> c) { _comm = std::move(c); }
+  const Comm* comm() const { return _comm.get(); }
+
   // Diagnostics: every following GEMM writes per-CTA phase timestamps into
   // `buf` (16 u64 per CTA, first `ctas` CTAs); null turns it off.
   void set_trace(unsigned long long* buf, int ctas)
@@ -114,6 +122,7 @@ private:
   __nv_bfloat16* _deq = nullptr;
   size_t _deq_bytes = 0;
   int* _err_word = nullptr;
+  std::unique_ptr<Comm> _comm;
   unsigned long long* _trace = nullptr;
   int _trace_ctas = 0;
 };

@@ -19,6 +19,7 @@ ERRORS = {
     -8: "LTX_E_ALIGN", -9: "LTX_E_ABORTED",
 }
 SB_F16, SB_BF16, SB_F32 = 0, 1, 2
+TP_ID_BYTES = 128
 ROUTE_FUSED, ROUTE_DEQUANT_ONCE = 0, 1
 EPI_STORE, EPI_GELU, EPI_GATED_RES = 0, 1, 2
 
@@ -45,6 +46,10 @@ SIGNATURES = {
     "ltx_qlinear_ex": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P,
                             _P]),
     "ltx_qlinear_i8_static": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "ltx_launch_count": (ctypes.c_ulonglong, []),
+    "ltx_tp_unique_id": (_I, [_P, _I]),
+    "ltx_ctx_set_tp": (_I, [_P, _I, _I, _P]),
+    "ltx_tp_allreduce": (_I, [_P, _P, ctypes.c_size_t, _I, _P]),
     "ltx_set_route": (_I, [_P, _I]),
     "ltx_set_tiers": (_I, [_P, _I, _I, _I]),
     "ltx_i8_takes": (_I, [_P, _I, _I, _I]),
@@ -176,6 +181,22 @@ class Context:
     def set_tiers(self, i8_gemm=False, sage_attn=False, sage_dense_layers=0):
         self._ok(self.lib.ltx_set_tiers(self.h, int(i8_gemm), int(sage_attn),
                                         sage_dense_layers), "set_tiers")
+
+    def set_tp(self, rank, world, uid=None):
+        """Join a tensor-parallel group (uid: the bytes of tp_unique_id() made
+        on rank 0; ignored when world == 1)."""
+        buf = None
+        if world > 1:
+            buf = ctypes.create_string_buffer(bytes(uid), TP_ID_BYTES)
+        self._ok(self.lib.ltx_ctx_set_tp(self.h, rank, world, buf), "set_tp")
+        self.tp = (rank, world)
+
+    def allreduce(self, t, stream=None):
+        """In-place sum of a contiguous f32 or bf16 device tensor over the group."""
+        import torch
+        dtype = {torch.float32: 0, torch.bfloat16: 1}[t.dtype]
+        self._ok(self.lib.ltx_tp_allreduce(self.h, _ptr(t), t.numel(), dtype,
+                                           _stream(stream)), "tp_allreduce")
 
     def i8_takes(self, M, K, N):
         return bool(self.lib.ltx_i8_takes(self.h, M, K, N))
@@ -449,6 +470,20 @@ class Block:
             self.close()
         except Exception:
             pass
+
+
+def launch_count():
+    """Kernels the library has launched in this process so far."""
+    return int(load().ltx_launch_count())
+
+
+def tp_unique_id():
+    """A fresh tensor-parallel rendezvous id (bytes), made on rank 0."""
+    buf = ctypes.create_string_buffer(TP_ID_BYTES)
+    rc = load().ltx_tp_unique_id(buf, TP_ID_BYTES)
+    if rc != LTX_OK:
+        raise LtxError(rc, "tp_unique_id: NCCL unavailable")
+    return buf.raw
 
 
 PROGRESS_FN = ctypes.CFUNCTYPE(_I, _I, _I, _P)
