@@ -1,5 +1,5 @@
 // ptx.cuh -- sm_100a primitives used by the ltx25 kernels: mbarriers with
-// bounded waits, TMA tile loads (no multicast anywhere), tcgen05 TMEM
+// bounded waits, TMA tile loads (each CTA fetches its own tiles), tcgen05 TMEM
 // allocation / MMA / load / store, and the UMMA descriptors.
 //
 // Every wait here gives up after a wall-clock bound (kWaitNs) and reports
