@@ -57,4 +57,15 @@ int launch_attention(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
                      int ldg, int tq, int tk, int heads, int head_dim,
                      cudaStream_t s);
 
+// tcgen05 flash attention for head_dim 128 (attention_tc.cu): the same
+// contract as launch_attention plus a V^T scratch of
+// attention_tc_scratch(tk, heads, head_dim) elements and the context's error
+// word for bounded waits.  q, k, v, o 16-byte aligned, strides % 8 == 0.
+size_t attention_tc_scratch(int tk, int heads, int head_dim);
+int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k, int ldk,
+                        const __nv_bfloat16* v, int ldv, __nv_bfloat16* vt,
+                        size_t vt_elems, __nv_bfloat16* o, int ldo,
+                        const __nv_bfloat16* gate, int ldg, int tq, int tk, int heads,
+                        int head_dim, int* err, cudaStream_t s);
+
 }  // namespace ltx

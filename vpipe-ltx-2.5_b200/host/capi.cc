@@ -346,13 +346,14 @@ int ltx_attention(ltx_ctx* ctx, const void* q, int ldq, const void* k, int ldk,
   if (ctx == nullptr) return LTX_E_NULL;
   if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
     return fail(ctx, LTX_E_NULL, "attention: null");
-  const int rc = ltx::launch_attention(
-      static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k),
-      ldk, static_cast<const __nv_bfloat16*>(v), ldv, static_cast<__nv_bfloat16*>(o),
-      ldo, static_cast<const __nv_bfloat16*>(gate_logits), ldg, tq, tk, heads,
-      head_dim, S(stream));
-  if (rc == -2) return fail(ctx, LTX_E_SHAPE, "attention: head_dim must be 64 or 128, strides % 8");
-  if (rc != 0) return fail(ctx, LTX_E_CUDA, "attention launch failed");
+  std::string e;
+  if (!ctx->ops.attention(S(stream), static_cast<const __nv_bfloat16*>(q), ldq,
+                          static_cast<const __nv_bfloat16*>(k), ldk,
+                          static_cast<const __nv_bfloat16*>(v), ldv,
+                          static_cast<__nv_bfloat16*>(o), ldo,
+                          static_cast<const __nv_bfloat16*>(gate_logits), ldg, tq, tk,
+                          heads, head_dim, &e))
+    return fail(ctx, code_for(e), e);
   return LTX_OK;
 }
 

@@ -427,6 +427,10 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   _arp->video = std::max(_arp->video, vt);
   _arp->audio = std::max(_arp->audio, at);
   _arp->text = std::max(_arp->text, tt);
+  // The attention's V^T scratch for the widest head_dim-128 stream.
+  if (!_ops->reserve_attention((int)mx({vt, at, tt}),
+                               std::max(_video.attn1.inner, _audio.attn1.inner), err))
+    return false;
   // The GEMMs' own scratch (int8 tier) follows the largest projection.
   return _ops->reserve((int)mx({vt, at, tt}), (int)mx({3 * vd, (size_t)_video.ff_hidden}),
                        (int)mx({vd, (size_t)_video.ff_hidden}), err);
@@ -487,9 +491,9 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
       return false;
     glog = _arp->glog;
   }
-  if (ltx::launch_attention(_arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog,
-                            a.heads, tq, tkv, a.heads, a.head_dim, s) != 0)
-    return fail(err, "attention launch failed");
+  if (!_ops->attention(s, _arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog, a.heads, tq,
+                       tkv, a.heads, a.head_dim, err))
+    return false;
   return true;
 }
 

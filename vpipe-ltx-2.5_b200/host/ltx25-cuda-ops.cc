@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include "../csrc/block_ops.h"
 #include "../csrc/kernels.h"
 
 namespace ltx25 {
@@ -83,6 +84,7 @@ CudaOps::~CudaOps()
   cudaFree(_xq);
   cudaFree(_sx);
   cudaFree(_deq);
+  cudaFree(_vt);
   cudaFree(_err_word);
   cudaSetDevice(prev);
 }
@@ -317,6 +319,49 @@ bool CudaOps::linear_i8_scratch(cudaStream_t s, const __nv_bfloat16* x,
   }
   return gemm_(s, ltx::MODE_I8, xq, K, w.wq, nullptr, bias, y, N, M, K, N,
                ltx::EPI_STORE, nullptr, sx, w.sw, err);
+}
+
+bool CudaOps::reserve_attention(int keys, int width, std::string* err)
+{
+  const size_t need = ltx::attention_tc_scratch(keys, 1, width);
+  if (need <= _vt_elems) return true;
+  cudaFree(_vt);
+  _vt = nullptr;
+  _vt_elems = 0;
+  if (!cuda_ok(cudaMalloc(&_vt, need * sizeof(__nv_bfloat16)), "cudaMalloc(attention scratch)", err))
+    return false;
+  _vt_elems = need;
+  return true;
+}
+
+bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
+                        const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v,
+                        int ldv, __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate,
+                        int ldg, int tq, int tk, int heads, int head_dim,
+                        std::string* err)
+{
+  if (_attn_mode < 0) {
+    const char* e = getenv("LTX25_ATTN");
+    _attn_mode = (e != nullptr && strcmp(e, "mma") == 0) ? 0 : 1;
+  }
+  int rc;
+  if (head_dim == 128 && _attn_mode == 1) {
+    if (!reserve_attention(tk, heads * head_dim, err)) return false;
+    rc = ltx::launch_attention_tc(q, ldq, k, ldk, v, ldv, _vt, _vt_elems, o, ldo, gate, ldg,
+                                  tq, tk, heads, head_dim, _err_word, s);
+  } else {
+    rc = ltx::launch_attention(q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, heads,
+                               head_dim, s);
+  }
+  if (rc == -2) {
+    if (err) *err = "attention shape: head_dim must be 64 or 128, strides % 8, 16-byte aligned";
+    return false;
+  }
+  if (rc != 0) {
+    if (err) *err = "attention launch failed";
+    return false;
+  }
+  return true;
 }
 
 int CudaOps::check(cudaStream_t s, std::string* err) const

@@ -99,6 +99,15 @@ public:
   // Reads and clears the device error word.  0 when clean.
   int check(cudaStream_t s, std::string* err) const;
 
+  // Softmax attention (ltx_attention): head_dim 128 runs the tcgen05 flash
+  // kernel (with its V^T scratch), head_dim 64 the warp-MMA kernel.
+  bool attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
+                 const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v, int ldv,
+                 __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg,
+                 int tq, int tk, int heads, int head_dim, std::string* err);
+  // Pre-size the attention scratch for up to `keys` keys x `width` columns.
+  bool reserve_attention(int keys, int width, std::string* err);
+
 private:
   bool ensure_(size_t i8_bytes, size_t deq_bytes, std::string* err);
   bool gemm_(cudaStream_t s, int mode, const void* x, int ldx,
@@ -121,6 +130,9 @@ private:
   size_t _xq_bytes = 0;
   __nv_bfloat16* _deq = nullptr;
   size_t _deq_bytes = 0;
+  __nv_bfloat16* _vt = nullptr;    // attention: V^T
+  size_t _vt_elems = 0;
+  int _attn_mode = -1;             // LTX25_ATTN: 0 = always warp-MMA
   int* _err_word = nullptr;
   std::unique_ptr<Comm> _comm;
   unsigned long long* _trace = nullptr;

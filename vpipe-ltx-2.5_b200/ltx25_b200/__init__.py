@@ -340,12 +340,12 @@ def qk_norm_rope(ctx, x, heads, head_dim, gain=None, cos=None, sin=None,
 
 
 def attention(ctx, q, k, v, heads, head_dim, gate=None, tq=None, tk=None,
-              stream=None):
+              stream=None, out=None):
     import torch
     tq = q.shape[0] if tq is None else tq
     tk = k.shape[0] if tk is None else tk
-    o = torch.empty((tq, heads * head_dim), dtype=torch.bfloat16,
-                    device=q.device)
+    o = out if out is not None else torch.empty((tq, heads * head_dim), dtype=torch.bfloat16,
+                                                device=q.device)
     ctx._ok(ctx.lib.ltx_attention(
         ctx.h, _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v),
         v.stride(0), _ptr(o), o.stride(0), _ptr(gate),
