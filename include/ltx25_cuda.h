@@ -176,6 +176,12 @@ LTX_API int ltx_set_tiers(ltx_ctx* ctx, int i8_gemm, int sage_attn,
  * Replaces MetalOps::i8_takes (src/ltx25-metal-ops.cc:761-768). */
 LTX_API int ltx_i8_takes(const ltx_ctx* ctx, int M, int K, int N);
 
+/* Whether the sage tier takes an attention of this head width
+ * (MetalOps::sage_takes, src/ltx25-metal-ops.cc:897-905): 64 and 128, while
+ * the tier is on.  The standalone ltx_attention takes it whenever this says
+ * yes; a block's attentions only from layer sage_dense_layers on. */
+LTX_API int ltx_sage_takes(const ltx_ctx* ctx, int head_dim);
+
 /* ---- pieces exposed for parity tests -----------------------------------
  * The dequantized weight exactly as the GEMMs see it: out[N][K] bf16 =
  * s*q + z rounded once (the M5 dequant-once expansion,
@@ -298,6 +304,12 @@ LTX_API int ltx_block_finalize(ltx_block* b);
 /* Size the block's scratch arena once (MetalBlock::reserve). */
 LTX_API int ltx_block_reserve(ltx_block* b, int max_video_tokens,
                               int max_audio_tokens, int max_text_tokens);
+
+/* The block's index in its model (MetalBlock::forward's layer,
+ * src/ltx25-block-metal.h:307-311): with the sage tier on, blocks below
+ * sage_dense_layers keep dense attention.  Default 0; ltx_stack_add_block
+ * sets it to the block's position. */
+LTX_API int ltx_block_set_layer(ltx_block* b, int layer);
 
 /* Run the block on `stream`; video->x and audio->x are updated in place
  * (MetalBlock::forward, src/ltx25-block-metal.h:307-311). */

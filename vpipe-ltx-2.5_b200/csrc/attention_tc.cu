@@ -46,12 +46,15 @@ enum : int {
   FERR_DRAIN = 0x64,
 };
 
-template <int D>
+template <int D, bool I8>
 struct FaCfg {
   static constexpr int kAtom = 128 * 128;             // 128 rows x 128 B
-  static constexpr int kQBytes = kFaBQ * D * 2;       // D/64 atoms
-  static constexpr int kKBytes = kFaBK * D * 2;       // D/64 atoms
-  static constexpr int kVAtom = D * 128;              // D rows x 64 keys
+  // Q and K tiles: bf16 [128][D] in D/64 atoms, or int8 [128][128 B] (D
+  // padded to 128 bytes) in one atom.
+  static constexpr int kQKAtoms = I8 ? 1 : D / 64;
+  static constexpr int kQBytes = kQKAtoms * kAtom;
+  static constexpr int kKBytes = kQKAtoms * kAtom;
+  static constexpr int kVAtom = D * 128;              // V^T: D rows x 64 keys
   static constexpr int kVBytes = 2 * kVAtom;          // 128 keys
   static constexpr int kStageBytes = kKBytes + kVBytes;
   static constexpr int kBarBytes = 256;
@@ -68,6 +71,11 @@ struct FaParams {
   int tq, tk, ntiles;
   float scale_log2;
   int* err;
+  // int8 QK (sage): per-block scales sq[head][query block], sk[head][key
+  // block]; the int8 tiles are head-major with tq_pad / tk_pad rows a head.
+  const float* sq;
+  const float* sk;
+  int nqb, tq_pad, tk_pad;
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -83,15 +91,15 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int D>
+template <int D, bool I8>
 __global__ void __launch_bounds__(kFaThreads, 1)
     fa_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                  const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_vt, FaParams p)
 {
-  using C = FaCfg<D>;
+  using C = FaCfg<D, I8>;
   constexpr int S = kFaStages;
-  constexpr int kQAtoms = D / 64;
+  constexpr int kQAtoms = C::kQKAtoms;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -150,8 +158,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (lane == 0) {
       uint32_t armed = 0, armed_par = 0;
       mbar_arrive_expect_tx(q_full, C::kQBytes);
-      for (int a = 0; a < kQAtoms; ++a)
-        tma_load_2d(&tm_q, q_full, s_q + a * C::kAtom, h * D + a * 64, q0);
+      for (int a = 0; a < kQAtoms; ++a) {
+        if constexpr (I8)
+          tma_load_2d(&tm_q, q_full, s_q, 0, h * p.tq_pad + q0);
+        else
+          tma_load_2d(&tm_q, q_full, s_q + a * C::kAtom, h * D + a * 64, q0);
+      }
       for (int j = 0; j < n; ++j) {
         const int st = j % S;
         const uint32_t ph = (uint32_t)(j / S) & 1u;
@@ -159,8 +171,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         uint8_t* sk = s_kv + st * C::kStageBytes;
         uint8_t* sv = sk + C::kKBytes;
         mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
-        for (int a = 0; a < kQAtoms; ++a)
-          tma_load_2d(&tm_k, &k_full[st], sk + a * C::kAtom, h * D + a * 64, j * kFaBK);
+        for (int a = 0; a < kQAtoms; ++a) {
+          if constexpr (I8)
+            tma_load_2d(&tm_k, &k_full[st], sk, 0, h * p.tk_pad + j * kFaBK);
+          else
+            tma_load_2d(&tm_k, &k_full[st], sk + a * C::kAtom, h * D + a * 64, j * kFaBK);
+        }
         mbar_arrive_expect_tx(&v_full[st], C::kVBytes);
         for (int a = 0; a < 2; ++a)
           tma_load_2d(&tm_vt, &v_full[st], sv + a * C::kVAtom, j * kFaBK + a * 64, h * D);
@@ -180,7 +196,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16(kFaBQ, kFaBK);
+      constexpr uint32_t idesc_s = I8 ? idesc_s8(kFaBQ, kFaBK) : idesc_bf16(kFaBQ, kFaBK);
       constexpr uint32_t idesc_o = idesc_bf16(kFaBQ, D);
       bool ok = mbar_wait(q_full, 0, s_abort, p.err, FERR_MMA);
       for (int j = 0; ok && j <= n; ++j) {
@@ -190,12 +206,21 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           tc_fence_after();
           const uint32_t sk = smem_u32(s_kv + st * C::kStageBytes);
           const uint32_t d = tmem + C::kSCol + (uint32_t)(j & 1) * kFaBK;
+          if constexpr (I8) {
+            // int8 rows of 128 B: K = 32 per instruction, D/32 of them.
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (uint32_t)((kk >> 2) * C::kAtom);
-            umma_f16_ss(d, sdesc_k128_sw128(smem_u32(s_q) + off) + (uint64_t)(2 * (kk & 3)),
-                        sdesc_k128_sw128(sk + off) + (uint64_t)(2 * (kk & 3)), idesc_s,
-                        kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 32; ++kk)
+              umma_i8_ss(d, sdesc_k128_sw128(smem_u32(s_q)) + (uint64_t)(2 * kk),
+                         sdesc_k128_sw128(sk) + (uint64_t)(2 * kk), idesc_s,
+                         kk > 0 ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (uint32_t)((kk >> 2) * C::kAtom);
+              umma_f16_ss(d, sdesc_k128_sw128(smem_u32(s_q) + off) + (uint64_t)(2 * (kk & 3)),
+                          sdesc_k128_sw128(sk + off) + (uint64_t)(2 * (kk & 3)), idesc_s,
+                          kk > 0 ? 1u : 0u);
+            }
           }
           umma_commit(&s_full[j & 1]);
         }
@@ -228,7 +253,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + (int)lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const float c = p.scale_log2;
+    const float c0 = p.scale_log2 * (I8 ? p.sq[h * p.nqb + blockIdx.x] : 1.0f);
     float m_run = 0.0f, l_run = 0.0f;
     bool ok = true;
     for (int i = 0; i < n; ++i) {
@@ -245,9 +270,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         uint32_t v[32];
         tmem_ld32(scol + (uint32_t)(c4 * 32), v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s[c4 * 32 + e] = __uint_as_float(v[e]);
+        for (int e = 0; e < 32; ++e)
+          s[c4 * 32 + e] = I8 ? (float)(int)v[e] : __uint_as_float(v[e]);
       }
       tmem_wait_ld();
+      // exp2-domain factor of this tile's raw scores (the int8 path folds
+      // in the key block's scale; the scales are positive)
+      const float c = I8 ? c0 * p.sk[h * p.ntiles + i] : c0;
       const int valid = p.tk - i * kFaBK;
       float mx = -3.0e38f;
 #pragma unroll
@@ -367,10 +396,98 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// mean[c] = (1/tk) sum_t k[t][c] for c < cols: the per-channel key mean the
+// sage tier subtracts (each thread one column pair, a CTA 64 token slices).
+__global__ void __launch_bounds__(256)
+    col_mean_kernel(const __nv_bfloat16* __restrict__ k, int ldk, int tk, int cols,
+                    float* __restrict__ mean)
+{
+  __shared__ float part[8][64];
+  const int c = blockIdx.x * 64 + (threadIdx.x & 63);
+  const int slice = threadIdx.x >> 6;           // 4 token slices
+  float acc = 0.0f;
+  if (c < cols)
+    for (int t = slice; t < tk; t += 4) acc += __bfloat162float(k[(size_t)t * ldk + c]);
+  part[slice][threadIdx.x & 63] = acc;
+  __syncthreads();
+  if (slice == 0 && c < cols)
+    mean[c] = (part[0][threadIdx.x] + part[1][threadIdx.x] + part[2][threadIdx.x] +
+               part[3][threadIdx.x]) / (float)tk;
+}
+
+// One 128-token block of one head to int8 with one scale: x (minus the
+// channel mean, when given) / (absmax / 127), rounded to nearest even,
+// into rows of 128 bytes (D <= 128; the rest of the row and the rows past
+// `tokens` are zero).  out: [head][tpad][128], scale: [head][tpad / 128].
+// Thread pair (2r, 2r+1) owns row r, 64 bytes each.
+template <int D>
+__global__ void __launch_bounds__(256)
+    quant_block_i8_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int tokens,
+                          const float* __restrict__ mean, int8_t* __restrict__ out,
+                          float* __restrict__ scale, int tpad)
+{
+  __shared__ float red[8];
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int nb = tpad / 128;
+  const int r = threadIdx.x >> 1;
+  const int c0 = (threadIdx.x & 1) * 64;
+  const int t = b * 128 + r;
+  float v[64];
+  float amax = 0.0f;
+#pragma unroll
+  for (int e8 = 0; e8 < 8; ++e8) {
+    const int c = c0 + e8 * 8;
+    if (c < D && t < tokens) {
+      const uint4 w = *reinterpret_cast<const uint4*>(x + (size_t)t * ldx + h * D + c);
+      const __nv_bfloat162* hw = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(hw[i]);
+        v[e8 * 8 + 2 * i] = f.x;
+        v[e8 * 8 + 2 * i + 1] = f.y;
+      }
+      if (mean != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[e8 * 8 + i] -= mean[h * D + c + i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[e8 * 8 + i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[e8 * 8 + i]));
+  }
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w]);
+  const float sc = m > 0.0f ? m / 127.0f : 1.0f;
+  if (threadIdx.x == 0) scale[h * nb + b] = sc;
+  uint32_t words[16];
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int q = __float2int_rn(__fdiv_rn(v[4 * w + e], sc));
+      q = q > 127 ? 127 : (q < -127 ? -127 : q);
+      word |= (uint32_t)(q & 0xff) << (8 * e);
+    }
+    words[w] = word;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)h * tpad + (size_t)t) * 128 + c0);
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+    dst[w] = make_uint4(words[4 * w], words[4 * w + 1], words[4 * w + 2], words[4 * w + 3]);
+}
+
 PFN_encodeTiled g_fa_encode = nullptr;
 
 bool fa_encode(CUtensorMap* map, const void* gaddr, uint64_t inner, uint64_t outer,
-               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer)
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)
 {
   if (g_fa_encode == nullptr) {
     void* fn = nullptr;
@@ -385,11 +502,59 @@ bool fa_encode(CUtensorMap* map, const void* gaddr, uint64_t inner, uint64_t out
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  return g_fa_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(gaddr), dims,
+  return g_fa_encode(map, dt, 2, const_cast<void*>(gaddr), dims,
                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+
+template <int D, bool I8>
+int launch_fa(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtensorMap& tv_map,
+              const FaParams& prm, int heads, cudaStream_t s)
+{
+  using C = FaCfg<D, I8>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(fa_tc_kernel<D, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmem) != cudaSuccess)
+      return -1;
+    attr = true;
+  }
+  fa_tc_kernel<D, I8><<<dim3((prm.tq + kFaBQ - 1) / kFaBQ, heads), kFaThreads, C::kSmem, s>>>(
+      tq_map, tk_map, tv_map, prm);
+  return launched();
+}
+
+FaParams fa_params(__nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg, int tq,
+                   int tk, int D, int* err)
+{
+  FaParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.o = o;
+  prm.gate = gate;
+  prm.ldo = ldo;
+  prm.ldg = ldg;
+  prm.tq = tq;
+  prm.tk = tk;
+  prm.ntiles = (tk + kFaBK - 1) / kFaBK;
+  prm.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+  prm.err = err;
+  return prm;
+}
+
+// V^T into the scratch and its tensor map.
+int prepare_vt(const __nv_bfloat16* v, int ldv, int tk, int cols, int D, __nv_bfloat16* vt,
+               CUtensorMap* map, cudaStream_t s)
+{
+  const int ldvt = (tk + 7) / 8 * 8;
+  transpose_kernel<<<dim3((tk + 63) / 64, (cols + 63) / 64), 256, 0, s>>>(v, ldv, tk, cols, vt,
+                                                                         ldvt);
+  if (launched() != 0) return -1;
+  return fa_encode(map, vt, (uint64_t)tk, (uint64_t)cols, (uint64_t)ldvt * 2, 64, D) ? 0 : -1;
+}
+
+bool aligned16(const void* a) { return (reinterpret_cast<uintptr_t>(a) & 15u) == 0; }
 
 }  // namespace
 
@@ -407,43 +572,83 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
 {
   if (tq <= 0 || tk <= 0 || heads <= 0) return 0;
   if (head_dim != 128) return -2;
-  if ((ldq | ldk | ldv) % 8 != 0 || ldo % 8 != 0 ||
-      (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) % 16 != 0)
+  if ((ldq | ldk | ldv) % 8 != 0 || ldo % 8 != 0 || !aligned16(q) || !aligned16(k) ||
+      !aligned16(v) || !aligned16(o))
     return -2;
   if (vt_elems < attention_tc_scratch(tk, heads, head_dim)) return -3;
   constexpr int D = 128;
-  using C = FaCfg<D>;
   const int cols = heads * D;
-  const int ldvt = (tk + 7) / 8 * 8;
-  transpose_kernel<<<dim3((tk + 63) / 64, (cols + 63) / 64), 256, 0, s>>>(v, ldv, tk, cols, vt,
-                                                                         ldvt);
+  CUtensorMap tq_map, tk_map, tv_map;
+  if (prepare_vt(v, ldv, tk, cols, D, vt, &tv_map, s) != 0) return -1;
+  if (!fa_encode(&tq_map, q, (uint64_t)cols, (uint64_t)tq, (uint64_t)ldq * 2, 64, kFaBQ) ||
+      !fa_encode(&tk_map, k, (uint64_t)cols, (uint64_t)tk, (uint64_t)ldk * 2, 64, kFaBK))
+    return -1;
+  return launch_fa<D, false>(tq_map, tk_map, tv_map, fa_params(o, ldo, gate, ldg, tq, tk, D, err),
+                             heads, s);
+}
+
+SageScratch sage_scratch_need(int tq, int tk, int heads, int head_dim)
+{
+  SageScratch n;
+  const size_t tqp = ((size_t)tq + 127) / 128 * 128, tkp = ((size_t)tk + 127) / 128 * 128;
+  n.qi8 = (size_t)heads * tqp * 128;
+  n.ki8 = (size_t)heads * tkp * 128;
+  n.scales = (size_t)heads * (tqp + tkp) / 128;
+  n.mean = (size_t)heads * head_dim;
+  n.vt = attention_tc_scratch(tk, heads, head_dim);
+  return n;
+}
+
+int launch_sage_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k, int ldk,
+                   const __nv_bfloat16* v, int ldv, const SageBuffers& sb,
+                   __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg, int tq,
+                   int tk, int heads, int head_dim, int* err, cudaStream_t s)
+{
+  if (tq <= 0 || tk <= 0 || heads <= 0) return 0;
+  if (head_dim != 128 && head_dim != 64) return -2;
+  if ((ldq | ldk | ldv) % 8 != 0 || ldo % 8 != 0 || !aligned16(v) || !aligned16(o))
+    return -2;
+  const SageScratch need = sage_scratch_need(tq, tk, heads, head_dim);
+  if (sb.cap.qi8 < need.qi8 || sb.cap.ki8 < need.ki8 || sb.cap.scales < need.scales ||
+      sb.cap.mean < need.mean || sb.cap.vt < need.vt)
+    return -3;
+  const int D = head_dim;
+  const int cols = heads * D;
+  const int tqp = (tq + 127) / 128 * 128, tkp = (tk + 127) / 128 * 128;
+  float* sq = sb.scales;
+  float* sk = sb.scales + (size_t)heads * (tqp / 128);
+  // K - mean(K) over tokens (exact under softmax), then per-block int8.
+  col_mean_kernel<<<(cols + 63) / 64, 256, 0, s>>>(k, ldk, tk, cols, sb.mean);
+  if (launched() != 0) return -1;
+  if (D == 128) {
+    quant_block_i8_kernel<128><<<dim3(tqp / 128, heads), 256, 0, s>>>(q, ldq, tq, nullptr,
+                                                                     sb.qi8, sq, tqp);
+    if (launched() != 0) return -1;
+    quant_block_i8_kernel<128><<<dim3(tkp / 128, heads), 256, 0, s>>>(k, ldk, tk, sb.mean,
+                                                                     sb.ki8, sk, tkp);
+  } else {
+    quant_block_i8_kernel<64><<<dim3(tqp / 128, heads), 256, 0, s>>>(q, ldq, tq, nullptr,
+                                                                    sb.qi8, sq, tqp);
+    if (launched() != 0) return -1;
+    quant_block_i8_kernel<64><<<dim3(tkp / 128, heads), 256, 0, s>>>(k, ldk, tk, sb.mean,
+                                                                    sb.ki8, sk, tkp);
+  }
   if (launched() != 0) return -1;
   CUtensorMap tq_map, tk_map, tv_map;
-  if (!fa_encode(&tq_map, q, (uint64_t)cols, (uint64_t)tq, (uint64_t)ldq * 2, 64, kFaBQ) ||
-      !fa_encode(&tk_map, k, (uint64_t)cols, (uint64_t)tk, (uint64_t)ldk * 2, 64, kFaBK) ||
-      !fa_encode(&tv_map, vt, (uint64_t)tk, (uint64_t)cols, (uint64_t)ldvt * 2, 64, D))
+  if (prepare_vt(v, ldv, tk, cols, D, sb.vt, &tv_map, s) != 0) return -1;
+  if (!fa_encode(&tq_map, sb.qi8, 128, (uint64_t)heads * tqp, 128, 128, kFaBQ,
+                 CU_TENSOR_MAP_DATA_TYPE_UINT8) ||
+      !fa_encode(&tk_map, sb.ki8, 128, (uint64_t)heads * tkp, 128, 128, kFaBK,
+                 CU_TENSOR_MAP_DATA_TYPE_UINT8))
     return -1;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(fa_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmem) != cudaSuccess)
-      return -1;
-    attr = true;
-  }
-  FaParams prm;
-  prm.o = o;
-  prm.gate = gate;
-  prm.ldo = ldo;
-  prm.ldg = ldg;
-  prm.tq = tq;
-  prm.tk = tk;
-  prm.ntiles = (tk + kFaBK - 1) / kFaBK;
-  prm.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-  prm.err = err;
-  fa_tc_kernel<D><<<dim3((tq + kFaBQ - 1) / kFaBQ, heads), kFaThreads, C::kSmem, s>>>(
-      tq_map, tk_map, tv_map, prm);
-  return launched();
+  FaParams prm = fa_params(o, ldo, gate, ldg, tq, tk, D, err);
+  prm.sq = sq;
+  prm.sk = sk;
+  prm.nqb = tqp / 128;
+  prm.tq_pad = tqp;
+  prm.tk_pad = tkp;
+  return D == 128 ? launch_fa<128, true>(tq_map, tk_map, tv_map, prm, heads, s)
+                  : launch_fa<64, true>(tq_map, tk_map, tv_map, prm, heads, s);
 }
 
 }  // namespace ltx

@@ -68,4 +68,24 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
                         const __nv_bfloat16* gate, int ldg, int tq, int tk, int heads,
                         int head_dim, int* err, cudaStream_t s);
 
+// The sage tier (int8 QK^T, one scale per 128-token block, K smoothed by
+// its per-channel mean; P V in bf16): scratch sizes in elements and the
+// buffers, then the launch (head_dim 64 or 128).
+struct SageScratch {
+  size_t qi8 = 0, ki8 = 0, scales = 0, mean = 0, vt = 0;
+};
+struct SageBuffers {
+  int8_t* qi8 = nullptr;
+  int8_t* ki8 = nullptr;
+  float* scales = nullptr;
+  float* mean = nullptr;
+  __nv_bfloat16* vt = nullptr;
+  SageScratch cap;
+};
+SageScratch sage_scratch_need(int tq, int tk, int heads, int head_dim);
+int launch_sage_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k, int ldk,
+                   const __nv_bfloat16* v, int ldv, const SageBuffers& sb,
+                   __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg, int tq,
+                   int tk, int heads, int head_dim, int* err, cudaStream_t s);
+
 }  // namespace ltx

@@ -56,23 +56,22 @@ __device__ __forceinline__ float gelu_tanh(float x)
   return 0.5f * x * (1.0f + t);
 }
 
+// One output pair (features n, n+1 of one token): bias, then GELU or the
+// gated residual (x = x + gate * (acc + bias), `res` the two bf16 of x).
+// bias / gate are this thread's pair, loaded once per tile.
 template <int EPI>
-__device__ __forceinline__ uint32_t epi_pair(float a, float b, int n,
-                                             const GemmParams& p,
-                                             const __nv_bfloat16* yrow)
+__device__ __forceinline__ uint32_t epi_pair(float a, float b, bool has_bias,
+                                             float2 bias, float2 g, uint32_t res)
 {
-  if (p.bias != nullptr) {
-    const __nv_bfloat162 bb =
-        *reinterpret_cast<const __nv_bfloat162*>(p.bias + n);
-    a += __bfloat162float(bb.x);
-    b += __bfloat162float(bb.y);
+  if (has_bias) {
+    a += bias.x;
+    b += bias.y;
   }
   if constexpr (EPI == EPI_GELU) {
     a = gelu_tanh(a);
     b = gelu_tanh(b);
   } else if constexpr (EPI == EPI_GATED_RES) {
-    const float2 g = *reinterpret_cast<const float2*>(p.gate + n);
-    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(yrow + n);
+    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&res);
     a = fmaf(g.x, a, __bfloat162float(h.x));
     b = fmaf(g.y, b, __bfloat162float(h.y));
   }
@@ -478,6 +477,14 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
         const int nn = nrow + (int)lane;
         csx = nn < p.N ? p.sw[nn] : 0.0f;
       }
+      float2 ebias = make_float2(0.0f, 0.0f), egate = make_float2(0.0f, 0.0f);
+      if (n_pair < p.N) {
+        if (p.bias != nullptr) {
+          const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(p.bias + n_pair);
+          ebias = make_float2(__bfloat162float(bb.x), __bfloat162float(bb.y));
+        }
+        if constexpr (EPI == EPI_GATED_RES) egate = *reinterpret_cast<const float2*>(p.gate + n_pair);
+      }
       constexpr int kChunks = TN / 32;
       const int c_last = ((kChunks - 1 - egrp) / 2) * 2 + egrp;
 #pragma unroll 1
@@ -523,6 +530,18 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
           }
           continue;
         }
+        // The residual of this chunk's 16 sites, all loaded before any
+        // store (one memory latency per chunk, not one per token).
+        uint32_t res[16];
+        if constexpr (EPI == EPI_GATED_RES) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int j = j0 + 2 * k + odd;
+            res[k] = (j < p.M && n_pair < p.N)
+                         ? *reinterpret_cast<const uint32_t*>(p.y + (size_t)j * p.ldy + n_pair)
+                         : 0u;
+          }
+        }
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           // even lane keeps token 2k, odd lane keeps token 2k+1
@@ -537,9 +556,9 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
             b *= sj;
           }
           if (j < p.M && n_pair < p.N) {
-            __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
-            const uint32_t o = epi_pair<EPI>(a, b, n_pair, p, yrow);
-            *reinterpret_cast<uint32_t*>(yrow + n_pair) = o;
+            const uint32_t o = epi_pair<EPI>(a, b, p.bias != nullptr, ebias, egate,
+                                             EPI == EPI_GATED_RES ? res[k] : 0u);
+            *reinterpret_cast<uint32_t*>(p.y + (size_t)j * p.ldy + n_pair) = o;
           }
         }
       }
@@ -594,12 +613,22 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
         }
       }
       __nv_bfloat16* yrow = p.y + (size_t)j * p.ldy;
-      const uint32_t o0 = epi_pair<EPI>(sum.x, sum.y, n, p, yrow);
-      *reinterpret_cast<uint32_t*>(yrow + n) = o0;
-      if (n + 2 < p.N) {   // N is even but need not be a multiple of 4
-        const uint32_t o1 = epi_pair<EPI>(sum.z, sum.w, n + 2, p, yrow);
-        *reinterpret_cast<uint32_t*>(yrow + n + 2) = o1;
-      }
+      auto site = [&](float a, float b, int nn) {
+        float2 bias = make_float2(0.0f, 0.0f), g = make_float2(0.0f, 0.0f);
+        uint32_t res = 0u;
+        if (p.bias != nullptr) {
+          const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(p.bias + nn);
+          bias = make_float2(__bfloat162float(bb.x), __bfloat162float(bb.y));
+        }
+        if constexpr (EPI == EPI_GATED_RES) {
+          g = *reinterpret_cast<const float2*>(p.gate + nn);
+          res = *reinterpret_cast<const uint32_t*>(yrow + nn);
+        }
+        *reinterpret_cast<uint32_t*>(yrow + nn) =
+            epi_pair<EPI>(a, b, p.bias != nullptr, bias, g, res);
+      };
+      site(sum.x, sum.y, n);
+      if (n + 2 < p.N) site(sum.z, sum.w, n + 2);   // N is even, not always % 4
     }
     // Peers may still be reading this CTA's partial: leave together.
     cluster_sync_all();

@@ -268,6 +268,12 @@ int ltx_i8_takes(const ltx_ctx* ctx, int M, int K, int N)
   return ctx->ops.i8_takes(M, K, N) ? 1 : 0;
 }
 
+int ltx_sage_takes(const ltx_ctx* ctx, int head_dim)
+{
+  if (ctx == nullptr) return 0;
+  return ctx->ops.sage_takes(head_dim) ? 1 : 0;
+}
+
 int ltx_dequant(ltx_ctx* ctx, const ltx_qweight* w, void* out, void* stream)
 {
   if (ctx == nullptr) return LTX_E_NULL;
@@ -352,7 +358,7 @@ int ltx_attention(ltx_ctx* ctx, const void* q, int ldq, const void* k, int ldk,
                           static_cast<const __nv_bfloat16*>(v), ldv,
                           static_cast<__nv_bfloat16*>(o), ldo,
                           static_cast<const __nv_bfloat16*>(gate_logits), ldg, tq, tk,
-                          heads, head_dim, &e))
+                          heads, head_dim, &e, /*layer*/ 1 << 30))
     return fail(ctx, code_for(e), e);
   return LTX_OK;
 }
@@ -478,6 +484,14 @@ int ltx_block_reserve(ltx_block* b, int max_video_tokens, int max_audio_tokens,
   return LTX_OK;
 }
 
+int ltx_block_set_layer(ltx_block* b, int layer)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  if (layer < 0) return bfail(b, LTX_E_SHAPE, "set_layer: negative layer");
+  b->blk->set_layer(layer);
+  return LTX_OK;
+}
+
 int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
                       const ltx_stream_io* audio, void* stream)
 {
@@ -543,6 +557,7 @@ int ltx_stack_add_block(ltx_stack* s, ltx_block* b)
   if (!b->blk->finalized()) return sfail(s, LTX_E_STATE, "add_block: block not finalized");
   if (!s->blocks.empty() && !s->blocks[0]->blk->same_widths(*b->blk))
     return sfail(s, LTX_E_SHAPE, "add_block: widths differ from block 0");
+  b->blk->set_layer((int)s->blocks.size());
   s->blocks.push_back(b);
   s->reserved = false;
   return LTX_OK;

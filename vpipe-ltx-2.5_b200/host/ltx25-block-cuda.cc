@@ -427,9 +427,14 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   _arp->video = std::max(_arp->video, vt);
   _arp->audio = std::max(_arp->audio, at);
   _arp->text = std::max(_arp->text, tt);
-  // The attention's V^T scratch for the widest head_dim-128 stream.
+  // The attention's V^T scratch for the widest head_dim-128 stream, and the
+  // sage tier's when it is on.
   if (!_ops->reserve_attention((int)mx({vt, at, tt}),
                                std::max(_video.attn1.inner, _audio.attn1.inner), err))
+    return false;
+  if (_ops->sage_on() &&
+      !_ops->reserve_sage((int)mx({vt, at}), (int)mx({vt, at, tt}),
+                          std::max(_video.attn1.heads, _audio.attn1.heads), 128, err))
     return false;
   // The GEMMs' own scratch (int8 tier) follows the largest projection.
   return _ops->reserve((int)mx({vt, at, tt}), (int)mx({3 * vd, (size_t)_video.ff_hidden}),
@@ -492,7 +497,7 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     glog = _arp->glog;
   }
   if (!_ops->attention(s, _arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog, a.heads, tq,
-                       tkv, a.heads, a.head_dim, err))
+                       tkv, a.heads, a.head_dim, err, _layer))
     return false;
   return true;
 }

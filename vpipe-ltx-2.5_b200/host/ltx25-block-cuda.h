@@ -126,6 +126,11 @@ public:
 
   bool finalized() const { return _final; }
   CudaOps* ops() const { return _ops; }
+  // The block's index in its stack: the sage tier leaves blocks below
+  // sage_dense_layers dense (MetalBlock::forward's layer argument,
+  // src/ltx25-block-metal.h:307-311).
+  void set_layer(int layer) { _layer = layer; }
+  int layer() const { return _layer; }
   bool same_widths(const CudaBlock& o) const
   {
     return _vdim == o._vdim && _vheads == o._vheads && _adim == o._adim &&
@@ -183,6 +188,7 @@ private:
   CudaStreamW _video, _audio;
   CudaAttn _a2v, _v2a;
   bool _final = false;
+  int _layer = 0;
 
   std::shared_ptr<BlockArena> _arp;
 };

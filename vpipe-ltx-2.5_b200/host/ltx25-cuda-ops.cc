@@ -85,6 +85,10 @@ CudaOps::~CudaOps()
   cudaFree(_sx);
   cudaFree(_deq);
   cudaFree(_vt);
+  cudaFree(_sb.qi8);
+  cudaFree(_sb.ki8);
+  cudaFree(_sb.scales);
+  cudaFree(_sb.mean);
   cudaFree(_err_word);
   cudaSetDevice(prev);
 }
@@ -334,18 +338,45 @@ bool CudaOps::reserve_attention(int keys, int width, std::string* err)
   return true;
 }
 
+bool CudaOps::reserve_sage(int tq, int tk, int heads, int head_dim, std::string* err)
+{
+  const ltx::SageScratch need = ltx::sage_scratch_need(tq, tk, heads, head_dim);
+  auto grow = [&](void** ptr, size_t* cap, size_t n, size_t elt) {
+    if (n <= *cap) return true;
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    *cap = 0;
+    if (!cuda_ok(cudaMalloc(ptr, n * elt), "cudaMalloc(sage scratch)", err)) return false;
+    *cap = n;
+    return true;
+  };
+  if (!grow((void**)&_sb.qi8, &_sb.cap.qi8, need.qi8, 1) ||
+      !grow((void**)&_sb.ki8, &_sb.cap.ki8, need.ki8, 1) ||
+      !grow((void**)&_sb.scales, &_sb.cap.scales, need.scales, sizeof(float)) ||
+      !grow((void**)&_sb.mean, &_sb.cap.mean, need.mean, sizeof(float)))
+    return false;
+  if (!reserve_attention(tk, heads * head_dim, err)) return false;
+  _sb.vt = _vt;
+  _sb.cap.vt = _vt_elems;
+  return true;
+}
+
 bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
                         const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v,
                         int ldv, __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate,
                         int ldg, int tq, int tk, int heads, int head_dim,
-                        std::string* err)
+                        std::string* err, int layer)
 {
   if (_attn_mode < 0) {
     const char* e = getenv("LTX25_ATTN");
     _attn_mode = (e != nullptr && strcmp(e, "mma") == 0) ? 0 : 1;
   }
   int rc;
-  if (head_dim == 128 && _attn_mode == 1) {
+  if (sage_for(layer, head_dim)) {
+    if (!reserve_sage(tq, tk, heads, head_dim, err)) return false;
+    rc = ltx::launch_sage_tc(q, ldq, k, ldk, v, ldv, _sb, o, ldo, gate, ldg, tq, tk, heads,
+                             head_dim, _err_word, s);
+  } else if (head_dim == 128 && _attn_mode == 1) {
     if (!reserve_attention(tk, heads * head_dim, err)) return false;
     rc = ltx::launch_attention_tc(q, ldq, k, ldk, v, ldv, _vt, _vt_elems, o, ldo, gate, ldg,
                                   tq, tk, heads, head_dim, _err_word, s);

@@ -15,6 +15,7 @@
 #include <string>
 
 #include "ltx25-comm.h"
+#include "../csrc/block_ops.h"
 
 namespace ltx25 {
 
@@ -100,11 +101,26 @@ public:
   int check(cudaStream_t s, std::string* err) const;
 
   // Softmax attention (ltx_attention): head_dim 128 runs the tcgen05 flash
-  // kernel (with its V^T scratch), head_dim 64 the warp-MMA kernel.
+  // kernel (with its V^T scratch), head_dim 64 the warp-MMA kernel.  With
+  // the sage tier on and `layer` >= sage_dense_layers, both widths take the
+  // int8-QK kernel instead (sdpa_steel's sage_layer, src/ltx25-metal-ops.cc:
+  // 1243-1289).  layer < 0: never sage.
   bool attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
                  const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v, int ldv,
                  __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg,
-                 int tq, int tk, int heads, int head_dim, std::string* err);
+                 int tq, int tk, int heads, int head_dim, std::string* err,
+                 int layer = -1);
+  // MetalOps::sage_takes (src/ltx25-metal-ops.cc:897-905): the widths the
+  // int8 twin exists for, while the tier is on.
+  bool sage_takes(int head_dim) const
+  {
+    return _sage && (head_dim == 64 || head_dim == 128);
+  }
+  bool sage_for(int layer, int head_dim) const
+  {
+    return layer >= 0 && layer >= _sage_dense && sage_takes(head_dim);
+  }
+  bool reserve_sage(int tq, int tk, int heads, int head_dim, std::string* err);
   // Pre-size the attention scratch for up to `keys` keys x `width` columns.
   bool reserve_attention(int keys, int width, std::string* err);
 
@@ -132,6 +148,7 @@ private:
   size_t _deq_bytes = 0;
   __nv_bfloat16* _vt = nullptr;    // attention: V^T
   size_t _vt_elems = 0;
+  ltx::SageBuffers _sb;            // sage tier: int8 Q/K, scales, key mean
   int _attn_mode = -1;             // LTX25_ATTN: 0 = always warp-MMA
   int* _err_word = nullptr;
   std::unique_ptr<Comm> _comm;

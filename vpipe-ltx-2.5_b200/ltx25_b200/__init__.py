@@ -53,6 +53,8 @@ SIGNATURES = {
     "ltx_set_route": (_I, [_P, _I]),
     "ltx_set_tiers": (_I, [_P, _I, _I, _I]),
     "ltx_i8_takes": (_I, [_P, _I, _I, _I]),
+    "ltx_sage_takes": (_I, [_P, _I]),
+    "ltx_block_set_layer": (_I, [_P, _I]),
     "ltx_dequant": (_I, [_P, _P, _P, _P]),
     "ltx_quant_rows_i8": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "ltx_pack_w8g64": (_I, [_P, _P, _I, _I, _P, _P, _P, _P]),
@@ -197,6 +199,9 @@ class Context:
         dtype = {torch.float32: 0, torch.bfloat16: 1}[t.dtype]
         self._ok(self.lib.ltx_tp_allreduce(self.h, _ptr(t), t.numel(), dtype,
                                            _stream(stream)), "tp_allreduce")
+
+    def sage_takes(self, head_dim):
+        return bool(self.lib.ltx_sage_takes(self.h, head_dim))
 
     def i8_takes(self, M, K, N):
         return bool(self.lib.ltx_i8_takes(self.h, M, K, N))
@@ -425,6 +430,9 @@ class Block:
     def reserve(self, max_video, max_audio, max_text):
         self._ok(self.ctx.lib.ltx_block_reserve(self.h, max_video, max_audio,
                                                 max_text), "block_reserve")
+
+    def set_layer(self, layer):
+        self._ok(self.ctx.lib.ltx_block_set_layer(self.h, layer), "block_set_layer")
 
     @staticmethod
     def make_io(s):
