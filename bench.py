@@ -384,6 +384,68 @@ def run_stack(args):
     return 0
 
 
+def run_attn(args):
+    """The video stream's self-attention (8160 x 8160 tokens, 32 heads of
+    128) alone: the tcgen05 flash kernel (or, with --sage, the int8-QK
+    tier), with q/k/v (200 MB) above L2."""
+    import torch
+    import ltx25_b200 as L
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    tq = tk = 8160
+    heads, D = 32, 128
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    q = torch.randn((tq, heads * D), generator=gen, device=dev).to(torch.bfloat16)
+    kv = torch.randn((tk, 2 * heads * D), generator=gen, device=dev).to(torch.bfloat16)
+    gate = torch.randn((tq, heads), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ctx.set_tiers(sage_attn=args.sage)
+    run = lambda: L.attention(ctx, q, kv[:, :heads * D], kv[:, heads * D:], heads, D,
+                              gate=gate, out=out)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    ctx.check()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    n0 = L.launch_count()
+    with ClockSampler(gpu_id) as clk:
+        for e0, e1 in evs:
+            e0.record()
+            run()
+            e1.record()
+        torch.cuda.synchronize()
+    launches = (L.launch_count() - n0) // max(args.steps, 1)
+    ctx.check()
+    ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in evs])
+    fl = 4.0 * tq * tk * heads * D
+    peak_tf, _, peak_kind = peaks()
+    tf = fl / (ms * 1e-3) / 1e12
+    line = {
+        "metric": "video self-attention TFLOP/s (8160x8160, 32 heads x 128)" +
+                  (" [sage int8 QK]" if args.sage else ""),
+        "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": "int8 QK / bf16 PV" if args.sage else "bf16",
+        "data": "synthetic N(0,1) q/k/v, gated",
+        "config": {"workload": "attention 8160x8160x32x128 + gate; q/k/v 200 MB > L2"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak_tf,
+                     "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(tf / peak_tf, 3),
+                     "traffic": None},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    ctx.set_tiers()
+    ctx.close()
+    return 0
+
+
 def run_block(args):
     """one joint AV block, 8160 video + 126 audio + 256
     text tokens at the real widths, synthetic w8g64 weights."""
@@ -486,12 +548,16 @@ def main():
     ap.add_argument("--only", type=int, default=None,
                     help="profile one sweep shape (index into SHAPES)")
     ap.add_argument("--blocks", type=int, default=48, help="stack depth (--workload stack)")
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "block", "stack"],
+    ap.add_argument("--sage", action="store_true", help="sage_attn tier (--workload attn)")
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "block", "stack", "attn"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
     if args.workload == "block" and args.impl == "ours":
         return run_block(args)
+    if args.workload == "attn" and args.impl == "ours":
+        args.warmup = max(args.warmup, 3)
+        return run_attn(args)
     if args.workload == "stack" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_stack(args)
