@@ -549,6 +549,8 @@ def main():
                     help="profile one sweep shape (index into SHAPES)")
     ap.add_argument("--blocks", type=int, default=48, help="stack depth (--workload stack)")
     ap.add_argument("--sage", action="store_true", help="sage_attn tier (--workload attn)")
+    ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
+                    help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="sweep", choices=["sweep", "block", "stack", "attn"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
@@ -582,6 +584,9 @@ def main():
         pg = dist
 
     ctx = L.Context(local)
+    route = {"auto": L.ROUTE_AUTO, "fused": L.ROUTE_FUSED,
+             "dequant": L.ROUTE_DEQUANT_ONCE}[args.route]
+    ctx.set_route(route)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     weights, xs, ys = [], [], []
@@ -618,12 +623,14 @@ def main():
     torch.cuda.synchronize()
     gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    n_launch0 = L.launch_count()
     with ClockSampler(gpu_id) as clk:
         t_start.record(stream)
         for s in range(args.steps):
             step(evs[s])
         t_end.record(stream)
         torch.cuda.synchronize()
+    launches = L.launch_count() - n_launch0
     if pg is not None:
         pg.barrier()
     ctx.check()
@@ -713,20 +720,25 @@ def main():
             "l2": "inputs larger than L2: the sweep's operands total ~1.5 GB "
                   "and each shape's are evicted by the others between repeats",
             "parallelism": f"replicas x{world} (no data-path collective)",
+            "route": args.route,
         },
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3),
                 "api": "ltx_qlinear via ctypes, pinned host buffers"},
-        "gpu_launches": len(SHAPES) * args.steps,
+        "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "roofline": {
             "bound": "tensor", "achieved": round(achieved, 1),
             "peak": bf16_peak, "unit": "TFLOP/s",
             "frac": round(achieved / bf16_peak, 4),
             "peak_source": f"{peak_kind} bf16_tflops (burst)",
-            "kernel": "gemm_tc_kernel<MODE_W8G64,TN=256> over the 6 M=8160 shapes",
-            "traffic": prof.get("video_bytes_per_launch"),
+            "kernel": ("dequant_w8_kernel + gemm_tc_kernel<MODE_BF16,TN=256> (route auto: "
+                       "M >= %d expands the weight once per call, src/ltx25-metal-ops.cc:"
+                       "468-545) over the 6 M=8160 shapes; time covers both" % L.DEQUANT_MIN_M)
+                      if args.route != "fused" else
+                      "gemm_tc_kernel<MODE_W8G64,TN=256> over the 6 M=8160 shapes",
+            "traffic": prof.get("video_bytes_per_launch_" + args.route),
         },
         "roofline_hbm": {
             "bound": "hbm", "achieved": round(achieved_hbm, 1),

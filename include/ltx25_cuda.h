@@ -55,7 +55,8 @@ enum { LTX_SB_F16 = 0, LTX_SB_BF16 = 1, LTX_SB_F32 = 2 };
  * VPIPE_LTX25_NO_DEQUANT_MMA A/B, src/ltx25-metal-ops.cc:532-569). */
 enum {
   LTX_ROUTE_FUSED = 0,         /* w8g64 dequant-fused tcgen05 GEMM */
-  LTX_ROUTE_DEQUANT_ONCE = 1   /* expand to bf16 scratch, dense GEMM */
+  LTX_ROUTE_DEQUANT_ONCE = 1,  /* expand to bf16 scratch, dense GEMM */
+  LTX_ROUTE_AUTO = 2           /* DEQUANT_ONCE from LTX_DEQUANT_MIN_M rows, else FUSED */
 };
 
 /* Fused epilogues of ltx_qlinear_ex. */
@@ -162,7 +163,13 @@ LTX_API int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                    int ldx, const void* bias, void* y, int ldy, int M, int K,
                    int N, int epilogue, const void* gate, void* stream);
 
-/* Route for quantized weights (LTX_ROUTE_*).  Default FUSED. */
+/* Route for quantized weights (LTX_ROUTE_*).  Default AUTO, the reference's
+ * own choice (MetalOps::linear -> dequant_mma_, src/ltx25-metal-ops.cc:
+ * 343-347, 468-545): a call tall enough to be tensor-bound expands the
+ * weight once into the context's bf16 scratch and runs the dense tcgen05
+ * GEMM; below it (audio, text) the fused kernel, which reads 1.06 bytes per
+ * weight instead of 5.  The crossover on B200 is LTX_DEQUANT_MIN_M rows. */
+#define LTX_DEQUANT_MIN_M 1536
 LTX_API int ltx_set_route(ltx_ctx* ctx, int route);
 
 /* ---- acceleration tiers ------------------------------------------------

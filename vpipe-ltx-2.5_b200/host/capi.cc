@@ -246,10 +246,11 @@ int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype, void* str
 int ltx_set_route(ltx_ctx* ctx, int route)
 {
   if (ctx == nullptr) return LTX_E_NULL;
-  if (route != LTX_ROUTE_FUSED && route != LTX_ROUTE_DEQUANT_ONCE)
+  if (route != LTX_ROUTE_FUSED && route != LTX_ROUTE_DEQUANT_ONCE && route != LTX_ROUTE_AUTO)
     return fail(ctx, LTX_E_SHAPE, "unknown route");
   ctx->ops.set_route(route == LTX_ROUTE_FUSED ? ltx25::Route::Fused
-                                              : ltx25::Route::DequantOnce);
+                     : route == LTX_ROUTE_DEQUANT_ONCE ? ltx25::Route::DequantOnce
+                                                       : ltx25::Route::Auto);
   return LTX_OK;
 }
 

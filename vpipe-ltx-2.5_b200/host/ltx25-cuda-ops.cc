@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include "../../include/ltx25_cuda.h"
 #include "../csrc/block_ops.h"
 #include "../csrc/kernels.h"
 
@@ -153,7 +154,9 @@ bool CudaOps::reserve(int max_tokens, int max_n, int max_k, std::string* err)
   // The split-K partials live in shared memory; only the int8 tier's
   // quantized activations and the dequant-once expansion need HBM scratch.
   const size_t i8 = _i8 ? (size_t)max_tokens * max_k : 0;
-  const size_t deq = _route == Route::DequantOnce ? (size_t)max_n * max_k * 2 : 0;
+  const bool expand = _route == Route::DequantOnce ||
+                      (_route == Route::Auto && max_tokens >= LTX_DEQUANT_MIN_M);
+  const size_t deq = expand ? (size_t)max_n * max_k * 2 : 0;
   return ensure_(i8, deq, err);
 }
 
@@ -276,7 +279,7 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
     return gemm_(s, ltx::MODE_I8, _xq, K, w.wq, nullptr, bias, y, ldy, M, K,
                  N, epi, gate, _sx, w.sw, err);
   }
-  if (_route == Route::DequantOnce) {
+  if (_route == Route::DequantOnce || (_route == Route::Auto && M >= LTX_DEQUANT_MIN_M)) {
     if (!ensure_(0, (size_t)N * K * 2, err)) return false;
     if (ltx::launch_dequant_w8(w.codes, w.sz, N, K, _deq, s) != 0) {
       if (err) *err = "dequant launch failed";

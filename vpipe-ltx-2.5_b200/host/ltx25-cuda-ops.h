@@ -35,7 +35,7 @@ struct QWeight {
   int device = 0;
 };
 
-enum class Route { Fused = 0, DequantOnce = 1 };
+enum class Route { Fused = 0, DequantOnce = 1, Auto = 2 };
 
 class CudaOps {
 public:
@@ -134,7 +134,7 @@ private:
 
   int _dev = -1;
   int _sms = 148;
-  Route _route = Route::Fused;
+  Route _route = Route::Auto;
   bool _i8 = false;
   bool _sage = false;
   int _sage_dense = 0;

@@ -20,7 +20,8 @@ ERRORS = {
 }
 SB_F16, SB_BF16, SB_F32 = 0, 1, 2
 TP_ID_BYTES = 128
-ROUTE_FUSED, ROUTE_DEQUANT_ONCE = 0, 1
+ROUTE_FUSED, ROUTE_DEQUANT_ONCE, ROUTE_AUTO = 0, 1, 2
+DEQUANT_MIN_M = 1536
 EPI_STORE, EPI_GELU, EPI_GATED_RES = 0, 1, 2
 
 _P = ctypes.c_void_p
