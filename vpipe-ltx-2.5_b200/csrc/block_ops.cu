@@ -72,6 +72,12 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8])
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+__device__ __forceinline__ uint32_t pack2(float lo, float hi)
+{
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __global__ void vec_add_kernel(const float* __restrict__ a,
                                const __nv_bfloat16* __restrict__ b,
                                float* __restrict__ out, int n)
@@ -83,47 +89,95 @@ __global__ void vec_add_kernel(const float* __restrict__ a,
 }
 
 // out = (rms_norm(x) if norm) * (1 + scale) + shift.  scale/shift may be
-// null (0).  dim % 8 == 0; a thread owns 8-element chunks.
-template <bool NORM>
+// null (0).  dim % 8 == 0; a thread owns 8-element chunks of ROWS rows, so
+// the f32 scale/shift vectors are read once per CTA thread (not per row)
+// and ROWS rows of loads are in flight together.  Per row the arithmetic
+// and the reduction order are those of a one-row CTA.
+template <bool NORM, int ROWS, int CH>
 __global__ void __launch_bounds__(kRowThreads)
     row_mod_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
-                   __nv_bfloat16* __restrict__ out, int ldo, int dim,
+                   __nv_bfloat16* __restrict__ out, int ldo, int rows, int dim,
                    const float* __restrict__ scale,
                    const float* __restrict__ shift, float eps)
 {
-  __shared__ float red[33];
-  const __nv_bfloat16* xr = x + (size_t)blockIdx.x * ldx;
-  __nv_bfloat16* orow = out + (size_t)blockIdx.x * ldo;
-  constexpr int kMaxChunks = 4;   // dim <= 256 * 8 * 4 = 8192
-  float v[kMaxChunks][8];
-  int nch = 0;
-  float ss = 0.0f;
+  __shared__ float red[ROWS][33];
+  const int r0 = blockIdx.x * ROWS;
+  float sc[CH][8], sh[CH][8];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < CH; ++c) {
     const int k = (c * kRowThreads + threadIdx.x) * 8;
-    if (k < dim) {
-      load8(xr + k, v[c]);
-      if (NORM) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+    for (int i = 0; i < 8; ++i) sc[c][i] = sh[c][i] = 0.0f;
+    if (k < dim) {
+      if (scale != nullptr) {
+        const float4 a = *reinterpret_cast<const float4*>(scale + k);
+        const float4 b = *reinterpret_cast<const float4*>(scale + k + 4);
+        sc[c][0] = a.x; sc[c][1] = a.y; sc[c][2] = a.z; sc[c][3] = a.w;
+        sc[c][4] = b.x; sc[c][5] = b.y; sc[c][6] = b.z; sc[c][7] = b.w;
       }
-      nch = c + 1;
+      if (shift != nullptr) {
+        const float4 a = *reinterpret_cast<const float4*>(shift + k);
+        const float4 b = *reinterpret_cast<const float4*>(shift + k + 4);
+        sh[c][0] = a.x; sh[c][1] = a.y; sh[c][2] = a.z; sh[c][3] = a.w;
+        sh[c][4] = b.x; sh[c][5] = b.y; sh[c][6] = b.z; sh[c][7] = b.w;
+      }
     }
   }
-  float inv = 1.0f;
-  if (NORM) inv = rsqrtf(block_sum(ss, red) / (float)dim + eps);
+  float v[ROWS][CH][8];
+  float ss[ROWS];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    if (c >= nch) break;
-    const int k = (c * kRowThreads + threadIdx.x) * 8;
-    float o[8];
+  for (int r = 0; r < ROWS; ++r) {
+    ss[r] = 0.0f;
+    const bool live = r0 + r < rows;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float sc = scale != nullptr ? scale[k + i] : 0.0f;
-      const float sh = shift != nullptr ? shift[k + i] : 0.0f;
-      o[i] = fmaf(v[c][i] * inv, 1.0f + sc, sh);
+    for (int c = 0; c < CH; ++c) {
+      const int k = (c * kRowThreads + threadIdx.x) * 8;
+      if (live && k < dim) {
+        load8(x + (size_t)(r0 + r) * ldx + k, v[r][c]);
+        if (NORM) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ss[r] = fmaf(v[r][c][i], v[r][c][i], ss[r]);
+        }
+      }
     }
-    store8(orow + k, o);
+  }
+  float inv[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) inv[r] = 1.0f;
+  if (NORM) {
+    // block_sum for ROWS values at once (same tree per row)
+    const int w = threadIdx.x >> 5;
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      float t = ss[r];
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if ((threadIdx.x & 31) == 0) red[r][w] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[r][threadIdx.x] : 0.0f;
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (threadIdx.x == 0) red[r][32] = t;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) inv[r] = rsqrtf(red[r][32] / (float)dim + eps);
+  }
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    if (r0 + r >= rows) break;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int k = (c * kRowThreads + threadIdx.x) * 8;
+      if (k >= dim) continue;
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = fmaf(v[r][c][i] * inv[r], 1.0f + sc[c][i], sh[c][i]);
+      store8(out + (size_t)(r0 + r) * ldo + k, o);
+    }
   }
 }
 
@@ -166,21 +220,44 @@ __global__ void __launch_bounds__(kRowThreads)
   const float inv = rsqrtf(total / (float)norm_width + eps);
   const int half = head_dim / 2;
   __nv_bfloat16* orow = out + (size_t)t * ldo;
-  for (int idx = threadIdx.x; idx < heads * half; idx += kRowThreads) {
-    const int h = idx / half, j = idx % half;
+  // Four consecutive rotation pairs (j .. j+3 of one head) per step: float4
+  // gain / cos / sin reads, 8-byte stores.  half % 4 == 0 (32 or 64).
+  const int quads = heads * half / 4;
+  for (int idx = threadIdx.x; idx < quads; idx += kRowThreads) {
+    const int h = (idx * 4) / half, j = (idx * 4) % half;
     const int ia = h * head_dim + j, ib = ia + half;
-    float a = srow[ia] * inv * (gain != nullptr ? gain[ia] : 1.0f);
-    float b = srow[ib] * inv * (gain != nullptr ? gain[ib] : 1.0f);
+    float a[4], b[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      a[e] = srow[ia + e] * inv;
+      b[e] = srow[ib + e] * inv;
+    }
+    if (gain != nullptr) {
+      const float4 ga = *reinterpret_cast<const float4*>(gain + ia);
+      const float4 gb = *reinterpret_cast<const float4*>(gain + ib);
+      a[0] *= ga.x; a[1] *= ga.y; a[2] *= ga.z; a[3] *= ga.w;
+      b[0] *= gb.x; b[1] *= gb.y; b[2] *= gb.z; b[3] *= gb.w;
+    }
     if (cosb != nullptr) {
       const size_t o = ((size_t)(head0 + h) * tokens + t) * half + j;
-      const float c = cosb[o], s = sinb[o];
-      const float ra = a * c - b * s;
-      const float rb = b * c + a * s;
-      a = ra;
-      b = rb;
+      const float4 c4 = *reinterpret_cast<const float4*>(cosb + o);
+      const float4 s4 = *reinterpret_cast<const float4*>(sinb + o);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float ra = a[e] * cc[e] - b[e] * sn[e];
+        const float rb = b[e] * cc[e] + a[e] * sn[e];
+        a[e] = ra;
+        b[e] = rb;
+      }
     }
-    orow[ia] = __float2bfloat16_rn(a);
-    orow[ib] = __float2bfloat16_rn(b);
+    uint2 wa, wb;
+    wa.x = pack2(a[0], a[1]);
+    wa.y = pack2(a[2], a[3]);
+    wb.x = pack2(b[0], b[1]);
+    wb.y = pack2(b[2], b[3]);
+    *reinterpret_cast<uint2*>(orow + ia) = wa;
+    *reinterpret_cast<uint2*>(orow + ib) = wb;
   }
 }
 
@@ -270,12 +347,24 @@ int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
 {
   if (rows <= 0) return 0;
   if (dim % 8 != 0 || dim > kRowThreads * 8 * 4) return -2;
-  if (norm) {
-    row_mod_kernel<true><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, dim,
-                                                      scale, shift, eps);
+  if (((reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(shift)) & 15u) != 0)
+    return -2;
+  if (dim <= kRowThreads * 8 * 2) {
+    constexpr int R = 4;
+    const unsigned grid = (unsigned)((rows + R - 1) / R);
+    if (norm)
+      row_mod_kernel<true, R, 2><<<grid, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
+                                                             scale, shift, eps);
+    else
+      row_mod_kernel<false, R, 2><<<grid, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
+                                                              scale, shift, eps);
   } else {
-    row_mod_kernel<false><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, dim,
-                                                       scale, shift, eps);
+    if (norm)
+      row_mod_kernel<true, 1, 4><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
+                                                             scale, shift, eps);
+    else
+      row_mod_kernel<false, 1, 4><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
+                                                              scale, shift, eps);
   }
   return launched();
 }
@@ -288,7 +377,10 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
 {
   if (rows <= 0) return 0;
   const int inner = heads * head_dim;
-  if (inner % 8 != 0 || head_dim % 2 != 0) return -2;
+  if (inner % 8 != 0 || head_dim % 8 != 0 || ldo % 4 != 0 ||
+      ((reinterpret_cast<uintptr_t>(gain) | reinterpret_cast<uintptr_t>(cosb) |
+        reinterpret_cast<uintptr_t>(sinb)) & 15u) != 0)
+    return -2;
   const size_t smem = (size_t)inner * sizeof(float);
   if (smem > 48 * 1024) {
     static bool attr = false;
