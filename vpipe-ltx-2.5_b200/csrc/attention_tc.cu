@@ -23,6 +23,7 @@
 // timeout sets the context's error word and the CTA drains and exits.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "block_ops.h"
@@ -363,6 +364,331 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ---- two query tiles per CTA (head_dim 128, bf16) ---------------------
+//
+// The same tile math as fa_tc_kernel, with 256 query rows per CTA in two
+// 128-row tiles, each with its own softmax warpgroup and its own O and S in
+// TMEM (O0 | O1 | S0 | S1 = 512 columns).  The MMA warp interleaves them:
+//   S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 PV1_1 S1_2 | ...
+// so while one warpgroup runs its softmax the tensor core computes the
+// other tile's P V and next S -- in steady state four MMAs per key tile
+// against two softmaxes, neither waiting on the other.  K (3 stages) and V^T
+// (2 stages) have separate rings and producers.  The softmax reads each S
+// row twice from TMEM (max, then exp) to stay within 168 registers.
+constexpr int kFa2Threads = 384;   // w0 Q/K TMA, w1 MMA, w2 V TMA, w4-7 / w8-11 softmax
+constexpr int kFa2KStages = 3;
+constexpr int kFa2VStages = 2;
+
+struct Fa2Cfg {
+  static constexpr int D = 128;
+  static constexpr int kAtom = 128 * 128;
+  static constexpr int kQTile = 2 * kAtom;            // 128 rows x 128 dims
+  static constexpr int kKStage = 2 * kAtom;
+  static constexpr int kVStage = 2 * kAtom;           // 128 dims x 128 keys
+  static constexpr int kSmem =
+      1024 + 2 * kQTile + kFa2KStages * kKStage + kFa2VStages * kVStage + 256;
+  static constexpr uint32_t kOCol = 0;                 // O_t at t * 128
+  static constexpr uint32_t kSCol = 256;               // S_t at 256 + t * 128
+};
+
+__global__ void __launch_bounds__(kFa2Threads, 1)
+    fa2_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                  const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_vt, FaParams p)
+{
+  using C = Fa2Cfg;
+  constexpr int D = C::D;
+  constexpr int SK = kFa2KStages, SV = kFa2VStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_q = base;                                 // tile t at t * kQTile
+  uint8_t* s_k = s_q + 2 * C::kQTile;
+  uint8_t* s_v = s_k + SK * C::kKStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_v + SV * C::kVStage);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + SK;
+  uint64_t* v_full = k_empty + SK;
+  uint64_t* v_empty = v_full + SV;
+  uint64_t* s_full = v_empty + SV;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * 2 * kFaBQ;
+  const int h = blockIdx.y;
+  const int n = p.ntiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < SK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < SV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_vt);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- Q, K TMA
+    if (lane == 0) {
+      uint32_t armed = 0, armed_par = 0;
+      mbar_arrive_expect_tx(q_full, 2 * C::kQTile);
+      for (int t = 0; t < 2; ++t)
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(&tm_q, q_full, s_q + t * C::kQTile + a * C::kAtom, h * D + a * 64,
+                      q0 + t * kFaBQ);
+      for (int j = 0; j < n; ++j) {
+        const int st = j % SK;
+        const uint32_t ph = (uint32_t)(j / SK) & 1u;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, s_abort, p.err, FERR_PRODUCER)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::kKStage);
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(&tm_k, &k_full[st], s_k + st * C::kKStage + a * C::kAtom,
+                      h * D + a * 64, j * kFaBK);
+        armed |= 1u << st;
+        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+      }
+      volatile int no_abort = 0;
+      mbar_wait(q_full, 0, &no_abort, p.err, FERR_DRAIN);
+      for (int st = 0; st < SK; ++st)
+        if (armed & (1u << st))
+          mbar_wait(&k_full[st], (armed_par >> st) & 1u, &no_abort, p.err, FERR_DRAIN);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------- V TMA
+    if (lane == 0) {
+      uint32_t armed = 0, armed_par = 0;
+      for (int j = 0; j < n; ++j) {
+        const int st = j % SV;
+        const uint32_t ph = (uint32_t)(j / SV) & 1u;
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, s_abort, p.err, FERR_PRODUCER)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::kVStage);
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(&tm_vt, &v_full[st], s_v + st * C::kVStage + a * (D * 128),
+                      j * kFaBK + a * 64, h * D);
+        armed |= 1u << st;
+        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+      }
+      volatile int no_abort = 0;
+      for (int st = 0; st < SV; ++st)
+        if (armed & (1u << st))
+          mbar_wait(&v_full[st], (armed_par >> st) & 1u, &no_abort, p.err, FERR_DRAIN);
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16(kFaBQ, kFaBK);
+      constexpr uint32_t idesc_o = idesc_bf16(kFaBQ, D);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t sk = smem_u32(s_k + (j % SK) * C::kKStage);
+        const uint32_t sq = smem_u32(s_q + t * C::kQTile);
+        const uint32_t d = tmem + C::kSCol + (uint32_t)t * kFaBK;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * C::kAtom);
+          umma_f16_ss(d, sdesc_k128_sw128(sq + off) + (uint64_t)(2 * (kk & 3)),
+                      sdesc_k128_sw128(sk + off) + (uint64_t)(2 * (kk & 3)), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t sv = smem_u32(s_v + (j % SV) * C::kVStage);
+        const uint32_t pa = tmem + C::kSCol + (uint32_t)t * kFaBK;
+#pragma unroll
+        for (int kk = 0; kk < kFaBK / 16; ++kk)
+          umma_f16_ts(tmem + C::kOCol + (uint32_t)t * D, pa + (uint32_t)(kk * 8),
+                      sdesc_k128_sw128(sv + (uint32_t)((kk >> 2) * (D * 128))) +
+                          (uint64_t)(2 * (kk & 3)),
+                      idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_full, 0, s_abort, p.err, FERR_MMA) &&
+                mbar_wait(&k_full[0], 0, s_abort, p.err, FERR_MMA);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const bool more = j + 1 < n;
+        // tile 0: P V, then its next S (in-order: the S MMA overwrites
+        // S0 only after this P V has read P0 from it)
+        if (!mbar_wait(&p_full[0], (uint32_t)j & 1u, s_abort, p.err, FERR_MMA) ||
+            !mbar_wait(&v_full[j % SV], (uint32_t)(j / SV) & 1u, s_abort, p.err, FERR_MMA))
+          break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&k_full[(j + 1) % SK], (uint32_t)((j + 1) / SK) & 1u, s_abort, p.err,
+                         FERR_MMA))
+            break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        if (!mbar_wait(&p_full[1], (uint32_t)j & 1u, s_abort, p.err, FERR_MMA)) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&v_empty[j % SV]);
+        if (more) {
+          issue_s(1, j + 1);
+          umma_commit(&k_empty[(j + 1) % SK]);
+        }
+      }
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.err, FERR_DRAIN);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int t = (warp - 4) >> 2;                      // query tile
+    const int q = warp & 3;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t scol = tmem + lane_base + C::kSCol + (uint32_t)t * kFaBK;
+    const uint32_t ocol = tmem + lane_base + C::kOCol + (uint32_t)t * D;
+    const float c = p.scale_log2;
+    float m_run = 0.0f, l_run = 0.0f;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      if (!mbar_wait(&s_full[t], (uint32_t)i & 1u, s_abort, p.err, FERR_SOFTMAX)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int valid = p.tk - i * kFaBK;
+      float mx = -3.0e38f;
+#pragma unroll
+      for (int c4 = 0; c4 < kFaBK / 32; ++c4) {
+        uint32_t v[32];
+        tmem_ld32(scol + (uint32_t)(c4 * 32), v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c4 * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
+      }
+      const float m_tile = mx * c;
+      if (i == 0) m_run = m_tile;
+      const bool need = i > 0 && m_tile > m_run + kRescale;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = need ? m_tile : m_run;
+        const float f = fast_exp2(m_run - m_new);
+        l_run *= f;
+        if (!mbar_wait(&o_done[t], (uint32_t)(i - 1) & 1u, s_abort, p.err, FERR_SOFTMAX)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c4 = 0; c4 < D / 32; ++c4) {
+          uint32_t v[32];
+          tmem_ld32(ocol + (uint32_t)(c4 * 32), v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * f);
+          tmem_st32(ocol + (uint32_t)(c4 * 32), v);
+        }
+        m_run = m_new;
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        // keys [64 h2, 64 h2 + 64) -> P columns [32 h2, 32 h2 + 32); the S
+        // columns this overwrites were read above or in the previous half
+        uint32_t a[32], b[32], pk[32];
+        tmem_ld32(scol + (uint32_t)(h2 * 64), a);
+        tmem_ld32(scol + (uint32_t)(h2 * 64 + 32), b);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int k0 = h2 * 64 + 2 * e;
+          const float s0 = k0 < valid ? __uint_as_float(a[2 * e]) : -3.0e38f;
+          const float s1 = k0 + 1 < valid ? __uint_as_float(a[2 * e + 1]) : -3.0e38f;
+          const float p0 = fast_exp2(fmaf(s0, c, -m_run));
+          const float p1 = fast_exp2(fmaf(s1, c, -m_run));
+          sum += p0 + p1;
+          pk[e] = pack_bf16(p0, p1);
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int k0 = h2 * 64 + 32 + 2 * e;
+          const float s0 = k0 < valid ? __uint_as_float(b[2 * e]) : -3.0e38f;
+          const float s1 = k0 + 1 < valid ? __uint_as_float(b[2 * e + 1]) : -3.0e38f;
+          const float p0 = fast_exp2(fmaf(s0, c, -m_run));
+          const float p1 = fast_exp2(fmaf(s1, c, -m_run));
+          sum += p0 + p1;
+          pk[16 + e] = pack_bf16(p0, p1);
+        }
+        tmem_st32(scol + (uint32_t)(h2 * 32), pk);
+      }
+      l_run += sum;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && n > 0 &&
+        mbar_wait(&o_done[t], (uint32_t)(n - 1) & 1u, s_abort, p.err, FERR_SOFTMAX)) {
+      tc_fence_after();
+      const int row = q0 + t * kFaBQ + q * 32 + (int)lane;
+      float g = 1.0f / l_run;
+      if (p.gate != nullptr && row < p.tq)
+        g *= 2.0f / (1.0f + __expf(-__bfloat162float(p.gate[(size_t)row * p.ldg + h])));
+      __nv_bfloat16* orow = p.o + (size_t)row * p.ldo + h * D;
+#pragma unroll
+      for (int c4 = 0; c4 < D / 32; ++c4) {
+        uint32_t v[32];
+        tmem_ld32(ocol + (uint32_t)(c4 * 32), v);
+        tmem_wait_ld();
+        if (row < p.tq) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(v[8 * e + 0]) * g, __uint_as_float(v[8 * e + 1]) * g);
+            w.y = pack_bf16(__uint_as_float(v[8 * e + 2]) * g, __uint_as_float(v[8 * e + 3]) * g);
+            w.z = pack_bf16(__uint_as_float(v[8 * e + 4]) * g, __uint_as_float(v[8 * e + 5]) * g);
+            w.w = pack_bf16(__uint_as_float(v[8 * e + 6]) * g, __uint_as_float(v[8 * e + 7]) * g);
+            *reinterpret_cast<uint4*>(orow + c4 * 32 + 8 * e) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 // vt[c][t] = v[t][c]: c < cols (= heads * D), t < tk.  64 x 64 tiles.
 __global__ void __launch_bounds__(256)
     transpose_kernel(const __nv_bfloat16* __restrict__ v, int ldv, int tk, int cols,
@@ -583,8 +909,23 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
   if (!fa_encode(&tq_map, q, (uint64_t)cols, (uint64_t)tq, (uint64_t)ldq * 2, 64, kFaBQ) ||
       !fa_encode(&tk_map, k, (uint64_t)cols, (uint64_t)tk, (uint64_t)ldk * 2, 64, kFaBK))
     return -1;
-  return launch_fa<D, false>(tq_map, tk_map, tv_map, fa_params(o, ldo, gate, ldg, tq, tk, D, err),
-                             heads, s);
+  const FaParams prm = fa_params(o, ldo, gate, ldg, tq, tk, D, err);
+  static int two_tiles = -1;
+  if (two_tiles < 0) {
+    const char* e = getenv("LTX25_FA_TILES");
+    two_tiles = (e != nullptr && e[0] == '1') ? 0 : 1;
+  }
+  if (tq <= kFaBQ || !two_tiles) return launch_fa<D, false>(tq_map, tk_map, tv_map, prm, heads, s);
+  static bool attr2 = false;
+  if (!attr2) {
+    if (cudaFuncSetAttribute(fa2_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Fa2Cfg::kSmem) != cudaSuccess)
+      return -1;
+    attr2 = true;
+  }
+  fa2_tc_kernel<<<dim3((tq + 2 * kFaBQ - 1) / (2 * kFaBQ), heads), kFa2Threads, Fa2Cfg::kSmem,
+                  s>>>(tq_map, tk_map, tv_map, prm);
+  return launched();
 }
 
 SageScratch sage_scratch_need(int tq, int tk, int heads, int head_dim)
