@@ -586,15 +586,34 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
       }
       tc_fence_after();
       const int valid = p.tk - i * kFaBK;
-      float mx = -3.0e38f;
+      const bool full = valid >= kFaBK;        // warp-uniform: no masking
+      float mx;
+      {
+        // row max: two 64-column reads, four independent max chains
+        float m4[4] = {-3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};
 #pragma unroll
-      for (int c4 = 0; c4 < kFaBK / 32; ++c4) {
-        uint32_t v[32];
-        tmem_ld32(scol + (uint32_t)(c4 * 32), v);
-        tmem_wait_ld();
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t a[32], b[32];
+          tmem_ld32(scol + (uint32_t)(h2 * 64), a);
+          tmem_ld32(scol + (uint32_t)(h2 * 64 + 32), b);
+          tmem_wait_ld();
+          if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c4 * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
+            for (int e = 0; e < 32; e += 2) {
+              m4[0] = fmaxf(m4[0], __uint_as_float(a[e]));
+              m4[1] = fmaxf(m4[1], __uint_as_float(a[e + 1]));
+              m4[2] = fmaxf(m4[2], __uint_as_float(b[e]));
+              m4[3] = fmaxf(m4[3], __uint_as_float(b[e + 1]));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (h2 * 64 + e < valid) m4[0] = fmaxf(m4[0], __uint_as_float(a[e]));
+              if (h2 * 64 + 32 + e < valid) m4[1] = fmaxf(m4[1], __uint_as_float(b[e]));
+            }
+          }
+        }
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
       const float m_tile = mx * c;
       if (i == 0) m_run = m_tile;
@@ -628,26 +647,26 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
         tmem_ld32(scol + (uint32_t)(h2 * 64), a);
         tmem_ld32(scol + (uint32_t)(h2 * 64 + 32), b);
         tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (h2 * 64 + e >= valid) a[e] = __float_as_uint(-3.0e38f);
+            if (h2 * 64 + 32 + e >= valid) b[e] = __float_as_uint(-3.0e38f);
+          }
+        }
+        float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int k0 = h2 * 64 + 2 * e;
-          const float s0 = k0 < valid ? __uint_as_float(a[2 * e]) : -3.0e38f;
-          const float s1 = k0 + 1 < valid ? __uint_as_float(a[2 * e + 1]) : -3.0e38f;
-          const float p0 = fast_exp2(fmaf(s0, c, -m_run));
-          const float p1 = fast_exp2(fmaf(s1, c, -m_run));
-          sum += p0 + p1;
+          const float p0 = fast_exp2(fmaf(__uint_as_float(a[2 * e]), c, -m_run));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(a[2 * e + 1]), c, -m_run));
+          const float p2 = fast_exp2(fmaf(__uint_as_float(b[2 * e]), c, -m_run));
+          const float p3 = fast_exp2(fmaf(__uint_as_float(b[2 * e + 1]), c, -m_run));
+          s0 += p0 + p1;
+          s1 += p2 + p3;
           pk[e] = pack_bf16(p0, p1);
+          pk[16 + e] = pack_bf16(p2, p3);
         }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int k0 = h2 * 64 + 32 + 2 * e;
-          const float s0 = k0 < valid ? __uint_as_float(b[2 * e]) : -3.0e38f;
-          const float s1 = k0 + 1 < valid ? __uint_as_float(b[2 * e + 1]) : -3.0e38f;
-          const float p0 = fast_exp2(fmaf(s0, c, -m_run));
-          const float p1 = fast_exp2(fmaf(s1, c, -m_run));
-          sum += p0 + p1;
-          pk[16 + e] = pack_bf16(p0, p1);
-        }
+        sum += s0 + s1;
         tmem_st32(scol + (uint32_t)(h2 * 32), pk);
       }
       l_run += sum;
