@@ -266,3 +266,35 @@ def test_dense_narrow_outputs(ctx, M, N):
     assert np.all(y[M] == 7.0)       # the guard row is untouched
     want = lib.linear_f64(lib.bf16_to_f32(x), lib.bf16_to_f32(wd))
     assert lib.rel_l2(y[:M], want) < TOL
+
+
+@pytest.mark.parametrize("M,N,K,epi", [(2048, 4096, 1024, 0), (1900, 4096, 2048, 2), (8160, 2048, 4096, 1)])
+def test_dense_pair_path(ctx, M, N, K, epi):
+    """The expanded-weight GEMM on CTA pairs (cta_group::2, M = 256 across two
+    SMs; the default at these sizes) equals the single-CTA kernel bit for bit
+    (same K order per output) and meets the oracle bar, for each epilogue."""
+    import os
+    import torch
+    import ltx25_b200 as L
+    xb, codes, scales, biases, _ = make(M, N, K, seed=9)
+    w = L.QWeight.upload(ctx, codes, scales, biases, N, K)
+    xd = to_dev(xb)
+    gate = torch.randn(N, device="cuda") * 0.5 if epi == L.EPI_GATED_RES else None
+    y0 = torch.randn((M, N), device="cuda").to(torch.bfloat16)
+    outs = {}
+    ctx.set_route(L.ROUTE_DEQUANT_ONCE)
+    try:
+        for pair in ("1", "0"):
+            os.environ["LTX25_FORCE_PAIR"] = pair
+            y = y0.clone()
+            L.qlinear(ctx, w, xd, out=y, epilogue=epi, gate=gate)
+            torch.cuda.synchronize()
+            outs[pair] = y
+    finally:
+        os.environ.pop("LTX25_FORCE_PAIR", None)
+        ctx.set_route(L.ROUTE_AUTO)
+    ctx.check()
+    assert torch.equal(outs["1"], outs["0"])
+    if epi == L.EPI_STORE:
+        want = oracle_y(xb, codes, scales, biases, K)
+        assert lib.rel_l2(from_dev(outs["1"]), want) < TOL

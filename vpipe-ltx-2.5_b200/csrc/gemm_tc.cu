@@ -92,7 +92,8 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
   constexpr int A = C::kASlots > 0 ? C::kASlots : 1;
   constexpr int kDeqWarps = 8;
   constexpr int kWT = PAIR ? 2 * C::kBM : C::kBM;   // weight rows per tile
-  static_assert(!PAIR || MODE == MODE_W8G64, "pairs run the w8g64 path");
+  static_assert(!PAIR || MODE == MODE_W8G64 || MODE == MODE_BF16,
+                "pairs run the w8g64 and bf16 paths");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -185,7 +186,14 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
           armed |= 1u << stage;
           armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
           const int kx = kb * C::kKPerStage;
-          if constexpr (PAIR) {
+          if constexpr (PAIR && MODE == MODE_BF16) {
+            // Both CTAs' halves of both operands complete on the leader's
+            // barrier, which the leader arms for all four.
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (C::kXStage + C::kWStage));
+            const uint32_t lf = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(&tm_x, lf, s_x + stage * C::kXStage, kx, xrow0);
+            tma_load_2d_pair(&tm_w, lf, s_w + stage * C::kWStage, kx, wrow0);
+          } else if constexpr (PAIR) {
             // Both halves of the activation tile complete on the leader's
             // barrier (it arms them); the codes on this CTA's own.
             if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kXStage);
@@ -219,11 +227,14 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
       }
       // Let every load this CTA tracks land before the CTA can exit (in a
       // pair, the activation halves are tracked by the leader's MMA).
-      for (int s = 0; s < S; ++s) {
+      // (A dense pair's loads all complete on the leader's barriers: the
+      // leader drains them, and the final cluster barrier holds the peer.)
+      const bool drains = !(PAIR && MODE == MODE_BF16) || leader;
+      for (int s = 0; s < S && drains; ++s) {
         if (armed & (1u << s)) {
           volatile int no_abort = 0;
-          mbar_wait(PAIR ? &cfull[s] : &full[s], (armed_par >> s) & 1u,
-                    &no_abort, p.err, KERR_DRAIN);
+          mbar_wait((PAIR && MODE == MODE_W8G64) ? &cfull[s] : &full[s],
+                    (armed_par >> s) & 1u, &no_abort, p.err, KERR_DRAIN);
         }
       }
     }
@@ -275,7 +286,12 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
-            if constexpr (PAIR) {
+            if constexpr (PAIR && MODE == MODE_BF16) {
+              const uint64_t adesc =
+                  sdesc_k128_sw128(smem_u32(s_w + stage * C::kWStage));
+              umma_f16_ss_pair(d, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk),
+                               idesc, accum);
+            } else if constexpr (PAIR) {
               umma_f16_ts_pair(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
                                bdesc + (uint64_t)(2 * kk), idesc, accum);
             } else if constexpr (MODE == MODE_W8G64) {
@@ -296,8 +312,10 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
           if constexpr (PAIR) {
             umma_commit_pair(smem_u32(&empty[stage]));
             umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
-            umma_commit_pair(smem_u32(&aempty[aslot]));
-            umma_commit_pair(mapa_shared(smem_u32(&aempty[aslot]), 1));
+            if constexpr (MODE == MODE_W8G64) {
+              umma_commit_pair(smem_u32(&aempty[aslot]));
+              umma_commit_pair(mapa_shared(smem_u32(&aempty[aslot]), 1));
+            }
           } else {
             umma_commit(&empty[stage]);
             if constexpr (MODE == MODE_W8G64) umma_commit(&aempty[aslot]);
@@ -770,7 +788,7 @@ int launch_epi(const GemmLaunch& L, cudaStream_t stream)
 template <int MODE>
 int launch_tn(const GemmLaunch& L, cudaStream_t stream)
 {
-  if constexpr (MODE == MODE_W8G64) {
+  if constexpr (MODE == MODE_W8G64 || MODE == MODE_BF16) {
     if (L.pair) return L.tn == 256 ? launch_epi<MODE, 256, true>(L, stream) : -4;
   } else {
     if (L.pair) return -4;

@@ -322,6 +322,19 @@ __device__ __forceinline__ void umma_f16_ts_pair(uint32_t d, uint32_t a_tmem,
       : "memory");
 }
 
+// D (+)= A(smem) * B(smem), M = 256 across the CTA pair: each CTA's shared
+// memory holds its 128 rows of A and its half of B at the same offsets, each
+// CTA's TMEM its 128 rows of D.  Issued by the leader CTA only.
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d, uint64_t a, uint64_t b,
+                                                 uint32_t idesc, uint32_t acc)
+{
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 // Arrive once on the mbarrier at shared::cluster address `caddr` (this CTA's
 // or the peer's) when the pair MMAs issued so far have completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t caddr)

@@ -45,11 +45,14 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
   p.kblocks = K / kpb;
   p.tn = M <= 128 ? 128 : 256;
   // CTA pairs (M = 256 MMA over two SMs) halve the activation bytes each SM
-  // streams per FLOP; measured slower than single CTAs so far (the
-  // cross-CTA hand-off of dequantized A slots), so opt-in for A/B.
-  p.pair = false;
+  // streams per FLOP.  The dense path pairs by default once there are
+  // enough tiles; the fused w8g64 path measured slower paired (the
+  // cross-CTA hand-off of dequantized A slots), so opt-in there.
+  p.pair = mode == ltx::MODE_BF16 && M >= 1024 && N % 256 == 0 &&
+           ((M + 255) / 256) * (N / 256) >= sms / 2;
   if (const char* e = std::getenv("LTX25_FORCE_PAIR")) {
-    p.pair = mode == ltx::MODE_W8G64 && std::atoi(e) != 0 && M > 128;
+    p.pair = (mode == ltx::MODE_W8G64 || mode == ltx::MODE_BF16) && std::atoi(e) != 0 &&
+             M > 128 && N % 256 == 0;
   }
   if (p.pair) p.tn = 256;
   if (const char* e = std::getenv("LTX25_FORCE_TN")) {
