@@ -259,7 +259,8 @@ def run_stack(args):
         if rank == 0:
             uid.copy_(torch.frombuffer(bytearray(L.tp_unique_id()), dtype=torch.uint8))
         pg.broadcast(uid, src=0)
-        ctx.set_tp(rank, world, bytes(uid.cpu().numpy().tobytes()))
+        join = ctx.set_sp if args.parallel == "sp" else ctx.set_tp
+        join(rank, world, bytes(uid.cpu().numpy().tobytes()))
     vdim, vh, adim, ah = 4096, 32, 2048, 32
     frames, hh, ww, at, tt = 16, 17, 30, 126, 256
     vt = frames * hh * ww
@@ -361,7 +362,7 @@ def run_stack(args):
         "config": {"workload": f"{nblk}-block joint AV stack: video 8160x4096 (16x17x30), "
                                "audio 126x2048, text 256; weights and activations far "
                                "above L2 every step",
-                   "parallelism": f"tp{world}"},
+                   "parallelism": f"{args.parallel}{world}"},
         "e2e": {"value": round(e2e_ms / 1e3, 4), "unit": "s/step",
                 "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
         "gpu_launches": int(launches),
@@ -548,6 +549,9 @@ def main():
     ap.add_argument("--only", type=int, default=None,
                     help="profile one sweep shape (index into SHAPES)")
     ap.add_argument("--blocks", type=int, default=48, help="stack depth (--workload stack)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "sp"],
+                    help="stack under torchrun: tensor parallel (BASELINE config 5) or "
+                         "sequence/head parallel")
     ap.add_argument("--sage", action="store_true", help="sage_attn tier (--workload attn)")
     ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
                     help="qlinear route for quantized weights (sweep)")

@@ -341,6 +341,16 @@ LTX_API unsigned long long ltx_launch_count(void);
 #define LTX_TP_ID_BYTES 128
 LTX_API int ltx_tp_unique_id(void* id, int bytes);
 LTX_API int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id);
+/* Sequence (head) parallelism instead: blocks keep their weights whole
+ * and each rank runs 1/world of the video tokens through the GEMMs, the row
+ * ops, the text and audio->video cross attentions and the feed-forward with
+ * no communication; the video self-attention and the video->audio keys
+ * switch to a head split by all-to-all (DeepSpeed-Ulysses) and back.  The
+ * audio stream (126 tokens) is replicated.  Callers still pass and get the
+ * WHOLE x on every rank (the stack gathers the shards once, at its end).
+ * The video token count must divide by world; heads by world. */
+LTX_API int ltx_ctx_set_sp(ltx_ctx* ctx, int rank, int world, const void* id);
+
 /* In-place sum over the group on `stream`; dtype 0 = f32, 1 = bf16. */
 LTX_API int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype,
                              void* stream);

@@ -1,10 +1,11 @@
-"""Tensor-parallel block and stack on 2 GPUs (BASELINE config 5's multi-GPU
-leg), against the one-GPU block and the CPU oracle.
+"""Multi-GPU block and stack on 2 GPUs (BASELINE config 5's multi-GPU leg),
+tensor parallel (ltx_ctx_set_tp) and sequence parallel (ltx_ctx_set_sp),
+against the one-GPU block and the CPU oracle.
 
-Two spawned processes, one per GPU, join one NCCL group through
-ltx_ctx_set_tp (rendezvous id made here), load the same full weights (each
-keeps its shard), and run a block and a 2-block stack on the same
-replicated inputs.  Checked: both ranks end with the same x; it matches the
+Two spawned processes, one per GPU, join one NCCL group (rendezvous id made
+here), load the same full weights (tensor parallel: each keeps its shard;
+sequence parallel: each keeps them whole and runs half the video tokens),
+and run a block and a 2-block stack on the same replicated inputs.  Checked: both ranks end with the same x; it matches the
 oracle at the block bars of tests/test_block_gpu.py and the one-GPU device
 block within bf16.  Skipped with fewer than 2 GPUs.  NVLS is off in the
 workers, and a worker that does not finish in time is killed by PID.
@@ -68,27 +69,28 @@ def _run(ctx, world_blocks, ins):
     return one, two, deqs
 
 
-def _worker(rank, world, uid, out_dir):
+def _worker(rank, world, uid, out_dir, mode):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
     import ltx25_b200 as L
     torch.cuda.set_device(rank)
     ctx = L.Context(rank)
-    ctx.set_tp(rank, world, uid)
+    (ctx.set_tp if mode == "tp" else ctx.set_sp)(rank, world, uid)
     t, t2, ins = _setup()
     one, two, _ = _run(ctx, [t, t2], ins)
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), v1=one[0], a1=one[1], v2=two[0], a2=two[1])
     ctx.close()
 
 
-def test_tp2_block_and_stack(ctx, tmp_path):
+@pytest.mark.parametrize("mode", ["tp", "sp"])
+def test_two_gpu_block_and_stack(ctx, tmp_path, mode):
     import torch
     import torch.multiprocessing as mp
     import ltx25_b200 as L
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     uid = L.tp_unique_id()
-    pc = mp.start_processes(_worker, args=(WORLD, uid, str(tmp_path)), nprocs=WORLD,
+    pc = mp.start_processes(_worker, args=(WORLD, uid, str(tmp_path), mode), nprocs=WORLD,
                             join=False, start_method="spawn")
     try:
         for _ in range(60):

@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kRowThreads)
                         const float* __restrict__ cosb,
                         const float* __restrict__ sinb, int tokens, float eps,
                         const float* __restrict__ sumsq, int norm_width,
-                        int head0)
+                        int head0, int tbl_tokens, int tok0)
 {
   extern __shared__ float srow[];   // the normalized row, f32 [inner]
   __shared__ float red[33];
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kRowThreads)
       b[0] *= gb.x; b[1] *= gb.y; b[2] *= gb.z; b[3] *= gb.w;
     }
     if (cosb != nullptr) {
-      const size_t o = ((size_t)(head0 + h) * tokens + t) * half + j;
+      const size_t o = ((size_t)(head0 + h) * tbl_tokens + tok0 + t) * half + j;
       const float4 c4 = *reinterpret_cast<const float4*>(cosb + o);
       const float4 s4 = *reinterpret_cast<const float4*>(sinb + o);
       const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -310,6 +310,53 @@ __global__ void gated_residual_kernel(__nv_bfloat16* __restrict__ x, int ldx,
   }
 }
 
+// dst[p][t][c] = src[t][p * cpr + c]: a token-major [rows][ranks * cpr]
+// matrix regrouped into one contiguous [rows][cpr] block per rank (the send
+// side of an all-to-all).  8 columns per thread.
+__global__ void a2a_pack_kernel(const __nv_bfloat16* __restrict__ src, int ld, int rows,
+                                int ranks, int cpr, __nv_bfloat16* __restrict__ dst)
+{
+  const int c8 = cpr / 8;
+  const size_t total = (size_t)ranks * rows * c8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % c8) * 8;
+    const size_t pt = i / c8;
+    const int t = (int)(pt % rows), p = (int)(pt / rows);
+    *reinterpret_cast<uint4*>(dst + ((size_t)p * rows + t) * cpr + c) =
+        *reinterpret_cast<const uint4*>(src + (size_t)t * ld + (size_t)p * cpr + c);
+  }
+}
+
+// dst[t][p * cpr + c] = src[p][t][c] (* 2 sigmoid(gate[t][p * cpr / D + c / D])
+// when gate is given): the receive side of an all-to-all back to token-major
+// rows, applying the attention's per-head gate on the way.
+__global__ void a2a_unpack_kernel(const __nv_bfloat16* __restrict__ src, int rows, int ranks,
+                                  int cpr, __nv_bfloat16* __restrict__ dst, int ldd,
+                                  const __nv_bfloat16* __restrict__ gate, int ldg, int head_dim)
+{
+  const int c8 = cpr / 8;
+  const size_t total = (size_t)ranks * rows * c8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % c8) * 8;
+    const size_t pt = i / c8;
+    const int t = (int)(pt % rows), p = (int)(pt / rows);
+    uint4 w = *reinterpret_cast<const uint4*>(src + ((size_t)p * rows + t) * cpr + c);
+    if (gate != nullptr) {
+      const int col = p * cpr + c;
+      const float g = __bfloat162float(gate[(size_t)t * ldg + col / head_dim]);
+      const float f = 2.0f / (1.0f + __expf(-g));
+      float v[8];
+      load8(reinterpret_cast<const __nv_bfloat16*>(&w), v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] *= f;
+      store8(reinterpret_cast<__nv_bfloat16*>(&w), v);
+    }
+    *reinterpret_cast<uint4*>(dst + (size_t)t * ldd + (size_t)p * cpr + c) = w;
+  }
+}
+
 __global__ void f32_to_bf16_kernel(const float* __restrict__ a,
                                    __nv_bfloat16* __restrict__ out, size_t n)
 {
@@ -373,7 +420,8 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
                         int ldo, int rows, int heads, int head_dim,
                         const float* gain, const float* cosb,
                         const float* sinb, float eps, cudaStream_t s,
-                        const float* sumsq, int norm_width, int head0)
+                        const float* sumsq, int norm_width, int head0, int tbl_tokens,
+                        int tok0)
 {
   if (rows <= 0) return 0;
   const int inner = heads * head_dim;
@@ -393,7 +441,33 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
   }
   qk_norm_rope_kernel<<<rows, kRowThreads, smem, s>>>(
       in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq,
-      norm_width > 0 ? norm_width : inner, head0);
+      norm_width > 0 ? norm_width : inner, head0, tbl_tokens > 0 ? tbl_tokens : rows, tok0);
+  return launched();
+}
+
+int launch_a2a_pack(const __nv_bfloat16* src, int ld, int rows, int ranks, int cpr,
+                    __nv_bfloat16* dst, cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  if (cpr % 8 != 0 || ld % 8 != 0) return -2;
+  const size_t total = (size_t)ranks * rows * (cpr / 8);
+  size_t grid = (total + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  a2a_pack_kernel<<<(unsigned)grid, 256, 0, s>>>(src, ld, rows, ranks, cpr, dst);
+  return launched();
+}
+
+int launch_a2a_unpack(const __nv_bfloat16* src, int rows, int ranks, int cpr,
+                      __nv_bfloat16* dst, int ldd, const __nv_bfloat16* gate, int ldg,
+                      int head_dim, cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  if (cpr % 8 != 0 || ldd % 8 != 0 || (gate != nullptr && head_dim % 8 != 0)) return -2;
+  const size_t total = (size_t)ranks * rows * (cpr / 8);
+  size_t grid = (total + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  a2a_unpack_kernel<<<(unsigned)grid, 256, 0, s>>>(src, rows, ranks, cpr, dst, ldd, gate, ldg,
+                                                   head_dim);
   return launched();
 }
 

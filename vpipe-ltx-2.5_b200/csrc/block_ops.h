@@ -29,7 +29,8 @@ int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
 
 // RMSNorm over the whole heads*head_dim row with gain (f32, may be null),
 // then split-half RoPE with [heads][rows][head_dim/2] f32 tables (may be
-// null).  in: row stride ldi; out: row stride ldo.  Tensor-parallel form:
+// null; token t reads table row tok0 + t of tbl_tokens).  in: row stride
+// ldi; out: row stride ldo.  Tensor-parallel form:
 // the row holds heads [head0, head0 + heads) of a wider row whose per-token
 // sum of squares (over norm_width columns) is given in sumsq.
 int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
@@ -37,7 +38,16 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
                         const float* gain, const float* cosb,
                         const float* sinb, float eps, cudaStream_t s,
                         const float* sumsq = nullptr, int norm_width = 0,
-                        int head0 = 0);
+                        int head0 = 0, int tbl_tokens = 0, int tok0 = 0);
+
+// All-to-all regrouping (sequence parallel): pack [rows][ranks * cpr] into
+// [ranks][rows][cpr]; unpack the reverse, optionally times the per-head
+// gate 2 sigmoid(gate[t][head]).  cpr % 8 == 0.
+int launch_a2a_pack(const __nv_bfloat16* src, int ld, int rows, int ranks, int cpr,
+                    __nv_bfloat16* dst, cudaStream_t s);
+int launch_a2a_unpack(const __nv_bfloat16* src, int rows, int ranks, int cpr,
+                      __nv_bfloat16* dst, int ldd, const __nv_bfloat16* gate, int ldg,
+                      int head_dim, cudaStream_t s);
 
 // out[r] = sum of squares of row r's first `cols` values, f32.
 int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,

@@ -231,6 +231,21 @@ int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id)
   return LTX_OK;
 }
 
+int ltx_ctx_set_sp(ltx_ctx* ctx, int rank, int world, const void* id)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, LTX_E_SHAPE, "set_sp: rank outside [0, world)");
+  if (ctx->ops.comm() != nullptr) return fail(ctx, LTX_E_STATE, "set_sp: already set");
+  if (world == 1) return LTX_OK;
+  if (id == nullptr) return fail(ctx, LTX_E_NULL, "set_sp: null id");
+  auto c = std::make_unique<ltx25::Comm>();
+  std::string e;
+  if (!c->init(ctx->ops.device(), rank, world, id, &e)) return fail(ctx, LTX_E_CUDA, e);
+  ctx->ops.set_comm(std::move(c), /*sequence*/ true);
+  return LTX_OK;
+}
+
 int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype, void* stream)
 {
   if (ctx == nullptr) return LTX_E_NULL;
@@ -591,22 +606,37 @@ int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
   if (begin < 0 || begin > end || end > n)
     return sfail(s, LTX_E_SHAPE, "forward: block range outside the stack");
   if (!s->reserved) return sfail(s, LTX_E_STATE, "forward before reserve");
-  ltx25::StreamIO v = to_io(video), a = to_io(audio);
+  ltx25::StreamIO whole = to_io(video), a = to_io(audio);
+  // Sequence parallel: each rank runs its token shard through every block
+  // and the shards are gathered once, after the last.
+  ltx25::StreamIO v = whole;
+  const bool sp = s->blocks[0]->blk->sequence_parallel();
+  if (sp) {
+    std::string e;
+    if (!s->blocks[0]->blk->shard_io(whole, &v, &e)) return sfail(s, LTX_E_SHAPE, e);
+  }
   for (int i = begin; i < end; ++i) {
     if (progress != nullptr && progress(i, n, user) == 0)
+      // (sequence parallel: x's shards stay where each rank left them, and
+      // every rank must take the same decision -- the next collective
+      // would otherwise wait for ranks that stopped)
       return sfail(s, LTX_E_ABORTED, "aborted at block " + std::to_string(i));
     ltx25::CudaBlock* blk = s->blocks[(size_t)i]->blk;
     if (blk->arena() != s->arena)
       return sfail(s, LTX_E_STATE, "block " + std::to_string(i) +
                                        " was reserved outside the stack");
     std::string e;
-    if (!blk->forward(S(stream), v, a, &e)) {
+    if (!(sp ? blk->forward_shard(S(stream), v, a, &e) : blk->forward(S(stream), v, a, &e))) {
       int code = code_for(e);
       if (e.find("arena") != std::string::npos) code = LTX_E_STATE;
       if (e.find("neither stream") != std::string::npos || e.find("missing") != std::string::npos)
         code = LTX_E_NULL;
       return sfail(s, code, "block " + std::to_string(i) + ": " + e);
     }
+  }
+  if (sp && end > begin) {
+    std::string e;
+    if (!s->blocks[0]->blk->gather_video(S(stream), whole, &e)) return sfail(s, LTX_E_CUDA, e);
   }
   return LTX_OK;
 }

@@ -353,8 +353,14 @@ bool CudaBlock::finalize(std::string* err)
 {
   if (_final) return true;
   _comm = _ops->comm();
-  _tp_world = _comm ? _comm->world() : 1;
-  _tp_rank = _comm ? _comm->rank() : 0;
+  _sp = _ops->sequence_parallel();
+  _sp_world = _sp ? _comm->world() : 1;
+  _sp_rank = _sp ? _comm->rank() : 0;
+  // Tensor parallel shards the weights; sequence parallel keeps them whole.
+  _tp_world = (_comm && !_sp) ? _comm->world() : 1;
+  _tp_rank = (_comm && !_sp) ? _comm->rank() : 0;
+  if (_sp && (_vheads % _sp_world != 0 || _aheads % _sp_world != 0))
+    return fail(err, "sequence parallel shape: heads do not split over the ranks");
   if (!build_stream_(false, _video, err) || !build_stream_(true, _audio, err))
     return false;
   // Both cross-attentions run at the AUDIO head count and head width
@@ -377,16 +383,17 @@ BlockArena::~BlockArena()
   for (void* p : {(void*)normed, (void*)qkv, (void*)qn, (void*)kn, (void*)att,
                   (void*)glog, (void*)ctxmod, (void*)kvp, (void*)ff, (void*)qv,
                   (void*)kva, (void*)qa, (void*)kvv, (void*)mods, (void*)part,
-                  (void*)ssq})
+                  (void*)ssq, (void*)sp_send, (void*)sp_recv})
     cudaFree(p);
 }
 
 bool BlockArena::ensure(int i, size_t n, std::string* err)
 {
-  void** slots[16] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
+  void** slots[18] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
                       (void**)&att, (void**)&glog, (void**)&ctxmod, (void**)&kvp,
                       (void**)&ff, (void**)&qv, (void**)&kva, (void**)&qa,
-                      (void**)&kvv, (void**)&mods, (void**)&part, (void**)&ssq};
+                      (void**)&kvv, (void**)&mods, (void**)&part, (void**)&ssq,
+                      (void**)&sp_send, (void**)&sp_recv};
   if (n <= cap[i]) return true;
   const size_t elt = (i == 13 || i == 15) ? sizeof(float) : sizeof(__nv_bfloat16);
   cudaFree(*slots[i]);
@@ -407,7 +414,7 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   const size_t vd = _vdim, ad = _adim;
   const size_t ai = ad;   // audio inner (the cross attentions' width too)
   auto mx = [](std::initializer_list<size_t> l) { return std::max(l); };
-  const size_t need[16] = {
+  const size_t need[18] = {
       mx({vt * vd, at * ad}),                                        // normed
       mx({vt * 3 * vd, at * 3 * ad, vt * vd, vt * ai, at * ai}),     // qkv / q
       mx({vt * vd, at * ad, vt * ai}),                               // qn
@@ -420,9 +427,13 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
       vt * vd, at * ad, at * ad, vt * vd,                            // qv kva qa kvv
       (size_t)MOD_ROWS * (vd + ad),                                  // mods
       _tp_world > 1 ? mx({vt * vd, at * ad}) : 0,                    // part
-      _tp_world > 1 ? 2 * (vt + at + tt) : 0};                       // ssq
+      _tp_world > 1 ? 2 * (vt + at + tt) : 0,                        // ssq
+      // sequence parallel: q, k, v of one head group for the whole sequence
+      // (the video self-attention), or the v2a keys/values / outputs
+      _sp ? 3 * vt * vd / _sp_world + at * ai : 0,                   // sp_send
+      _sp ? 3 * vt * vd / _sp_world + at * ai : 0};                  // sp_recv
   _arp = share ? share : std::make_shared<BlockArena>();
-  for (int i = 0; i < 16; ++i)
+  for (int i = 0; i < 18; ++i)
     if (!_arp->ensure(i, need[i], err)) return false;
   _arp->video = std::max(_arp->video, vt);
   _arp->audio = std::max(_arp->audio, at);
@@ -443,10 +454,8 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
 
 bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
                         const __nv_bfloat16* xq, int tq,
-                        const __nv_bfloat16* xkv, int tkv, const float* qcos,
-                        const float* qsin, const float* kcos,
-                        const float* ksin, __nv_bfloat16* out,
-                        std::string* err)
+                        const __nv_bfloat16* xkv, int tkv, const RopeRef& qr,
+                        const RopeRef& kr, __nv_bfloat16* out, std::string* err)
 {
   const int I = a.inner;
   const __nv_bfloat16 *qraw, *kraw, *vraw;
@@ -483,11 +492,11 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     kss = _arp->ssq + tq;
   }
   if (ltx::launch_qk_norm_rope(qraw, ldq, _arp->qn, I, tq, a.heads, a.head_dim,
-                               a.q_norm, qcos, qsin, kEps, s, qss, a.norm_width,
-                               a.head0) != 0 ||
+                               a.q_norm, qr.cos, qr.sin, kEps, s, qss, a.norm_width,
+                               a.head0, qr.tbl_tokens, qr.tok0) != 0 ||
       ltx::launch_qk_norm_rope(kraw, ldkv, _arp->kn, I, tkv, a.heads,
-                               a.head_dim, a.k_norm, kcos, ksin, kEps, s, kss,
-                               a.norm_width, a.head0) != 0)
+                               a.head_dim, a.k_norm, kr.cos, kr.sin, kEps, s, kss,
+                               a.norm_width, a.head0, kr.tbl_tokens, kr.tok0) != 0)
     return fail(err, "q/k norm + rope launch failed");
   const __nv_bfloat16* glog = nullptr;
   if (a.gate.N > 0) {
@@ -499,6 +508,89 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   if (!_ops->attention(s, _arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog, a.heads, tq,
                        tkv, a.heads, a.head_dim, err, _layer))
     return false;
+  return true;
+}
+
+bool CudaBlock::attend_self_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfloat16* xq,
+                                int tl, const RopeRef& r, __nv_bfloat16* out,
+                                std::string* err)
+{
+  // Tokens are sharded, weights whole: q, k, v of this rank's tl tokens for
+  // ALL heads, then an all-to-all to the whole sequence for this rank's
+  // heads, attention, and an all-to-all back (DeepSpeed-Ulysses layout).
+  const int I = a.inner, N = _sp_world, Il = I / N, tv = tl * N, hl = a.heads / N;
+  if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _arp->qkv, 3 * I, tl, a.qdim, 3 * I,
+                    ltx::EPI_STORE, nullptr, err))
+    return false;
+  if (ltx::launch_qk_norm_rope(_arp->qkv, 3 * I, _arp->qn, I, tl, a.heads, a.head_dim,
+                               a.q_norm, r.cos, r.sin, kEps, s, nullptr, 0, 0, r.tbl_tokens,
+                               r.tok0) != 0 ||
+      ltx::launch_qk_norm_rope(_arp->qkv + I, 3 * I, _arp->kn, I, tl, a.heads, a.head_dim,
+                               a.k_norm, r.cos, r.sin, kEps, s, nullptr, 0, 0, r.tbl_tokens,
+                               r.tok0) != 0)
+    return fail(err, "q/k norm + rope launch failed");
+  const size_t blk = (size_t)tv * Il;   // one of q, k, v for this rank's heads
+  if (ltx::launch_a2a_pack(_arp->qn, I, tl, N, Il, _arp->sp_send, s) != 0 ||
+      ltx::launch_a2a_pack(_arp->kn, I, tl, N, Il, _arp->sp_send + blk, s) != 0 ||
+      ltx::launch_a2a_pack(_arp->qkv + 2 * I, 3 * I, tl, N, Il, _arp->sp_send + 2 * blk, s) != 0)
+    return fail(err, "all-to-all pack launch failed");
+  if (!_comm->alltoall_bf16(_arp->sp_send, _arp->sp_recv, (size_t)tl * Il, 3, blk, s, err))
+    return false;
+  // gate logits of this rank's tokens, all heads (applied on the way back)
+  if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _arp->glog, a.heads, tl, a.qdim,
+                    a.heads, ltx::EPI_STORE, nullptr, err))
+    return false;
+  const __nv_bfloat16* qh = _arp->sp_recv;
+  if (!_ops->attention(s, qh, Il, qh + blk, Il, qh + 2 * blk, Il, _arp->sp_send, Il, nullptr,
+                       0, tv, tv, hl, a.head_dim, err, _layer))
+    return false;
+  if (!_comm->alltoall_bf16(_arp->sp_send, _arp->sp_recv, (size_t)tl * Il, 1, 0, s, err))
+    return false;
+  if (ltx::launch_a2a_unpack(_arp->sp_recv, tl, N, Il, out, I, _arp->glog, a.heads,
+                             a.head_dim, s) != 0)
+    return fail(err, "all-to-all unpack launch failed");
+  return true;
+}
+
+bool CudaBlock::attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfloat16* xq,
+                               int tq, const RopeRef& qr, const __nv_bfloat16* xkv, int tl,
+                               const RopeRef& kr, __nv_bfloat16* out, std::string* err)
+{
+  // Audio queries (replicated) against the whole video sequence: this
+  // rank's video keys/values go to their heads' owners, each rank attends
+  // all audio queries for its heads, and the outputs are gathered.
+  const int I = a.inner, N = _sp_world, Il = I / N, tv = tl * N, hl = a.heads / N;
+  if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _arp->qkv, I, tq, a.qdim, I, ltx::EPI_STORE,
+                    nullptr, err) ||
+      !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _arp->kvp, 2 * I, tl, a.kvdim, 2 * I,
+                    ltx::EPI_STORE, nullptr, err))
+    return false;
+  if (ltx::launch_qk_norm_rope(_arp->qkv, I, _arp->qn, I, tq, a.heads, a.head_dim, a.q_norm,
+                               qr.cos, qr.sin, kEps, s, nullptr, 0, 0, qr.tbl_tokens,
+                               qr.tok0) != 0 ||
+      ltx::launch_qk_norm_rope(_arp->kvp, 2 * I, _arp->kn, I, tl, a.heads, a.head_dim,
+                               a.k_norm, kr.cos, kr.sin, kEps, s, nullptr, 0, 0, kr.tbl_tokens,
+                               kr.tok0) != 0)
+    return fail(err, "q/k norm + rope launch failed");
+  const size_t blk = (size_t)tv * Il;
+  if (ltx::launch_a2a_pack(_arp->kn, I, tl, N, Il, _arp->sp_send, s) != 0 ||
+      ltx::launch_a2a_pack(_arp->kvp + I, 2 * I, tl, N, Il, _arp->sp_send + blk, s) != 0)
+    return fail(err, "all-to-all pack launch failed");
+  if (!_comm->alltoall_bf16(_arp->sp_send, _arp->sp_recv, (size_t)tl * Il, 2, blk, s, err))
+    return false;
+  if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _arp->glog, a.heads, tq, a.qdim, a.heads,
+                    ltx::EPI_STORE, nullptr, err))
+    return false;
+  // this rank's heads of every audio query -> sp_send [rank][tq][Il]
+  __nv_bfloat16* mine = _arp->sp_send + (size_t)_sp_rank * tq * Il;
+  if (!_ops->attention(s, _arp->qn + (size_t)_sp_rank * Il, I, _arp->sp_recv, Il,
+                       _arp->sp_recv + blk, Il, mine, Il, nullptr, 0, tq, tv, hl,
+                       a.head_dim, err, _layer))
+    return false;
+  if (!_comm->allgather_bf16(mine, _arp->sp_send, (size_t)tq * Il, s, err)) return false;
+  if (ltx::launch_a2a_unpack(_arp->sp_send, tq, N, Il, out, I, _arp->glog, a.heads,
+                             a.head_dim, s) != 0)
+    return fail(err, "gather unpack launch failed");
   return true;
 }
 
@@ -536,8 +628,11 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
   if (ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_MSA + 1) * d,
                            mods + MOD_MSA * d, kEps, true, s))
     return fail(err, "ada_zero launch failed");
-  if (!attend_(s, w.attn1, _arp->normed, n, _arp->normed, n, io.pe_cos, io.pe_sin,
-               io.pe_cos, io.pe_sin, _arp->att, err))
+  const RopeRef self_r{io.pe_cos, io.pe_sin, io.tokens_all > 0 ? io.tokens_all : n, io.tok0};
+  const bool sp = _sp && &w == &_video;
+  if (sp ? !attend_self_sp_(s, w.attn1, _arp->normed, n, self_r, _arp->att, err)
+         : !attend_(s, w.attn1, _arp->normed, n, _arp->normed, n, self_r, self_r, _arp->att,
+                    err))
     return false;
   if (!out_proj_(s, _arp->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, n, d,
                  mods + (MOD_MSA + 2) * d, err))
@@ -550,8 +645,8 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                            mods + (MOD_PROMPT + 1) * d, mods + MOD_PROMPT * d,
                            kEps, false, s))
     return fail(err, "modulation launch failed");
-  if (!attend_(s, w.attn2, _arp->normed, n, _arp->ctxmod, io.text_tokens, nullptr,
-               nullptr, nullptr, nullptr, _arp->att, err))
+  if (!attend_(s, w.attn2, _arp->normed, n, _arp->ctxmod, io.text_tokens, RopeRef{},
+               RopeRef{}, _arp->att, err))
     return false;
   return out_proj_(s, _arp->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x, n, d,
                    mods + (MOD_CA + 2) * d, err);
@@ -574,8 +669,42 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                    mods + (MOD_MLP + 2) * d, err);
 }
 
-bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
-                        std::string* err)
+bool CudaBlock::shard_io(const StreamIO& whole, StreamIO* shard, std::string* err) const
+{
+  *shard = whole;
+  if (!_sp || !whole.present || whole.tokens <= 0) return true;
+  if (whole.tokens % _sp_world != 0)
+    return fail(err, "sequence parallel shape: " + std::to_string(whole.tokens) +
+                         " video tokens do not split over " + std::to_string(_sp_world) +
+                         " ranks");
+  const int tl = whole.tokens / _sp_world;
+  shard->x = whole.x + (size_t)_sp_rank * tl * _vdim;
+  shard->tokens = tl;
+  shard->tok0 = _sp_rank * tl;
+  shard->tokens_all = whole.tokens;
+  return true;
+}
+
+bool CudaBlock::gather_video(cudaStream_t s, const StreamIO& whole, std::string* err) const
+{
+  if (!_sp || !whole.present || whole.tokens <= 0) return true;
+  const size_t cnt = (size_t)(whole.tokens / _sp_world) * _vdim;
+  return _comm->allgather_bf16(whole.x + (size_t)_sp_rank * cnt, whole.x, cnt, s, err);
+}
+
+bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a, std::string* err)
+{
+  if (!_sp) return forward_impl_(s, v, a, err);
+  StreamIO vl;
+  return shard_io(v, &vl, err) && forward_impl_(s, vl, a, err) && gather_video(s, v, err);
+}
+
+bool CudaBlock::forward_shard(cudaStream_t s, StreamIO& v, StreamIO& a, std::string* err)
+{
+  return forward_impl_(s, v, a, err);
+}
+
+bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::string* err)
 {
   if (!_final) return fail(err, "forward before finalize");
   if (!_arp) return fail(err, "forward before reserve");
@@ -617,14 +746,17 @@ bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a,
                              vm + (MOD_AV + 3) * vd, kEps, true, s))
       return fail(err, "cross ada_zero launch failed");
     // a2v: video queries, audio keys/values
-    if (!attend_(s, _a2v, _arp->qv, v.tokens, _arp->kva, a.tokens, v.cpe_cos,
-                 v.cpe_sin, a.cpe_cos, a.cpe_sin, _arp->att, err) ||
+    const RopeRef vc{v.cpe_cos, v.cpe_sin, v.tokens_all > 0 ? v.tokens_all : v.tokens, v.tok0};
+    const RopeRef ac{a.cpe_cos, a.cpe_sin, a.tokens, 0};
+    if (!attend_(s, _a2v, _arp->qv, v.tokens, _arp->kva, a.tokens, vc, ac, _arp->att, err) ||
         !out_proj_(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, v.tokens, vd,
                    vm + MOD_AVG * vd, err))
       return false;
     // v2a: audio queries, video keys/values
-    if (!attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, v.tokens, a.cpe_cos,
-                 a.cpe_sin, v.cpe_cos, v.cpe_sin, _arp->att, err) ||
+    if ((_sp ? !attend_v2a_sp_(s, _v2a, _arp->qa, a.tokens, ac, _arp->kvv, v.tokens, vc,
+                               _arp->att, err)
+             : !attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, v.tokens, ac, vc, _arp->att,
+                        err)) ||
         !out_proj_(s, _arp->att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, a.tokens, ad,
                    am + MOD_AVG * ad, err))
       return false;

@@ -72,6 +72,16 @@ struct StreamIO {
   const float* cpe_sin = nullptr;
   int tokens = 0, text_tokens = 0;
   bool present = true;
+  // Sequence parallel: x holds tokens [tok0, tok0 + tokens) of tokens_all,
+  // which index the RoPE tables (0: this io is the whole sequence).
+  int tok0 = 0, tokens_all = 0;
+};
+
+// A RoPE table view: [heads][tbl_tokens][half] f32, rows read from tok0 on.
+struct RopeRef {
+  const float* cos = nullptr;
+  const float* sin = nullptr;
+  int tbl_tokens = 0, tok0 = 0;
 };
 
 // The scratch ONE block forward needs, shared by every block of a stack
@@ -85,7 +95,9 @@ struct BlockArena {
   float* mods = nullptr;      // adaLN rows, f32
   __nv_bfloat16* part = nullptr;   // row-split partial sums (tensor parallel)
   float* ssq = nullptr;            // per-token q/k sums of squares (tensor parallel)
-  size_t cap[16] = {};        // element capacity of each buffer above
+  __nv_bfloat16* sp_send = nullptr;   // all-to-all staging (sequence parallel)
+  __nv_bfloat16* sp_recv = nullptr;
+  size_t cap[18] = {};        // element capacity of each buffer above
   size_t video = 0, audio = 0, text = 0;   // reserved token maxima
   ~BlockArena();
   // Grow buffer i (in the order declared) to at least n elements.
@@ -120,9 +132,19 @@ public:
                std::shared_ptr<BlockArena> share = nullptr);
   const std::shared_ptr<BlockArena>& arena() const { return _arp; }
 
-  // Run the block; video.x / audio.x are updated in place.
+  // Run the block; video.x / audio.x are updated in place.  Sequence
+  // parallel: every rank passes the whole x and gets the whole x back.
   bool forward(cudaStream_t s, StreamIO& video, StreamIO& audio,
                std::string* err);
+  // Sequence parallel, for a stack: `video` is this rank's token shard
+  // (see shard_io); the caller gathers x once after the last block.
+  bool forward_shard(cudaStream_t s, StreamIO& video, StreamIO& audio, std::string* err);
+  bool sequence_parallel() const { return _sp; }
+  // This rank's shard of a whole-sequence video io; false (with err) when
+  // the tokens do not split evenly.
+  bool shard_io(const StreamIO& whole, StreamIO* shard, std::string* err) const;
+  // All-gather the video x shards back into the whole x on every rank.
+  bool gather_video(cudaStream_t s, const StreamIO& whole, std::string* err) const;
 
   bool finalized() const { return _final; }
   CudaOps* ops() const { return _ops; }
@@ -151,9 +173,17 @@ private:
                    std::string* err);
   bool build_stream_(bool audio, CudaStreamW& w, std::string* err);
   bool attend_(cudaStream_t s, const CudaAttn& a, const __nv_bfloat16* xq,
-               int tq, const __nv_bfloat16* xkv, int tkv, const float* qcos,
-               const float* qsin, const float* kcos, const float* ksin,
-               __nv_bfloat16* out, std::string* err);
+               int tq, const __nv_bfloat16* xkv, int tkv, const RopeRef& qr,
+               const RopeRef& kr, __nv_bfloat16* out, std::string* err);
+  // Sequence parallel: the video self-attention over the whole sequence
+  // (all-to-all to heads and back) and v2a (video keys to heads, outputs
+  // gathered); inputs are this rank's token rows.
+  bool attend_self_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfloat16* xq, int tl,
+                       const RopeRef& r, __nv_bfloat16* out, std::string* err);
+  bool attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfloat16* xq, int tq,
+                      const RopeRef& qr, const __nv_bfloat16* xkv, int tl,
+                      const RopeRef& kr, __nv_bfloat16* out, std::string* err);
+  bool forward_impl_(cudaStream_t s, StreamIO& video, StreamIO& audio, std::string* err);
   bool first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                    std::string* err);
   bool ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
@@ -183,6 +213,8 @@ private:
   int _vdim, _vheads, _adim, _aheads;
   const Comm* _comm = nullptr;   // set at finalize when the context is sharded
   int _tp_rank = 0, _tp_world = 1;
+  bool _sp = false;              // sequence parallel (weights whole)
+  int _sp_rank = 0, _sp_world = 1;
   std::map<std::string, Staged> _staged;
   std::vector<void*> _owned;   // device buffers this block frees
   CudaStreamW _video, _audio;

@@ -17,6 +17,11 @@ struct Nccl {
   decltype(&ncclCommDestroy) comm_destroy = nullptr;
   decltype(&ncclAllReduce) all_reduce = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
+  decltype(&ncclSend) send = nullptr;
+  decltype(&ncclRecv) recv = nullptr;
+  decltype(&ncclGroupStart) group_start = nullptr;
+  decltype(&ncclGroupEnd) group_end = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
   bool ok = false;
   std::string why;
 };
@@ -41,8 +46,14 @@ const Nccl& nccl()
     n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     n.all_reduce = reinterpret_cast<decltype(n.all_reduce)>(dlsym(h, "ncclAllReduce"));
     n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
+    n.send = reinterpret_cast<decltype(n.send)>(dlsym(h, "ncclSend"));
+    n.recv = reinterpret_cast<decltype(n.recv)>(dlsym(h, "ncclRecv"));
+    n.group_start = reinterpret_cast<decltype(n.group_start)>(dlsym(h, "ncclGroupStart"));
+    n.group_end = reinterpret_cast<decltype(n.group_end)>(dlsym(h, "ncclGroupEnd"));
+    n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
     n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce &&
-           n.error_string;
+           n.error_string && n.send && n.recv && n.group_start && n.group_end &&
+           n.all_gather;
     if (!n.ok) n.why = "NCCL library lacks a required symbol";
   });
   return n;
@@ -109,6 +120,36 @@ bool Comm::allreduce_sum(void* buf, size_t count, int dtype, cudaStream_t s,
   return nccl_ok(nccl().all_reduce(buf, buf, count, t, ncclSum,
                                    static_cast<ncclComm_t>(_comm), s),
                  "ncclAllReduce", err);
+}
+
+bool Comm::alltoall_bf16(const void* send, void* recv, size_t count, int n, size_t stride,
+                         cudaStream_t s, std::string* err) const
+{
+  if (_comm == nullptr || count == 0) return true;
+  const Nccl& nc = nccl();
+  const ncclComm_t c = static_cast<ncclComm_t>(_comm);
+  const size_t blk = count * 2;   // bytes per peer block
+  if (!nccl_ok(nc.group_start(), "ncclGroupStart", err)) return false;
+  bool ok = true;
+  for (int i = 0; i < n && ok; ++i) {
+    const char* sb = static_cast<const char*>(send) + i * stride * 2;
+    char* rb = static_cast<char*>(recv) + i * stride * 2;
+    for (int p = 0; p < _world && ok; ++p) {
+      ok = nccl_ok(nc.send(sb + p * blk, count, ncclBfloat16, p, c, s), "ncclSend", err) &&
+           nccl_ok(nc.recv(rb + p * blk, count, ncclBfloat16, p, c, s), "ncclRecv", err);
+    }
+  }
+  const bool ended = nccl_ok(nc.group_end(), "ncclGroupEnd", ok ? err : nullptr);
+  return ok && ended;
+}
+
+bool Comm::allgather_bf16(const void* send, void* recv, size_t count, cudaStream_t s,
+                          std::string* err) const
+{
+  if (_comm == nullptr || count == 0) return true;
+  return nccl_ok(nccl().all_gather(send, recv, count, ncclBfloat16,
+                                   static_cast<ncclComm_t>(_comm), s),
+                 "ncclAllGather", err);
 }
 
 }  // namespace ltx25

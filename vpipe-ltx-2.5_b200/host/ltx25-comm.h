@@ -26,6 +26,15 @@ public:
   // In-place sum over the group on `s`.  dtype: 0 = f32, 1 = bf16.
   bool allreduce_sum(void* buf, size_t count, int dtype, cudaStream_t s,
                      std::string* err) const;
+  // bf16 all-to-all: `count` elements to and from every rank; block p of
+  // `send` goes to rank p, block p of `recv` comes from rank p.  `n` such
+  // exchanges (send + i * stride, recv + i * stride) in one NCCL group.
+  bool alltoall_bf16(const void* send, void* recv, size_t count, int n, size_t stride,
+                     cudaStream_t s, std::string* err) const;
+  // bf16 all-gather: rank r's `count` elements land at recv + r * count
+  // (send may be recv + rank * count: in place).
+  bool allgather_bf16(const void* send, void* recv, size_t count, cudaStream_t s,
+                      std::string* err) const;
 
   int rank() const { return _rank; }
   int world() const { return _world; }

@@ -84,10 +84,16 @@ public:
   int num_sms() const { return _sms; }
   int* err_word() const { return _err_word; }
 
-  // Tensor parallelism: blocks finalized after this shard their weights
-  // over the group (rank, world); null comm = one GPU.
-  void set_comm(std::unique_ptr<Comm> c) { _comm = std::move(c); }
+  // Multi-GPU: blocks finalized after this either shard their weights over
+  // the group (tensor parallel) or keep them whole and shard the video
+  // tokens (sequence parallel, `sequence` true); null comm = one GPU.
+  void set_comm(std::unique_ptr<Comm> c, bool sequence = false)
+  {
+    _comm = std::move(c);
+    _sequence = sequence;
+  }
   const Comm* comm() const { return _comm.get(); }
+  bool sequence_parallel() const { return _comm != nullptr && _sequence; }
 
   // Diagnostics: every following GEMM writes per-CTA phase timestamps into
   // `buf` (16 u64 per CTA, first `ctas` CTAs); null turns it off.
@@ -152,6 +158,7 @@ private:
   int _attn_mode = -1;             // LTX25_ATTN: 0 = always warp-MMA
   int* _err_word = nullptr;
   std::unique_ptr<Comm> _comm;
+  bool _sequence = false;
   unsigned long long* _trace = nullptr;
   int _trace_ctas = 0;
 };

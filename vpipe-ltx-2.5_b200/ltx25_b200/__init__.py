@@ -50,6 +50,7 @@ SIGNATURES = {
     "ltx_launch_count": (ctypes.c_ulonglong, []),
     "ltx_tp_unique_id": (_I, [_P, _I]),
     "ltx_ctx_set_tp": (_I, [_P, _I, _I, _P]),
+    "ltx_ctx_set_sp": (_I, [_P, _I, _I, _P]),
     "ltx_tp_allreduce": (_I, [_P, _P, ctypes.c_size_t, _I, _P]),
     "ltx_set_route": (_I, [_P, _I]),
     "ltx_set_tiers": (_I, [_P, _I, _I, _I]),
@@ -193,6 +194,14 @@ class Context:
             buf = ctypes.create_string_buffer(bytes(uid), TP_ID_BYTES)
         self._ok(self.lib.ltx_ctx_set_tp(self.h, rank, world, buf), "set_tp")
         self.tp = (rank, world)
+
+    def set_sp(self, rank, world, uid=None):
+        """Join a sequence-parallel group (see ltx_ctx_set_sp)."""
+        buf = None
+        if world > 1:
+            buf = ctypes.create_string_buffer(bytes(uid), TP_ID_BYTES)
+        self._ok(self.lib.ltx_ctx_set_sp(self.h, rank, world, buf), "set_sp")
+        self.sp = (rank, world)
 
     def allreduce(self, t, stream=None):
         """In-place sum of a contiguous f32 or bf16 device tensor over the group."""
