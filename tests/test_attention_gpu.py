@@ -28,16 +28,19 @@ def reference(q, k, v, heads, gate=None):
     return o.reshape(tq, heads * D)
 
 
-@pytest.mark.parametrize("tq,tk,heads,gated,qscale", [
-    (128, 128, 1, False, 1.0), (129, 300, 2, True, 1.0), (1000, 777, 2, True, 1.0),
-    (1, 1, 1, False, 1.0), (5, 1000, 3, True, 1.0), (2048, 2048, 4, True, 1.0),
-    (8160, 256, 4, True, 1.0), (1500, 1500, 2, False, 6.0), (8160, 8160, 2, True, 1.0)])
-def test_tc_attention_matches_fp32(ctx, tq, tk, heads, gated, qscale):
+@pytest.mark.parametrize("tq,tk,heads,gated,qscale,D", [
+    (128, 128, 1, False, 1.0, 128), (129, 300, 2, True, 1.0, 128), (1000, 777, 2, True, 1.0, 128),
+    (1, 1, 1, False, 1.0, 128), (5, 1000, 3, True, 1.0, 128), (2048, 2048, 4, True, 1.0, 128),
+    (8160, 256, 4, True, 1.0, 128), (1500, 1500, 2, False, 6.0, 128),
+    (8160, 8160, 2, True, 1.0, 128),
+    # split over the keys (few query tiles): the video->audio shape and others
+    (126, 8160, 32, True, 1.0, 64), (126, 2000, 4, False, 6.0, 64), (100, 4000, 2, True, 1.0, 128),
+    (126, 8160, 4, True, 1.0, 64)])
+def test_tc_attention_matches_fp32(ctx, tq, tk, heads, gated, qscale, D):
     import torch
     import ltx25_b200 as L
     g = torch.Generator(device="cuda")
     g.manual_seed(tq * 31 + tk)
-    D = 128
     inner = heads * D
     q = (torch.randn((tq, inner), generator=g, device="cuda") * qscale).to(torch.bfloat16)
     kv = torch.randn((tk, 2 * inner), generator=g, device="cuda").to(torch.bfloat16)

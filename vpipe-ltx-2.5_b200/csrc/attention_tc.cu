@@ -77,6 +77,13 @@ struct FaParams {
   const float* sq;
   const float* sk;
   int nqb, tq_pad, tk_pad;
+  // split-KV (grid z > 1): each CTA covers key tiles [z n / splits,
+  // (z+1) n / splits) and leaves its unnormalized O and (max, sum) in
+  // part_o [split][tq][heads][D] / part_ml [split][tq][heads][2] (f32).
+  int splits;
+  float* part_o;
+  float* part_ml;
+  int heads;
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -122,7 +129,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const uint32_t lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * kFaBQ;
   const int h = blockIdx.y;
-  const int n = p.ntiles;
+  // key tiles [jb, jb + n) of p.ntiles (all of them unless split)
+  const int jb = (int)((long long)blockIdx.z * p.ntiles / p.splits);
+  const int n = (int)((long long)(blockIdx.z + 1) * p.ntiles / p.splits) - jb;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -172,15 +181,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         uint8_t* sk = s_kv + st * C::kStageBytes;
         uint8_t* sv = sk + C::kKBytes;
         mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
+        const int jg = jb + j;   // global key tile
         for (int a = 0; a < kQAtoms; ++a) {
           if constexpr (I8)
-            tma_load_2d(&tm_k, &k_full[st], sk, 0, h * p.tk_pad + j * kFaBK);
+            tma_load_2d(&tm_k, &k_full[st], sk, 0, h * p.tk_pad + jg * kFaBK);
           else
-            tma_load_2d(&tm_k, &k_full[st], sk + a * C::kAtom, h * D + a * 64, j * kFaBK);
+            tma_load_2d(&tm_k, &k_full[st], sk + a * C::kAtom, h * D + a * 64, jg * kFaBK);
         }
         mbar_arrive_expect_tx(&v_full[st], C::kVBytes);
         for (int a = 0; a < 2; ++a)
-          tma_load_2d(&tm_vt, &v_full[st], sv + a * C::kVAtom, j * kFaBK + a * 64, h * D);
+          tma_load_2d(&tm_vt, &v_full[st], sv + a * C::kVAtom, jg * kFaBK + a * 64, h * D);
         armed |= 1u << st;
         armed_par = (armed_par & ~(1u << st)) | (ph << st);
       }
@@ -277,8 +287,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       tmem_wait_ld();
       // exp2-domain factor of this tile's raw scores (the int8 path folds
       // in the key block's scale; the scales are positive)
-      const float c = I8 ? c0 * p.sk[h * p.ntiles + i] : c0;
-      const int valid = p.tk - i * kFaBK;
+      const float c = I8 ? c0 * p.sk[h * p.ntiles + jb + i] : c0;
+      const int valid = p.tk - (jb + i) * kFaBK;
       float mx = -3.0e38f;
 #pragma unroll
       for (int e = 0; e < kFaBK; ++e) {
@@ -331,7 +341,27 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
     }
-    if (ok && n > 0 &&
+    if (ok && n > 0 && p.splits > 1 &&
+        mbar_wait(o_done, (uint32_t)(n - 1) & 1u, s_abort, p.err, FERR_SOFTMAX)) {
+      // split-KV partial: unnormalized O and this split's (max, sum)
+      tc_fence_after();
+      const int row = q0 + r;
+      const size_t site = ((size_t)blockIdx.z * p.tq + row) * p.heads + h;
+      float* po = p.part_o + site * D;
+#pragma unroll
+      for (int c4 = 0; c4 < D / 32; ++c4) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + C::kOCol + (uint32_t)(c4 * 32), v);
+        tmem_wait_ld();
+        if (row < p.tq) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            *reinterpret_cast<uint4*>(po + c4 * 32 + 4 * e) =
+                make_uint4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+        }
+      }
+      if (row < p.tq) *reinterpret_cast<float2*>(p.part_ml + site * 2) = make_float2(m_run, l_run);
+    } else if (ok && n > 0 &&
         mbar_wait(o_done, (uint32_t)(n - 1) & 1u, s_abort, p.err, FERR_SOFTMAX)) {
       tc_fence_after();
       const int row = q0 + r;
@@ -708,6 +738,45 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// Merge split-KV partials: for each (row, head), weights 2^(m_s - max m),
+// o = sum_s w_s O_s / sum_s w_s l_s, times the gate; 4 columns per thread.
+__global__ void fa_combine_kernel(const float* __restrict__ part_o,
+                                  const float* __restrict__ part_ml, int splits, int tq,
+                                  int heads, int D, __nv_bfloat16* __restrict__ o, int ldo,
+                                  const __nv_bfloat16* __restrict__ gate, int ldg)
+{
+  const int d4 = D / 4;
+  const size_t total = (size_t)tq * heads * d4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % d4) * 4;
+    const size_t rh = i / d4;                 // row * heads + h
+    const int h = (int)(rh % heads), row = (int)(rh / heads);
+    float mx = -3.0e38f;
+    for (int sp = 0; sp < splits; ++sp)
+      mx = fmaxf(mx, part_ml[((size_t)sp * tq * heads + rh) * 2]);
+    float l = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (int sp = 0; sp < splits; ++sp) {
+      const size_t site = (size_t)sp * tq * heads + rh;
+      const float2 ml = *reinterpret_cast<const float2*>(part_ml + site * 2);
+      const float w = fast_exp2(ml.x - mx);
+      l += w * ml.y;
+      const float4 v = *reinterpret_cast<const float4*>(part_o + site * D + c);
+      a0 += w * v.x;
+      a1 += w * v.y;
+      a2 += w * v.z;
+      a3 += w * v.w;
+    }
+    float g = 1.0f / l;
+    if (gate != nullptr)
+      g *= 2.0f / (1.0f + __expf(-__bfloat162float(gate[(size_t)row * ldg + h])));
+    uint2 out;
+    out.x = pack_bf16(a0 * g, a1 * g);
+    out.y = pack_bf16(a2 * g, a3 * g);
+    *reinterpret_cast<uint2*>(o + (size_t)row * ldo + h * D + c) = out;
+  }
+}
+
 // vt[c][t] = v[t][c]: c < cols (= heads * D), t < tk.  64 x 64 tiles.
 __global__ void __launch_bounds__(256)
     transpose_kernel(const __nv_bfloat16* __restrict__ v, int ldv, int tk, int cols,
@@ -866,8 +935,9 @@ int launch_fa(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtens
       return -1;
     attr = true;
   }
-  fa_tc_kernel<D, I8><<<dim3((prm.tq + kFaBQ - 1) / kFaBQ, heads), kFaThreads, C::kSmem, s>>>(
-      tq_map, tk_map, tv_map, prm);
+  fa_tc_kernel<D, I8>
+      <<<dim3((prm.tq + kFaBQ - 1) / kFaBQ, heads, prm.splits), kFaThreads, C::kSmem, s>>>(
+          tq_map, tk_map, tv_map, prm);
   return launched();
 }
 
@@ -885,6 +955,7 @@ FaParams fa_params(__nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg
   prm.ntiles = (tk + kFaBK - 1) / kFaBK;
   prm.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
   prm.err = err;
+  prm.splits = 1;
   return prm;
 }
 
@@ -909,32 +980,68 @@ size_t attention_tc_scratch(int tk, int heads, int head_dim)
   return ldvt * (size_t)heads * head_dim;
 }
 
+int attention_tc_splits(int tq, int tk, int heads)
+{
+  const int ctas = (tq + kFaBQ - 1) / kFaBQ * heads;
+  const int n = (tk + kFaBK - 1) / kFaBK;
+  if (ctas >= 148 || n < 4) return 1;
+  int sp = (2 * 148 + ctas - 1) / ctas;
+  sp = sp > n / 2 ? n / 2 : sp;
+  return sp > 32 ? 32 : (sp < 1 ? 1 : sp);
+}
+
+size_t attention_tc_part(int tq, int tk, int heads, int head_dim)
+{
+  const int sp = attention_tc_splits(tq, tk, heads);
+  return sp > 1 ? (size_t)sp * tq * heads * (head_dim + 2) : 0;
+}
+
 int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k, int ldk,
                         const __nv_bfloat16* v, int ldv, __nv_bfloat16* vt,
                         size_t vt_elems, __nv_bfloat16* o, int ldo,
                         const __nv_bfloat16* gate, int ldg, int tq, int tk, int heads,
-                        int head_dim, int* err, cudaStream_t s)
+                        int head_dim, int* err, cudaStream_t s, float* part,
+                        size_t part_elems)
 {
   if (tq <= 0 || tk <= 0 || heads <= 0) return 0;
-  if (head_dim != 128) return -2;
+  if (head_dim != 128 && head_dim != 64) return -2;
   if ((ldq | ldk | ldv) % 8 != 0 || ldo % 8 != 0 || !aligned16(q) || !aligned16(k) ||
       !aligned16(v) || !aligned16(o))
     return -2;
   if (vt_elems < attention_tc_scratch(tk, heads, head_dim)) return -3;
-  constexpr int D = 128;
+  const int D = head_dim;
   const int cols = heads * D;
   CUtensorMap tq_map, tk_map, tv_map;
   if (prepare_vt(v, ldv, tk, cols, D, vt, &tv_map, s) != 0) return -1;
   if (!fa_encode(&tq_map, q, (uint64_t)cols, (uint64_t)tq, (uint64_t)ldq * 2, 64, kFaBQ) ||
       !fa_encode(&tk_map, k, (uint64_t)cols, (uint64_t)tk, (uint64_t)ldk * 2, 64, kFaBK))
     return -1;
-  const FaParams prm = fa_params(o, ldo, gate, ldg, tq, tk, D, err);
+  FaParams prm = fa_params(o, ldo, gate, ldg, tq, tk, D, err);
+  const int splits = attention_tc_splits(tq, tk, heads);
+  if (splits > 1) {
+    // few query tiles, many keys (video->audio): split the keys, merge after
+    if (part == nullptr || part_elems < attention_tc_part(tq, tk, heads, D)) return -3;
+    prm.splits = splits;
+    prm.heads = heads;
+    prm.part_o = part;
+    prm.part_ml = part + (size_t)splits * tq * heads * D;
+    const int rc = D == 128 ? launch_fa<128, false>(tq_map, tk_map, tv_map, prm, heads, s)
+                            : launch_fa<64, false>(tq_map, tk_map, tv_map, prm, heads, s);
+    if (rc != 0) return rc;
+    const size_t total = (size_t)tq * heads * (D / 4);
+    size_t grid = (total + 255) / 256;
+    if (grid > 148 * 8) grid = 148 * 8;
+    fa_combine_kernel<<<(unsigned)grid, 256, 0, s>>>(prm.part_o, prm.part_ml, splits, tq, heads,
+                                                     D, o, ldo, gate, ldg);
+    return launched();
+  }
+  if (D == 64) return launch_fa<64, false>(tq_map, tk_map, tv_map, prm, heads, s);
   static int two_tiles = -1;
   if (two_tiles < 0) {
     const char* e = getenv("LTX25_FA_TILES");
     two_tiles = (e != nullptr && e[0] == '1') ? 0 : 1;
   }
-  if (tq <= kFaBQ || !two_tiles) return launch_fa<D, false>(tq_map, tk_map, tv_map, prm, heads, s);
+  if (tq <= kFaBQ || !two_tiles) return launch_fa<128, false>(tq_map, tk_map, tv_map, prm, heads, s);
   static bool attr2 = false;
   if (!attr2) {
     if (cudaFuncSetAttribute(fa2_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -67,16 +67,21 @@ int launch_attention(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
                      int ldg, int tq, int tk, int heads, int head_dim,
                      cudaStream_t s);
 
-// tcgen05 flash attention for head_dim 128 (attention_tc.cu): the same
+// tcgen05 flash attention for head_dim 128 / 64 (attention_tc.cu): the same
 // contract as launch_attention plus a V^T scratch of
 // attention_tc_scratch(tk, heads, head_dim) elements and the context's error
 // word for bounded waits.  q, k, v, o 16-byte aligned, strides % 8 == 0.
 size_t attention_tc_scratch(int tk, int heads, int head_dim);
+// Key splits the kernel will use (few query tiles and many keys: > 1, with
+// f32 partials of attention_tc_part elements merged by a second kernel).
+int attention_tc_splits(int tq, int tk, int heads);
+size_t attention_tc_part(int tq, int tk, int heads, int head_dim);
 int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k, int ldk,
                         const __nv_bfloat16* v, int ldv, __nv_bfloat16* vt,
                         size_t vt_elems, __nv_bfloat16* o, int ldo,
                         const __nv_bfloat16* gate, int ldg, int tq, int tk, int heads,
-                        int head_dim, int* err, cudaStream_t s);
+                        int head_dim, int* err, cudaStream_t s, float* part = nullptr,
+                        size_t part_elems = 0);
 
 // The sage tier (int8 QK^T, one scale per 128-token block, K smoothed by
 // its per-channel mean; P V in bf16): scratch sizes in elements and the

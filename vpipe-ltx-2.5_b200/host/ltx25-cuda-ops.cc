@@ -89,6 +89,7 @@ CudaOps::~CudaOps()
   cudaFree(_sx);
   cudaFree(_deq);
   cudaFree(_vt);
+  cudaFree(_part);
   cudaFree(_sb.qi8);
   cudaFree(_sb.ki8);
   cudaFree(_sb.scales);
@@ -367,6 +368,19 @@ bool CudaOps::reserve_sage(int tq, int tk, int heads, int head_dim, std::string*
   return true;
 }
 
+bool CudaOps::reserve_split(int tq, int tk, int heads, int head_dim, std::string* err)
+{
+  const size_t part = ltx::attention_tc_part(tq, tk, heads, head_dim);
+  if (part <= _part_elems) return true;
+  cudaFree(_part);
+  _part = nullptr;
+  _part_elems = 0;
+  if (!cuda_ok(cudaMalloc(&_part, part * sizeof(float)), "cudaMalloc(attention partials)", err))
+    return false;
+  _part_elems = part;
+  return true;
+}
+
 bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
                         const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v,
                         int ldv, __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate,
@@ -382,10 +396,16 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
     if (!reserve_sage(tq, tk, heads, head_dim, err)) return false;
     rc = ltx::launch_sage_tc(q, ldq, k, ldk, v, ldv, _sb, o, ldo, gate, ldg, tq, tk, heads,
                              head_dim, _err_word, s);
-  } else if (head_dim == 128 && _attn_mode == 1) {
+  } else if (_attn_mode == 1 &&
+             (head_dim == 128 ||
+              (head_dim == 64 && ltx::attention_tc_splits(tq, tk, heads) > 1))) {
+    // tcgen05 kernel: every head_dim-128 attention, and the head_dim-64 ones
+    // with few query tiles over many keys (video->audio), which it splits
+    // over the keys; the other head_dim-64 ones stay on the warp-MMA kernel.
     if (!reserve_attention(tk, heads * head_dim, err)) return false;
+    if (!reserve_split(tq, tk, heads, head_dim, err)) return false;
     rc = ltx::launch_attention_tc(q, ldq, k, ldk, v, ldv, _vt, _vt_elems, o, ldo, gate, ldg,
-                                  tq, tk, heads, head_dim, _err_word, s);
+                                  tq, tk, heads, head_dim, _err_word, s, _part, _part_elems);
   } else {
     rc = ltx::launch_attention(q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, heads,
                                head_dim, s);

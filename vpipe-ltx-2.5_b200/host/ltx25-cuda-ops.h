@@ -127,6 +127,8 @@ public:
     return layer >= 0 && layer >= _sage_dense && sage_takes(head_dim);
   }
   bool reserve_sage(int tq, int tk, int heads, int head_dim, std::string* err);
+  // Pre-size the split-KV partials for an attention of this shape.
+  bool reserve_split(int tq, int tk, int heads, int head_dim, std::string* err);
   // Pre-size the attention scratch for up to `keys` keys x `width` columns.
   bool reserve_attention(int keys, int width, std::string* err);
 
@@ -154,6 +156,8 @@ private:
   size_t _deq_bytes = 0;
   __nv_bfloat16* _vt = nullptr;    // attention: V^T
   size_t _vt_elems = 0;
+  float* _part = nullptr;          // attention: split-KV partials
+  size_t _part_elems = 0;
   ltx::SageBuffers _sb;            // sage tier: int8 Q/K, scales, key mean
   int _attn_mode = -1;             // LTX25_ATTN: 0 = always warp-MMA
   int* _err_word = nullptr;
