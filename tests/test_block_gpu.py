@@ -218,3 +218,34 @@ def test_block_refuses_partial_weights(ctx):
     assert "audio_attn2.k_norm.weight" in str(e.value)
     with pytest.raises(L.LtxError):
         blk.reserve(8, 8, 8)
+
+
+def test_side_stream_is_bit_identical(ctx):
+    """The audio stream on the side CUDA stream (the default) gives the same
+    bits as the whole block issued on one stream."""
+    import os
+    import torch
+    import subprocess
+    import sys
+    import json
+    code = r"""
+import os, sys, json, numpy as np
+sys.path[:0] = %r
+import torch, ltx25_b200 as L
+from test_block_gpu import build, to_dev, host, SMALL
+ctx = L.Context(0)
+blk, ow, ins = build(ctx, SMALL, seed=31, grid=(2, 3, 4))
+dv, da = to_dev(ins["video"]), to_dev(ins["audio"])
+blk.forward(dv, da); torch.cuda.synchronize(); ctx.check()
+np.save(sys.argv[1] + "_v.npy", host(dv["x"])); np.save(sys.argv[1] + "_a.npy", host(da["x"]))
+""" % (sys.path,)
+    import tempfile
+    d = tempfile.mkdtemp()
+    outs = []
+    for flag in ("1", "0"):
+        env = dict(os.environ, LTX25_SIDE_STREAM=flag)
+        base = os.path.join(d, "side" + flag)
+        subprocess.run([sys.executable, "-c", code, base], check=True, env=env,
+                       cwd=os.path.dirname(os.path.abspath(__file__)))
+        outs.append((np.load(base + "_v.npy"), np.load(base + "_a.npy")))
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])

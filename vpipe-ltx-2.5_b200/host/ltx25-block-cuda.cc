@@ -435,6 +435,17 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   _arp = share ? share : std::make_shared<BlockArena>();
   for (int i = 0; i < 18; ++i)
     if (!_arp->ensure(i, need[i], err)) return false;
+  // The audio stream's own buffers, so that it can run beside the video
+  // stream on a second CUDA stream (shared by the blocks like the rest).
+  {
+    const size_t na[18] = {
+        at * ad, mx({at * 3 * ad, at * ai}), at * ad, mx({at * ad, tt * ad, at * ai}),
+        at * ad, at * (size_t)_aheads, tt * ad, mx({tt * 2 * ad, at * 2 * ai}),
+        at * (size_t)_audio.ff_hidden, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+    if (!_arp->side) _arp->side = std::make_shared<BlockArena>();
+    for (int i = 0; i < 18; ++i)
+      if (!_arp->side->ensure(i, na[i], err)) return false;
+  }
   _arp->video = std::max(_arp->video, vt);
   _arp->audio = std::max(_arp->audio, at);
   _arp->text = std::max(_arp->text, tt);
@@ -463,22 +474,22 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   const __nv_bfloat16 *qraw, *kraw, *vraw;
   int ldq, ldkv;
   if (a.self) {
-    if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _arp->qkv, 3 * I, tq, a.qdim,
+    if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _cur->qkv, 3 * I, tq, a.qdim,
                       3 * I, ltx::EPI_STORE, nullptr, err))
       return false;
-    qraw = _arp->qkv;
-    kraw = _arp->qkv + I;
-    vraw = _arp->qkv + 2 * I;
+    qraw = _cur->qkv;
+    kraw = _cur->qkv + I;
+    vraw = _cur->qkv + 2 * I;
     ldq = ldkv = 3 * I;
   } else {
-    if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _arp->qkv, I, tq, a.qdim, I,
+    if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _cur->qkv, I, tq, a.qdim, I,
                       ltx::EPI_STORE, nullptr, err) ||
-        !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _arp->kvp, 2 * I, tkv,
+        !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _cur->kvp, 2 * I, tkv,
                       a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err))
       return false;
-    qraw = _arp->qkv;
-    kraw = _arp->kvp;
-    vraw = _arp->kvp + I;
+    qraw = _cur->qkv;
+    kraw = _cur->kvp;
+    vraw = _cur->kvp + I;
     ldq = I;
     ldkv = 2 * I;
   }
@@ -486,28 +497,28 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   // reduces the per-token sums of squares (q rows then k rows) first.
   const float *qss = nullptr, *kss = nullptr;
   if (a.norm_width != I) {
-    if (ltx::launch_row_sumsq(qraw, ldq, tq, I, _arp->ssq, s) != 0 ||
-        ltx::launch_row_sumsq(kraw, ldkv, tkv, I, _arp->ssq + tq, s) != 0)
+    if (ltx::launch_row_sumsq(qraw, ldq, tq, I, _cur->ssq, s) != 0 ||
+        ltx::launch_row_sumsq(kraw, ldkv, tkv, I, _cur->ssq + tq, s) != 0)
       return fail(err, "q/k sum-of-squares launch failed");
-    if (!_comm->allreduce_sum(_arp->ssq, (size_t)tq + tkv, 0, s, err)) return false;
-    qss = _arp->ssq;
-    kss = _arp->ssq + tq;
+    if (!_comm->allreduce_sum(_cur->ssq, (size_t)tq + tkv, 0, s, err)) return false;
+    qss = _cur->ssq;
+    kss = _cur->ssq + tq;
   }
-  if (ltx::launch_qk_norm_rope(qraw, ldq, _arp->qn, I, tq, a.heads, a.head_dim,
+  if (ltx::launch_qk_norm_rope(qraw, ldq, _cur->qn, I, tq, a.heads, a.head_dim,
                                a.q_norm, qr.cos, qr.sin, kEps, s, qss, a.norm_width,
                                a.head0, qr.tbl_tokens, qr.tok0) != 0 ||
-      ltx::launch_qk_norm_rope(kraw, ldkv, _arp->kn, I, tkv, a.heads,
+      ltx::launch_qk_norm_rope(kraw, ldkv, _cur->kn, I, tkv, a.heads,
                                a.head_dim, a.k_norm, kr.cos, kr.sin, kEps, s, kss,
                                a.norm_width, a.head0, kr.tbl_tokens, kr.tok0) != 0)
     return fail(err, "q/k norm + rope launch failed");
   const __nv_bfloat16* glog = nullptr;
   if (a.gate.N > 0) {
-    if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _arp->glog, a.heads, tq,
+    if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _cur->glog, a.heads, tq,
                       a.qdim, a.heads, ltx::EPI_STORE, nullptr, err))
       return false;
-    glog = _arp->glog;
+    glog = _cur->glog;
   }
-  if (!_ops->attention(s, _arp->qn, I, _arp->kn, I, vraw, ldkv, out, I, glog, a.heads, tq,
+  if (!_ops->attention(s, _cur->qn, I, _cur->kn, I, vraw, ldkv, out, I, glog, a.heads, tq,
                        tkv, a.heads, a.head_dim, err, _layer))
     return false;
   return true;
@@ -521,34 +532,34 @@ bool CudaBlock::attend_self_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bf
   // ALL heads, then an all-to-all to the whole sequence for this rank's
   // heads, attention, and an all-to-all back (DeepSpeed-Ulysses layout).
   const int I = a.inner, N = _sp_world, Il = I / N, tv = tl * N, hl = a.heads / N;
-  if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _arp->qkv, 3 * I, tl, a.qdim, 3 * I,
+  if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _cur->qkv, 3 * I, tl, a.qdim, 3 * I,
                     ltx::EPI_STORE, nullptr, err))
     return false;
-  if (ltx::launch_qk_norm_rope(_arp->qkv, 3 * I, _arp->qn, I, tl, a.heads, a.head_dim,
+  if (ltx::launch_qk_norm_rope(_cur->qkv, 3 * I, _cur->qn, I, tl, a.heads, a.head_dim,
                                a.q_norm, r.cos, r.sin, kEps, s, nullptr, 0, 0, r.tbl_tokens,
                                r.tok0) != 0 ||
-      ltx::launch_qk_norm_rope(_arp->qkv + I, 3 * I, _arp->kn, I, tl, a.heads, a.head_dim,
+      ltx::launch_qk_norm_rope(_cur->qkv + I, 3 * I, _cur->kn, I, tl, a.heads, a.head_dim,
                                a.k_norm, r.cos, r.sin, kEps, s, nullptr, 0, 0, r.tbl_tokens,
                                r.tok0) != 0)
     return fail(err, "q/k norm + rope launch failed");
   const size_t blk = (size_t)tv * Il;   // one of q, k, v for this rank's heads
-  if (ltx::launch_a2a_pack(_arp->qn, I, tl, N, Il, _arp->sp_send, s) != 0 ||
-      ltx::launch_a2a_pack(_arp->kn, I, tl, N, Il, _arp->sp_send + blk, s) != 0 ||
-      ltx::launch_a2a_pack(_arp->qkv + 2 * I, 3 * I, tl, N, Il, _arp->sp_send + 2 * blk, s) != 0)
+  if (ltx::launch_a2a_pack(_cur->qn, I, tl, N, Il, _cur->sp_send, s) != 0 ||
+      ltx::launch_a2a_pack(_cur->kn, I, tl, N, Il, _cur->sp_send + blk, s) != 0 ||
+      ltx::launch_a2a_pack(_cur->qkv + 2 * I, 3 * I, tl, N, Il, _cur->sp_send + 2 * blk, s) != 0)
     return fail(err, "all-to-all pack launch failed");
-  if (!_comm->alltoall_bf16(_arp->sp_send, _arp->sp_recv, (size_t)tl * Il, 3, blk, s, err))
+  if (!_comm->alltoall_bf16(_cur->sp_send, _cur->sp_recv, (size_t)tl * Il, 3, blk, s, err))
     return false;
   // gate logits of this rank's tokens, all heads (applied on the way back)
-  if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _arp->glog, a.heads, tl, a.qdim,
+  if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _cur->glog, a.heads, tl, a.qdim,
                     a.heads, ltx::EPI_STORE, nullptr, err))
     return false;
-  const __nv_bfloat16* qh = _arp->sp_recv;
-  if (!_ops->attention(s, qh, Il, qh + blk, Il, qh + 2 * blk, Il, _arp->sp_send, Il, nullptr,
+  const __nv_bfloat16* qh = _cur->sp_recv;
+  if (!_ops->attention(s, qh, Il, qh + blk, Il, qh + 2 * blk, Il, _cur->sp_send, Il, nullptr,
                        0, tv, tv, hl, a.head_dim, err, _layer))
     return false;
-  if (!_comm->alltoall_bf16(_arp->sp_send, _arp->sp_recv, (size_t)tl * Il, 1, 0, s, err))
+  if (!_comm->alltoall_bf16(_cur->sp_send, _cur->sp_recv, (size_t)tl * Il, 1, 0, s, err))
     return false;
-  if (ltx::launch_a2a_unpack(_arp->sp_recv, tl, N, Il, out, I, _arp->glog, a.heads,
+  if (ltx::launch_a2a_unpack(_cur->sp_recv, tl, N, Il, out, I, _cur->glog, a.heads,
                              a.head_dim, s) != 0)
     return fail(err, "all-to-all unpack launch failed");
   return true;
@@ -562,35 +573,35 @@ bool CudaBlock::attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfl
   // rank's video keys/values go to their heads' owners, each rank attends
   // all audio queries for its heads, and the outputs are gathered.
   const int I = a.inner, N = _sp_world, Il = I / N, tv = tl * N, hl = a.heads / N;
-  if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _arp->qkv, I, tq, a.qdim, I, ltx::EPI_STORE,
+  if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _cur->qkv, I, tq, a.qdim, I, ltx::EPI_STORE,
                     nullptr, err) ||
-      !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _arp->kvp, 2 * I, tl, a.kvdim, 2 * I,
+      !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _cur->kvp, 2 * I, tl, a.kvdim, 2 * I,
                     ltx::EPI_STORE, nullptr, err))
     return false;
-  if (ltx::launch_qk_norm_rope(_arp->qkv, I, _arp->qn, I, tq, a.heads, a.head_dim, a.q_norm,
+  if (ltx::launch_qk_norm_rope(_cur->qkv, I, _cur->qn, I, tq, a.heads, a.head_dim, a.q_norm,
                                qr.cos, qr.sin, kEps, s, nullptr, 0, 0, qr.tbl_tokens,
                                qr.tok0) != 0 ||
-      ltx::launch_qk_norm_rope(_arp->kvp, 2 * I, _arp->kn, I, tl, a.heads, a.head_dim,
+      ltx::launch_qk_norm_rope(_cur->kvp, 2 * I, _cur->kn, I, tl, a.heads, a.head_dim,
                                a.k_norm, kr.cos, kr.sin, kEps, s, nullptr, 0, 0, kr.tbl_tokens,
                                kr.tok0) != 0)
     return fail(err, "q/k norm + rope launch failed");
   const size_t blk = (size_t)tv * Il;
-  if (ltx::launch_a2a_pack(_arp->kn, I, tl, N, Il, _arp->sp_send, s) != 0 ||
-      ltx::launch_a2a_pack(_arp->kvp + I, 2 * I, tl, N, Il, _arp->sp_send + blk, s) != 0)
+  if (ltx::launch_a2a_pack(_cur->kn, I, tl, N, Il, _cur->sp_send, s) != 0 ||
+      ltx::launch_a2a_pack(_cur->kvp + I, 2 * I, tl, N, Il, _cur->sp_send + blk, s) != 0)
     return fail(err, "all-to-all pack launch failed");
-  if (!_comm->alltoall_bf16(_arp->sp_send, _arp->sp_recv, (size_t)tl * Il, 2, blk, s, err))
+  if (!_comm->alltoall_bf16(_cur->sp_send, _cur->sp_recv, (size_t)tl * Il, 2, blk, s, err))
     return false;
-  if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _arp->glog, a.heads, tq, a.qdim, a.heads,
+  if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _cur->glog, a.heads, tq, a.qdim, a.heads,
                     ltx::EPI_STORE, nullptr, err))
     return false;
   // this rank's heads of every audio query -> sp_send [rank][tq][Il]
-  __nv_bfloat16* mine = _arp->sp_send + (size_t)_sp_rank * tq * Il;
-  if (!_ops->attention(s, _arp->qn + (size_t)_sp_rank * Il, I, _arp->sp_recv, Il,
-                       _arp->sp_recv + blk, Il, mine, Il, nullptr, 0, tq, tv, hl,
+  __nv_bfloat16* mine = _cur->sp_send + (size_t)_sp_rank * tq * Il;
+  if (!_ops->attention(s, _cur->qn + (size_t)_sp_rank * Il, I, _cur->sp_recv, Il,
+                       _cur->sp_recv + blk, Il, mine, Il, nullptr, 0, tq, tv, hl,
                        a.head_dim, err, _layer))
     return false;
-  if (!_comm->allgather_bf16(mine, _arp->sp_send, (size_t)tq * Il, s, err)) return false;
-  if (ltx::launch_a2a_unpack(_arp->sp_send, tq, N, Il, out, I, _arp->glog, a.heads,
+  if (!_comm->allgather_bf16(mine, _cur->sp_send, (size_t)tq * Il, s, err)) return false;
+  if (ltx::launch_a2a_unpack(_cur->sp_send, tq, N, Il, out, I, _cur->glog, a.heads,
                              a.head_dim, s) != 0)
     return fail(err, "gather unpack launch failed");
   return true;
@@ -605,11 +616,11 @@ bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
     return _ops->linear(s, in, k, w, bias, x, d, n, k, d, ltx::EPI_GATED_RES, gate, err);
   // Row split: this rank's K columns give a partial product; the sum over
   // ranks, then the bias and the gated residual, once.
-  if (!_ops->linear(s, in, k, w, nullptr, _arp->part, d, n, k, d, ltx::EPI_STORE,
+  if (!_ops->linear(s, in, k, w, nullptr, _cur->part, d, n, k, d, ltx::EPI_STORE,
                     nullptr, err) ||
-      !_comm->allreduce_sum(_arp->part, (size_t)n * d, 1, s, err))
+      !_comm->allreduce_sum(_cur->part, (size_t)n * d, 1, s, err))
     return false;
-  if (ltx::launch_gated_residual(x, d, _arp->part, bias, gate, n, d, s) != 0)
+  if (ltx::launch_gated_residual(x, d, _cur->part, bias, gate, n, d, s) != 0)
     return fail(err, "gated residual launch failed");
   return true;
 }
@@ -627,30 +638,30 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                           mods + MOD_PROMPT * d, 2 * d, s))
     return fail(err, "adaLN rows launch failed");
   // normed = rms_norm(x) * (1 + scale) + shift;  x += gate * attn1(normed)
-  if (ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_MSA + 1) * d,
+  if (ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_MSA + 1) * d,
                            mods + MOD_MSA * d, kEps, true, s))
     return fail(err, "ada_zero launch failed");
   const RopeRef self_r{io.pe_cos, io.pe_sin, io.tokens_all > 0 ? io.tokens_all : n, io.tok0};
   const bool sp = _sp && &w == &_video;
-  if (sp ? !attend_self_sp_(s, w.attn1, _arp->normed, n, self_r, _arp->att, err)
-         : !attend_(s, w.attn1, _arp->normed, n, _arp->normed, n, self_r, self_r, _arp->att,
+  if (sp ? !attend_self_sp_(s, w.attn1, _cur->normed, n, self_r, _cur->att, err)
+         : !attend_(s, w.attn1, _cur->normed, n, _cur->normed, n, self_r, self_r, _cur->att,
                     err))
     return false;
-  if (!out_proj_(s, _arp->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, n, d,
+  if (!out_proj_(s, _cur->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, n, d,
                  mods + (MOD_MSA + 2) * d, err))
     return false;
   // Text cross-attention: query = mod(rms_norm(x)) (= ada_zero with the
   // cross rows), key/value = context modulated by the prompt table + driver.
-  if (ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_CA + 1) * d,
+  if (ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_CA + 1) * d,
                            mods + MOD_CA * d, kEps, true, s) ||
-      ltx::launch_ada_zero(io.context, d, _arp->ctxmod, d, io.text_tokens, d,
+      ltx::launch_ada_zero(io.context, d, _cur->ctxmod, d, io.text_tokens, d,
                            mods + (MOD_PROMPT + 1) * d, mods + MOD_PROMPT * d,
                            kEps, false, s))
     return fail(err, "modulation launch failed");
-  if (!attend_(s, w.attn2, _arp->normed, n, _arp->ctxmod, io.text_tokens, RopeRef{},
-               RopeRef{}, _arp->att, err))
+  if (!attend_(s, w.attn2, _cur->normed, n, _cur->ctxmod, io.text_tokens, RopeRef{},
+               RopeRef{}, _cur->att, err))
     return false;
-  return out_proj_(s, _arp->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x, n, d,
+  return out_proj_(s, _cur->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x, n, d,
                    mods + (MOD_CA + 2) * d, err);
 }
 
@@ -662,12 +673,12 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
   float* mods = _arp->mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
   if (ltx::launch_vec_add(w.scale_shift + 3 * d, io.timesteps ? io.timesteps + 3 * d : nullptr,
                           mods + MOD_MLP * d, 3 * d, s) ||
-      ltx::launch_ada_zero(io.x, d, _arp->normed, d, n, d, mods + (MOD_MLP + 1) * d,
+      ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_MLP + 1) * d,
                            mods + MOD_MLP * d, kEps, true, s))
     return fail(err, "ff pre-norm launch failed");
-  return _ops->linear(s, _arp->normed, d, w.ff_in, w.ff_in_b, _arp->ff, w.ff_hidden, n,
+  return _ops->linear(s, _cur->normed, d, w.ff_in, w.ff_in_b, _cur->ff, w.ff_hidden, n,
                       d, w.ff_hidden, ltx::EPI_GELU, nullptr, err) &&
-         out_proj_(s, _arp->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, n, d,
+         out_proj_(s, _cur->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, n, d,
                    mods + (MOD_MLP + 2) * d, err);
 }
 
@@ -723,8 +734,18 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
     if (on && (io->x == nullptr || io->context == nullptr || io->timesteps == nullptr))
       return fail(err, "stream input missing x, context or timesteps");
   }
+  // The audio stream runs beside the video one on the context's second
+  // CUDA stream while they are independent (first halves, feed-forwards),
+  // when nothing it launches shares scratch or a communicator with video.
+  const bool conc = rv && ra && _tp_world == 1 && _ops->audio_side_ok(a.tokens, a.text_tokens, _aheads, _adim / _aheads, _layer);
+  cudaStream_t sa = conc ? _ops->aux_stream(err) : s;
+  if (conc && sa == nullptr) return false;
+  if (conc && !_ops->fork(s, sa, 0, err)) return false;
+  _cur = conc ? _arp->side.get() : _arp.get();
+  if (ra && !first_half_(sa, _audio, a, err)) return false;
+  _cur = _arp.get();
   if (rv && !first_half_(s, _video, v, err)) return false;
-  if (ra && !first_half_(s, _audio, a, err)) return false;
+  if (conc && !_ops->fork(sa, s, 1, err)) return false;
 
   if (rv && ra) {
     // src/ltx25-block-ref.cc:336-385.  Both directions read the PRE-cross
@@ -764,8 +785,12 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
       return false;
   }
 
+  if (conc && !_ops->fork(s, sa, 2, err)) return false;
+  _cur = conc ? _arp->side.get() : _arp.get();
+  if (ra && !ff_(sa, _audio, a, err)) return false;
+  _cur = _arp.get();
   if (rv && !ff_(s, _video, v, err)) return false;
-  if (ra && !ff_(s, _audio, a, err)) return false;
+  if (conc && !_ops->fork(sa, s, 3, err)) return false;
   return true;
 }
 

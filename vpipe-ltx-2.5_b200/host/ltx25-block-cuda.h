@@ -98,6 +98,7 @@ struct BlockArena {
   __nv_bfloat16* sp_send = nullptr;   // all-to-all staging (sequence parallel)
   __nv_bfloat16* sp_recv = nullptr;
   size_t cap[18] = {};        // element capacity of each buffer above
+  std::shared_ptr<BlockArena> side;    // the audio stream's own buffers (side stream)
   size_t video = 0, audio = 0, text = 0;   // reserved token maxima
   ~BlockArena();
   // Grow buffer i (in the order declared) to at least n elements.
@@ -223,6 +224,7 @@ private:
   int _layer = 0;
 
   std::shared_ptr<BlockArena> _arp;
+  BlockArena* _cur = nullptr;    // the buffers the stream being issued uses
 };
 
 }  // namespace ltx25

@@ -88,6 +88,9 @@ CudaOps::~CudaOps()
   cudaFree(_xq);
   cudaFree(_sx);
   cudaFree(_deq);
+  for (cudaEvent_t e : _ev)
+    if (e != nullptr) cudaEventDestroy(e);
+  if (_aux != nullptr) cudaStreamDestroy(_aux);
   cudaFree(_vt);
   cudaFree(_part);
   cudaFree(_sb.qi8);
@@ -366,6 +369,41 @@ bool CudaOps::reserve_sage(int tq, int tk, int heads, int head_dim, std::string*
   _sb.vt = _vt;
   _sb.cap.vt = _vt_elems;
   return true;
+}
+
+cudaStream_t CudaOps::aux_stream(std::string* err)
+{
+  if (_aux != nullptr) return _aux;
+  int lo = 0, hi = 0;
+  cudaDeviceGetStreamPriorityRange(&lo, &hi);
+  if (!cuda_ok(cudaStreamCreateWithPriority(&_aux, cudaStreamNonBlocking, hi), "aux stream", err))
+    return nullptr;
+  for (cudaEvent_t& e : _ev)
+    if (!cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "aux events", err))
+      return nullptr;
+  return _aux;
+}
+
+bool CudaOps::fork(cudaStream_t from, cudaStream_t to, int slot, std::string* err)
+{
+  return cuda_ok(cudaEventRecord(_ev[slot], from), "event record", err) &&
+         cuda_ok(cudaStreamWaitEvent(to, _ev[slot], 0), "stream wait", err);
+}
+
+bool CudaOps::audio_side_ok(int tokens, int text_tokens, int heads, int head_dim,
+                            int layer) const
+{
+  static const bool off = [] {
+    const char* e = getenv("LTX25_SIDE_STREAM");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (off) return false;
+  const int m = std::max(tokens, text_tokens);
+  if (m >= LTX_DEQUANT_MIN_M || (_i8 && m >= 1024) || _route == Route::DequantOnce) return false;
+  if (sage_for(layer, head_dim)) return false;
+  if (head_dim == 128) return false;   // would take the tcgen05 kernel and its scratch
+  return ltx::attention_tc_splits(tokens, tokens, heads) == 1 &&
+         ltx::attention_tc_splits(tokens, text_tokens, heads) == 1;
 }
 
 bool CudaOps::reserve_split(int tq, int tk, int heads, int head_dim, std::string* err)

@@ -127,6 +127,14 @@ public:
     return layer >= 0 && layer >= _sage_dense && sage_takes(head_dim);
   }
   bool reserve_sage(int tq, int tk, int heads, int head_dim, std::string* err);
+  // A second stream (highest priority) and events for running a block's
+  // audio stream beside its video stream.  fork(a, b, i): b waits for what
+  // a has issued so far (event slot i).
+  cudaStream_t aux_stream(std::string* err);
+  bool fork(cudaStream_t from, cudaStream_t to, int slot, std::string* err);
+  // True when an audio stream of this geometry launches nothing that uses
+  // the context's scratch (fused GEMMs only, warp-MMA attentions, no tier).
+  bool audio_side_ok(int tokens, int text_tokens, int heads, int head_dim, int layer) const;
   // Pre-size the split-KV partials for an attention of this shape.
   bool reserve_split(int tq, int tk, int heads, int head_dim, std::string* err);
   // Pre-size the attention scratch for up to `keys` keys x `width` columns.
@@ -156,6 +164,8 @@ private:
   size_t _deq_bytes = 0;
   __nv_bfloat16* _vt = nullptr;    // attention: V^T
   size_t _vt_elems = 0;
+  cudaStream_t _aux = nullptr;
+  cudaEvent_t _ev[4] = {};
   float* _part = nullptr;          // attention: split-KV partials
   size_t _part_elems = 0;
   ltx::SageBuffers _sb;            // sage tier: int8 Q/K, scales, key mean
