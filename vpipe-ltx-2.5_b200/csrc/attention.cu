@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(128)
                       const __nv_bfloat16* __restrict__ gate, int ldg, int tq,
                       int tk, float scale_log2)
 {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kChunks = D / 8;               // 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sq = smem;                          // [64][D]
@@ -275,14 +277,10 @@ int launch_attention(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr = true;
     }
-    flash_attn_kernel<128><<<grid, 128, smem, s>>>(q, ldq, k, ldk, v, ldv, o,
-                                                   ldo, gate, ldg, tq, tk,
-                                                   scale_log2);
+    launch_k(flash_attn_kernel<128>, dim3(grid), dim3(128), smem, s, 1, q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, scale_log2);
   } else if (head_dim == 64) {
     const int smem = (kBM + 4 * kBN) * 64 * 2;
-    flash_attn_kernel<64><<<grid, 128, smem, s>>>(q, ldq, k, ldk, v, ldv, o,
-                                                  ldo, gate, ldg, tq, tk,
-                                                  scale_log2);
+    launch_k(flash_attn_kernel<64>, dim3(grid), dim3(128), smem, s, 1, q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, scale_log2);
   } else {
     return -2;
   }

@@ -162,6 +162,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  // prologue done (barriers, TMEM): wait for the previous kernel, let the
+  // next one start its own prologue
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA
@@ -486,6 +490,10 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  // prologue done (barriers, TMEM): wait for the previous kernel, let the
+  // next one start its own prologue
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ----------------------------------------------------------- Q, K TMA
@@ -745,6 +753,8 @@ __global__ void fa_combine_kernel(const float* __restrict__ part_o,
                                   int heads, int D, __nv_bfloat16* __restrict__ o, int ldo,
                                   const __nv_bfloat16* __restrict__ gate, int ldg)
 {
+  pdl_wait();
+  pdl_trigger();
   const int d4 = D / 4;
   const size_t total = (size_t)tq * heads * d4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -782,6 +792,8 @@ __global__ void __launch_bounds__(256)
     transpose_kernel(const __nv_bfloat16* __restrict__ v, int ldv, int tk, int cols,
                      __nv_bfloat16* __restrict__ vt, int ldvt)
 {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __nv_bfloat16 tile[64][64 + 8];
   const int t0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
   // load: 64 rows x 64 columns, 8 columns (16 B) per thread
@@ -816,6 +828,8 @@ __global__ void __launch_bounds__(256)
     col_mean_kernel(const __nv_bfloat16* __restrict__ k, int ldk, int tk, int cols,
                     float* __restrict__ mean)
 {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float part[8][64];
   const int c = blockIdx.x * 64 + (threadIdx.x & 63);
   const int slice = threadIdx.x >> 6;           // 4 token slices
@@ -840,6 +854,8 @@ __global__ void __launch_bounds__(256)
                           const float* __restrict__ mean, int8_t* __restrict__ out,
                           float* __restrict__ scale, int tpad)
 {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8];
   const int b = blockIdx.x, h = blockIdx.y;
   const int nb = tpad / 128;
@@ -935,9 +951,7 @@ int launch_fa(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtens
       return -1;
     attr = true;
   }
-  fa_tc_kernel<D, I8>
-      <<<dim3((prm.tq + kFaBQ - 1) / kFaBQ, heads, prm.splits), kFaThreads, C::kSmem, s>>>(
-          tq_map, tk_map, tv_map, prm);
+  launch_k(fa_tc_kernel<D, I8>, dim3(dim3((prm.tq + kFaBQ - 1) / kFaBQ, heads, prm.splits)), dim3(kFaThreads), C::kSmem, s, 1, tq_map, tk_map, tv_map, prm);
   return launched();
 }
 
@@ -964,8 +978,7 @@ int prepare_vt(const __nv_bfloat16* v, int ldv, int tk, int cols, int D, __nv_bf
                CUtensorMap* map, cudaStream_t s)
 {
   const int ldvt = (tk + 7) / 8 * 8;
-  transpose_kernel<<<dim3((tk + 63) / 64, (cols + 63) / 64), 256, 0, s>>>(v, ldv, tk, cols, vt,
-                                                                         ldvt);
+  launch_k(transpose_kernel, dim3(dim3((tk + 63) / 64, (cols + 63) / 64)), dim3(256), 0, s, 1, v, ldv, tk, cols, vt, ldvt);
   if (launched() != 0) return -1;
   return fa_encode(map, vt, (uint64_t)tk, (uint64_t)cols, (uint64_t)ldvt * 2, 64, D) ? 0 : -1;
 }
@@ -1031,8 +1044,7 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
     const size_t total = (size_t)tq * heads * (D / 4);
     size_t grid = (total + 255) / 256;
     if (grid > 148 * 8) grid = 148 * 8;
-    fa_combine_kernel<<<(unsigned)grid, 256, 0, s>>>(prm.part_o, prm.part_ml, splits, tq, heads,
-                                                     D, o, ldo, gate, ldg);
+    launch_k(fa_combine_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, prm.part_o, prm.part_ml, splits, tq, heads, D, o, ldo, gate, ldg);
     return launched();
   }
   if (D == 64) return launch_fa<64, false>(tq_map, tk_map, tv_map, prm, heads, s);
@@ -1049,8 +1061,7 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
       return -1;
     attr2 = true;
   }
-  fa2_tc_kernel<<<dim3((tq + 2 * kFaBQ - 1) / (2 * kFaBQ), heads), kFa2Threads, Fa2Cfg::kSmem,
-                  s>>>(tq_map, tk_map, tv_map, prm);
+  launch_k(fa2_tc_kernel, dim3(dim3((tq + 2 * kFaBQ - 1) / (2 * kFaBQ), heads)), dim3(kFa2Threads), Fa2Cfg::kSmem, s, 1, tq_map, tk_map, tv_map, prm);
   return launched();
 }
 
@@ -1085,20 +1096,16 @@ int launch_sage_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k, int 
   float* sq = sb.scales;
   float* sk = sb.scales + (size_t)heads * (tqp / 128);
   // K - mean(K) over tokens (exact under softmax), then per-block int8.
-  col_mean_kernel<<<(cols + 63) / 64, 256, 0, s>>>(k, ldk, tk, cols, sb.mean);
+  launch_k(col_mean_kernel, dim3((cols + 63) / 64), dim3(256), 0, s, 1, k, ldk, tk, cols, sb.mean);
   if (launched() != 0) return -1;
   if (D == 128) {
-    quant_block_i8_kernel<128><<<dim3(tqp / 128, heads), 256, 0, s>>>(q, ldq, tq, nullptr,
-                                                                     sb.qi8, sq, tqp);
+    launch_k(quant_block_i8_kernel<128>, dim3(dim3(tqp / 128, heads)), dim3(256), 0, s, 1, q, ldq, tq, nullptr, sb.qi8, sq, tqp);
     if (launched() != 0) return -1;
-    quant_block_i8_kernel<128><<<dim3(tkp / 128, heads), 256, 0, s>>>(k, ldk, tk, sb.mean,
-                                                                     sb.ki8, sk, tkp);
+    launch_k(quant_block_i8_kernel<128>, dim3(dim3(tkp / 128, heads)), dim3(256), 0, s, 1, k, ldk, tk, sb.mean, sb.ki8, sk, tkp);
   } else {
-    quant_block_i8_kernel<64><<<dim3(tqp / 128, heads), 256, 0, s>>>(q, ldq, tq, nullptr,
-                                                                    sb.qi8, sq, tqp);
+    launch_k(quant_block_i8_kernel<64>, dim3(dim3(tqp / 128, heads)), dim3(256), 0, s, 1, q, ldq, tq, nullptr, sb.qi8, sq, tqp);
     if (launched() != 0) return -1;
-    quant_block_i8_kernel<64><<<dim3(tkp / 128, heads), 256, 0, s>>>(k, ldk, tk, sb.mean,
-                                                                    sb.ki8, sk, tkp);
+    launch_k(quant_block_i8_kernel<64>, dim3(dim3(tkp / 128, heads)), dim3(256), 0, s, 1, k, ldk, tk, sb.mean, sb.ki8, sk, tkp);
   }
   if (launched() != 0) return -1;
   CUtensorMap tq_map, tk_map, tv_map;

@@ -82,6 +82,8 @@ __global__ void vec_add_kernel(const float* __restrict__ a,
                                const __nv_bfloat16* __restrict__ b,
                                float* __restrict__ out, int n)
 {
+  pdl_wait();
+  pdl_trigger();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += gridDim.x * blockDim.x) {
     out[i] = a[i] + (b != nullptr ? __bfloat162float(b[i]) : 0.0f);
@@ -100,6 +102,8 @@ __global__ void __launch_bounds__(kRowThreads)
                    const float* __restrict__ scale,
                    const float* __restrict__ shift, float eps)
 {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[ROWS][33];
   const int r0 = blockIdx.x * ROWS;
   float sc[CH][8], sh[CH][8];
@@ -193,6 +197,8 @@ __global__ void __launch_bounds__(kRowThreads)
                         const float* __restrict__ sumsq, int norm_width,
                         int head0, int tbl_tokens, int tok0)
 {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float srow[];   // the normalized row, f32 [inner]
   __shared__ float red[33];
   const int inner = heads * head_dim;
@@ -266,6 +272,8 @@ __global__ void __launch_bounds__(kRowThreads)
     row_sumsq_kernel(const __nv_bfloat16* __restrict__ in, int ldi, int cols,
                      float* __restrict__ out)
 {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[33];
   const __nv_bfloat16* xr = in + (size_t)blockIdx.x * ldi;
   float ss = 0.0f;
@@ -288,6 +296,8 @@ __global__ void gated_residual_kernel(__nv_bfloat16* __restrict__ x, int ldx,
                                       const float* __restrict__ gate, int rows,
                                       int dim)
 {
+  pdl_wait();
+  pdl_trigger();
   const int chunks = dim / 8;
   const size_t total = (size_t)rows * chunks;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -316,6 +326,8 @@ __global__ void gated_residual_kernel(__nv_bfloat16* __restrict__ x, int ldx,
 __global__ void a2a_pack_kernel(const __nv_bfloat16* __restrict__ src, int ld, int rows,
                                 int ranks, int cpr, __nv_bfloat16* __restrict__ dst)
 {
+  pdl_wait();
+  pdl_trigger();
   const int c8 = cpr / 8;
   const size_t total = (size_t)ranks * rows * c8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -335,6 +347,8 @@ __global__ void a2a_unpack_kernel(const __nv_bfloat16* __restrict__ src, int row
                                   int cpr, __nv_bfloat16* __restrict__ dst, int ldd,
                                   const __nv_bfloat16* __restrict__ gate, int ldg, int head_dim)
 {
+  pdl_wait();
+  pdl_trigger();
   const int c8 = cpr / 8;
   const size_t total = (size_t)ranks * rows * c8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -360,6 +374,8 @@ __global__ void a2a_unpack_kernel(const __nv_bfloat16* __restrict__ src, int row
 __global__ void f32_to_bf16_kernel(const float* __restrict__ a,
                                    __nv_bfloat16* __restrict__ out, size_t n)
 {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     out[i] = __float2bfloat16_rn(a[i]);
@@ -373,7 +389,7 @@ int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
   if (n == 0) return 0;
   size_t grid = (n + 255) / 256;
   if (grid > 4096) grid = 4096;
-  f32_to_bf16_kernel<<<(unsigned)grid, 256, 0, s>>>(a, out, n);
+  launch_k(f32_to_bf16_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, a, out, n);
   return launched();
 }
 
@@ -384,7 +400,7 @@ int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,
   const int threads = 256;
   int grid = (n + threads - 1) / threads;
   if (grid > 1024) grid = 1024;
-  vec_add_kernel<<<grid, threads, 0, s>>>(a, b, out, n);
+  launch_k(vec_add_kernel, dim3(grid), dim3(threads), 0, s, 1, a, b, out, n);
   return launched();
 }
 
@@ -400,18 +416,14 @@ int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
     constexpr int R = 4;
     const unsigned grid = (unsigned)((rows + R - 1) / R);
     if (norm)
-      row_mod_kernel<true, R, 2><<<grid, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
-                                                             scale, shift, eps);
+      launch_k(row_mod_kernel<true, R, 2>, dim3(grid), dim3(kRowThreads), 0, s, 1, x, ldx, out, ldo, rows, dim, scale, shift, eps);
     else
-      row_mod_kernel<false, R, 2><<<grid, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
-                                                              scale, shift, eps);
+      launch_k(row_mod_kernel<false, R, 2>, dim3(grid), dim3(kRowThreads), 0, s, 1, x, ldx, out, ldo, rows, dim, scale, shift, eps);
   } else {
     if (norm)
-      row_mod_kernel<true, 1, 4><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
-                                                             scale, shift, eps);
+      launch_k(row_mod_kernel<true, 1, 4>, dim3(rows), dim3(kRowThreads), 0, s, 1, x, ldx, out, ldo, rows, dim, scale, shift, eps);
     else
-      row_mod_kernel<false, 1, 4><<<rows, kRowThreads, 0, s>>>(x, ldx, out, ldo, rows, dim,
-                                                              scale, shift, eps);
+      launch_k(row_mod_kernel<false, 1, 4>, dim3(rows), dim3(kRowThreads), 0, s, 1, x, ldx, out, ldo, rows, dim, scale, shift, eps);
   }
   return launched();
 }
@@ -439,9 +451,7 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
       attr = true;
     }
   }
-  qk_norm_rope_kernel<<<rows, kRowThreads, smem, s>>>(
-      in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq,
-      norm_width > 0 ? norm_width : inner, head0, tbl_tokens > 0 ? tbl_tokens : rows, tok0);
+  launch_k(qk_norm_rope_kernel, dim3(rows), dim3(kRowThreads), smem, s, 1, in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq, norm_width > 0 ? norm_width : inner, head0, tbl_tokens > 0 ? tbl_tokens : rows, tok0);
   return launched();
 }
 
@@ -453,7 +463,7 @@ int launch_a2a_pack(const __nv_bfloat16* src, int ld, int rows, int ranks, int c
   const size_t total = (size_t)ranks * rows * (cpr / 8);
   size_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
-  a2a_pack_kernel<<<(unsigned)grid, 256, 0, s>>>(src, ld, rows, ranks, cpr, dst);
+  launch_k(a2a_pack_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, src, ld, rows, ranks, cpr, dst);
   return launched();
 }
 
@@ -466,8 +476,7 @@ int launch_a2a_unpack(const __nv_bfloat16* src, int rows, int ranks, int cpr,
   const size_t total = (size_t)ranks * rows * (cpr / 8);
   size_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
-  a2a_unpack_kernel<<<(unsigned)grid, 256, 0, s>>>(src, rows, ranks, cpr, dst, ldd, gate, ldg,
-                                                   head_dim);
+  launch_k(a2a_unpack_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, src, rows, ranks, cpr, dst, ldd, gate, ldg, head_dim);
   return launched();
 }
 
@@ -476,7 +485,7 @@ int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,
 {
   if (rows <= 0) return 0;
   if (cols % 8 != 0 || ldi % 8 != 0) return -2;
-  row_sumsq_kernel<<<rows, kRowThreads, 0, s>>>(in, ldi, cols, out);
+  launch_k(row_sumsq_kernel, dim3(rows), dim3(kRowThreads), 0, s, 1, in, ldi, cols, out);
   return launched();
 }
 
@@ -489,8 +498,7 @@ int launch_gated_residual(__nv_bfloat16* x, int ldx, const __nv_bfloat16* part,
   const size_t total = (size_t)rows * (dim / 8);
   size_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
-  gated_residual_kernel<<<(unsigned)grid, 256, 0, s>>>(x, ldx, part, bias, gate,
-                                                      rows, dim);
+  launch_k(gated_residual_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, x, ldx, part, bias, gate, rows, dim);
   return launched();
 }
 

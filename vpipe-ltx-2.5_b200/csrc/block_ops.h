@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "pdl.cuh"
+
 namespace ltx {
 
 // Status of the kernel launch just issued (0 or -1), counting it when it

@@ -162,6 +162,10 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
   if constexpr (PAIR) cluster_sync_all();   // peer barriers live before use
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  // prologue done (barriers, TMEM): wait for the previous kernel, let the
+  // next one start its own prologue
+  pdl_wait();
+  pdl_trigger();
   if (tr != nullptr && threadIdx.x == 0) tr[TR_SETUP] = clock64();
 
   if (warp == 0) {
@@ -754,23 +758,7 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
     grid = p.num_tiles;
     cluster = p.splits;
   }
-  if (cluster > 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid, 1, 1);
-    cfg.blockDim = dim3(C::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, tx, tw, tsz, p) != cudaSuccess) return -3;
-    return launched() == 0 ? 0 : -3;
-  }
-  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tx, tw, tsz, p);
+  launch_k(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, cluster, tx, tw, tsz, p);
   return launched() == 0 ? 0 : -3;
 }
 

@@ -23,6 +23,8 @@ __global__ void pack_sz_kernel(const void* __restrict__ scales,
                                const void* __restrict__ biases, int dtype,
                                int N, int G, uint32_t* __restrict__ sz)
 {
+  pdl_wait();
+  pdl_trigger();
   const long long total = (long long)N * G;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
        i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -48,6 +50,8 @@ __global__ void dequant_w8_kernel(const uint8_t* __restrict__ codes,
                                   const uint32_t* __restrict__ sz, int N,
                                   int K, __nv_bfloat16* __restrict__ out)
 {
+  pdl_wait();
+  pdl_trigger();
   const long long chunks = (long long)N * (K / 16);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
        i < chunks; i += (long long)gridDim.x * blockDim.x) {
@@ -85,6 +89,8 @@ __global__ void quant_rows_i8_kernel(const __nv_bfloat16* __restrict__ x,
                                      int8_t* __restrict__ q,
                                      float* __restrict__ scale)
 {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.y;
   const int g = blockIdx.x;
   const __nv_bfloat16* xs = x + (size_t)row * ldx + (size_t)g * group;
@@ -144,6 +150,8 @@ __global__ void pack_w8g64_kernel(const float* __restrict__ w, int N, int K,
                                   uint16_t* __restrict__ scales,
                                   uint16_t* __restrict__ biases)
 {
+  pdl_wait();
+  pdl_trigger();
   const int G = K / 64;
   const long long warp_id =
       (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
@@ -191,8 +199,7 @@ int grid_for(long long work, int threads)
 int launch_pack_sz(const void* scales, const void* biases, int dtype, int N,
                    int G, uint32_t* sz, cudaStream_t stream)
 {
-  pack_sz_kernel<<<grid_for((long long)N * G, 256), 256, 0, stream>>>(
-      scales, biases, dtype, N, G, sz);
+  launch_k(pack_sz_kernel, dim3(grid_for((long long)N * G, 256)), dim3(256), 0, stream, 1, scales, biases, dtype, N, G, sz);
   return launched();
 }
 
@@ -203,16 +210,14 @@ int launch_pack_w8g64(const float* w, int N, int K, uint32_t* codes,
   const long long threads = (long long)N * (K / 64) * 32;
   const int block = 256;
   const long long grid = (threads + block - 1) / block;
-  pack_w8g64_kernel<<<(unsigned)grid, block, 0, stream>>>(w, N, K, codes,
-                                                          scales, biases);
+  launch_k(pack_w8g64_kernel, dim3((unsigned)grid), dim3(block), 0, stream, 1, w, N, K, codes, scales, biases);
   return launched();
 }
 
 int launch_dequant_w8(const uint8_t* codes, const uint32_t* sz, int N, int K,
                       __nv_bfloat16* out, cudaStream_t stream)
 {
-  dequant_w8_kernel<<<grid_for((long long)N * (K / 16), 256), 256, 0,
-                      stream>>>(codes, sz, N, K, out);
+  launch_k(dequant_w8_kernel, dim3(grid_for((long long)N * (K / 16), 256)), dim3(256), 0, stream, 1, codes, sz, N, K, out);
   return launched();
 }
 
@@ -225,8 +230,7 @@ int launch_quant_rows_i8(const __nv_bfloat16* x, int rows, int K, int ldx,
   if (threads > 256) threads = 256;
   threads = (threads + 31) / 32 * 32;
   dim3 grid(K / group, rows);
-  quant_rows_i8_kernel<<<grid, threads, 0, stream>>>(x, K, ldx, group, q,
-                                                     scale);
+  launch_k(quant_rows_i8_kernel, dim3(grid), dim3(threads), 0, stream, 1, x, K, ldx, group, q, scale);
   return launched();
 }
 
