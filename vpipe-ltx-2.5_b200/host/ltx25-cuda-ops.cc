@@ -63,8 +63,13 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
   p.m_tiles = (M + p.tn - 1) / p.tn;
   const int tiles = p.m_tiles * p.n_tiles;
   p.splits = 1;
-  if (!p.pair && tiles * 2 <= sms && p.kblocks >= 4) {
-    p.splits = std::min(std::min(sms / tiles, p.kblocks / 2), 8);
+  // Split K over a cluster until ~128 CTAs stream the weight.  Measured on
+  // B200 (M = 126, 16-64 weight tiles): clusters of up to 6 CTAs and grids
+  // of <= 128 CTAs win; 8-CTA clusters and 3-way splits of 48 tiles place
+  // poorly across the GPCs and run a second wave (24.6 vs 36.9 us at
+  // K=8192 N=2048; 21.3 vs 31.6 us at K=2048 N=6144).
+  if (!p.pair && tiles * 2 <= 128 && p.kblocks >= 4) {
+    p.splits = std::min(std::min(128 / tiles, p.kblocks / 2), 6);
     if (p.splits < 1) p.splits = 1;
   }
   // A/B override of the K split (the reference's tile knobs,
