@@ -93,6 +93,35 @@ __device__ __forceinline__ float fast_exp2(float x)
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Packed f32 pairs (sm_100 f32x2): d = a * b + c and d = a + b, lane-wise.
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b,
+                                                    unsigned long long c)
+{
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ unsigned long long fadd2(unsigned long long a, unsigned long long b)
+{
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ unsigned long long pair2(uint32_t lo, uint32_t hi)
+{
+  return ((unsigned long long)hi << 32) | lo;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
 {
   const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -637,11 +666,11 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
           tmem_wait_ld();
           if (full) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              m4[0] = fmaxf(m4[0], __uint_as_float(a[e]));
-              m4[1] = fmaxf(m4[1], __uint_as_float(a[e + 1]));
-              m4[2] = fmaxf(m4[2], __uint_as_float(b[e]));
-              m4[3] = fmaxf(m4[3], __uint_as_float(b[e + 1]));
+            for (int e = 0; e < 32; e += 4) {
+              m4[0] = max3f(m4[0], __uint_as_float(a[e]), __uint_as_float(a[e + 1]));
+              m4[1] = max3f(m4[1], __uint_as_float(a[e + 2]), __uint_as_float(a[e + 3]));
+              m4[2] = max3f(m4[2], __uint_as_float(b[e]), __uint_as_float(b[e + 1]));
+              m4[3] = max3f(m4[3], __uint_as_float(b[e + 2]), __uint_as_float(b[e + 3]));
             }
           } else {
 #pragma unroll
@@ -692,19 +721,25 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
             if (h2 * 64 + 32 + e >= valid) b[e] = __float_as_uint(-3.0e38f);
           }
         }
-        float s0 = 0.0f, s1 = 0.0f;
+        // exponent arguments two at a time (f32x2 FMA), sums likewise
+        const unsigned long long c2 = pair2(__float_as_uint(c), __float_as_uint(c));
+        const unsigned long long nm2 = pair2(__float_as_uint(-m_run), __float_as_uint(-m_run));
+        unsigned long long sa = 0ull, sb = 0ull;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(a[2 * e]), c, -m_run));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(a[2 * e + 1]), c, -m_run));
-          const float p2 = fast_exp2(fmaf(__uint_as_float(b[2 * e]), c, -m_run));
-          const float p3 = fast_exp2(fmaf(__uint_as_float(b[2 * e + 1]), c, -m_run));
-          s0 += p0 + p1;
-          s1 += p2 + p3;
+          const unsigned long long xa = ffma2(pair2(a[2 * e], a[2 * e + 1]), c2, nm2);
+          const unsigned long long xb = ffma2(pair2(b[2 * e], b[2 * e + 1]), c2, nm2);
+          const float p0 = fast_exp2(__uint_as_float((uint32_t)xa));
+          const float p1 = fast_exp2(__uint_as_float((uint32_t)(xa >> 32)));
+          const float p2 = fast_exp2(__uint_as_float((uint32_t)xb));
+          const float p3 = fast_exp2(__uint_as_float((uint32_t)(xb >> 32)));
+          sa = fadd2(sa, pair2(__float_as_uint(p0), __float_as_uint(p1)));
+          sb = fadd2(sb, pair2(__float_as_uint(p2), __float_as_uint(p3)));
           pk[e] = pack_bf16(p0, p1);
           pk[16 + e] = pack_bf16(p2, p3);
         }
-        sum += s0 + s1;
+        const unsigned long long st2 = fadd2(sa, sb);
+        sum += __uint_as_float((uint32_t)st2) + __uint_as_float((uint32_t)(st2 >> 32));
         tmem_st32(scol + (uint32_t)(h2 * 32), pk);
       }
       l_run += sum;
