@@ -15,7 +15,6 @@
 #include "block_ops.h"
 
 #include <atomic>
-#include <cstdlib>
 
 namespace ltx {
 
@@ -183,113 +182,6 @@ __global__ void __launch_bounds__(kRowThreads)
       for (int i = 0; i < 8; ++i) o[i] = fmaf(v[r][c][i] * inv[r], 1.0f + sc[c][i], sh[c][i]);
       store8(out + (size_t)(r0 + r) * ldo + k, o);
     }
-  }
-}
-
-// The same op for dim <= 4096 as a persistent kernel: one CTA per SM walks
-// groups of 4 rows, issuing the next group's loads before it reduces and
-// stores the current one, with (1 + scale) and shift staged once in shared
-// memory.  Per row the arithmetic and reduction order are row_mod_kernel's.
-template <bool NORM>
-__global__ void __launch_bounds__(kRowThreads, 1)
-    row_mod_persist_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
-                           __nv_bfloat16* __restrict__ out, int ldo, int rows, int dim,
-                           const float* __restrict__ scale,
-                           const float* __restrict__ shift, float eps)
-{
-  constexpr int R = 4, CH = 2;
-  extern __shared__ float s_mod[];          // [0, dim): 1 + scale, [dim, 2 dim): shift
-  __shared__ float red[R][33];
-  pdl_wait();
-  pdl_trigger();
-  for (int k = threadIdx.x * 4; k < dim; k += kRowThreads * 4) {
-    const float4 a = scale != nullptr ? *reinterpret_cast<const float4*>(scale + k)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 b = shift != nullptr ? *reinterpret_cast<const float4*>(shift + k)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    s_mod[k] = 1.0f + a.x;
-    s_mod[k + 1] = 1.0f + a.y;
-    s_mod[k + 2] = 1.0f + a.z;
-    s_mod[k + 3] = 1.0f + a.w;
-    s_mod[dim + k] = b.x;
-    s_mod[dim + k + 1] = b.y;
-    s_mod[dim + k + 2] = b.z;
-    s_mod[dim + k + 3] = b.w;
-  }
-  __syncthreads();
-  const int groups = (rows + R - 1) / R;
-  float buf[2][R][CH][8];
-  auto load = [&](float (&v)[R][CH][8], int g) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = g * R + r;
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int k = (c * kRowThreads + threadIdx.x) * 8;
-        if (row < rows && k < dim) load8(x + (size_t)row * ldx + k, v[r][c]);
-      }
-    }
-  };
-  auto finish = [&](float (&v)[R][CH][8], int g) {
-    float inv[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) inv[r] = 1.0f;
-    if (NORM) {
-      const int w = threadIdx.x >> 5;
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        float t = 0.0f;
-#pragma unroll
-        for (int c = 0; c < CH; ++c) {
-          const int k = (c * kRowThreads + threadIdx.x) * 8;
-          if (g * R + r < rows && k < dim) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) t = fmaf(v[r][c][i], v[r][c][i], t);
-          }
-        }
-        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if ((threadIdx.x & 31) == 0) red[r][w] = t;
-      }
-      __syncthreads();
-      if (threadIdx.x < 32) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          float t = threadIdx.x < (blockDim.x >> 5) ? red[r][threadIdx.x] : 0.0f;
-          for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-          if (threadIdx.x == 0) red[r][32] = t;
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int r = 0; r < R; ++r) inv[r] = rsqrtf(red[r][32] / (float)dim + eps);
-      __syncthreads();   // red is rewritten by the next group
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = g * R + r;
-      if (row >= rows) break;
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int k = (c * kRowThreads + threadIdx.x) * 8;
-        if (k >= dim) continue;
-        float o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o[i] = fmaf(v[r][c][i] * inv[r], s_mod[k + i], s_mod[dim + k + i]);
-        store8(out + (size_t)row * ldo + k, o);
-      }
-    }
-  };
-  int g = blockIdx.x;
-  if (g < groups) load(buf[0], g);
-  for (; g < groups; g += 2 * gridDim.x) {
-    const int g1 = g + gridDim.x;
-    if (g1 < groups) load(buf[1], g1);
-    finish(buf[0], g);
-    if (g1 >= groups) break;
-    const int g2 = g1 + gridDim.x;
-    if (g2 < groups) load(buf[0], g2);
-    finish(buf[1], g1);
   }
 }
 
@@ -512,17 +404,6 @@ int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,
   return launched();
 }
 
-namespace {
-bool row_mod_simple()
-{
-  static const bool v = [] {
-    const char* e = getenv("LTX25_ROWMOD");
-    return e != nullptr && e[0] == '0';
-  }();
-  return v;
-}
-}  // namespace
-
 int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
                     int ldo, int rows, int dim, const float* scale,
                     const float* shift, float eps, bool norm, cudaStream_t s)
@@ -531,18 +412,7 @@ int launch_ada_zero(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out,
   if (dim % 8 != 0 || dim > kRowThreads * 8 * 4) return -2;
   if (((reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(shift)) & 15u) != 0)
     return -2;
-  if (dim <= kRowThreads * 8 * 2 && rows >= 148 * 8 && !row_mod_simple()) {
-    // tall: persistent, one CTA per SM, next rows' loads in flight
-    const int groups = (rows + 3) / 4;
-    const unsigned grid = (unsigned)(groups < 148 ? groups : 148);
-    const size_t smem = (size_t)2 * dim * sizeof(float);
-    if (norm)
-      launch_k(row_mod_persist_kernel<true>, dim3(grid), dim3(kRowThreads), smem, s, 1, x, ldx,
-               out, ldo, rows, dim, scale, shift, eps);
-    else
-      launch_k(row_mod_persist_kernel<false>, dim3(grid), dim3(kRowThreads), smem, s, 1, x,
-               ldx, out, ldo, rows, dim, scale, shift, eps);
-  } else if (dim <= kRowThreads * 8 * 2) {
+  if (dim <= kRowThreads * 8 * 2) {
     constexpr int R = 4;
     const unsigned grid = (unsigned)((rows + R - 1) / R);
     if (norm)
