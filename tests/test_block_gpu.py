@@ -48,7 +48,8 @@ def host(t):
 # ------------------------------------------------------------------ ops
 
 @pytest.mark.parametrize("rows,dim,norm", [(37, 256, True), (8, 4096, True),
-                                           (5, 2048, False), (130, 128, True)])
+                                           (5, 2048, False), (130, 128, True),
+                                           (8160, 4096, True), (2001, 2048, False)])
 def test_ada_zero(ctx, rows, dim, norm):
     import ltx25_b200 as L
     rng = np.random.default_rng(rows + dim)
