@@ -88,6 +88,12 @@ LTX_API int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k);
  * (the reference's wait_ok(), src/ltx25-dit.cc:1920-1931). */
 LTX_API int ltx_ctx_check(ltx_ctx* ctx, void* stream);
 
+/* Self-test of the failure path above, with no fault: a kernel waits
+ * `bound_ms` (1..2000) on a barrier nothing arrives at and gives up the way
+ * every pipeline wait does; the next ltx_ctx_check on that stream returns
+ * LTX_E_KERNEL, and the context stays usable. */
+LTX_API int ltx_ctx_selftest_timeout(ltx_ctx* ctx, int bound_ms, void* stream);
+
 /* Diagnostics (the reference's VPIPE_LTX25_BLOCK_PROFILE role, src/
  * ltx25-dit.cc:1597-1598): every following GEMM launch writes 16 u64 per
  * CTA for its first `max_ctas` CTAs into the device buffer `buf` -- SM

@@ -60,4 +60,8 @@ int launch_quant_rows_i8(const __nv_bfloat16* x, int rows, int K, int ldx,
 // f32 scales.
 bool i8_static_scratch(int device, int8_t** codes, float** scales, std::string* err);
 
+// A one-thread kernel that waits `bound_ms` (1..2000) on an mbarrier nothing
+// arrives at and records the timeout in `err` (watchdog.cu).
+int launch_watchdog_probe(int* err, int bound_ms, cudaStream_t s);
+
 }  // namespace ltx

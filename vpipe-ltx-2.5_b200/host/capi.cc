@@ -89,6 +89,15 @@ int ltx_ctx_check(ltx_ctx* ctx, void* stream)
   return LTX_OK;
 }
 
+int ltx_ctx_selftest_timeout(ltx_ctx* ctx, int bound_ms, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  const int rc = ltx::launch_watchdog_probe(ctx->ops.err_word(), bound_ms, S(stream));
+  if (rc == -2) return fail(ctx, LTX_E_SHAPE, "selftest: bound_ms outside 1..2000");
+  if (rc != 0) return fail(ctx, LTX_E_CUDA, "selftest launch failed");
+  return LTX_OK;
+}
+
 int ltx_ctx_set_trace(ltx_ctx* ctx, void* buf, int max_ctas)
 {
   if (ctx == nullptr) return LTX_E_NULL;
@@ -227,7 +236,11 @@ int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id)
   auto c = std::make_unique<ltx25::Comm>();
   std::string e;
   if (!c->init(ctx->ops.device(), rank, world, id, &e)) return fail(ctx, LTX_E_CUDA, e);
-  ctx->ops.set_comm(std::move(c));
+  // A second communicator lets the audio stream's all-reduces run on the
+  // side stream beside the video stream's; without it, one stream.
+  auto side = std::make_unique<ltx25::Comm>();
+  if (!c->split(side.get(), &e)) side.reset();
+  ctx->ops.set_comm(std::move(c), false, std::move(side));
   return LTX_OK;
 }
 

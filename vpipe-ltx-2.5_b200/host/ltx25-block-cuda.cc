@@ -353,6 +353,8 @@ bool CudaBlock::finalize(std::string* err)
 {
   if (_final) return true;
   _comm = _ops->comm();
+  _comm_side = _ops->side_comm();
+  _ccur = _comm;
   _sp = _ops->sequence_parallel();
   _sp_world = _sp ? _comm->world() : 1;
   _sp_rank = _sp ? _comm->rank() : 0;
@@ -441,7 +443,8 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
     const size_t na[18] = {
         at * ad, mx({at * 3 * ad, at * ai}), at * ad, mx({at * ad, tt * ad, at * ai}),
         at * ad, at * (size_t)_aheads, tt * ad, mx({tt * 2 * ad, at * 2 * ai}),
-        at * (size_t)_audio.ff_hidden, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+        at * (size_t)_audio.ff_hidden, 0, 0, 0, 0, 0,
+        _tp_world > 1 ? at * ad : 0, _tp_world > 1 ? 2 * (at + tt) : 0, 0, 0};
     if (!_arp->side) _arp->side = std::make_shared<BlockArena>();
     for (int i = 0; i < 18; ++i)
       if (!_arp->side->ensure(i, na[i], err)) return false;
@@ -500,7 +503,7 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     if (ltx::launch_row_sumsq(qraw, ldq, tq, I, _cur->ssq, s) != 0 ||
         ltx::launch_row_sumsq(kraw, ldkv, tkv, I, _cur->ssq + tq, s) != 0)
       return fail(err, "q/k sum-of-squares launch failed");
-    if (!_comm->allreduce_sum(_cur->ssq, (size_t)tq + tkv, 0, s, err)) return false;
+    if (!_ccur->allreduce_sum(_cur->ssq, (size_t)tq + tkv, 0, s, err)) return false;
     qss = _cur->ssq;
     kss = _cur->ssq + tq;
   }
@@ -618,7 +621,7 @@ bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
   // ranks, then the bias and the gated residual, once.
   if (!_ops->linear(s, in, k, w, nullptr, _cur->part, d, n, k, d, ltx::EPI_STORE,
                     nullptr, err) ||
-      !_comm->allreduce_sum(_cur->part, (size_t)n * d, 1, s, err))
+      !_ccur->allreduce_sum(_cur->part, (size_t)n * d, 1, s, err))
     return false;
   if (ltx::launch_gated_residual(x, d, _cur->part, bias, gate, n, d, s) != 0)
     return fail(err, "gated residual launch failed");
@@ -737,13 +740,16 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
   // The audio stream runs beside the video one on the context's second
   // CUDA stream while they are independent (first halves, feed-forwards),
   // when nothing it launches shares scratch or a communicator with video.
-  const bool conc = rv && ra && _tp_world == 1 && _ops->audio_side_ok(a.tokens, a.text_tokens, _aheads, _adim / _aheads, _layer);
+  const bool conc = rv && ra && (_tp_world == 1 || _comm_side != nullptr) &&
+                    _ops->audio_side_ok(a.tokens, a.text_tokens, _aheads, _adim / _aheads, _layer);
   cudaStream_t sa = conc ? _ops->aux_stream(err) : s;
   if (conc && sa == nullptr) return false;
   if (conc && !_ops->fork(s, sa, 0, err)) return false;
   _cur = conc ? _arp->side.get() : _arp.get();
+  _ccur = conc ? _comm_side : _comm;
   if (ra && !first_half_(sa, _audio, a, err)) return false;
   _cur = _arp.get();
+  _ccur = _comm;
   if (rv && !first_half_(s, _video, v, err)) return false;
   if (conc && !_ops->fork(sa, s, 1, err)) return false;
 
@@ -787,8 +793,10 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
 
   if (conc && !_ops->fork(s, sa, 2, err)) return false;
   _cur = conc ? _arp->side.get() : _arp.get();
+  _ccur = conc ? _comm_side : _comm;
   if (ra && !ff_(sa, _audio, a, err)) return false;
   _cur = _arp.get();
+  _ccur = _comm;
   if (rv && !ff_(s, _video, v, err)) return false;
   if (conc && !_ops->fork(sa, s, 3, err)) return false;
   return true;

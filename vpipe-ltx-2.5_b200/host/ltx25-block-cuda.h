@@ -213,6 +213,8 @@ private:
   CudaOps* _ops;
   int _vdim, _vheads, _adim, _aheads;
   const Comm* _comm = nullptr;   // set at finalize when the context is sharded
+  const Comm* _comm_side = nullptr;   // the side stream's (tensor parallel)
+  const Comm* _ccur = nullptr;        // the communicator of the stream being issued
   int _tp_rank = 0, _tp_world = 1;
   bool _sp = false;              // sequence parallel (weights whole)
   int _sp_rank = 0, _sp_world = 1;

@@ -22,6 +22,7 @@ struct Nccl {
   decltype(&ncclGroupStart) group_start = nullptr;
   decltype(&ncclGroupEnd) group_end = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclCommSplit) comm_split = nullptr;
   bool ok = false;
   std::string why;
 };
@@ -51,6 +52,7 @@ const Nccl& nccl()
     n.group_start = reinterpret_cast<decltype(n.group_start)>(dlsym(h, "ncclGroupStart"));
     n.group_end = reinterpret_cast<decltype(n.group_end)>(dlsym(h, "ncclGroupEnd"));
     n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
+    n.comm_split = reinterpret_cast<decltype(n.comm_split)>(dlsym(h, "ncclCommSplit"));
     n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce &&
            n.error_string && n.send && n.recv && n.group_start && n.group_end &&
            n.all_gather;
@@ -120,6 +122,23 @@ bool Comm::allreduce_sum(void* buf, size_t count, int dtype, cudaStream_t s,
   return nccl_ok(nccl().all_reduce(buf, buf, count, t, ncclSum,
                                    static_cast<ncclComm_t>(_comm), s),
                  "ncclAllReduce", err);
+}
+
+bool Comm::split(Comm* out, std::string* err) const
+{
+  const Nccl& n = nccl();
+  if (_comm == nullptr || n.comm_split == nullptr) {
+    if (err) *err = "comm split unavailable";
+    return false;
+  }
+  ncclComm_t c = nullptr;
+  if (!nccl_ok(n.comm_split(static_cast<ncclComm_t>(_comm), 0, _rank, &c, nullptr),
+               "ncclCommSplit", err))
+    return false;
+  out->_comm = c;
+  out->_rank = _rank;
+  out->_world = _world;
+  return true;
 }
 
 bool Comm::alltoall_bf16(const void* send, void* recv, size_t count, int n, size_t stride,

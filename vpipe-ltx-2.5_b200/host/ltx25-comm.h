@@ -36,6 +36,10 @@ public:
   bool allgather_bf16(const void* send, void* recv, size_t count, cudaStream_t s,
                       std::string* err) const;
 
+  // A second communicator over the same ranks (ncclCommSplit), for
+  // collectives issued on another stream.
+  bool split(Comm* out, std::string* err) const;
+
   int rank() const { return _rank; }
   int world() const { return _world; }
 

@@ -87,12 +87,16 @@ public:
   // Multi-GPU: blocks finalized after this either shard their weights over
   // the group (tensor parallel) or keep them whole and shard the video
   // tokens (sequence parallel, `sequence` true); null comm = one GPU.
-  void set_comm(std::unique_ptr<Comm> c, bool sequence = false)
+  void set_comm(std::unique_ptr<Comm> c, bool sequence = false,
+                std::unique_ptr<Comm> side = nullptr)
   {
     _comm = std::move(c);
+    _comm_side = std::move(side);
     _sequence = sequence;
   }
   const Comm* comm() const { return _comm.get(); }
+  // The communicator for collectives on the side stream (null: none).
+  const Comm* side_comm() const { return _comm_side.get(); }
   bool sequence_parallel() const { return _comm != nullptr && _sequence; }
 
   // Diagnostics: every following GEMM writes per-CTA phase timestamps into
@@ -172,6 +176,7 @@ private:
   int _attn_mode = -1;             // LTX25_ATTN: 0 = always warp-MMA
   int* _err_word = nullptr;
   std::unique_ptr<Comm> _comm;
+  std::unique_ptr<Comm> _comm_side;
   bool _sequence = false;
   unsigned long long* _trace = nullptr;
   int _trace_ctas = 0;

@@ -38,6 +38,7 @@ SIGNATURES = {
     "ltx_ctx_reserve": (_I, [_P, _I, _I, _I]),
     "ltx_ctx_check": (_I, [_P, _P]),
     "ltx_ctx_set_trace": (_I, [_P, _P, _I]),
+    "ltx_ctx_selftest_timeout": (_I, [_P, _I, _P]),
     "ltx_qweight_upload": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                                 ctypes.POINTER(_P)]),
     "ltx_dweight_upload": (_I, [_P, _P, _I, _I, _I, ctypes.POINTER(_P)]),
@@ -185,6 +186,11 @@ class Context:
     def set_tiers(self, i8_gemm=False, sage_attn=False, sage_dense_layers=0):
         self._ok(self.lib.ltx_set_tiers(self.h, int(i8_gemm), int(sage_attn),
                                         sage_dense_layers), "set_tiers")
+
+    def selftest_timeout(self, bound_ms=100, stream=None):
+        """Launch the bounded-wait self-test (ltx_ctx_selftest_timeout)."""
+        self._ok(self.lib.ltx_ctx_selftest_timeout(self.h, bound_ms, _stream(stream)),
+                 "selftest_timeout")
 
     def set_tp(self, rank, world, uid=None):
         """Join a tensor-parallel group (uid: the bytes of tp_unique_id() made
