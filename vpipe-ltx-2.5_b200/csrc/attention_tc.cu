@@ -781,6 +781,356 @@ __global__ void __launch_bounds__(kFa2Threads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// The 64 exponentials of one half row: p = 2^(s c - m), packed to bf16 pairs
+// (low half = even column) and summed in two f32x2 chains.
+__device__ __forceinline__ void fa3_exp(const uint32_t (&a)[32], const uint32_t (&b)[32],
+                                        unsigned long long c2, unsigned long long nm2,
+                                        uint32_t (&pk)[32], unsigned long long& sa,
+                                        unsigned long long& sb)
+{
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const unsigned long long xa = ffma2(pair2(a[2 * e], a[2 * e + 1]), c2, nm2);
+    const unsigned long long xb = ffma2(pair2(b[2 * e], b[2 * e + 1]), c2, nm2);
+    const float p0 = fast_exp2(__uint_as_float((uint32_t)xa));
+    const float p1 = fast_exp2(__uint_as_float((uint32_t)(xa >> 32)));
+    const float p2 = fast_exp2(__uint_as_float((uint32_t)xb));
+    const float p3 = fast_exp2(__uint_as_float((uint32_t)(xb >> 32)));
+    sa = fadd2(sa, pair2(__float_as_uint(p0), __float_as_uint(p1)));
+    sb = fadd2(sb, pair2(__float_as_uint(p2), __float_as_uint(p3)));
+    pk[e] = pack_bf16(p0, p1);
+    pk[16 + e] = pack_bf16(p2, p3);
+  }
+}
+
+// ---- two query tiles, each row's scores split over two warps -----------
+//
+// fa2_tc_kernel's schedule with 16 softmax warps instead of 8: the two
+// warps that share a TMEM lane quarter split a row's 128 scores (64 each,
+// one TMEM read per tile), combine the row max through shared memory behind
+// a per-tile named barrier, and each rescale / normalize half of O.  Four
+// softmax warps per SM sub-partition hide the TMEM-read latency that bounds
+// the eight-warp version.
+constexpr int kFa3Threads = 640;   // w0 Q/K TMA, w1 MMA, w2 V TMA, w4-11 / w12-19 softmax
+constexpr int kFa3KStages = 2;     // one K stage fewer: room for the row-max exchange
+
+struct Fa3Cfg : Fa2Cfg {
+  static constexpr int kSmem =
+      1024 + 2 * kQTile + kFa3KStages * kKStage + kFa2VStages * kVStage + 256;
+};
+
+__global__ void __launch_bounds__(kFa3Threads, 1)
+    fa3_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                  const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_vt, FaParams p)
+{
+  using C = Fa3Cfg;
+  constexpr int D = C::D;
+  constexpr int SK = kFa3KStages, SV = kFa2VStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_q = base;                                 // tile t at t * kQTile
+  uint8_t* s_k = s_q + 2 * C::kQTile;
+  uint8_t* s_v = s_k + SK * C::kKStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_v + SV * C::kVStage);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + SK;
+  uint64_t* v_full = k_empty + SK;
+  uint64_t* v_empty = v_full + SV;
+  uint64_t* s_full = v_empty + SV;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  // row-max exchange between the two half-row warps: [tile][parity][half][row]
+  __shared__ float s_mx[2][2][2][kFaBQ];
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * 2 * kFaBQ;
+  const int h = blockIdx.y;
+  const int n = p.ntiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < SK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < SV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 8);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_vt);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  // prologue done (barriers, TMEM): wait for the previous kernel, let the
+  // next one start its own prologue
+  pdl_wait();
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- Q, K TMA
+    if (lane == 0) {
+      uint32_t armed = 0, armed_par = 0;
+      mbar_arrive_expect_tx(q_full, 2 * C::kQTile);
+      for (int t = 0; t < 2; ++t)
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(&tm_q, q_full, s_q + t * C::kQTile + a * C::kAtom, h * D + a * 64,
+                      q0 + t * kFaBQ);
+      for (int j = 0; j < n; ++j) {
+        const int st = j % SK;
+        const uint32_t ph = (uint32_t)(j / SK) & 1u;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, s_abort, p.err, FERR_PRODUCER)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::kKStage);
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(&tm_k, &k_full[st], s_k + st * C::kKStage + a * C::kAtom,
+                      h * D + a * 64, j * kFaBK);
+        armed |= 1u << st;
+        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+      }
+      volatile int no_abort = 0;
+      mbar_wait(q_full, 0, &no_abort, p.err, FERR_DRAIN);
+      for (int st = 0; st < SK; ++st)
+        if (armed & (1u << st))
+          mbar_wait(&k_full[st], (armed_par >> st) & 1u, &no_abort, p.err, FERR_DRAIN);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------- V TMA
+    if (lane == 0) {
+      uint32_t armed = 0, armed_par = 0;
+      for (int j = 0; j < n; ++j) {
+        const int st = j % SV;
+        const uint32_t ph = (uint32_t)(j / SV) & 1u;
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, s_abort, p.err, FERR_PRODUCER)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::kVStage);
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(&tm_vt, &v_full[st], s_v + st * C::kVStage + a * (D * 128),
+                      j * kFaBK + a * 64, h * D);
+        armed |= 1u << st;
+        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+      }
+      volatile int no_abort = 0;
+      for (int st = 0; st < SV; ++st)
+        if (armed & (1u << st))
+          mbar_wait(&v_full[st], (armed_par >> st) & 1u, &no_abort, p.err, FERR_DRAIN);
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16(kFaBQ, kFaBK);
+      constexpr uint32_t idesc_o = idesc_bf16(kFaBQ, D);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t sk = smem_u32(s_k + (j % SK) * C::kKStage);
+        const uint32_t sq = smem_u32(s_q + t * C::kQTile);
+        const uint32_t d = tmem + C::kSCol + (uint32_t)t * kFaBK;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * C::kAtom);
+          umma_f16_ss(d, sdesc_k128_sw128(sq + off) + (uint64_t)(2 * (kk & 3)),
+                      sdesc_k128_sw128(sk + off) + (uint64_t)(2 * (kk & 3)), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t sv = smem_u32(s_v + (j % SV) * C::kVStage);
+        const uint32_t pa = tmem + C::kSCol + (uint32_t)t * kFaBK;
+#pragma unroll
+        for (int kk = 0; kk < kFaBK / 16; ++kk)
+          umma_f16_ts(tmem + C::kOCol + (uint32_t)t * D, pa + (uint32_t)(kk * 8),
+                      sdesc_k128_sw128(sv + (uint32_t)((kk >> 2) * (D * 128))) +
+                          (uint64_t)(2 * (kk & 3)),
+                      idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_full, 0, s_abort, p.err, FERR_MMA) &&
+                mbar_wait(&k_full[0], 0, s_abort, p.err, FERR_MMA);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const bool more = j + 1 < n;
+        // tile 0: P V, then its next S (in-order: the S MMA overwrites
+        // S0 only after this P V has read P0 from it)
+        if (!mbar_wait(&p_full[0], (uint32_t)j & 1u, s_abort, p.err, FERR_MMA) ||
+            !mbar_wait(&v_full[j % SV], (uint32_t)(j / SV) & 1u, s_abort, p.err, FERR_MMA))
+          break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&k_full[(j + 1) % SK], (uint32_t)((j + 1) / SK) & 1u, s_abort, p.err,
+                         FERR_MMA))
+            break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        if (!mbar_wait(&p_full[1], (uint32_t)j & 1u, s_abort, p.err, FERR_MMA)) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&v_empty[j % SV]);
+        if (more) {
+          issue_s(1, j + 1);
+          umma_commit(&k_empty[(j + 1) % SK]);
+        }
+      }
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.err, FERR_DRAIN);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    // warps 4-11: tile 0, 12-19: tile 1; within a tile the first four take
+    // score columns [0, 64), the next four [64, 128) of the same rows.
+    const int t = (warp - 4) >> 3;
+    const int hh = ((warp - 4) >> 2) & 1;
+    const int q = warp & 3;
+    const int r = q * 32 + (int)lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t scol = tmem + lane_base + C::kSCol + (uint32_t)t * kFaBK;
+    const uint32_t ocol = tmem + lane_base + C::kOCol + (uint32_t)t * D + (uint32_t)hh * (D / 2);
+    const float c = p.scale_log2;
+    float m_run = 0.0f, l_run = 0.0f;
+    bool ok = true;
+    // Every warp of a tile takes the same n + 1 named barriers, also after an
+    // abort (which then only skips the TMEM work), so none is left waiting.
+    for (int i = 0; i < n; ++i) {
+      ok = __all_sync(0xffffffffu,
+                      ok && mbar_wait(&s_full[t], (uint32_t)i & 1u, s_abort, p.err, FERR_SOFTMAX));
+      // after an abort the reads below see whatever TMEM holds (still
+      // allocated); only the mbarrier traffic is skipped
+      uint32_t a[32], b[32];
+      float m4[4] = {-3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};
+      tc_fence_after();
+      const int valid = p.tk - i * kFaBK - hh * 64;   // valid columns of this half
+      tmem_ld32(scol + (uint32_t)(hh * 64), a);
+      tmem_ld32(scol + (uint32_t)(hh * 64 + 32), b);
+      tmem_wait_ld();
+      if (valid < 64) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (e >= valid) a[e] = __float_as_uint(-3.0e38f);
+          if (32 + e >= valid) b[e] = __float_as_uint(-3.0e38f);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        m4[0] = max3f(m4[0], __uint_as_float(a[e]), __uint_as_float(a[e + 1]));
+        m4[1] = max3f(m4[1], __uint_as_float(a[e + 2]), __uint_as_float(a[e + 3]));
+        m4[2] = max3f(m4[2], __uint_as_float(b[e]), __uint_as_float(b[e + 1]));
+        m4[3] = max3f(m4[3], __uint_as_float(b[e + 2]), __uint_as_float(b[e + 3]));
+      }
+      // the row's max over both halves: exchange through shared memory (both
+      // halves have their scores in registers after this barrier, so either
+      // may then overwrite the TMEM columns with P)
+      s_mx[t][i & 1][hh][r] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      named_bar_sync(1 + t, 256);
+      if (!ok) continue;
+      const float mx = fmaxf(s_mx[t][i & 1][0][r], s_mx[t][i & 1][1][r]);
+      const float m_tile = mx * c;
+      if (i == 0) m_run = m_tile;
+      const bool need = i > 0 && m_tile > m_run + kRescale;
+      // the O rescale waits until P is in TMEM, so the scores' registers are
+      // free by then (P must only land before p_full is signalled)
+      const bool rescale = __any_sync(0xffffffffu, need);
+      float f = 1.0f;
+      if (rescale) {
+        const float m_new = need ? m_tile : m_run;
+        f = fast_exp2(m_run - m_new);
+        l_run *= f;
+        m_run = m_new;
+      }
+      const unsigned long long c2 = pair2(__float_as_uint(c), __float_as_uint(c));
+      const unsigned long long nm2 = pair2(__float_as_uint(-m_run), __float_as_uint(-m_run));
+      unsigned long long sa = 0ull, sb = 0ull;
+      uint32_t pk[32];
+      fa3_exp(a, b, c2, nm2, pk, sa, sb);
+      tmem_st32(scol + (uint32_t)(hh * 32), pk);
+      const unsigned long long st2 = fadd2(sa, sb);
+      l_run += __uint_as_float((uint32_t)st2) + __uint_as_float((uint32_t)(st2 >> 32));
+      if (rescale)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&o_done[t], (uint32_t)(i - 1) & 1u, s_abort, p.err,
+                                  FERR_SOFTMAX));
+      if (rescale && ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c4 = 0; c4 < D / 64; ++c4) {
+          uint32_t v[32];
+          tmem_ld32(ocol + (uint32_t)(c4 * 32), v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * f);
+          tmem_st32(ocol + (uint32_t)(c4 * 32), v);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&p_full[t]);
+    }
+    // the row's sum over both halves (parity slot 0/1 of tile i are free now)
+    s_mx[t][n & 1][hh][r] = l_run;
+    named_bar_sync(1 + t, 256);
+    const float l_row = s_mx[t][n & 1][0][r] + s_mx[t][n & 1][1][r];
+    if (ok && n > 0 &&
+        mbar_wait(&o_done[t], (uint32_t)(n - 1) & 1u, s_abort, p.err, FERR_SOFTMAX)) {
+      tc_fence_after();
+      const int row = q0 + t * kFaBQ + r;
+      float g = 1.0f / l_row;
+      if (p.gate != nullptr && row < p.tq)
+        g *= 2.0f / (1.0f + __expf(-__bfloat162float(p.gate[(size_t)row * p.ldg + h])));
+      __nv_bfloat16* orow = p.o + (size_t)row * p.ldo + h * D + hh * (D / 2);
+#pragma unroll
+      for (int c4 = 0; c4 < D / 64; ++c4) {
+        uint32_t v[32];
+        tmem_ld32(ocol + (uint32_t)(c4 * 32), v);
+        tmem_wait_ld();
+        if (row < p.tq) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(v[8 * e + 0]) * g, __uint_as_float(v[8 * e + 1]) * g);
+            w.y = pack_bf16(__uint_as_float(v[8 * e + 2]) * g, __uint_as_float(v[8 * e + 3]) * g);
+            w.z = pack_bf16(__uint_as_float(v[8 * e + 4]) * g, __uint_as_float(v[8 * e + 5]) * g);
+            w.w = pack_bf16(__uint_as_float(v[8 * e + 6]) * g, __uint_as_float(v[8 * e + 7]) * g);
+            *reinterpret_cast<uint4*>(orow + c4 * 32 + 8 * e) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 // Merge split-KV partials: for each (row, head), weights 2^(m_s - max m),
 // o = sum_s w_s O_s / sum_s w_s l_s, times the gate; 4 columns per thread.
 __global__ void fa_combine_kernel(const float* __restrict__ part_o,
@@ -1089,6 +1439,26 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
     two_tiles = (e != nullptr && e[0] == '1') ? 0 : 1;
   }
   if (tq <= kFaBQ || !two_tiles) return launch_fa<128, false>(tq_map, tk_map, tv_map, prm, heads, s);
+  // kernel for tq > 128: split rows (default) or whole rows a softmax warp
+  // (LTX25_FA_KIND=2)
+  static int kind = -1;
+  if (kind < 0) {
+    const char* e = getenv("LTX25_FA_KIND");
+    kind = (e != nullptr && e[0] == '2') ? 2 : 3;
+  }
+  const dim3 grid2((tq + 2 * kFaBQ - 1) / (2 * kFaBQ), heads);
+  if (kind == 3) {
+    static bool attr3 = false;
+    if (!attr3) {
+      if (cudaFuncSetAttribute(fa3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Fa3Cfg::kSmem) != cudaSuccess)
+        return -1;
+      attr3 = true;
+    }
+    launch_k(fa3_tc_kernel, grid2, dim3(kFa3Threads), Fa3Cfg::kSmem, s, 1, tq_map, tk_map,
+             tv_map, prm);
+    return launched();
+  }
   static bool attr2 = false;
   if (!attr2) {
     if (cudaFuncSetAttribute(fa2_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1096,7 +1466,8 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
       return -1;
     attr2 = true;
   }
-  launch_k(fa2_tc_kernel, dim3(dim3((tq + 2 * kFaBQ - 1) / (2 * kFaBQ), heads)), dim3(kFa2Threads), Fa2Cfg::kSmem, s, 1, tq_map, tk_map, tv_map, prm);
+  launch_k(fa2_tc_kernel, grid2, dim3(kFa2Threads), Fa2Cfg::kSmem, s, 1, tq_map, tk_map, tv_map,
+           prm);
   return launched();
 }
 
