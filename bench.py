@@ -82,6 +82,22 @@ def peaks():
         return 1590.0, 6650.0, "fallback"
 
 
+def tensor_peak_for(clocks):
+    """Burst or sustained bf16 peak from MEASURED_PEAKS.json, by the clocks the
+    timed region ran at: below 85 % of the maximum SM clock the run was in the
+    power-capped regime the sustained figure was measured in."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        burst, sus = float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"])
+    except Exception:
+        return 1590.0, "fallback (burst)"
+    mhz, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if mhz is not None and mx and mhz < 0.85 * mx:
+        return sus, "measured bf16_tflops_sustained (median SM clock %.0f of %.0f MHz)" % (mhz, mx)
+    return burst, "measured bf16_tflops (burst)"
+
+
 def traffic_from_profile():
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu
     summary (profiles/traffic.json), or None."""
@@ -115,16 +131,27 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a while to print its first sample; the timed
+            # region starts only once it does (at most 5 s), so short regions
+            # are sampled too
+            t0 = time.monotonic()
+            while not self.lines and time.monotonic() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
+        self.t_start = time.monotonic()
+        self.t_stop = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
     def __exit__(self, *a):
+        self.t_stop = time.monotonic()
         if self.proc is not None:
+            # one more sample period so the region's tail is covered
+            time.sleep(0.15)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -133,10 +160,15 @@ class ClockSampler:
             self.t.join(timeout=5)
 
     def summary(self):
+        """Median SM clock and the throttle reasons seen over the samples
+        taken inside the timed region (the sample just after it included)."""
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
                  "sw_power_cap"]
-        for ln in self.lines:
+        stop = (self.t_stop if self.t_stop is not None else time.monotonic()) + 0.15
+        for ts, ln in self.lines:
+            if ts < self.t_start or ts > stop:
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -711,6 +743,8 @@ def main():
         cpu = {"value": f / s / 1e12, "unit": UNIT, "cores": 1, "kind": kind,
                "sample": sample_desc(), "seconds": round(s, 2)}
 
+    clocks = clk.summary()
+    tpeak, tpeak_kind = tensor_peak_for(clocks)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -731,12 +765,13 @@ def main():
                 "ms_per_step": round(e2e_ms, 3),
                 "api": "ltx_qlinear via ctypes, pinned host buffers"},
         "gpu_launches": int(launches),
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "roofline": {
             "bound": "tensor", "achieved": round(achieved, 1),
-            "peak": bf16_peak, "unit": "TFLOP/s",
-            "frac": round(achieved / bf16_peak, 4),
-            "peak_source": f"{peak_kind} bf16_tflops (burst)",
+            "peak": tpeak, "unit": "TFLOP/s",
+            "frac": round(achieved / tpeak, 4),
+            "frac_of_burst": round(achieved / bf16_peak, 4),
+            "peak_source": tpeak_kind,
             "kernel": ("dequant_w8_kernel + gemm_tc_kernel<MODE_BF16,TN=256> (route auto: "
                        "M >= %d expands the weight once per call, src/ltx25-metal-ops.cc:"
                        "468-545) over the 6 M=8160 shapes; time covers both" % L.DEQUANT_MIN_M)

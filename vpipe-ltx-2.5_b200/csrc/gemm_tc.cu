@@ -1,6 +1,7 @@
 // gemm_tc.cu -- kernel body and launcher for the tcgen05 GEMM described in
 // gemm_tc.cuh.
 #include <cstdio>
+#include <cstdlib>
 
 #include "gemm_tc.cuh"
 #include "block_ops.h"
@@ -10,7 +11,7 @@ namespace ltx {
 
 namespace {
 
-constexpr int kGroupM = 8;  // raster: 8 token tiles share each weight sweep
+constexpr int kGroupM = 8;  // default raster: 8 token tiles share each weight sweep
 
 __device__ __forceinline__ void decode_tile(const GemmParams& p, int t,
                                             int& m_tile, int& n_tile,
@@ -18,10 +19,11 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t,
 {
   const int split = t % p.splits;
   const int mn = t / p.splits;
-  const int group = kGroupM * p.n_tiles;
+  const int group_m = p.group_m > 0 ? p.group_m : kGroupM;
+  const int group = group_m * p.n_tiles;
   const int g = mn / group;
-  const int first_m = g * kGroupM;
-  const int gm = min(p.m_tiles - first_m, kGroupM);
+  const int first_m = g * group_m;
+  const int gm = min(p.m_tiles - first_m, group_m);
   const int r = mn - g * group;
   m_tile = first_m + r % gm;
   n_tile = r / gm;
@@ -710,7 +712,13 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
   using C = GemmCfg<MODE, TN, PAIR>;
   CUtensorMap tx, tw, tsz;
   memset(&tsz, 0, sizeof(tsz));
-  const GemmParams& p = L.p;
+  GemmParams p = L.p;
+  static int group_m = -1;
+  if (group_m < 0) {
+    const char* e = getenv("LTX25_GROUP_M");
+    group_m = e != nullptr ? atoi(e) : 0;
+  }
+  if (p.group_m == 0) p.group_m = group_m;
   if (MODE == MODE_I8) {
     if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.x, p.K, p.M, L.ldx,
                    128, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))

@@ -71,6 +71,7 @@ struct GemmParams {
   const float* sx;             // MODE_I8: [M] token scales
   const float* sw;             // MODE_I8: [N] channel scales
   int* err;                    // device error word (0 = ok)
+  int group_m;                 // raster: token tiles per weight sweep (0 = 8)
   // Diagnostics (null = off): kTraceSlots u64 per CTA for the first
   // `trace_ctas` CTAs -- phase timestamps (clock64) and the MMA issuer's
   // cumulative wait cycles per barrier kind.
@@ -102,7 +103,7 @@ struct GemmCfg {
   static constexpr int kSZStage = MODE == MODE_W8G64 ? kBM * 4 : 0;
   static constexpr int kStageBytes = kXStage + kWStage + kSZStage;
   static constexpr int kStages =
-      (220 * 1024) / kStageBytes > 8 ? 8 : (220 * 1024) / kStageBytes;
+      (224 * 1024) / kStageBytes > 8 ? 8 : (224 * 1024) / kStageBytes;
   static constexpr int kNAcc =
       MODE == MODE_W8G64 ? (2 * TN + 4 * 32 <= 512 ? 2 : 1) : 2;
   static constexpr int kASlotsRaw = (512 - kNAcc * TN) / 32;
