@@ -169,6 +169,43 @@ LTX_API int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                    int ldx, const void* bias, void* y, int ldy, int M, int K,
                    int N, int epilogue, const void* gate, void* stream);
 
+/* ---- low-rank adapters ---------------------------------------------------
+ * Replace one module's LoraPair as LoraAdapter::load binds it (src/
+ * ltx25-lora.h:48-56, src/ltx25-lora.cc:56-124) and MetalOps::lora_add
+ * (src/ltx25-metal-ops.h:107-132, src/ltx25-metal-ops.cc:986-1000).
+ * a is [rank][k] and b [n][rank], bf16, both in the [out][in] order the
+ * checkpoint stores (neither is transposed).  `scale` -- lora_scale times
+ * the adapter's alpha / rank, which the caller reads from its metadata --
+ * is folded into a at upload: a' = bf16(f32(a) * scale), one rounding, as
+ * the reference's loader does.  k must be a multiple of 8, n even.
+ * on_device != 0: a and b are device memory.  The pair is copied; the
+ * caller's arrays may be freed after the call. */
+typedef struct ltx_lora ltx_lora;
+LTX_API int ltx_lora_upload(ltx_ctx* ctx, const uint16_t* a, const uint16_t* b, int rank,
+                            int k, int n, float scale, int on_device, ltx_lora** out);
+LTX_API void ltx_lora_free(ltx_lora* l);
+LTX_API int ltx_lora_info(const ltx_lora* l, int* rank, int* k, int* n);
+
+/* y[M][N] += (x[M][K] . A^T) . B^T for a y that already holds the linear
+ * it adapts (MetalOps::lora_add).  K == k, N == n; row strides ldx, ldy in
+ * elements.  x.A^T goes to the context's scratch; the add is the second
+ * GEMM's epilogue, so no [M][N] delta is written (the reference's
+ * matrix-core pair, src/ltx25-metal-ops.h:850-866). */
+LTX_API int ltx_lora_add(ltx_ctx* ctx, const ltx_lora* l, const void* x, int ldx, void* y,
+                         int ldy, int M, int K, int N, void* stream);
+
+/* ltx_qlinear_ex with an adapter on the linear: y = epilogue(x.W^T + bias
+ * + (x.A^T).B^T).  The delta is contracted in the linear's own GEMM
+ * accumulator (extra K blocks after the weight's), so it lands before the
+ * GELU / gated residual, where the reference's MetalBlock::lora_ puts it
+ * (between a linear and its consumer, src/ltx25-block-metal.cc:404-420).
+ * An adapted linear takes the bf16 route (the pack expanded once) whatever
+ * its M or tier.  l == NULL is ltx_qlinear_ex. */
+LTX_API int ltx_qlinear_lora(ltx_ctx* ctx, const ltx_qweight* w, const ltx_lora* l,
+                             const void* x, int ldx, const void* bias, void* y, int ldy,
+                             int M, int K, int N, int epilogue, const void* gate,
+                             void* stream);
+
 /* Route for quantized weights (LTX_ROUTE_*).  Default AUTO, the reference's
  * own choice (MetalOps::linear -> dequant_mma_, src/ltx25-metal-ops.cc:
  * 343-347, 468-545): a call tall enough to be tensor-bound expands the
@@ -309,6 +346,22 @@ LTX_API int ltx_block_set_qlinear(ltx_block* b, const char* name,
 LTX_API int ltx_block_set_tensor(ltx_block* b, const char* name,
                                  const float* data, int rows, int cols,
                                  int on_device);
+
+/* Attach one module's adapter (MetalBlock::lora_ with the LoraBlock the
+ * reference's loader builds, src/ltx25-block-metal.cc:404-420, src/
+ * ltx25-lora.h:58-76) under the module's reference name: "attn1.to_q",
+ * ".to_k", ".to_v", ".to_out.0", ".to_gate_logits" of attn1, attn2,
+ * audio_attn1, audio_attn2, audio_to_video_attn, video_to_audio_attn, and
+ * "ff.net.0.proj", "ff.net.2", "audio_ff.net.0.proj", "audio_ff.net.2".
+ * Call before ltx_block_finalize, which checks each pair against its base
+ * linear (LTX_E_SHAPE), shards it like the base weight under tensor
+ * parallelism and copies it; the pair may be freed afterwards.  A name this
+ * block does not apply returns LTX_E_UNSUPPORTED, as the reference's loader
+ * refuses an adapter naming a module it would not apply; after finalize,
+ * LTX_E_STATE.  Each adapted linear contracts its delta in its own GEMM
+ * (ltx_qlinear_lora), before the norm / GELU / gated residual that consumes
+ * it. */
+LTX_API int ltx_block_set_lora(ltx_block* b, const char* module, const ltx_lora* l);
 
 /* Check every required tensor is present (naming the first missing one,
  * as load_block_weights does), fuse the q/k/v and k/v packs, upload. */

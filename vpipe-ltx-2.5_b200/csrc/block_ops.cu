@@ -381,7 +381,47 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ a,
     out[i] = __float2bfloat16_rn(a[i]);
 }
 
+__global__ void fill_f32_kernel(float* __restrict__ out, float v, size_t n)
+{
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = v;
+}
+
+// out = bf16(f32(in) * scale), one rounding (the adapter's scale fold,
+// src/ltx25-lora.cc:56-68)
+__global__ void scale_bf16_kernel(const __nv_bfloat16* __restrict__ in,
+                                  __nv_bfloat16* __restrict__ out, float scale, size_t n)
+{
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __float2bfloat16_rn(__bfloat162float(in[i]) * scale);
+}
+
 }  // namespace
+
+int launch_fill_f32(float* out, float v, size_t n, cudaStream_t s)
+{
+  if (n == 0) return 0;
+  size_t grid = (n + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  launch_k(fill_f32_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, out, v, n);
+  return launched();
+}
+
+int launch_scale_bf16(const __nv_bfloat16* in, __nv_bfloat16* out, float scale, size_t n,
+                      cudaStream_t s)
+{
+  if (n == 0) return 0;
+  size_t grid = (n + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  launch_k(scale_bf16_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, in, out, scale, n);
+  return launched();
+}
 
 int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
                        cudaStream_t s)

@@ -18,6 +18,11 @@ unsigned long long launch_count();
 
 int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
                        cudaStream_t s);
+// out[i] = v
+int launch_fill_f32(float* out, float v, size_t n, cudaStream_t s);
+// out[i] = bf16(f32(in[i]) * scale), round to nearest even; in == out is fine
+int launch_scale_bf16(const __nv_bfloat16* in, __nv_bfloat16* out, float scale, size_t n,
+                      cudaStream_t s);
 
 // out[i] = a[i] + b[i] (b bf16, may be null), f32.
 int launch_vec_add(const float* a, const __nv_bfloat16* b, float* out, int n,

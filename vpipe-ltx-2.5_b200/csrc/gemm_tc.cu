@@ -87,7 +87,9 @@ template <int MODE, int TN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_w,
-                   const __grid_constant__ CUtensorMap tm_sz, GemmParams p)
+                   const __grid_constant__ CUtensorMap tm_sz,
+                   const __grid_constant__ CUtensorMap tm_ew,
+                   const __grid_constant__ CUtensorMap tm_ex, GemmParams p)
 {
   using C = GemmCfg<MODE, TN, PAIR>;
   constexpr int S = C::kStages;
@@ -191,14 +193,18 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
           if (tr) w_empty += clock64() - c0;
           armed |= 1u << stage;
           armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
-          const int kx = kb * C::kKPerStage;
+          // K blocks past kblocks_main contract the extension (r.B^T)
+          const bool ext = MODE == MODE_BF16 && p.kblocks_main > 0 && kb >= p.kblocks_main;
+          const CUtensorMap* mx = ext ? &tm_ex : &tm_x;
+          const CUtensorMap* mw = ext ? &tm_ew : &tm_w;
+          const int kx = (ext ? kb - p.kblocks_main : kb) * C::kKPerStage;
           if constexpr (PAIR && MODE == MODE_BF16) {
             // Both CTAs' halves of both operands complete on the leader's
             // barrier, which the leader arms for all four.
             if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (C::kXStage + C::kWStage));
             const uint32_t lf = mapa_shared(smem_u32(&full[stage]), 0);
-            tma_load_2d_pair(&tm_x, lf, s_x + stage * C::kXStage, kx, xrow0);
-            tma_load_2d_pair(&tm_w, lf, s_w + stage * C::kWStage, kx, wrow0);
+            tma_load_2d_pair(mx, lf, s_x + stage * C::kXStage, kx, xrow0);
+            tma_load_2d_pair(mw, lf, s_w + stage * C::kWStage, kx, wrow0);
           } else if constexpr (PAIR) {
             // Both halves of the activation tile complete on the leader's
             // barrier (it arms them); the codes on this CTA's own.
@@ -210,8 +216,8 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
             tma_load_2d(&tm_sz, &cfull[stage], s_sz + stage * C::kBM, wrow0, kb);
           } else {
             mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-            tma_load_2d(&tm_x, &full[stage], s_x + stage * C::kXStage, kx, xrow0);
-            tma_load_2d(&tm_w, &full[stage], s_w + stage * C::kWStage, kx, wrow0);
+            tma_load_2d(mx, &full[stage], s_x + stage * C::kXStage, kx, xrow0);
+            tma_load_2d(mw, &full[stage], s_w + stage * C::kWStage, kx, wrow0);
             if constexpr (MODE == MODE_W8G64) {
               tma_load_2d(&tm_sz, &full[stage], s_sz + stage * C::kBM, wrow0, kb);
             }
@@ -744,6 +750,20 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
         return -1;
     }
   }
+  // The extension maps: the adapter's B [N][ext_k] beside the weight and
+  // r [M][ext_k] beside the activations, same boxes; copies of the main
+  // maps when there is no extension (never read then).
+  CUtensorMap tew = tw, tex = tx;
+  if (L.ext_k > 0) {
+    if (MODE != MODE_BF16 || L.ext_k % 8 != 0 || L.ld_ext < L.ext_k || L.ld_ext % 8 != 0 ||
+        L.ext_w == nullptr || L.ext_x == nullptr)
+      return -1;
+    if (!encode_2d(&tew, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, L.ext_w, L.ext_k, p.N,
+                   (uint64_t)L.ext_k * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&tex, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, L.ext_x, L.ext_k, p.M,
+                   (uint64_t)L.ld_ext * 2, 64, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return -1;
+  }
   auto kern = gemm_tc_kernel<MODE, TN, EPI, PAIR>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -766,7 +786,8 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
     grid = p.num_tiles;
     cluster = p.splits;
   }
-  launch_k(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, cluster, tx, tw, tsz, p);
+  launch_k(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, cluster, tx, tw, tsz,
+           tew, tex, p);
   return launched() == 0 ? 0 : -3;
 }
 

@@ -62,7 +62,11 @@ struct GemmParams {
   int M, N, K;             // tokens, output features, input features
   int m_tiles, n_tiles;    // ceil(M/TN), ceil(N/128)
   int splits;              // K splits (1 = no split)
-  int kblocks;             // K / bytes-per-stage
+  int kblocks;             // K blocks in all (main + extension)
+  // K blocks of x.W^T; the blocks after them read the extension maps (a
+  // low-rank adapter's r.B^T, MODE_BF16 only) into the same accumulator.
+  // 0 or == kblocks: no extension.
+  int kblocks_main;
   int num_tiles;           // m_tiles * n_tiles * splits
   int ldy;                 // row stride of y, elements
   const __nv_bfloat16* bias;   // [N] or null

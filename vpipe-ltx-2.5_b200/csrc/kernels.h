@@ -32,6 +32,12 @@ struct GemmLaunch {
   int ldx = 0;             // elements
   const void* w = nullptr; // u8 codes [N][K] / bf16 [N][K] / int8 [N][K]
   const uint32_t* sz = nullptr;  // MODE_W8G64: [K/64][N] (scale | zp << 16)
+  // K extension (MODE_BF16): ext_w bf16 [N][ext_k] and ext_x bf16
+  // [M][ld_ext], contracted over ext_k after the main K (ext_k % 8 == 0).
+  const void* ext_w = nullptr;
+  const void* ext_x = nullptr;
+  int ext_k = 0;
+  int ld_ext = 0;
   GemmParams p{};
 };
 

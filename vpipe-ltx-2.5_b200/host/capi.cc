@@ -21,6 +21,10 @@ struct ltx_qweight {
   ltx25::QWeight w;
 };
 
+struct ltx_lora {
+  ltx25::LoraPair p;
+};
+
 namespace {
 
 int fail(ltx_ctx* c, int code, const std::string& m)
@@ -173,6 +177,95 @@ int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x, int ldx,
                        static_cast<const __nv_bfloat16*>(bias),
                        static_cast<__nv_bfloat16*>(y), ldy, M, K, N, epilogue,
                        static_cast<const float*>(gate), &e))
+    return fail(ctx, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_lora_upload(ltx_ctx* ctx, const uint16_t* a, const uint16_t* b, int rank, int k,
+                    int n, float scale, int on_device, ltx_lora** out)
+{
+  if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  ltx_lora* l = new (std::nothrow) ltx_lora();
+  if (l == nullptr) return fail(ctx, LTX_E_OOM, "host allocation failed");
+  std::string e;
+  if (!ltx25::upload_lora(ctx->ops, a, b, rank, k, n, scale, on_device != 0, &l->p, &e)) {
+    delete l;
+    return fail(ctx, code_for(e), e);
+  }
+  *out = l;
+  return LTX_OK;
+}
+
+void ltx_lora_free(ltx_lora* l)
+{
+  if (l == nullptr) return;
+  ltx25::free_lora(&l->p);
+  delete l;
+}
+
+int ltx_lora_info(const ltx_lora* l, int* rank, int* k, int* n)
+{
+  if (l == nullptr) return LTX_E_NULL;
+  if (rank) *rank = l->p.rank;
+  if (k) *k = l->p.k;
+  if (n) *n = l->p.n;
+  return LTX_OK;
+}
+
+int ltx_lora_add(ltx_ctx* ctx, const ltx_lora* l, const void* x, int ldx, void* y, int ldy,
+                 int M, int K, int N, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (l == nullptr || x == nullptr || y == nullptr)
+    return fail(ctx, LTX_E_NULL, "lora_add: null adapter, x or y");
+  if (K != l->p.k || N != l->p.n)
+    return fail(ctx, LTX_E_SHAPE,
+                "lora_add shape: K " + std::to_string(K) + ", N " + std::to_string(N) +
+                    " against the pair's k " + std::to_string(l->p.k) + ", n " +
+                    std::to_string(l->p.n));
+  if (M <= 0) return LTX_OK;
+  std::string e;
+  ltx25::LoraExt ext;
+  ext.a = l->p.a;
+  ext.b = l->p.b;
+  ext.r = l->p.r8;
+  ext.rbuf = ctx->ops.lora_rbuf((size_t)M * l->p.r8, &e);
+  if (ext.rbuf == nullptr) return fail(ctx, code_for(e), e);
+  if (!ctx->ops.lora_add(S(stream), static_cast<const __nv_bfloat16*>(x), ldx, ext,
+                         static_cast<__nv_bfloat16*>(y), ldy, M, K, N, &e))
+    return fail(ctx, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_qlinear_lora(ltx_ctx* ctx, const ltx_qweight* w, const ltx_lora* l, const void* x,
+                     int ldx, const void* bias, void* y, int ldy, int M, int K, int N,
+                     int epilogue, const void* gate, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (l == nullptr)
+    return ltx_qlinear_ex(ctx, w, x, ldx, bias, y, ldy, M, K, N, epilogue, gate, stream);
+  if (w == nullptr || x == nullptr || y == nullptr)
+    return fail(ctx, LTX_E_NULL, "qlinear_lora: null weight, x or y");
+  if (epilogue < LTX_EPI_STORE || epilogue > LTX_EPI_GATED_RES)
+    return fail(ctx, LTX_E_SHAPE, "qlinear_lora: unknown epilogue");
+  if (K != l->p.k || N != l->p.n)
+    return fail(ctx, LTX_E_SHAPE,
+                "qlinear_lora shape: K " + std::to_string(K) + ", N " + std::to_string(N) +
+                    " against the pair's k " + std::to_string(l->p.k) + ", n " +
+                    std::to_string(l->p.n));
+  if (M <= 0) return fail(ctx, LTX_E_SHAPE, "qlinear_lora shape: M <= 0");
+  std::string e;
+  ltx25::LoraExt ext;
+  ext.a = l->p.a;
+  ext.b = l->p.b;
+  ext.r = l->p.r8;
+  ext.rbuf = ctx->ops.lora_rbuf((size_t)M * l->p.r8, &e);
+  if (ext.rbuf == nullptr) return fail(ctx, code_for(e), e);
+  if (!ctx->ops.linear(S(stream), static_cast<const __nv_bfloat16*>(x), ldx, w->w,
+                       static_cast<const __nv_bfloat16*>(bias),
+                       static_cast<__nv_bfloat16*>(y), ldy, M, K, N, epilogue,
+                       static_cast<const float*>(gate), &e, &ext))
     return fail(ctx, code_for(e), e);
   return LTX_OK;
 }
@@ -489,6 +582,19 @@ int ltx_block_set_tensor(ltx_block* b, const char* name, const float* data,
   std::string e;
   if (!b->blk->set_tensor(name, data, rows, cols, on_device != 0, &e))
     return bfail(b, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_block_set_lora(ltx_block* b, const char* module, const ltx_lora* l)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  if (module == nullptr || l == nullptr)
+    return bfail(b, LTX_E_NULL, "set_lora: null module name or adapter");
+  std::string e;
+  if (!b->blk->set_lora(module, l->p, &e)) {
+    const int code = e.find("finalized") != std::string::npos ? LTX_E_STATE : code_for(e);
+    return bfail(b, code, e);
+  }
   return LTX_OK;
 }
 

@@ -193,6 +193,103 @@ bool CudaBlock::fuse_(const std::vector<Part>& parts, QWeight* out,
   return true;
 }
 
+namespace {
+
+// The modules an adapter may name, as the reference's loader binds them
+// (src/ltx25-lora.cc:328-360).
+bool known_module(const std::string& m)
+{
+  for (const char* a : {"attn1", "attn2", "audio_attn1", "audio_attn2",
+                        "audio_to_video_attn", "video_to_audio_attn"})
+    for (const char* s : {".to_q", ".to_k", ".to_v", ".to_out.0", ".to_gate_logits"})
+      if (m == std::string(a) + s) return true;
+  for (const char* f : {"ff.net.0.proj", "ff.net.2", "audio_ff.net.0.proj", "audio_ff.net.2"})
+    if (m == f) return true;
+  return false;
+}
+
+}  // namespace
+
+bool CudaBlock::set_lora(const std::string& module, const LoraPair& pair, std::string* err)
+{
+  if (_final) return fail(err, "block already finalized (attach adapters before finalize)");
+  if (!known_module(module))
+    return fail(err, "adapter names '" + module + "', which this block does not apply "
+                     "(not run by this build)");
+  if (pair.a == nullptr || pair.b == nullptr || pair.rank <= 0)
+    return fail(err, "adapter '" + module + "': null pair");
+  _lora[module] = pair;
+  return true;
+}
+
+const LoraPair* CudaBlock::lora_of_(const std::string& module, int k, int n,
+                                    std::string* err) const
+{
+  auto it = _lora.find(module);
+  if (it == _lora.end()) return nullptr;
+  const LoraPair& p = it->second;
+  if (p.k != k || p.n != n) {
+    if (err && err->empty())
+      *err = "adapter '" + module + "' is [" + std::to_string(p.n) + "][" +
+             std::to_string(p.rank) + "] x [" + std::to_string(p.rank) + "][" +
+             std::to_string(p.k) + "], the base linear reads " + std::to_string(k) +
+             " and writes " + std::to_string(n) + " (shape)";
+    return nullptr;
+  }
+  return &p;
+}
+
+bool CudaBlock::build_lora_(const std::vector<LPart>& parts, int K, LoraSite* out,
+                            std::string* err)
+{
+  int r = 0, N = 0;
+  for (const LPart& pt : parts) {
+    if (pt.p != nullptr) r += pt.p->r8;
+    N += pt.rows;
+  }
+  *out = LoraSite{};
+  if (r == 0) return true;
+  __nv_bfloat16 *a = nullptr, *b = nullptr;
+  if (!cuda_ok(cudaMalloc(&a, (size_t)r * K * 2), "cudaMalloc(adapter a)", err)) return false;
+  _owned.push_back(a);
+  if (!cuda_ok(cudaMalloc(&b, (size_t)N * r * 2), "cudaMalloc(adapter b)", err)) return false;
+  _owned.push_back(b);
+  if (!cuda_ok(cudaMemset(b, 0, (size_t)N * r * 2), "adapter b", err)) return false;
+  int ro = 0, n0 = 0;
+  for (const LPart& pt : parts) {
+    if (pt.p != nullptr) {
+      const LoraPair& p = *pt.p;
+      if (pt.k0 + K > p.k || pt.r0 + pt.rows > p.n)
+        return fail(err, "adapter shard out of range");
+      if (!cuda_ok(cudaMemcpy2D(a + (size_t)ro * K, (size_t)K * 2, p.a + pt.k0, (size_t)p.k * 2,
+                                (size_t)K * 2, p.r8, cudaMemcpyDeviceToDevice),
+                   "adapter a", err) ||
+          !cuda_ok(cudaMemcpy2D(b + (size_t)n0 * r + ro, (size_t)r * 2,
+                                p.b + (size_t)pt.r0 * p.r8, (size_t)p.r8 * 2, (size_t)p.r8 * 2,
+                                pt.rows, cudaMemcpyDeviceToDevice),
+                   "adapter b", err))
+        return false;
+      ro += p.r8;
+    }
+    n0 += pt.rows;
+  }
+  out->a = a;
+  out->b = b;
+  out->r = r;
+  _lora_rmax = std::max(_lora_rmax, r);
+  return true;
+}
+
+const LoraExt* CudaBlock::lx_(const LoraSite& site, LoraExt* tmp) const
+{
+  if (site.r == 0) return nullptr;
+  tmp->a = site.a;
+  tmp->b = site.b;
+  tmp->r = site.r;
+  tmp->rbuf = _cur->lr;
+  return tmp;
+}
+
 bool CudaBlock::build_attn_(const std::string& p, bool self, int qdim,
                             int kvdim, int heads, int head_dim, int odim,
                             CudaAttn& a, std::string* err)
@@ -302,7 +399,28 @@ bool CudaBlock::build_attn_(const std::string& p, bool self, int qdim,
                     (size_t)R * hl, (size_t)hl))
       return false;
   }
-  return true;
+  // Adapters, sharded like the weights they ride on: q/k/v and gate rows
+  // of this rank's heads; the output projection's A keeps this rank's K
+  // columns (its partial products are summed with the base's).
+  std::string lerr;
+  const LoraPair* lq = lora_of_(p + ".to_q", qdim, inner, &lerr);
+  const LoraPair* lk = lora_of_(p + ".to_k", kvdim, inner, &lerr);
+  const LoraPair* lv = lora_of_(p + ".to_v", kvdim, inner, &lerr);
+  const LoraPair* lo = lora_of_(p + ".to_out.0", inner, odim, &lerr);
+  const LoraPair* lg = lora_of_(p + ".to_gate_logits", qdim, heads, &lerr);
+  if (!lerr.empty()) return fail(err, lerr);
+  if (lg != nullptr && a.gate.N == 0)
+    return fail(err, p + ".to_gate_logits: adapter on a block without gate logits");
+  if (self) {
+    if (!build_lora_({{lq, c0, il, 0}, {lk, c0, il, 0}, {lv, c0, il, 0}}, qdim, &a.l_qkv, err))
+      return false;
+  } else {
+    if (!build_lora_({{lq, c0, il, 0}}, qdim, &a.l_q, err) ||
+        !build_lora_({{lk, c0, il, 0}, {lv, c0, il, 0}}, kvdim, &a.l_kv, err))
+      return false;
+  }
+  return build_lora_({{lo, 0, odim, W > 1 ? c0 : 0}}, W > 1 ? il : inner, &a.l_o, err) &&
+         build_lora_({{lg, R * hl, hl, 0}}, qdim, &a.l_gate, err);
 }
 
 bool CudaBlock::build_stream_(bool audio, CudaStreamW& w, std::string* err)
@@ -334,6 +452,13 @@ bool CudaBlock::build_stream_(bool audio, CudaStreamW& w, std::string* err)
   w.ff_hidden = fl;
   if (!fuse_({{&fi->second.q, f0, fl, 0, 0}}, &w.ff_in, err) ||
       !fuse_({{&fo->second.q, 0, d, W > 1 ? f0 : 0, W > 1 ? fl : 0}}, &w.ff_out, err))
+    return false;
+  std::string lerr;
+  const LoraPair* lfi = lora_of_(pre + "ff.net.0.proj", d, hidden, &lerr);
+  const LoraPair* lfo = lora_of_(pre + "ff.net.2", hidden, d, &lerr);
+  if (!lerr.empty()) return fail(err, lerr);
+  if (!build_lora_({{lfi, f0, fl, 0}}, d, &w.l_ff_in, err) ||
+      !build_lora_({{lfo, 0, d, W > 1 ? f0 : 0}}, W > 1 ? fl : hidden, &w.l_ff_out, err))
     return false;
   // Video ff has no bias, audio ff does (src/ltx25-dit-weights.cc:482-486).
   if (!take_bf16_(pre + "ff.net.0.proj.bias", hidden, &w.ff_in_b, err, false, f0, fl) ||
@@ -376,6 +501,12 @@ bool CudaBlock::finalize(std::string* err)
   for (auto& kv : _staged)
     if (kv.second.quant) free_qweight(&kv.second.q);
   _staged.clear();
+  _lora.clear();   // copied into the sites; the caller's pairs are free now
+  _audio_lora = false;
+  for (const CudaAttn* at : {&_audio.attn1, &_audio.attn2})
+    for (const LoraSite* ls : {&at->l_qkv, &at->l_q, &at->l_kv, &at->l_o, &at->l_gate})
+      _audio_lora = _audio_lora || ls->r > 0;
+  _audio_lora = _audio_lora || _audio.l_ff_in.r > 0 || _audio.l_ff_out.r > 0;
   _final = true;
   return true;
 }
@@ -385,17 +516,17 @@ BlockArena::~BlockArena()
   for (void* p : {(void*)normed, (void*)qkv, (void*)qn, (void*)kn, (void*)att,
                   (void*)glog, (void*)ctxmod, (void*)kvp, (void*)ff, (void*)qv,
                   (void*)kva, (void*)qa, (void*)kvv, (void*)mods, (void*)part,
-                  (void*)ssq, (void*)sp_send, (void*)sp_recv})
+                  (void*)ssq, (void*)sp_send, (void*)sp_recv, (void*)lr})
     cudaFree(p);
 }
 
 bool BlockArena::ensure(int i, size_t n, std::string* err)
 {
-  void** slots[18] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
+  void** slots[19] = {(void**)&normed, (void**)&qkv, (void**)&qn, (void**)&kn,
                       (void**)&att, (void**)&glog, (void**)&ctxmod, (void**)&kvp,
                       (void**)&ff, (void**)&qv, (void**)&kva, (void**)&qa,
                       (void**)&kvv, (void**)&mods, (void**)&part, (void**)&ssq,
-                      (void**)&sp_send, (void**)&sp_recv};
+                      (void**)&sp_send, (void**)&sp_recv, (void**)&lr};
   if (n <= cap[i]) return true;
   const size_t elt = (i == 13 || i == 15) ? sizeof(float) : sizeof(__nv_bfloat16);
   cudaFree(*slots[i]);
@@ -416,7 +547,7 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   const size_t vd = _vdim, ad = _adim;
   const size_t ai = ad;   // audio inner (the cross attentions' width too)
   auto mx = [](std::initializer_list<size_t> l) { return std::max(l); };
-  const size_t need[18] = {
+  const size_t need[19] = {
       mx({vt * vd, at * ad}),                                        // normed
       mx({vt * 3 * vd, at * 3 * ad, vt * vd, vt * ai, at * ai}),     // qkv / q
       mx({vt * vd, at * ad, vt * ai}),                               // qn
@@ -433,20 +564,22 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
       // sequence parallel: q, k, v of one head group for the whole sequence
       // (the video self-attention), or the v2a keys/values / outputs
       _sp ? 3 * vt * vd / _sp_world + at * ai : 0,                   // sp_send
-      _sp ? 3 * vt * vd / _sp_world + at * ai : 0};                  // sp_recv
+      _sp ? 3 * vt * vd / _sp_world + at * ai : 0,                   // sp_recv
+      mx({vt, at, tt}) * (size_t)_lora_rmax};                        // lr
   _arp = share ? share : std::make_shared<BlockArena>();
-  for (int i = 0; i < 18; ++i)
+  for (int i = 0; i < 19; ++i)
     if (!_arp->ensure(i, need[i], err)) return false;
   // The audio stream's own buffers, so that it can run beside the video
   // stream on a second CUDA stream (shared by the blocks like the rest).
   {
-    const size_t na[18] = {
+    const size_t na[19] = {
         at * ad, mx({at * 3 * ad, at * ai}), at * ad, mx({at * ad, tt * ad, at * ai}),
         at * ad, at * (size_t)_aheads, tt * ad, mx({tt * 2 * ad, at * 2 * ai}),
         at * (size_t)_audio.ff_hidden, 0, 0, 0, 0, 0,
-        _tp_world > 1 ? at * ad : 0, _tp_world > 1 ? 2 * (at + tt) : 0, 0, 0};
+        _tp_world > 1 ? at * ad : 0, _tp_world > 1 ? 2 * (at + tt) : 0, 0, 0,
+        mx({at, tt}) * (size_t)_lora_rmax};
     if (!_arp->side) _arp->side = std::make_shared<BlockArena>();
-    for (int i = 0; i < 18; ++i)
+    for (int i = 0; i < 19; ++i)
       if (!_arp->side->ensure(i, na[i], err)) return false;
   }
   _arp->video = std::max(_arp->video, vt);
@@ -476,9 +609,10 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   const int I = a.inner;
   const __nv_bfloat16 *qraw, *kraw, *vraw;
   int ldq, ldkv;
+  LoraExt lx;
   if (a.self) {
     if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _cur->qkv, 3 * I, tq, a.qdim,
-                      3 * I, ltx::EPI_STORE, nullptr, err))
+                      3 * I, ltx::EPI_STORE, nullptr, err, lx_(a.l_qkv, &lx)))
       return false;
     qraw = _cur->qkv;
     kraw = _cur->qkv + I;
@@ -486,9 +620,9 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     ldq = ldkv = 3 * I;
   } else {
     if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _cur->qkv, I, tq, a.qdim, I,
-                      ltx::EPI_STORE, nullptr, err) ||
+                      ltx::EPI_STORE, nullptr, err, lx_(a.l_q, &lx)) ||
         !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _cur->kvp, 2 * I, tkv,
-                      a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err))
+                      a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err, lx_(a.l_kv, &lx)))
       return false;
     qraw = _cur->qkv;
     kraw = _cur->kvp;
@@ -517,7 +651,7 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   const __nv_bfloat16* glog = nullptr;
   if (a.gate.N > 0) {
     if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _cur->glog, a.heads, tq,
-                      a.qdim, a.heads, ltx::EPI_STORE, nullptr, err))
+                      a.qdim, a.heads, ltx::EPI_STORE, nullptr, err, lx_(a.l_gate, &lx)))
       return false;
     glog = _cur->glog;
   }
@@ -535,8 +669,9 @@ bool CudaBlock::attend_self_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bf
   // ALL heads, then an all-to-all to the whole sequence for this rank's
   // heads, attention, and an all-to-all back (DeepSpeed-Ulysses layout).
   const int I = a.inner, N = _sp_world, Il = I / N, tv = tl * N, hl = a.heads / N;
+  LoraExt lx;
   if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _cur->qkv, 3 * I, tl, a.qdim, 3 * I,
-                    ltx::EPI_STORE, nullptr, err))
+                    ltx::EPI_STORE, nullptr, err, lx_(a.l_qkv, &lx)))
     return false;
   if (ltx::launch_qk_norm_rope(_cur->qkv, 3 * I, _cur->qn, I, tl, a.heads, a.head_dim,
                                a.q_norm, r.cos, r.sin, kEps, s, nullptr, 0, 0, r.tbl_tokens,
@@ -554,7 +689,7 @@ bool CudaBlock::attend_self_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bf
     return false;
   // gate logits of this rank's tokens, all heads (applied on the way back)
   if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _cur->glog, a.heads, tl, a.qdim,
-                    a.heads, ltx::EPI_STORE, nullptr, err))
+                    a.heads, ltx::EPI_STORE, nullptr, err, lx_(a.l_gate, &lx)))
     return false;
   const __nv_bfloat16* qh = _cur->sp_recv;
   if (!_ops->attention(s, qh, Il, qh + blk, Il, qh + 2 * blk, Il, _cur->sp_send, Il, nullptr,
@@ -576,10 +711,11 @@ bool CudaBlock::attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfl
   // rank's video keys/values go to their heads' owners, each rank attends
   // all audio queries for its heads, and the outputs are gathered.
   const int I = a.inner, N = _sp_world, Il = I / N, tv = tl * N, hl = a.heads / N;
+  LoraExt lx;
   if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _cur->qkv, I, tq, a.qdim, I, ltx::EPI_STORE,
-                    nullptr, err) ||
+                    nullptr, err, lx_(a.l_q, &lx)) ||
       !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _cur->kvp, 2 * I, tl, a.kvdim, 2 * I,
-                    ltx::EPI_STORE, nullptr, err))
+                    ltx::EPI_STORE, nullptr, err, lx_(a.l_kv, &lx)))
     return false;
   if (ltx::launch_qk_norm_rope(_cur->qkv, I, _cur->qn, I, tq, a.heads, a.head_dim, a.q_norm,
                                qr.cos, qr.sin, kEps, s, nullptr, 0, 0, qr.tbl_tokens,
@@ -595,7 +731,7 @@ bool CudaBlock::attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfl
   if (!_comm->alltoall_bf16(_cur->sp_send, _cur->sp_recv, (size_t)tl * Il, 2, blk, s, err))
     return false;
   if (!_ops->linear(s, xq, a.qdim, a.gate, a.gate_b, _cur->glog, a.heads, tq, a.qdim, a.heads,
-                    ltx::EPI_STORE, nullptr, err))
+                    ltx::EPI_STORE, nullptr, err, lx_(a.l_gate, &lx)))
     return false;
   // this rank's heads of every audio query -> sp_send [rank][tq][Il]
   __nv_bfloat16* mine = _cur->sp_send + (size_t)_sp_rank * tq * Il;
@@ -613,14 +749,17 @@ bool CudaBlock::attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfl
 bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
                           const QWeight& w, const __nv_bfloat16* bias,
                           __nv_bfloat16* x, int n, int d, const float* gate,
-                          std::string* err)
+                          std::string* err, const LoraSite* lora)
 {
+  LoraExt lx;
+  const LoraExt* ext = lora != nullptr ? lx_(*lora, &lx) : nullptr;
   if (_tp_world == 1)
-    return _ops->linear(s, in, k, w, bias, x, d, n, k, d, ltx::EPI_GATED_RES, gate, err);
-  // Row split: this rank's K columns give a partial product; the sum over
-  // ranks, then the bias and the gated residual, once.
+    return _ops->linear(s, in, k, w, bias, x, d, n, k, d, ltx::EPI_GATED_RES, gate, err, ext);
+  // Row split: this rank's K columns give a partial product (the adapter's
+  // too, from its A columns); the sum over ranks, then the bias and the
+  // gated residual, once.
   if (!_ops->linear(s, in, k, w, nullptr, _cur->part, d, n, k, d, ltx::EPI_STORE,
-                    nullptr, err) ||
+                    nullptr, err, ext) ||
       !_ccur->allreduce_sum(_cur->part, (size_t)n * d, 1, s, err))
     return false;
   if (ltx::launch_gated_residual(x, d, _cur->part, bias, gate, n, d, s) != 0)
@@ -651,7 +790,7 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                     err))
     return false;
   if (!out_proj_(s, _cur->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, n, d,
-                 mods + (MOD_MSA + 2) * d, err))
+                 mods + (MOD_MSA + 2) * d, err, &w.attn1.l_o))
     return false;
   // Text cross-attention: query = mod(rms_norm(x)) (= ada_zero with the
   // cross rows), key/value = context modulated by the prompt table + driver.
@@ -665,7 +804,7 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                RopeRef{}, _cur->att, err))
     return false;
   return out_proj_(s, _cur->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x, n, d,
-                   mods + (MOD_CA + 2) * d, err);
+                   mods + (MOD_CA + 2) * d, err, &w.attn2.l_o);
 }
 
 bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
@@ -679,10 +818,11 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
       ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_MLP + 1) * d,
                            mods + MOD_MLP * d, kEps, true, s))
     return fail(err, "ff pre-norm launch failed");
+  LoraExt lx;
   return _ops->linear(s, _cur->normed, d, w.ff_in, w.ff_in_b, _cur->ff, w.ff_hidden, n,
-                      d, w.ff_hidden, ltx::EPI_GELU, nullptr, err) &&
+                      d, w.ff_hidden, ltx::EPI_GELU, nullptr, err, lx_(w.l_ff_in, &lx)) &&
          out_proj_(s, _cur->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, n, d,
-                   mods + (MOD_MLP + 2) * d, err);
+                   mods + (MOD_MLP + 2) * d, err, &w.l_ff_out);
 }
 
 bool CudaBlock::shard_io(const StreamIO& whole, StreamIO* shard, std::string* err) const
@@ -740,7 +880,9 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
   // The audio stream runs beside the video one on the context's second
   // CUDA stream while they are independent (first halves, feed-forwards),
   // when nothing it launches shares scratch or a communicator with video.
-  const bool conc = rv && ra && (_tp_world == 1 || _comm_side != nullptr) &&
+  // An adapted audio linear takes the bf16 route and expands its pack into
+  // the context's one dequant scratch, so such blocks keep audio in line.
+  const bool conc = rv && ra && (_tp_world == 1 || _comm_side != nullptr) && !_audio_lora &&
                     _ops->audio_side_ok(a.tokens, a.text_tokens, _aheads, _adim / _aheads, _layer);
   cudaStream_t sa = conc ? _ops->aux_stream(err) : s;
   if (conc && sa == nullptr) return false;
@@ -779,7 +921,7 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
     const RopeRef ac{a.cpe_cos, a.cpe_sin, a.tokens, 0};
     if (!attend_(s, _a2v, _arp->qv, v.tokens, _arp->kva, a.tokens, vc, ac, _arp->att, err) ||
         !out_proj_(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, v.tokens, vd,
-                   vm + MOD_AVG * vd, err))
+                   vm + MOD_AVG * vd, err, &_a2v.l_o))
       return false;
     // v2a: audio queries, video keys/values
     if ((_sp ? !attend_v2a_sp_(s, _v2a, _arp->qa, a.tokens, ac, _arp->kvv, v.tokens, vc,
@@ -787,7 +929,7 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
              : !attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, v.tokens, ac, vc, _arp->att,
                         err)) ||
         !out_proj_(s, _arp->att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, a.tokens, ad,
-                   am + MOD_AVG * ad, err))
+                   am + MOD_AVG * ad, err, &_v2a.l_o))
       return false;
   }
 

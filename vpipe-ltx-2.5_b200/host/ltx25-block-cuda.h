@@ -28,6 +28,15 @@
 
 namespace ltx25 {
 
+// One GEMM site's adapters (src/ltx25-lora.h:58-76): the pairs of the
+// modules the GEMM computes, A stacked [r][K] and B block-diagonal [N][r]
+// over the site's output rows, sharded like the base weight.  r == 0: none.
+struct LoraSite {
+  __nv_bfloat16* a = nullptr;
+  __nv_bfloat16* b = nullptr;
+  int r = 0;
+};
+
 struct CudaAttn {
   QWeight qkv;        // fused [q; k; v] (self-attention)
   QWeight q, kv;      // q and fused [k; v] (cross-attentions)
@@ -45,6 +54,7 @@ struct CudaAttn {
   // spans (== inner on one GPU).
   int heads = 0, head_dim = 0, inner = 0, qdim = 0, kvdim = 0, odim = 0;
   int head0 = 0, norm_width = 0;
+  LoraSite l_qkv, l_q, l_kv, l_o, l_gate;   // adapters of the sites above
 };
 
 struct CudaStreamW {
@@ -56,6 +66,7 @@ struct CudaStreamW {
   float* prompt_scale_shift = nullptr;  // 2 * dim
   float* cross_table = nullptr;         // 5 * dim
   int dim = 0, heads = 0, ff_hidden = 0;
+  LoraSite l_ff_in, l_ff_out;
 };
 
 // One stream's per-forward inputs (device pointers; see ltx_stream_io).
@@ -97,7 +108,8 @@ struct BlockArena {
   float* ssq = nullptr;            // per-token q/k sums of squares (tensor parallel)
   __nv_bfloat16* sp_send = nullptr;   // all-to-all staging (sequence parallel)
   __nv_bfloat16* sp_recv = nullptr;
-  size_t cap[18] = {};        // element capacity of each buffer above
+  __nv_bfloat16* lr = nullptr;        // an adapter site's x.A^T
+  size_t cap[19] = {};        // element capacity of each buffer above
   std::shared_ptr<BlockArena> side;    // the audio stream's own buffers (side stream)
   size_t video = 0, audio = 0, text = 0;   // reserved token maxima
   ~BlockArena();
@@ -124,6 +136,13 @@ public:
   // Assemble the block: every required tensor must be present (the
   // reference refuses a partial map, src/ltx25-block-ref.cc:424-432), fuse
   // the q/k/v and k/v packs, upload the rest.  Frees the staged parts.
+  // Attach one module's low-rank adapter (MetalBlock::lora_, src/
+  // ltx25-block-metal.cc:404-420) under the reference's module name
+  // ("attn1.to_q", "audio_ff.net.2", ...; src/ltx25-lora.cc:328-360).
+  // Before finalize, which checks the pair against the base linear's widths
+  // and copies it (sharded like the base weight); the pair may be freed
+  // after finalize.  An unknown module name is refused.
+  bool set_lora(const std::string& module, const LoraPair& pair, std::string* err);
   bool finalize(std::string* err);
 
   // Size the scratch arena once for the largest geometry.  `share`, when
@@ -204,11 +223,21 @@ private:
     int r0, rows, k0, kcols;
   };
   bool fuse_(const std::vector<Part>& parts, QWeight* out, std::string* err);
+  // One adapter site from its modules' pairs (null: not adapted): rows
+  // [r0, r0 + rows) of each pair's B in site order, A columns [k0, k0 + K).
+  struct LPart {
+    const LoraPair* p;
+    int r0, rows, k0;
+  };
+  bool build_lora_(const std::vector<LPart>& parts, int K, LoraSite* out, std::string* err);
+  const LoraPair* lora_of_(const std::string& module, int k, int n, std::string* err) const;
+  // The extension for a site, x.A^T into the current arena's scratch.
+  const LoraExt* lx_(const LoraSite& site, LoraExt* tmp) const;
   // x += gate * (att . Wo^T + bias), row-split and reduced under tensor
   // parallelism.
   bool out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k, const QWeight& w,
                  const __nv_bfloat16* bias, __nv_bfloat16* x, int n, int d,
-                 const float* gate, std::string* err);
+                 const float* gate, std::string* err, const LoraSite* lora = nullptr);
 
   CudaOps* _ops;
   int _vdim, _vheads, _adim, _aheads;
@@ -219,6 +248,9 @@ private:
   bool _sp = false;              // sequence parallel (weights whole)
   int _sp_rank = 0, _sp_world = 1;
   std::map<std::string, Staged> _staged;
+  std::map<std::string, LoraPair> _lora;   // attached pairs, until finalize
+  int _lora_rmax = 0;                      // widest site (arena sizing)
+  bool _audio_lora = false;                // an audio-stream site is adapted
   std::vector<void*> _owned;   // device buffers this block frees
   CudaStreamW _video, _audio;
   CudaAttn _a2v, _v2a;

@@ -42,7 +42,8 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
 {
   Plan p;
   const int kpb = mode == ltx::MODE_I8 ? 128 : 64;
-  p.kblocks = K / kpb;
+  // a K tail past the last full block reads as zeros (TMA fill)
+  p.kblocks = (K + kpb - 1) / kpb;
   p.tn = M <= 128 ? 128 : 256;
   // CTA pairs (M = 256 MMA over two SMs) halve the activation bytes each SM
   // streams per FLOP.  The dense path pairs by default once there are
@@ -103,6 +104,8 @@ CudaOps::~CudaOps()
   cudaFree(_sb.scales);
   cudaFree(_sb.mean);
   cudaFree(_err_word);
+  cudaFree(_ones);
+  cudaFree(_lora_r);
   cudaSetDevice(prev);
 }
 
@@ -210,9 +213,13 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
                     const void* wptr, const uint32_t* sz,
                     const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy,
                     int M, int K, int N, int epi, const float* gate,
-                    const float* sx, const float* sw, std::string* err)
+                    const float* sx, const float* sw, std::string* err,
+                    const LoraExt* ext)
 {
-  const Plan pl = plan_gemm(mode, M, N, K, _sms);
+  // An extension adds ceil(r / 64) K blocks after the main K.
+  const int ext_k = (ext != nullptr) ? ext->r : 0;
+  const int ext_kb = (ext_k + 63) / 64;
+  const Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms);
   ltx::GemmLaunch L;
   L.mode = mode;
   L.tn = pl.tn;
@@ -231,6 +238,13 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.n_tiles = pl.n_tiles;
   p.splits = pl.splits;
   p.kblocks = pl.kblocks;
+  p.kblocks_main = pl.kblocks - ext_kb;
+  if (ext_k > 0) {
+    L.ext_w = ext->b;
+    L.ext_x = ext->rbuf;
+    L.ext_k = ext_k;
+    L.ld_ext = ext_k;
+  }
   p.num_tiles = pl.m_tiles * pl.n_tiles * pl.splits;
   p.ldy = ldy;
   p.bias = bias;
@@ -254,7 +268,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
 bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
                      const QWeight& w, const __nv_bfloat16* bias,
                      __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
-                     const float* gate, std::string* err)
+                     const float* gate, std::string* err, const LoraExt* lora)
 {
   if (x == nullptr || y == nullptr) {
     if (err) *err = "linear: null x or y";
@@ -276,6 +290,33 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
   if (epi == ltx::EPI_GATED_RES && gate == nullptr) {
     if (err) *err = "linear: gated residual needs a gate";
     return false;
+  }
+  if (lora != nullptr && lora->r > 0) {
+    // r = x.A^T, then the linear with r.B^T contracted after its own K.
+    // The int8 tier's s32 accumulator cannot hold the bf16 delta and the
+    // fused w8g64 kernel's A operand is dequantized in TMEM, so an adapted
+    // linear takes the bf16 route: the dense weight, or the pack expanded
+    // once into the scratch.
+    if (lora->a == nullptr || lora->b == nullptr || lora->rbuf == nullptr ||
+        lora->r % 8 != 0 || !aligned(lora->a, 16) || !aligned(lora->b, 16) ||
+        !aligned(lora->rbuf, 16)) {
+      if (err) *err = "linear: adapter needs a, b, r scratch (16-byte aligned) and rank % 8 == 0";
+      return false;
+    }
+    if (!gemm_(s, ltx::MODE_BF16, x, ldx, lora->a, nullptr, nullptr, lora->rbuf, lora->r, M,
+               K, lora->r, ltx::EPI_STORE, nullptr, nullptr, nullptr, err))
+      return false;
+    const void* wb = w.w;
+    if (w.quantized) {
+      if (!ensure_(0, (size_t)N * K * 2, err)) return false;
+      if (ltx::launch_dequant_w8(w.codes, w.sz, N, K, _deq, s) != 0) {
+        if (err) *err = "dequant launch failed";
+        return false;
+      }
+      wb = _deq;
+    }
+    return gemm_(s, ltx::MODE_BF16, x, ldx, wb, nullptr, bias, y, ldy, M, K, N, epi, gate,
+                 nullptr, nullptr, err, lora);
   }
   if (!w.quantized) {
     return gemm_(s, ltx::MODE_BF16, x, ldx, w.w, nullptr, bias, y, ldy, M, K,
@@ -302,6 +343,58 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
   }
   return gemm_(s, ltx::MODE_W8G64, x, ldx, w.codes, w.sz, bias, y, ldy, M, K,
                N, epi, gate, nullptr, nullptr, err);
+}
+
+__nv_bfloat16* CudaOps::lora_rbuf(size_t elems, std::string* err)
+{
+  if (elems <= _lora_r_elems) return _lora_r;
+  cudaFree(_lora_r);
+  _lora_r = nullptr;
+  _lora_r_elems = 0;
+  if (!cuda_ok(cudaMalloc(&_lora_r, elems * 2), "cudaMalloc(lora scratch)", err))
+    return nullptr;
+  _lora_r_elems = elems;
+  return _lora_r;
+}
+
+const float* CudaOps::ones_(int n, cudaStream_t s, std::string* err)
+{
+  if (n <= _ones_n) return _ones;
+  cudaFree(_ones);
+  _ones = nullptr;
+  _ones_n = 0;
+  if (!cuda_ok(cudaMalloc(&_ones, (size_t)n * sizeof(float)), "cudaMalloc(ones)", err))
+    return nullptr;
+  if (ltx::launch_fill_f32(_ones, 1.0f, n, s) != 0) {
+    if (err) *err = "fill launch failed";
+    return nullptr;
+  }
+  _ones_n = n;
+  return _ones;
+}
+
+bool CudaOps::lora_add(cudaStream_t s, const __nv_bfloat16* x, int ldx, const LoraExt& lora,
+                       __nv_bfloat16* y, int ldy, int M, int K, int N, std::string* err)
+{
+  if (M <= 0 || K <= 0 || N <= 0 || lora.r <= 0) return true;   // nothing to add
+  if (x == nullptr || y == nullptr || lora.a == nullptr || lora.b == nullptr ||
+      lora.rbuf == nullptr) {
+    if (err) *err = "lora_add: null operand";
+    return false;
+  }
+  if (K % 8 != 0 || lora.r % 8 != 0 || !aligned(x, 16) || ldx % 8 != 0 || ldx < K ||
+      !aligned(y, 4) || ldy % 2 != 0 || ldy < N || !aligned(lora.rbuf, 16)) {
+    if (err) *err = "lora_add: K % 8, rank % 8, x 16-byte aligned (ldx % 8), y 4-byte aligned";
+    return false;
+  }
+  const float* one = ones_(N, s, err);
+  if (one == nullptr) return false;
+  // r = x.A^T; y = y + 1 * (r.B^T): the gated-residual epilogue reads y
+  // and writes it once, so the delta never exists as its own [M][N].
+  return gemm_(s, ltx::MODE_BF16, x, ldx, lora.a, nullptr, nullptr, lora.rbuf, lora.r, M, K,
+               lora.r, ltx::EPI_STORE, nullptr, nullptr, nullptr, err) &&
+         gemm_(s, ltx::MODE_BF16, lora.rbuf, lora.r, lora.b, nullptr, nullptr, y, ldy, M,
+               lora.r, N, ltx::EPI_GATED_RES, one, nullptr, nullptr, err);
 }
 
 bool CudaOps::linear_i8_scratch(cudaStream_t s, const __nv_bfloat16* x,
@@ -564,6 +657,56 @@ bool upload_dweight(const CudaOps& ops, const uint16_t* wsrc, int N, int K,
   }
   *out = w;
   return true;
+}
+
+bool upload_lora(const CudaOps& ops, const uint16_t* a, const uint16_t* b, int rank, int k,
+                 int n, float scale, bool on_device, LoraPair* out, std::string* err)
+{
+  if (a == nullptr || b == nullptr || out == nullptr) {
+    if (err) *err = "lora upload: null tensor";
+    return false;
+  }
+  if (rank <= 0 || k <= 0 || n <= 0 || k % 8 != 0 || n % 2 != 0) {
+    if (err)
+      *err = "lora upload shape: rank " + std::to_string(rank) + ", k " + std::to_string(k) +
+             " (multiple of 8), n " + std::to_string(n) + " (even)";
+    return false;
+  }
+  LoraPair p;
+  p.rank = rank;
+  p.r8 = (rank + 7) / 8 * 8;
+  p.k = k;
+  p.n = n;
+  p.device = ops.device();
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  const size_t na = (size_t)p.r8 * k, nb = (size_t)n * p.r8;
+  bool ok = cuda_ok(cudaMalloc(&p.a, na * 2), "cudaMalloc(lora a)", err) &&
+            cuda_ok(cudaMalloc(&p.b, nb * 2), "cudaMalloc(lora b)", err) &&
+            cuda_ok(cudaMemset(p.a, 0, na * 2), "lora a", err) &&
+            cuda_ok(cudaMemset(p.b, 0, nb * 2), "lora b", err) &&
+            cuda_ok(cudaMemcpy(p.a, a, (size_t)rank * k * 2, kind), "upload lora a", err) &&
+            cuda_ok(cudaMemcpy2D(p.b, (size_t)p.r8 * 2, b, (size_t)rank * 2, (size_t)rank * 2, n,
+                                 kind),
+                    "upload lora b", err);
+  if (ok && scale != 1.0f) {
+    ok = ltx::launch_scale_bf16(p.a, p.a, scale, (size_t)rank * k, nullptr) == 0 &&
+         cuda_ok(cudaDeviceSynchronize(), "lora scale", err);
+    if (!ok && err && err->empty()) *err = "lora scale launch failed";
+  }
+  if (!ok) {
+    free_lora(&p);
+    return false;
+  }
+  *out = p;
+  return true;
+}
+
+void free_lora(LoraPair* p)
+{
+  if (p == nullptr) return;
+  cudaFree(p->a);
+  cudaFree(p->b);
+  *p = LoraPair{};
 }
 
 void free_qweight(QWeight* w)

@@ -35,6 +35,29 @@ struct QWeight {
   int device = 0;
 };
 
+// A low-rank adapter riding on one linear (the reference's LoraPair and
+// lora_add, src/ltx25-lora.h:48-56, src/ltx25-metal-ops.cc:986-1000):
+// y = epilogue(x.W^T + bias + (x.A^T).B^T).  The delta is contracted in the
+// linear's own accumulator (extra K blocks of the tcgen05 GEMM), so it
+// lands before the epilogue's GELU / gated residual exactly where the
+// reference adds it (between the linear and its consumer).
+struct LoraExt {
+  const __nv_bfloat16* a = nullptr;   // [r][K], the scale folded in
+  const __nv_bfloat16* b = nullptr;   // [N][r]
+  int r = 0;                          // rank padded to a multiple of 8
+  __nv_bfloat16* rbuf = nullptr;      // [M][r] scratch: x.A^T
+};
+
+// One module's uploaded adapter pair (src/ltx25-lora.h:48-56): a [r8][k]
+// with the scale folded in, b [n][r8], the rank padded to r8 (a multiple of
+// 8, so every row is 16-byte aligned for TMA) with zero rows / columns.
+struct LoraPair {
+  __nv_bfloat16* a = nullptr;
+  __nv_bfloat16* b = nullptr;
+  int rank = 0, r8 = 0, k = 0, n = 0;
+  int device = 0;
+};
+
 enum class Route { Fused = 0, DequantOnce = 1, Auto = 2 };
 
 class CudaOps {
@@ -48,10 +71,20 @@ public:
   bool reserve(int max_tokens, int max_n, int max_k, std::string* err);
 
   // y[M][N] = x[M][K] . W^T (+ bias), epilogue per ltx::EpiMode.
+  // `lora` (optional): a low-rank adapter on this linear, contracted in
+  // the same accumulator (see LoraExt).  A linear carrying one runs the
+  // bf16 route whatever its M and tier.
   bool linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
               const QWeight& w, const __nv_bfloat16* bias, __nv_bfloat16* y,
               int ldy, int M, int K, int N, int epi,
-              const float* gate, std::string* err);
+              const float* gate, std::string* err, const LoraExt* lora = nullptr);
+
+  // MetalOps::lora_add (src/ltx25-metal-ops.cc:986-1000) on its own:
+  // y[M][N] += (x[M][K].A^T).B^T for a y that already holds the linear.
+  // The add is the second GEMM's epilogue (gated residual at gate 1), so
+  // no [M][N] delta is written; `lora.rbuf` holds x.A^T.
+  bool lora_add(cudaStream_t s, const __nv_bfloat16* x, int ldx, const LoraExt& lora,
+                __nv_bfloat16* y, int ldy, int M, int K, int N, std::string* err);
 
   void set_route(Route r) { _route = r; }
   Route route() const { return _route; }
@@ -150,8 +183,18 @@ private:
              const void* wptr, const uint32_t* sz, const __nv_bfloat16* bias,
              __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
              const float* gate, const float* sx, const float* sw,
-             std::string* err);
+             std::string* err, const LoraExt* ext = nullptr);
+  // f32 ones [n] (the gate of lora_add's accumulate), grown on demand
+  const float* ones_(int n, cudaStream_t s, std::string* err);
+public:
+  // The context's x.A^T scratch for the standalone adapter calls, >= elems.
+  __nv_bfloat16* lora_rbuf(size_t elems, std::string* err);
+private:
 
+  float* _ones = nullptr;
+  int _ones_n = 0;
+  __nv_bfloat16* _lora_r = nullptr;
+  size_t _lora_r_elems = 0;
   int _dev = -1;
   int _sms = 148;
   Route _route = Route::Auto;
@@ -191,5 +234,10 @@ bool upload_qweight(const CudaOps& ops, const uint32_t* codes,
 bool upload_dweight(const CudaOps& ops, const uint16_t* w, int N, int K,
                     bool on_device, QWeight* out, std::string* err);
 void free_qweight(QWeight* w);
+// LoraAdapter::load's per-module bind (src/ltx25-lora.cc:56-124): a [rank][k]
+// and b [n][rank] bf16; a' = bf16(f32(a) * scale), one rounding.
+bool upload_lora(const CudaOps& ops, const uint16_t* a, const uint16_t* b, int rank, int k,
+                 int n, float scale, bool on_device, LoraPair* out, std::string* err);
+void free_lora(LoraPair* p);
 
 }  // namespace ltx25

@@ -48,6 +48,12 @@ SIGNATURES = {
     "ltx_qlinear_ex": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P,
                             _P]),
     "ltx_qlinear_i8_static": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "ltx_lora_upload": (_I, [_P, _P, _P, _I, _I, _I, ctypes.c_float, _I, ctypes.POINTER(_P)]),
+    "ltx_lora_free": (None, [_P]),
+    "ltx_lora_info": (_I, [_P] + [ctypes.POINTER(_I)] * 3),
+    "ltx_lora_add": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
+    "ltx_qlinear_lora": (_I, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "ltx_block_set_lora": (_I, [_P, ctypes.c_char_p, _P]),
     "ltx_launch_count": (ctypes.c_ulonglong, []),
     "ltx_tp_unique_id": (_I, [_P, _I]),
     "ltx_ctx_set_tp": (_I, [_P, _I, _I, _P]),
@@ -288,6 +294,65 @@ def qlinear(ctx, w, x, bias=None, out=None, epilogue=EPI_STORE, gate=None,
     return out
 
 
+class Lora:
+    """ltx_lora: one module's low-rank adapter pair (a [rank][k], b [n][rank],
+    bf16), `scale` folded into a at upload."""
+
+    def __init__(self, ctx, a, b, scale=1.0):
+        """a, b: torch bf16 tensors on the device (or numpy uint16 bf16 bits on
+        the host)."""
+        import numpy as np
+        self.ctx = ctx
+        rank, k = a.shape
+        n = b.shape[0]
+        if b.shape[1] != rank:
+            raise ValueError("lora: a is [rank][k], b must be [n][rank]")
+        h = ctypes.c_void_p()
+        if isinstance(a, np.ndarray):
+            a = np.ascontiguousarray(a, dtype=np.uint16)
+            b = np.ascontiguousarray(b, dtype=np.uint16)
+            pa, pb, dev = a.ctypes.data_as(_P), b.ctypes.data_as(_P), 0
+        else:
+            a, b = a.contiguous(), b.contiguous()
+            pa, pb, dev = _ptr(a), _ptr(b), 1
+        ctx._ok(ctx.lib.ltx_lora_upload(ctx.h, pa, pb, rank, k, n, float(scale), dev,
+                                        ctypes.byref(h)), "lora_upload")
+        self.h, self.rank, self.k, self.n = h, rank, k, n
+
+    def free(self):
+        if self.h is not None and self.h.value:
+            self.ctx.lib.ltx_lora_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def lora_add(ctx, lora, x, y, stream=None):
+    """ltx_lora_add: y += (x @ A.T) @ B.T in place (MetalOps::lora_add)."""
+    M = x.shape[0]
+    ctx._ok(ctx.lib.ltx_lora_add(ctx.h, lora.h, _ptr(x), x.stride(0), _ptr(y), y.stride(0),
+                                 M, lora.k, lora.n, _stream(stream)), "lora_add")
+    return y
+
+
+def qlinear_lora(ctx, w, lora, x, bias=None, out=None, epilogue=EPI_STORE, gate=None,
+                 stream=None):
+    """ltx_qlinear_lora: y = epilogue(x @ W.T + bias + (x @ A.T) @ B.T)."""
+    import torch
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, w.N), dtype=torch.bfloat16, device=x.device)
+    ctx._ok(ctx.lib.ltx_qlinear_lora(ctx.h, w.h, lora.h if lora is not None else None, _ptr(x),
+                                     x.stride(0), _ptr(bias), _ptr(out), out.stride(0), M, w.K,
+                                     w.N, epilogue, _ptr(gate), _stream(stream)),
+            "qlinear_lora")
+    return out
+
+
 def qlinear_i8_static(ctx, w, x, bias=None, out=None, stream=None):
     """ltx_qlinear_i8_static: the int8 tier on the library's fixed scratch
     array (no device allocation in the call).  x: contiguous [M][K] bf16."""
@@ -437,6 +502,13 @@ class Block:
                 deq[name] = np.asarray(arr, dtype=np.float32)
         torch.cuda.synchronize()
         return deq
+
+    def set_lora(self, module, lora):
+        """ltx_block_set_lora: attach `lora` (a Lora) to the module named as
+        the reference names it ("attn1.to_q", "ff.net.2", ...)."""
+        self._keep.append(lora)
+        self._ok(self.ctx.lib.ltx_block_set_lora(self.h, module.encode(), lora.h),
+                 f"set_lora({module})")
 
     def finalize(self):
         # Staged device tensors are read here; they may be dropped after.
