@@ -479,6 +479,102 @@ def run_attn(args):
     return 0
 
 
+def run_lora(args):
+    """Low-rank adapters on a qlinear at the reference's own adapter
+    benchmark shapes (tests/ltx25-lora-apply-test.cc:498-510): the x2
+    upscaler's rank-32 projection and feed-forward widening over 32640
+    tokens, and the distilled adapter's rank 450 over 8160.  Arms: the
+    plain qlinear, the adapted qlinear with the delta in the same GEMM
+    (ltx_qlinear_lora), and the plain qlinear followed by the standalone
+    lora_add (the reference's form).  The adapter's arithmetic is 2*rank/K
+    of the linear, the floor for its cost."""
+    import torch
+    import ltx25_b200 as L
+    world, rank_, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    shapes = [("x2 upscaler attn proj, rank 32", 32640, 4096, 4096, 32),
+              ("x2 upscaler ff widening, rank 32", 32640, 4096, 16384, 32),
+              ("distilled adapter, rank 450", 8160, 4096, 4096, 450)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    rows = []
+    n0 = L.launch_count()
+    total = {"plain": 0.0, "fused": 0.0, "separate": 0.0}
+    with ClockSampler(gpu_id) as clk:
+        for name, M, K, N, r in shapes:
+            w = torch.randn((N, K), generator=gen, device=dev) * 0.02
+            c, s_, b_ = L.pack_w8g64(ctx, w)
+            del w
+            q = L.QWeight.upload(ctx, c, s_, b_, N, K, on_device=True)
+            a = (torch.randn((r, K), generator=gen, device=dev) * (3.0 / (r * K) ** 0.5)).to(
+                torch.bfloat16)
+            b = torch.randn((N, r), generator=gen, device=dev).to(torch.bfloat16)
+            lo = L.Lora(ctx, a, b)
+            x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            arms = {"plain": lambda: L.qlinear(ctx, q, x, out=y),
+                    "fused": lambda: L.qlinear_lora(ctx, q, lo, x, out=y),
+                    "separate": lambda: (L.qlinear(ctx, q, x, out=y), L.lora_add(ctx, lo, x, y))}
+            # arms interleaved step by step, rotating the order, so clock and
+            # power drift fall on all three alike
+            names = list(arms)
+            for _ in range(args.warmup):
+                for arm in names:
+                    arms[arm]()
+            torch.cuda.synchronize()
+            evs = {arm: [(torch.cuda.Event(enable_timing=True),
+                          torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+                   for arm in names}
+            for i in range(args.steps):
+                for j in range(len(names)):
+                    arm = names[(i + j) % len(names)]
+                    e0, e1 = evs[arm][i]
+                    e0.record()
+                    arms[arm]()
+                    e1.record()
+            torch.cuda.synchronize()
+            res = {arm: statistics.median([e0.elapsed_time(e1) for e0, e1 in evs[arm]])
+                   for arm in names}
+            for arm in names:
+                total[arm] += res[arm]
+            ctx.check()
+            rows.append({"shape": name, "M": M, "K": K, "N": N, "rank": r,
+                         "plain_us": round(res["plain"] * 1e3, 1),
+                         "fused_us": round(res["fused"] * 1e3, 1),
+                         "separate_us": round(res["separate"] * 1e3, 1),
+                         "fused_overhead": round(res["fused"] / res["plain"] - 1, 4),
+                         "separate_overhead": round(res["separate"] / res["plain"] - 1, 4),
+                         "arithmetic_overhead": round(2.0 * r / K, 4)})
+            lo.free()
+            q.free()
+            del x, y, a, b
+    launches = L.launch_count() - n0
+    fl = sum(2.0 * M * K * N + 2.0 * M * r * (K + N) for _, M, K, N, r in shapes)
+    tf = fl / (total["fused"] * 1e-3) / 1e12
+    clocks = clk.summary()
+    tpeak, tpeak_kind = tensor_peak_for(clocks)
+    line = {
+        "metric": "adapted w8g64 qlinear TFLOP/s (linear + rank-r adapter), reference LoRA shapes",
+        "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total["fused"], 4), "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic N(0,1) x, N(0,0.02) w8g64 weights, adapter pairs "
+                                 "scaled like the reference test's",
+        "config": {"workload": "qlinear + LoRA at tests/ltx25-lora-apply-test.cc:498-510 shapes"},
+        "per_shape": rows, "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tpeak,
+                     "peak_source": tpeak_kind, "unit": "TFLOP/s", "frac": round(tf / tpeak, 3),
+                     "traffic": None},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
 def run_block(args):
     """one joint AV block, 8160 video + 126 audio + 256
     text tokens at the real widths, synthetic w8g64 weights."""
@@ -587,7 +683,8 @@ def main():
     ap.add_argument("--sage", action="store_true", help="sage_attn tier (--workload attn)")
     ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
                     help="qlinear route for quantized weights (sweep)")
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "block", "stack", "attn"],
+    ap.add_argument("--workload", default="sweep",
+                    choices=["sweep", "block", "stack", "attn", "lora"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
@@ -596,6 +693,9 @@ def main():
     if args.workload == "attn" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_attn(args)
+    if args.workload == "lora" and args.impl == "ours":
+        args.warmup = max(args.warmup, 3)
+        return run_lora(args)
     if args.workload == "stack" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_stack(args)
