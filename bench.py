@@ -575,6 +575,81 @@ def run_lora(args):
     return 0
 
 
+def run_trunk(args):
+    """The trunk around the block loop at BASELINE config 4's geometry: video
+    patchify (8160 tokens, 128 latent channels -> 4096, channel-major input,
+    the keyframe embedding on the first frame's 510 tokens) and output head
+    (LayerNorm, modulation, 4096 -> 128, channel-major out), and the audio
+    pair (126 tokens, 128 <-> 2048).  HBM-bound: the algorithmic bytes are
+    the activations in and out plus the packed weights."""
+    import torch
+    import ltx25_b200 as L
+    world, rank_, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(17)
+    z, oc = 128, 128
+    legs = []
+    nbytes = 0.0
+    for T, dim, first in ((8160, 4096, 17 * 30), (126, 2048, 0)):
+        wi = torch.randn((dim, z), generator=gen, device=dev) * 0.05
+        wo = torch.randn((oc, dim), generator=gen, device=dev) * 0.02
+        qi = L.QWeight.upload(ctx, *L.pack_w8g64(ctx, wi), dim, z, on_device=True)
+        qo = L.QWeight.upload(ctx, *L.pack_w8g64(ctx, wo), oc, dim, on_device=True)
+        lat = torch.randn((z, T), generator=gen, device=dev).to(torch.bfloat16)
+        pre = torch.randn((dim,), generator=gen, device=dev).to(torch.bfloat16)
+        bi = torch.zeros((dim,), device=dev, dtype=torch.bfloat16)
+        bo = torch.zeros((oc,), device=dev, dtype=torch.bfloat16)
+        ss = (torch.randn((2, dim), generator=gen, device=dev) * 0.2).float().contiguous()
+        x = torch.empty((T, dim), device=dev, dtype=torch.bfloat16)
+        out = torch.empty((oc, T), device=dev, dtype=torch.bfloat16)
+        legs.append(lambda qi=qi, qo=qo, lat=lat, pre=pre, bi=bi, bo=bo, ss=ss, x=x, out=out,
+                    first=first: (L.patchify(ctx, qi, lat, bias=bi, channel_major=True,
+                                             prefix=pre, prefix_rows=first, out=x),
+                                  L.output_head(ctx, qo, x, ss, bias=bo, channel_major=True,
+                                                out=out)))
+        nbytes += 2.0 * T * z + 2.0 * T * dim + dim * z * (1 + 4 / 64)      # patchify
+        nbytes += 2.0 * T * dim + 2.0 * T * oc + oc * dim * (1 + 4 / 64)     # head
+    step = lambda: [f() for f in legs]
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    ctx.check()
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    n0 = L.launch_count()
+    with ClockSampler(gpu_id) as clk:
+        for e0, e1 in evs:
+            e0.record()
+            step()
+            e1.record()
+        torch.cuda.synchronize()
+    launches = (L.launch_count() - n0) // max(args.steps, 1)
+    ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in evs])
+    _, hbm_peak, peak_kind = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "DiT trunk (patchify + output head, video and audio) GB/s of activations",
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic N(0,1) latents, w8g64 weights",
+        "config": {"workload": "patchify 8160x128->4096 (+keyframe rows) and head "
+                               "8160x4096->128, audio 126x128<->2048; channel-major ends"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(gbs / hbm_peak, 3),
+                     "traffic": None},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
 def run_block(args):
     """one joint AV block, 8160 video + 126 audio + 256
     text tokens at the real widths, synthetic w8g64 weights."""
@@ -684,7 +759,7 @@ def main():
     ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
                     help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="sweep",
-                    choices=["sweep", "block", "stack", "attn", "lora"],
+                    choices=["sweep", "block", "stack", "attn", "lora", "trunk"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
@@ -693,6 +768,8 @@ def main():
     if args.workload == "attn" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_attn(args)
+    if args.workload == "trunk" and args.impl == "ours":
+        return run_trunk(args)
     if args.workload == "lora" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_lora(args)

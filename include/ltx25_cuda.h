@@ -206,6 +206,28 @@ LTX_API int ltx_qlinear_lora(ltx_ctx* ctx, const ltx_qweight* w, const ltx_lora*
                              int M, int K, int N, int epilogue, const void* gate,
                              void* stream);
 
+/* ---- the trunk around the block loop ------------------------------------
+ * Ltx25Dit's patchify (src/ltx25-dit.cc:1509-1540): x[T][dim] = latent .
+ * W^T + bias (+ the adapter's delta, l may be NULL), then `prefix` [dim]
+ * added to rows [0, prefix_rows) -- the keyframe position embedding on the
+ * first latent frame's tokens (NULL / 0: none).  latent is bf16 token-major
+ * [T][z], or channel-major [z][T] (the VAE's layout) when channel_major;
+ * the pack to token-major (w fastest) runs on the device. */
+LTX_API int ltx_patchify(ltx_ctx* ctx, const ltx_qweight* w, const void* bias, const ltx_lora* l,
+                         const void* latent, int channel_major, const void* prefix,
+                         int prefix_rows, void* x, int T, int z, int dim, void* stream);
+
+/* Ltx25Dit's output head (src/ltx25-dit.cc:2000-2045): LayerNorm over dim
+ * (no affine -- NOT an RMSNorm -- eps 1e-6), then x * (1 + scale) + shift,
+ * then proj_out (+ bias, + adapter) -> out bf16 [T][out_ch], or the
+ * channel-major [out_ch][T] the sampler and VAE take when channel_major.
+ * shift_scale: f32 [2][dim], the shift row first: the head's 2-row table
+ * with the embedded timestep added to both rows (the caller's adaLN). */
+LTX_API int ltx_output_head(ltx_ctx* ctx, const void* x, const float* shift_scale,
+                            const ltx_qweight* w, const void* bias, const ltx_lora* l,
+                            void* out, int channel_major, int T, int dim, int out_ch,
+                            void* stream);
+
 /* Route for quantized weights (LTX_ROUTE_*).  Default AUTO, the reference's
  * own choice (MetalOps::linear -> dequant_mma_, src/ltx25-metal-ops.cc:
  * 343-347, 468-545): a call tall enough to be tensor-bound expands the

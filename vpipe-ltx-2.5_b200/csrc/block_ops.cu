@@ -381,6 +381,110 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ a,
     out[i] = __float2bfloat16_rn(a[i]);
 }
 
+// The DiT output head's normalization (src/ltx25-dit.cc:2010-2031):
+// out = LayerNorm(x) * (1 + scale) + shift, LayerNorm without affine
+// (population variance, eps), f32 statistics in two block reductions.  One
+// CTA per row; a thread holds CH chunks of 8 elements (dim <= 256 * 8 * CH).
+template <int CH>
+__global__ void __launch_bounds__(kRowThreads)
+    layer_norm_mod_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                          __nv_bfloat16* __restrict__ out, int ldo, int dim,
+                          const float* __restrict__ shift, const float* __restrict__ scale,
+                          float eps)
+{
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  float v[CH][8];
+  float sum = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int k = (c * kRowThreads + threadIdx.x) * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[c][i] = 0.0f;
+    if (k < dim) {
+      load8(x + (size_t)row * ldx + k, v[c]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum += v[c][i];
+    }
+  }
+  auto block_sum = [&](float t) {
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float u = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+      for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+      if (threadIdx.x == 0) red[32] = u;
+    }
+    __syncthreads();
+    const float r = red[32];
+    __syncthreads();
+    return r;
+  };
+  const float mean = block_sum(sum) / (float)dim;
+  float sq = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int k = (c * kRowThreads + threadIdx.x) * 8;
+    if (k < dim) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[c][i] - mean;
+        sq = fmaf(d, d, sq);
+      }
+    }
+  }
+  const float inv = rsqrtf(block_sum(sq) / (float)dim + eps);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int k = (c * kRowThreads + threadIdx.x) * 8;
+    if (k >= dim) continue;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      o[i] = fmaf((v[c][i] - mean) * inv, 1.0f + scale[k + i], shift[k + i]);
+    store8(out + (size_t)row * ldo + k, o);
+  }
+}
+
+// x[r][c] += vec[c] for r < rows (the keyframe position embedding added to
+// the first frame's tokens, src/ltx25-kernels.metal:349-358)
+__global__ void add_row_prefix_kernel(__nv_bfloat16* __restrict__ x, int ldx,
+                                      const __nv_bfloat16* __restrict__ vec, int rows, int cols)
+{
+  pdl_wait();
+  pdl_trigger();
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, c = i - r * cols;
+    __nv_bfloat16* p = x + r * ldx + c;
+    *p = __float2bfloat16_rn(__bfloat162float(*p) + __bfloat162float(vec[c]));
+  }
+}
+
+// dst[c][r] = src[r][c] through a 32 x 33 shared tile (coalesced both sides)
+__global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, int lds,
+                                      __nv_bfloat16* __restrict__ dst, int ldd, int rows,
+                                      int cols)
+{
+  pdl_wait();
+  pdl_trigger();
+  __shared__ __nv_bfloat16 t[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) t[i][threadIdx.x] = src[(size_t)r * lds + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[(size_t)c * ldd + r] = t[threadIdx.x][i];
+  }
+}
+
 __global__ void fill_f32_kernel(float* __restrict__ out, float v, size_t n)
 {
   pdl_wait();
@@ -403,6 +507,43 @@ __global__ void scale_bf16_kernel(const __nv_bfloat16* __restrict__ in,
 }
 
 }  // namespace
+
+int launch_layer_norm_mod(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out, int ldo,
+                          int rows, int dim, const float* shift, const float* scale, float eps,
+                          cudaStream_t s)
+{
+  if (rows <= 0) return 0;
+  if (dim % 8 != 0 || dim > kRowThreads * 8 * 4 || shift == nullptr || scale == nullptr ||
+      ldx % 8 != 0 || ldo % 8 != 0)
+    return -2;
+  if (dim <= kRowThreads * 8 * 2)
+    launch_k(layer_norm_mod_kernel<2>, dim3(rows), dim3(kRowThreads), 0, s, 1, x, ldx, out, ldo,
+             dim, shift, scale, eps);
+  else
+    launch_k(layer_norm_mod_kernel<4>, dim3(rows), dim3(kRowThreads), 0, s, 1, x, ldx, out, ldo,
+             dim, shift, scale, eps);
+  return launched();
+}
+
+int launch_add_row_prefix(__nv_bfloat16* x, int ldx, const __nv_bfloat16* vec, int rows,
+                          int cols, cudaStream_t s)
+{
+  if (rows <= 0 || cols <= 0) return 0;
+  size_t grid = ((size_t)rows * cols + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  launch_k(add_row_prefix_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, x, ldx, vec, rows,
+           cols);
+  return launched();
+}
+
+int launch_transpose_bf16(const __nv_bfloat16* src, int lds, __nv_bfloat16* dst, int ldd,
+                          int rows, int cols, cudaStream_t s)
+{
+  if (rows <= 0 || cols <= 0) return 0;
+  launch_k(transpose_bf16_kernel, dim3((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)),
+           dim3(32, 8), 0, s, 1, src, lds, dst, ldd, rows, cols);
+  return launched();
+}
 
 int launch_fill_f32(float* out, float v, size_t n, cudaStream_t s)
 {

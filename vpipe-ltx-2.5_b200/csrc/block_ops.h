@@ -20,6 +20,17 @@ int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
                        cudaStream_t s);
 // out[i] = v
 int launch_fill_f32(float* out, float v, size_t n, cudaStream_t s);
+// out = LayerNorm(x) (no affine, population variance) * (1 + scale) + shift;
+// dim % 8 == 0, dim <= 8192, shift / scale f32 [dim]
+int launch_layer_norm_mod(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out, int ldo,
+                          int rows, int dim, const float* shift, const float* scale, float eps,
+                          cudaStream_t s);
+// x[r][c] += vec[c], r < rows
+int launch_add_row_prefix(__nv_bfloat16* x, int ldx, const __nv_bfloat16* vec, int rows,
+                          int cols, cudaStream_t s);
+// dst[c][r] = src[r][c]
+int launch_transpose_bf16(const __nv_bfloat16* src, int lds, __nv_bfloat16* dst, int ldd,
+                          int rows, int cols, cudaStream_t s);
 // out[i] = bf16(f32(in[i]) * scale), round to nearest even; in == out is fine
 int launch_scale_bf16(const __nv_bfloat16* in, __nv_bfloat16* out, float scale, size_t n,
                       cudaStream_t s);

@@ -270,6 +270,43 @@ int ltx_qlinear_lora(ltx_ctx* ctx, const ltx_qweight* w, const ltx_lora* l, cons
   return LTX_OK;
 }
 
+int ltx_patchify(ltx_ctx* ctx, const ltx_qweight* w, const void* bias, const ltx_lora* l,
+                 const void* latent, int channel_major, const void* prefix, int prefix_rows,
+                 void* x, int T, int z, int dim, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (w == nullptr) return fail(ctx, LTX_E_NULL, "patchify: null weight");
+  if (w->w.K != z || w->w.N != dim)
+    return fail(ctx, LTX_E_SHAPE, "patchify shape: the weight is [" + std::to_string(w->w.N) +
+                                      "][" + std::to_string(w->w.K) + "]");
+  std::string e;
+  if (!ctx->ops.patchify(S(stream), w->w, static_cast<const __nv_bfloat16*>(bias),
+                         l != nullptr ? &l->p : nullptr,
+                         static_cast<const __nv_bfloat16*>(latent), channel_major != 0,
+                         static_cast<const __nv_bfloat16*>(prefix), prefix_rows,
+                         static_cast<__nv_bfloat16*>(x), T, z, dim, &e))
+    return fail(ctx, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_output_head(ltx_ctx* ctx, const void* x, const float* shift_scale, const ltx_qweight* w,
+                    const void* bias, const ltx_lora* l, void* out, int channel_major, int T,
+                    int dim, int out_ch, void* stream)
+{
+  if (ctx == nullptr) return LTX_E_NULL;
+  if (w == nullptr) return fail(ctx, LTX_E_NULL, "output head: null weight");
+  if (w->w.K != dim || w->w.N != out_ch)
+    return fail(ctx, LTX_E_SHAPE, "output head shape: proj_out is [" + std::to_string(w->w.N) +
+                                      "][" + std::to_string(w->w.K) + "]");
+  std::string e;
+  if (!ctx->ops.output_head(S(stream), static_cast<const __nv_bfloat16*>(x), shift_scale, w->w,
+                            static_cast<const __nv_bfloat16*>(bias),
+                            l != nullptr ? &l->p : nullptr, static_cast<__nv_bfloat16*>(out),
+                            channel_major != 0, T, dim, out_ch, &e))
+    return fail(ctx, code_for(e), e);
+  return LTX_OK;
+}
+
 int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                 const void* bias, void* y, int M, int K, int N, void* stream)
 {

@@ -106,6 +106,8 @@ CudaOps::~CudaOps()
   cudaFree(_err_word);
   cudaFree(_ones);
   cudaFree(_lora_r);
+  cudaFree(_tr[0]);
+  cudaFree(_tr[1]);
   cudaSetDevice(prev);
 }
 
@@ -355,6 +357,110 @@ __nv_bfloat16* CudaOps::lora_rbuf(size_t elems, std::string* err)
     return nullptr;
   _lora_r_elems = elems;
   return _lora_r;
+}
+
+__nv_bfloat16* CudaOps::trunk_buf_(int i, size_t elems, std::string* err)
+{
+  if (elems <= _tr_elems[i]) return _tr[i];
+  cudaFree(_tr[i]);
+  _tr[i] = nullptr;
+  _tr_elems[i] = 0;
+  if (!cuda_ok(cudaMalloc(&_tr[i], elems * 2 + 256), "cudaMalloc(trunk scratch)", err))
+    return nullptr;
+  _tr_elems[i] = elems;
+  return _tr[i];
+}
+
+bool CudaOps::patchify(cudaStream_t s, const QWeight& w, const __nv_bfloat16* bias,
+                       const LoraPair* lora, const __nv_bfloat16* latent, bool channel_major,
+                       const __nv_bfloat16* prefix, int prefix_rows, __nv_bfloat16* x, int T,
+                       int z, int dim, std::string* err)
+{
+  if (latent == nullptr || x == nullptr) {
+    if (err) *err = "patchify: null latent or x";
+    return false;
+  }
+  if (T <= 0 || prefix_rows < 0 || prefix_rows > T || (prefix_rows > 0 && prefix == nullptr)) {
+    if (err) *err = "patchify shape: T, prefix_rows (need a prefix vector for prefix rows)";
+    return false;
+  }
+  const __nv_bfloat16* in = latent;
+  if (channel_major) {
+    __nv_bfloat16* packed = trunk_buf_(0, (size_t)T * z, err);
+    if (packed == nullptr) return false;
+    if (ltx::launch_transpose_bf16(latent, T, packed, z, z, T, s) != 0) {
+      if (err) *err = "patchify pack launch failed";
+      return false;
+    }
+    in = packed;
+  }
+  LoraExt ext;
+  if (lora != nullptr) {
+    if (lora->k != z || lora->n != dim) {
+      if (err) *err = "patchify adapter shape: pair widths disagree with the projection";
+      return false;
+    }
+    ext.a = lora->a;
+    ext.b = lora->b;
+    ext.r = lora->r8;
+    ext.rbuf = lora_rbuf((size_t)T * lora->r8, err);
+    if (ext.rbuf == nullptr) return false;
+  }
+  if (!linear(s, in, z, w, bias, x, dim, T, z, dim, ltx::EPI_STORE, nullptr, err,
+              lora != nullptr ? &ext : nullptr))
+    return false;
+  if (prefix_rows > 0 && ltx::launch_add_row_prefix(x, dim, prefix, prefix_rows, dim, s) != 0) {
+    if (err) *err = "keyframe embedding launch failed";
+    return false;
+  }
+  return true;
+}
+
+bool CudaOps::output_head(cudaStream_t s, const __nv_bfloat16* x, const float* shift_scale,
+                          const QWeight& w, const __nv_bfloat16* bias, const LoraPair* lora,
+                          __nv_bfloat16* out, bool channel_major, int T, int dim, int out_ch,
+                          std::string* err)
+{
+  if (x == nullptr || shift_scale == nullptr || out == nullptr) {
+    if (err) *err = "output head: null x, shift/scale table or out";
+    return false;
+  }
+  if (T <= 0 || dim % 8 != 0 || !aligned(shift_scale, 16)) {
+    if (err) *err = "output head shape: dim % 8, table 16-byte aligned";
+    return false;
+  }
+  __nv_bfloat16* tmp = trunk_buf_(0, (size_t)T * dim, err);
+  if (tmp == nullptr) return false;
+  if (ltx::launch_layer_norm_mod(x, dim, tmp, dim, T, dim, shift_scale, shift_scale + dim,
+                                 1e-6f, s) != 0) {
+    if (err) *err = "output head norm launch failed";
+    return false;
+  }
+  __nv_bfloat16* y = out;
+  if (channel_major) {
+    y = trunk_buf_(1, (size_t)T * out_ch, err);
+    if (y == nullptr) return false;
+  }
+  LoraExt ext;
+  if (lora != nullptr) {
+    if (lora->k != dim || lora->n != out_ch) {
+      if (err) *err = "output head adapter shape: pair widths disagree with proj_out";
+      return false;
+    }
+    ext.a = lora->a;
+    ext.b = lora->b;
+    ext.r = lora->r8;
+    ext.rbuf = lora_rbuf((size_t)T * lora->r8, err);
+    if (ext.rbuf == nullptr) return false;
+  }
+  if (!linear(s, tmp, dim, w, bias, y, out_ch, T, dim, out_ch, ltx::EPI_STORE, nullptr, err,
+              lora != nullptr ? &ext : nullptr))
+    return false;
+  if (channel_major && ltx::launch_transpose_bf16(y, out_ch, out, T, T, out_ch, s) != 0) {
+    if (err) *err = "output head unpack launch failed";
+    return false;
+  }
+  return true;
 }
 
 const float* CudaOps::ones_(int n, cudaStream_t s, std::string* err)

@@ -79,6 +79,24 @@ public:
               int ldy, int M, int K, int N, int epi,
               const float* gate, std::string* err, const LoraExt* lora = nullptr);
 
+  // Ltx25Dit's patchify (src/ltx25-dit.cc:1509-1540): x[T][dim] =
+  // latent . W^T + bias (+ adapter), then `prefix` [dim] added to rows
+  // [0, prefix_rows) (the keyframe position embedding).  `latent` is
+  // token-major [T][z], or channel-major [z][T] when channel_major (packed
+  // on the device first, the DiT's inline pack).
+  bool patchify(cudaStream_t s, const QWeight& w, const __nv_bfloat16* bias,
+                const LoraPair* lora, const __nv_bfloat16* latent, bool channel_major,
+                const __nv_bfloat16* prefix, int prefix_rows, __nv_bfloat16* x, int T, int z,
+                int dim, std::string* err);
+  // Ltx25Dit's output head (src/ltx25-dit.cc:2000-2045): LayerNorm (no
+  // affine, eps 1e-6), x * (1 + scale) + shift with shift_scale f32 [2][dim]
+  // (shift row first), then proj_out (+ bias, + adapter) -> out [T][out_ch],
+  // or [out_ch][T] when channel_major.
+  bool output_head(cudaStream_t s, const __nv_bfloat16* x, const float* shift_scale,
+                   const QWeight& w, const __nv_bfloat16* bias, const LoraPair* lora,
+                   __nv_bfloat16* out, bool channel_major, int T, int dim, int out_ch,
+                   std::string* err);
+
   // MetalOps::lora_add (src/ltx25-metal-ops.cc:986-1000) on its own:
   // y[M][N] += (x[M][K].A^T).B^T for a y that already holds the linear.
   // The add is the second GEMM's epilogue (gated residual at gate 1), so
@@ -195,6 +213,10 @@ private:
   int _ones_n = 0;
   __nv_bfloat16* _lora_r = nullptr;
   size_t _lora_r_elems = 0;
+  // the trunk's scratch: packed latents / normalized rows, token-major out
+  __nv_bfloat16* _tr[2] = {nullptr, nullptr};
+  size_t _tr_elems[2] = {0, 0};
+  __nv_bfloat16* trunk_buf_(int i, size_t elems, std::string* err);
   int _dev = -1;
   int _sms = 148;
   Route _route = Route::Auto;

@@ -54,6 +54,8 @@ SIGNATURES = {
     "ltx_lora_add": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "ltx_qlinear_lora": (_I, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "ltx_block_set_lora": (_I, [_P, ctypes.c_char_p, _P]),
+    "ltx_patchify": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _P]),
+    "ltx_output_head": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ltx_launch_count": (ctypes.c_ulonglong, []),
     "ltx_tp_unique_id": (_I, [_P, _I]),
     "ltx_ctx_set_tp": (_I, [_P, _I, _I, _P]),
@@ -350,6 +352,36 @@ def qlinear_lora(ctx, w, lora, x, bias=None, out=None, epilogue=EPI_STORE, gate=
                                      x.stride(0), _ptr(bias), _ptr(out), out.stride(0), M, w.K,
                                      w.N, epilogue, _ptr(gate), _stream(stream)),
             "qlinear_lora")
+    return out
+
+
+def patchify(ctx, w, latent, bias=None, lora=None, channel_major=False, prefix=None,
+             prefix_rows=0, out=None, stream=None):
+    """ltx_patchify: latent [T][z] (or [z][T] with channel_major) -> x [T][dim]."""
+    import torch
+    T = latent.shape[1] if channel_major else latent.shape[0]
+    z, dim = w.K, w.N
+    if out is None:
+        out = torch.empty((T, dim), dtype=torch.bfloat16, device=latent.device)
+    ctx._ok(ctx.lib.ltx_patchify(ctx.h, w.h, _ptr(bias), lora.h if lora is not None else None,
+                                 _ptr(latent), int(channel_major), _ptr(prefix), prefix_rows,
+                                 _ptr(out), T, z, dim, _stream(stream)), "patchify")
+    return out
+
+
+def output_head(ctx, w, x, shift_scale, bias=None, lora=None, channel_major=False, out=None,
+                stream=None):
+    """ltx_output_head: LayerNorm, modulate by shift_scale f32 [2][dim], proj_out."""
+    import torch
+    T, dim = x.shape
+    oc = w.N
+    if out is None:
+        shape = (oc, T) if channel_major else (T, oc)
+        out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+    ctx._ok(ctx.lib.ltx_output_head(ctx.h, _ptr(x), _ptr(shift_scale), w.h, _ptr(bias),
+                                    lora.h if lora is not None else None, _ptr(out),
+                                    int(channel_major), T, dim, oc, _stream(stream)),
+            "output_head")
     return out
 
 
