@@ -470,6 +470,56 @@ LTX_API int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
                               ltx_progress_fn progress, void* user,
                               void* stream);
 
+/* ---- checkpoints ---------------------------------------------------------
+ * The on-disk pack reader (the WeightSet the reference binds through,
+ * src/ltx25-dit-weights.cc:230-403, src/ltx25-lora.cc:180-300): a
+ * safetensors file mapped read-only, its header parsed once -- u64 header
+ * length, JSON {name: {dtype, shape, data_offsets}, "__metadata__": {..}},
+ * data.  A header that is not the format's (unknown dtype, offsets outside
+ * the data or disagreeing with shape x dtype, truncated file, trailing
+ * bytes) is refused whole: LTX_E_SHAPE with the reason in `err`. */
+typedef struct ltx_st ltx_st;
+enum {
+  LTX_ST_F32 = 0, LTX_ST_F16 = 1, LTX_ST_BF16 = 2, LTX_ST_U32 = 3, LTX_ST_I32 = 4,
+  LTX_ST_U8 = 5, LTX_ST_I8 = 6, LTX_ST_F64 = 7, LTX_ST_I64 = 8, LTX_ST_U16 = 9,
+  LTX_ST_I16 = 10, LTX_ST_BOOL = 11
+};
+LTX_API int ltx_st_open(const char* path, ltx_st** out, char* err, int err_len);
+LTX_API void ltx_st_close(ltx_st* f);
+LTX_API int ltx_st_count(const ltx_st* f);
+LTX_API const char* ltx_st_name(const ltx_st* f, int i);
+/* index of `name`, or -1 */
+LTX_API int ltx_st_find(const ltx_st* f, const char* name);
+/* shape: room for 8 dimensions; data points into the mapping. */
+LTX_API int ltx_st_info(const ltx_st* f, int i, int* dtype, int* ndim, int64_t* shape,
+                        const void** data, uint64_t* bytes);
+/* a __metadata__ string value, or NULL */
+LTX_API const char* ltx_st_metadata(const ltx_st* f, const char* key);
+/* n elements of a float tensor (F32 / F16 / BF16) from element `off`, as
+ * f32 (F16 and BF16 widened exactly); LTX_E_SHAPE for another dtype or a
+ * range past the tensor. */
+LTX_API int ltx_st_read_f32(const ltx_st* f, int i, uint64_t off, uint64_t n, float* out);
+
+/* Stage every tensor of one block from a checkpoint: the names under
+ * `prefix` (e.g. "model.diffusion_model.transformer_blocks.7.") with the
+ * prefix stripped.  A quantized linear is the "X.weight" u32 codes +
+ * "X.scales" + "X.biases" triplet (need_q_, src/ltx25-dit-weights.cc:
+ * 352-403): staged as ltx_block_set_qlinear (F16 / BF16 / F32 scales);
+ * every other float tensor as ltx_block_set_tensor.  A pack that closes at
+ * another group or bit width returns LTX_E_UNSUPPORTED (this build runs
+ * w8g64).  Then ltx_block_finalize as usual. */
+LTX_API int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix);
+
+/* One module's adapter pair from an adapter file: "<module>.lora_A.weight"
+ * [rank][k] and "<module>.lora_B.weight" [n][rank] (any float dtype), the
+ * rank derived from each against the base widths and cross-checked
+ * (bind_pair_, src/ltx25-lora.cc:69-124); the factor is lora_scale times
+ * alpha / rank when the file's __metadata__ names lora_alpha and lora_rank
+ * (src/ltx25-lora.cc:265-287).  LTX_E_STATE when the module is not
+ * adapted. */
+LTX_API int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, int n,
+                             float lora_scale, ltx_lora** out);
+
 #ifdef __cplusplus
 }
 #endif

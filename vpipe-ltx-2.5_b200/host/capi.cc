@@ -1,6 +1,8 @@
 // capi.cc -- the extern "C" boundary declared in include/ltx25_cuda.h, over
 // the C++ host mirror (CudaOps and friends).
+#include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <memory>
 #include <new>
 #include <string>
@@ -11,6 +13,7 @@
 #include "../csrc/block_ops.h"
 #include "ltx25-block-cuda.h"
 #include "ltx25-cuda-ops.h"
+#include "ltx25-safetensors.h"
 
 struct ltx_ctx {
   ltx25::CudaOps ops;
@@ -23,6 +26,10 @@ struct ltx_qweight {
 
 struct ltx_lora {
   ltx25::LoraPair p;
+};
+
+struct ltx_st {
+  ltx25::SafeTensors f;
 };
 
 namespace {
@@ -795,6 +802,191 @@ int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
     if (!s->blocks[0]->blk->gather_video(S(stream), whole, &e)) return sfail(s, LTX_E_CUDA, e);
   }
   return LTX_OK;
+}
+
+
+// ---- checkpoints ----------------------------------------------------------
+
+int ltx_st_open(const char* path, ltx_st** out, char* err, int err_len)
+{
+  if (out == nullptr || path == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  ltx_st* f = new (std::nothrow) ltx_st();
+  if (f == nullptr) return LTX_E_OOM;
+  std::string e;
+  if (!f->f.open(path, &e)) {
+    delete f;
+    if (err != nullptr && err_len > 0) {
+      std::strncpy(err, e.c_str(), (size_t)err_len - 1);
+      err[err_len - 1] = '\0';
+    }
+    return e.find("cannot") != std::string::npos ? LTX_E_NULL : LTX_E_SHAPE;
+  }
+  *out = f;
+  return LTX_OK;
+}
+
+void ltx_st_close(ltx_st* f) { delete f; }
+
+int ltx_st_count(const ltx_st* f) { return f == nullptr ? 0 : f->f.count(); }
+
+const char* ltx_st_name(const ltx_st* f, int i)
+{
+  if (f == nullptr || i < 0 || i >= f->f.count()) return nullptr;
+  return f->f.at(i).name.c_str();
+}
+
+int ltx_st_find(const ltx_st* f, const char* name)
+{
+  if (f == nullptr || name == nullptr) return -1;
+  return f->f.find(name);
+}
+
+int ltx_st_info(const ltx_st* f, int i, int* dtype, int* ndim, int64_t* shape,
+                const void** data, uint64_t* bytes)
+{
+  if (f == nullptr) return LTX_E_NULL;
+  if (i < 0 || i >= f->f.count()) return LTX_E_SHAPE;
+  const ltx25::StTensor& t = f->f.at(i);
+  if (dtype) *dtype = t.dtype;
+  if (ndim) *ndim = (int)t.shape.size();
+  if (shape)
+    for (size_t d = 0; d < t.shape.size() && d < 8; ++d) shape[d] = t.shape[d];
+  if (data) *data = t.data;
+  if (bytes) *bytes = t.bytes;
+  return LTX_OK;
+}
+
+int ltx_st_read_f32(const ltx_st* f, int i, uint64_t off, uint64_t n, float* out)
+{
+  if (f == nullptr || out == nullptr) return LTX_E_NULL;
+  if (i < 0 || i >= f->f.count()) return LTX_E_SHAPE;
+  if (!ltx25::SafeTensors::to_f32(f->f.at(i), (size_t)off, (size_t)n, out)) return LTX_E_SHAPE;
+  return LTX_OK;
+}
+
+const char* ltx_st_metadata(const ltx_st* f, const char* key)
+{
+  if (f == nullptr || key == nullptr) return nullptr;
+  const std::string* v = f->f.metadata(key);
+  return v == nullptr ? nullptr : v->c_str();
+}
+
+int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  if (f == nullptr || prefix == nullptr)
+    return bfail(b, LTX_E_NULL, "load: null checkpoint or prefix");
+  const std::string pre(prefix);
+  const ltx25::SafeTensors& st = f->f;
+  int bound = 0;
+  std::string e;
+  // Quantized linears first: a "X.scales" with its "X.weight" codes and
+  // "X.biases" (need_q_, src/ltx25-dit-weights.cc:352-403).  The build
+  // runs the w8g64 pack: 8-bit codes (K = 4 x the u32 columns) in groups
+  // of 64; any other pack that closes is refused, not mis-read.
+  std::vector<bool> used((size_t)st.count(), false);
+  for (int i = 0; i < st.count(); ++i) {
+    const ltx25::StTensor& sc = st.at(i);
+    const std::string& n = sc.name;
+    if (n.compare(0, pre.size(), pre) != 0 || n.size() < 7 ||
+        n.compare(n.size() - 7, 7, ".scales") != 0)
+      continue;
+    const std::string base = n.substr(0, n.size() - 7);
+    const int wi = st.find(base + ".weight"), bi = st.find(base + ".biases");
+    if (wi < 0 || bi < 0)
+      return bfail(b, LTX_E_STATE, "load: '" + base + "' has scales but no weight or biases");
+    const ltx25::StTensor& cw = st.at(wi);
+    const ltx25::StTensor& bz = st.at(bi);
+    if (cw.dtype != ltx25::ST_U32 || cw.shape.size() != 2 || sc.shape.size() != 2 ||
+        bz.shape != sc.shape || bz.dtype != sc.dtype || cw.shape[0] != sc.shape[0])
+      return bfail(b, LTX_E_SHAPE, "load: '" + base + "' is not a u32 codes / scales / biases "
+                                   "triplet of matching rows");
+    const int64_t N = cw.shape[0], K = cw.shape[1] * 4, G = sc.shape[1];
+    if (G <= 0 || K % G != 0 || K / G != 64)
+      return bfail(b, LTX_E_UNSUPPORTED,
+                   "load: '" + base + "' closes at K " + std::to_string(K) + " with " +
+                       std::to_string(G) + " groups; this build runs the w8g64 pack only "
+                       "(not run by this build)");
+    int sbd = -1;
+    if (sc.dtype == ltx25::ST_F16) sbd = LTX_SB_F16;
+    else if (sc.dtype == ltx25::ST_BF16) sbd = LTX_SB_BF16;
+    else if (sc.dtype == ltx25::ST_F32) sbd = LTX_SB_F32;
+    if (sbd < 0) return bfail(b, LTX_E_UNSUPPORTED, "load: '" + base + "' scales dtype");
+    if (!b->blk->set_qlinear(base.substr(pre.size()) + ".weight",
+                             reinterpret_cast<const uint32_t*>(cw.data), sc.data, bz.data, sbd,
+                             (int)N, (int)K, false, &e))
+      return bfail(b, code_for(e), e);
+    used[(size_t)i] = used[(size_t)wi] = used[(size_t)bi] = true;
+    ++bound;
+  }
+  // Everything else under the prefix: float tensors, staged as f32.
+  std::vector<float> buf;
+  for (int i = 0; i < st.count(); ++i) {
+    const ltx25::StTensor& t = st.at(i);
+    if (used[(size_t)i] || t.name.compare(0, pre.size(), pre) != 0) continue;
+    if (t.dtype != ltx25::ST_F32 && t.dtype != ltx25::ST_F16 && t.dtype != ltx25::ST_BF16)
+      return bfail(b, LTX_E_UNSUPPORTED, "load: '" + t.name + "' is not a float tensor");
+    size_t n = 1;
+    for (int64_t d : t.shape) n *= (size_t)d;
+    if (n == 0) continue;
+    buf.resize(n);
+    if (!ltx25::SafeTensors::to_f32(t, 0, n, buf.data()))
+      return bfail(b, LTX_E_SHAPE, "load: '" + t.name + "' could not be read");
+    const int rows = t.shape.empty() ? 1 : (int)t.shape[0];
+    const int cols = t.shape.size() <= 1 ? 0 : (int)(n / (size_t)rows);
+    if (!b->blk->set_tensor(t.name.substr(pre.size()), buf.data(), rows, cols, false, &e))
+      return bfail(b, code_for(e), e);
+    ++bound;
+  }
+  if (bound == 0) return bfail(b, LTX_E_STATE, "load: no tensor under '" + pre + "'");
+  return LTX_OK;
+}
+
+int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, int n,
+                     float lora_scale, ltx_lora** out)
+{
+  if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  if (f == nullptr || module == nullptr)
+    return fail(ctx, LTX_E_NULL, "lora load: null checkpoint or module");
+  const ltx25::SafeTensors& st = f->f;
+  const std::string m(module);
+  const int ai = st.find(m + ".lora_A.weight"), bi = st.find(m + ".lora_B.weight");
+  if (ai < 0 && bi < 0) return fail(ctx, LTX_E_STATE, "lora load: '" + m + "' is not adapted");
+  if (ai < 0 || bi < 0)
+    return fail(ctx, LTX_E_SHAPE, "lora load: '" + m + "' has only one of lora_A / lora_B");
+  const ltx25::StTensor& a = st.at(ai);
+  const ltx25::StTensor& b = st.at(bi);
+  // rank from each tensor's size against the base widths, cross-checked
+  // (bind_pair_, src/ltx25-lora.cc:96-117)
+  const size_t ea = a.bytes / std::max<size_t>(1, ltx25::SafeTensors::elem_size(a.dtype));
+  const size_t eb = b.bytes / std::max<size_t>(1, ltx25::SafeTensors::elem_size(b.dtype));
+  if (k <= 0 || n <= 0 || ea % (size_t)k != 0 || eb % (size_t)n != 0)
+    return fail(ctx, LTX_E_SHAPE, "lora load: '" + m + "' does not divide by its base widths");
+  const size_t ra = ea / (size_t)k, rb = eb / (size_t)n;
+  if (ra == 0 || ra != rb)
+    return fail(ctx, LTX_E_SHAPE, "lora load: '" + m + "' rank disagrees between lora_A (" +
+                                      std::to_string(ra) + ") and lora_B (" + std::to_string(rb) +
+                                      ")");
+  // lora_scale times alpha / rank when the file's metadata names both
+  // (LoraAdapter::load, src/ltx25-lora.cc:265-287)
+  double factor = lora_scale;
+  auto num = [&](const char* key, double* v) {
+    const std::string* s = st.metadata(key);
+    if (s == nullptr || s->empty()) return false;
+    char* end = nullptr;
+    *v = std::strtod(s->c_str(), &end);
+    return end != s->c_str();
+  };
+  double alpha = 0.0, rank = 0.0;
+  if (num("lora_alpha", &alpha) && num("lora_rank", &rank) && rank > 0.0 && alpha > 0.0)
+    factor *= alpha / rank;
+  std::vector<uint16_t> ab(ea), bb(eb);
+  if (!ltx25::SafeTensors::to_bf16(a, 0, ea, ab.data()) ||
+      !ltx25::SafeTensors::to_bf16(b, 0, eb, bb.data()))
+    return fail(ctx, LTX_E_UNSUPPORTED, "lora load: '" + m + "' is not a float pair");
+  return ltx_lora_upload(ctx, ab.data(), bb.data(), (int)ra, k, n, (float)factor, 0, out);
 }
 
 }  // extern "C"

@@ -55,6 +55,19 @@ SIGNATURES = {
     "ltx_qlinear_lora": (_I, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "ltx_block_set_lora": (_I, [_P, ctypes.c_char_p, _P]),
     "ltx_patchify": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _P]),
+    "ltx_st_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P), _P, _I]),
+    "ltx_st_close": (None, [_P]),
+    "ltx_st_count": (_I, [_P]),
+    "ltx_st_name": (ctypes.c_char_p, [_P, _I]),
+    "ltx_st_find": (_I, [_P, ctypes.c_char_p]),
+    "ltx_st_info": (_I, [_P, _I, ctypes.POINTER(_I), ctypes.POINTER(_I),
+                         ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_P),
+                         ctypes.POINTER(ctypes.c_uint64)]),
+    "ltx_st_read_f32": (_I, [_P, _I, ctypes.c_uint64, ctypes.c_uint64, _P]),
+    "ltx_st_metadata": (ctypes.c_char_p, [_P, ctypes.c_char_p]),
+    "ltx_block_load_st": (_I, [_P, _P, ctypes.c_char_p]),
+    "ltx_lora_load_st": (_I, [_P, _P, ctypes.c_char_p, _I, _I, ctypes.c_float,
+                              ctypes.POINTER(_P)]),
     "ltx_output_head": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ltx_launch_count": (ctypes.c_ulonglong, []),
     "ltx_tp_unique_id": (_I, [_P, _I]),
@@ -333,6 +346,88 @@ class Lora:
             pass
 
 
+ST_DTYPES = {0: "F32", 1: "F16", 2: "BF16", 3: "U32", 4: "I32", 5: "U8", 6: "I8", 7: "F64",
+             8: "I64", 9: "U16", 10: "I16", 11: "BOOL"}
+
+
+class SafeTensors:
+    """ltx_st: a safetensors checkpoint mapped by the library (no GPU)."""
+
+    def __init__(self, path):
+        self.lib = load()
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(512)
+        rc = self.lib.ltx_st_open(str(path).encode(), ctypes.byref(h), buf, 512)
+        if rc != LTX_OK:
+            raise LtxError(rc, f"st_open: {buf.value.decode()}")
+        self.h = h
+
+    def __len__(self):
+        return self.lib.ltx_st_count(self.h)
+
+    def names(self):
+        return [self.lib.ltx_st_name(self.h, i).decode() for i in range(len(self))]
+
+    def find(self, name):
+        return self.lib.ltx_st_find(self.h, name.encode())
+
+    def info(self, i):
+        dt, nd = ctypes.c_int(), ctypes.c_int()
+        shape = (ctypes.c_int64 * 8)()
+        data, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+        rc = self.lib.ltx_st_info(self.h, i, ctypes.byref(dt), ctypes.byref(nd), shape,
+                                  ctypes.byref(data), ctypes.byref(nbytes))
+        if rc != LTX_OK:
+            raise LtxError(rc, "st_info")
+        return ST_DTYPES[dt.value], [shape[d] for d in range(nd.value)], data.value, nbytes.value
+
+    def raw(self, name):
+        """The tensor's bytes (a copy) as a numpy uint8 array."""
+        import numpy as np
+        _, _, ptr, nbytes = self.info(self.find(name))
+        return np.ctypeslib.as_array((ctypes.c_uint8 * nbytes).from_address(ptr)).copy() \
+            if nbytes else np.zeros(0, np.uint8)
+
+    def read_f32(self, name):
+        import numpy as np
+        i = self.find(name)
+        _, shape, _, _ = self.info(i)
+        n = int(np.prod(shape)) if shape else 1
+        out = np.empty(n, np.float32)
+        rc = self.lib.ltx_st_read_f32(self.h, i, 0, n, out.ctypes.data_as(_P))
+        if rc != LTX_OK:
+            raise LtxError(rc, f"st_read_f32({name})")
+        return out.reshape(shape)
+
+    def metadata(self, key):
+        v = self.lib.ltx_st_metadata(self.h, key.encode())
+        return None if v is None else v.decode()
+
+    def close(self):
+        if self.h is not None and self.h.value:
+            self.lib.ltx_st_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def lora_from_st(ctx, st, module, k, n, lora_scale=1.0):
+    """ltx_lora_load_st: one module's pair from an adapter file."""
+    h = ctypes.c_void_p()
+    ctx._ok(ctx.lib.ltx_lora_load_st(ctx.h, st.h, module.encode(), k, n, float(lora_scale),
+                                     ctypes.byref(h)), f"lora_load_st({module})")
+    lo = Lora.__new__(Lora)
+    lo.ctx, lo.h = ctx, h
+    r = ctypes.c_int()
+    ctx.lib.ltx_lora_info(h, ctypes.byref(r), None, None)
+    lo.rank, lo.k, lo.n = r.value, k, n
+    return lo
+
+
 def lora_add(ctx, lora, x, y, stream=None):
     """ltx_lora_add: y += (x @ A.T) @ B.T in place (MetalOps::lora_add)."""
     M = x.shape[0]
@@ -534,6 +629,10 @@ class Block:
                 deq[name] = np.asarray(arr, dtype=np.float32)
         torch.cuda.synchronize()
         return deq
+
+    def load_st(self, st, prefix):
+        """ltx_block_load_st: stage every tensor under `prefix` of a checkpoint."""
+        self._ok(self.ctx.lib.ltx_block_load_st(self.h, st.h, prefix.encode()), "load_st")
 
     def set_lora(self, module, lora):
         """ltx_block_set_lora: attach `lora` (a Lora) to the module named as
