@@ -520,6 +520,35 @@ LTX_API int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
 LTX_API int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, int n,
                              float lora_scale, ltx_lora** out);
 
+/* ---- the trunk's adaLN chains (host) --------------------------------------
+ * Ltx25Dit::adaln_ (src/ltx25-dit.cc:51-160): the 256-channel timestep
+ * sinusoid (max period 10000, no downscale shift, flip_sin_to_cos: the row
+ * is [cos | sin]) through emb.timestep_embedder.linear_1 -> SiLU ->
+ * linear_2 -> SiLU -> the root `linear`, as host GEMVs over bf16 weights
+ * with f64 sums stored f32, split over host threads by output row.  The
+ * reference runs them on the host once per denoise level and step; the
+ * caller passes the timestep it feeds (sigma times the timestep scale
+ * multiplier).  out: [out_dim] (the k*dim modulation driver); embedded:
+ * [dim] = the linear_2 output, before the SiLU -- the `embedded_timestep`
+ * the output head adds to its table -- or NULL.  threads <= 0: the host's
+ * count. */
+typedef struct ltx_adaln ltx_adaln;
+/* bf16 [dim][256], [dim], [dim][dim], [dim], [out_dim][dim], [out_dim];
+ * biases may be NULL.  Copied. */
+LTX_API int ltx_adaln_create(const uint16_t* w1, const uint16_t* b1, const uint16_t* w2,
+                             const uint16_t* b2, const uint16_t* w3, const uint16_t* b3,
+                             int dim, int out_dim, ltx_adaln** out);
+/* From a checkpoint: prefix + "emb.timestep_embedder.linear_1", "..._2",
+ * "linear" (.weight / .bias), e.g. prefix "model.diffusion_model.
+ * adaln_single."; any float dtype, rounded to bf16 as the reference's
+ * loader does. */
+LTX_API int ltx_adaln_load_st(const ltx_st* f, const char* prefix, ltx_adaln** out, char* err,
+                              int err_len);
+LTX_API void ltx_adaln_free(ltx_adaln* a);
+LTX_API int ltx_adaln_dims(const ltx_adaln* a, int* dim, int* out_dim);
+LTX_API int ltx_adaln_run(const ltx_adaln* a, double timestep, float* out, float* embedded,
+                          int threads);
+
 #ifdef __cplusplus
 }
 #endif

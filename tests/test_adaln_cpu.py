@@ -1,0 +1,75 @@
+"""The trunk's adaLN chains on the host (SURVEY row (f)4's host adaLN):
+the library's chain against the numpy restatement of Ltx25Dit::adaln_,
+the [cos | sin] order and embedded_timestep's tap as controls, thread-count
+independence, and the chain bound from a checkpoint."""
+import numpy as np
+import pytest
+
+from oracle import adaln_np, lib
+
+import st_file
+
+DIM, OUT = 64, 9 * 64
+
+
+def _weights(seed):
+    rng = np.random.default_rng(seed)
+    f = lambda *s, sc=1.0: lib.f32_to_bf16((rng.standard_normal(s) * sc).astype(np.float32))
+    return (f(DIM, 256, sc=0.1), f(DIM, sc=0.1), f(DIM, DIM, sc=0.15), f(DIM, sc=0.1),
+            f(OUT, DIM, sc=0.15), f(OUT, sc=0.1))
+
+
+@pytest.mark.parametrize("t", [0.0, 1.0, 37.5, 500.0, 999.0])
+def test_chain_matches_restatement(t):
+    import ltx25_b200 as L
+    w = _weights(1)
+    a = L.AdaLN(*w)
+    out, emb = a(t)
+    want, want_emb = adaln_np.chain(t, *w)
+    assert lib.rel_l2(out, want) < 1e-6
+    assert lib.rel_l2(emb, want_emb) < 1e-6
+    a.close()
+
+
+def test_controls_and_threads():
+    import ltx25_b200 as L
+    w = _weights(2)
+    a = L.AdaLN(*w)
+    out, emb = a(250.0, threads=1)
+    out8, emb8 = a(250.0, threads=8)
+    assert np.array_equal(out, out8) and np.array_equal(emb, emb8)
+    # [sin | cos] instead: a clean forward driven by the wrong half
+    s = adaln_np.sinusoid(250.0)
+    flipped = np.concatenate([s[128:], s[:128]])
+    h1 = adaln_np.silu(adaln_np.gemv(flipped, w[0], w[1]))
+    wrong = adaln_np.gemv(adaln_np.silu(adaln_np.gemv(h1, w[2], w[3])), w[4], w[5])
+    assert lib.rel_l2(out, wrong) > 0.05
+    # embedded_timestep is the SECOND linear's output, not the third's
+    assert emb.shape == (DIM,)
+    assert lib.rel_l2(emb, adaln_np.chain(250.0, *w)[1]) < 1e-6
+    a.close()
+
+
+def test_chain_from_checkpoint(tmp_path):
+    import ltx25_b200 as L
+    w = _weights(3)
+    pre = "model.diffusion_model.adaln_single."
+    names = ["emb.timestep_embedder.linear_1.weight", "emb.timestep_embedder.linear_1.bias",
+             "emb.timestep_embedder.linear_2.weight", "emb.timestep_embedder.linear_2.bias",
+             "linear.weight", "linear.bias"]
+    tensors = {pre + n: a for n, a in zip(names, w)}
+    # one tensor stored F32: the reader rounds it to bf16 as the loader does
+    tensors[pre + "linear.weight"] = lib.bf16_to_f32(w[4])
+    bf = tuple(pre + n for n in names if n != "linear.weight")
+    p = st_file.write(tmp_path / "trunk.safetensors", tensors, bf16=bf)
+    st = L.SafeTensors(p)
+    a = L.AdaLN(st=st, prefix=pre)
+    assert (a.dim, a.out_dim) == (DIM, OUT)
+    out, emb = a(640.0)
+    want, want_emb = adaln_np.chain(640.0, *w)
+    assert lib.rel_l2(out, want) < 1e-6 and lib.rel_l2(emb, want_emb) < 1e-6
+    with pytest.raises(L.LtxError) as e:
+        L.AdaLN(st=st, prefix="model.diffusion_model.audio_adaln_single.")
+    assert e.value.code == -7
+    a.close()
+    st.close()

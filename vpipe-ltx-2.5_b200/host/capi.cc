@@ -13,6 +13,7 @@
 #include "../csrc/block_ops.h"
 #include "ltx25-block-cuda.h"
 #include "ltx25-cuda-ops.h"
+#include "ltx25-adaln.h"
 #include "ltx25-safetensors.h"
 
 struct ltx_ctx {
@@ -30,6 +31,10 @@ struct ltx_lora {
 
 struct ltx_st {
   ltx25::SafeTensors f;
+};
+
+struct ltx_adaln {
+  ltx25::AdaLNChain c;
 };
 
 namespace {
@@ -987,6 +992,102 @@ int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, i
       !ltx25::SafeTensors::to_bf16(b, 0, eb, bb.data()))
     return fail(ctx, LTX_E_UNSUPPORTED, "lora load: '" + m + "' is not a float pair");
   return ltx_lora_upload(ctx, ab.data(), bb.data(), (int)ra, k, n, (float)factor, 0, out);
+}
+
+
+// ---- the trunk's adaLN chains (host) ---------------------------------------
+
+int ltx_adaln_create(const uint16_t* w1, const uint16_t* b1, const uint16_t* w2,
+                     const uint16_t* b2, const uint16_t* w3, const uint16_t* b3, int dim,
+                     int out_dim, ltx_adaln** out)
+{
+  if (out == nullptr || w1 == nullptr || w2 == nullptr || w3 == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  if (dim <= 0 || out_dim <= 0) return LTX_E_SHAPE;
+  ltx_adaln* a = new (std::nothrow) ltx_adaln();
+  if (a == nullptr) return LTX_E_OOM;
+  ltx25::AdaLNChain& c = a->c;
+  c.dim = dim;
+  c.out_dim = out_dim;
+  const size_t d = (size_t)dim, od = (size_t)out_dim;
+  c.w1.assign(w1, w1 + d * 256);
+  c.w2.assign(w2, w2 + d * d);
+  c.w3.assign(w3, w3 + od * d);
+  if (b1 != nullptr) c.b1.assign(b1, b1 + d);
+  if (b2 != nullptr) c.b2.assign(b2, b2 + d);
+  if (b3 != nullptr) c.b3.assign(b3, b3 + od);
+  *out = a;
+  return LTX_OK;
+}
+
+int ltx_adaln_load_st(const ltx_st* f, const char* prefix, ltx_adaln** out, char* err,
+                      int err_len)
+{
+  if (out == nullptr || f == nullptr || prefix == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  const std::string pre(prefix);
+  const ltx25::SafeTensors& st = f->f;
+  auto say = [&](const std::string& m, int code) {
+    if (err != nullptr && err_len > 0) {
+      std::strncpy(err, m.c_str(), (size_t)err_len - 1);
+      err[err_len - 1] = '\0';
+    }
+    return code;
+  };
+  // bind_adaln_'s names (src/ltx25-lora.cc:145-158): the timestep
+  // embedder's two linears, then the root projection
+  const std::string n1 = pre + "emb.timestep_embedder.linear_1", n2 =
+                         pre + "emb.timestep_embedder.linear_2", n3 = pre + "linear";
+  const int i1 = st.find(n1 + ".weight"), i2 = st.find(n2 + ".weight"),
+            i3 = st.find(n3 + ".weight");
+  if (i1 < 0 || i2 < 0 || i3 < 0)
+    return say("adaln: missing '" + (i1 < 0 ? n1 : i2 < 0 ? n2 : n3) + ".weight'", LTX_E_STATE);
+  const ltx25::StTensor &t1 = st.at(i1), &t2 = st.at(i2), &t3 = st.at(i3);
+  if (t1.shape.size() != 2 || t1.shape[1] != 256 || t2.shape.size() != 2 ||
+      t2.shape[0] != t1.shape[0] || t2.shape[1] != t1.shape[0] || t3.shape.size() != 2 ||
+      t3.shape[1] != t1.shape[0])
+    return say("adaln: shapes are not [dim][256], [dim][dim], [out][dim]", LTX_E_SHAPE);
+  ltx_adaln* a = new (std::nothrow) ltx_adaln();
+  if (a == nullptr) return LTX_E_OOM;
+  ltx25::AdaLNChain& c = a->c;
+  c.dim = (int)t1.shape[0];
+  c.out_dim = (int)t3.shape[0];
+  auto rd = [&](const ltx25::StTensor& t, std::vector<uint16_t>* v) {
+    size_t n = 1;
+    for (int64_t d : t.shape) n *= (size_t)d;
+    v->resize(n);
+    return ltx25::SafeTensors::to_bf16(t, 0, n, v->data());
+  };
+  auto bias = [&](const std::string& n, size_t want, std::vector<uint16_t>* v) {
+    const int i = st.find(n + ".bias");
+    if (i < 0) return true;   // a linear without bias
+    return rd(st.at(i), v) && v->size() == want;
+  };
+  if (!rd(t1, &c.w1) || !rd(t2, &c.w2) || !rd(t3, &c.w3) ||
+      !bias(n1, (size_t)c.dim, &c.b1) || !bias(n2, (size_t)c.dim, &c.b2) ||
+      !bias(n3, (size_t)c.out_dim, &c.b3)) {
+    delete a;
+    return say("adaln: a tensor is not float or a bias has the wrong width", LTX_E_SHAPE);
+  }
+  *out = a;
+  return LTX_OK;
+}
+
+void ltx_adaln_free(ltx_adaln* a) { delete a; }
+
+int ltx_adaln_dims(const ltx_adaln* a, int* dim, int* out_dim)
+{
+  if (a == nullptr) return LTX_E_NULL;
+  if (dim) *dim = a->c.dim;
+  if (out_dim) *out_dim = a->c.out_dim;
+  return LTX_OK;
+}
+
+int ltx_adaln_run(const ltx_adaln* a, double timestep, float* out, float* embedded, int threads)
+{
+  if (a == nullptr || out == nullptr) return LTX_E_NULL;
+  ltx25::adaln_run(a->c, timestep, out, embedded, threads);
+  return LTX_OK;
 }
 
 }  // extern "C"

@@ -66,6 +66,11 @@ SIGNATURES = {
     "ltx_st_read_f32": (_I, [_P, _I, ctypes.c_uint64, ctypes.c_uint64, _P]),
     "ltx_st_metadata": (ctypes.c_char_p, [_P, ctypes.c_char_p]),
     "ltx_block_load_st": (_I, [_P, _P, ctypes.c_char_p]),
+    "ltx_adaln_create": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, ctypes.POINTER(_P)]),
+    "ltx_adaln_load_st": (_I, [_P, ctypes.c_char_p, ctypes.POINTER(_P), _P, _I]),
+    "ltx_adaln_free": (None, [_P]),
+    "ltx_adaln_dims": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "ltx_adaln_run": (_I, [_P, ctypes.c_double, _P, _P, _I]),
     "ltx_lora_load_st": (_I, [_P, _P, ctypes.c_char_p, _I, _I, ctypes.c_float,
                               ctypes.POINTER(_P)]),
     "ltx_output_head": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
@@ -406,6 +411,58 @@ class SafeTensors:
     def close(self):
         if self.h is not None and self.h.value:
             self.lib.ltx_st_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class AdaLN:
+    """ltx_adaln: one trunk adaLN chain on the host (no GPU)."""
+
+    def __init__(self, w1=None, b1=None, w2=None, b2=None, w3=None, b3=None, st=None,
+                 prefix=None):
+        """bf16-bit numpy arrays [dim][256], [dim], [dim][dim], [dim],
+        [out][dim], [out] -- or a SafeTensors and the chain's prefix."""
+        import numpy as np
+        self.lib = load()
+        h = ctypes.c_void_p()
+        if st is not None:
+            buf = ctypes.create_string_buffer(512)
+            rc = self.lib.ltx_adaln_load_st(st.h, prefix.encode(), ctypes.byref(h), buf, 512)
+            if rc != LTX_OK:
+                raise LtxError(rc, f"adaln_load_st: {buf.value.decode()}")
+        else:
+            arrs = [None if a is None else np.ascontiguousarray(a, np.uint16)
+                    for a in (w1, b1, w2, b2, w3, b3)]
+            self._keep = arrs
+            ptrs = [None if a is None else a.ctypes.data_as(_P) for a in arrs]
+            rc = self.lib.ltx_adaln_create(*ptrs, arrs[0].shape[0], arrs[4].shape[0],
+                                           ctypes.byref(h))
+            if rc != LTX_OK:
+                raise LtxError(rc, "adaln_create")
+        self.h = h
+        d, od = ctypes.c_int(), ctypes.c_int()
+        self.lib.ltx_adaln_dims(h, ctypes.byref(d), ctypes.byref(od))
+        self.dim, self.out_dim = d.value, od.value
+
+    def __call__(self, timestep, threads=0):
+        """(driver [out_dim], embedded_timestep [dim]) as f32 numpy."""
+        import numpy as np
+        out = np.empty(self.out_dim, np.float32)
+        emb = np.empty(self.dim, np.float32)
+        rc = self.lib.ltx_adaln_run(self.h, float(timestep), out.ctypes.data_as(_P),
+                                    emb.ctypes.data_as(_P), threads)
+        if rc != LTX_OK:
+            raise LtxError(rc, "adaln_run")
+        return out, emb
+
+    def close(self):
+        if self.h is not None and self.h.value:
+            self.lib.ltx_adaln_free(self.h)
             self.h = None
 
     def __del__(self):
