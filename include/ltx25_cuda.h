@@ -520,6 +520,39 @@ LTX_API int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
 LTX_API int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, int n,
                              float lora_scale, ltx_lora** out);
 
+/* ---- the embeddings connector ---------------------------------------------
+ * Replaces Ltx25Connector (src/ltx25-connector.cc:38-260): the 1-D
+ * transformer between the text encoder and the DiT.  Per block: RMSNorm,
+ * q / k / v with bias, q / k RMS gain over the whole width and the 1-D
+ * index RoPE at the connector's own max_pos (position i spans [i, i + 1)),
+ * full attention with the optional per-head gate, out projection with bias
+ * and a PLAIN residual; RMSNorm, the biased GELU feed-forward (4x), a plain
+ * residual; then an optional RMSNorm (norm_output).  Padded positions
+ * (t >= n_valid) are replaced by the learnable registers tiled over the
+ * sequence before the first block.  Tensor names are relative to the
+ * connector root ("transformer_1d_blocks.{i}.attn1.to_q.weight",
+ * "learnable_registers", ...); linears as w8g64 packs or dense f32. */
+typedef struct ltx_connector ltx_connector;
+LTX_API int ltx_connector_create(ltx_ctx* ctx, int heads, int head_dim, int layers,
+                                 int registers, int norm_output, double theta, int max_pos,
+                                 int rope_f64, ltx_connector** out);
+LTX_API void ltx_connector_destroy(ltx_connector* c);
+LTX_API const char* ltx_connector_last_error(const ltx_connector* c);
+LTX_API int ltx_connector_set_qlinear(ltx_connector* c, const char* name, const uint32_t* codes,
+                                      const void* scales, const void* biases, int sb_dtype,
+                                      int N, int K, int on_device);
+LTX_API int ltx_connector_set_tensor(ltx_connector* c, const char* name, const float* data,
+                                     int rows, int cols, int on_device);
+/* every tensor under `root` of a checkpoint (e.g. "model.diffusion_model.
+ * video_embeddings_connector.") */
+LTX_API int ltx_connector_load_st(ltx_connector* c, const ltx_st* f, const char* root);
+LTX_API int ltx_connector_finalize(ltx_connector* c);
+/* tokens: a multiple of the register count (LTX_E_SHAPE otherwise) */
+LTX_API int ltx_connector_reserve(ltx_connector* c, int tokens);
+/* out [tokens][dim] bf16 = connector(in); in == out allowed */
+LTX_API int ltx_connector_forward(ltx_connector* c, const void* in, void* out, int tokens,
+                                  int n_valid, void* stream);
+
 /* ---- the trunk's adaLN chains (host) --------------------------------------
  * Ltx25Dit::adaln_ (src/ltx25-dit.cc:51-160): the 256-channel timestep
  * sinusoid (max period 10000, no downscale shift, flip_sin_to_cos: the row

@@ -485,6 +485,22 @@ __global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, int
   }
 }
 
+// x[t][d] = regs[t % R][d] for t >= n_valid: the learnable registers tiled
+// over the padded positions (src/ltx25-kernels.metal:382-396)
+__global__ void fill_registers_kernel(__nv_bfloat16* __restrict__ x, int ldx,
+                                      const __nv_bfloat16* __restrict__ regs, int dim, int R,
+                                      int n_valid, int T)
+{
+  pdl_wait();
+  pdl_trigger();
+  const size_t n = (size_t)(T - n_valid) * dim;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int t = n_valid + (int)(i / dim), d = (int)(i % dim);
+    x[(size_t)t * ldx + d] = regs[(size_t)(t % R) * dim + d];
+  }
+}
+
 __global__ void fill_f32_kernel(float* __restrict__ out, float v, size_t n)
 {
   pdl_wait();
@@ -542,6 +558,18 @@ int launch_transpose_bf16(const __nv_bfloat16* src, int lds, __nv_bfloat16* dst,
   if (rows <= 0 || cols <= 0) return 0;
   launch_k(transpose_bf16_kernel, dim3((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)),
            dim3(32, 8), 0, s, 1, src, lds, dst, ldd, rows, cols);
+  return launched();
+}
+
+int launch_fill_registers(__nv_bfloat16* x, int ldx, const __nv_bfloat16* regs, int dim, int R,
+                          int n_valid, int T, cudaStream_t s)
+{
+  if (R <= 0 || n_valid >= T) return 0;
+  if (n_valid < 0) return -2;
+  size_t grid = ((size_t)(T - n_valid) * dim + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  launch_k(fill_registers_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, x, ldx, regs, dim, R,
+           n_valid, T);
   return launched();
 }
 

@@ -20,6 +20,9 @@ int launch_f32_to_bf16(const float* a, __nv_bfloat16* out, size_t n,
                        cudaStream_t s);
 // out[i] = v
 int launch_fill_f32(float* out, float v, size_t n, cudaStream_t s);
+// x[t] = regs[t % R] for n_valid <= t < T (rows of dim elements)
+int launch_fill_registers(__nv_bfloat16* x, int ldx, const __nv_bfloat16* regs, int dim, int R,
+                          int n_valid, int T, cudaStream_t s);
 // out = LayerNorm(x) (no affine, population variance) * (1 + scale) + shift;
 // dim % 8 == 0, dim <= 8192, shift / scale f32 [dim]
 int launch_layer_norm_mod(const __nv_bfloat16* x, int ldx, __nv_bfloat16* out, int ldo,

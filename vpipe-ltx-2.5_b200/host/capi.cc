@@ -14,6 +14,7 @@
 #include "ltx25-block-cuda.h"
 #include "ltx25-cuda-ops.h"
 #include "ltx25-adaln.h"
+#include "ltx25-connector-cuda.h"
 #include "ltx25-safetensors.h"
 
 struct ltx_ctx {
@@ -877,19 +878,20 @@ const char* ltx_st_metadata(const ltx_st* f, const char* key)
   return v == nullptr ? nullptr : v->c_str();
 }
 
-int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
+}  // extern "C"
+
+namespace {
+
+// Stage every tensor under `pre`: the "X.weight" u32 codes / "X.scales" /
+// "X.biases" triplets through `qfn` (need_q_, src/ltx25-dit-weights.cc:
+// 352-403; this build runs w8g64: 8-bit codes, K = 4 x the u32 columns, in
+// groups of 64; any other pack that closes is refused, not mis-read), every
+// other float tensor as f32 through `tfn`.  Returns an LTX_* code.
+template <class Q, class T>
+int load_prefix(const ltx25::SafeTensors& st, const std::string& pre, Q qfn, T tfn,
+                std::string* msg)
 {
-  if (b == nullptr) return LTX_E_NULL;
-  if (f == nullptr || prefix == nullptr)
-    return bfail(b, LTX_E_NULL, "load: null checkpoint or prefix");
-  const std::string pre(prefix);
-  const ltx25::SafeTensors& st = f->f;
   int bound = 0;
-  std::string e;
-  // Quantized linears first: a "X.scales" with its "X.weight" codes and
-  // "X.biases" (need_q_, src/ltx25-dit-weights.cc:352-403).  The build
-  // runs the w8g64 pack: 8-bit codes (K = 4 x the u32 columns) in groups
-  // of 64; any other pack that closes is refused, not mis-read.
   std::vector<bool> used((size_t)st.count(), false);
   for (int i = 0; i < st.count(); ++i) {
     const ltx25::StTensor& sc = st.at(i);
@@ -899,53 +901,92 @@ int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
       continue;
     const std::string base = n.substr(0, n.size() - 7);
     const int wi = st.find(base + ".weight"), bi = st.find(base + ".biases");
-    if (wi < 0 || bi < 0)
-      return bfail(b, LTX_E_STATE, "load: '" + base + "' has scales but no weight or biases");
+    if (wi < 0 || bi < 0) {
+      *msg = "load: '" + base + "' has scales but no weight or biases";
+      return LTX_E_STATE;
+    }
     const ltx25::StTensor& cw = st.at(wi);
     const ltx25::StTensor& bz = st.at(bi);
     if (cw.dtype != ltx25::ST_U32 || cw.shape.size() != 2 || sc.shape.size() != 2 ||
-        bz.shape != sc.shape || bz.dtype != sc.dtype || cw.shape[0] != sc.shape[0])
-      return bfail(b, LTX_E_SHAPE, "load: '" + base + "' is not a u32 codes / scales / biases "
-                                   "triplet of matching rows");
+        bz.shape != sc.shape || bz.dtype != sc.dtype || cw.shape[0] != sc.shape[0]) {
+      *msg = "load: '" + base + "' is not a u32 codes / scales / biases triplet of matching rows";
+      return LTX_E_SHAPE;
+    }
     const int64_t N = cw.shape[0], K = cw.shape[1] * 4, G = sc.shape[1];
-    if (G <= 0 || K % G != 0 || K / G != 64)
-      return bfail(b, LTX_E_UNSUPPORTED,
-                   "load: '" + base + "' closes at K " + std::to_string(K) + " with " +
-                       std::to_string(G) + " groups; this build runs the w8g64 pack only "
-                       "(not run by this build)");
+    if (G <= 0 || K % G != 0 || K / G != 64) {
+      *msg = "load: '" + base + "' closes at K " + std::to_string(K) + " with " +
+             std::to_string(G) + " groups; this build runs the w8g64 pack only "
+             "(not run by this build)";
+      return LTX_E_UNSUPPORTED;
+    }
     int sbd = -1;
     if (sc.dtype == ltx25::ST_F16) sbd = LTX_SB_F16;
     else if (sc.dtype == ltx25::ST_BF16) sbd = LTX_SB_BF16;
     else if (sc.dtype == ltx25::ST_F32) sbd = LTX_SB_F32;
-    if (sbd < 0) return bfail(b, LTX_E_UNSUPPORTED, "load: '" + base + "' scales dtype");
-    if (!b->blk->set_qlinear(base.substr(pre.size()) + ".weight",
-                             reinterpret_cast<const uint32_t*>(cw.data), sc.data, bz.data, sbd,
-                             (int)N, (int)K, false, &e))
-      return bfail(b, code_for(e), e);
+    if (sbd < 0) {
+      *msg = "load: '" + base + "' scales dtype";
+      return LTX_E_UNSUPPORTED;
+    }
+    std::string e;
+    if (!qfn(base.substr(pre.size()) + ".weight", reinterpret_cast<const uint32_t*>(cw.data),
+             sc.data, bz.data, sbd, (int)N, (int)K, &e)) {
+      *msg = e;
+      return code_for(e);
+    }
     used[(size_t)i] = used[(size_t)wi] = used[(size_t)bi] = true;
     ++bound;
   }
-  // Everything else under the prefix: float tensors, staged as f32.
   std::vector<float> buf;
   for (int i = 0; i < st.count(); ++i) {
     const ltx25::StTensor& t = st.at(i);
     if (used[(size_t)i] || t.name.compare(0, pre.size(), pre) != 0) continue;
-    if (t.dtype != ltx25::ST_F32 && t.dtype != ltx25::ST_F16 && t.dtype != ltx25::ST_BF16)
-      return bfail(b, LTX_E_UNSUPPORTED, "load: '" + t.name + "' is not a float tensor");
+    if (t.dtype != ltx25::ST_F32 && t.dtype != ltx25::ST_F16 && t.dtype != ltx25::ST_BF16) {
+      *msg = "load: '" + t.name + "' is not a float tensor";
+      return LTX_E_UNSUPPORTED;
+    }
     size_t n = 1;
     for (int64_t d : t.shape) n *= (size_t)d;
     if (n == 0) continue;
     buf.resize(n);
-    if (!ltx25::SafeTensors::to_f32(t, 0, n, buf.data()))
-      return bfail(b, LTX_E_SHAPE, "load: '" + t.name + "' could not be read");
+    if (!ltx25::SafeTensors::to_f32(t, 0, n, buf.data())) {
+      *msg = "load: '" + t.name + "' could not be read";
+      return LTX_E_SHAPE;
+    }
     const int rows = t.shape.empty() ? 1 : (int)t.shape[0];
     const int cols = t.shape.size() <= 1 ? 0 : (int)(n / (size_t)rows);
-    if (!b->blk->set_tensor(t.name.substr(pre.size()), buf.data(), rows, cols, false, &e))
-      return bfail(b, code_for(e), e);
+    std::string e;
+    if (!tfn(t.name.substr(pre.size()), buf.data(), rows, cols, &e)) {
+      *msg = e;
+      return code_for(e);
+    }
     ++bound;
   }
-  if (bound == 0) return bfail(b, LTX_E_STATE, "load: no tensor under '" + pre + "'");
+  if (bound == 0) {
+    *msg = "load: no tensor under '" + pre + "'";
+    return LTX_E_STATE;
+  }
   return LTX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
+{
+  if (b == nullptr) return LTX_E_NULL;
+  if (f == nullptr || prefix == nullptr)
+    return bfail(b, LTX_E_NULL, "load: null checkpoint or prefix");
+  std::string msg;
+  const int rc = load_prefix(
+      f->f, prefix,
+      [&](const std::string& n, const uint32_t* c, const void* sc, const void* bz, int sbd, int N,
+          int K, std::string* e) { return b->blk->set_qlinear(n, c, sc, bz, sbd, N, K, false, e); },
+      [&](const std::string& n, const float* d, int rows, int cols, std::string* e) {
+        return b->blk->set_tensor(n, d, rows, cols, false, e);
+      },
+      &msg);
+  return rc == LTX_OK ? LTX_OK : bfail(b, rc, msg);
 }
 
 int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, int n,
@@ -994,6 +1035,131 @@ int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, i
   return ltx_lora_upload(ctx, ab.data(), bb.data(), (int)ra, k, n, (float)factor, 0, out);
 }
 
+
+// ---- the embeddings connector -------------------------------------------------
+
+}  // extern "C"
+
+struct ltx_connector {
+  ltx_ctx* ctx = nullptr;
+  ltx25::CudaConnector* c = nullptr;
+  std::string err;
+};
+
+namespace {
+
+int cfail(ltx_connector* c, int code, const std::string& m)
+{
+  if (c != nullptr) c->err = m;
+  return code;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltx_connector_create(ltx_ctx* ctx, int heads, int head_dim, int layers, int registers,
+                         int norm_output, double theta, int max_pos, int rope_f64,
+                         ltx_connector** out)
+{
+  if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
+  *out = nullptr;
+  if (heads <= 0 || head_dim <= 0 || layers <= 0 || registers < 0 || max_pos <= 0)
+    return fail(ctx, LTX_E_SHAPE, "connector shape");
+  ltx_connector* c = new (std::nothrow) ltx_connector();
+  if (c == nullptr) return LTX_E_OOM;
+  c->ctx = ctx;
+  c->c = new (std::nothrow) ltx25::CudaConnector(&ctx->ops, heads, head_dim, layers, registers,
+                                                 norm_output != 0, theta, max_pos,
+                                                 rope_f64 != 0);
+  if (c->c == nullptr) {
+    delete c;
+    return LTX_E_OOM;
+  }
+  *out = c;
+  return LTX_OK;
+}
+
+void ltx_connector_destroy(ltx_connector* c)
+{
+  if (c == nullptr) return;
+  delete c->c;
+  delete c;
+}
+
+const char* ltx_connector_last_error(const ltx_connector* c)
+{
+  return c == nullptr ? "null connector" : c->err.c_str();
+}
+
+int ltx_connector_set_qlinear(ltx_connector* c, const char* name, const uint32_t* codes,
+                              const void* scales, const void* biases, int sb_dtype, int N, int K,
+                              int on_device)
+{
+  if (c == nullptr) return LTX_E_NULL;
+  if (name == nullptr) return cfail(c, LTX_E_NULL, "set_qlinear: null name");
+  std::string e;
+  if (!c->c->set_qlinear(name, codes, scales, biases, sb_dtype, N, K, on_device != 0, &e))
+    return cfail(c, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_connector_set_tensor(ltx_connector* c, const char* name, const float* data, int rows,
+                             int cols, int on_device)
+{
+  if (c == nullptr) return LTX_E_NULL;
+  if (name == nullptr) return cfail(c, LTX_E_NULL, "set_tensor: null name");
+  std::string e;
+  if (!c->c->set_tensor(name, data, rows, cols, on_device != 0, &e))
+    return cfail(c, code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_connector_load_st(ltx_connector* c, const ltx_st* f, const char* root)
+{
+  if (c == nullptr) return LTX_E_NULL;
+  if (f == nullptr || root == nullptr)
+    return cfail(c, LTX_E_NULL, "load: null checkpoint or root");
+  std::string msg;
+  const int rc = load_prefix(
+      f->f, root,
+      [&](const std::string& n, const uint32_t* q, const void* sc, const void* bz, int sbd, int N,
+          int K, std::string* e) { return c->c->set_qlinear(n, q, sc, bz, sbd, N, K, false, e); },
+      [&](const std::string& n, const float* d, int rows, int cols, std::string* e) {
+        return c->c->set_tensor(n, d, rows, cols, false, e);
+      },
+      &msg);
+  return rc == LTX_OK ? LTX_OK : cfail(c, rc, msg);
+}
+
+int ltx_connector_finalize(ltx_connector* c)
+{
+  if (c == nullptr) return LTX_E_NULL;
+  std::string e;
+  if (!c->c->finalize(&e))
+    return cfail(c, e.find("missing") != std::string::npos ? LTX_E_STATE : code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_connector_reserve(ltx_connector* c, int tokens)
+{
+  if (c == nullptr) return LTX_E_NULL;
+  std::string e;
+  if (!c->c->reserve(tokens, &e))
+    return cfail(c, e.find("before") != std::string::npos ? LTX_E_STATE : code_for(e), e);
+  return LTX_OK;
+}
+
+int ltx_connector_forward(ltx_connector* c, const void* in, void* out, int tokens, int n_valid,
+                          void* stream)
+{
+  if (c == nullptr) return LTX_E_NULL;
+  std::string e;
+  if (!c->c->forward(S(stream), static_cast<const __nv_bfloat16*>(in),
+                     static_cast<__nv_bfloat16*>(out), tokens, n_valid, &e))
+    return cfail(c, e.find("before") != std::string::npos ? LTX_E_STATE : code_for(e), e);
+  return LTX_OK;
+}
 
 // ---- the trunk's adaLN chains (host) ---------------------------------------
 

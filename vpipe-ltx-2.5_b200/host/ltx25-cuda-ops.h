@@ -207,6 +207,9 @@ private:
 public:
   // The context's x.A^T scratch for the standalone adapter calls, >= elems.
   __nv_bfloat16* lora_rbuf(size_t elems, std::string* err);
+  // f32 ones [>= n]: the gate of a plain residual through the gated-residual
+  // epilogue (y += 1 * (x W^T + b)).
+  const float* ones(int n, cudaStream_t s, std::string* err) { return ones_(n, s, err); }
 private:
 
   float* _ones = nullptr;

@@ -67,6 +67,16 @@ SIGNATURES = {
     "ltx_st_metadata": (ctypes.c_char_p, [_P, ctypes.c_char_p]),
     "ltx_block_load_st": (_I, [_P, _P, ctypes.c_char_p]),
     "ltx_adaln_create": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, ctypes.POINTER(_P)]),
+    "ltx_connector_create": (_I, [_P, _I, _I, _I, _I, _I, ctypes.c_double, _I, _I,
+                                  ctypes.POINTER(_P)]),
+    "ltx_connector_destroy": (None, [_P]),
+    "ltx_connector_last_error": (ctypes.c_char_p, [_P]),
+    "ltx_connector_set_qlinear": (_I, [_P, ctypes.c_char_p, _P, _P, _P, _I, _I, _I, _I]),
+    "ltx_connector_set_tensor": (_I, [_P, ctypes.c_char_p, _P, _I, _I, _I]),
+    "ltx_connector_load_st": (_I, [_P, _P, ctypes.c_char_p]),
+    "ltx_connector_finalize": (_I, [_P]),
+    "ltx_connector_reserve": (_I, [_P, _I]),
+    "ltx_connector_forward": (_I, [_P, _P, _P, _I, _I, _P]),
     "ltx_adaln_load_st": (_I, [_P, ctypes.c_char_p, ctypes.POINTER(_P), _P, _I]),
     "ltx_adaln_free": (None, [_P]),
     "ltx_adaln_dims": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
@@ -418,6 +428,78 @@ class SafeTensors:
             self.close()
         except Exception:
             pass
+
+
+class Connector:
+    """ltx_connector: the embeddings connector on the GPU."""
+
+    def __init__(self, ctx, heads, head_dim, layers, registers, norm_output=True, theta=10000.0,
+                 max_pos=4096, rope_f64=True):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        ctx._ok(ctx.lib.ltx_connector_create(ctx.h, heads, head_dim, layers, registers,
+                                             int(norm_output), float(theta), max_pos,
+                                             int(rope_f64), ctypes.byref(h)), "connector_create")
+        self.h, self.dim = h, heads * head_dim
+        self._keep = []
+
+    def err(self):
+        return self.ctx.lib.ltx_connector_last_error(self.h).decode()
+
+    def _ok(self, rc, what):
+        if rc != LTX_OK:
+            raise LtxError(rc, f"{what}: {self.err()}")
+
+    def load(self, tensors, device="cuda"):
+        """Stage a name -> f32 array map: the 2-D linears w8g64-packed on the
+        device, the rest as f32.  Returns the dequantized weights (numpy)."""
+        import numpy as np
+        import torch
+        deq = {}
+        for name, arr in tensors.items():
+            t = torch.as_tensor(np.ascontiguousarray(arr, dtype=np.float32)).to(device)
+            if t.dim() == 2 and name.endswith(".weight") and "to_gate_logits" not in name:
+                N, K = t.shape
+                c, s, b = pack_w8g64(self.ctx, t)
+                self._ok(self.ctx.lib.ltx_connector_set_qlinear(
+                    self.h, name.encode(), _ptr(c), _ptr(s), _ptr(b), SB_BF16, N, K, 1),
+                    f"set_qlinear({name})")
+                q = QWeight.upload(self.ctx, c, s, b, N, K, on_device=True)
+                deq[name] = dequant(self.ctx, q).float().cpu().numpy()
+                q.free()
+            else:
+                t = t.contiguous()
+                self._keep.append(t)
+                rows, cols = (t.shape[0], t.shape[1]) if t.dim() == 2 else (t.numel(), 0)
+                self._ok(self.ctx.lib.ltx_connector_set_tensor(
+                    self.h, name.encode(), _ptr(t), rows, cols, 1), f"set_tensor({name})")
+                deq[name] = np.asarray(arr, dtype=np.float32)
+        torch.cuda.synchronize()
+        return deq
+
+    def load_st(self, st, root):
+        self._ok(self.ctx.lib.ltx_connector_load_st(self.h, st.h, root.encode()), "load_st")
+
+    def finalize(self):
+        self._ok(self.ctx.lib.ltx_connector_finalize(self.h), "connector_finalize")
+        self._keep = []
+
+    def reserve(self, tokens):
+        self._ok(self.ctx.lib.ltx_connector_reserve(self.h, tokens), "connector_reserve")
+
+    def forward(self, x, n_valid, out=None, stream=None):
+        import torch
+        if out is None:
+            out = torch.empty_like(x)
+        self._ok(self.ctx.lib.ltx_connector_forward(self.h, _ptr(x), _ptr(out), x.shape[0],
+                                                    n_valid, _stream(stream)),
+                 "connector_forward")
+        return out
+
+    def close(self):
+        if self.h is not None and self.h.value:
+            self.ctx.lib.ltx_connector_destroy(self.h)
+            self.h = None
 
 
 class AdaLN:
