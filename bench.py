@@ -650,6 +650,64 @@ def run_trunk(args):
     return 0
 
 
+def run_connector(args):
+    """The video embeddings connector at the model's geometry: 8 blocks of
+    32 x 128 heads over 256 caption tokens (100 real, the rest registers),
+    w8g64 linears; tensor-bound GEMMs on a short sequence."""
+    import torch
+    import ltx25_b200 as L
+    from ltx25_b200.synth import connector_tensors
+    world, rank_, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    heads, hd, layers, regs, T, nv = 32, 128, 8, 128, 256, 100
+    dim = heads * hd
+    c = L.Connector(ctx, heads, hd, layers, regs)
+    c.load(connector_tensors(dim, heads, layers, regs, seed=3, device=dev), want_deq=False)
+    c.finalize()
+    c.reserve(T)
+    x = (torch.randn((T, dim), device=dev)).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    for _ in range(max(args.warmup, 3)):
+        c.forward(x, nv, out=out)
+    torch.cuda.synchronize()
+    ctx.check()
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    n0 = L.launch_count()
+    with ClockSampler(gpu_id) as clk:
+        for e0, e1 in evs:
+            e0.record()
+            c.forward(x, nv, out=out)
+            e1.record()
+        torch.cuda.synchronize()
+    launches = (L.launch_count() - n0) // max(args.steps, 1)
+    ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in evs])
+    fl = layers * (2.0 * T * dim * dim * 4 + 2.0 * T * dim * 4 * dim * 2 +
+                   4.0 * T * T * dim + 2.0 * T * dim * heads)
+    tf = fl / (ms * 1e-3) / 1e12
+    peak_tf, _, peak_kind = peaks()
+    line = {
+        "metric": "video embeddings connector TFLOP/s (8 blocks, 256 tokens, 4096 wide)",
+        "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic N(0,1) captions, random w8g64 weights",
+        "config": {"workload": "connector 8 x (attn 32x128, ff 4x), 256 tokens, 100 valid"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak_tf,
+                     "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(tf / peak_tf, 3),
+                     "traffic": None},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    c.close()
+    ctx.close()
+    return 0
+
+
 def run_block(args):
     """one joint AV block, 8160 video + 126 audio + 256
     text tokens at the real widths, synthetic w8g64 weights."""
@@ -759,7 +817,7 @@ def main():
     ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
                     help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="sweep",
-                    choices=["sweep", "block", "stack", "attn", "lora", "trunk"],
+                    choices=["sweep", "block", "stack", "attn", "lora", "trunk", "connector"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
@@ -768,6 +826,8 @@ def main():
     if args.workload == "attn" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_attn(args)
+    if args.workload == "connector" and args.impl == "ours":
+        return run_connector(args)
     if args.workload == "trunk" and args.impl == "ours":
         return run_trunk(args)
     if args.workload == "lora" and args.impl == "ours":

@@ -450,30 +450,36 @@ class Connector:
         if rc != LTX_OK:
             raise LtxError(rc, f"{what}: {self.err()}")
 
-    def load(self, tensors, device="cuda"):
-        """Stage a name -> f32 array map: the 2-D linears w8g64-packed on the
-        device, the rest as f32.  Returns the dequantized weights (numpy)."""
+    def load(self, tensors, device="cuda", want_deq=True):
+        """Stage a name -> f32 array (numpy or torch) map: the 2-D linears
+        w8g64-packed on the device, the rest as f32.  Returns the weights
+        as the GPU uses them (numpy; empty when want_deq is False)."""
         import numpy as np
         import torch
         deq = {}
         for name, arr in tensors.items():
-            t = torch.as_tensor(np.ascontiguousarray(arr, dtype=np.float32)).to(device)
+            if isinstance(arr, torch.Tensor):
+                t = arr.to(device=device, dtype=torch.float32)
+            else:
+                t = torch.as_tensor(np.ascontiguousarray(arr, dtype=np.float32)).to(device)
             if t.dim() == 2 and name.endswith(".weight") and "to_gate_logits" not in name:
                 N, K = t.shape
                 c, s, b = pack_w8g64(self.ctx, t)
                 self._ok(self.ctx.lib.ltx_connector_set_qlinear(
                     self.h, name.encode(), _ptr(c), _ptr(s), _ptr(b), SB_BF16, N, K, 1),
                     f"set_qlinear({name})")
-                q = QWeight.upload(self.ctx, c, s, b, N, K, on_device=True)
-                deq[name] = dequant(self.ctx, q).float().cpu().numpy()
-                q.free()
+                if want_deq:
+                    q = QWeight.upload(self.ctx, c, s, b, N, K, on_device=True)
+                    deq[name] = dequant(self.ctx, q).float().cpu().numpy()
+                    q.free()
             else:
                 t = t.contiguous()
                 self._keep.append(t)
                 rows, cols = (t.shape[0], t.shape[1]) if t.dim() == 2 else (t.numel(), 0)
                 self._ok(self.ctx.lib.ltx_connector_set_tensor(
                     self.h, name.encode(), _ptr(t), rows, cols, 1), f"set_tensor({name})")
-                deq[name] = np.asarray(arr, dtype=np.float32)
+                if want_deq:
+                    deq[name] = t.float().cpu().numpy()
         torch.cuda.synchronize()
         return deq
 

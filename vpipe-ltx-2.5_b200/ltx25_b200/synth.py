@@ -104,3 +104,31 @@ def random_stream_inputs(dim, tokens, text_tokens, heads, gen, device="cuda",
         "cross_gate": n(dim, s=0.1), "prompt_timestep": n(2 * dim, s=0.1),
         "pe": pe, "cross_pe": cross_pe, "present": True,
     }
+
+
+def connector_tensors(dim, heads, layers, registers, seed=0, device="cuda", gated=True):
+    """Random embeddings-connector weights under the reference's names, as
+    device f32 tensors (fan-in scaled linears, small biases, unit-ish norm
+    gains, N(0, 1) registers)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    n = lambda *s, sc=0.02: torch.randn(s, generator=g, device=device) * sc
+    t = {}
+    if registers > 0:
+        t["learnable_registers"] = n(registers, dim, sc=1.0)
+    for i in range(layers):
+        p = f"transformer_1d_blocks.{i}."
+        for m in ("to_q", "to_k", "to_v", "to_out.0"):
+            t[p + f"attn1.{m}.weight"] = n(dim, dim, sc=dim ** -0.5)
+            t[p + f"attn1.{m}.bias"] = n(dim)
+        t[p + "attn1.q_norm.weight"] = 1.0 + n(dim, sc=0.1)
+        t[p + "attn1.k_norm.weight"] = 1.0 + n(dim, sc=0.1)
+        if gated:
+            t[p + "attn1.to_gate_logits.weight"] = n(heads, dim, sc=dim ** -0.5)
+            t[p + "attn1.to_gate_logits.bias"] = n(heads)
+        t[p + "ff.net.0.proj.weight"] = n(4 * dim, dim, sc=dim ** -0.5)
+        t[p + "ff.net.0.proj.bias"] = n(4 * dim)
+        t[p + "ff.net.2.weight"] = n(dim, 4 * dim, sc=(4 * dim) ** -0.5)
+        t[p + "ff.net.2.bias"] = n(dim)
+    return t
