@@ -477,7 +477,8 @@ LTX_API int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
  * length, JSON {name: {dtype, shape, data_offsets}, "__metadata__": {..}},
  * data.  A header that is not the format's (unknown dtype, offsets outside
  * the data or disagreeing with shape x dtype, truncated file, trailing
- * bytes) is refused whole: LTX_E_SHAPE with the reason in `err`. */
+ * bytes) is refused whole: LTX_E_SHAPE with the reason in `err`; a file
+ * that cannot be opened or mapped: LTX_E_STATE. */
 typedef struct ltx_st ltx_st;
 enum {
   LTX_ST_F32 = 0, LTX_ST_F16 = 1, LTX_ST_BF16 = 2, LTX_ST_U32 = 3, LTX_ST_I32 = 4,

@@ -113,8 +113,9 @@ def test_refuses_malformed_headers(tmp_path, case):
 
 def test_missing_file_and_nulls():
     import ltx25_b200 as L
-    with pytest.raises(L.LtxError):
+    with pytest.raises(L.LtxError) as e:
         _open("/nonexistent/dir/x.safetensors")
+    assert e.value.code == -7
     lib = L.load()
     assert lib.ltx_st_count(None) == 0
     assert lib.ltx_st_name(None, 0) is None

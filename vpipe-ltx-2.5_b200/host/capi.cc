@@ -826,7 +826,7 @@ int ltx_st_open(const char* path, ltx_st** out, char* err, int err_len)
       std::strncpy(err, e.c_str(), (size_t)err_len - 1);
       err[err_len - 1] = '\0';
     }
-    return e.find("cannot") != std::string::npos ? LTX_E_NULL : LTX_E_SHAPE;
+    return e.find("cannot") != std::string::npos ? LTX_E_STATE : LTX_E_SHAPE;
   }
   *out = f;
   return LTX_OK;
