@@ -124,3 +124,62 @@ def test_missing_file_and_nulls():
     assert lib.ltx_block_load_st(None, None, b"") == -1
     assert lib.ltx_lora_load_st(None, None, b"", 1, 1, 1.0, None) == -1
     lib.ltx_st_close(None)
+
+
+def test_random_headers_never_crash(tmp_path):
+    """Property: any header bytes either parse into tensors that lie inside
+    the data, or are refused with LTX_E_SHAPE -- never a crash or a tensor
+    reaching past the file."""
+    from hypothesis import given, settings, strategies as s
+    import ltx25_b200 as L
+
+    ident = s.text(alphabet="abc._", min_size=1, max_size=6)
+    entry = s.fixed_dictionaries({
+        "dtype": s.sampled_from(["F32", "F16", "BF16", "U32", "I8", "X9", ""]),
+        "shape": s.lists(s.integers(-2, 6), max_size=3),
+        "data_offsets": s.lists(s.integers(-4, 80), min_size=0, max_size=3),
+    })
+    header = s.dictionaries(ident, entry, max_size=4)
+    path = tmp_path / "fuzz.safetensors"
+
+    @settings(max_examples=300, deadline=None)
+    @given(header, s.integers(0, 96), s.booleans())
+    def run(h, data_len, garble):
+        raw = json.dumps(h).encode()
+        if garble and raw:
+            raw = raw[: len(raw) // 2]
+        with open(path, "wb") as f:
+            f.write(struct.pack("<Q", len(raw)))
+            f.write(raw)
+            f.write(b"\x5a" * data_len)
+        try:
+            st = L.SafeTensors(path)
+        except L.LtxError as e:
+            assert e.code == -2, str(e)
+            return
+        for i in range(len(st)):
+            _, shape, ptr, nbytes = st.info(i)
+            assert nbytes <= data_len
+        st.close()
+
+    run()
+
+
+def test_device_free_apis_refuse_nulls():
+    """The adapter, connector and adaLN entry points refuse null handles
+    without touching a device."""
+    import ltx25_b200 as L
+    lib = L.load()
+    assert lib.ltx_connector_create(None, 4, 64, 1, 8, 1, 10000.0, 4096, 1, None) == -1
+    assert lib.ltx_connector_load_st(None, None, b"") == -1
+    assert lib.ltx_connector_finalize(None) == -1
+    assert lib.ltx_connector_reserve(None, 8) == -1
+    assert lib.ltx_connector_forward(None, None, None, 8, 8, None) == -1
+    assert lib.ltx_connector_last_error(None) == b"null connector"
+    lib.ltx_connector_destroy(None)
+    assert lib.ltx_adaln_run(None, 1.0, None, None, 0) == -1
+    assert lib.ltx_adaln_create(None, None, None, None, None, None, 8, 8, None) == -1
+    assert lib.ltx_adaln_load_st(None, b"", None, None, 0) == -1
+    lib.ltx_adaln_free(None)
+    assert lib.ltx_patchify(None, None, None, None, None, 0, None, 0, None, 1, 128, 64, None) == -1
+    assert lib.ltx_output_head(None, None, None, None, None, None, None, 0, 1, 64, 8, None) == -1
