@@ -1,4 +1,4 @@
-"""The trunk's adaLN chains on the host (SURVEY row (f)4's host adaLN):
+"""The trunk's adaLN chains on the host (src/ltx25-dit.cc:51-160):
 the library's chain against the numpy restatement of Ltx25Dit::adaln_,
 the [cos | sin] order and embedded_timestep's tap as controls, thread-count
 independence, and the chain bound from a checkpoint."""

@@ -1,6 +1,6 @@
-"""Blocks and adapters bound from safetensors checkpoints (SURVEY row
-(f)4): a block staged by ltx_block_load_st from a file holding w8g64 packs
-(codes u32 + F16 or BF16 scales / biases, the reference's on-disk layout)
+"""Blocks and adapters bound from safetensors checkpoints (the reference's
+loader, src/ltx25-dit-weights.cc): a block staged by ltx_block_load_st from
+a file holding w8g64 packs (codes u32 + F16 or BF16 scales / biases, the reference's on-disk layout)
 runs bit-identical to the same block staged tensor by tensor; a pack at
 another group is refused; an adapter read with ltx_lora_load_st carries
 the file's alpha / rank factor."""

@@ -1,4 +1,4 @@
-"""The embeddings connector on the GPU against the numpy
+"""The embeddings connector on the GPU (src/ltx25-connector.cc) against the numpy
 restatement of Ltx25Connector::forward: padded positions replaced by the
 tiled registers, full attention, plain residuals, biased feed-forward, the
 output norm.  The reference pads its golden deliberately (100 valid of 256,

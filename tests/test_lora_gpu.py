@@ -1,4 +1,4 @@
-"""Low-rank adapters on the GPU (SURVEY row (f)3, the reference's
+"""Low-rank adapters on the GPU (the reference's
 tests/ltx25-lora-apply-test.cc): the standalone op against f64 on the host,
 the adapted qlinear (delta in the GEMM's accumulator) against the oracle
 under each epilogue, and the adapted block against the CPU block with the

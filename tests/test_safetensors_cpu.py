@@ -1,4 +1,4 @@
-"""The checkpoint reader without a GPU (SURVEY row (f)4): tensors, dtypes,
+"""The checkpoint reader without a GPU: tensors, dtypes,
 shapes, bytes and __metadata__ read back exactly; F16 / BF16 widened exactly;
 every malformed header refused whole."""
 import json

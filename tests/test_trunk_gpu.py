@@ -1,4 +1,4 @@
-"""The DiT trunk around the block loop on the GPU: the
+"""The DiT trunk around the block loop on the GPU (src/ltx25-dit.cc): the
 patchify projection with its token pack and keyframe embedding, and the
 output head (LayerNorm, 2-row modulation, proj_out), at the model's widths,
 against the numpy restatement of tests/ltx25-trunk-test.cc's formulas.
