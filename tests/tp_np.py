@@ -11,7 +11,11 @@ implements it:
     applied once;
   * ff.net.0 keeps hidden columns [rank*F/W, ...) (GELU is per column),
     ff.net.2 the same K columns, reduced like the output projections;
-  * everything else (adaLN rows, modulation, norms of x) is replicated.
+  * everything else (adaLN rows, modulation, norms of x) is replicated;
+  * a runtime adapter (y += (x A^T) B^T, lora_np) follows its linear: on a
+    column-split site A is whole and B keeps this rank's output rows; on a
+    row-split site (to_out.0, ff.net.2) A keeps this rank's K columns, B is
+    whole, and the delta joins the partial product before the reduction.
 
 `block_forward_tp` with world == 1 is block_np.block_forward; with world > 1
 it must equal it up to summation order, which tests/test_tp_cpu.py checks
@@ -19,13 +23,26 @@ over gloo ranks.
 """
 import numpy as np
 
-from oracle import block_np, rope_np
+from oracle import block_np, lora_np, rope_np
 from oracle.block_np import F32, F64
 
 EPS = 1e-6
 
 
-def _attn_tp(t, prefix, x, ctx, pe, k_pe, heads, head_dim, rank, world, allreduce):
+def _lin(lora, module, inp, w, b, rows=slice(None), kcols=slice(None)):
+    """One sharded linear plus its adapter's share: output rows `rows` of
+    the full linear, reading only input columns `kcols` (a row-split site's
+    partial product, no bias there)."""
+    y = block_np.linear(inp, w, b)
+    pair = None if lora is None else lora.get(module)
+    if pair is None:
+        return y
+    a, bb = pair
+    return (y.astype(F64) + lora_np.delta(inp, a[:, kcols], bb[rows])).astype(F32)
+
+
+def _attn_tp(t, prefix, x, ctx, pe, k_pe, heads, head_dim, rank, world, allreduce,
+             lora=None):
     hl = heads // world
     il = hl * head_dim
     c0 = rank * il
@@ -33,10 +50,11 @@ def _attn_tp(t, prefix, x, ctx, pe, k_pe, heads, head_dim, rank, world, allreduc
     cols = slice(c0, c0 + il)
     w = lambda n: t.get(f"{prefix}.{n}")
 
-    def lin(inp, name, rows=True):
+    def lin(inp, name):
         wt = w(f"{name}.weight")
         b = w(f"{name}.bias")
-        return block_np.linear(inp, wt[cols] if rows else wt, None if b is None else b[cols])
+        return _lin(lora, f"{prefix}.{name}", inp, wt[cols], None if b is None else b[cols],
+                    rows=cols)
 
     q = lin(x, "to_q")
     k = lin(ctx, "to_k")
@@ -60,23 +78,27 @@ def _attn_tp(t, prefix, x, ctx, pe, k_pe, heads, head_dim, rank, world, allreduc
     gw = w("to_gate_logits.weight")
     if gw is not None:
         gb = w("to_gate_logits.bias")
-        g = block_np.linear(x, gw[hs], None if gb is None else gb[hs])
+        g = _lin(lora, f"{prefix}.to_gate_logits", x, gw[hs], None if gb is None else gb[hs],
+                 rows=hs)
         gate = (F32(2.0) / (F32(1.0) + np.exp(-g))).astype(F32)
         att = (att.reshape(att.shape[0], hl, head_dim) * gate[:, :, None]).astype(F32) \
             .reshape(att.shape)
-    part = block_np.linear(att, w("to_out.0.weight")[:, cols]).astype(F64)
+    part = _lin(lora, f"{prefix}.to_out.0", att, w("to_out.0.weight")[:, cols], None,
+                kcols=cols).astype(F64)
     allreduce(part)
     b = w("to_out.0.bias")
     return (part + (0.0 if b is None else np.asarray(b, F32).astype(F64))).astype(F32)
 
 
-def _ff_tp(t, pre, xin, rank, world, allreduce):
+def _ff_tp(t, pre, xin, rank, world, allreduce, lora=None):
     wi = t[f"{pre}ff.net.0.proj.weight"]
     fl = wi.shape[0] // world
     cols = slice(rank * fl, (rank + 1) * fl)
     bi = t.get(f"{pre}ff.net.0.proj.bias")
-    h = block_np.gelu_tanh(block_np.linear(xin, wi[cols], None if bi is None else bi[cols]))
-    part = block_np.linear(h, t[f"{pre}ff.net.2.weight"][:, cols]).astype(F64)
+    h = block_np.gelu_tanh(_lin(lora, f"{pre}ff.net.0.proj", xin, wi[cols],
+                                None if bi is None else bi[cols], rows=cols))
+    part = _lin(lora, f"{pre}ff.net.2", h, t[f"{pre}ff.net.2.weight"][:, cols], None,
+                kcols=cols).astype(F64)
     allreduce(part)
     bo = t.get(f"{pre}ff.net.2.bias")
     return (part + (0.0 if bo is None else np.asarray(bo, F32).astype(F64))).astype(F32)
@@ -110,10 +132,13 @@ def _ff(t, pre, s, dim, tp):
     s["x"] = (s["x"] + _ff_tp(t, pre, scaled, *tp) * mlp[2]).astype(F32)
 
 
-def block_forward_tp(t, video, audio, vdim, vheads, adim, aheads, rank, world, allreduce):
+def block_forward_tp(t, video, audio, vdim, vheads, adim, aheads, rank, world, allreduce,
+                     lora=None):
     """block_np.block_forward (src/ltx25-block-ref.cc:308-389) on one rank's
-    shard; `allreduce(arr)` sums a float64 numpy array in place over ranks."""
-    tp = (rank, world, allreduce)
+    shard; `allreduce(arr)` sums a float64 numpy array in place over ranks.
+    `lora`: module -> (A [rank][K], B [N][rank]) f32 values of the FULL
+    adapters (each rank takes its share), or None."""
+    tp = (rank, world, allreduce, lora)
     v = dict(video)
     a = dict(audio)
     v["x"] = np.asarray(v["x"], F32).copy()
