@@ -33,6 +33,7 @@ def reference(q, k, v, heads, gate=None):
     (1, 1, 1, False, 1.0, 128), (5, 1000, 3, True, 1.0, 128), (2048, 2048, 4, True, 1.0, 128),
     (8160, 256, 4, True, 1.0, 128), (1500, 1500, 2, False, 6.0, 128),
     (8160, 8160, 2, True, 1.0, 128), (300, 100, 2, True, 1.0, 128), (257, 129, 1, False, 1.0, 128),
+    (200, 50, 2, True, 1.0, 128),
     # split over the keys (few query tiles): the video->audio shape and others
     (126, 8160, 32, True, 1.0, 64), (126, 2000, 4, False, 6.0, 64), (100, 4000, 2, True, 1.0, 128),
     (126, 8160, 4, True, 1.0, 64)])
