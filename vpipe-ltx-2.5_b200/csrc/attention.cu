@@ -271,12 +271,8 @@ int launch_attention(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
   const dim3 grid((tq + kBM - 1) / kBM, heads);
   if (head_dim == 128) {
     const int smem = (kBM + 4 * kBN) * 128 * 2;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(flash_attn_kernel<128>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      attr = true;
-    }
+    static std::atomic<unsigned long long> attr{0};
+    if (!smem_limit_once(flash_attn_kernel<128>, smem, attr)) return -1;
     launch_k(flash_attn_kernel<128>, dim3(grid), dim3(128), smem, s, 1, q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, scale_log2);
   } else if (head_dim == 64) {
     const int smem = (kBM + 4 * kBN) * 64 * 2;

@@ -1329,13 +1329,8 @@ int launch_fa(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtens
               const FaParams& prm, int heads, cudaStream_t s)
 {
   using C = FaCfg<D, I8>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(fa_tc_kernel<D, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmem) != cudaSuccess)
-      return -1;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  if (!smem_limit_once(fa_tc_kernel<D, I8>, C::kSmem, attr)) return -1;
   launch_k(fa_tc_kernel<D, I8>, dim3(dim3((prm.tq + kFaBQ - 1) / kFaBQ, heads, prm.splits)), dim3(kFaThreads), C::kSmem, s, 1, tq_map, tk_map, tv_map, prm);
   return launched();
 }
@@ -1433,39 +1428,27 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
     return launched();
   }
   if (D == 64) return launch_fa<64, false>(tq_map, tk_map, tv_map, prm, heads, s);
-  static int two_tiles = -1;
-  if (two_tiles < 0) {
+  static const int two_tiles = [] {
     const char* e = getenv("LTX25_FA_TILES");
-    two_tiles = (e != nullptr && e[0] == '1') ? 0 : 1;
-  }
+    return (e != nullptr && e[0] == '1') ? 0 : 1;
+  }();
   if (tq <= kFaBQ || !two_tiles) return launch_fa<128, false>(tq_map, tk_map, tv_map, prm, heads, s);
   // kernel for tq > 128: split rows (default) or whole rows a softmax warp
   // (LTX25_FA_KIND=2)
-  static int kind = -1;
-  if (kind < 0) {
+  static const int kind = [] {
     const char* e = getenv("LTX25_FA_KIND");
-    kind = (e != nullptr && e[0] == '2') ? 2 : 3;
-  }
+    return (e != nullptr && e[0] == '2') ? 2 : 3;
+  }();
   const dim3 grid2((tq + 2 * kFaBQ - 1) / (2 * kFaBQ), heads);
   if (kind == 3) {
-    static bool attr3 = false;
-    if (!attr3) {
-      if (cudaFuncSetAttribute(fa3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               Fa3Cfg::kSmem) != cudaSuccess)
-        return -1;
-      attr3 = true;
-    }
+    static std::atomic<unsigned long long> attr3{0};
+    if (!smem_limit_once(fa3_tc_kernel, Fa3Cfg::kSmem, attr3)) return -1;
     launch_k(fa3_tc_kernel, grid2, dim3(kFa3Threads), Fa3Cfg::kSmem, s, 1, tq_map, tk_map,
              tv_map, prm);
     return launched();
   }
-  static bool attr2 = false;
-  if (!attr2) {
-    if (cudaFuncSetAttribute(fa2_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Fa2Cfg::kSmem) != cudaSuccess)
-      return -1;
-    attr2 = true;
-  }
+  static std::atomic<unsigned long long> attr2{0};
+  if (!smem_limit_once(fa2_tc_kernel, Fa2Cfg::kSmem, attr2)) return -1;
   launch_k(fa2_tc_kernel, grid2, dim3(kFa2Threads), Fa2Cfg::kSmem, s, 1, tq_map, tk_map, tv_map,
            prm);
   return launched();

@@ -652,13 +652,8 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
     return -2;
   const size_t smem = (size_t)inner * sizeof(float);
   if (smem > 48 * 1024) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(qk_norm_rope_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           96 * 1024);
-      attr = true;
-    }
+    static std::atomic<unsigned long long> attr{0};
+    if (!smem_limit_once(qk_norm_rope_kernel, 96 * 1024, attr)) return -1;
   }
   launch_k(qk_norm_rope_kernel, dim3(rows), dim3(kRowThreads), smem, s, 1, in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq, norm_width > 0 ? norm_width : inner, head0, tbl_tokens > 0 ? tbl_tokens : rows, tok0);
   return launched();

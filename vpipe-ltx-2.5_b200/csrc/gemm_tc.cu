@@ -719,11 +719,11 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
   CUtensorMap tx, tw, tsz;
   memset(&tsz, 0, sizeof(tsz));
   GemmParams p = L.p;
-  static int group_m = -1;
-  if (group_m < 0) {
+  static const int group_m = [] {
     const char* e = getenv("LTX25_GROUP_M");
-    group_m = e != nullptr ? atoi(e) : 0;
-  }
+    const int g = e != nullptr ? atoi(e) : 0;
+    return g > 0 ? g : 0;
+  }();
   if (p.group_m == 0) p.group_m = group_m;
   if (MODE == MODE_I8) {
     if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.x, p.K, p.M, L.ldx,
@@ -765,13 +765,8 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
       return -1;
   }
   auto kern = gemm_tc_kernel<MODE, TN, EPI, PAIR>;
-  static bool attr_done = false;
-  if (!attr_done) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmemBytes) != cudaSuccess)
-      return -2;
-    attr_done = true;
-  }
+  static std::atomic<unsigned long long> attr_done{0};
+  if (!smem_limit_once(kern, C::kSmemBytes, attr_done)) return -2;
   int cluster = 1;
   int grid = p.num_tiles < L.num_sms ? p.num_tiles : L.num_sms;
   if (PAIR) {

@@ -17,6 +17,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <utility>
 
@@ -39,6 +40,24 @@ inline bool pdl_enabled()
     return !(e != nullptr && e[0] == '0');
   }();
   return on;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per device.  Function
+// attributes belong to the device's context, so a process that drives several
+// GPUs (one context per host thread) sets it on each; `done` is the call
+// site's own mask, one bit per device ordinal.
+template <typename... KArgs>
+bool smem_limit_once(void (*kern)(KArgs...), int bytes, std::atomic<unsigned long long>& done)
+{
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  const unsigned long long bit = 1ull << dev;
+  if ((done.load(std::memory_order_acquire) & bit) != 0) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
 }
 
 // cudaLaunchKernelEx with the PDL attribute (and a cluster size when > 1).
