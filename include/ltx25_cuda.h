@@ -14,6 +14,12 @@
  *     for the last failure on a context is ltx_ctx_last_error().
  *   - Calls on one context are serialized by the caller (the reference's
  *     one-encoder-per-stack discipline, src/ltx25-block-metal.h:162-163).
+ *   - A context is bound to the device it was created on.  Every call on a
+ *     context, or on a block, stack, connector, weight or adapter made from
+ *     one, runs on that device whatever device the calling thread has
+ *     selected, and leaves the thread's selection as it found it; so one
+ *     thread may drive contexts on several GPUs.  ltx_ctx_create alone
+ *     leaves its device selected.  `stream` must belong to that device.
  *   - Nothing is computed on the CPU: without a usable sm_100a device the
  *     context cannot be created and every op fails with LTX_E_CUDA.
  */

@@ -48,6 +48,32 @@ int fail(ltx_ctx* c, int code, const std::string& m)
 
 cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Every call on a context, or on an object made from one, runs on the
+// context's device whatever device the calling thread has selected (one
+// thread may drive several contexts); the thread's own selection is put
+// back on return.  ltx_ctx_create alone leaves its device selected.
+class OnDevice {
+public:
+  explicit OnDevice(int dev)
+  {
+    int cur = -1;
+    if (dev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != dev &&
+        cudaSetDevice(dev) == cudaSuccess)
+      _prev = cur;
+  }
+  ~OnDevice()
+  {
+    if (_prev >= 0) cudaSetDevice(_prev);
+  }
+  OnDevice(const OnDevice&) = delete;
+  OnDevice& operator=(const OnDevice&) = delete;
+
+private:
+  int _prev = -1;
+};
+
+int dev_of(const ltx_ctx* c) { return c == nullptr ? -1 : c->ops.device(); }
+
 // Map a message from the host mirror to an error code.
 int code_for(const std::string& m)
 {
@@ -90,6 +116,7 @@ const char* ltx_ctx_last_error(const ltx_ctx* ctx)
 
 int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   std::string e;
   if (!ctx->ops.reserve(max_tokens, max_n, max_k, &e)) return fail(ctx, code_for(e), e);
@@ -98,6 +125,7 @@ int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k)
 
 int ltx_ctx_check(ltx_ctx* ctx, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   std::string e;
   const int h = ctx->ops.check(S(stream), &e);
@@ -108,6 +136,7 @@ int ltx_ctx_check(ltx_ctx* ctx, void* stream)
 
 int ltx_ctx_selftest_timeout(ltx_ctx* ctx, int bound_ms, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   const int rc = ltx::launch_watchdog_probe(ctx->ops.err_word(), bound_ms, S(stream));
   if (rc == -2) return fail(ctx, LTX_E_SHAPE, "selftest: bound_ms outside 1..2000");
@@ -117,6 +146,7 @@ int ltx_ctx_selftest_timeout(ltx_ctx* ctx, int bound_ms, void* stream)
 
 int ltx_ctx_set_trace(ltx_ctx* ctx, void* buf, int max_ctas)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   ctx->ops.set_trace(static_cast<unsigned long long*>(buf),
                      buf == nullptr ? 0 : max_ctas);
@@ -127,6 +157,7 @@ int ltx_qweight_upload(ltx_ctx* ctx, const uint32_t* codes, const void* scales,
                        const void* biases, int sb_dtype, int N, int K, int bits,
                        int group, int on_device, ltx_qweight** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   ltx_qweight* q = new (std::nothrow) ltx_qweight();
@@ -144,6 +175,7 @@ int ltx_qweight_upload(ltx_ctx* ctx, const uint32_t* codes, const void* scales,
 int ltx_dweight_upload(ltx_ctx* ctx, const uint16_t* w_bf16, int N, int K,
                        int on_device, ltx_qweight** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   ltx_qweight* q = new (std::nothrow) ltx_qweight();
@@ -159,6 +191,7 @@ int ltx_dweight_upload(ltx_ctx* ctx, const uint16_t* w_bf16, int N, int K,
 
 void ltx_qweight_free(ltx_qweight* w)
 {
+  OnDevice on_(w == nullptr ? -1 : w->w.device);
   if (w == nullptr) return;
   ltx25::free_qweight(&w->w);
   delete w;
@@ -180,6 +213,7 @@ int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x, int ldx,
                    const void* bias, void* y, int ldy, int M, int K, int N,
                    int epilogue, const void* gate, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (w == nullptr || x == nullptr || y == nullptr)
     return fail(ctx, LTX_E_NULL, "qlinear: null weight, x or y");
@@ -197,6 +231,7 @@ int ltx_qlinear_ex(ltx_ctx* ctx, const ltx_qweight* w, const void* x, int ldx,
 int ltx_lora_upload(ltx_ctx* ctx, const uint16_t* a, const uint16_t* b, int rank, int k,
                     int n, float scale, int on_device, ltx_lora** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   ltx_lora* l = new (std::nothrow) ltx_lora();
@@ -212,6 +247,7 @@ int ltx_lora_upload(ltx_ctx* ctx, const uint16_t* a, const uint16_t* b, int rank
 
 void ltx_lora_free(ltx_lora* l)
 {
+  OnDevice on_(l == nullptr ? -1 : l->p.device);
   if (l == nullptr) return;
   ltx25::free_lora(&l->p);
   delete l;
@@ -229,6 +265,7 @@ int ltx_lora_info(const ltx_lora* l, int* rank, int* k, int* n)
 int ltx_lora_add(ltx_ctx* ctx, const ltx_lora* l, const void* x, int ldx, void* y, int ldy,
                  int M, int K, int N, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (l == nullptr || x == nullptr || y == nullptr)
     return fail(ctx, LTX_E_NULL, "lora_add: null adapter, x or y");
@@ -255,6 +292,7 @@ int ltx_qlinear_lora(ltx_ctx* ctx, const ltx_qweight* w, const ltx_lora* l, cons
                      int ldx, const void* bias, void* y, int ldy, int M, int K, int N,
                      int epilogue, const void* gate, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (l == nullptr)
     return ltx_qlinear_ex(ctx, w, x, ldx, bias, y, ldy, M, K, N, epilogue, gate, stream);
@@ -287,6 +325,7 @@ int ltx_patchify(ltx_ctx* ctx, const ltx_qweight* w, const void* bias, const ltx
                  const void* latent, int channel_major, const void* prefix, int prefix_rows,
                  void* x, int T, int z, int dim, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (w == nullptr) return fail(ctx, LTX_E_NULL, "patchify: null weight");
   if (w->w.K != z || w->w.N != dim)
@@ -306,6 +345,7 @@ int ltx_output_head(ltx_ctx* ctx, const void* x, const float* shift_scale, const
                     const void* bias, const ltx_lora* l, void* out, int channel_major, int T,
                     int dim, int out_ch, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (w == nullptr) return fail(ctx, LTX_E_NULL, "output head: null weight");
   if (w->w.K != dim || w->w.N != out_ch)
@@ -323,6 +363,7 @@ int ltx_output_head(ltx_ctx* ctx, const void* x, const float* shift_scale, const
 int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                 const void* bias, void* y, int M, int K, int N, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   return ltx_qlinear_ex(ctx, w, x, K, bias, y, N, M, K, N, LTX_EPI_STORE,
                         nullptr, stream);
 }
@@ -331,6 +372,7 @@ int ltx_qlinear_i8_static(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
                           const void* bias, void* y, int M, int K, int N,
                           void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (w == nullptr || x == nullptr || y == nullptr)
     return fail(ctx, LTX_E_NULL, "qlinear_i8_static: null weight, x or y");
@@ -370,6 +412,7 @@ int ltx_tp_unique_id(void* id, int bytes)
 
 int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (world < 1 || rank < 0 || rank >= world)
     return fail(ctx, LTX_E_SHAPE, "set_tp: rank outside [0, world)");
@@ -389,6 +432,7 @@ int ltx_ctx_set_tp(ltx_ctx* ctx, int rank, int world, const void* id)
 
 int ltx_ctx_set_sp(ltx_ctx* ctx, int rank, int world, const void* id)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (world < 1 || rank < 0 || rank >= world)
     return fail(ctx, LTX_E_SHAPE, "set_sp: rank outside [0, world)");
@@ -404,6 +448,7 @@ int ltx_ctx_set_sp(ltx_ctx* ctx, int rank, int world, const void* id)
 
 int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (buf == nullptr && count > 0) return fail(ctx, LTX_E_NULL, "tp_allreduce: null buffer");
   if (dtype != 0 && dtype != 1) return fail(ctx, LTX_E_SHAPE, "tp_allreduce: dtype 0 or 1");
@@ -416,6 +461,7 @@ int ltx_tp_allreduce(ltx_ctx* ctx, void* buf, size_t count, int dtype, void* str
 
 int ltx_set_route(ltx_ctx* ctx, int route)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (route != LTX_ROUTE_FUSED && route != LTX_ROUTE_DEQUANT_ONCE && route != LTX_ROUTE_AUTO)
     return fail(ctx, LTX_E_SHAPE, "unknown route");
@@ -428,6 +474,7 @@ int ltx_set_route(ltx_ctx* ctx, int route)
 int ltx_set_tiers(ltx_ctx* ctx, int i8_gemm, int sage_attn,
                   int sage_dense_layers)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   ctx->ops.set_i8_gemm(i8_gemm != 0);
   ctx->ops.set_sage(sage_attn != 0, sage_dense_layers < 0 ? 0 : sage_dense_layers);
@@ -448,6 +495,7 @@ int ltx_sage_takes(const ltx_ctx* ctx, int head_dim)
 
 int ltx_dequant(ltx_ctx* ctx, const ltx_qweight* w, void* out, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (w == nullptr || out == nullptr) return fail(ctx, LTX_E_NULL, "dequant: null");
   if (!w->w.quantized) return fail(ctx, LTX_E_SHAPE, "dequant: weight is dense");
@@ -460,6 +508,7 @@ int ltx_dequant(ltx_ctx* ctx, const ltx_qweight* w, void* out, void* stream)
 int ltx_quant_rows_i8(ltx_ctx* ctx, const void* x, int rows, int K, int group,
                       void* q, void* scale, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (x == nullptr || q == nullptr || scale == nullptr)
     return fail(ctx, LTX_E_NULL, "quant_rows_i8: null");
@@ -475,6 +524,7 @@ int ltx_quant_rows_i8(ltx_ctx* ctx, const void* x, int rows, int K, int group,
 int ltx_pack_w8g64(ltx_ctx* ctx, const float* w, int N, int K, uint32_t* codes,
                    uint16_t* scales, uint16_t* biases, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (w == nullptr || codes == nullptr || scales == nullptr || biases == nullptr)
     return fail(ctx, LTX_E_NULL, "pack_w8g64: null");
@@ -489,6 +539,7 @@ int ltx_ada_zero(ltx_ctx* ctx, const void* x, void* out, int rows, int dim,
                  const float* scale, const float* shift, int normalize,
                  void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (x == nullptr || out == nullptr) return fail(ctx, LTX_E_NULL, "ada_zero: null");
   const int rc = ltx::launch_ada_zero(static_cast<const __nv_bfloat16*>(x), dim,
@@ -504,6 +555,7 @@ int ltx_qk_norm_rope(ltx_ctx* ctx, const void* in, int ld_in, void* out,
                      int rows, int heads, int head_dim, const float* gain,
                      const float* cos_tab, const float* sin_tab, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (in == nullptr || out == nullptr) return fail(ctx, LTX_E_NULL, "qk_norm_rope: null");
   if ((cos_tab == nullptr) != (sin_tab == nullptr))
@@ -521,6 +573,7 @@ int ltx_attention(ltx_ctx* ctx, const void* q, int ldq, const void* k, int ldk,
                   const void* gate_logits, int ldg, int tq, int tk, int heads,
                   int head_dim, void* stream)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr) return LTX_E_NULL;
   if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
     return fail(ctx, LTX_E_NULL, "attention: null");
@@ -581,6 +634,7 @@ extern "C" {
 int ltx_block_create(ltx_ctx* ctx, int video_dim, int video_heads,
                      int audio_dim, int audio_heads, ltx_block** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   if (video_dim <= 0 || video_heads <= 0 || audio_dim <= 0 || audio_heads <= 0 ||
@@ -601,6 +655,7 @@ int ltx_block_create(ltx_ctx* ctx, int video_dim, int video_heads,
 
 void ltx_block_destroy(ltx_block* b)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return;
   delete b->blk;
   delete b;
@@ -615,6 +670,7 @@ int ltx_block_set_qlinear(ltx_block* b, const char* name, const uint32_t* codes,
                           const void* scales, const void* biases, int sb_dtype,
                           int N, int K, int on_device)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   if (name == nullptr) return bfail(b, LTX_E_NULL, "set_qlinear: null name");
   std::string e;
@@ -627,6 +683,7 @@ int ltx_block_set_qlinear(ltx_block* b, const char* name, const uint32_t* codes,
 int ltx_block_set_tensor(ltx_block* b, const char* name, const float* data,
                          int rows, int cols, int on_device)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   if (name == nullptr || data == nullptr) return bfail(b, LTX_E_NULL, "set_tensor: null");
   std::string e;
@@ -637,6 +694,7 @@ int ltx_block_set_tensor(ltx_block* b, const char* name, const float* data,
 
 int ltx_block_set_lora(ltx_block* b, const char* module, const ltx_lora* l)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   if (module == nullptr || l == nullptr)
     return bfail(b, LTX_E_NULL, "set_lora: null module name or adapter");
@@ -650,6 +708,7 @@ int ltx_block_set_lora(ltx_block* b, const char* module, const ltx_lora* l)
 
 int ltx_block_finalize(ltx_block* b)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   std::string e;
   if (!b->blk->finalize(&e)) {
@@ -662,6 +721,7 @@ int ltx_block_finalize(ltx_block* b)
 int ltx_block_reserve(ltx_block* b, int max_video_tokens, int max_audio_tokens,
                       int max_text_tokens)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   std::string e;
   if (!b->blk->reserve(max_video_tokens, max_audio_tokens, max_text_tokens, &e))
@@ -671,6 +731,7 @@ int ltx_block_reserve(ltx_block* b, int max_video_tokens, int max_audio_tokens,
 
 int ltx_block_set_layer(ltx_block* b, int layer)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   if (layer < 0) return bfail(b, LTX_E_SHAPE, "set_layer: negative layer");
   b->blk->set_layer(layer);
@@ -680,6 +741,7 @@ int ltx_block_set_layer(ltx_block* b, int layer)
 int ltx_block_forward(ltx_block* b, const ltx_stream_io* video,
                       const ltx_stream_io* audio, void* stream)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   ltx25::StreamIO v = to_io(video), a = to_io(audio);
   std::string e;
@@ -718,6 +780,7 @@ extern "C" {
 
 int ltx_stack_create(ltx_ctx* ctx, ltx_stack** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   ltx_stack* s = new (std::nothrow) ltx_stack();
@@ -727,7 +790,11 @@ int ltx_stack_create(ltx_ctx* ctx, ltx_stack** out)
   return LTX_OK;
 }
 
-void ltx_stack_destroy(ltx_stack* s) { delete s; }
+void ltx_stack_destroy(ltx_stack* s)
+{
+  OnDevice on_(dev_of(s == nullptr ? nullptr : s->ctx));
+  delete s;
+}
 
 const char* ltx_stack_last_error(const ltx_stack* s)
 {
@@ -736,6 +803,7 @@ const char* ltx_stack_last_error(const ltx_stack* s)
 
 int ltx_stack_add_block(ltx_stack* s, ltx_block* b)
 {
+  OnDevice on_(dev_of(s == nullptr ? nullptr : s->ctx));
   if (s == nullptr) return LTX_E_NULL;
   if (b == nullptr) return sfail(s, LTX_E_NULL, "add_block: null block");
   if (b->ctx != s->ctx) return sfail(s, LTX_E_STATE, "add_block: block of another context");
@@ -753,6 +821,7 @@ int ltx_stack_size(const ltx_stack* s) { return s == nullptr ? 0 : (int)s->block
 int ltx_stack_reserve(ltx_stack* s, int max_video_tokens, int max_audio_tokens,
                       int max_text_tokens)
 {
+  OnDevice on_(dev_of(s == nullptr ? nullptr : s->ctx));
   if (s == nullptr) return LTX_E_NULL;
   if (s->blocks.empty()) return sfail(s, LTX_E_STATE, "reserve: empty stack");
   if (!s->arena) s->arena = std::make_shared<ltx25::BlockArena>();
@@ -769,6 +838,7 @@ int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
                       const ltx_stream_io* audio, int begin, int end,
                       ltx_progress_fn progress, void* user, void* stream)
 {
+  OnDevice on_(dev_of(s == nullptr ? nullptr : s->ctx));
   if (s == nullptr) return LTX_E_NULL;
   const int n = (int)s->blocks.size();
   if (end < 0) end = n;
@@ -974,6 +1044,7 @@ extern "C" {
 
 int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
 {
+  OnDevice on_(dev_of(b == nullptr ? nullptr : b->ctx));
   if (b == nullptr) return LTX_E_NULL;
   if (f == nullptr || prefix == nullptr)
     return bfail(b, LTX_E_NULL, "load: null checkpoint or prefix");
@@ -992,6 +1063,7 @@ int ltx_block_load_st(ltx_block* b, const ltx_st* f, const char* prefix)
 int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, int n,
                      float lora_scale, ltx_lora** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   if (f == nullptr || module == nullptr)
@@ -1062,6 +1134,7 @@ int ltx_connector_create(ltx_ctx* ctx, int heads, int head_dim, int layers, int 
                          int norm_output, double theta, int max_pos, int rope_f64,
                          ltx_connector** out)
 {
+  OnDevice on_(dev_of(ctx));
   if (ctx == nullptr || out == nullptr) return LTX_E_NULL;
   *out = nullptr;
   if (heads <= 0 || head_dim <= 0 || layers <= 0 || registers < 0 || max_pos <= 0)
@@ -1082,6 +1155,7 @@ int ltx_connector_create(ltx_ctx* ctx, int heads, int head_dim, int layers, int 
 
 void ltx_connector_destroy(ltx_connector* c)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return;
   delete c->c;
   delete c;
@@ -1096,6 +1170,7 @@ int ltx_connector_set_qlinear(ltx_connector* c, const char* name, const uint32_t
                               const void* scales, const void* biases, int sb_dtype, int N, int K,
                               int on_device)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return LTX_E_NULL;
   if (name == nullptr) return cfail(c, LTX_E_NULL, "set_qlinear: null name");
   std::string e;
@@ -1107,6 +1182,7 @@ int ltx_connector_set_qlinear(ltx_connector* c, const char* name, const uint32_t
 int ltx_connector_set_tensor(ltx_connector* c, const char* name, const float* data, int rows,
                              int cols, int on_device)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return LTX_E_NULL;
   if (name == nullptr) return cfail(c, LTX_E_NULL, "set_tensor: null name");
   std::string e;
@@ -1117,6 +1193,7 @@ int ltx_connector_set_tensor(ltx_connector* c, const char* name, const float* da
 
 int ltx_connector_load_st(ltx_connector* c, const ltx_st* f, const char* root)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return LTX_E_NULL;
   if (f == nullptr || root == nullptr)
     return cfail(c, LTX_E_NULL, "load: null checkpoint or root");
@@ -1134,6 +1211,7 @@ int ltx_connector_load_st(ltx_connector* c, const ltx_st* f, const char* root)
 
 int ltx_connector_finalize(ltx_connector* c)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return LTX_E_NULL;
   std::string e;
   if (!c->c->finalize(&e))
@@ -1143,6 +1221,7 @@ int ltx_connector_finalize(ltx_connector* c)
 
 int ltx_connector_reserve(ltx_connector* c, int tokens)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return LTX_E_NULL;
   std::string e;
   if (!c->c->reserve(tokens, &e))
@@ -1153,6 +1232,7 @@ int ltx_connector_reserve(ltx_connector* c, int tokens)
 int ltx_connector_forward(ltx_connector* c, const void* in, void* out, int tokens, int n_valid,
                           void* stream)
 {
+  OnDevice on_(dev_of(c == nullptr ? nullptr : c->ctx));
   if (c == nullptr) return LTX_E_NULL;
   std::string e;
   if (!c->c->forward(S(stream), static_cast<const __nv_bfloat16*>(in),
