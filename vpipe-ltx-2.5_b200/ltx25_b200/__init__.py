@@ -975,3 +975,6 @@ def geometry_tables(frames, height, width, audio_tokens, vdim, vheads, adim,
     a_s, a_e = audio_seconds(audio_tokens)
     a_self = rope_table(a_s, a_e, [max_pos_a], adim, aheads)
     return v_self, a_self, v_cross, a_self
+
+
+from .watch import RankWatch  # noqa: E402  (host-only: the stack's progress hook over ranks)
