@@ -650,6 +650,101 @@ def run_trunk(args):
     return 0
 
 
+# The adaLN chains of one denoise step (Ltx25Dit::compute_adaln_step_,
+# src/ltx25-dit.cc:178-236), one noise level each: (name, width, rows of the
+# root linear's output).
+ADALN_CHAINS = [("video", 4096, 9), ("prompt", 4096, 2), ("av_video_ss", 4096, 4),
+                ("av_a2v_gate", 4096, 1), ("audio", 2048, 9), ("audio_prompt", 2048, 2),
+                ("av_audio_ss", 2048, 4), ("av_v2a_gate", 2048, 1)]
+
+
+def host_read_gbs(threads, nbytes=1 << 30):
+    """Host memory read rate with `threads` threads: a torch CPU sum over a
+    1 GiB f32 tensor (best of 3), the roofline for host streaming code."""
+    import torch
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        a = torch.ones(nbytes // 4, dtype=torch.float32)
+        a.sum()
+        best = float("inf")
+        for _ in range(3):
+            t0 = time.perf_counter()
+            a.sum()
+            best = min(best, time.perf_counter() - t0)
+        return nbytes / best / 1e9
+    finally:
+        torch.set_num_threads(old)
+
+
+def run_adaln(args):
+    """The trunk's adaLN chains for one denoise step on the HOST (no GPU):
+    the eight chains of ADALN_CHAINS at BASELINE config 4's widths (video 4096,
+    audio 2048), each sinusoid -> linear_1 -> SiLU -> linear_2 -> SiLU ->
+    linear as f64-sum GEMVs over bf16 weights, split over the host's threads.
+    Host-memory-bound: the algorithmic bytes are the bf16 weights (~851 MB a
+    step)."""
+    import numpy as np
+    import ltx25_b200 as L
+    rng = np.random.default_rng(23)
+
+    def bits(*shape, sc):
+        a = (rng.standard_normal(shape, dtype=np.float32) * np.float32(sc))
+        return (a.view(np.uint32) >> 16).astype(np.uint16)
+
+    chains, nbytes, video_w = [], 0, None
+    for name, dim, rows in ADALN_CHAINS:
+        w = (bits(dim, 256, sc=0.05), bits(dim, sc=0.01), bits(dim, dim, sc=0.02),
+             bits(dim, sc=0.01), bits(rows * dim, dim, sc=0.02), bits(rows * dim, sc=0.01))
+        chains.append(L.AdaLN(*w))
+        nbytes += 2 * (w[0].size + w[1].size + w[2].size + w[3].size + w[4].size + w[5].size)
+        if name == "video":
+            video_w = w
+    threads = os.cpu_count() or 1
+    sigma = 0.725
+    step = lambda: [c(sigma * 1000.0, threads=threads) for c in chains]
+    for _ in range(max(args.warmup, 3)):
+        step()
+    steps = max(1, min(args.steps, 50))
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        ts.append(time.perf_counter() - t0)
+    sec = statistics.median(ts)
+    gbs = nbytes / sec / 1e9
+    peak = host_read_gbs(threads)
+    line = {
+        "metric": "host adaLN chains of one denoise step, GB/s of bf16 weights",
+        "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 0, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(sec * 1e3, 3),
+        "higher_is_better": True, "dtype": "bf16 weights, f64 sums",
+        "data": "synthetic N(0, 0.02) bf16 weights",
+        "config": {"workload": "8 adaLN chains (video / audio timestep 9 rows, prompt 2, "
+                               "a2v / v2a scale-shift 4, gates 1; widths 4096 / 2048), "
+                               "one noise level each; host code, no GPU",
+                   "threads": threads, "weight_bytes": int(nbytes)},
+        "gpu_launches": 0,
+        "roofline": {"bound": "host memory", "achieved": round(gbs, 2), "peak": round(peak, 2),
+                     "unit": "GB/s", "frac": round(gbs / peak, 3), "traffic": None,
+                     "peak_source": f"measured here: torch CPU sum over 1 GiB, {threads} threads"},
+    }
+    if not args.no_cpu_baseline:
+        # the numpy restatement of the chain (the port), video chain only
+        from oracle import adaln_np
+        t0 = time.perf_counter()
+        adaln_np.chain(sigma * 1000.0, *video_w)
+        t = time.perf_counter() - t0
+        vb = 2 * sum(a.size for a in video_w)
+        line["cpu_baseline"] = {"value": round(vb / t / 1e9, 3), "unit": "GB/s", "cores": threads,
+                                "kind": "port",
+                                "sample": "oracle/adaln_np.chain on the video chain (one run)"}
+    print(json.dumps(line), flush=True)
+    for c in chains:
+        c.close()
+    return 0
+
+
 def run_connector(args):
     """The video embeddings connector at the model's geometry: 8 blocks of
     32 x 128 heads over 256 caption tokens (100 real, the rest registers),
@@ -817,7 +912,8 @@ def main():
     ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
                     help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="sweep",
-                    choices=["sweep", "block", "stack", "attn", "lora", "trunk", "connector"],
+                    choices=["sweep", "block", "stack", "attn", "lora", "trunk", "connector",
+                             "adaln"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
@@ -830,6 +926,8 @@ def main():
         return run_connector(args)
     if args.workload == "trunk" and args.impl == "ours":
         return run_trunk(args)
+    if args.workload == "adaln" and args.impl == "ours":
+        return run_adaln(args)
     if args.workload == "lora" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_lora(args)

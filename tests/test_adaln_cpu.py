@@ -73,3 +73,43 @@ def test_chain_from_checkpoint(tmp_path):
     assert e.value.code == -7
     a.close()
     st.close()
+
+
+_SCALAR = """
+import sys, numpy as np
+sys.path.insert(0, sys.argv[1])
+import ltx25_b200 as L
+w = [np.load(sys.argv[2] + f"/w{i}.npy") for i in range(6)]
+out, emb = L.AdaLN(*w)(float(sys.argv[3]))
+np.save(sys.argv[2] + "/out.npy", out)
+np.save(sys.argv[2] + "/emb.npy", emb)
+"""
+
+
+@pytest.mark.parametrize("in_dim", [64, 67, 4096])
+def test_vector_and_scalar_sums_are_bit_identical(tmp_path, in_dim):
+    """The host's vector dot (AVX2 + FMA) and the scalar one sum the same
+    eight partial sums in the same order, and f32 x bf16 products are exact
+    in f64: the chain's bits must not depend on which one ran (the scalar
+    form runs in a child process with LTX25_HOST_SIMD=0).  in_dim 67 leaves
+    a tail after the last full group of eight."""
+    import os
+    import subprocess
+    import sys
+    import ltx25_b200 as L
+    rng = np.random.default_rng(in_dim)
+    f = lambda *s, sc=1.0: lib.f32_to_bf16((rng.standard_normal(s) * sc).astype(np.float32))
+    w = (f(in_dim, 256, sc=0.1), f(in_dim, sc=0.1), f(in_dim, in_dim, sc=0.15),
+         f(in_dim, sc=0.1), f(3 * in_dim, in_dim, sc=0.15), f(3 * in_dim, sc=0.1))
+    for i, a in enumerate(w):
+        np.save(tmp_path / f"w{i}.npy", a)
+    out, emb = L.AdaLN(*w)(123.25)
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                       "vpipe-ltx-2.5_b200")
+    env = dict(os.environ, LTX25_HOST_SIMD="0")
+    subprocess.run([sys.executable, "-c", _SCALAR, pkg, str(tmp_path), "123.25"], env=env,
+                   check=True, timeout=300)
+    assert np.array_equal(out.view(np.uint32), np.load(tmp_path / "out.npy").view(np.uint32))
+    assert np.array_equal(emb.view(np.uint32), np.load(tmp_path / "emb.npy").view(np.uint32))
+    want, _ = adaln_np.chain(123.25, *w)
+    assert lib.rel_l2(out, want) < 1e-6

@@ -3,7 +3,9 @@
 // block's modulation driver (Ltx25Dit::adaln_, src/ltx25-dit.cc:51-160).
 // The reference runs them as host GEMVs over bf16 weights with f64 sums,
 // once per denoise level and step, before the block loop; so does this,
-// split over host threads by output row.
+// split over host threads by output row, each row summed in a fixed order
+// (sixteen interleaved partial sums; AVX2 + FMA where the host has it,
+// LTX25_HOST_SIMD=0 forces the scalar form, which gives the same bits).
 #pragma once
 
 #include <cstdint>
