@@ -650,6 +650,107 @@ def run_trunk(args):
     return 0
 
 
+def run_i8(args):
+    """BASELINE config 3, the i8_gemm tier: per-token symmetric int8
+    quantization of X [8160][4096] (N(0,1), 0.1 % of entries x20) and the
+    kind::i8 tcgen05 GEMM against W [16384][4096] (w8g64 from N(0, 0.02),
+    requantized per output channel once, in the warm-up), int32 accumulate,
+    rescaled to bf16.  A step is one ltx_qlinear call with the tier on: the
+    activation quantization kernel plus the GEMM.  The working set (X 67 MB,
+    int8 W 67 MB, Y 267 MB) is above L2."""
+    import torch
+    import ltx25_b200 as L
+    world, rank_, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    M, K, N = 8160, 4096, 16384
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(29)
+    x = torch.randn((M, K), generator=gen, device=dev)
+    x = torch.where(torch.rand((M, K), generator=gen, device=dev) < 1e-3, x * 20.0, x)
+    x = x.to(torch.bfloat16)
+    w32 = torch.randn((N, K), generator=gen, device=dev) * 0.02
+    codes, scales, zps = L.pack_w8g64(ctx, w32)
+    qw = L.QWeight.upload(ctx, codes, scales, zps, N, K, on_device=True)
+    del w32
+    y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+    ctx.set_tiers(i8_gemm=True)
+    if not ctx.i8_takes(M, K, N):
+        raise RuntimeError("the int8 tier does not take BASELINE config 3's shape")
+    run = lambda: L.qlinear(ctx, qw, x, out=y)
+    for _ in range(max(args.warmup, 3)):
+        run()
+    torch.cuda.synchronize()
+    ctx.check()
+    steps = max(1, args.steps)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
+    n0 = L.launch_count()
+    with ClockSampler(gpu_id) as clk:
+        for e0, e1 in evs:
+            e0.record()
+            run()
+            e1.record()
+        torch.cuda.synchronize()
+    launches = (L.launch_count() - n0) // steps
+    ctx.check()
+    ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in evs])
+    ops = 2.0 * M * N * K
+    tops = ops / (ms * 1e-3) / 1e12
+    clocks = clk.summary()
+    bf16_peak, bf16_kind = tensor_peak_for(clocks)
+    peak = 2.0 * bf16_peak
+    line = {
+        "metric": "i8_gemm tier qlinear TOP/s (BASELINE config 3)",
+        "value": round(tops, 1), "unit": "TOP/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "vs_baseline": None, "dtype": "int8 x int8 -> int32, bf16 out",
+        "data": "synthetic N(0,1) activations with 0.1 % x20 outliers; N(0, 0.02) weights "
+                "w8g64-packed on device",
+        "config": {"workload": "BASELINE config 3: X [8160][4096] per-token int8, "
+                               "W [16384][4096] per-channel int8; quantization + GEMM",
+                   "l2": "working set 400 MB > L2"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor (int8)", "achieved": round(tops, 1),
+                     "peak": round(peak, 1), "unit": "TOP/s", "frac": round(tops / peak, 3),
+                     "traffic": None,
+                     "peak_source": "2 x " + bf16_kind + " (assumption: dense int8 rate = "
+                                    "2 x dense bf16, NVIDIA's nominal ratio)"},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        # the C restatement of the tier (oracle/ltx_oracle.c: per-token
+        # quantizer + integer GEMM) on a bounded sample: 256 tokens x 2048
+        # output features, full K, all host threads
+        import numpy as np
+        from oracle import lib
+        rows, feats = 256, 2048
+        xs = x[:rows].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        cs = codes[:feats].cpu().numpy().view(np.uint32)
+        ss = scales[:feats].cpu().numpy().view(np.uint16)
+        zs = zps[:feats].cpu().numpy().view(np.uint16)
+        deq = lib.dequant_bf16(cs, ss, zs, K)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        xq, sx = lib.quant_rows_i8(xs, K)
+        wq, sw = lib.quant_rows_i8(deq, K)
+        lib.i8_gemm(xq, sx, wq, sw, None, K, threads=threads)
+        t = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(2.0 * rows * feats * K / t / 1e12, 5),
+                                "unit": "TOP/s", "cores": threads, "kind": "port",
+                                "sample": f"oracle/ltx_oracle.c quantizer + integer GEMM, first "
+                                          f"{rows} tokens x first {feats} output features, "
+                                          f"full K",
+                                "seconds": round(t, 2)}
+    print(json.dumps(line), flush=True)
+    ctx.set_tiers(i8_gemm=False)
+    ctx.close()
+    return 0
+
+
 # The adaLN chains of one denoise step (Ltx25Dit::compute_adaln_step_,
 # src/ltx25-dit.cc:178-236), one noise level each: (name, width, rows of the
 # root linear's output).
@@ -913,7 +1014,7 @@ def main():
                     help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="sweep",
                     choices=["sweep", "block", "stack", "attn", "lora", "trunk", "connector",
-                             "adaln"],
+                             "adaln", "i8"],
                     help="sweep: BASELINE config 2 (the headline); block: one "
                          "joint AV block at 960x544x121 (config 4)")
     args = ap.parse_args()
@@ -928,6 +1029,8 @@ def main():
         return run_trunk(args)
     if args.workload == "adaln" and args.impl == "ours":
         return run_adaln(args)
+    if args.workload == "i8" and args.impl == "ours":
+        return run_i8(args)
     if args.workload == "lora" and args.impl == "ours":
         args.warmup = max(args.warmup, 3)
         return run_lora(args)
