@@ -803,16 +803,25 @@ def run_adaln(args):
             video_w = w
     threads = os.cpu_count() or 1
     sigma = 0.725
-    step = lambda: [c(sigma * 1000.0, threads=threads) for c in chains]
+    tsteps = [sigma * 1000.0] * len(chains)
+    # the step's chains at once (ltx_adaln_run_many), and one after another
+    # (ltx_adaln_run per chain, the reference's order) for comparison
+    step = lambda: L.adaln_run_many(chains, tsteps, threads=threads)
+    one_by_one = lambda: [c(t, threads=threads) for c, t in zip(chains, tsteps)]
     for _ in range(max(args.warmup, 3)):
         step()
+        one_by_one()
     steps = max(1, min(args.steps, 50))
-    ts = []
+    ts, ts1 = [], []
     for _ in range(steps):
         t0 = time.perf_counter()
         step()
         ts.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        one_by_one()
+        ts1.append(time.perf_counter() - t0)
     sec = statistics.median(ts)
+    sec1 = statistics.median(ts1)
     gbs = nbytes / sec / 1e9
     peak = host_read_gbs(threads)
     line = {
@@ -824,7 +833,9 @@ def run_adaln(args):
         "config": {"workload": "8 adaLN chains (video / audio timestep 9 rows, prompt 2, "
                                "a2v / v2a scale-shift 4, gates 1; widths 4096 / 2048), "
                                "one noise level each; host code, no GPU",
-                   "threads": threads, "weight_bytes": int(nbytes)},
+                   "threads": threads, "weight_bytes": int(nbytes),
+                   "api": "ltx_adaln_run_many (one thread set for the step's chains)",
+                   "one_chain_at_a_time_ms": round(sec1 * 1e3, 3)},
         "gpu_launches": 0,
         "roofline": {"bound": "host memory", "achieved": round(gbs, 2), "peak": round(peak, 2),
                      "unit": "GB/s", "frac": round(gbs / peak, 3), "traffic": None,

@@ -113,3 +113,29 @@ def test_vector_and_scalar_sums_are_bit_identical(tmp_path, in_dim):
     assert np.array_equal(emb.view(np.uint32), np.load(tmp_path / "emb.npy").view(np.uint32))
     want, _ = adaln_np.chain(123.25, *w)
     assert lib.rel_l2(out, want) < 1e-6
+
+
+def test_a_step_of_chains_at_once_equals_each_alone():
+    """ltx_adaln_run_many (a denoise step's chains on one thread set, rows
+    split across the chains) gives each chain's bits as ltx_adaln_run does,
+    at chains of different widths and timesteps, and refuses bad arguments."""
+    import ltx25_b200 as L
+    rng = np.random.default_rng(7)
+    f = lambda *s, sc=1.0: lib.f32_to_bf16((rng.standard_normal(s) * sc).astype(np.float32))
+    chains = []
+    for dim, rows in ((96, 9), (64, 2), (96, 1), (40, 4)):
+        chains.append(L.AdaLN(f(dim, 256, sc=0.1), f(dim, sc=0.1), f(dim, dim, sc=0.15),
+                              f(dim, sc=0.1), f(rows * dim, dim, sc=0.15), None))
+    ts = [725.0, 725.0, 312.5, 0.0]
+    for threads in (1, 3, 8):
+        many = L.adaln_run_many(chains, ts, threads=threads)
+        for c, t, (out, emb) in zip(chains, ts, many):
+            o1, e1 = c(t, threads=threads)
+            assert np.array_equal(out.view(np.uint32), o1.view(np.uint32))
+            assert np.array_equal(emb.view(np.uint32), e1.view(np.uint32))
+    assert L.adaln_run_many([], []) == []
+    lib_ = chains[0].lib
+    assert lib_.ltx_adaln_run_many(None, None, None, None, 2, 0) == -1     # LTX_E_NULL
+    assert lib_.ltx_adaln_run_many(None, None, None, None, -1, 0) == -2    # LTX_E_SHAPE
+    for c in chains:
+        c.close()

@@ -1336,4 +1336,19 @@ int ltx_adaln_run(const ltx_adaln* a, double timestep, float* out, float* embedd
   return LTX_OK;
 }
 
+int ltx_adaln_run_many(const ltx_adaln* const* chains, const double* timesteps,
+                       float* const* outs, float* const* embedded, int count, int threads)
+{
+  if (count < 0) return LTX_E_SHAPE;
+  if (count == 0) return LTX_OK;
+  if (chains == nullptr || timesteps == nullptr || outs == nullptr) return LTX_E_NULL;
+  std::vector<const ltx25::AdaLNChain*> cs((size_t)count);
+  for (int i = 0; i < count; ++i) {
+    if (chains[i] == nullptr || outs[i] == nullptr) return LTX_E_NULL;
+    cs[(size_t)i] = &chains[i]->c;
+  }
+  ltx25::adaln_run_many(cs.data(), timesteps, outs, embedded, count, threads);
+  return LTX_OK;
+}
+
 }  // extern "C"

@@ -151,31 +151,67 @@ void timestep_sinusoid(double t, int channels, float* out)
   }
 }
 
-void adaln_run(const AdaLNChain& c, double t, float* out, float* embedded, int threads)
+void adaln_run_many(const AdaLNChain* const* chains, const double* t, float* const* out,
+                    float* const* embedded, int count, int threads)
 {
+  if (count <= 0) return;
   if (threads <= 0) threads = (int)std::max(1u, std::thread::hardware_concurrency());
   threads = std::min(threads, 64);
-  const int dim = c.dim, od = c.out_dim;
-  std::vector<float> proj(256);
-  timestep_sinusoid(t, 256, proj.data());
-  const std::vector<double> x1(proj.begin(), proj.end());
-  // The three linears' inputs in f64 (silu applied), and h2 itself for
-  // `embedded`.  Each thread owns a row range of every stage; the stages
-  // are separated by a barrier, since each reads the whole previous output.
-  std::vector<double> x2((size_t)dim), x3((size_t)dim);
-  std::vector<float> h1((size_t)dim), h2((size_t)dim);
-  const int nt = std::max(1, std::min(threads, std::max(dim, od) / 64));
+  // Per chain: the sinusoid and the three linears' inputs in f64 (SiLU
+  // applied), and h1 / h2 in f32 (h2 is `embedded`).  Every stage's rows,
+  // over all chains, are split evenly over one set of threads, with a
+  // barrier between the stages (each reads the whole previous output of its
+  // own chain).
+  struct Work {
+    const AdaLNChain* c;
+    std::vector<double> x1, x2, x3;
+    std::vector<float> h1, h2;
+  };
+  std::vector<Work> w((size_t)count);
+  long long rows[3] = {0, 0, 0};
+  for (int i = 0; i < count; ++i) {
+    Work& k = w[(size_t)i];
+    k.c = chains[i];
+    std::vector<float> proj(256);
+    timestep_sinusoid(t[i], 256, proj.data());
+    k.x1.assign(proj.begin(), proj.end());
+    k.x2.resize((size_t)k.c->dim);
+    k.x3.resize((size_t)k.c->dim);
+    k.h1.resize((size_t)k.c->dim);
+    k.h2.resize((size_t)k.c->dim);
+    rows[0] += k.c->dim;
+    rows[1] += k.c->dim;
+    rows[2] += k.c->out_dim;
+  }
+  const long long most = std::max(rows[0], rows[2]);
+  const int nt = (int)std::max(1LL, std::min((long long)threads, most / 64));
   StageBarrier bar(nt);
-  auto part = [](int n, int k, int parts) { return (int)((long long)n * k / parts); };
+  // rows [g0, g1) of stage `stage`, numbered across the chains in order
+  auto stage_rows = [&](int stage, long long g0, long long g1) {
+    long long base = 0;
+    for (Work& k : w) {
+      const int n = stage == 2 ? k.c->out_dim : k.c->dim;
+      const long long lo = std::max(g0, base), hi = std::min(g1, base + n);
+      if (lo < hi) {
+        const int a = (int)(lo - base), b = (int)(hi - base);
+        if (stage == 0) {
+          gemv_rows(k.x1.data(), k.c->w1, k.c->b1, 256, a, b, k.h1.data());
+          for (int o = a; o < b; ++o) k.x2[(size_t)o] = (double)silu1(k.h1[(size_t)o]);
+        } else if (stage == 1) {
+          gemv_rows(k.x2.data(), k.c->w2, k.c->b2, k.c->dim, a, b, k.h2.data());
+          for (int o = a; o < b; ++o) k.x3[(size_t)o] = (double)silu1(k.h2[(size_t)o]);
+        } else {
+          gemv_rows(k.x3.data(), k.c->w3, k.c->b3, k.c->dim, a, b, out[&k - w.data()]);
+        }
+      }
+      base += n;
+    }
+  };
   auto work = [&](int k) {
-    int a = part(dim, k, nt), b = part(dim, k + 1, nt);
-    gemv_rows(x1.data(), c.w1, c.b1, 256, a, b, h1.data());
-    for (int o = a; o < b; ++o) x2[(size_t)o] = (double)silu1(h1[(size_t)o]);
-    bar.wait();
-    gemv_rows(x2.data(), c.w2, c.b2, dim, a, b, h2.data());
-    for (int o = a; o < b; ++o) x3[(size_t)o] = (double)silu1(h2[(size_t)o]);
-    bar.wait();
-    gemv_rows(x3.data(), c.w3, c.b3, dim, part(od, k, nt), part(od, k + 1, nt), out);
+    for (int stage = 0; stage < 3; ++stage) {
+      if (stage > 0) bar.wait();
+      stage_rows(stage, rows[stage] * k / nt, rows[stage] * (k + 1) / nt);
+    }
   };
   if (nt == 1) {
     work(0);
@@ -186,7 +222,17 @@ void adaln_run(const AdaLNChain& c, double t, float* out, float* embedded, int t
     work(0);
     for (auto& th : pool) th.join();
   }
-  if (embedded != nullptr) std::memcpy(embedded, h2.data(), (size_t)dim * 4);
+  for (int i = 0; i < count; ++i)
+    if (embedded != nullptr && embedded[i] != nullptr)
+      std::memcpy(embedded[i], w[(size_t)i].h2.data(), (size_t)w[(size_t)i].c->dim * 4);
+}
+
+void adaln_run(const AdaLNChain& c, double t, float* out, float* embedded, int threads)
+{
+  const AdaLNChain* cs[1] = {&c};
+  float* outs[1] = {out};
+  float* embs[1] = {embedded};
+  adaln_run_many(cs, &t, outs, embs, 1, threads);
 }
 
 }  // namespace ltx25

@@ -28,4 +28,12 @@ void timestep_sinusoid(double t, int channels, float* out);
 // linear_1(sinusoid(t)))) (may be null); `threads` <= 0: the host's count.
 void adaln_run(const AdaLNChain& c, double t, float* out, float* embedded, int threads);
 
+// `count` chains at once (a denoise step's chains, each at its own
+// timestep) on one set of host threads: each stage's rows over all chains
+// are split evenly, with one barrier per stage.  Every row is summed exactly
+// as adaln_run sums it, so the results are the same bits.  embedded (or any
+// of its entries) may be null.
+void adaln_run_many(const AdaLNChain* const* chains, const double* t, float* const* out,
+                    float* const* embedded, int count, int threads);
+
 }  // namespace ltx25

@@ -81,6 +81,7 @@ SIGNATURES = {
     "ltx_adaln_free": (None, [_P]),
     "ltx_adaln_dims": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "ltx_adaln_run": (_I, [_P, ctypes.c_double, _P, _P, _I]),
+    "ltx_adaln_run_many": (_I, [_P, _P, _P, _P, _I, _I]),
     "ltx_lora_load_st": (_I, [_P, _P, ctypes.c_char_p, _I, _I, ctypes.c_float,
                               ctypes.POINTER(_P)]),
     "ltx_output_head": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
@@ -506,6 +507,28 @@ class Connector:
         if self.h is not None and self.h.value:
             self.ctx.lib.ltx_connector_destroy(self.h)
             self.h = None
+
+
+def adaln_run_many(chains, timesteps, threads=0):
+    """ltx_adaln_run_many: a denoise step's chains at once on one set of host
+    threads.  Returns [(driver, embedded_timestep)] as f32 numpy, in order;
+    the same bits as calling each chain alone."""
+    import numpy as np
+    if len(chains) != len(timesteps):
+        raise ValueError("one timestep per chain")
+    n = len(chains)
+    if n == 0:
+        return []
+    outs = [np.empty(c.out_dim, np.float32) for c in chains]
+    embs = [np.empty(c.dim, np.float32) for c in chains]
+    hs = (_P * n)(*[c.h.value for c in chains])
+    ts = (ctypes.c_double * n)(*[float(t) for t in timesteps])
+    po = (_P * n)(*[o.ctypes.data for o in outs])
+    pe = (_P * n)(*[e.ctypes.data for e in embs])
+    rc = chains[0].lib.ltx_adaln_run_many(hs, ts, po, pe, n, threads)
+    if rc != LTX_OK:
+        raise LtxError(rc, "adaln_run_many")
+    return list(zip(outs, embs))
 
 
 class AdaLN:
