@@ -154,3 +154,33 @@ def test_arguments_are_checked():
     assert all(w(i, 4) for i in range(4))
     w.abort("done")
     assert not w(0, 4) and w.failed == (0, "abort requested: done")
+
+
+def test_tcp_store_clients_agree():
+    """The same protocol over a TCPStore on 127.0.0.1 (the store a multi-node
+    run would use), each rank holding its own client: a rank leaving after
+    step 0 block 5 stops the others there."""
+    import datetime
+    import torch.distributed as dist
+    import ltx25_b200 as L
+    world = 3
+    master = dist.TCPStore("127.0.0.1", 0, world, True,
+                           timeout=datetime.timedelta(seconds=30), wait_for_workers=False)
+    port = master.port
+    res = {}
+
+    def rank(r):
+        store = dist.TCPStore("127.0.0.1", port, world, False,
+                              timeout=datetime.timedelta(seconds=30))
+        w = L.RankWatch(store, r, world, timeout_s=2.0, prefix="tcp")
+        res[r] = _run(w, 1, exit_at=(0, 5) if r == 2 else None)
+
+    th = [threading.Thread(target=rank, args=(r,)) for r in range(world)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=60)
+    assert all(not t.is_alive() for t in th)
+    for r in (0, 1):
+        assert res[r][0] == [(0, b) for b in range(5)], res[r][0]
+        assert res[r][1][0] == 2
