@@ -78,3 +78,34 @@ def test_rope_tables_match_reference_golden(golden):
     np.testing.assert_allclose(c, g["cross__cos"], atol=1.2e-7)
     # spans: the time axis equals the reference's video_time_seconds
     np.testing.assert_array_equal(np.unique(s[0]), g["vtime"][:2])
+
+
+_ONE_THREAD_TABLE = """
+import sys, numpy as np
+sys.path.insert(0, sys.argv[1])
+import ltx25_b200 as L
+s, e = L.video_spans(16, 17, 30)
+c, sn = L.rope_table(s, e, [20, 2048, 2048], 4096, 32)
+np.save(sys.argv[2] + "/c.npy", c)
+np.save(sys.argv[2] + "/s.npy", sn)
+"""
+
+
+def test_rope_table_threads_give_the_same_bits(tmp_path):
+    """The video table at BASELINE config 4's geometry (8160 tokens, 32
+    heads) built over the host's threads equals, bit for bit, the table
+    built on one thread (LTX25_HOST_THREADS=1 in a child process)."""
+    import os
+    import subprocess
+    import sys
+    import numpy as np
+    import ltx25_b200 as L
+    s, e = L.video_spans(16, 17, 30)
+    c, sn = L.rope_table(s, e, [20, 2048, 2048], 4096, 32)
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                       "vpipe-ltx-2.5_b200")
+    env = dict(os.environ, LTX25_HOST_THREADS="1")
+    subprocess.run([sys.executable, "-c", _ONE_THREAD_TABLE, pkg, str(tmp_path)], env=env,
+                   check=True, timeout=300)
+    assert np.array_equal(c.view(np.uint32), np.load(tmp_path / "c.npy").view(np.uint32))
+    assert np.array_equal(sn.view(np.uint32), np.load(tmp_path / "s.npy").view(np.uint32))

@@ -12,8 +12,11 @@
 //   * video positions are pixels on h/w and SECONDS on t (scale factors
 //     8/32/32, causal first frame), audio positions are seconds of mel
 //     frames (hop 160 at 16 kHz, 4 mel frames per latent, causal).
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 #include "../../include/ltx25_cuda.h"
@@ -38,6 +41,21 @@ std::vector<float> ladder(double theta, int n_axes, int inner, int f64)
   return out;
 }
 
+// Host threads for a table of `tokens` rows: the host's count, or
+// LTX25_HOST_THREADS when set, at most one per 256 tokens.  Every element
+// is computed the same way on any thread, so the table does not depend on
+// the count.
+int table_threads(int tokens)
+{
+  static const int cap = [] {
+    const char* e = std::getenv("LTX25_HOST_THREADS");
+    int n = e != nullptr ? std::atoi(e) : 0;
+    if (n <= 0) n = (int)std::thread::hardware_concurrency();
+    return std::max(1, std::min(n, 64));
+  }();
+  return std::max(1, std::min(cap, tokens / 256));
+}
+
 }  // namespace
 
 extern "C" {
@@ -59,29 +77,45 @@ int ltx_rope_table(const double* starts, const double* ends, int n_axes,
   const int used = n_freq * n_axes;
   const int pad = half * heads - used;
   if (pad < 0) return LTX_E_SHAPE;
-  std::vector<float> rc((size_t)(pad + used)), rs((size_t)(pad + used));
-  for (int i = 0; i < pad; ++i) {
-    rc[(size_t)i] = 1.0f;
-    rs[(size_t)i] = 0.0f;
-  }
-  for (int t = 0; t < tokens; ++t) {
-    for (int f = 0; f < n_freq; ++f) {
-      for (int a = 0; a < n_axes; ++a) {
-        const size_t idx = (size_t)a * tokens + t;
-        const float mid = (float)((starts[idx] + ends[idx]) * 0.5);
-        const float frac = mid / (float)max_pos[a];
-        const float ang = lad[(size_t)f] * (frac * 2.0f - 1.0f);
-        const size_t k = (size_t)pad + (size_t)f * n_axes + a;
-        rc[k] = std::cos(ang);
-        rs[k] = std::sin(ang);
+  // tokens [t0, t1): one padded row at a time in the thread's own scratch,
+  // then split per head
+  auto rows = [&](int t0, int t1) {
+    std::vector<float> rc((size_t)(pad + used)), rs((size_t)(pad + used));
+    for (int i = 0; i < pad; ++i) {
+      rc[(size_t)i] = 1.0f;
+      rs[(size_t)i] = 0.0f;
+    }
+    for (int t = t0; t < t1; ++t) {
+      for (int f = 0; f < n_freq; ++f) {
+        for (int a = 0; a < n_axes; ++a) {
+          const size_t idx = (size_t)a * tokens + t;
+          const float mid = (float)((starts[idx] + ends[idx]) * 0.5);
+          const float frac = mid / (float)max_pos[a];
+          const float ang = lad[(size_t)f] * (frac * 2.0f - 1.0f);
+          const size_t k = (size_t)pad + (size_t)f * n_axes + a;
+          rc[k] = std::cos(ang);
+          rs[k] = std::sin(ang);
+        }
+      }
+      for (int h = 0; h < heads; ++h) {
+        const size_t dst = ((size_t)h * tokens + t) * half;
+        std::memcpy(cos_out + dst, rc.data() + (size_t)h * half, half * sizeof(float));
+        std::memcpy(sin_out + dst, rs.data() + (size_t)h * half, half * sizeof(float));
       }
     }
-    for (int h = 0; h < heads; ++h) {
-      const size_t dst = ((size_t)h * tokens + t) * half;
-      std::memcpy(cos_out + dst, rc.data() + (size_t)h * half, half * sizeof(float));
-      std::memcpy(sin_out + dst, rs.data() + (size_t)h * half, half * sizeof(float));
-    }
+  };
+  const int nt = table_threads(tokens);
+  if (nt == 1) {
+    rows(0, tokens);
+    return LTX_OK;
   }
+  std::vector<std::thread> pool;
+  pool.reserve((size_t)nt - 1);
+  for (int k = 1; k < nt; ++k)
+    pool.emplace_back(rows, (int)((long long)tokens * k / nt),
+                      (int)((long long)tokens * (k + 1) / nt));
+  rows(0, (int)((long long)tokens / nt));
+  for (auto& th : pool) th.join();
   return LTX_OK;
 }
 
