@@ -74,7 +74,8 @@ def _raw(tmp_path, header_obj=None, header_bytes=None, data=b"", length=None):
 
 @pytest.mark.parametrize("case", [
     "short", "length_past_end", "not_object", "bad_json", "unknown_dtype", "offsets_vs_shape",
-    "past_data", "duplicate", "trailing", "float_shape", "missing_offsets", "negative_dim"])
+    "past_data", "duplicate", "trailing", "float_shape", "missing_offsets", "negative_dim",
+    "repeated_shape", "repeated_dtype", "nine_dims"])
 def test_refuses_malformed_headers(tmp_path, case):
     import ltx25_b200 as L
     ok = {"t": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]}}
@@ -103,6 +104,17 @@ def test_refuses_malformed_headers(tmp_path, case):
         p = _raw(tmp_path, {"t": {"dtype": "F32", "shape": [2.0], "data_offsets": [0, 8]}}, data=data)
     elif case == "missing_offsets":
         p = _raw(tmp_path, {"t": {"dtype": "F32", "shape": [2]}}, data=data)
+    elif case == "repeated_shape":
+        # [1] then [2]: appended, the shape would read [1, 2] and match the data
+        p = _raw(tmp_path, header_bytes=b'{"t": {"dtype": "F32", "shape": [1], "shape": [2], '
+                 b'"data_offsets": [0, 8]}}', data=data)
+    elif case == "repeated_dtype":
+        p = _raw(tmp_path, header_bytes=b'{"t": {"dtype": "F16", "dtype": "F32", "shape": [2], '
+                 b'"data_offsets": [0, 8]}}', data=data)
+    elif case == "nine_dims":
+        # consistent with its data, but more dimensions than the ABI's shape holds
+        p = _raw(tmp_path, {"t": {"dtype": "F32", "shape": [1] * 8 + [2],
+                                  "data_offsets": [0, 8]}}, data=data)
     else:
         p = _raw(tmp_path, {"t": {"dtype": "F32", "shape": [-2], "data_offsets": [0, 8]}}, data=data)
     with pytest.raises(L.LtxError) as e:
@@ -183,3 +195,15 @@ def test_device_free_apis_refuse_nulls():
     lib.ltx_adaln_free(None)
     assert lib.ltx_patchify(None, None, None, None, None, 0, None, 0, None, 1, 128, 64, None) == -1
     assert lib.ltx_output_head(None, None, None, None, None, None, None, 0, 1, 64, 8, None) == -1
+
+
+def test_eight_dimensions_is_the_limit(tmp_path):
+    """A tensor of 8 dimensions (the ABI's shape slots) opens and reports
+    all of them; the nine-dimension case above is refused."""
+    import ltx25_b200 as L
+    p = _raw(tmp_path, {"t": {"dtype": "F32", "shape": [1] * 7 + [2],
+                              "data_offsets": [0, 8]}}, data=b"\0" * 8)
+    st = _open(p)
+    _, shape, _, nbytes = st.info(0)
+    assert list(shape) == [1] * 7 + [2] and nbytes == 8
+    st.close()

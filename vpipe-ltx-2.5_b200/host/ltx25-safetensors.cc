@@ -310,12 +310,20 @@ bool SafeTensors::parse(const uint8_t* base, size_t size, std::string* err)
       t.name = name;
       std::string dt;
       int64_t b0 = -1, b1 = -1;
-      bool have_shape = false, have_dtype = false, ok = j.eat('{') || j.bad("expected '{'");
+      bool have_shape = false, have_dtype = false, have_offsets = false;
+      bool ok = j.eat('{') || j.bad("expected '{'");
       if (ok && !j.eat('}')) {
         do {
           std::string k;
           ok = j.str(&k) && (j.eat(':') || j.bad("expected ':'"));
           if (!ok) break;
+          // one of each key: a repeated one would silently replace (or, for
+          // shape, extend) what the first said
+          if ((k == "dtype" && have_dtype) || (k == "shape" && have_shape) ||
+              (k == "data_offsets" && have_offsets)) {
+            ok = j.bad("tensor '" + name + "' repeats its " + k);
+            break;
+          }
           if (k == "dtype") {
             ok = j.str(&dt);
             have_dtype = true;
@@ -325,12 +333,16 @@ bool SafeTensors::parse(const uint8_t* base, size_t size, std::string* err)
             if (ok && !j.eat(']')) {
               do {
                 int64_t d = 0;
-                ok = j.integer(&d) && (d >= 0 || j.bad("negative dimension"));
+                ok = j.integer(&d) && (d >= 0 || j.bad("negative dimension")) &&
+                     (t.shape.size() < (size_t)kStMaxDims ||
+                      j.bad("tensor '" + name + "' has more than " +
+                            std::to_string(kStMaxDims) + " dimensions"));
                 if (ok) t.shape.push_back(d);
               } while (ok && j.eat(','));
               ok = ok && (j.eat(']') || j.bad("expected ']'"));
             }
           } else if (k == "data_offsets") {
+            have_offsets = true;
             ok = (j.eat('[') || j.bad("data_offsets is not an array")) && j.integer(&b0) &&
                  (j.eat(',') || j.bad("data_offsets needs two entries")) && j.integer(&b1) &&
                  (j.eat(']') || j.bad("data_offsets has more than two entries"));

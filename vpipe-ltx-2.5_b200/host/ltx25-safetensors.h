@@ -19,6 +19,10 @@ enum StDtype : int {
   ST_I8 = 6, ST_F64 = 7, ST_I64 = 8, ST_U16 = 9, ST_I16 = 10, ST_BOOL = 11,
 };
 
+// A header whose tensor has more dimensions than this is refused (the C
+// ABI's ltx_st_info hands a shape back in 8 slots).
+constexpr int kStMaxDims = 8;
+
 struct StTensor {
   std::string name;
   int dtype = 0;
