@@ -1,5 +1,6 @@
 // capi.cc -- the extern "C" boundary declared in include/ltx25_cuda.h, over
 // the C++ host mirror (CudaOps and friends).
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
@@ -1095,7 +1096,7 @@ int ltx_lora_load_st(ltx_ctx* ctx, const ltx_st* f, const char* module, int k, i
     if (s == nullptr || s->empty()) return false;
     char* end = nullptr;
     *v = std::strtod(s->c_str(), &end);
-    return end != s->c_str();
+    return end != s->c_str() && std::isfinite(*v);
   };
   double alpha = 0.0, rank = 0.0;
   if (num("lora_alpha", &alpha) && num("lora_rank", &rank) && rank > 0.0 && alpha > 0.0)
