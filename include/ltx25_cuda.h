@@ -591,8 +591,8 @@ LTX_API int ltx_adaln_run(const ltx_adaln* a, double timestep, float* out, float
 /* A denoise step's chains at once (Ltx25Dit::compute_adaln_step_,
  * src/ltx25-dit.cc:178-236, runs them one after another): chains[i] at
  * timesteps[i] into outs[i] (and embedded[i] when embedded and the entry are
- * non-NULL), on one set of host threads with each stage's rows over all
- * chains split evenly.  Same bits as count separate ltx_adaln_run calls. */
+ * non-NULL), each stage's rows over all chains split evenly over the host
+ * threads.  Same bits as count separate ltx_adaln_run calls. */
 LTX_API int ltx_adaln_run_many(const ltx_adaln* const* chains, const double* timesteps,
                                float* const* outs, float* const* embedded, int count,
                                int threads);

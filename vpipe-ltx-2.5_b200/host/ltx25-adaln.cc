@@ -1,12 +1,11 @@
 // ltx25-adaln.cc -- see ltx25-adaln.h.
 #include "ltx25-adaln.h"
+#include "ltx25-threads.h"
 
 #include <algorithm>
 #include <cmath>
-#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
-#include <mutex>
 #include <thread>
 
 #if defined(__x86_64__)
@@ -113,31 +112,6 @@ void gemv_rows(const double* xd, const std::vector<uint16_t>& w,
 
 float silu1(float z) { return z / (1.0f + std::exp(-z)); }
 
-// A reusable barrier for one chain's threads (C++17 has no std::barrier).
-class StageBarrier {
-public:
-  explicit StageBarrier(int n) : _n(n) {}
-  void wait()
-  {
-    std::unique_lock<std::mutex> lk(_m);
-    const unsigned gen = _gen;
-    if (++_count == _n) {
-      _count = 0;
-      ++_gen;
-      _cv.notify_all();
-      return;
-    }
-    _cv.wait(lk, [&] { return _gen != gen; });
-  }
-
-private:
-  std::mutex _m;
-  std::condition_variable _cv;
-  int _n;
-  int _count = 0;
-  unsigned _gen = 0;
-};
-
 }  // namespace
 
 void timestep_sinusoid(double t, int channels, float* out)
@@ -159,9 +133,8 @@ void adaln_run_many(const AdaLNChain* const* chains, const double* t, float* con
   threads = std::min(threads, 64);
   // Per chain: the sinusoid and the three linears' inputs in f64 (SiLU
   // applied), and h1 / h2 in f32 (h2 is `embedded`).  Every stage's rows,
-  // over all chains, are split evenly over one set of threads, with a
-  // barrier between the stages (each reads the whole previous output of its
-  // own chain).
+  // over all chains, are split evenly over the threads; the stages run one
+  // after another (each reads the whole previous output of its own chain).
   struct Work {
     const AdaLNChain* c;
     std::vector<double> x1, x2, x3;
@@ -185,7 +158,6 @@ void adaln_run_many(const AdaLNChain* const* chains, const double* t, float* con
   }
   const long long most = std::max(rows[0], rows[2]);
   const int nt = (int)std::max(1LL, std::min((long long)threads, most / 64));
-  StageBarrier bar(nt);
   // rows [g0, g1) of stage `stage`, numbered across the chains in order
   auto stage_rows = [&](int stage, long long g0, long long g1) {
     long long base = 0;
@@ -207,21 +179,10 @@ void adaln_run_many(const AdaLNChain* const* chains, const double* t, float* con
       base += n;
     }
   };
-  auto work = [&](int k) {
-    for (int stage = 0; stage < 3; ++stage) {
-      if (stage > 0) bar.wait();
+  for (int stage = 0; stage < 3; ++stage)
+    run_parts(nt, [&](int k) {
       stage_rows(stage, rows[stage] * k / nt, rows[stage] * (k + 1) / nt);
-    }
-  };
-  if (nt == 1) {
-    work(0);
-  } else {
-    std::vector<std::thread> pool;
-    pool.reserve((size_t)nt - 1);
-    for (int k = 1; k < nt; ++k) pool.emplace_back(work, k);
-    work(0);
-    for (auto& th : pool) th.join();
-  }
+    });
   for (int i = 0; i < count; ++i)
     if (embedded != nullptr && embedded[i] != nullptr)
       std::memcpy(embedded[i], w[(size_t)i].h2.data(), (size_t)w[(size_t)i].c->dim * 4);

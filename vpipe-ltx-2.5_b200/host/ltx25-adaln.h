@@ -29,8 +29,8 @@ void timestep_sinusoid(double t, int channels, float* out);
 void adaln_run(const AdaLNChain& c, double t, float* out, float* embedded, int threads);
 
 // `count` chains at once (a denoise step's chains, each at its own
-// timestep) on one set of host threads: each stage's rows over all chains
-// are split evenly, with one barrier per stage.  Every row is summed exactly
+// timestep): each stage's rows over all chains are split evenly over the
+// host threads, the stages one after another.  Every row is summed exactly
 // as adaln_run sums it, so the results are the same bits.  embedded (or any
 // of its entries) may be null.
 void adaln_run_many(const AdaLNChain* const* chains, const double* t, float* const* out,

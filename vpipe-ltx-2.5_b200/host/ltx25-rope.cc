@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/ltx25_cuda.h"
+#include "ltx25-threads.h"
 
 namespace {
 
@@ -105,17 +106,9 @@ int ltx_rope_table(const double* starts, const double* ends, int n_axes,
     }
   };
   const int nt = table_threads(tokens);
-  if (nt == 1) {
-    rows(0, tokens);
-    return LTX_OK;
-  }
-  std::vector<std::thread> pool;
-  pool.reserve((size_t)nt - 1);
-  for (int k = 1; k < nt; ++k)
-    pool.emplace_back(rows, (int)((long long)tokens * k / nt),
-                      (int)((long long)tokens * (k + 1) / nt));
-  rows(0, (int)((long long)tokens / nt));
-  for (auto& th : pool) th.join();
+  ltx25::run_parts(nt, [&](int k) {
+    rows((int)((long long)tokens * k / nt), (int)((long long)tokens * (k + 1) / nt));
+  });
   return LTX_OK;
 }
 
