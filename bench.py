@@ -834,7 +834,7 @@ def run_adaln(args):
                                "a2v / v2a scale-shift 4, gates 1; widths 4096 / 2048), "
                                "one noise level each; host code, no GPU",
                    "threads": threads, "weight_bytes": int(nbytes),
-                   "api": "ltx_adaln_run_many (one thread set for the step's chains)",
+                   "api": "ltx_adaln_run_many (rows over all of the step's chains split over the threads)",
                    "one_chain_at_a_time_ms": round(sec1 * 1e3, 3)},
         "gpu_launches": 0,
         "roofline": {"bound": "host memory", "achieved": round(gbs, 2), "peak": round(peak, 2),
