@@ -47,11 +47,13 @@ enum {
   LTX_E_SHAPE = -2,       /* sizes disagree with the weight or the layout */
   LTX_E_UNSUPPORTED = -3, /* a pack this build does not run (not w8g64) */
   LTX_E_CUDA = -4,        /* a CUDA runtime call or launch failed */
-  LTX_E_OOM = -5,         /* device allocation failed */
+  LTX_E_OOM = -5,         /* device (or host) allocation failed */
   LTX_E_KERNEL = -6,      /* a kernel gave up on a bounded wait */
   LTX_E_STATE = -7,       /* call out of order (e.g. block not loaded) */
   LTX_E_ALIGN = -8,       /* a pointer is not 16-byte aligned */
-  LTX_E_ABORTED = -9      /* a progress callback asked to stop */
+  LTX_E_ABORTED = -9,     /* a progress callback asked to stop */
+  LTX_E_HOST = -10        /* the library's host code failed (an exception caught
+                             at the boundary; no C++ exception leaves the ABI) */
 };
 
 /* Data types of a pack's scales / zero-points as they arrive. */

@@ -16,7 +16,7 @@ LTX_OK = 0
 ERRORS = {
     -1: "LTX_E_NULL", -2: "LTX_E_SHAPE", -3: "LTX_E_UNSUPPORTED",
     -4: "LTX_E_CUDA", -5: "LTX_E_OOM", -6: "LTX_E_KERNEL", -7: "LTX_E_STATE",
-    -8: "LTX_E_ALIGN", -9: "LTX_E_ABORTED",
+    -8: "LTX_E_ALIGN", -9: "LTX_E_ABORTED", -10: "LTX_E_HOST",
 }
 SB_F16, SB_BF16, SB_F32 = 0, 1, 2
 TP_ID_BYTES = 128
