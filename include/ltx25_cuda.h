@@ -91,6 +91,12 @@ LTX_API int ltx_abi_version(void);
  * more grows the arena outside any graph capture. */
 LTX_API int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k);
 
+/* Bytes of device scratch the context holds now (what ltx_ctx_reserve and
+ * on-demand growth allocated; weights and block arenas are not counted).
+ * A host-side read; no device work.  No counterpart in the reference (its
+ * arena is sized by the caller, src/ltx25-block-metal.h:140-163). */
+LTX_API int ltx_ctx_scratch_bytes(const ltx_ctx* ctx, unsigned long long* bytes);
+
 /* Reads and clears the device-side error word that a kernel sets when one
  * of its bounded waits gave up.  LTX_OK when clean, LTX_E_KERNEL when not
  * (the reference's wait_ok(), src/ltx25-dit.cc:1920-1931). */
@@ -244,6 +250,16 @@ LTX_API int ltx_output_head(ltx_ctx* ctx, const void* x, const float* shift_scal
  * weight instead of 5.  The crossover on B200 is LTX_DEQUANT_MIN_M rows. */
 #define LTX_DEQUANT_MIN_M 1536
 LTX_API int ltx_set_route(ltx_ctx* ctx, int route);
+
+/* A/B overrides of the GEMM tile plan, the counterpart of the reference's
+ * tile knob (src/ltx25-metal-ops.h:793-795, src/ltx25-metal-ops.cc:223-226,
+ * VPIPE_LTX25_MMA_TILE, read once at construction): force_pair 1/0
+ * forces CTA pairs (cta_group::2, 256 weight rows over two SMs) on or off,
+ * force_tn 128/256 the token tile, force_splits 1..8 the K split; -1 leaves
+ * each to the planner.  A forced value the shape cannot take is ignored.
+ * The context starts from LTX25_FORCE_PAIR / _TN / _SPLITS, read once when
+ * it is created. */
+LTX_API int ltx_set_tile_plan(ltx_ctx* ctx, int force_pair, int force_tn, int force_splits);
 
 /* ---- acceleration tiers ------------------------------------------------
  * Replaces MetalOps::set_i8_gemm / set_sage (src/ltx25-metal-ops.h:151,

@@ -2,10 +2,15 @@
 library's fixed device array, so that the call allocates nothing.
 
 Checked against the existing entry point (ltx_qlinear with the int8 tier on)
-on the same weights and inputs, at the tolerance the int8 tests use, over two
-calls in a row of different shapes -- the second smaller, so the rows the
-first call left in the shared array must not leak into it.  Collected last so
-that it also runs after every other test in the same process.
+on the same weights and inputs over two calls in a row of different shapes --
+the second smaller, so the rows the first call left in the shared array must
+not leak into it.  Both entry points run the same quantize kernel and the same
+kind::i8 GEMM on the same operands, so the outputs must be equal bit for bit
+(tighter than the int8 tests' 3e-3 rel-L2 bar).  The static calls run on a
+second context whose own int8 scratch was never reserved, and neither that
+context's scratch nor the device's free memory may change across them.
+Collected last so that it also runs after every other test in the same
+process.
 """
 import numpy as np
 import pytest
@@ -36,6 +41,8 @@ def test_static_scratch_matches_the_int8_tier_on_two_calls(ctx):
     import torch
     import ltx25_b200 as L
     cases = [(2048, 4096, 4096, 1), (1100, 4096, 2048, 2)]
+    # the weights live on the shared test context, which makes their int8
+    # copies; the static calls run on a fresh context of their own
     ws = [_weight(ctx, N, K, seed=10 + s) for (_, K, N, s) in cases]
     xs = [_x(M, K, seed=20 + s) for (M, K, _, s) in cases]
     bias = (torch.randn(4096, device="cuda") * 0.01).to(torch.bfloat16)
@@ -49,14 +56,31 @@ def test_static_scratch_matches_the_int8_tier_on_two_calls(ctx):
         torch.cuda.synchronize()
     finally:
         ctx.set_tiers(i8_gemm=False)
-    got = [L.qlinear_i8_static(ctx, w, x, bias=b).float() for w, x, b in zip(ws, xs, bs)]
-    torch.cuda.synchronize()
-    ctx.check()
-    for (M, K, N, _), g, r in zip(cases, got, refs):
+    outs = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+            for (M, _, N, _) in cases]
+    fresh = L.Context(0)
+    try:
+        # warm the entry point once (its first call on a device looks up the
+        # array's address), then watch the allocations across the two calls
+        L.qlinear_i8_static(fresh, ws[1], xs[1], bias=bs[1], out=outs[1])
+        torch.cuda.synchronize()
+        cap0 = fresh.scratch_bytes()
+        free0 = torch.cuda.mem_get_info()[0]
+        for w, x, b, o in zip(ws, xs, bs, outs):
+            L.qlinear_i8_static(fresh, w, x, bias=b, out=o)
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+        fresh.check()
+        assert fresh.scratch_bytes() == cap0 == 0, "the static path grew context scratch"
+        assert free1 == free0, f"device free memory moved by {free0 - free1} bytes"
+    finally:
+        fresh.close()
+    for (M, K, N, _), g, r in zip(cases, outs, refs):
+        g = g.float()
         rel = float(((g - r).norm() / r.norm()).item())
-        print((M, K, N), rel, bool(torch.equal(g, r)))
         assert torch.isfinite(g).all()
         assert rel < TOL, ((M, K, N), rel)
+        assert torch.equal(g, r), ((M, K, N), rel)
     for w in ws:
         w.free()
 

@@ -142,6 +142,15 @@ int ltx_ctx_reserve(ltx_ctx* ctx, int max_tokens, int max_n, int max_k)
   });
 }
 
+int ltx_ctx_scratch_bytes(const ltx_ctx* ctx, unsigned long long* bytes)
+{
+  return guarded([&]() -> int {
+    if (ctx == nullptr || bytes == nullptr) return LTX_E_NULL;
+    *bytes = (unsigned long long)ctx->ops.scratch_bytes();
+    return LTX_OK;
+  });
+}
+
 int ltx_ctx_check(ltx_ctx* ctx, void* stream)
 {
   return guarded([&]() -> int {
@@ -526,6 +535,22 @@ int ltx_set_route(ltx_ctx* ctx, int route)
     ctx->ops.set_route(route == LTX_ROUTE_FUSED ? ltx25::Route::Fused
                        : route == LTX_ROUTE_DEQUANT_ONCE ? ltx25::Route::DequantOnce
                                                          : ltx25::Route::Auto);
+    return LTX_OK;
+  });
+}
+
+int ltx_set_tile_plan(ltx_ctx* ctx, int force_pair, int force_tn, int force_splits)
+{
+  return guarded([&]() -> int {
+    if (ctx == nullptr) return LTX_E_NULL;
+    if (force_pair < -1 || force_pair > 1 || !(force_tn == -1 || force_tn == 128 || force_tn == 256) ||
+        force_splits < -1 || force_splits == 0 || force_splits > 8)
+      return fail(ctx, LTX_E_SHAPE, "set_tile_plan: pair -1/0/1, tn -1/128/256, splits -1 or 1..8");
+    ltx25::PlanKnobs k;
+    k.pair = force_pair;
+    k.tn = force_tn;
+    k.splits = force_splits;
+    ctx->ops.set_plan_knobs(k);
     return LTX_OK;
   });
 }

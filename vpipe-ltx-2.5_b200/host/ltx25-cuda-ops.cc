@@ -38,7 +38,7 @@ struct Plan {
 // text shapes (M <= 128 / small tile counts) split K until the grid covers
 // the SMs, because those shapes are bound by reading the weight, not by
 // the tensor pipe.
-Plan plan_gemm(int mode, int M, int N, int K, int sms)
+Plan plan_gemm(int mode, int M, int N, int K, int sms, const PlanKnobs& kn)
 {
   Plan p;
   const int kpb = mode == ltx::MODE_I8 ? 128 : 64;
@@ -51,14 +51,13 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
   // cross-CTA hand-off of dequantized A slots), so opt-in there.
   p.pair = mode == ltx::MODE_BF16 && M >= 1024 && N % 256 == 0 &&
            ((M + 255) / 256) * (N / 256) >= sms / 2;
-  if (const char* e = std::getenv("LTX25_FORCE_PAIR")) {
-    p.pair = (mode == ltx::MODE_W8G64 || mode == ltx::MODE_BF16) && std::atoi(e) != 0 &&
+  if (kn.pair >= 0) {
+    p.pair = (mode == ltx::MODE_W8G64 || mode == ltx::MODE_BF16) && kn.pair != 0 &&
              M > 128 && N % 256 == 0;
   }
   if (p.pair) p.tn = 256;
-  if (const char* e = std::getenv("LTX25_FORCE_TN")) {
-    const int tn = std::atoi(e);
-    if (!p.pair && (tn == 128 || tn == 256)) p.tn = tn;
+  if (kn.tn >= 0) {
+    if (!p.pair && (kn.tn == 128 || kn.tn == 256)) p.tn = kn.tn;
   }
   p.n_tiles = (N + (p.pair ? 255 : 127)) / (p.pair ? 256 : 128);
   p.m_tiles = (M + p.tn - 1) / p.tn;
@@ -75,8 +74,8 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms)
   }
   // A/B override of the K split (the reference's tile knobs,
   // src/ltx25-metal-ops.cc:164-231).  Ignored when out of range.
-  if (const char* e = std::getenv("LTX25_FORCE_SPLITS")) {
-    const int sp = std::atoi(e);
+  if (kn.splits >= 0) {
+    const int sp = kn.splits;
     if (!p.pair && sp >= 1 && sp <= 8 && sp <= p.kblocks && (sp == 1 || tiles * sp <= sms))
       p.splits = sp;
   }
@@ -112,7 +111,12 @@ CudaOps::~CudaOps()
 }
 
 bool CudaOps::init(int device, std::string* err)
-{
+{  // the tile plan's A/B overrides start from the environment, read here
+  // once (LTX25_FORCE_PAIR, LTX25_FORCE_TN, LTX25_FORCE_SPLITS)
+  if (const char* e = std::getenv("LTX25_FORCE_PAIR")) _knobs.pair = std::atoi(e) != 0 ? 1 : 0;
+  if (const char* e = std::getenv("LTX25_FORCE_TN")) _knobs.tn = std::atoi(e);
+  if (const char* e = std::getenv("LTX25_FORCE_SPLITS")) _knobs.splits = std::atoi(e);
+
   int n = 0;
   if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount", err)) return false;
   if (device < 0 || device >= n) {
@@ -160,6 +164,18 @@ bool CudaOps::ensure_(size_t i8_bytes, size_t deq_bytes, std::string* err)
     _deq_bytes = deq_bytes;
   }
   return true;
+}
+
+size_t CudaOps::scratch_bytes() const
+{
+  size_t b = 0;
+  if (_xq_bytes > 0) b += _xq_bytes + _xq_bytes / 64 * sizeof(float) + 1024;
+  b += _deq_bytes + _vt_elems * sizeof(__nv_bfloat16) + _part_elems * sizeof(float);
+  b += _sb.cap.qi8 + _sb.cap.ki8 + (_sb.cap.scales + _sb.cap.mean) * sizeof(float);
+  b += (size_t)_ones_n * sizeof(float) + _lora_r_elems * sizeof(__nv_bfloat16);
+  if (_tr_elems[0] > 0) b += _tr_elems[0] * 2 + 256;
+  if (_tr_elems[1] > 0) b += _tr_elems[1] * 2 + 256;
+  return b;
 }
 
 bool CudaOps::reserve(int max_tokens, int max_n, int max_k, std::string* err)
@@ -221,7 +237,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   // An extension adds ceil(r / 64) K blocks after the main K.
   const int ext_k = (ext != nullptr) ? ext->r : 0;
   const int ext_kb = (ext_k + 63) / 64;
-  const Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms);
+  const Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms, _knobs);
   ltx::GemmLaunch L;
   L.mode = mode;
   L.tn = pl.tn;

@@ -60,6 +60,13 @@ struct LoraPair {
 
 enum class Route { Fused = 0, DequantOnce = 1, Auto = 2 };
 
+// A/B overrides of the GEMM tile plan (the reference's tile knob,
+// src/ltx25-metal-ops.h:793-795): CTA pairs on/off, the token tile, the
+// K split.  -1 = the planner's own choice.
+struct PlanKnobs {
+  int pair = -1, tn = -1, splits = -1;
+};
+
 class CudaOps {
 public:
   ~CudaOps();
@@ -69,6 +76,8 @@ public:
 
   // Grow the shared scratch to cover calls up to these sizes.
   bool reserve(int max_tokens, int max_n, int max_k, std::string* err);
+  // Bytes of device scratch the context holds now (it grows on demand).
+  size_t scratch_bytes() const;
 
   // y[M][N] = x[M][K] . W^T (+ bias), epilogue per ltx::EpiMode.
   // `lora` (optional): a low-rank adapter on this linear, contracted in
@@ -105,6 +114,8 @@ public:
                 __nv_bfloat16* y, int ldy, int M, int K, int N, std::string* err);
 
   void set_route(Route r) { _route = r; }
+  void set_plan_knobs(const PlanKnobs& k) { _knobs = k; }
+  const PlanKnobs& plan_knobs() const { return _knobs; }
   Route route() const { return _route; }
 
   void set_i8_gemm(bool on) { _i8 = on; }
@@ -223,6 +234,7 @@ private:
   int _dev = -1;
   int _sms = 148;
   Route _route = Route::Auto;
+  PlanKnobs _knobs;
   bool _i8 = false;
   bool _sage = false;
   int _sage_dense = 0;

@@ -36,6 +36,7 @@ SIGNATURES = {
     "ltx_ctx_destroy": (None, [_P]),
     "ltx_ctx_last_error": (ctypes.c_char_p, [_P]),
     "ltx_ctx_reserve": (_I, [_P, _I, _I, _I]),
+    "ltx_ctx_scratch_bytes": (_I, [_P, ctypes.POINTER(ctypes.c_ulonglong)]),
     "ltx_ctx_check": (_I, [_P, _P]),
     "ltx_ctx_set_trace": (_I, [_P, _P, _I]),
     "ltx_ctx_selftest_timeout": (_I, [_P, _I, _P]),
@@ -91,6 +92,7 @@ SIGNATURES = {
     "ltx_ctx_set_sp": (_I, [_P, _I, _I, _P]),
     "ltx_tp_allreduce": (_I, [_P, _P, ctypes.c_size_t, _I, _P]),
     "ltx_set_route": (_I, [_P, _I]),
+    "ltx_set_tile_plan": (_I, [_P, _I, _I, _I]),
     "ltx_set_tiers": (_I, [_P, _I, _I, _I]),
     "ltx_i8_takes": (_I, [_P, _I, _I, _I]),
     "ltx_sage_takes": (_I, [_P, _I]),
@@ -208,6 +210,12 @@ class Context:
         self._ok(self.lib.ltx_ctx_reserve(self.h, max_tokens, max_n, max_k),
                  "reserve")
 
+    def scratch_bytes(self):
+        """ltx_ctx_scratch_bytes: device scratch the context holds now."""
+        n = ctypes.c_ulonglong(0)
+        self._ok(self.lib.ltx_ctx_scratch_bytes(self.h, ctypes.byref(n)), "scratch_bytes")
+        return int(n.value)
+
     def check(self, stream=None):
         self._ok(self.lib.ltx_ctx_check(self.h, _stream(stream)), "check")
 
@@ -219,6 +227,11 @@ class Context:
 
     def set_route(self, route):
         self._ok(self.lib.ltx_set_route(self.h, route), "set_route")
+
+    def set_tile_plan(self, pair=-1, tn=-1, splits=-1):
+        """ltx_set_tile_plan: force CTA pairs / token tile / K split (-1 = the
+        planner's choice)."""
+        self._ok(self.lib.ltx_set_tile_plan(self.h, pair, tn, splits), "set_tile_plan")
 
     def set_tiers(self, i8_gemm=False, sage_attn=False, sage_dense_layers=0):
         self._ok(self.lib.ltx_set_tiers(self.h, int(i8_gemm), int(sage_attn),
