@@ -1,37 +1,37 @@
 #!/usr/bin/env python
-"""bench.py -- the w8g64 qlinear sweep of BASELINE config 2 on B200.
+"""bench.py -- LTX-2.5's w8g64 qlinear and the joint AV DiT on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload stack|sweep|qlinear|i8|block|...]
 
-A step is one pass of the DiT linear-shape sweep:
-nine w8g64 quantized linears at the shapes one LTX-2.5 block dispatches at
-960x544x121 -- video stream M=8160 (4096->4096 attention out, 4096->12288
-fused QKV, 4096->16384 FFN-up, 16384->4096 FFN-down), audio stream M=126
-(2048->2048, 2048->8192, 8192->2048), audio<->video cross projections
-(2048->4096, 4096->2048 at M=8160) -- each through the library's C ABI
-(ltx_qlinear).  Weights are N(0, 0.02) packed by the library's own w8g64
-quantizer (bit-identical to the reference packer), activations N(0, 1) bf16,
-all seeded.
+The default line is BASELINE config 5, the metric's "DiT s/denoise-step
+@960x544x121": a step is one forward of the 48-block joint audio-video stack
+over 8160 video + 126 audio + 256 text tokens, random-init w8g64 weights
+(seeded, generated and packed on the device), bf16 activations.  Under
+torchrun the stack is tensor parallel over the N ranks (column-split q/k/v
+and FF-up, row-split out-projections and FF-down, NCCL over NVLink): strong
+scaling, the same step at every N, time = max over ranks.
 
-value   whole-job TFLOP/s (algorithmic 2*M*N*K), inputs resident in HBM.
-e2e     the same through the C ABI with HOST buffers: each step copies every
-        activation in from pinned host memory and every output back out.
-roofline  tensor-bound: the w8g64 GEMM over the six M=8160 shapes, achieved
-        = their algorithmic FLOPs / their CUDA-event time inside the timed
-        region, against MEASURED_PEAKS.json bf16_tflops.  roofline_hbm: the
-        three M=126 audio shapes, algorithmic bytes (N*K codes + 4*N*K/64
-        scale/zero-point bytes + 2*M*(K+N) activations) / time, against
-        MEASURED_PEAKS.json hbm_gbs.
-cpu_baseline  the reference's own CPU dequantise-then-dense linear_
-        (oracle/_ref, compiled from the reference sources) on a bounded
-        sample, 1 core, rank 0 at N=1.
+value     s/step, inputs resident in HBM (weights ~21 GB / N stream every step).
+e2e       the same through the C ABI (ltx_stack_forward) with the stream
+          activations copied in from and out to pinned host memory each step.
+roofline  algorithmic FLOPs of the step (GEMMs 2*M*N*K + attention 4*tq*tk*d)
+          per GPU / time, against MEASURED_PEAKS.json: the sustained bf16 peak
+          for a timed region of a second or more, else the burst one; both
+          fractions are printed.
+sweep     BASELINE config 2, the w8g64 linear-shape sweep (nine shapes, each
+          through ltx_qlinear), measured on the same contexts after the stack:
+          roofline_sweep (tensor, the six M=8160 shapes) and roofline_hbm (HBM,
+          the three M=126 audio shapes) ride on the line.
+cpu_baseline  the reference's own CPU block_forward (oracle/_ref, compiled
+          from the reference sources) on a bounded full-width sample on all
+          host cores, extrapolated to the step by FLOPs; rank 0 at N=1.
 
---impl reference  times that reference CPU path alone on all host cores
-        (the reference has no GPU path that runs here: it is Apple Metal).
-
-Multi-GPU: one process per GPU, each running the sweep on its own copy of
-the workload (weak scaling, no data-path collective); the time is the max
-over ranks.
+--impl reference  that reference CPU path alone, same metric and config
+        (the reference's GPU path is Apple Metal, unavailable here).
+Other workloads (--workload): sweep (config 2 alone, N replicas), qlinear
+(config 1), i8 (config 3), block (config 4), attn, lora, trunk, connector,
+adaln.
 """
 import argparse
 import json
@@ -82,20 +82,41 @@ def peaks():
         return 1590.0, 6650.0, "fallback"
 
 
-def tensor_peak_for(clocks):
-    """Burst or sustained bf16 peak from MEASURED_PEAKS.json, by the clocks the
-    timed region ran at: below 85 % of the maximum SM clock the run was in the
-    power-capped regime the sustained figure was measured in."""
+# A timed region at least this long is a seconds-long loop under the power
+# cap, the regime MEASURED_PEAKS.json's sustained figure was measured in;
+# shorter regions are bursts.  Chosen by the region's length, never by a
+# clock sample, so the choice cannot flip on one nvidia-smi reading.
+SUSTAINED_REGION_S = 1.0
+
+
+def tensor_peak_for(region_s, clocks=None):
+    """The bf16 tensor peak for a timed region of `region_s` seconds.
+    Returns a dict: peak (the one the fraction uses), kind, burst, sustained
+    (both MEASURED_PEAKS.json figures, so either fraction can be read)."""
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
         burst, sus = float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"])
+        src = "measured"
     except Exception:
-        return 1590.0, "fallback (burst)"
-    mhz, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
-    if mhz is not None and mx and mhz < 0.85 * mx:
-        return sus, "measured bf16_tflops_sustained (median SM clock %.0f of %.0f MHz)" % (mhz, mx)
-    return burst, "measured bf16_tflops (burst)"
+        burst, sus, src = 1590.0, 1400.0, "fallback"
+    if region_s >= SUSTAINED_REGION_S:
+        peak, kind = sus, f"{src} bf16_tflops_sustained (timed region {region_s:.2f} s >= " \
+                          f"{SUSTAINED_REGION_S:.0f} s)"
+    else:
+        peak, kind = burst, f"{src} bf16_tflops (burst; timed region {region_s * 1e3:.0f} ms)"
+    return {"peak": peak, "kind": kind, "burst": burst, "sustained": sus}
+
+
+def roofline_fracs(achieved, pk, clocks):
+    """Both fractions and the clock-normalized rate (TFLOP/s per GHz of the
+    median SM clock) so the clock dependence can be read off the line."""
+    out = {"frac_of_burst": round(achieved / pk["burst"], 4),
+           "frac_of_sustained": round(achieved / pk["sustained"], 4)}
+    mhz = (clocks or {}).get("sm_mhz")
+    if mhz:
+        out["tflops_per_ghz"] = round(achieved / (mhz / 1e3), 1)
+    return out
 
 
 def traffic_from_profile():
@@ -192,6 +213,12 @@ def dist_setup():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return world, rank, local
+
+
+def gpu_index(local):
+    """The nvidia-smi index of this rank's GPU (CUDA_VISIBLE_DEVICES aware)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return vis.split(",")[local] if vis else str(local)
 
 
 def make_weights(L, ctx, torch, dev, K, N, gen):
@@ -318,15 +345,13 @@ def run_stack(args):
         st.forward(v, a)
     torch.cuda.synchronize()
     ctx.check()
-    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     if pg is not None:
         pg.barrier()
     torch.cuda.synchronize()
     n0 = L.launch_count()
-    with ClockSampler(gpu_id) as clk:
+    with ClockSampler(gpu_index(local)) as clk:
         for e0, e1 in evs:
             # x is reset outside the timed pair; weights (>19 GB / N) and the
             # activations stream through HBM every step, far above L2
@@ -336,11 +361,13 @@ def run_stack(args):
             st.forward(v, a, stream=stream)
             e1.record(stream)
         torch.cuda.synchronize()
-    launches = (L.launch_count() - n0) // max(args.steps, 1)
+    launches = L.launch_count() - n0
     if pg is not None:
         pg.barrier()
     ctx.check()
-    ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in evs])
+    times = [e0.elapsed_time(e1) for e0, e1 in evs]
+    ms = sum(times) / len(times)          # the K timed steps, x resets excluded
+    region_s = sum(times) * 1e-3
     if pg is not None:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -374,47 +401,63 @@ def run_stack(args):
         e2e_ms = float(t.item())
     ctx.check()
 
-    peak_tf, _, peak_kind = peaks()
-    try:
-        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-            peak_tf = float(json.load(f)["bf16_tflops_sustained"])
-            peak_kind = "measured (sustained)"
-    except Exception:
-        pass
     g, at_fl = block_flops(vt, at, tt, vdim, adim)
     step_flops = nblk * (g + at_fl)
     achieved = step_flops / (ms * 1e-3) / 1e12
     io_bytes = (vt * vdim + at * adim) * 2
+    clocks = clk.summary()
+    pk = tensor_peak_for(region_s)
+    per_gpu = achieved / world
     line = {
         "metric": "DiT s/denoise-step @960x544x121 (BASELINE config 5, 48-block stack)",
         "value": round(ms / 1e3, 4), "unit": "s/step", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded device-generated weights, w8g64)",
-        "config": {"workload": f"{nblk}-block joint AV stack: video 8160x4096 (16x17x30), "
-                               "audio 126x2048, text 256; weights and activations far "
-                               "above L2 every step",
-                   "parallelism": f"{args.parallel}{world}"},
+        "config": {"workload": f"{nblk}-block joint AV stack, one denoise step: video 8160x4096 "
+                               "(16x17x30), audio 126x2048, text 256",
+                   "parallelism": f"{args.parallel}{world}",
+                   "l2": "weights (~21 GB / N) and activations far above L2 every step"},
         "e2e": {"value": round(e2e_ms / 1e3, 4), "unit": "s/step",
-                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
+                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
+                "api": "ltx_stack_forward, x copied in from and out to pinned host memory"},
         "gpu_launches": int(launches),
         "algorithmic_tflop": round(step_flops / 1e12, 2),
         "tflops": round(achieved, 1),
-        "roofline": {"bound": "tensor", "achieved": round(achieved / world, 1),
-                     "peak": peak_tf, "peak_kind": peak_kind, "unit": "TFLOP/s per GPU",
-                     "frac": round(achieved / world / peak_tf, 3), "traffic": None},
-        "finite": ok, "clocks": clk.summary(),
+        "roofline": dict({"bound": "tensor", "achieved": round(per_gpu, 1),
+                          "peak": pk["peak"], "peak_source": pk["kind"],
+                          "unit": "TFLOP/s per GPU", "frac": round(per_gpu / pk["peak"], 4),
+                          "traffic": None},
+                         **roofline_fracs(per_gpu, pk, clocks)),
+        "finite": ok, "clocks": clocks,
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     st.close()
     for b in st.blocks:
         b.close()
+    if not args.no_sweep:
+        # BASELINE config 2 on the same contexts after the stack is freed
+        # (replicas under torchrun), so the qlinear evidence rides the line
+        sw = measure_sweep(args_for_sweep(args), ctx, dev, rank, world, pg, local)
+        line["sweep"] = sw
+        line["roofline_sweep"] = sw["roofline"]
+        line["roofline_hbm"] = sw["roofline_hbm"]
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = ref_block_baseline(blocks=nblk)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     ctx.close()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+def args_for_sweep(args):
+    """The sweep's own step count (its steps are ~3 ms, the stack's ~300)."""
+    import copy
+    a = copy.copy(args)
+    a.steps = max(args.steps, 20)
+    return a
 
 
 def run_attn(args):
@@ -556,7 +599,8 @@ def run_lora(args):
     fl = sum(2.0 * M * K * N + 2.0 * M * r * (K + N) for _, M, K, N, r in shapes)
     tf = fl / (total["fused"] * 1e-3) / 1e12
     clocks = clk.summary()
-    tpeak, tpeak_kind = tensor_peak_for(clocks)
+    pk = tensor_peak_for(total["fused"] * 1e-3)
+    tpeak, tpeak_kind = pk["peak"], pk["kind"]
     line = {
         "metric": "adapted w8g64 qlinear TFLOP/s (linear + rank-r adapter), reference LoRA shapes",
         "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
@@ -701,7 +745,8 @@ def run_i8(args):
     ops = 2.0 * M * N * K
     tops = ops / (ms * 1e-3) / 1e12
     clocks = clk.summary()
-    bf16_peak, bf16_kind = tensor_peak_for(clocks)
+    pk = tensor_peak_for(ms * steps * 1e-3)
+    bf16_peak, bf16_kind = pk["peak"], pk["kind"]
     peak = 2.0 * bf16_peak
     line = {
         "metric": "i8_gemm tier qlinear TOP/s (BASELINE config 3)",
@@ -915,6 +960,93 @@ def run_connector(args):
     return 0
 
 
+# ------------------------------------------------------ reference CPU block
+# The reference's own block_forward (src/ltx25-block-ref.cc:308-389, compiled
+# into oracle/_ref) on a bounded sample at the real widths: one random-init
+# block (video 4096 x 32 heads, audio 2048 x 32 heads), 8 video tokens (a
+# 2x2x2 grid), 4 audio, 8 text.  Its rate in algorithmic FLOP/s extrapolates
+# to the full geometry by FLOPs.
+REF_SAMPLE = {"vt": 8, "grid": (2, 2, 2), "at": 4, "tt": 8}
+_REF_BLOCK = {}
+
+
+def ref_block_setup():
+    if _REF_BLOCK:
+        return _REF_BLOCK
+    from oracle import block_np
+    from oracle import ref as oref
+    t0 = time.perf_counter()
+    kind = "reference" if oref.available() else "port"
+    tensors = block_np.random_block_tensors(4096, 32, 2048, 32, seed=3, f32_draws=True)
+    cfg = dict(vdim=4096, vheads=32, adim=2048, aheads=32, vt=REF_SAMPLE["vt"],
+               at=REF_SAMPLE["at"], tt=REF_SAMPLE["tt"])
+    inp = block_np.random_block_inputs(cfg, seed=4, video_grid=REF_SAMPLE["grid"])
+    if kind == "reference":
+        blk = oref.RefBlock(tensors, 4096, 32, 2048, 32)
+        del tensors
+
+        def fwd():
+            blk.forward(inp["video"], inp["audio"])
+        _REF_BLOCK["blk"] = blk
+    else:
+        def fwd():
+            block_np.block_forward(tensors, inp["video"], inp["audio"], 4096, 32, 2048, 32)
+    g, a = block_flops(REF_SAMPLE["vt"], REF_SAMPLE["at"], REF_SAMPLE["tt"], 4096, 2048)
+    _REF_BLOCK.update(fwd=fwd, kind=kind, sample_flops=g + a,
+                      setup_s=time.perf_counter() - t0)
+    return _REF_BLOCK
+
+
+def ref_block_round(threads):
+    """`threads` concurrent block_forward calls on the sample (ctypes drops
+    the GIL, so they run on as many cores).  Returns (FLOPs, seconds)."""
+    import concurrent.futures as cf
+    r = ref_block_setup()
+    t0 = time.perf_counter()
+    if threads <= 1:
+        r["fwd"]()
+    else:
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            for f in [ex.submit(r["fwd"]) for _ in range(threads)]:
+                f.result()
+    return threads * r["sample_flops"], time.perf_counter() - t0
+
+
+def ref_block_desc(threads):
+    s = REF_SAMPLE
+    return (f"{threads} concurrent block_forward calls (src/ltx25-block-ref.cc:308-389, "
+            f"f32 with f64 dot products) per round, each one random-init block at the real "
+            f"widths (video 4096x32 heads, audio 2048x32) on {s['vt']} video tokens "
+            f"({s['grid'][0]}x{s['grid'][1]}x{s['grid'][2]}), {s['at']} audio, {s['tt']} "
+            f"text; extrapolated to 8160/126/256 tokens by algorithmic FLOPs")
+
+
+def full_block_flops():
+    g, a = block_flops(8160, 126, 256, 4096, 2048)
+    return g + a
+
+
+def ref_block_baseline(blocks, rounds=2):
+    """cpu_baseline of the block and stack lines: the reference block on all
+    host cores, one warm-up round then `rounds` timed; returns the dict."""
+    threads = os.cpu_count() or 1
+    ref_block_round(threads)
+    fl = sec = 0.0
+    for _ in range(rounds):
+        f, t = ref_block_round(threads)
+        fl += f
+        sec += t
+    rate = fl / sec
+    per_block = full_block_flops() / rate
+    r = _REF_BLOCK
+    return {"value": round(per_block * blocks, 2) if blocks > 1 else round(per_block * 1e3, 1),
+            "unit": "s/step" if blocks > 1 else "ms", "cores": threads, "kind": r["kind"],
+            "sample": ref_block_desc(threads),
+            "gflops": round(rate / 1e9, 2), "seconds": round(sec, 2),
+            "setup_s": round(r["setup_s"], 1)}
+
+
+# ------------------------------------------------------------------ block
 def run_block(args):
     """one joint AV block, 8160 video + 126 audio + 256
     text tokens at the real widths, synthetic w8g64 weights."""
@@ -937,138 +1069,90 @@ def run_block(args):
     v = synth.random_stream_inputs(vdim, vt, tt, vh, gen, pe=dt(v_self), cross_pe=dt(v_cross))
     a = synth.random_stream_inputs(adim, at, tt, ah, gen, pe=dt(a_self), cross_pe=dt(a_cross))
     x0v, x0a = v["x"].clone(), a["x"].clone()
+    stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         blk.forward(v, a)
     torch.cuda.synchronize()
     ctx.check()
-    times = []
-    for _ in range(args.steps):
-        v["x"].copy_(x0v)
-        a["x"].copy_(x0a)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        blk.forward(v, a)
-        e1.record()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    n0 = L.launch_count()
+    with ClockSampler(gpu_index(local)) as clk:
+        for e0, e1 in evs:
+            # x is reset outside the timed pair; the block's weights (0.44 GB)
+            # and activations stream far above L2 every step
+            v["x"].copy_(x0v)
+            a["x"].copy_(x0a)
+            e0.record(stream)
+            blk.forward(v, a, stream=stream)
+            e1.record(stream)
         torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
+    launches = L.launch_count() - n0
     ctx.check()
+    times = [e0.elapsed_time(e1) for e0, e1 in evs]
     ms = statistics.median(times)
+    region_s = sum(times) * 1e-3
+
+    # end to end through the public API: host x in, host x out, every step
+    hv, ha = x0v.cpu().pin_memory(), x0a.cpu().pin_memory()
+    ov, oa = torch.empty_like(hv).pin_memory(), torch.empty_like(ha).pin_memory()
+    e2e_steps = max(1, min(args.steps, 20))
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        v["x"].copy_(hv, non_blocking=True)
+        a["x"].copy_(ha, non_blocking=True)
+        blk.forward(v, a, stream=stream)
+        ov.copy_(v["x"], non_blocking=True)
+        oa.copy_(a["x"], non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / e2e_steps
+    ctx.check()
+    io_bytes = (vt * vdim + at * adim) * 2
+
     gemm_flops, attn_flops = block_flops(vt, at, tt, vdim, adim)
+    achieved = (gemm_flops + attn_flops) / (ms * 1e-3) / 1e12
+    clocks = clk.summary()
+    pk = tensor_peak_for(region_s)
     line = {
         "metric": "DiT joint AV block forward ms @960x544x121 (BASELINE config 4)",
         "value": round(ms, 3), "unit": "ms", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": False,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
+        "scaling": "none", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded device-generated weights, w8g64)",
         "config": {"workload": "one block: video 8160x4096 (16x17x30), audio 126x2048, "
-                               "text 256, 3-axis video RoPE, 1-D audio RoPE"},
+                               "text 256, 3-axis video RoPE, 1-D audio RoPE",
+                   "l2": "weights 0.44 GB and activations above L2 every step"},
+        "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": io_bytes,
+                "d2h_bytes_per_step": io_bytes,
+                "api": "ltx_block_forward, x copied in from and out to pinned host memory"},
+        "gpu_launches": int(launches),
         "algorithmic_tflop": round((gemm_flops + attn_flops) / 1e12, 3),
-        "tflops": round((gemm_flops + attn_flops) / (ms * 1e-3) / 1e12, 1),
         "gemm_tflop": round(gemm_flops / 1e12, 3), "attention_tflop": round(attn_flops / 1e12, 3),
+        "roofline": dict({"bound": "tensor", "achieved": round(achieved, 1),
+                          "peak": pk["peak"], "peak_source": pk["kind"], "unit": "TFLOP/s",
+                          "frac": round(achieved / pk["peak"], 4), "traffic": None},
+                         **roofline_fracs(achieved, pk, clocks)),
+        "clocks": clocks,
     }
-    print(json.dumps(line), flush=True)
     blk.close()
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = ref_block_baseline(blocks=1)
+    print(json.dumps(line), flush=True)
     ctx.close()
     return 0
 
 
-def run_reference(args):
-    world, rank, _ = dist_setup()
-    if rank != 0:
-        return 0
-    threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        cpu_reference_sample(threads)
-    fl = 0.0
-    sec = 0.0
-    kind = "port"
-    for _ in range(args.steps):
-        f, s, kind = cpu_reference_sample(threads)
-        fl += f
-        sec += s
-    value = fl / sec / 1e12
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32/f64-accumulate",
-        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
-        "config": {"workload": "BASELINE config 2 sweep, bounded CPU sample",
-                   "sample": sample_desc()},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
-                         "kind": kind, "sample": sample_desc()},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-        "note": "the reference's GPU path is Apple Metal (unavailable on this "
-                "box); this arm is its CPU dequantise-then-dense qlinear",
-    }
-    print(json.dumps(line), flush=True)
-    return 0
-
-
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=20)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", type=int, default=None,
-                    help="profile one sweep shape (index into SHAPES)")
-    ap.add_argument("--blocks", type=int, default=48, help="stack depth (--workload stack)")
-    ap.add_argument("--parallel", default="tp", choices=["tp", "sp"],
-                    help="stack under torchrun: tensor parallel (BASELINE config 5) or "
-                         "sequence/head parallel")
-    ap.add_argument("--sage", action="store_true", help="sage_attn tier (--workload attn)")
-    ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
-                    help="qlinear route for quantized weights (sweep)")
-    ap.add_argument("--workload", default="sweep",
-                    choices=["sweep", "block", "stack", "attn", "lora", "trunk", "connector",
-                             "adaln", "i8"],
-                    help="sweep: BASELINE config 2 (the headline); block: one "
-                         "joint AV block at 960x544x121 (config 4)")
-    args = ap.parse_args()
-    if args.workload == "block" and args.impl == "ours":
-        return run_block(args)
-    if args.workload == "attn" and args.impl == "ours":
-        args.warmup = max(args.warmup, 3)
-        return run_attn(args)
-    if args.workload == "connector" and args.impl == "ours":
-        return run_connector(args)
-    if args.workload == "trunk" and args.impl == "ours":
-        return run_trunk(args)
-    if args.workload == "adaln" and args.impl == "ours":
-        return run_adaln(args)
-    if args.workload == "i8" and args.impl == "ours":
-        return run_i8(args)
-    if args.workload == "lora" and args.impl == "ours":
-        args.warmup = max(args.warmup, 3)
-        return run_lora(args)
-    if args.workload == "stack" and args.impl == "ours":
-        args.warmup = max(args.warmup, 3)
-        return run_stack(args)
-    if args.only is not None:
-        SHAPES[:] = [SHAPES[args.only]]
-    args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
-        return run_reference(args)
-
+# ------------------------------------------------------------------ sweep
+def measure_sweep(args, ctx, dev, rank, world, pg, local):
+    """BASELINE config 2 on one context: every shape of SHAPES through
+    ltx_qlinear, K timed steps (inputs resident), then the end-to-end leg
+    through host buffers.  Returns the sweep's figures as a dict."""
     import torch
     import ltx25_b200 as L
-
-    world, rank, local = dist_setup()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-        pg = dist
-
-    ctx = L.Context(local)
     route = {"auto": L.ROUTE_AUTO, "fused": L.ROUTE_FUSED,
              "dequant": L.ROUTE_DEQUANT_ONCE}[args.route]
     ctx.set_route(route)
@@ -1097,7 +1181,6 @@ def main():
     torch.cuda.synchronize()
     ctx.check()
 
-    # ---------------------------------------------------------- timed region
     evs = [[[torch.cuda.Event(enable_timing=True),
              torch.cuda.Event(enable_timing=True)] for _ in SHAPES]
            for _ in range(args.steps)]
@@ -1106,10 +1189,8 @@ def main():
     if pg is not None:
         pg.barrier()
     torch.cuda.synchronize()
-    gpu_id = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local)
     n_launch0 = L.launch_count()
-    with ClockSampler(gpu_id) as clk:
+    with ClockSampler(gpu_index(local)) as clk:
         t_start.record(stream)
         for s in range(args.steps):
             step(evs[s])
@@ -1128,24 +1209,22 @@ def main():
         t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms_total = float(t.item())
-
     step_flops = sum(flops(M, K, N) for _, M, K, N in SHAPES)
     ms_per_step = ms_total / args.steps
     value = world * step_flops / (ms_per_step * 1e-3) / 1e12
 
-    # ------------------------------------------------------------- e2e leg
+    # end to end: each step uploads every shape's input and downloads every
+    # result; the uploads run on one copy stream and the downloads on
+    # another, each shape's GEMM waits only for its own input, and the device
+    # buffers are double-buffered across steps, so PCIe in, PCIe out and the
+    # GEMMs overlap (a serving loop's pipelining) while every byte still
+    # crosses per step.
     xh = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs]
     yh = [torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for y in ys]
     for a, b in zip(xh, xs):
         a.copy_(b)
     h2d = sum(x.numel() * 2 for x in xs)
     d2h = sum(y.numel() * 2 for y in ys)
-
-    # Each step uploads every shape's input and downloads every result; the
-    # uploads run on one copy stream and the downloads on another, each
-    # shape's GEMM waits only for its own input, and the device buffers are
-    # double-buffered across steps, so PCIe in, PCIe out and the GEMMs overlap
-    # (a serving loop's pipelining) while every byte still crosses per step.
     copy_in = torch.cuda.Stream(dev)
     copy_out = torch.cuda.Stream(dev)
     xs2 = [xs, [torch.empty_like(x) for x in xs]]
@@ -1199,8 +1278,7 @@ def main():
     ctx.check()
     e2e_value = world * step_flops / (e2e_ms * 1e-3) / 1e12
 
-    # ------------------------------------------------------------- rooflines
-    bf16_peak, hbm_peak, peak_kind = peaks()
+    _, hbm_peak, _ = peaks()
     vid = [i for i, s in enumerate(SHAPES) if s[1] > 1024]
     aud = [i for i, s in enumerate(SHAPES) if s[1] <= 1024]
     vid_fl = sum(flops(*SHAPES[i][1:]) for i in vid) * args.steps
@@ -1210,7 +1288,6 @@ def main():
     achieved = vid_fl / vid_s / 1e12 if vid_s > 0 else 0.0
     achieved_hbm = aud_b / aud_s / 1e9 if aud_s > 0 else 0.0
     prof = traffic_from_profile() or {}
-
     per_shape = []
     for i, (name, M, K, N) in enumerate(SHAPES):
         t = per_shape_ms[i] / args.steps * 1e-3
@@ -1218,30 +1295,15 @@ def main():
                           "us": round(t * 1e6, 2),
                           "tflops": round(flops(M, K, N) / t / 1e12, 1),
                           "gbs": round(hbm_bytes(M, K, N) / t / 1e9, 1)})
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        f, s, kind = cpu_reference_sample(1)
-        cpu = {"value": f / s / 1e12, "unit": UNIT, "cores": 1, "kind": kind,
-               "sample": sample_desc(), "seconds": round(s, 2)}
-
     clocks = clk.summary()
-    tpeak, tpeak_kind = tensor_peak_for(clocks)
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT,
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) bf16 activations; N(0,0.02) weights "
-                "w8g64-packed on device, bit-identical to the reference packer)",
-        "config": {
-            "workload": "BASELINE config 2: DiT linear-shape sweep, all w8g64",
-            "shapes": [f"{n}: M={M} K={K} N={N}" for n, M, K, N in SHAPES],
-            "l2": "inputs larger than L2: the sweep's operands total ~1.5 GB "
-                  "and each shape's are evicted by the others between repeats",
-            "parallelism": f"replicas x{world} (no data-path collective)",
-            "route": args.route,
-        },
+    pk = tensor_peak_for(ms_total * 1e-3)
+    out = {
+        "value": round(value, 2), "unit": UNIT, "ms_per_step": round(ms_per_step, 4),
+        "steps": args.steps,
+        "shapes": [f"{n}: M={M} K={K} N={N}" for n, M, K, N in SHAPES],
+        "route": args.route,
+        "l2": "inputs larger than L2: the sweep's operands total ~1.5 GB and each shape's "
+              "are evicted by the others between repeats",
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3),
@@ -1250,37 +1312,377 @@ def main():
                        "buffered across steps"},
         "gpu_launches": int(launches),
         "clocks": clocks,
-        "roofline": {
+        "roofline": dict({
             "bound": "tensor", "achieved": round(achieved, 1),
-            "peak": tpeak, "unit": "TFLOP/s",
-            "frac": round(achieved / tpeak, 4),
-            "frac_of_burst": round(achieved / bf16_peak, 4),
-            "peak_source": tpeak_kind,
+            "peak": pk["peak"], "unit": "TFLOP/s",
+            "frac": round(achieved / pk["peak"], 4), "peak_source": pk["kind"],
             "kernel": ("dequant_w8_kernel + gemm_tc_kernel<MODE_BF16,TN=256> (route auto: "
                        "M >= %d expands the weight once per call, src/ltx25-metal-ops.cc:"
                        "468-545) over the 6 M=8160 shapes; time covers both" % L.DEQUANT_MIN_M)
                       if args.route != "fused" else
                       "gemm_tc_kernel<MODE_W8G64,TN=256> over the 6 M=8160 shapes",
-            "traffic": prof.get("video_bytes_per_launch_" + args.route),
-        },
+            "traffic": prof.get("video_bytes_per_launch_" + args.route)},
+            **roofline_fracs(achieved, pk, clocks)),
         "roofline_hbm": {
             "bound": "hbm", "achieved": round(achieved_hbm, 1),
             "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved_hbm / hbm_peak, 4),
-            "kernel": "gemm_tc_kernel<MODE_W8G64,TN=128> split-K, 3 M=126 shapes",
-            "traffic": prof.get("audio_bytes_per_launch"),
-        },
+            "kernel": "the small-M w8g64 path over the 3 M=126 shapes",
+            "traffic": prof.get("audio_bytes_per_launch")},
         "per_shape": per_shape,
-        "cpu_baseline": cpu,
+    }
+    for w in weights:
+        w.free()
+    del xs, ys, xs2, ys2, xh, yh
+    torch.cuda.synchronize()
+    return out
+
+
+def run_sweep(args):
+    """BASELINE config 2 as its own line (--workload sweep): N replicas."""
+    import torch
+    import ltx25_b200 as L
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+    ctx = L.Context(local)
+    sw = measure_sweep(args, ctx, dev, rank, world, pg, local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        f, s, kind = cpu_reference_sample(1)
+        cpu = {"value": f / s / 1e12, "unit": UNIT, "cores": 1, "kind": kind,
+               "sample": sample_desc(), "seconds": round(s, 2)}
+    line = {
+        "metric": METRIC, "value": sw["value"], "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sw["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 activations; N(0,0.02) weights "
+                "w8g64-packed on device, bit-identical to the reference packer)",
+        "config": {"workload": "BASELINE config 2: DiT linear-shape sweep, all w8g64",
+                   "shapes": sw["shapes"], "l2": sw["l2"],
+                   "parallelism": f"replicas x{world} (no data-path collective)",
+                   "route": args.route},
+        "e2e": sw["e2e"], "gpu_launches": sw["gpu_launches"], "clocks": sw["clocks"],
+        "roofline": sw["roofline"], "roofline_hbm": sw["roofline_hbm"],
+        "per_shape": sw["per_shape"], "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    for w in weights:
-        w.free()
     ctx.close()
     if pg is not None:
         pg.destroy_process_group()
     return 0
+
+
+# ------------------------------------------------------- config 1 qlinear
+Q1 = (1024, 4096, 4096)          # BASELINE config 1: M, K, N
+Q1_CPU_ROWS = 512                # cpu sample: the first 512 tokens, all N, full K
+L2_FLUSH_BYTES = 256 << 20       # > the 126 MB L2
+
+
+def run_qlinear(args):
+    """one w8g64 qlinear, X [1024][4096] ~ N(0, 1) bf16,
+    W [4096][4096] ~ N(0, 0.02) packed w8g64, bias [4096] ~ N(0, 0.01), bf16
+    out, through ltx_qlinear.  Its operands (34.6 MB) fit in L2, so a 256 MB
+    buffer is written between timed iterations (outside each event pair) and
+    every iteration starts from DRAM."""
+    import torch
+    import ltx25_b200 as L
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = L.Context(local)
+    M, K, N = Q1
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+    w32 = torch.randn((N, K), generator=gen, device=dev) * 0.02
+    bias = (torch.randn((N,), generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+    codes, scales, zps = L.pack_w8g64(ctx, w32)
+    qw = L.QWeight.upload(ctx, codes, scales, zps, N, K, on_device=True)
+    y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    ctx.reserve(M, N, K)
+    for _ in range(args.warmup):
+        flush.zero_()
+        L.qlinear(ctx, qw, x, bias=bias, out=y, stream=stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    n0 = L.launch_count()
+    with ClockSampler(gpu_index(local)) as clk:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            L.qlinear(ctx, qw, x, bias=bias, out=y, stream=stream)
+            e1.record(stream)
+        torch.cuda.synchronize()
+    launches = L.launch_count() - n0
+    ctx.check()
+    times = [e0.elapsed_time(e1) for e0, e1 in evs]
+    ms = sum(times) / len(times)
+    fl = flops(M, K, N)
+    byts = N * K + 4.0 * N * K / 64 + 2.0 * M * K + 2.0 * M * N + 2.0 * N
+    tf = fl / (ms * 1e-3) / 1e12
+
+    # end to end: x from pinned host memory in, y out, every step
+    xh = x.cpu().pin_memory()
+    yh = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    e2e = []
+    for _ in range(args.steps):
+        flush.zero_()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        x.copy_(xh, non_blocking=True)
+        L.qlinear(ctx, qw, x, bias=bias, out=y, stream=stream)
+        yh.copy_(y, non_blocking=True)
+        f1.record(stream)
+        e2e.append((f0, f1))
+    torch.cuda.synchronize()
+    ctx.check()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e) / len(e2e)
+    clocks = clk.summary()
+    pk = tensor_peak_for(sum(times) * 1e-3)
+    _, hbm_peak, _ = peaks()
+    line = {
+        "metric": "w8g64 qlinear TFLOP/s (BASELINE config 1)",
+        "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1) bf16 x, N(0,0.02) w8g64 weights, N(0,0.01) bias, seed 7",
+        "config": {"workload": "BASELINE config 1: qlinear 1024x4096 -> 4096 with bias",
+                   "l2": "operands 34.6 MB fit in L2: a 256 MB buffer is written between "
+                         "timed iterations, outside the event pairs"},
+        "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                "ms_per_step": round(e2e_ms, 4),
+                "api": "ltx_qlinear, x in from and y out to pinned host memory"},
+        "gpu_launches": int(launches),
+        "roofline": dict({"bound": "tensor", "achieved": round(tf, 1), "peak": pk["peak"],
+                          "peak_source": pk["kind"], "unit": "TFLOP/s",
+                          "frac": round(tf / pk["peak"], 4), "traffic": None,
+                          "kernel": "gemm_tc_kernel<MODE_W8G64> (fused route below "
+                                    "LTX_DEQUANT_MIN_M rows)"},
+                         **roofline_fracs(tf, pk, clocks)),
+        "hbm": {"algorithmic_bytes": int(byts), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+                "frac": round(byts / (ms * 1e-3) / 1e9 / hbm_peak, 4)},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        f, s, kind = ref_linear_sample(1)
+        line["cpu_baseline"] = {"value": round(f / s / 1e12, 6), "unit": "TFLOP/s", "cores": 1,
+                                "kind": kind, "sample": q1_sample_desc(), "seconds": round(s, 2)}
+    print(json.dumps(line), flush=True)
+    qw.free()
+    ctx.close()
+    return 0
+
+
+_Q1_CPU = {}
+
+
+def ref_linear_sample(threads):
+    """The reference's CPU qlinear for config 1 (dequantise-then-dense,
+    linear_ with f64 accumulation, src/ltx25-block-ref.cc:13-29) on the first
+    Q1_CPU_ROWS tokens, all N, full K; the weight is packed and dequantized
+    once, outside the timing.  Rows are split over `threads`.  Returns
+    (FLOPs, seconds, kind)."""
+    import concurrent.futures as cf
+    import numpy as np
+    from oracle import lib as olib
+    from oracle import ref as oref
+    if not _Q1_CPU:
+        M, K, N = Q1
+        kind = "reference" if oref.available() else "port"
+        rng = np.random.default_rng(7)
+        x = olib.bf16_to_f32(olib.f32_to_bf16(
+            rng.standard_normal((Q1_CPU_ROWS, K)).astype(np.float32)))
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        b = olib.bf16_to_f32(olib.f32_to_bf16((rng.standard_normal(N) * 0.01).astype(np.float32)))
+        _, _, _, deq = oref.pack(w, 8, 64) if kind == "reference" else olib.pack_affine(w, 8, 64)
+        if kind != "reference":
+            deq = olib.bf16_to_f32(deq) if deq.dtype == np.uint16 else deq
+        _Q1_CPU.update(x=x, w=deq, b=b, kind=kind)
+    c = _Q1_CPU
+    lin = oref.linear if c["kind"] == "reference" else (
+        lambda x, w, b: olib.linear_f64(x, w, b, 1))
+    rows = c["x"].shape[0]
+    t0 = time.perf_counter()
+    if threads <= 1:
+        lin(c["x"], c["w"], c["b"])
+    else:
+        step = max(1, (rows + threads - 1) // threads)
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            for f in [ex.submit(lin, c["x"][r:r + step], c["w"], c["b"])
+                      for r in range(0, rows, step)]:
+                f.result()
+    return flops(rows, Q1[1], Q1[2]), time.perf_counter() - t0, c["kind"]
+
+
+def q1_sample_desc():
+    return (f"reference linear_ (dequantise-then-dense, f64 accumulation) on the first "
+            f"{Q1_CPU_ROWS} of 1024 tokens x all 4096 output features, full K, bias; weight "
+            f"packed and dequantized once outside the timing")
+
+
+# ------------------------------------------------------------- reference arm
+def run_reference(args):
+    """--impl reference: the reference's own CPU implementation of the path
+    (oracle/_ref, compiled from the reference sources; the reference's GPU
+    path is Apple Metal, unavailable on this box) on the host cores, for the
+    same metric and config as the matching --workload.  Rank 0 only."""
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    wl = args.workload
+    if wl in ("stack", "block"):
+        ref_block_setup()
+        for _ in range(args.warmup):
+            ref_block_round(threads)
+        fl = sec = 0.0
+        for _ in range(args.steps):
+            f, s = ref_block_round(threads)
+            fl += f
+            sec += s
+        rate = fl / sec
+        per_block = full_block_flops() / rate
+        kind = _REF_BLOCK["kind"]
+        if wl == "stack":
+            value, unit = per_block * args.blocks, "s/step"
+            metric = "DiT s/denoise-step @960x544x121 (BASELINE config 5, 48-block stack)"
+            cfg = {"workload": f"{args.blocks}-block joint AV stack: video 8160x4096 "
+                               "(16x17x30), audio 126x2048, text 256; extrapolated from a "
+                               "bounded sample",
+                   "parallelism": f"{args.parallel}{args.gpus} (the CPU arm runs on rank 0's "
+                                  "host cores)"}
+        else:
+            value, unit = per_block * 1e3, "ms"
+            metric = "DiT joint AV block forward ms @960x544x121 (BASELINE config 4)"
+            cfg = {"workload": "one block: video 8160x4096 (16x17x30), audio 126x2048, text "
+                               "256; extrapolated from a bounded sample"}
+        desc = ref_block_desc(threads)
+        line = {"impl": "reference", "metric": metric, "value": round(value, 3), "unit": unit,
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(sec / args.steps * 1e3, 1), "higher_is_better": False,
+                "scaling": "strong" if wl == "stack" else "none", "vs_baseline": None,
+                "dtype": "f32/f64-accumulate", "data": "synthetic (seeded random-init block)",
+                "config": dict(cfg, sample=desc),
+                "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads,
+                                 "kind": kind, "sample": desc,
+                                 "gflops": round(rate / 1e9, 2)},
+                "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "the reference's GPU path is Apple Metal (unavailable on this box); "
+                        "this arm is its CPU block_forward on all host cores, each step one "
+                        "round of concurrent calls, extrapolated to the full geometry by "
+                        "algorithmic FLOPs"}
+        print(json.dumps(line), flush=True)
+        return 0
+    if wl == "qlinear":
+        for _ in range(args.warmup):
+            ref_linear_sample(threads)
+        fl = sec = 0.0
+        kind = "port"
+        for _ in range(args.steps):
+            f, s, kind = ref_linear_sample(threads)
+            fl += f
+            sec += s
+        value = fl / sec / 1e12
+        line = {"impl": "reference", "metric": "w8g64 qlinear TFLOP/s (BASELINE config 1)",
+                "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": sec / args.steps * 1e3,
+                "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+                "dtype": "f32/f64-accumulate", "data": "synthetic, seed 7",
+                "config": {"workload": "BASELINE config 1, bounded CPU sample",
+                           "sample": q1_sample_desc()},
+                "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
+                                 "kind": kind, "sample": q1_sample_desc()},
+                "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    if wl == "sweep":
+        for _ in range(args.warmup):
+            cpu_reference_sample(threads)
+        fl = sec = 0.0
+        kind = "port"
+        for _ in range(args.steps):
+            f, s, kind = cpu_reference_sample(threads)
+            fl += f
+            sec += s
+        value = fl / sec / 1e12
+        line = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": sec / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32/f64-accumulate",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": {"workload": "BASELINE config 2 sweep, bounded CPU sample",
+                       "sample": sample_desc()},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
+                             "kind": kind, "sample": sample_desc()},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "the reference's GPU path is Apple Metal (unavailable on this "
+                    "box); this arm is its CPU dequantise-then-dense qlinear",
+        }
+        print(json.dumps(line), flush=True)
+        return 0
+    print(json.dumps({"impl": "reference",
+                      "unavailable": f"no reference CPU arm for --workload {wl}: the reference "
+                                     "implements it only in Metal"}), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 10 for stack, 200 otherwise)")
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="stack: skip the config-2 sweep carried on the line")
+    ap.add_argument("--only", type=int, default=None,
+                    help="profile one sweep shape (index into SHAPES)")
+    ap.add_argument("--blocks", type=int, default=48, help="stack depth (--workload stack)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "sp"],
+                    help="stack under torchrun: tensor parallel (BASELINE config 5) or "
+                         "sequence/head parallel")
+    ap.add_argument("--sage", action="store_true", help="sage_attn tier (--workload attn)")
+    ap.add_argument("--route", default="auto", choices=["auto", "fused", "dequant"],
+                    help="qlinear route for quantized weights (sweep)")
+    ap.add_argument("--workload", default="stack",
+                    choices=["stack", "sweep", "qlinear", "block", "attn", "lora", "trunk",
+                             "connector", "adaln", "i8"],
+                    help="stack: BASELINE config 5, the 48-block denoise step (the "
+                         "headline, carrying the config-2 sweep); sweep: config 2 alone; "
+                         "qlinear: config 1; i8: config 3; block: config 4")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 10 if args.workload == "stack" else 200
+    args.warmup = max(args.warmup, 3)
+    if args.only is not None:
+        SHAPES[:] = [SHAPES[args.only]]
+    if args.impl == "reference":
+        return run_reference(args)
+    runs = {"stack": run_stack, "sweep": run_sweep, "qlinear": run_qlinear,
+            "block": run_block, "attn": run_attn, "lora": run_lora, "trunk": run_trunk,
+            "connector": run_connector, "adaln": run_adaln, "i8": run_i8}
+    return runs[args.workload](args)
 
 
 if __name__ == "__main__":

@@ -10,6 +10,8 @@
 //                                            -> CudaOpsAdapter::linear(stream, ...)
 //   set_i8_gemm / set_sage / i8_takes        -> set_tiers / i8_takes
 //   wait_ok() after a command buffer         -> wait_ok(stream, err)
+//   MetalBlock::create/upload/reserve/forward (src/ltx25-block-metal.h:245-325)
+//                                            -> CudaBlockAdapter
 //
 // MetalOps::linear returns nothing and reports shape errors at bind time; the
 // adapter's linear() throws std::runtime_error with the library's message on
@@ -44,6 +46,8 @@ public:
 
   ltx_qweight* handle() const { return h_; }
   bool valid() const { return h_ != nullptr; }
+  // Gives up ownership: the caller frees the handle with ltx_qweight_free.
+  ltx_qweight* release() { return std::exchange(h_, nullptr); }
 
 private:
   friend class CudaOpsAdapter;
@@ -94,7 +98,13 @@ public:
   void linear(void* stream, const void* x, const CudaQWeight& w, const void* bias, void* y,
               int M, int K, int N) const
   {
-    const int rc = ltx_qlinear(ctx_, w.handle(), x, bias, y, M, K, N, stream);
+    linear(stream, x, w.handle(), bias, y, M, K, N);
+  }
+  // The same on a handle the caller keeps owning.
+  void linear(void* stream, const void* x, const ltx_qweight* w, const void* bias, void* y,
+              int M, int K, int N) const
+  {
+    const int rc = ltx_qlinear(ctx_, w, x, bias, y, M, K, N, stream);
     if (rc != LTX_OK) throw std::runtime_error(ltx_ctx_last_error(ctx_));
   }
 
@@ -119,6 +129,58 @@ public:
 
 private:
   ltx_ctx* ctx_ = nullptr;
+};
+
+// One joint audio-video block (the reference's MetalBlock): tensors staged
+// under the reference's parameter names, finalize, reserve once per
+// geometry, then forward with x updated in place.  bool + err string like
+// MetalBlock's own calls.
+class CudaBlockAdapter {
+public:
+  CudaBlockAdapter() = default;
+  ~CudaBlockAdapter() { ltx_block_destroy(b_); }
+  CudaBlockAdapter(const CudaBlockAdapter&) = delete;
+  CudaBlockAdapter& operator=(const CudaBlockAdapter&) = delete;
+
+  bool create(const CudaOpsAdapter& ops, int video_dim, int video_heads, int audio_dim,
+              int audio_heads, std::string* err)
+  {
+    const int rc = ltx_block_create(ops.ctx(), video_dim, video_heads, audio_dim,
+                                    audio_heads, &b_);
+    if (rc != LTX_OK && err != nullptr)
+      *err = ops.ctx() != nullptr ? ltx_ctx_last_error(ops.ctx()) : "no context";
+    return rc == LTX_OK;
+  }
+  bool set_qlinear(const char* name, const uint32_t* codes, const void* scales,
+                   const void* biases, int sb_dtype, int N, int K, std::string* err)
+  {
+    return ok_(ltx_block_set_qlinear(b_, name, codes, scales, biases, sb_dtype, N, K, 0), err);
+  }
+  bool set_tensor(const char* name, const float* data, int rows, int cols, std::string* err)
+  {
+    return ok_(ltx_block_set_tensor(b_, name, data, rows, cols, 0), err);
+  }
+  bool finalize(std::string* err) { return ok_(ltx_block_finalize(b_), err); }
+  bool reserve(int video_tokens, int audio_tokens, int text_tokens, std::string* err)
+  {
+    return ok_(ltx_block_reserve(b_, video_tokens, audio_tokens, text_tokens), err);
+  }
+  bool set_layer(int layer, std::string* err) { return ok_(ltx_block_set_layer(b_, layer), err); }
+  bool forward(void* stream, const ltx_stream_io* video, const ltx_stream_io* audio,
+               std::string* err)
+  {
+    return ok_(ltx_block_forward(b_, video, audio, stream), err);
+  }
+  ltx_block* handle() const { return b_; }
+
+private:
+  bool ok_(int rc, std::string* err) const
+  {
+    if (rc == LTX_OK) return true;
+    if (err != nullptr) *err = b_ != nullptr ? ltx_block_last_error(b_) : "no block";
+    return false;
+  }
+  ltx_block* b_ = nullptr;
 };
 
 }  // namespace ltx25

@@ -218,16 +218,21 @@ def block_forward(t, video, audio, vdim, vheads, adim, aheads, eps=EPS,
 # ---- seeded synthetic weights and inputs ---------------------------------
 
 def random_block_tensors(vdim, vheads, adim, aheads, seed=0, ff_mult=4,
-                         w_std=None):
+                         w_std=None, f32_draws=False):
     """Random-init weights under the reference's names.  Matrices are
     N(0, w_std) (default 1/sqrt(fan_in)); biases N(0, 0.02); norm gains
     1 + N(0, 0.1); adaLN tables N(0, 0.1); gate logits N(0, 1/sqrt(in)).
     The video feed-forward has no bias, the audio one does
-    (src/ltx25-dit-weights.cc:482-486)."""
+    (src/ltx25-dit-weights.cc:482-486).  f32_draws draws the matrices in f32
+    (other values, same distribution; for timing at the real widths)."""
     rng = np.random.default_rng(seed)
 
     def mat(o, i):
         s = w_std if w_std is not None else 1.0 / np.sqrt(i)
+        if f32_draws:
+            m = rng.standard_normal((o, i), dtype=F32)
+            m *= F32(s)
+            return m
         return (rng.standard_normal((o, i)) * s).astype(F32)
 
     def vec(n, s=0.02, mean=0.0):

@@ -19,6 +19,11 @@ REPO = os.path.dirname(HERE)
 OUT_DIR = os.path.join(HERE, "lib")
 OBJ_DIR = os.path.join(HERE, "lib", "obj")
 LIB = os.path.join(OUT_DIR, "libltx25_cuda.so")
+# the plugin entry (plugin/ltx25-plugin-cuda.cc against the in-repo vpipe
+# stub headers), linked against LIB
+PLUGIN = os.path.join(OUT_DIR, "vpipe-ltx-2.5-b200.so")
+PLUGIN_SRC = os.path.join(HERE, "plugin", "ltx25-plugin-cuda.cc")
+CXX = os.environ.get("CXX", "g++")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -85,7 +90,25 @@ def build(force=False, jobs=8, verbose=False):
             r = subprocess.run(cmd, capture_output=True, text=True)
             if r.returncode != 0:
                 raise RuntimeError(f"link failed:\n{r.stdout}{r.stderr}")
+    build_plugin(force)
     return LIB
+
+
+def build_plugin(force=False):
+    """The plugin shim: host C++ only, warnings as errors, rpath to LIB."""
+    deps = [PLUGIN_SRC, LIB] + glob.glob(os.path.join(HERE, "plugin", "stub", "plugin", "*.h")) \
+        + glob.glob(os.path.join(REPO, "include", "*.h*"))
+    if not force and os.path.exists(PLUGIN) and \
+            os.path.getmtime(PLUGIN) >= max(os.path.getmtime(d) for d in deps):
+        return PLUGIN
+    cmd = [CXX, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-Werror",
+           "-fvisibility=hidden", "-I" + os.path.join(REPO, "include"),
+           "-I" + os.path.join(HERE, "plugin", "stub"), PLUGIN_SRC, "-o", PLUGIN,
+           "-L" + OUT_DIR, "-lltx25_cuda", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"plugin build failed:\n{' '.join(cmd)}\n{r.stdout}{r.stderr}")
+    return PLUGIN
 
 
 if __name__ == "__main__":
