@@ -57,7 +57,7 @@ def _folded(t, pairs):
     return f
 
 
-def _worker(rank, world, port, out_dir, adapted=False):
+def _worker(rank, world, port, out_dir, adapted=False, rows=False):
     import torch
     import torch.distributed as dist
     import tp_np
@@ -71,10 +71,20 @@ def _worker(rank, world, port, out_dir, adapted=False):
         def allreduce(arr):
             dist.all_reduce(torch.from_numpy(arr))
 
-        vx, ax = tp_np.block_forward_tp(t, ins["video"], ins["audio"], CFG["vdim"],
-                                        CFG["vheads"], CFG["adim"], CFG["aheads"],
-                                        rank, world, allreduce,
-                                        lora=_lora(t) if adapted else None)
+        def allgather(local):
+            parts = [torch.empty(local.shape, dtype=torch.float32) for _ in range(world)]
+            dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(local, np.float32)))
+            return np.concatenate([p.numpy() for p in parts], axis=0)
+
+        if rows:
+            vx, ax = tp_np.block_forward_tp_rows(t, ins["video"], ins["audio"], CFG["vdim"],
+                                                 CFG["vheads"], CFG["adim"], CFG["aheads"],
+                                                 rank, world, allreduce, allgather)
+        else:
+            vx, ax = tp_np.block_forward_tp(t, ins["video"], ins["audio"], CFG["vdim"],
+                                            CFG["vheads"], CFG["adim"], CFG["aheads"],
+                                            rank, world, allreduce,
+                                            lora=_lora(t) if adapted else None)
         np.save(os.path.join(out_dir, f"v{rank}.npy"), vx)
         np.save(os.path.join(out_dir, f"a{rank}.npy"), ax)
     finally:
@@ -105,6 +115,28 @@ def test_sharded_block_equals_the_oracle(tmp_path, world, adapted):
         pv, pa = block_np.block_forward(t, ins["video"], ins["audio"], CFG["vdim"],
                                         CFG["vheads"], CFG["adim"], CFG["aheads"])
         assert lib.rel_l2(v0, pv) > 1e-3 and lib.rel_l2(a0, pa) > 1e-3
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_sharded_residual_equals_the_oracle(tmp_path, world):
+    """Tensor parallel with the video residual kept by token rows (reduce-
+    scatter / all-gather; the GPU path's default when the tokens split
+    evenly): every rank ends with the same whole x, equal to the unsharded
+    oracle block up to summation order."""
+    import torch.multiprocessing as mp
+    mp.start_processes(_worker, args=(world, _port(), str(tmp_path), False, True),
+                       nprocs=world, join=True, start_method="spawn")
+    t, ins = _inputs()
+    wv, wa = block_np.block_forward(t, ins["video"], ins["audio"], CFG["vdim"],
+                                    CFG["vheads"], CFG["adim"], CFG["aheads"])
+    v0 = np.load(tmp_path / "v0.npy")
+    a0 = np.load(tmp_path / "a0.npy")
+    for r in range(1, world):
+        assert np.array_equal(np.load(tmp_path / f"v{r}.npy"), v0)
+        assert np.array_equal(np.load(tmp_path / f"a{r}.npy"), a0)
+    assert lib.rel_l2(v0, wv) < 1e-5
+    assert lib.rel_l2(a0, wa) < 1e-5
+    assert lib.rel_l2(v0, ins["video"]["x"]) > 1e-2
 
 
 @pytest.mark.parametrize("adapted", [False, True])

@@ -5,7 +5,10 @@ against the one-GPU block and the CPU oracle.
 Two spawned processes, one per GPU, join one NCCL group (rendezvous id made
 here), load the same full weights (tensor parallel: each keeps its shard;
 sequence parallel: each keeps them whole and runs half the video tokens),
-and run a block and a 2-block stack on the same replicated inputs.  Checked: both ranks end with the same x; it matches the
+and run a block and a 2-block stack on the same replicated inputs.  Tensor
+parallel runs with the residual sharded by token rows (the default when the
+tokens split evenly) and, in tp_allreduce, with x whole on every rank and the
+products all-reduced.  Checked: both ranks end with the same x; it matches the
 oracle at the block bars of tests/test_block_gpu.py and the one-GPU device
 block within bf16.  Skipped with fewer than 2 GPUs.  NVLS is off in the
 workers, and a worker that does not finish in time is killed by PID.
@@ -93,6 +96,10 @@ def _run(ctx, world_blocks, ins, lora=False):
 
 def _worker(rank, world, uid, out_dir, mode):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if mode.startswith("tp_allreduce"):
+        # the whole-x layout (all-reduced products) instead of the default
+        # row-sharded residual (reduce-scatter / all-gather)
+        os.environ["LTX25_TP_ROWS"] = "0"
     import torch
     import ltx25_b200 as L
     torch.cuda.set_device(rank)
@@ -104,7 +111,7 @@ def _worker(rank, world, uid, out_dir, mode):
     ctx.close()
 
 
-@pytest.mark.parametrize("mode", ["tp", "sp", "tp_lora", "sp_lora"])
+@pytest.mark.parametrize("mode", ["tp", "sp", "tp_lora", "sp_lora", "tp_allreduce"])
 def test_two_gpu_block_and_stack(ctx, tmp_path, mode):
     import torch
     import torch.multiprocessing as mp

@@ -166,3 +166,75 @@ def block_forward_tp(t, video, audio, vdim, vheads, adim, aheads, rank, world, a
     _ff(t, "", v, vdim, tp)
     _ff(t, "audio_", a, adim, tp)
     return v["x"], a["x"]
+
+
+# ---- the row-sharded residual (tensor parallel with the video x kept by
+# token rows between blocks, host/ltx25-block-cuda.cc `rows` paths) --------
+#
+# Rank r holds video rows [r*T/W, (r+1)*T/W) of x.  Each modulated input
+# (ada_zero, row-local) is formed for those rows and all-gathered; the
+# sharded projections then see all T rows exactly as above; each row-split
+# product is reduce-scattered (here: summed over ranks, then the rank keeps
+# its rows) and the gated residual touches only the rank's rows.  The audio
+# stream stays whole on every rank.  At the end the video rows are gathered.
+
+def _rows(arr, rank, world):
+    n = arr.shape[0] // world
+    return arr[rank * n:(rank + 1) * n]
+
+
+def block_forward_tp_rows(t, video, audio, vdim, vheads, adim, aheads, rank, world,
+                          allreduce, allgather):
+    """The same block with the video residual sharded by rows.
+    `allgather(local)` returns the rows of all ranks stacked in rank order."""
+    tp = (rank, world, allreduce, None)
+    v = dict(video)
+    a = dict(audio)
+    vx = _rows(np.asarray(v["x"], F32), rank, world).copy()     # this rank's rows
+    a["x"] = np.asarray(a["x"], F32).copy()
+    hd = vdim // vheads
+    table = t["scale_shift_table"]
+    # video first half
+    msa = block_np.ada_values(table, v["timesteps"], vdim, 0, 3)
+    normed = allgather(block_np.ada_zero(vx, EPS, msa[1], msa[0]))
+    sa = _attn_tp(t, "attn1", normed, normed, v.get("pe"), None, vheads, hd, *tp)
+    vx = (vx + _rows(sa, rank, world) * msa[2]).astype(F32)
+    ca = block_np.ada_values(table, v["timesteps"], vdim, 6, 9)
+    qin = allgather(block_np.mod(block_np.rms_norm(vx, EPS), ca[1], ca[0]))
+    pst = np.asarray(t["prompt_scale_shift_table"], F32).ravel()
+    shift, scale = pst[:vdim].copy(), pst[vdim:2 * vdim].copy()
+    pts = v.get("prompt_timestep")
+    if pts is not None and np.asarray(pts).size >= 2 * vdim:
+        pts = np.asarray(pts, F32).ravel()
+        shift = (shift + pts[:vdim]).astype(F32)
+        scale = (scale + pts[vdim:2 * vdim]).astype(F32)
+    kv = block_np.mod(v["context"], scale, shift)
+    co = _attn_tp(t, "attn2", qin, kv, None, None, vheads, hd, *tp)
+    vx = (vx + _rows(co, rank, world) * ca[2]).astype(F32)
+    # audio first half, whole
+    _first_half(t, "audio_", a, adim, aheads, tp)
+    # cross attentions from the pre-cross state
+    vx_pre, ax_pre = vx.copy(), a["x"].copy()
+    ahd = adim // aheads
+    vtab = t["scale_shift_table_a2v_ca_video"]
+    atab = t["scale_shift_table_a2v_ca_audio"]
+    vsc, vsh, vg = block_np.av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 0)
+    asc, ash, _ = block_np.av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 0)
+    qv = allgather(block_np.ada_zero(vx_pre, EPS, vsc, vsh))
+    kva = block_np.ada_zero(ax_pre, EPS, asc, ash)
+    o = _attn_tp(t, "audio_to_video_attn", qv, kva, v.get("cross_pe"), a.get("cross_pe"),
+                 aheads, ahd, *tp)
+    vx = (vx + _rows(o, rank, world) * vg).astype(F32)
+    asc, ash, ag = block_np.av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 2)
+    vsc, vsh, _ = block_np.av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 2)
+    qa = block_np.ada_zero(ax_pre, EPS, asc, ash)
+    kvv = allgather(block_np.ada_zero(vx_pre, EPS, vsc, vsh))
+    o = _attn_tp(t, "video_to_audio_attn", qa, kvv, a.get("cross_pe"), v.get("cross_pe"),
+                 aheads, ahd, *tp)
+    a["x"] = (a["x"] + o * ag).astype(F32)
+    # feed-forwards
+    mlp = block_np.ada_values(table, v["timesteps"], vdim, 3, 6)
+    scaled = allgather(block_np.ada_zero(vx, EPS, mlp[1], mlp[0]))
+    vx = (vx + _rows(_ff_tp(t, "", scaled, *tp), rank, world) * mlp[2]).astype(F32)
+    _ff(t, "audio_", a, adim, tp)
+    return allgather(vx), a["x"]

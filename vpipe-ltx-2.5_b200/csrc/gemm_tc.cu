@@ -31,6 +31,20 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t,
   kb1 = (int)((long long)(split + 1) * p.kblocks / p.splits);
 }
 
+// The i-th k-block a tile visits.  With one token tile (M <= TN: every CTA
+// of the grid reads the same activation rows), each weight tile starts its
+// K range at its own offset, so the CTAs that share a K range do not all
+// request the same activation lines from L2 at the same moment; otherwise
+// in order.  The producer and the MMA issuer walk the same sequence.
+__device__ __forceinline__ int kb_at(const GemmParams& p, int i, int n_tile, int kb0, int kb1)
+{
+  const int nkb = kb1 - kb0;
+  if (p.m_tiles != 1 || nkb <= 1) return kb0 + i;
+  int j = i + n_tile % nkb;
+  if (j >= nkb) j -= nkb;
+  return kb0 + j;
+}
+
 // Two u8 codes -> bf16x2 of s*q + z, rounded once (fma.rn.bf16x2).  The
 // codes become exact f32 integers through the 2^23 magic, whose upper half
 // is then exactly the bf16 of the code (an integer below 2^8 has no bits in
@@ -185,7 +199,8 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
         decode_tile(p, t, mt, nt, kb0, kb1);
         const int wrow0 = nt * kWT + rank * C::kBM;
         const int xrow0 = mt * TN + rank * C::kXRows;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0; i < kb1 - kb0; ++i) {
+          const int kb = kb_at(p, i, nt, kb0, kb1);
           const unsigned long long c0 = tr ? clock64() : 0ull;
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, p.err,
                          KERR_WAIT_PRODUCER))
@@ -271,7 +286,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
         if (tr) w_acc += clock64() - c0;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * TN);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0; i < kb1 - kb0; ++i) {
           if (tr) c0 = clock64();
           if (!mbar_wait(&full[stage], phase, s_abort, p.err, KERR_WAIT_MMA))
             goto mma_done;
@@ -297,7 +312,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
               sdesc_k128_sw128(smem_u32(s_x + stage * C::kXStage));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
+            const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
             if constexpr (PAIR && MODE == MODE_BF16) {
               const uint64_t adesc =
                   sdesc_k128_sw128(smem_u32(s_w + stage * C::kWStage));

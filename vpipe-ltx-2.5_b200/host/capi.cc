@@ -971,10 +971,11 @@ int ltx_stack_forward(ltx_stack* s, const ltx_stream_io* video,
       return sfail(s, LTX_E_SHAPE, "forward: block range outside the stack");
     if (!s->reserved) return sfail(s, LTX_E_STATE, "forward before reserve");
     ltx25::StreamIO whole = to_io(video), a = to_io(audio);
-    // Sequence parallel: each rank runs its token shard through every block
-    // and the shards are gathered once, after the last.
+    // Sequence parallel, and tensor parallel with the residual sharded by
+    // rows: each rank runs its token shard of x through every block and the
+    // shards are gathered once, after the last.
     ltx25::StreamIO v = whole;
-    const bool sp = s->blocks[0]->blk->sequence_parallel();
+    const bool sp = s->blocks[0]->blk->shards_video(whole.present ? whole.tokens : 0);
     if (sp) {
       std::string e;
       if (!s->blocks[0]->blk->shard_io(whole, &v, &e)) return sfail(s, LTX_E_SHAPE, e);

@@ -2,6 +2,7 @@
 #include "ltx25-block-cuda.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "../csrc/block_ops.h"
@@ -486,6 +487,9 @@ bool CudaBlock::finalize(std::string* err)
   // Tensor parallel shards the weights; sequence parallel keeps them whole.
   _tp_world = (_comm && !_sp) ? _comm->world() : 1;
   _tp_rank = (_comm && !_sp) ? _comm->rank() : 0;
+  // A/B switch for the tensor-parallel residual layout (LTX25_TP_ROWS=0:
+  // whole x on every rank, all-reduced products), read once per block.
+  if (const char* e = std::getenv("LTX25_TP_ROWS")) _tp_rows = e[0] != '0';
   if (_sp && (_vheads % _sp_world != 0 || _aheads % _sp_world != 0))
     return fail(err, "sequence parallel shape: heads do not split over the ranks");
   if (!build_stream_(false, _video, err) || !build_stream_(true, _audio, err))
@@ -749,7 +753,7 @@ bool CudaBlock::attend_v2a_sp_(cudaStream_t s, const CudaAttn& a, const __nv_bfl
 bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
                           const QWeight& w, const __nv_bfloat16* bias,
                           __nv_bfloat16* x, int n, int d, const float* gate,
-                          std::string* err, const LoraSite* lora)
+                          std::string* err, const LoraSite* lora, int n_all)
 {
   LoraExt lx;
   const LoraExt* ext = lora != nullptr ? lx_(*lora, &lx) : nullptr;
@@ -758,6 +762,18 @@ bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
   // Row split: this rank's K columns give a partial product (the adapter's
   // too, from its A columns); the sum over ranks, then the bias and the
   // gated residual, once.
+  if (n_all > n) {
+    // Row-sharded residual: the partial covers all n_all tokens; the
+    // reduce-scatter leaves this rank the sum for its own n rows only.
+    __nv_bfloat16* mine = _cur->part + (size_t)_tp_rank * n * d;
+    if (!_ops->linear(s, in, k, w, nullptr, _cur->part, d, n_all, k, d, ltx::EPI_STORE,
+                      nullptr, err, ext) ||
+        !_ccur->reduce_scatter_bf16(_cur->part, (size_t)n * d, s, err))
+      return false;
+    if (ltx::launch_gated_residual(x, d, mine, bias, gate, n, d, s) != 0)
+      return fail(err, "gated residual launch failed");
+    return true;
+  }
   if (!_ops->linear(s, in, k, w, nullptr, _cur->part, d, n, k, d, ltx::EPI_STORE,
                     nullptr, err, ext) ||
       !_ccur->allreduce_sum(_cur->part, (size_t)n * d, 1, s, err))
@@ -767,11 +783,25 @@ bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
   return true;
 }
 
+bool CudaBlock::gather_rows_(cudaStream_t s, __nv_bfloat16* buf, int n, int d,
+                             std::string* err) const
+{
+  return _ccur->allgather_bf16(buf + (size_t)_tp_rank * n * d, buf, (size_t)n * d, s, err);
+}
+
 bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                             std::string* err)
 {
   // src/ltx25-block-ref.cc:196-262
   const int n = io.tokens, d = w.dim;
+  // Tensor parallel with the residual sharded by token rows: this rank
+  // holds rows [tok0, tok0 + n) of x; each modulated input is formed for
+  // those rows into their place of a whole-sequence buffer and gathered, the
+  // projections see all n_all rows, and the row-split products are
+  // reduce-scattered back to the rank's rows.
+  const bool rows = &w == &_video && _tp_world > 1 && io.tokens_all > n;
+  const int nf = rows ? io.tokens_all : n;
+  const size_t off = rows ? (size_t)_tp_rank * n * d : 0;
   float* mods = _arp->mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
   if (ltx::launch_vec_add(w.scale_shift, io.timesteps, mods + MOD_MSA * d, 3 * d, s) ||
       ltx::launch_vec_add(w.scale_shift + 6 * d, io.timesteps ? io.timesteps + 6 * d : nullptr,
@@ -780,31 +810,35 @@ bool CudaBlock::first_half_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
                           mods + MOD_PROMPT * d, 2 * d, s))
     return fail(err, "adaLN rows launch failed");
   // normed = rms_norm(x) * (1 + scale) + shift;  x += gate * attn1(normed)
-  if (ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_MSA + 1) * d,
+  if (ltx::launch_ada_zero(io.x, d, _cur->normed + off, d, n, d, mods + (MOD_MSA + 1) * d,
                            mods + MOD_MSA * d, kEps, true, s))
     return fail(err, "ada_zero launch failed");
-  const RopeRef self_r{io.pe_cos, io.pe_sin, io.tokens_all > 0 ? io.tokens_all : n, io.tok0};
+  if (rows && !gather_rows_(s, _cur->normed, n, d, err)) return false;
+  const RopeRef self_r = rows ? RopeRef{io.pe_cos, io.pe_sin, nf, 0}
+                              : RopeRef{io.pe_cos, io.pe_sin,
+                                        io.tokens_all > 0 ? io.tokens_all : n, io.tok0};
   const bool sp = _sp && &w == &_video;
   if (sp ? !attend_self_sp_(s, w.attn1, _cur->normed, n, self_r, _cur->att, err)
-         : !attend_(s, w.attn1, _cur->normed, n, _cur->normed, n, self_r, self_r, _cur->att,
+         : !attend_(s, w.attn1, _cur->normed, nf, _cur->normed, nf, self_r, self_r, _cur->att,
                     err))
     return false;
   if (!out_proj_(s, _cur->att, w.attn1.inner, w.attn1.o, w.attn1.o_b, io.x, n, d,
-                 mods + (MOD_MSA + 2) * d, err, &w.attn1.l_o))
+                 mods + (MOD_MSA + 2) * d, err, &w.attn1.l_o, nf))
     return false;
   // Text cross-attention: query = mod(rms_norm(x)) (= ada_zero with the
   // cross rows), key/value = context modulated by the prompt table + driver.
-  if (ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_CA + 1) * d,
+  if (ltx::launch_ada_zero(io.x, d, _cur->normed + off, d, n, d, mods + (MOD_CA + 1) * d,
                            mods + MOD_CA * d, kEps, true, s) ||
       ltx::launch_ada_zero(io.context, d, _cur->ctxmod, d, io.text_tokens, d,
                            mods + (MOD_PROMPT + 1) * d, mods + MOD_PROMPT * d,
                            kEps, false, s))
     return fail(err, "modulation launch failed");
-  if (!attend_(s, w.attn2, _cur->normed, n, _cur->ctxmod, io.text_tokens, RopeRef{},
+  if (rows && !gather_rows_(s, _cur->normed, n, d, err)) return false;
+  if (!attend_(s, w.attn2, _cur->normed, nf, _cur->ctxmod, io.text_tokens, RopeRef{},
                RopeRef{}, _cur->att, err))
     return false;
   return out_proj_(s, _cur->att, w.attn2.inner, w.attn2.o, w.attn2.o_b, io.x, n, d,
-                   mods + (MOD_CA + 2) * d, err, &w.attn2.l_o);
+                   mods + (MOD_CA + 2) * d, err, &w.attn2.l_o, nf);
 }
 
 bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
@@ -812,45 +846,63 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
 {
   // src/ltx25-block-ref.cc:264-281
   const int n = io.tokens, d = w.dim;
+  const bool rows = &w == &_video && _tp_world > 1 && io.tokens_all > n;
+  const int nf = rows ? io.tokens_all : n;
+  const size_t off = rows ? (size_t)_tp_rank * n * d : 0;
   float* mods = _arp->mods + (&w == &_audio ? (size_t)MOD_ROWS * _vdim : 0);
   if (ltx::launch_vec_add(w.scale_shift + 3 * d, io.timesteps ? io.timesteps + 3 * d : nullptr,
                           mods + MOD_MLP * d, 3 * d, s) ||
-      ltx::launch_ada_zero(io.x, d, _cur->normed, d, n, d, mods + (MOD_MLP + 1) * d,
+      ltx::launch_ada_zero(io.x, d, _cur->normed + off, d, n, d, mods + (MOD_MLP + 1) * d,
                            mods + MOD_MLP * d, kEps, true, s))
     return fail(err, "ff pre-norm launch failed");
+  if (rows && !gather_rows_(s, _cur->normed, n, d, err)) return false;
   LoraExt lx;
-  return _ops->linear(s, _cur->normed, d, w.ff_in, w.ff_in_b, _cur->ff, w.ff_hidden, n,
+  return _ops->linear(s, _cur->normed, d, w.ff_in, w.ff_in_b, _cur->ff, w.ff_hidden, nf,
                       d, w.ff_hidden, ltx::EPI_GELU, nullptr, err, lx_(w.l_ff_in, &lx)) &&
          out_proj_(s, _cur->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, n, d,
-                   mods + (MOD_MLP + 2) * d, err, &w.l_ff_out);
+                   mods + (MOD_MLP + 2) * d, err, &w.l_ff_out, nf);
+}
+
+bool CudaBlock::shards_video(int tokens) const
+{
+  if (_sp) return true;
+  return _tp_world > 1 && _tp_rows && tokens > 0 && tokens % _tp_world == 0;
 }
 
 bool CudaBlock::shard_io(const StreamIO& whole, StreamIO* shard, std::string* err) const
 {
   *shard = whole;
-  if (!_sp || !whole.present || whole.tokens <= 0) return true;
-  if (whole.tokens % _sp_world != 0)
+  if (!whole.present || whole.tokens <= 0 || !shards_video(whole.tokens)) {
+    if (_sp && whole.present && whole.tokens > 0)
+      return fail(err, "sequence parallel shape: " + std::to_string(whole.tokens) +
+                           " video tokens do not split over " + std::to_string(_sp_world) +
+                           " ranks");
+    return true;
+  }
+  const int world = _sp ? _sp_world : _tp_world, rank = _sp ? _sp_rank : _tp_rank;
+  if (whole.tokens % world != 0)
     return fail(err, "sequence parallel shape: " + std::to_string(whole.tokens) +
-                         " video tokens do not split over " + std::to_string(_sp_world) +
+                         " video tokens do not split over " + std::to_string(world) +
                          " ranks");
-  const int tl = whole.tokens / _sp_world;
-  shard->x = whole.x + (size_t)_sp_rank * tl * _vdim;
+  const int tl = whole.tokens / world;
+  shard->x = whole.x + (size_t)rank * tl * _vdim;
   shard->tokens = tl;
-  shard->tok0 = _sp_rank * tl;
+  shard->tok0 = rank * tl;
   shard->tokens_all = whole.tokens;
   return true;
 }
 
 bool CudaBlock::gather_video(cudaStream_t s, const StreamIO& whole, std::string* err) const
 {
-  if (!_sp || !whole.present || whole.tokens <= 0) return true;
-  const size_t cnt = (size_t)(whole.tokens / _sp_world) * _vdim;
-  return _comm->allgather_bf16(whole.x + (size_t)_sp_rank * cnt, whole.x, cnt, s, err);
+  if (!whole.present || whole.tokens <= 0 || !shards_video(whole.tokens)) return true;
+  const int world = _sp ? _sp_world : _tp_world, rank = _sp ? _sp_rank : _tp_rank;
+  const size_t cnt = (size_t)(whole.tokens / world) * _vdim;
+  return _comm->allgather_bf16(whole.x + (size_t)rank * cnt, whole.x, cnt, s, err);
 }
 
 bool CudaBlock::forward(cudaStream_t s, StreamIO& v, StreamIO& a, std::string* err)
 {
-  if (!_sp) return forward_impl_(s, v, a, err);
+  if (!shards_video(v.present ? v.tokens : 0)) return forward_impl_(s, v, a, err);
   StreamIO vl;
   return shard_io(v, &vl, err) && forward_impl_(s, vl, a, err) && gather_video(s, v, err);
 }
@@ -906,27 +958,37 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
         ltx::launch_vec_add(_audio.cross_table, a.cross_scale_shift, am + MOD_AV * ad, 4 * ad, s) ||
         ltx::launch_vec_add(_audio.cross_table + 4 * ad, a.cross_gate, am + MOD_AVG * ad, ad, s))
       return fail(err, "cross adaLN launch failed");
+    // Row-sharded residual (tensor parallel): both modulations of this
+    // rank's video rows are formed in place and gathered to all rows.
+    const bool vrows = _tp_world > 1 && v.tokens_all > v.tokens;
+    const int vn = v.tokens, vnf = vrows ? v.tokens_all : vn;
+    const size_t voff = vrows ? (size_t)_tp_rank * vn * vd : 0;
     // av rows: [scale(lo=0), shift(lo=0), scale(lo=2), shift(lo=2)]
-    if (ltx::launch_ada_zero(v.x, vd, _arp->qv, vd, v.tokens, vd, vm + (MOD_AV + 0) * vd,
+    if (ltx::launch_ada_zero(v.x, vd, _arp->qv + voff, vd, vn, vd, vm + (MOD_AV + 0) * vd,
                              vm + (MOD_AV + 1) * vd, kEps, true, s) ||
         ltx::launch_ada_zero(a.x, ad, _arp->kva, ad, a.tokens, ad, am + (MOD_AV + 0) * ad,
                              am + (MOD_AV + 1) * ad, kEps, true, s) ||
         ltx::launch_ada_zero(a.x, ad, _arp->qa, ad, a.tokens, ad, am + (MOD_AV + 2) * ad,
                              am + (MOD_AV + 3) * ad, kEps, true, s) ||
-        ltx::launch_ada_zero(v.x, vd, _arp->kvv, vd, v.tokens, vd, vm + (MOD_AV + 2) * vd,
+        ltx::launch_ada_zero(v.x, vd, _arp->kvv + voff, vd, vn, vd, vm + (MOD_AV + 2) * vd,
                              vm + (MOD_AV + 3) * vd, kEps, true, s))
       return fail(err, "cross ada_zero launch failed");
+    if (vrows && (!gather_rows_(s, _arp->qv, vn, vd, err) ||
+                  !gather_rows_(s, _arp->kvv, vn, vd, err)))
+      return false;
     // a2v: video queries, audio keys/values
-    const RopeRef vc{v.cpe_cos, v.cpe_sin, v.tokens_all > 0 ? v.tokens_all : v.tokens, v.tok0};
+    const RopeRef vc = vrows ? RopeRef{v.cpe_cos, v.cpe_sin, vnf, 0}
+                             : RopeRef{v.cpe_cos, v.cpe_sin,
+                                       v.tokens_all > 0 ? v.tokens_all : v.tokens, v.tok0};
     const RopeRef ac{a.cpe_cos, a.cpe_sin, a.tokens, 0};
-    if (!attend_(s, _a2v, _arp->qv, v.tokens, _arp->kva, a.tokens, vc, ac, _arp->att, err) ||
-        !out_proj_(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, v.tokens, vd,
-                   vm + MOD_AVG * vd, err, &_a2v.l_o))
+    if (!attend_(s, _a2v, _arp->qv, vnf, _arp->kva, a.tokens, vc, ac, _arp->att, err) ||
+        !out_proj_(s, _arp->att, _a2v.inner, _a2v.o, _a2v.o_b, v.x, vn, vd,
+                   vm + MOD_AVG * vd, err, &_a2v.l_o, vnf))
       return false;
     // v2a: audio queries, video keys/values
     if ((_sp ? !attend_v2a_sp_(s, _v2a, _arp->qa, a.tokens, ac, _arp->kvv, v.tokens, vc,
                                _arp->att, err)
-             : !attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, v.tokens, ac, vc, _arp->att,
+             : !attend_(s, _v2a, _arp->qa, a.tokens, _arp->kvv, vnf, ac, vc, _arp->att,
                         err)) ||
         !out_proj_(s, _arp->att, _v2a.inner, _v2a.o, _v2a.o_b, a.x, a.tokens, ad,
                    am + MOD_AVG * ad, err, &_v2a.l_o))

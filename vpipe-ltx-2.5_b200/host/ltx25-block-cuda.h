@@ -160,6 +160,13 @@ public:
   // (see shard_io); the caller gathers x once after the last block.
   bool forward_shard(cudaStream_t s, StreamIO& video, StreamIO& audio, std::string* err);
   bool sequence_parallel() const { return _sp; }
+  // Whether a forward over `tokens` video tokens shards the video rows over
+  // the group: always under sequence parallelism; under tensor parallelism
+  // when the tokens split evenly over the ranks (the residual stream is then
+  // kept by token rows between the row-split and column-split products --
+  // reduce-scatter / all-gather instead of all-reduce -- and the per-token
+  // work runs on 1/world of the rows); never on one GPU.
+  bool shards_video(int tokens) const;
   // This rank's shard of a whole-sequence video io; false (with err) when
   // the tokens do not split evenly.
   bool shard_io(const StreamIO& whole, StreamIO* shard, std::string* err) const;
@@ -235,9 +242,15 @@ private:
   const LoraExt* lx_(const LoraSite& site, LoraExt* tmp) const;
   // x += gate * (att . Wo^T + bias), row-split and reduced under tensor
   // parallelism.
+  // With n_all > n (row-sharded residual), `in` holds all n_all token rows
+  // and x this rank's n: the partial is reduce-scattered to those rows.
   bool out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k, const QWeight& w,
                  const __nv_bfloat16* bias, __nv_bfloat16* x, int n, int d,
-                 const float* gate, std::string* err, const LoraSite* lora = nullptr);
+                 const float* gate, std::string* err, const LoraSite* lora = nullptr,
+                 int n_all = 0);
+  // All-gather this rank's n rows (in place at rank * n * d) of a
+  // [world * n][d] buffer on the current stream's communicator.
+  bool gather_rows_(cudaStream_t s, __nv_bfloat16* buf, int n, int d, std::string* err) const;
 
   CudaOps* _ops;
   int _vdim, _vheads, _adim, _aheads;
@@ -245,6 +258,7 @@ private:
   const Comm* _comm_side = nullptr;   // the side stream's (tensor parallel)
   const Comm* _ccur = nullptr;        // the communicator of the stream being issued
   int _tp_rank = 0, _tp_world = 1;
+  bool _tp_rows = true;          // tensor parallel: shard the residual by rows
   bool _sp = false;              // sequence parallel (weights whole)
   int _sp_rank = 0, _sp_world = 1;
   std::map<std::string, Staged> _staged;

@@ -2,6 +2,7 @@
 #include "ltx25-comm.h"
 
 #include <dlfcn.h>
+#include <cuda_bf16.h>
 #include <nccl.h>
 
 #include <cstring>
@@ -22,6 +23,7 @@ struct Nccl {
   decltype(&ncclGroupStart) group_start = nullptr;
   decltype(&ncclGroupEnd) group_end = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclReduceScatter) reduce_scatter = nullptr;
   decltype(&ncclCommSplit) comm_split = nullptr;
   bool ok = false;
   std::string why;
@@ -52,10 +54,12 @@ const Nccl& nccl()
     n.group_start = reinterpret_cast<decltype(n.group_start)>(dlsym(h, "ncclGroupStart"));
     n.group_end = reinterpret_cast<decltype(n.group_end)>(dlsym(h, "ncclGroupEnd"));
     n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
+    n.reduce_scatter =
+        reinterpret_cast<decltype(n.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
     n.comm_split = reinterpret_cast<decltype(n.comm_split)>(dlsym(h, "ncclCommSplit"));
     n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce &&
            n.error_string && n.send && n.recv && n.group_start && n.group_end &&
-           n.all_gather;
+           n.all_gather && n.reduce_scatter;
     if (!n.ok) n.why = "NCCL library lacks a required symbol";
   });
   return n;
@@ -169,6 +173,15 @@ bool Comm::allgather_bf16(const void* send, void* recv, size_t count, cudaStream
   return nccl_ok(nccl().all_gather(send, recv, count, ncclBfloat16,
                                    static_cast<ncclComm_t>(_comm), s),
                  "ncclAllGather", err);
+}
+
+bool Comm::reduce_scatter_bf16(void* buf, size_t count, cudaStream_t s, std::string* err) const
+{
+  if (_comm == nullptr || count == 0) return true;
+  __nv_bfloat16* b = static_cast<__nv_bfloat16*>(buf);
+  return nccl_ok(nccl().reduce_scatter(b, b + (size_t)_rank * count, count, ncclBfloat16,
+                                       ncclSum, static_cast<ncclComm_t>(_comm), s),
+                 "ncclReduceScatter", err);
 }
 
 }  // namespace ltx25

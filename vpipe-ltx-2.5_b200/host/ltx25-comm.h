@@ -36,6 +36,11 @@ public:
   bool allgather_bf16(const void* send, void* recv, size_t count, cudaStream_t s,
                       std::string* err) const;
 
+  // bf16 reduce-scatter in place: `buf` holds world * count elements on
+  // every rank; rank r's block [r * count, (r + 1) * count) ends as the sum
+  // of every rank's block r (the other blocks are left undefined).
+  bool reduce_scatter_bf16(void* buf, size_t count, cudaStream_t s, std::string* err) const;
+
   // A second communicator over the same ranks (ncclCommSplit), for
   // collectives issued on another stream.
   bool split(Comm* out, std::string* err) const;
