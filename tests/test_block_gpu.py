@@ -62,7 +62,10 @@ def test_ada_zero(ctx, rows, dim, norm):
 
 
 @pytest.mark.parametrize("heads,hd,rope,ld_extra", [(4, 64, True, 0), (3, 128, True, 128),
-                                                     (32, 128, True, 0), (2, 64, False, 64)])
+                                                     (32, 128, True, 0), (2, 64, False, 64),
+                                                     # register kernel: 2 / 8 / 4 rows a CTA
+                                                     (2, 128, True, 256), (4, 128, True, 0),
+                                                     (32, 64, True, 0)])
 def test_qk_norm_rope(ctx, heads, hd, rope, ld_extra):
     import torch
     import ltx25_b200 as L

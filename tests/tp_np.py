@@ -172,7 +172,9 @@ def block_forward_tp(t, video, audio, vdim, vheads, adim, aheads, rank, world, a
 # token rows between blocks, host/ltx25-block-cuda.cc `rows` paths) --------
 #
 # Rank r holds video rows [r*T/W, (r+1)*T/W) of x.  Each modulated input
-# (ada_zero, row-local) is formed for those rows and all-gathered; the
+# (ada_zero, row-local) is formed for those rows and all-gathered (for the
+# cross attentions x's rows are gathered once and both modulations formed
+# on all rows); the
 # sharded projections then see all T rows exactly as above; each row-split
 # product is reduce-scattered (here: summed over ranks, then the rank keeps
 # its rows) and the gated residual touches only the rank's rows.  The audio
@@ -214,13 +216,13 @@ def block_forward_tp_rows(t, video, audio, vdim, vheads, adim, aheads, rank, wor
     # audio first half, whole
     _first_half(t, "audio_", a, adim, aheads, tp)
     # cross attentions from the pre-cross state
-    vx_pre, ax_pre = vx.copy(), a["x"].copy()
+    vx_pre, ax_pre = allgather(vx), a["x"].copy()     # x's rows gathered once
     ahd = adim // aheads
     vtab = t["scale_shift_table_a2v_ca_video"]
     atab = t["scale_shift_table_a2v_ca_audio"]
     vsc, vsh, vg = block_np.av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 0)
     asc, ash, _ = block_np.av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 0)
-    qv = allgather(block_np.ada_zero(vx_pre, EPS, vsc, vsh))
+    qv = block_np.ada_zero(vx_pre, EPS, vsc, vsh)
     kva = block_np.ada_zero(ax_pre, EPS, asc, ash)
     o = _attn_tp(t, "audio_to_video_attn", qv, kva, v.get("cross_pe"), a.get("cross_pe"),
                  aheads, ahd, *tp)
@@ -228,7 +230,7 @@ def block_forward_tp_rows(t, video, audio, vdim, vheads, adim, aheads, rank, wor
     asc, ash, ag = block_np.av_ada(atab, a.get("cross_scale_shift"), a.get("cross_gate"), adim, 2)
     vsc, vsh, _ = block_np.av_ada(vtab, v.get("cross_scale_shift"), v.get("cross_gate"), vdim, 2)
     qa = block_np.ada_zero(ax_pre, EPS, asc, ash)
-    kvv = allgather(block_np.ada_zero(vx_pre, EPS, vsc, vsh))
+    kvv = block_np.ada_zero(vx_pre, EPS, vsc, vsh)
     o = _attn_tp(t, "video_to_audio_attn", qa, kvv, a.get("cross_pe"), v.get("cross_pe"),
                  aheads, ahd, *tp)
     a["x"] = (a["x"] + o * ag).astype(F32)

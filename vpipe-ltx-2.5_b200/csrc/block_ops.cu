@@ -267,6 +267,135 @@ __global__ void __launch_bounds__(kRowThreads)
   }
 }
 
+// The same op with each row held in registers: TR = quads / Q threads per
+// row, Q rotation quads (four pairs j..j+3 of one head, both halves) per
+// thread, 256 / TR rows per CTA.  One pass over the row: load, sum of
+// squares (warp shuffles, then the row's warps through shared memory),
+// normalize, gain, rotate, store -- no f32 copy of the row in shared
+// memory, and narrow rows (a tensor-parallel rank's heads) share a CTA.
+// Same arithmetic per element as qk_norm_rope_kernel; the sum of squares
+// is added in another order.
+template <int Q>
+__global__ void __launch_bounds__(kRowThreads)
+    qk_norm_rope_reg_kernel(const __nv_bfloat16* __restrict__ in, int ldi,
+                            __nv_bfloat16* __restrict__ out, int ldo, int heads,
+                            int head_dim, const float* __restrict__ gain,
+                            const float* __restrict__ cosb,
+                            const float* __restrict__ sinb, int tokens, float eps,
+                            const float* __restrict__ sumsq, int norm_width,
+                            int head0, int tbl_tokens, int tok0, int tr)
+{
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[kRowThreads / 32];
+  const int half = head_dim / 2;
+  const int rl = threadIdx.x / tr, li = threadIdx.x % tr;
+  const int t = blockIdx.x * (kRowThreads / tr) + rl;
+  const bool live = t < tokens;
+  const __nv_bfloat16* xr = in + (size_t)(live ? t : 0) * ldi;
+  float a[Q][4], b[Q][4];
+  int ia_[Q];
+  float ss = 0.0f;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const int idx = li + q * tr;
+    const int h = (idx * 4) / half, j = (idx * 4) % half;
+    const int ia = h * head_dim + j;
+    ia_[q] = ia;
+    uint2 ua = make_uint2(0u, 0u), ub = make_uint2(0u, 0u);
+    if (live) {
+      ua = *reinterpret_cast<const uint2*>(xr + ia);
+      ub = *reinterpret_cast<const uint2*>(xr + ia + half);
+    }
+    const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ua);
+    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&ub);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float2 fa = __bfloat1622float2(ha[e]), fb = __bfloat1622float2(hb[e]);
+      a[q][2 * e] = fa.x;
+      a[q][2 * e + 1] = fa.y;
+      b[q][2 * e] = fb.x;
+      b[q][2 * e + 1] = fb.y;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss = fmaf(a[q][e], a[q][e], fmaf(b[q][e], b[q][e], ss));
+  }
+  float total;
+  if (sumsq != nullptr) {
+    total = live ? sumsq[t] : 0.0f;
+  } else {
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[w] = ss;
+    __syncthreads();
+    const int w0 = (rl * tr) >> 5, nw = tr >> 5;
+    total = 0.0f;
+    for (int i = 0; i < nw; ++i) total += red[w0 + i];
+  }
+  if (!live) return;
+  const float inv = rsqrtf(total / (float)norm_width + eps);
+  __nv_bfloat16* orow = out + (size_t)t * ldo;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const int ia = ia_[q], ib = ia + half;
+    const int h = ia / head_dim, j = ia % head_dim;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      a[q][e] *= inv;
+      b[q][e] *= inv;
+    }
+    if (gain != nullptr) {
+      const float4 ga = *reinterpret_cast<const float4*>(gain + ia);
+      const float4 gb = *reinterpret_cast<const float4*>(gain + ib);
+      a[q][0] *= ga.x; a[q][1] *= ga.y; a[q][2] *= ga.z; a[q][3] *= ga.w;
+      b[q][0] *= gb.x; b[q][1] *= gb.y; b[q][2] *= gb.z; b[q][3] *= gb.w;
+    }
+    if (cosb != nullptr) {
+      const size_t o = ((size_t)(head0 + h) * tbl_tokens + tok0 + t) * half + j;
+      const float4 c4 = *reinterpret_cast<const float4*>(cosb + o);
+      const float4 s4 = *reinterpret_cast<const float4*>(sinb + o);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float ra = a[q][e] * cc[e] - b[q][e] * sn[e];
+        const float rb = b[q][e] * cc[e] + a[q][e] * sn[e];
+        a[q][e] = ra;
+        b[q][e] = rb;
+      }
+    }
+    uint2 wa, wb;
+    wa.x = pack2(a[q][0], a[q][1]);
+    wa.y = pack2(a[q][2], a[q][3]);
+    wb.x = pack2(b[q][0], b[q][1]);
+    wb.y = pack2(b[q][2], b[q][3]);
+    *reinterpret_cast<uint2*>(orow + ia) = wa;
+    *reinterpret_cast<uint2*>(orow + ib) = wb;
+  }
+}
+
+// One warp per row, eight rows per CTA: out[t] = the sum of squares of row
+// t's `cols` values (f32), for the tensor-parallel q/k norms.
+__global__ void __launch_bounds__(kRowThreads)
+    row_sumsq_warp_kernel(const __nv_bfloat16* __restrict__ in, int ldi, int rows, int cols,
+                          float* __restrict__ out)
+{
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= rows) return;
+  const __nv_bfloat16* xr = in + (size_t)t * ldi;
+  float ss = 0.0f;
+  for (int k = lane * 8; k < cols; k += 32 * 8) {
+    float v[8];
+    load8(xr + k, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) out[t] = ss;
+}
+
 // out[t] = sum of squares of row t's `cols` values (f32).
 __global__ void __launch_bounds__(kRowThreads)
     row_sumsq_kernel(const __nv_bfloat16* __restrict__ in, int ldi, int cols,
@@ -650,6 +779,26 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
       ((reinterpret_cast<uintptr_t>(gain) | reinterpret_cast<uintptr_t>(cosb) |
         reinterpret_cast<uintptr_t>(sinb)) & 15u) != 0)
     return -2;
+  // The register form when a row's rotation quads split into whole warps
+  // that tile a CTA: Q = 4 quads a thread (2 for narrow rows).
+  const int half = head_dim / 2;
+  const int quads = heads * half / 4;
+  if (half % 4 == 0 && ldi % 4 == 0 && ldo % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(in) & 7u) == 0 && (reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
+    for (const int Q : {4, 2}) {
+      const int tr = quads / Q;
+      if (quads % Q != 0 || tr % 32 != 0 || tr > kRowThreads || kRowThreads % tr != 0) continue;
+      const int rpb = kRowThreads / tr;
+      const dim3 grid((unsigned)((rows + rpb - 1) / rpb));
+      const int nw = norm_width > 0 ? norm_width : inner;
+      const int tt = tbl_tokens > 0 ? tbl_tokens : rows;
+      if (Q == 4)
+        launch_k(qk_norm_rope_reg_kernel<4>, grid, dim3(kRowThreads), 0, s, 1, in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq, nw, head0, tt, tok0, tr);
+      else
+        launch_k(qk_norm_rope_reg_kernel<2>, grid, dim3(kRowThreads), 0, s, 1, in, ldi, out, ldo, heads, head_dim, gain, cosb, sinb, rows, eps, sumsq, nw, head0, tt, tok0, tr);
+      return launched();
+    }
+  }
   const size_t smem = (size_t)inner * sizeof(float);
   if (smem > 48 * 1024) {
     static std::atomic<unsigned long long> attr{0};
@@ -689,6 +838,11 @@ int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,
 {
   if (rows <= 0) return 0;
   if (cols % 8 != 0 || ldi % 8 != 0) return -2;
+  if (cols <= 2048) {
+    const int rpb = kRowThreads / 32;
+    launch_k(row_sumsq_warp_kernel, dim3((unsigned)((rows + rpb - 1) / rpb)), dim3(kRowThreads), 0, s, 1, in, ldi, rows, cols, out);
+    return launched();
+  }
   launch_k(row_sumsq_kernel, dim3(rows), dim3(kRowThreads), 0, s, 1, in, ldi, cols, out);
   return launched();
 }

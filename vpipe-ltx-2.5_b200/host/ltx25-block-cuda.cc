@@ -958,24 +958,26 @@ bool CudaBlock::forward_impl_(cudaStream_t s, StreamIO& v, StreamIO& a, std::str
         ltx::launch_vec_add(_audio.cross_table, a.cross_scale_shift, am + MOD_AV * ad, 4 * ad, s) ||
         ltx::launch_vec_add(_audio.cross_table + 4 * ad, a.cross_gate, am + MOD_AVG * ad, ad, s))
       return fail(err, "cross adaLN launch failed");
-    // Row-sharded residual (tensor parallel): both modulations of this
-    // rank's video rows are formed in place and gathered to all rows.
+    // Row-sharded residual (tensor parallel): x's rows are gathered once
+    // (into the idle `normed` buffer) and both video modulations formed on
+    // all rows, one all-gather instead of two.
     const bool vrows = _tp_world > 1 && v.tokens_all > v.tokens;
     const int vn = v.tokens, vnf = vrows ? v.tokens_all : vn;
-    const size_t voff = vrows ? (size_t)_tp_rank * vn * vd : 0;
+    const __nv_bfloat16* vxs = v.x;
+    if (vrows) {
+      if (!_comm->allgather_bf16(v.x, _arp->normed, (size_t)vn * vd, s, err)) return false;
+      vxs = _arp->normed;
+    }
     // av rows: [scale(lo=0), shift(lo=0), scale(lo=2), shift(lo=2)]
-    if (ltx::launch_ada_zero(v.x, vd, _arp->qv + voff, vd, vn, vd, vm + (MOD_AV + 0) * vd,
+    if (ltx::launch_ada_zero(vxs, vd, _arp->qv, vd, vnf, vd, vm + (MOD_AV + 0) * vd,
                              vm + (MOD_AV + 1) * vd, kEps, true, s) ||
         ltx::launch_ada_zero(a.x, ad, _arp->kva, ad, a.tokens, ad, am + (MOD_AV + 0) * ad,
                              am + (MOD_AV + 1) * ad, kEps, true, s) ||
         ltx::launch_ada_zero(a.x, ad, _arp->qa, ad, a.tokens, ad, am + (MOD_AV + 2) * ad,
                              am + (MOD_AV + 3) * ad, kEps, true, s) ||
-        ltx::launch_ada_zero(v.x, vd, _arp->kvv + voff, vd, vn, vd, vm + (MOD_AV + 2) * vd,
+        ltx::launch_ada_zero(vxs, vd, _arp->kvv, vd, vnf, vd, vm + (MOD_AV + 2) * vd,
                              vm + (MOD_AV + 3) * vd, kEps, true, s))
       return fail(err, "cross ada_zero launch failed");
-    if (vrows && (!gather_rows_(s, _arp->qv, vn, vd, err) ||
-                  !gather_rows_(s, _arp->kvv, vn, vd, err)))
-      return false;
     // a2v: video queries, audio keys/values
     const RopeRef vc = vrows ? RopeRef{v.cpe_cos, v.cpe_sin, vnf, 0}
                              : RopeRef{v.cpe_cos, v.cpe_sin,
