@@ -37,7 +37,9 @@ def fold(w, a, b):
     """W + B . A with f64 sums, stored f32 (tests/ltx25-lora-apply-test.cc:
     357-370).  w [N][K], a [rank][K], b [N][rank]."""
     ba = np.asarray(b, F32).astype(F64) @ np.asarray(a, F32).astype(F64)
-    return (np.asarray(w, F32) + ba).astype(F32)
+    # each f64 sum is rounded to f32 first, then added in f32, as the
+    # reference's `w.v[...] += (float)acc` does
+    return (np.asarray(w, F32) + ba.astype(F32)).astype(F32)
 
 
 def make_pair(rng, rank, k, n):

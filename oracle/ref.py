@@ -59,6 +59,11 @@ def load():
         lib.ref_build_cross_rope.argtypes = [P, P, I, I, I, I, P, P]
         lib.ref_video_time_seconds.argtypes = [I, I, ctypes.c_double, I, P]
         lib.ref_audio_time_seconds.argtypes = [I, P]
+        lib.ref_adaln_chain.argtypes = [ctypes.c_double, P, P, P, P, P, P, I, I, P, P]
+        lib.ref_adaln_chain.restype = I
+        lib.ref_lora_gemv.argtypes = [P, P, P, I, I, I, P]
+        lib.ref_lora_fold.argtypes = [P, P, P, I, I, I]
+        lib.ref_lora_scale.argtypes = [P, P, ctypes.c_size_t, ctypes.c_double]
         _LIB = lib
     return _LIB
 
@@ -142,6 +147,48 @@ def audio_time_seconds(tokens):
     out = np.zeros(tokens, np.float64)
     load().ref_audio_time_seconds(tokens, _p(out))
     return out
+
+
+def adaln_chain(t, w1, b1, w2, b2, w3, b3):
+    """Ltx25Dit::adaln_ over the reference's own host helpers
+    (src/ltx25-dit.cc:30-160): returns (driver, embedded_timestep) f32.
+    Weights / biases are bf16 bits [out][in] / [out] (biases may be None)."""
+    arrs = [None if a is None else np.ascontiguousarray(a, dtype=np.uint16)
+            for a in (w1, b1, w2, b2, w3, b3)]
+    dim, out_dim = arrs[0].shape[0], arrs[4].shape[0]
+    out = np.zeros(out_dim, np.float32)
+    emb = np.zeros(dim, np.float32)
+    load().ref_adaln_chain(float(t), *[_p(a) for a in arrs], dim, out_dim, _p(out), _p(emb))
+    return out, emb
+
+
+def lora_gemv(x, a_bits, b_bits, y):
+    """y + B (A x): the reference's host adapter GEMV (src/ltx25-dit.cc:77-103)."""
+    a = np.ascontiguousarray(a_bits, np.uint16)
+    b = np.ascontiguousarray(b_bits, np.uint16)
+    xx = np.ascontiguousarray(x, np.float32)
+    yy = np.ascontiguousarray(y, np.float32).copy()
+    load().ref_lora_gemv(_p(xx), _p(a), _p(b), a.shape[0], a.shape[1], b.shape[0], _p(yy))
+    return yy
+
+
+def lora_fold(w, a, b):
+    """W + B A by the reference adapter test's fold
+    (tests/ltx25-lora-apply-test.cc:353-366); f32 values."""
+    ww = np.ascontiguousarray(w, np.float32).copy()
+    aa = np.ascontiguousarray(a, np.float32)
+    bb = np.ascontiguousarray(b, np.float32)
+    load().ref_lora_fold(_p(ww), _p(aa), _p(bb), aa.shape[0], aa.shape[1], bb.shape[0])
+    return ww
+
+
+def lora_scale(a_bits, factor):
+    """bf16 bits of A with the factor folded in as scaled_ does it
+    (src/ltx25-lora.cc:53-67)."""
+    s = np.ascontiguousarray(a_bits, np.uint16)
+    d = np.empty_like(s)
+    load().ref_lora_scale(_p(s), _p(d), s.size, float(factor))
+    return d
 
 
 class RefBlock:

@@ -25,6 +25,31 @@ namespace refpack {
 #include "ref_packer.inc"        // reference test helpers, verbatim
 }  // namespace refpack
 
+// The host adaLN chain's helpers of src/ltx25-dit.cc:30-135, verbatim, over
+// shims of the two vpipe types they read (a bf16 buffer's contents() /
+// empty(), an adapter pair's widths and buffers).
+namespace refdit {
+struct SharedBuffer {
+  const void* p = nullptr;
+  const void* contents() const { return p; }
+  bool empty() const { return p == nullptr; }
+};
+struct LoraPair {
+  SharedBuffer a, b;
+  int rank = 0, k = 0, n = 0;
+  bool valid() const { return rank > 0 && a.p != nullptr && b.p != nullptr; }
+};
+#include "ref_dit.inc"
+}  // namespace refdit
+
+// The adapter test's CPU fold (tests/ltx25-lora-apply-test.cc:330-366) and
+// the bf16 rounding src/ltx25-lora.cc's scaled_ folds the factor with
+// (lines 27-47), verbatim.
+namespace reflora {
+#include "ref_lora_test.inc"
+#include "ref_lora_bits.inc"
+}  // namespace reflora
+
 namespace {
 
 void put_err(char* err, int errlen, const std::string& m)
@@ -257,6 +282,70 @@ void ref_audio_time_seconds(int tokens, double* out)
 {
   const std::vector<double> v = ltx25::audio_time_seconds(tokens);
   std::memcpy(out, v.data(), v.size() * sizeof(double));
+}
+
+// Ltx25Dit::adaln_ (src/ltx25-dit.cc:137-160) without adapters, driven
+// through the reference's own helpers: sinusoid(t) -> linear_1 -> SiLU ->
+// linear_2 (= embedded) -> SiLU -> linear.  Weights and biases bf16 bits
+// ([out][in]); bias pointers may be null.
+int ref_adaln_chain(double t, const uint16_t* w1, const uint16_t* b1, const uint16_t* w2,
+                    const uint16_t* b2, const uint16_t* w3, const uint16_t* b3, int dim,
+                    int out_dim, float* out, float* embedded)
+{
+  using refdit::SharedBuffer;
+  const SharedBuffer W1{w1}, B1{b1}, W2{w2}, B2{b2}, W3{w3}, B3{b3};
+  std::vector<float> proj = refdit::timestep_sinusoid_(t, 256);
+  std::vector<float> h1, h2, o;
+  refdit::gemv_host_(proj, W1, B1, 256, dim, h1);
+  refdit::silu_(h1);
+  refdit::gemv_host_(h1, W2, B2, dim, dim, h2);
+  if (embedded != nullptr) std::memcpy(embedded, h2.data(), h2.size() * sizeof(float));
+  std::vector<float> act = h2;
+  refdit::silu_(act);
+  refdit::gemv_host_(act, W3, B3, dim, out_dim, o);
+  std::memcpy(out, o.data(), o.size() * sizeof(float));
+  return 0;
+}
+
+// y[n] += B (A x): the reference's host adapter GEMV (lora_gemv_host_,
+// src/ltx25-dit.cc:77-103); a [rank][k], b [n][rank] bf16 bits.
+void ref_lora_gemv(const float* x, const uint16_t* a, const uint16_t* b, int rank, int k,
+                   int n, float* y)
+{
+  refdit::LoraPair p;
+  p.a.p = a;
+  p.b.p = b;
+  p.rank = rank;
+  p.k = k;
+  p.n = n;
+  std::vector<float> xv(x, x + k), yv(y, y + n);
+  refdit::lora_gemv_host_(xv, p, yv);
+  std::memcpy(y, yv.data(), (size_t)n * sizeof(float));
+}
+
+// W[n][k] += B A with the adapter test's fold (f32 values).
+void ref_lora_fold(float* w, const float* a, const float* b, int rank, int k, int n)
+{
+  ltx25::Mat m;
+  m.rows = n;
+  m.cols = k;
+  m.v.assign(w, w + (size_t)n * k);
+  reflora::HostPair p;
+  p.a.assign(a, a + (size_t)rank * k);
+  p.b.assign(b, b + (size_t)n * rank);
+  p.rank = rank;
+  p.k = k;
+  p.n = n;
+  reflora::fold(m, p);
+  std::memcpy(w, m.v.data(), (size_t)n * k * sizeof(float));
+}
+
+// The factor folded into A as scaled_ does it (src/ltx25-lora.cc:63):
+// d = f32_to_bf16_(bf16_to_f32_(s) * (float)factor), element by element.
+void ref_lora_scale(const uint16_t* s, uint16_t* d, size_t n, double factor)
+{
+  for (size_t i = 0; i < n; ++i)
+    d[i] = reflora::f32_to_bf16_(reflora::bf16_to_f32_(s[i]) * (float)factor);
 }
 
 }  // extern "C"

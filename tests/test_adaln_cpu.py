@@ -31,6 +31,24 @@ def test_chain_matches_restatement(t):
     a.close()
 
 
+@pytest.mark.parametrize("t", [0.0, 37.5, 999.0])
+def test_chain_matches_the_reference_helpers(t):
+    """The library's host chain against Ltx25Dit::adaln_'s own helpers
+    (timestep_sinusoid_, gemv_host_, silu_; src/ltx25-dit.cc:30-160),
+    compiled from the reference sources into oracle/_ref."""
+    from oracle import ref
+    if not ref.available():
+        pytest.skip("oracle/_ref not built (no reference tree at build time)")
+    import ltx25_b200 as L
+    w = _weights(4)
+    a = L.AdaLN(*w)
+    out, emb = a(t)
+    want, want_emb = ref.adaln_chain(t, *w)
+    assert lib.rel_l2(out, want) < 1e-6
+    assert lib.rel_l2(emb, want_emb) < 1e-6
+    a.close()
+
+
 def test_controls_and_threads():
     import ltx25_b200 as L
     w = _weights(2)

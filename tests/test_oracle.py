@@ -7,7 +7,7 @@ present here the restatement is also checked against it live.
 import numpy as np
 import pytest
 
-from oracle import block_np, lib, ref, rope_np
+from oracle import block_np, lib, lora_np, ref, rope_np
 
 
 def test_pack_matches_reference_golden(golden):
@@ -159,3 +159,50 @@ def test_restatement_vs_live_reference():
         b = ref.pack(w, bits, group)
         for x, y in zip(a, b):
             assert np.array_equal(x, y)
+
+
+# ---- the trunk's adaLN chain and the adapters, pinned to the reference's own
+# host helpers (src/ltx25-dit.cc:30-160, src/ltx25-lora.cc:27-67,
+# tests/ltx25-lora-apply-test.cc:330-366, compiled into oracle/_ref)
+
+def _need_ref():
+    from oracle import ref
+    if not ref.available():
+        pytest.skip("oracle/_ref not built (no reference tree at build time)")
+    return ref
+
+
+@pytest.mark.parametrize("t", [0.0, 1.0, 500.0, 999.0])
+def test_adaln_restatement_matches_the_reference_chain(t):
+    ref = _need_ref()
+    from oracle import adaln_np
+    rng = np.random.default_rng(5)
+    f = lambda *s, sc=1.0: lib.f32_to_bf16((rng.standard_normal(s) * sc).astype(np.float32))
+    w = (f(96, 256, sc=0.1), f(96, sc=0.1), f(96, 96, sc=0.15), f(96, sc=0.1),
+         f(4 * 96, 96, sc=0.15), f(4 * 96, sc=0.1))
+    out, emb = ref.adaln_chain(t, *w)
+    want, want_emb = adaln_np.chain(t, *w)
+    assert lib.rel_l2(want, out) < 1e-6 and lib.rel_l2(want_emb, emb) < 1e-6
+    # a chain without biases (the reference's gemv_host_ takes an empty b)
+    out0, _ = ref.adaln_chain(t, w[0], None, w[2], None, w[4], None)
+    want0, _ = adaln_np.chain(t, w[0], None, w[2], None, w[4], None)
+    assert lib.rel_l2(want0, out0) < 1e-6
+
+
+def test_lora_restatements_match_the_reference_helpers():
+    ref = _need_ref()
+    rng = np.random.default_rng(9)
+    a_bits, b_bits = lora_np.make_pair(rng, 7, 96, 40)
+    a, b = lib.bf16_to_f32(a_bits), lib.bf16_to_f32(b_bits)
+    w = (rng.standard_normal((40, 96)) * 0.05).astype(np.float32)
+    # W += B A: the test's fold, exactly (same f64 sum order per element)
+    assert np.array_equal(lora_np.fold(w, a, b), ref.lora_fold(w, a, b))
+    # the factor folded into A: one RNE rounding, bit for bit
+    for factor in (1.0, 0.5, 0.37, 2.5):
+        assert np.array_equal(lora_np.fold_scale(a_bits, factor), ref.lora_scale(a_bits, factor))
+    # one row's delta against the reference's host adapter GEMV
+    x = rng.standard_normal(96).astype(np.float32)
+    y0 = rng.standard_normal(40).astype(np.float32)
+    got = ref.lora_gemv(x, a_bits, b_bits, y0)
+    want = y0.astype(np.float64) + lora_np.delta(x[None, :], a, b)[0]
+    assert lib.rel_l2(got, want) < 1e-6
