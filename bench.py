@@ -1535,6 +1535,83 @@ def q1_sample_desc():
             f"packed and dequantized once outside the timing")
 
 
+# ------------------------------------------------- dense GEMM against cuBLAS
+def run_cublas_ab(args):
+    """The dense tcgen05 GEMM (gemm_tc_kernel<MODE_BF16>, the expand-once
+    route's second half) against cuBLAS (torch.matmul, a library GEMM) on
+    the six M=8160 sweep shapes with the same bf16 operands, arms
+    interleaved step by step so clocks and power fall on both alike.  The
+    comparison DESIGN's dense-GEMM figures quote."""
+    import numpy as np
+    import torch
+    import ltx25_b200 as L
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = L.Context(0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    rows = []
+    tot = {"ours": 0.0, "cublas": 0.0}
+    fl_all = 0.0
+    n0 = L.launch_count()
+    with ClockSampler(gpu_index(0)) as clk:
+        for name, M, K, N in SHAPES:
+            if M <= 1024:
+                continue
+            x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+            w = (torch.randn((N, K), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+            qw = L.QWeight.upload_dense(ctx, w.view(torch.int16).cpu().numpy().view(np.uint16),
+                                        N, K)
+            y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+            arms = {"ours": lambda: L.qlinear(ctx, qw, x, out=y),
+                    "cublas": lambda: torch.matmul(x, w.t(), out=y)}
+            for _ in range(args.warmup):
+                for f in arms.values():
+                    f()
+            evs = {a: [] for a in arms}
+            for i in range(args.steps):
+                for a in (list(arms) if i % 2 == 0 else list(arms)[::-1]):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    arms[a]()
+                    e1.record()
+                    evs[a].append((e0, e1))
+            torch.cuda.synchronize()
+            ctx.check()
+            fl = flops(M, K, N)
+            row = {"shape": name, "M": M, "K": K, "N": N}
+            for a in arms:
+                ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in evs[a]])
+                tot[a] += ms * args.steps
+                row[a + "_tflops"] = round(fl / (ms * 1e-3) / 1e12, 1)
+            row["ratio"] = round(row["ours_tflops"] / row["cublas_tflops"], 3)
+            fl_all += fl * args.steps
+            rows.append(row)
+            qw.free()
+            del x, w, y
+    launches = L.launch_count() - n0
+    ours = fl_all / (tot["ours"] * 1e-3) / 1e12
+    cub = fl_all / (tot["cublas"] * 1e-3) / 1e12
+    pk = tensor_peak_for(tot["ours"] * 1e-3 / 2)
+    line = {
+        "metric": "dense bf16 tcgen05 GEMM vs cuBLAS, six M=8160 sweep shapes",
+        "value": round(ours, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic N(0,1) x, N(0,0.02) bf16 weights",
+        "config": {"workload": "gemm_tc_kernel<MODE_BF16> vs torch.matmul, arms interleaved"},
+        "cublas_tflops": round(cub, 1), "ratio_to_cublas": round(ours / cub, 3),
+        "per_shape": rows, "gpu_launches": int(launches),
+        "roofline": dict({"bound": "tensor", "achieved": round(ours, 1), "peak": pk["peak"],
+                          "peak_source": pk["kind"], "unit": "TFLOP/s",
+                          "frac": round(ours / pk["peak"], 4), "traffic": None},
+                         **roofline_fracs(ours, pk, clk.summary())),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
 # ------------------------------------------------------------- reference arm
 def run_reference(args):
     """--impl reference: the reference's own CPU implementation of the path
@@ -1667,7 +1744,7 @@ def main():
                     help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="stack",
                     choices=["stack", "sweep", "qlinear", "block", "attn", "lora", "trunk",
-                             "connector", "adaln", "i8"],
+                             "connector", "adaln", "i8", "cublas_ab"],
                     help="stack: BASELINE config 5, the 48-block denoise step (the "
                          "headline, carrying the config-2 sweep); sweep: config 2 alone; "
                          "qlinear: config 1; i8: config 3; block: config 4")
@@ -1681,7 +1758,8 @@ def main():
         return run_reference(args)
     runs = {"stack": run_stack, "sweep": run_sweep, "qlinear": run_qlinear,
             "block": run_block, "attn": run_attn, "lora": run_lora, "trunk": run_trunk,
-            "connector": run_connector, "adaln": run_adaln, "i8": run_i8}
+            "connector": run_connector, "adaln": run_adaln, "i8": run_i8,
+            "cublas_ab": run_cublas_ab}
     return runs[args.workload](args)
 
 

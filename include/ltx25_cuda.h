@@ -166,7 +166,11 @@ LTX_API int ltx_qlinear(ltx_ctx* ctx, const ltx_qweight* w, const void* x,
  *   - The array (32 MiB + 64 KiB) is held by every GPU that loads the
  *     library until the process exits.  The first call on a device looks up
  *     its address (cudaGetSymbolAddress, with that device current); make
- *     that first call before any stream capture.
+ *     that first call before any stream capture.  The address is kept for
+ *     the life of the process: after cudaDeviceReset (or the primary
+ *     context's release and re-creation) the module loads at another
+ *     address, so a process that resets a device must not call this entry
+ *     point on that device again.
  *   - All calls on a device share the array and it keeps the last call's
  *     contents; calls whose kernels overlap on the GPU race on it. */
 #define LTX_I8_STATIC_MAX_CODES 33554432

@@ -1179,10 +1179,13 @@ __global__ void __launch_bounds__(256)
 {
   pdl_wait();
   pdl_trigger();
-  __shared__ __nv_bfloat16 tile[64][64 + 8];
-  const int t0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
-  // load: 64 rows x 64 columns, 8 columns (16 B) per thread
-  for (int i = threadIdx.x; i < 64 * 8; i += 256) {
+  // A 128-token x 64-column tile a CTA, four 16-byte loads and stores a
+  // thread.  Rows of 66 elements (33 words) put the load phase's element
+  // stores and the store phase's column reads on distinct banks; each
+  // column's 16 tokens of a store step are one 32-byte sector of vt.
+  __shared__ __nv_bfloat16 tile[128][66];
+  const int t0 = blockIdx.x * 128, c0 = blockIdx.y * 64;
+  for (int i = threadIdx.x; i < 128 * 8; i += 256) {
     const int rr = i >> 3, cc = (i & 7) * 8;
     uint4 w = make_uint4(0, 0, 0, 0);
     if (t0 + rr < tk && c0 + cc < cols)
@@ -1192,8 +1195,9 @@ __global__ void __launch_bounds__(256)
     for (int k = 0; k < 8; ++k) tile[rr][cc + k] = e[k];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 64 * 8; i += 256) {
-    const int cc = i >> 3, rr = (i & 7) * 8;
+  for (int i = threadIdx.x; i < 128 * 8; i += 256) {
+    const int j = i & 127;
+    const int cc = j >> 1, rr = (i >> 7) * 16 + (j & 1) * 8;
     if (c0 + cc >= cols || t0 + rr >= tk) continue;
     __align__(16) __nv_bfloat16 e[8];
 #pragma unroll
@@ -1358,7 +1362,7 @@ int prepare_vt(const __nv_bfloat16* v, int ldv, int tk, int cols, int D, __nv_bf
                CUtensorMap* map, cudaStream_t s)
 {
   const int ldvt = (tk + 7) / 8 * 8;
-  launch_k(transpose_kernel, dim3(dim3((tk + 63) / 64, (cols + 63) / 64)), dim3(256), 0, s, 1, v, ldv, tk, cols, vt, ldvt);
+  launch_k(transpose_kernel, dim3(dim3((tk + 127) / 128, (cols + 63) / 64)), dim3(256), 0, s, 1, v, ldv, tk, cols, vt, ldvt);
   if (launched() != 0) return -1;
   return fa_encode(map, vt, (uint64_t)tk, (uint64_t)cols, (uint64_t)ldvt * 2, 64, D) ? 0 : -1;
 }

@@ -92,11 +92,13 @@ __global__ void vec_add_kernel(const float* __restrict__ a,
 
 // out = (rms_norm(x) if norm) * (1 + scale) + shift.  scale/shift may be
 // null (0).  dim % 8 == 0; a thread owns 8-element chunks of ROWS rows, so
-// the f32 scale/shift vectors are read once per CTA thread (not per row)
-// and ROWS rows of loads are in flight together.  Per row the arithmetic
-// and the reduction order are those of a one-row CTA.
+// ROWS rows of loads are in flight together.  The rows stay in registers as
+// raw bf16 (4 registers a chunk, widened when used) and the f32 scale/shift
+// chunks are read only after the reduction, so the kernel fits three CTAs
+// on an SM (12 rows in flight) where a float-resident form fits two.  Per
+// row the arithmetic and the reduction order are those of a one-row CTA.
 template <bool NORM, int ROWS, int CH>
-__global__ void __launch_bounds__(kRowThreads)
+__global__ void __launch_bounds__(kRowThreads, 3)
     row_mod_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                    __nv_bfloat16* __restrict__ out, int ldo, int rows, int dim,
                    const float* __restrict__ scale,
@@ -106,28 +108,7 @@ __global__ void __launch_bounds__(kRowThreads)
   pdl_trigger();
   __shared__ float red[ROWS][33];
   const int r0 = blockIdx.x * ROWS;
-  float sc[CH][8], sh[CH][8];
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    const int k = (c * kRowThreads + threadIdx.x) * 8;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sc[c][i] = sh[c][i] = 0.0f;
-    if (k < dim) {
-      if (scale != nullptr) {
-        const float4 a = *reinterpret_cast<const float4*>(scale + k);
-        const float4 b = *reinterpret_cast<const float4*>(scale + k + 4);
-        sc[c][0] = a.x; sc[c][1] = a.y; sc[c][2] = a.z; sc[c][3] = a.w;
-        sc[c][4] = b.x; sc[c][5] = b.y; sc[c][6] = b.z; sc[c][7] = b.w;
-      }
-      if (shift != nullptr) {
-        const float4 a = *reinterpret_cast<const float4*>(shift + k);
-        const float4 b = *reinterpret_cast<const float4*>(shift + k + 4);
-        sh[c][0] = a.x; sh[c][1] = a.y; sh[c][2] = a.z; sh[c][3] = a.w;
-        sh[c][4] = b.x; sh[c][5] = b.y; sh[c][6] = b.z; sh[c][7] = b.w;
-      }
-    }
-  }
-  float v[ROWS][CH][8];
+  uint4 v[ROWS][CH];
   float ss[ROWS];
 #pragma unroll
   for (int r = 0; r < ROWS; ++r) {
@@ -136,11 +117,22 @@ __global__ void __launch_bounds__(kRowThreads)
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int k = (c * kRowThreads + threadIdx.x) * 8;
-      if (live && k < dim) {
-        load8(x + (size_t)(r0 + r) * ldx + k, v[r][c]);
-        if (NORM) {
+      v[r][c] = make_uint4(0u, 0u, 0u, 0u);
+      if (live && k < dim)
+        v[r][c] = *reinterpret_cast<const uint4*>(x + (size_t)(r0 + r) * ldx + k);
+    }
+  }
+  if (NORM) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) ss[r] = fmaf(v[r][c][i], v[r][c][i], ss[r]);
+    for (int r = 0; r < ROWS; ++r) {
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[r][c]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 t = __bfloat1622float2(h[i]);
+          ss[r] = fmaf(t.x, t.x, ss[r]);
+          ss[r] = fmaf(t.y, t.y, ss[r]);
         }
       }
     }
@@ -171,15 +163,35 @@ __global__ void __launch_bounds__(kRowThreads)
     for (int r = 0; r < ROWS; ++r) inv[r] = rsqrtf(red[r][32] / (float)dim + eps);
   }
 #pragma unroll
-  for (int r = 0; r < ROWS; ++r) {
-    if (r0 + r >= rows) break;
+  for (int c = 0; c < CH; ++c) {
+    const int k = (c * kRowThreads + threadIdx.x) * 8;
+    if (k >= dim) continue;
+    float sc[8], sh[8];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int k = (c * kRowThreads + threadIdx.x) * 8;
-      if (k >= dim) continue;
+    for (int i = 0; i < 8; ++i) sc[i] = sh[i] = 0.0f;
+    if (scale != nullptr) {
+      const float4 a = *reinterpret_cast<const float4*>(scale + k);
+      const float4 b = *reinterpret_cast<const float4*>(scale + k + 4);
+      sc[0] = a.x; sc[1] = a.y; sc[2] = a.z; sc[3] = a.w;
+      sc[4] = b.x; sc[5] = b.y; sc[6] = b.z; sc[7] = b.w;
+    }
+    if (shift != nullptr) {
+      const float4 a = *reinterpret_cast<const float4*>(shift + k);
+      const float4 b = *reinterpret_cast<const float4*>(shift + k + 4);
+      sh[0] = a.x; sh[1] = a.y; sh[2] = a.z; sh[3] = a.w;
+      sh[4] = b.x; sh[5] = b.y; sh[6] = b.z; sh[7] = b.w;
+    }
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      if (r0 + r >= rows) break;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[r][c]);
       float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = fmaf(v[r][c][i] * inv[r], 1.0f + sc[c][i], sh[c][i]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 t = __bfloat1622float2(h[i]);
+        o[2 * i] = fmaf(t.x * inv[r], 1.0f + sc[2 * i], sh[2 * i]);
+        o[2 * i + 1] = fmaf(t.y * inv[r], 1.0f + sc[2 * i + 1], sh[2 * i + 1]);
+      }
       store8(out + (size_t)(r0 + r) * ldo + k, o);
     }
   }

@@ -43,7 +43,8 @@ void* g_addr[kMaxDevices] = {};
 
 // The device address of the array on `device`.  Looked up once per device,
 // with that device current (the name g_i8_static is only a host-side handle
-// in this file, not a device address); later calls read the cached pointer.
+// in this file, not a device address); later calls read the cached pointer,
+// which a device reset would leave stale (the header says so).
 bool i8_static_scratch(int device, int8_t** codes, float** scales, std::string* err)
 {
   if (device < 0 || device >= kMaxDevices) {

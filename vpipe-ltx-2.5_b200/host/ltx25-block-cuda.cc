@@ -594,6 +594,8 @@ bool CudaBlock::reserve(int max_video, int max_audio, int max_text,
   if (!_ops->reserve_attention((int)mx({vt, at, tt}),
                                std::max(_video.attn1.inner, _audio.attn1.inner), err))
     return false;
+  // The audio stream's attentions on the side stream have their own V^T.
+  if (!_ops->reserve_attention_side((int)mx({at, tt}), _audio.attn1.inner, err)) return false;
   // v2a (audio queries over every video key) splits over the keys.
   if (!_ops->reserve_split((int)at, (int)vt, _v2a.heads, _v2a.head_dim, err)) return false;
   if (_ops->sage_on() &&

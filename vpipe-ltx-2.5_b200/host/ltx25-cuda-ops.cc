@@ -97,6 +97,7 @@ CudaOps::~CudaOps()
     if (e != nullptr) cudaEventDestroy(e);
   if (_aux != nullptr) cudaStreamDestroy(_aux);
   cudaFree(_vt);
+  cudaFree(_vt_side);
   cudaFree(_part);
   cudaFree(_sb.qi8);
   cudaFree(_sb.ki8);
@@ -170,7 +171,8 @@ size_t CudaOps::scratch_bytes() const
 {
   size_t b = 0;
   if (_xq_bytes > 0) b += _xq_bytes + _xq_bytes / 64 * sizeof(float) + 1024;
-  b += _deq_bytes + _vt_elems * sizeof(__nv_bfloat16) + _part_elems * sizeof(float);
+  b += _deq_bytes + (_vt_elems + _vt_side_elems) * sizeof(__nv_bfloat16) +
+       _part_elems * sizeof(float);
   b += _sb.cap.qi8 + _sb.cap.ki8 + (_sb.cap.scales + _sb.cap.mean) * sizeof(float);
   b += (size_t)_ones_n * sizeof(float) + _lora_r_elems * sizeof(__nv_bfloat16);
   if (_tr_elems[0] > 0) b += _tr_elems[0] * 2 + 256;
@@ -568,6 +570,20 @@ bool CudaOps::reserve_attention(int keys, int width, std::string* err)
   return true;
 }
 
+bool CudaOps::reserve_attention_side(int keys, int width, std::string* err)
+{
+  const size_t need = ltx::attention_tc_scratch(keys, 1, width);
+  if (need <= _vt_side_elems) return true;
+  cudaFree(_vt_side);
+  _vt_side = nullptr;
+  _vt_side_elems = 0;
+  if (!cuda_ok(cudaMalloc(&_vt_side, need * sizeof(__nv_bfloat16)),
+               "cudaMalloc(side attention scratch)", err))
+    return false;
+  _vt_side_elems = need;
+  return true;
+}
+
 bool CudaOps::reserve_sage(int tq, int tk, int heads, int head_dim, std::string* err)
 {
   const ltx::SageScratch need = ltx::sage_scratch_need(tq, tk, heads, head_dim);
@@ -621,7 +637,8 @@ bool CudaOps::audio_side_ok(int tokens, int text_tokens, int heads, int head_dim
   const int m = std::max(tokens, text_tokens);
   if (m >= LTX_DEQUANT_MIN_M || (_i8 && m >= 1024) || _route == Route::DequantOnce) return false;
   if (sage_for(layer, head_dim)) return false;
-  if (head_dim == 128) return false;   // would take the tcgen05 kernel and its scratch
+  // only 64-wide heads (this model's audio stream) go to the side stream
+  if (head_dim == 128) return false;
   return ltx::attention_tc_splits(tokens, tokens, heads) == 1 &&
          ltx::attention_tc_splits(tokens, text_tokens, heads) == 1;
 }
@@ -654,16 +671,28 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
     if (!reserve_sage(tq, tk, heads, head_dim, err)) return false;
     rc = ltx::launch_sage_tc(q, ldq, k, ldk, v, ldv, _sb, o, ldo, gate, ldg, tq, tk, heads,
                              head_dim, _err_word, s);
-  } else if (_attn_mode == 1 &&
-             (head_dim == 128 ||
-              (head_dim == 64 && ltx::attention_tc_splits(tq, tk, heads) > 1))) {
-    // tcgen05 kernel: every head_dim-128 attention, and the head_dim-64 ones
-    // with few query tiles over many keys (video->audio), which it splits
-    // over the keys; the other head_dim-64 ones stay on the warp-MMA kernel.
-    if (!reserve_attention(tk, heads * head_dim, err)) return false;
-    if (!reserve_split(tq, tk, heads, head_dim, err)) return false;
-    rc = ltx::launch_attention_tc(q, ldq, k, ldk, v, ldv, _vt, _vt_elems, o, ldo, gate, ldg,
-                                  tq, tk, heads, head_dim, _err_word, s, _part, _part_elems);
+  } else if (_attn_mode == 1 && (head_dim == 128 || head_dim == 64) &&
+             !(s == _aux && _aux != nullptr && ltx::attention_tc_splits(tq, tk, heads) > 1)) {
+    // tcgen05 kernel for every head_dim-128 and head_dim-64 attention.  The
+    // side (audio) stream runs beside the video stream, so its V^T copy has
+    // a buffer of its own; the key-split form (partials scratch) stays on
+    // the main stream.
+    const bool side = _aux != nullptr && s == _aux;
+    __nv_bfloat16* vt = nullptr;
+    size_t vt_elems = 0;
+    if (side) {
+      if (!reserve_attention_side(tk, heads * head_dim, err)) return false;
+      vt = _vt_side;
+      vt_elems = _vt_side_elems;
+    } else {
+      if (!reserve_attention(tk, heads * head_dim, err)) return false;
+      if (!reserve_split(tq, tk, heads, head_dim, err)) return false;
+      vt = _vt;
+      vt_elems = _vt_elems;
+    }
+    rc = ltx::launch_attention_tc(q, ldq, k, ldk, v, ldv, vt, vt_elems, o, ldo, gate, ldg,
+                                  tq, tk, heads, head_dim, _err_word, s,
+                                  side ? nullptr : _part, side ? 0 : _part_elems);
   } else {
     rc = ltx::launch_attention(q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, heads,
                                head_dim, s);

@@ -205,6 +205,8 @@ public:
   bool reserve_split(int tq, int tk, int heads, int head_dim, std::string* err);
   // Pre-size the attention scratch for up to `keys` keys x `width` columns.
   bool reserve_attention(int keys, int width, std::string* err);
+  // The same for attentions issued on the side (audio) stream.
+  bool reserve_attention_side(int keys, int width, std::string* err);
 
 private:
   bool ensure_(size_t i8_bytes, size_t deq_bytes, std::string* err);
@@ -248,6 +250,8 @@ private:
   size_t _deq_bytes = 0;
   __nv_bfloat16* _vt = nullptr;    // attention: V^T
   size_t _vt_elems = 0;
+  __nv_bfloat16* _vt_side = nullptr;   // the side (audio) stream's V^T
+  size_t _vt_side_elems = 0;
   cudaStream_t _aux = nullptr;
   cudaEvent_t _ev[4] = {};
   float* _part = nullptr;          // attention: split-KV partials
