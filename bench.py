@@ -1612,6 +1612,94 @@ def run_cublas_ab(args):
     return 0
 
 
+# --------------------------------------------------------- GEMM phase trace
+TRACE_NAMES = ["entry", "setup", "first_tma", "last_tma", "first_full_deq", "first_mma",
+               "last_commit", "first_acc", "epi_done", "reduced", "end"]
+
+
+def run_gemm_trace(args):
+    """The w8g64 GEMM's own phase trace (ltx_ctx_set_trace: clock64 stamps
+    and per-role wait counters of every CTA) on the three audio shapes of
+    the sweep, one uncontended long-K shape, and the video FFN-up shape on
+    the fused route (single CTAs and CTA pairs).  Prints per-CTA medians:
+    phase stamps from entry, and per-k-block cycles of the MMA issuer's span
+    and of each role's waits.  L2 flushed before every traced call.  The
+    evidence behind the small-M and fused-kernel analysis in DESIGN."""
+    import numpy as np
+    import torch
+    import ltx25_b200 as L
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = L.Context(0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    small, big = 128 * 128 + 128 * 64 + 512, 256 * 128 + 128 * 64 + 512   # bytes a k-block stages
+    cases = [("audio 2048->2048", 126, 2048, 2048, None, small),
+             ("audio FFN-up", 126, 2048, 8192, None, small),
+             ("audio FFN-down", 126, 8192, 2048, None, small),
+             ("uncontended K=65536", 126, 65536, 128, None, small),
+             ("video FFN-up fused", 8160, 4096, 16384, 0, big),
+             ("video FFN-up fused pair", 8160, 4096, 16384, 1, small)]   # a pair CTA: half the tokens
+    out = []
+    for name, M, K, N, pair, stage_bytes in cases:
+        w32 = torch.randn((N, K), generator=gen, device=dev) * 0.02
+        c, sc, zp = L.pack_w8g64(ctx, w32)
+        del w32
+        qw = L.QWeight.upload(ctx, c, sc, zp, N, K, on_device=True)
+        x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+        if pair is not None:
+            ctx.set_route(L.ROUTE_FUSED)
+            ctx.set_tile_plan(pair=pair)
+        for _ in range(3):
+            L.qlinear(ctx, qw, x, out=y)
+        ts = []
+        for _ in range(5):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            L.qlinear(ctx, qw, x, out=y)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        tr = torch.zeros((148, 24), dtype=torch.int64, device=dev)
+        flush.zero_()
+        torch.cuda.synchronize()
+        ctx.set_trace(tr, 148)
+        L.qlinear(ctx, qw, x, out=y)
+        torch.cuda.synchronize()
+        ctx.set_trace(None, 0)
+        ctx.set_tile_plan()
+        ctx.set_route(L.ROUTE_AUTO)
+        ctx.check()
+        t = tr.cpu().numpy().astype(np.int64)
+        t = t[t[:, 0] != 0]
+        rel = t[:, :11] - t[:, 0:1]
+        tiles = float(np.median(t[:, 11]))
+        kbs = float(np.median(t[:, 21])) * 2       # the traced dequant group takes every other
+        span = float(np.median(rel[:, 6] - rel[:, 5]))
+        per = lambda col, n: round(float(np.median(t[:, col])) / max(n, 1), 1)
+        out.append({
+            "case": name, "M": M, "K": K, "N": N, "us": round(min(ts) * 1e3, 2),
+            "ctas": int(len(t)), "tiles_per_cta": tiles, "kblocks_per_cta": kbs,
+            "phase_cycles": {n: int(np.median(rel[:, i])) for i, n in enumerate(TRACE_NAMES)},
+            "mma_span_cycles_per_kblock": round(span / max(kbs, 1), 1),
+            "stage_bytes_per_clk": round(stage_bytes * max(kbs, 1) / max(span, 1), 1),
+            "mma_wait_full_per_kblock": per(12, kbs), "mma_wait_a_per_kblock": per(13, kbs),
+            "mma_wait_acc_per_tile": per(14, tiles), "producer_wait_empty_per_kblock": per(15, kbs),
+            "dequant_per_block": {"wait_full": per(16, kbs / 2), "load": per(17, kbs / 2),
+                                  "math": per(18, kbs / 2), "store": per(19, kbs / 2),
+                                  "wait_aempty": per(20, kbs / 2)},
+        })
+        qw.free()
+        del x, y
+    print(json.dumps({"metric": "w8g64 GEMM phase trace (cycles, per-CTA medians)",
+                      "value": None, "unit": "cycles", "cases": out}), flush=True)
+    ctx.close()
+    return 0
+
+
 # ------------------------------------------------------------- reference arm
 def run_reference(args):
     """--impl reference: the reference's own CPU implementation of the path
@@ -1744,7 +1832,7 @@ def main():
                     help="qlinear route for quantized weights (sweep)")
     ap.add_argument("--workload", default="stack",
                     choices=["stack", "sweep", "qlinear", "block", "attn", "lora", "trunk",
-                             "connector", "adaln", "i8", "cublas_ab"],
+                             "connector", "adaln", "i8", "cublas_ab", "gemm_trace"],
                     help="stack: BASELINE config 5, the 48-block denoise step (the "
                          "headline, carrying the config-2 sweep); sweep: config 2 alone; "
                          "qlinear: config 1; i8: config 3; block: config 4")
@@ -1759,7 +1847,7 @@ def main():
     runs = {"stack": run_stack, "sweep": run_sweep, "qlinear": run_qlinear,
             "block": run_block, "attn": run_attn, "lora": run_lora, "trunk": run_trunk,
             "connector": run_connector, "adaln": run_adaln, "i8": run_i8,
-            "cublas_ab": run_cublas_ab}
+            "cublas_ab": run_cublas_ab, "gemm_trace": run_gemm_trace}
     return runs[args.workload](args)
 
 

@@ -91,7 +91,22 @@ def build(force=False, jobs=8, verbose=False):
             if r.returncode != 0:
                 raise RuntimeError(f"link failed:\n{r.stdout}{r.stderr}")
     build_plugin(force)
+    build_diag(force)
     return LIB
+
+
+def build_diag(force=False):
+    """Measurement tools under diag/ (not linked into the library)."""
+    for src in sorted(glob.glob(os.path.join(HERE, "diag", "*.cu"))):
+        out = os.path.join(OUT_DIR, "diag_" + os.path.splitext(os.path.basename(src))[0])
+        deps = [src] + headers()
+        if not force and os.path.exists(out) and \
+                os.path.getmtime(out) >= max(os.path.getmtime(d) for d in deps):
+            continue
+        cmd = [NVCC] + ARCH + ["-O3", "-std=c++17", src, "-o", out]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"diag build failed:\n{' '.join(cmd)}\n{r.stdout}{r.stderr}")
 
 
 def build_plugin(force=False):
