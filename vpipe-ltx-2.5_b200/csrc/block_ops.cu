@@ -15,6 +15,7 @@
 #include "block_ops.h"
 
 #include <atomic>
+#include <cstdlib>
 
 namespace ltx {
 
@@ -795,7 +796,11 @@ int launch_qk_norm_rope(const __nv_bfloat16* in, int ldi, __nv_bfloat16* out,
   // that tile a CTA: Q = 4 quads a thread (2 for narrow rows).
   const int half = head_dim / 2;
   const int quads = heads * half / 4;
-  if (half % 4 == 0 && ldi % 4 == 0 && ldo % 4 == 0 &&
+  static const bool smem_form = [] {
+    const char* e = std::getenv("LTX25_QK_SMEM");   // A/B: the shared-memory form
+    return e != nullptr && e[0] == '1';
+  }();
+  if (!smem_form && half % 4 == 0 && ldi % 4 == 0 && ldo % 4 == 0 &&
       (reinterpret_cast<uintptr_t>(in) & 7u) == 0 && (reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
     for (const int Q : {4, 2}) {
       const int tr = quads / Q;

@@ -39,7 +39,7 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t,
 __device__ __forceinline__ int kb_at(const GemmParams& p, int i, int n_tile, int kb0, int kb1)
 {
   const int nkb = kb1 - kb0;
-  if (p.m_tiles != 1 || nkb <= 1) return kb0 + i;
+  if (p.krot == 0 || p.m_tiles != 1 || nkb <= 1) return kb0 + i;
   int j = i + n_tile % nkb;
   if (j >= nkb) j -= nkb;
   return kb0 + j;
@@ -740,6 +740,11 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
     return g > 0 ? g : 0;
   }();
   if (p.group_m == 0) p.group_m = group_m;
+  static const int krot = [] {
+    const char* e = getenv("LTX25_KROT");   // A/B: 0 = every tile walks K in order
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  p.krot = krot;
   if (MODE == MODE_I8) {
     if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.x, p.K, p.M, L.ldx,
                    128, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))

@@ -76,6 +76,7 @@ struct GemmParams {
   const float* sw;             // MODE_I8: [N] channel scales
   int* err;                    // device error word (0 = ok)
   int group_m;                 // raster: token tiles per weight sweep (0 = 8)
+  int krot;                    // 1: rotate each tile's K start (one token tile)
   // Diagnostics (null = off): kTraceSlots u64 per CTA for the first
   // `trace_ctas` CTAs -- phase timestamps (clock64) and the MMA issuer's
   // cumulative wait cycles per barrier kind.
