@@ -72,3 +72,37 @@ def test_tc_attention_writes_only_its_rows(ctx):
     assert torch.all(big[tq:] == 7.0)
     want = reference(q, k, v, heads)
     assert float(((out.float() - want).norm() / want.norm()).item()) < BAR
+
+
+@pytest.mark.parametrize("tq,tk,heads,gated", [(126, 126, 32, True), (126, 256, 32, True),
+                                               (100, 77, 3, False), (1, 5, 1, True)])
+def test_tc_attention_64_unsplit(tq, tk, heads, gated):
+    """The unsplit 64-wide attentions (the audio stream's) through the
+    tcgen05 kernel, the path LTX25_ATTN64=tc selects (by default they run
+    the warp-MMA kernel), on a context created with the switch set."""
+    import os
+    import torch
+    import ltx25_b200 as L
+    old = os.environ.get("LTX25_ATTN64")
+    os.environ["LTX25_ATTN64"] = "tc"
+    c = L.Context(0)
+    try:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(tq * 7 + tk)
+        D, inner = 64, heads * 64
+        q = torch.randn((tq, inner), generator=g, device="cuda").to(torch.bfloat16)
+        kv = torch.randn((tk, 2 * inner), generator=g, device="cuda").to(torch.bfloat16)
+        gate = torch.randn((tq, heads), generator=g, device="cuda").to(torch.bfloat16) if gated else None
+        got = L.attention(c, q, kv[:, :inner], kv[:, inner:], heads, D, gate=gate).float()
+        torch.cuda.synchronize()
+        c.check()
+        want = reference(q, kv[:, :inner], kv[:, inner:], heads, gate)
+        rel = float(((got - want).norm() / want.norm()).item())
+        assert torch.isfinite(got).all()
+        assert rel < BAR, rel
+    finally:
+        c.close()
+        if old is None:
+            os.environ.pop("LTX25_ATTN64", None)
+        else:
+            os.environ["LTX25_ATTN64"] = old

@@ -665,16 +665,19 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
   if (_attn_mode < 0) {
     const char* e = getenv("LTX25_ATTN");
     _attn_mode = (e != nullptr && strcmp(e, "mma") == 0) ? 0 : 1;
-    // A/B: head_dim-64 attentions over few keys on the warp-MMA kernel
+    // The unsplit 64-wide attentions (the audio stream's, 126-256 keys) run
+    // the warp-MMA kernel: on the side stream beside the video GEMMs the
+    // tcgen05 kernel (its V^T copy, its shared memory and tensor memory)
+    // measured 5 % slower a block.  LTX25_ATTN64=tc selects it.
     const char* e64 = getenv("LTX25_ATTN64");
-    _attn64_mma = e64 != nullptr && strcmp(e64, "mma") == 0;
+    _attn64_mma = !(e64 != nullptr && strcmp(e64, "tc") == 0);
   }
   int rc;
   const bool on_side = _aux != nullptr && s == _aux;
   const int splits = ltx::attention_tc_splits(tq, tk, heads);
-  // tcgen05 for head_dim 128 and 64 (the unsplit 64-wide ones on the
-  // warp-MMA kernel when LTX25_ATTN64=mma); the key-split form needs the
-  // main stream's partials scratch
+  // tcgen05 for head_dim 128 and the key-split 64-wide attentions (the
+  // unsplit 64-wide ones too with LTX25_ATTN64=tc); the key-split form needs
+  // the main stream's partials scratch
   const bool tc = _attn_mode == 1 && !(on_side && splits > 1) &&
                   (head_dim == 128 || (head_dim == 64 && (splits > 1 || !_attn64_mma)));
   if (sage_for(layer, head_dim)) {
@@ -682,10 +685,9 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
     rc = ltx::launch_sage_tc(q, ldq, k, ldk, v, ldv, _sb, o, ldo, gate, ldg, tq, tk, heads,
                              head_dim, _err_word, s);
   } else if (tc) {
-    // tcgen05 kernel for every head_dim-128 and head_dim-64 attention.  The
-    // side (audio) stream runs beside the video stream, so its V^T copy has
-    // a buffer of its own; the key-split form (partials scratch) stays on
-    // the main stream.
+    // tcgen05 kernel.  On the side (audio) stream, beside the video stream,
+    // its V^T copy has a buffer of its own; the key-split form (partials
+    // scratch) stays on the main stream.
     const bool side = on_side;
     __nv_bfloat16* vt = nullptr;
     size_t vt_elems = 0;
