@@ -487,9 +487,11 @@ bool CudaBlock::finalize(std::string* err)
   // Tensor parallel shards the weights; sequence parallel keeps them whole.
   _tp_world = (_comm && !_sp) ? _comm->world() : 1;
   _tp_rank = (_comm && !_sp) ? _comm->rank() : 0;
-  // A/B switch for the tensor-parallel residual layout (LTX25_TP_ROWS=0:
-  // whole x on every rank, all-reduced products), read once per block.
+  // A/B switches for the tensor-parallel residual layout (LTX25_TP_ROWS=0:
+  // whole x on every rank, all-reduced products) and for the feed-forward's
+  // two overlapped chunks (LTX25_TP_FF_CHUNKS=0: one), read once per block.
   if (const char* e = std::getenv("LTX25_TP_ROWS")) _tp_rows = e[0] != '0';
+  if (const char* e = std::getenv("LTX25_TP_FF_CHUNKS")) _tp_ff_chunks = e[0] != '0';
   if (_sp && (_vheads % _sp_world != 0 || _aheads % _sp_world != 0))
     return fail(err, "sequence parallel shape: heads do not split over the ranks");
   if (!build_stream_(false, _video, err) || !build_stream_(true, _audio, err))
@@ -857,12 +859,62 @@ bool CudaBlock::ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
       ltx::launch_ada_zero(io.x, d, _cur->normed + off, d, n, d, mods + (MOD_MLP + 1) * d,
                            mods + MOD_MLP * d, kEps, true, s))
     return fail(err, "ff pre-norm launch failed");
+  if (rows && _tp_ff_chunks && n % 2 == 0) return ff_rows_chunked_(s, w, io, mods, err);
   if (rows && !gather_rows_(s, _cur->normed, n, d, err)) return false;
   LoraExt lx;
   return _ops->linear(s, _cur->normed, d, w.ff_in, w.ff_in_b, _cur->ff, w.ff_hidden, nf,
                       d, w.ff_hidden, ltx::EPI_GELU, nullptr, err, lx_(w.l_ff_in, &lx)) &&
          out_proj_(s, _cur->ff, w.ff_hidden, w.ff_out, w.ff_out_b, io.x, n, d,
                    mods + (MOD_MLP + 2) * d, err, &w.l_ff_out, nf);
+}
+
+bool CudaBlock::ff_rows_chunked_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
+                                 const float* mods, std::string* err)
+{
+  // The feed-forward is token-local, so with the residual sharded by rows it
+  // runs in two chunks: each rank's first and second halves of its rows.
+  // The collectives go on the communication stream in one fixed order --
+  // all-gather chunk 0, all-gather chunk 1, reduce-scatter chunk 0,
+  // reduce-scatter chunk 1 -- each chunk's products waiting only for its own
+  // gather, each reduce-scatter only for its own products: the second
+  // gather runs under the first chunk's GEMMs and the first reduce-scatter
+  // under the second's.  Every rank issues the same collectives in the same
+  // order, and the compute stream waits for the last one before anything
+  // after the feed-forward can touch the communicator.
+  const int n = io.tokens, d = w.dim, h = n / 2, W = _tp_world, R = _tp_rank;
+  const int nfh = h * W;                         // gathered rows of one chunk
+  cudaStream_t cs = _ops->comm_stream(err);
+  if (cs == nullptr) return false;
+  __nv_bfloat16* G[2] = {_cur->normed, _cur->normed + (size_t)nfh * d};
+  __nv_bfloat16* H[2] = {_cur->ff, _cur->ff + (size_t)nfh * w.ff_hidden};
+  __nv_bfloat16* P[2] = {_cur->part, _cur->part + (size_t)nfh * d};
+  for (int c = 0; c < 2; ++c)
+    if (ltx::launch_ada_zero(io.x + (size_t)c * h * d, d, G[c] + (size_t)R * h * d, d, h, d,
+                             mods + (MOD_MLP + 1) * d, mods + MOD_MLP * d, kEps, true, s))
+      return fail(err, "ff pre-norm launch failed");
+  // the communication stream starts after everything issued on s so far
+  if (!_ops->cfork(s, cs, 0, err)) return false;
+  for (int c = 0; c < 2; ++c)
+    if (!_comm->allgather_bf16(G[c] + (size_t)R * h * d, G[c], (size_t)h * d, cs, err) ||
+        !_ops->crecord(cs, 1 + c, err))          // event 1 + c: chunk c gathered
+      return false;
+  LoraExt lx;
+  for (int c = 0; c < 2; ++c) {
+    if (!_ops->cwait(s, 1 + c, err) ||
+        !_ops->linear(s, G[c], d, w.ff_in, w.ff_in_b, H[c], w.ff_hidden, nfh, d, w.ff_hidden,
+                      ltx::EPI_GELU, nullptr, err, lx_(w.l_ff_in, &lx)) ||
+        !_ops->linear(s, H[c], w.ff_hidden, w.ff_out, nullptr, P[c], d, nfh, w.ff_hidden, d,
+                      ltx::EPI_STORE, nullptr, err, lx_(w.l_ff_out, &lx)) ||
+        !_ops->cfork(s, cs, 3 + c, err) ||       // cs: chunk c's products done
+        !_comm->reduce_scatter_bf16(P[c], (size_t)h * d, cs, err))
+      return false;
+  }
+  if (!_ops->cfork(cs, s, 5, err)) return false;   // s: both reduce-scatters done
+  for (int c = 0; c < 2; ++c)
+    if (ltx::launch_gated_residual(io.x + (size_t)c * h * d, d, P[c] + (size_t)R * h * d,
+                                   w.ff_out_b, mods + (MOD_MLP + 2) * d, h, d, s) != 0)
+      return fail(err, "gated residual launch failed");
+  return true;
 }
 
 bool CudaBlock::shards_video(int tokens) const

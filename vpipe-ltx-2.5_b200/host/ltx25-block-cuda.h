@@ -215,6 +215,10 @@ private:
                    std::string* err);
   bool ff_(cudaStream_t s, const CudaStreamW& w, StreamIO& io,
            std::string* err);
+  // The row-sharded feed-forward in two chunks with its collectives on the
+  // communication stream, overlapped with the other chunk's GEMMs.
+  bool ff_rows_chunked_(cudaStream_t s, const CudaStreamW& w, StreamIO& io, const float* mods,
+                        std::string* err);
   // Upload tensor `name` (count elements in all) as f32 / bf16, keeping
   // elements [off, off + n) (n = 0: all).
   bool take_f32_(const std::string& name, size_t count, float** out,
@@ -259,6 +263,7 @@ private:
   const Comm* _ccur = nullptr;        // the communicator of the stream being issued
   int _tp_rank = 0, _tp_world = 1;
   bool _tp_rows = true;          // tensor parallel: shard the residual by rows
+  bool _tp_ff_chunks = true;     // ... and run the feed-forward in two chunks
   bool _sp = false;              // sequence parallel (weights whole)
   int _sp_rank = 0, _sp_world = 1;
   std::map<std::string, Staged> _staged;

@@ -96,6 +96,9 @@ CudaOps::~CudaOps()
   for (cudaEvent_t e : _ev)
     if (e != nullptr) cudaEventDestroy(e);
   if (_aux != nullptr) cudaStreamDestroy(_aux);
+  for (cudaEvent_t e : _cev)
+    if (e != nullptr) cudaEventDestroy(e);
+  if (_cstream != nullptr) cudaStreamDestroy(_cstream);
   cudaFree(_vt);
   cudaFree(_vt_side);
   cudaFree(_part);
@@ -618,6 +621,33 @@ cudaStream_t CudaOps::aux_stream(std::string* err)
     if (!cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "aux events", err))
       return nullptr;
   return _aux;
+}
+
+cudaStream_t CudaOps::comm_stream(std::string* err)
+{
+  if (_cstream != nullptr) return _cstream;
+  if (!cuda_ok(cudaStreamCreateWithFlags(&_cstream, cudaStreamNonBlocking), "comm stream", err))
+    return nullptr;
+  for (cudaEvent_t& e : _cev)
+    if (!cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "comm events", err))
+      return nullptr;
+  return _cstream;
+}
+
+bool CudaOps::cfork(cudaStream_t from, cudaStream_t to, int slot, std::string* err)
+{
+  return cuda_ok(cudaEventRecord(_cev[slot], from), "event record", err) &&
+         cuda_ok(cudaStreamWaitEvent(to, _cev[slot], 0), "stream wait", err);
+}
+
+bool CudaOps::crecord(cudaStream_t from, int slot, std::string* err)
+{
+  return cuda_ok(cudaEventRecord(_cev[slot], from), "event record", err);
+}
+
+bool CudaOps::cwait(cudaStream_t to, int slot, std::string* err)
+{
+  return cuda_ok(cudaStreamWaitEvent(to, _cev[slot], 0), "stream wait", err);
 }
 
 bool CudaOps::fork(cudaStream_t from, cudaStream_t to, int slot, std::string* err)

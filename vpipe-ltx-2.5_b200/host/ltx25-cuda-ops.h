@@ -198,6 +198,15 @@ public:
   // a has issued so far (event slot i).
   cudaStream_t aux_stream(std::string* err);
   bool fork(cudaStream_t from, cudaStream_t to, int slot, std::string* err);
+  // A stream for collectives issued beside the compute stream (tensor
+  // parallel), and its own events: cfork(a, b, i) makes b wait for what a
+  // has issued so far.
+  cudaStream_t comm_stream(std::string* err);
+  bool cfork(cudaStream_t from, cudaStream_t to, int slot, std::string* err);
+  // The two halves of cfork: record event `slot` on `from`; make `to` wait
+  // for it.
+  bool crecord(cudaStream_t from, int slot, std::string* err);
+  bool cwait(cudaStream_t to, int slot, std::string* err);
   // True when an audio stream of this geometry launches nothing that uses
   // the context's scratch (fused GEMMs only, warp-MMA attentions, no tier).
   bool audio_side_ok(int tokens, int text_tokens, int heads, int head_dim, int layer) const;
@@ -253,6 +262,8 @@ private:
   __nv_bfloat16* _vt_side = nullptr;   // the side (audio) stream's V^T
   size_t _vt_side_elems = 0;
   cudaStream_t _aux = nullptr;
+  cudaStream_t _cstream = nullptr;
+  cudaEvent_t _cev[8] = {};
   cudaEvent_t _ev[4] = {};
   float* _part = nullptr;          // attention: split-KV partials
   size_t _part_elems = 0;
