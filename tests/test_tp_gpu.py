@@ -8,9 +8,9 @@ sequence parallel: each keeps them whole and runs half the video tokens),
 and run a block and a 2-block stack on the same replicated inputs.  Tensor
 parallel runs with the residual sharded by token rows (the default when the
 tokens split evenly) and, in tp_allreduce, with x whole on every rank and the
-products all-reduced, and in tp_onechunk with the feed-forward in one piece
-(by default it runs as two token chunks whose collectives overlap the other
-chunk's GEMMs).  Checked: both ranks end with the same x; it matches the
+products all-reduced, and in tp_chunked with the feed-forward as two token
+chunks whose collectives overlap the other chunk's GEMMs (the default from 8
+ranks).  Checked: both ranks end with the same x; it matches the
 oracle at the block bars of tests/test_block_gpu.py and the one-GPU device
 block within bf16.  Skipped with fewer than 2 GPUs.  NVLS is off in the
 workers, and a worker that does not finish in time is killed by PID.
@@ -102,10 +102,10 @@ def _worker(rank, world, uid, out_dir, mode):
         # the whole-x layout (all-reduced products) instead of the default
         # row-sharded residual (reduce-scatter / all-gather)
         os.environ["LTX25_TP_ROWS"] = "0"
-    if mode.startswith("tp_onechunk"):
-        # the row-sharded feed-forward in one piece instead of two chunks
-        # whose collectives overlap the other chunk's GEMMs
-        os.environ["LTX25_TP_FF_CHUNKS"] = "0"
+    if mode.startswith("tp_chunked"):
+        # the row-sharded feed-forward as two token chunks whose collectives
+        # overlap the other chunk's GEMMs (the default from 8 ranks)
+        os.environ["LTX25_TP_FF_CHUNKS"] = "1"
     import torch
     import ltx25_b200 as L
     torch.cuda.set_device(rank)
@@ -118,7 +118,7 @@ def _worker(rank, world, uid, out_dir, mode):
 
 
 @pytest.mark.parametrize("mode", ["tp", "sp", "tp_lora", "sp_lora", "tp_allreduce",
-                                  "tp_onechunk"])
+                                  "tp_chunked", "tp_chunked_lora"])
 def test_two_gpu_block_and_stack(ctx, tmp_path, mode):
     import torch
     import torch.multiprocessing as mp

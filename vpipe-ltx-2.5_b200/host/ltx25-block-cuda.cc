@@ -489,7 +489,12 @@ bool CudaBlock::finalize(std::string* err)
   _tp_rank = (_comm && !_sp) ? _comm->rank() : 0;
   // A/B switches for the tensor-parallel residual layout (LTX25_TP_ROWS=0:
   // whole x on every rank, all-reduced products) and for the feed-forward's
-  // two overlapped chunks (LTX25_TP_FF_CHUNKS=0: one), read once per block.
+  // two overlapped chunks (LTX25_TP_FF_CHUNKS=0 / 1), read once per block.
+  // The chunks pay ~0.06-0.2 ms of smaller GEMMs and extra launches a block
+  // (measured with the collectives stubbed out) to hide half of the
+  // feed-forward's gather and reduce-scatter, which grow toward 2 x 67 MB a
+  // block as the group does: on from 8 ranks by default.
+  _tp_ff_chunks = _tp_world >= 8;
   if (const char* e = std::getenv("LTX25_TP_ROWS")) _tp_rows = e[0] != '0';
   if (const char* e = std::getenv("LTX25_TP_FF_CHUNKS")) _tp_ff_chunks = e[0] != '0';
   if (_sp && (_vheads % _sp_world != 0 || _aheads % _sp_world != 0))

@@ -263,7 +263,7 @@ private:
   const Comm* _ccur = nullptr;        // the communicator of the stream being issued
   int _tp_rank = 0, _tp_world = 1;
   bool _tp_rows = true;          // tensor parallel: shard the residual by rows
-  bool _tp_ff_chunks = true;     // ... and run the feed-forward in two chunks
+  bool _tp_ff_chunks = false;    // ... and run the feed-forward in two chunks
   bool _sp = false;              // sequence parallel (weights whole)
   int _sp_rank = 0, _sp_world = 1;
   std::map<std::string, Staged> _staged;
