@@ -259,6 +259,8 @@ LTX_API int ltx_set_route(ltx_ctx* ctx, int route);
  * tile knob (src/ltx25-metal-ops.h:793-795, src/ltx25-metal-ops.cc:223-226,
  * VPIPE_LTX25_MMA_TILE, read once at construction): force_pair 1/0
  * forces CTA pairs (cta_group::2, 256 weight rows over two SMs) on or off,
+ * 2 forces pairs holding two weight blocks per CTA (512 weight rows per
+ * pair tile; dense bf16 weights with N % 512 == 0, else as 1),
  * force_tn 128/256 the token tile, force_splits 1..8 the K split; -1 leaves
  * each to the planner.  A forced value the shape cannot take is ignored.
  * The context starts from LTX25_FORCE_PAIR / _TN / _SPLITS, read once when

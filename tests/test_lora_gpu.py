@@ -123,6 +123,45 @@ def test_qlinear_lora_matches_oracle(ctx, M, epi):
     q.free()
 
 
+@pytest.mark.parametrize("M,N,epi", [(2048, 1024, 2), (1900, 2048, 0)])
+def test_dense_lora_tile_plans_agree(ctx, M, N, epi):
+    """The adapter as a K extension of the expanded-weight GEMM: single CTAs,
+    CTA pairs and pairs holding two weight blocks per CTA give the same bits
+    (the same K order per output) and the oracle's result."""
+    import torch
+    import ltx25_b200 as L
+    rng = np.random.default_rng(M + N)
+    K, rank = 1024, 24
+    q, wdeq = _quantized(ctx, rng, N, K)
+    a, b = lora_np.make_pair(rng, rank, K, N)
+    lo = L.Lora(ctx, _bits_to_dev(a), _bits_to_dev(b))
+    x = bf16r(rng.standard_normal((M, K)))
+    gate = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).cuda()
+    y0 = bf16r(rng.standard_normal((M, N)))
+    outs = {}
+    ctx.set_route(L.ROUTE_DEQUANT_ONCE)
+    try:
+        for pair in (2, 1, 0):
+            ctx.set_tile_plan(pair=pair, splits=1)
+            yd = dev_bf16(y0)
+            L.qlinear_lora(ctx, q, lo, dev_bf16(x), out=yd, epilogue=epi,
+                           gate=gate if epi == 2 else None)
+            torch.cuda.synchronize()
+            outs[pair] = yd
+    finally:
+        ctx.set_tile_plan()
+        ctx.set_route(L.ROUTE_AUTO)
+    ctx.check()
+    assert torch.equal(outs[2], outs[0])
+    assert torch.equal(outs[1], outs[0])
+    acc = x.astype(np.float64) @ wdeq.astype(np.float64).T + \
+        lora_np.delta(x, lib.bf16_to_f32(a), lib.bf16_to_f32(b))
+    want = acc if epi == 0 else y0 + gate.cpu().numpy() * acc
+    assert lib.rel_l2(host(outs[2]), want) < 1e-2
+    lo.free()
+    q.free()
+
+
 def test_qlinear_lora_without_adapter_is_qlinear(ctx):
     import torch
     import ltx25_b200 as L

@@ -268,11 +268,16 @@ def test_dense_narrow_outputs(ctx, M, N):
     assert lib.rel_l2(y[:M], want) < TOL
 
 
-@pytest.mark.parametrize("M,N,K,epi", [(2048, 4096, 1024, 0), (1900, 4096, 2048, 2), (8160, 2048, 4096, 1)])
+@pytest.mark.parametrize("M,N,K,epi", [(2048, 4096, 1024, 0), (1900, 4096, 2048, 2),
+                                       (8160, 2048, 4096, 1), (700, 1536, 1024, 0),
+                                       (4000, 3072, 512, 2)])
 def test_dense_pair_path(ctx, M, N, K, epi):
     """The expanded-weight GEMM on CTA pairs (cta_group::2, M = 256 across two
-    SMs; the default at these sizes) equals the single-CTA kernel bit for bit
-    (same K order per output) and meets the oracle bar, for each epilogue."""
+    SMs; the default at these sizes) and on pairs holding two weight blocks
+    per CTA (512 weight rows per tile; N = 1536 is no multiple of 512 and
+    falls back to one block) equals the single-CTA kernel without a K split
+    bit for bit (same K order per output) and meets the oracle bar, for each
+    epilogue."""
     import torch
     import ltx25_b200 as L
     xb, codes, scales, biases, _ = make(M, N, K, seed=9)
@@ -283,8 +288,8 @@ def test_dense_pair_path(ctx, M, N, K, epi):
     outs = {}
     ctx.set_route(L.ROUTE_DEQUANT_ONCE)
     try:
-        for pair in ("1", "0"):
-            ctx.set_tile_plan(pair=int(pair))
+        for pair in ("2", "1", "0"):
+            ctx.set_tile_plan(pair=int(pair), splits=1)
             y = y0.clone()
             L.qlinear(ctx, w, xd, out=y, epilogue=epi, gate=gate)
             torch.cuda.synchronize()
@@ -294,6 +299,7 @@ def test_dense_pair_path(ctx, M, N, K, epi):
         ctx.set_route(L.ROUTE_AUTO)
     ctx.check()
     assert torch.equal(outs["1"], outs["0"])
+    assert torch.equal(outs["2"], outs["0"])
     if epi == L.EPI_STORE:
         want = oracle_y(xb, codes, scales, biases, K)
         assert lib.rel_l2(from_dev(outs["1"]), want) < TOL

@@ -31,6 +31,25 @@ __device__ __forceinline__ void decode_tile(const GemmParams& p, int t,
   kb1 = (int)((long long)(split + 1) * p.kblocks / p.splits);
 }
 
+// Unit u of the persistent loop: its tile, and the weight blocks it takes
+// (blocks [blk0, blk0 + nblk) of the tile's WB).
+template <int WB>
+__device__ __forceinline__ void decode_unit(const GemmParams& p, int u, int& m_tile,
+                                            int& n_tile, int& kb0, int& kb1,
+                                            int& blk0, int& nblk)
+{
+  int t = u;
+  blk0 = 0;
+  nblk = WB;
+  if (WB > 1 && u >= p.full_units) {
+    const int h = u - p.full_units;
+    t = p.full_units + (h >> 1);
+    blk0 = h & 1;
+    nblk = 1;
+  }
+  decode_tile(p, t, m_tile, n_tile, kb0, kb1);
+}
+
 // The i-th k-block a tile visits.  With one token tile (M <= TN: every CTA
 // of the grid reads the same activation rows), each weight tile starts its
 // K range at its own offset, so the CTAs that share a K range do not all
@@ -97,19 +116,23 @@ __device__ __forceinline__ uint32_t epi_pair(float a, float b, bool has_bias,
 
 }  // namespace
 
-template <int MODE, int TN, int EPI, bool PAIR>
-__global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
+template <int MODE, int TN, int EPI, bool PAIR, int WB>
+__global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_sz,
                    const __grid_constant__ CUtensorMap tm_ew,
                    const __grid_constant__ CUtensorMap tm_ex, GemmParams p)
 {
-  using C = GemmCfg<MODE, TN, PAIR>;
+  using C = GemmCfg<MODE, TN, PAIR, WB>;
   constexpr int S = C::kStages;
   constexpr int A = C::kASlots > 0 ? C::kASlots : 1;
   constexpr int kDeqWarps = 8;
-  constexpr int kWT = PAIR ? 2 * C::kBM : C::kBM;   // weight rows per tile
+  constexpr int kCta = PAIR ? 2 : 1;
+  // weight rows per tile; weight block g of a tile starts kBlk rows after
+  // block g - 1, and CTA `rank` holds rows [rank * kBM, +kBM) of each block
+  constexpr int kBlk = kCta * C::kBM;
+  constexpr int kWT = WB * kBlk;
   static_assert(!PAIR || MODE == MODE_W8G64 || MODE == MODE_BF16,
                 "pairs run the w8g64 and bf16 paths");
 
@@ -155,7 +178,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
-      mbar_init(&accempty[i], PAIR ? 16 : 8);
+      mbar_init(&accempty[i], kCta * C::kEpiWarps);
     }
     mbar_init(drain, 1);
     *s_abort = 0;
@@ -194,10 +217,10 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
       uint32_t armed = 0, armed_par = 0;   // per-stage: armed once / parity
       unsigned long long w_empty = 0;
       bool first = true;
-      for (int t = unit0; t < p.num_tiles; t += unit_step) {
-        int mt, nt, kb0, kb1;
-        decode_tile(p, t, mt, nt, kb0, kb1);
-        const int wrow0 = nt * kWT + rank * C::kBM;
+      for (int u = unit0; u < p.num_units; u += unit_step) {
+        int mt, nt, kb0, kb1, blk0, nblk;
+        decode_unit<WB>(p, u, mt, nt, kb0, kb1, blk0, nblk);
+        const int wrow0 = nt * kWT + blk0 * kBlk + rank * C::kBM;
         const int xrow0 = mt * TN + rank * C::kXRows;
         for (int i = 0; i < kb1 - kb0; ++i) {
           const int kb = kb_at(p, i, nt, kb0, kb1);
@@ -216,10 +239,13 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
           if constexpr (PAIR && MODE == MODE_BF16) {
             // Both CTAs' halves of both operands complete on the leader's
             // barrier, which the leader arms for all four.
-            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (C::kXStage + C::kWStage));
+            if (leader)
+              mbar_arrive_expect_tx(&full[stage], 2 * (C::kXStage + nblk * (C::kBM * 128)));
             const uint32_t lf = mapa_shared(smem_u32(&full[stage]), 0);
             tma_load_2d_pair(mx, lf, s_x + stage * C::kXStage, kx, xrow0);
-            tma_load_2d_pair(mw, lf, s_w + stage * C::kWStage, kx, wrow0);
+            for (int g = 0; g < nblk; ++g)
+              tma_load_2d_pair(mw, lf, s_w + stage * C::kWStage + g * (C::kBM * 128), kx,
+                               wrow0 + g * kBlk);
           } else if constexpr (PAIR) {
             // Both halves of the activation tile complete on the leader's
             // barrier (it arms them); the codes on this CTA's own.
@@ -275,17 +301,17 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
       uint32_t phase = 0, aphase = 0, accphase = 0;
       unsigned long long w_full = 0, w_a = 0, w_acc = 0, n_tiles = 0;
       bool first = true;
-      for (int t = unit0; t < p.num_tiles; t += unit_step) {
-        int mt, nt, kb0, kb1;
-        decode_tile(p, t, mt, nt, kb0, kb1);
+      for (int u = unit0; u < p.num_units; u += unit_step) {
+        int mt, nt, kb0, kb1, blk0, nblk;
+        decode_unit<WB>(p, u, mt, nt, kb0, kb1, blk0, nblk);
         ++n_tiles;
         unsigned long long c0 = tr ? clock64() : 0ull;
-        if (!mbar_wait(&accempty[acc], accphase ^ 1, s_abort, p.err,
+        if (!mbar_wait(&accempty[acc * WB], accphase ^ 1, s_abort, p.err,
                        KERR_WAIT_MMA))
           goto mma_done;
         if (tr) w_acc += clock64() - c0;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(acc * TN);
+        const uint32_t d = tmem + (uint32_t)(acc * WB * TN);
         for (int i = 0; i < kb1 - kb0; ++i) {
           if (tr) c0 = clock64();
           if (!mbar_wait(&full[stage], phase, s_abort, p.err, KERR_WAIT_MMA))
@@ -310,29 +336,49 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
           tc_fence_after();
           const uint64_t bdesc =
               sdesc_k128_sw128(smem_u32(s_x + stage * C::kXStage));
+          if constexpr (PAIR && MODE == MODE_BF16) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-            if constexpr (PAIR && MODE == MODE_BF16) {
-              const uint64_t adesc =
-                  sdesc_k128_sw128(smem_u32(s_w + stage * C::kWStage));
-              umma_f16_ss_pair(d, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk),
-                               idesc, accum);
-            } else if constexpr (PAIR) {
-              umma_f16_ts_pair(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
-                               bdesc + (uint64_t)(2 * kk), idesc, accum);
-            } else if constexpr (MODE == MODE_W8G64) {
-              umma_f16_ts(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
-                          bdesc + (uint64_t)(2 * kk), idesc, accum);
-            } else {
-              const uint64_t adesc =
-                  sdesc_k128_sw128(smem_u32(s_w + stage * C::kWStage));
-              if constexpr (MODE == MODE_I8) {
-                umma_i8_ss(d, adesc + (uint64_t)(2 * kk),
-                           bdesc + (uint64_t)(2 * kk), idesc, accum);
-              } else {
-                umma_f16_ss(d, adesc + (uint64_t)(2 * kk),
+            for (int g = 0; g < WB; ++g) {
+              if (g > 0 && i == 0) {
+                // A later accumulator of the set is claimed only here, so
+                // the first block's MMAs overlap the epilogue's drain of it.
+                // (A half unit leaves it unwritten but still completes its
+                // phase, so the barrier phases stay one per unit.)
+                if (!mbar_wait(&accempty[acc * WB + g], accphase ^ 1, s_abort, p.err,
+                               KERR_WAIT_MMA))
+                  goto mma_done;
+                tc_fence_after();
+              }
+              if (g >= nblk) continue;
+              const uint64_t adesc = sdesc_k128_sw128(
+                  smem_u32(s_w + stage * C::kWStage + g * (C::kBM * 128)));
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                umma_f16_ss_pair(d + (uint32_t)(g * TN), adesc + (uint64_t)(2 * kk),
+                                 bdesc + (uint64_t)(2 * kk), idesc,
+                                 (i > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (PAIR) {
+                umma_f16_ts_pair(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
+                                 bdesc + (uint64_t)(2 * kk), idesc, accum);
+              } else if constexpr (MODE == MODE_W8G64) {
+                umma_f16_ts(d, tmem + (uint32_t)(C::kACol0 + aslot * 32 + kk * 8),
                             bdesc + (uint64_t)(2 * kk), idesc, accum);
+              } else {
+                const uint64_t adesc =
+                    sdesc_k128_sw128(smem_u32(s_w + stage * C::kWStage));
+                if constexpr (MODE == MODE_I8) {
+                  umma_i8_ss(d, adesc + (uint64_t)(2 * kk),
+                             bdesc + (uint64_t)(2 * kk), idesc, accum);
+                } else {
+                  umma_f16_ss(d, adesc + (uint64_t)(2 * kk),
+                              bdesc + (uint64_t)(2 * kk), idesc, accum);
+                }
               }
             }
           }
@@ -358,11 +404,14 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
             phase ^= 1;
           }
         }
-        if constexpr (PAIR) {
-          umma_commit_pair(smem_u32(&accfull[acc]));
-          umma_commit_pair(mapa_shared(smem_u32(&accfull[acc]), 1));
-        } else {
-          umma_commit(&accfull[acc]);
+#pragma unroll
+        for (int g = 0; g < WB; ++g) {
+          if constexpr (PAIR) {
+            umma_commit_pair(smem_u32(&accfull[acc * WB + g]));
+            umma_commit_pair(mapa_shared(smem_u32(&accfull[acc * WB + g]), 1));
+          } else {
+            umma_commit(&accfull[acc * WB + g]);
+          }
         }
         if (++acc == C::kNAcc) {
           acc = 0;
@@ -386,7 +435,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, p.err, KERR_DRAIN);
     }
-  } else if (warp < 2 + kDeqWarps) {
+  } else if (warp < C::kEpiWarp0) {
     // ------------------------------------------------------------ dequant
     // Two groups of four warps (one warp per TMEM lane quarter each) take
     // alternate k-blocks: codes from shared memory -> bf16 -> TMEM A slot.
@@ -401,9 +450,9 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
       const bool tw = tr != nullptr && warp == 2 && lane == 0;
       unsigned long long d_full = 0, d_load = 0, d_math = 0, d_st = 0,
                          d_ae = 0, d_blocks = 0;
-      for (int t = unit0; t < p.num_tiles; t += unit_step) {
+      for (int u = unit0; u < p.num_units; u += unit_step) {
         int mt, nt, kb0, kb1;
-        decode_tile(p, t, mt, nt, kb0, kb1);
+        decode_tile(p, u, mt, nt, kb0, kb1);   // one weight block: units are tiles
         for (int kb = kb0; kb < kb1; ++kb, ++seq) {
           if ((seq & 1) != grp) continue;
           const int stage = seq % S;
@@ -488,126 +537,170 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR>::kThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    // Two groups of four warps (one per lane quarter) drain alternate
-    // 32-column chunks, halving the time the accumulator is held.
+    // Groups of four warps (one per lane quarter) drain alternate 32-column
+    // chunks, so the accumulator is held for a fraction of a tile.
+    constexpr int kEG = C::kEpiWarps / 4;
     const int q = warp & 3;
-    const int egrp = (warp - 2 - kDeqWarps) >> 2;
+    const int egrp = (warp - C::kEpiWarp0) >> 2;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     int acc = 0;
     uint32_t accphase = 0;
-    const bool te = tr != nullptr && warp == 2 + kDeqWarps && lane == 0;
+    const bool te = tr != nullptr && warp == C::kEpiWarp0 && lane == 0;
     unsigned long long e_wait = 0, e_work = 0;
-    for (int t = unit0; t < p.num_tiles; t += unit_step) {
-      int mt, nt, kb0, kb1;
-      decode_tile(p, t, mt, nt, kb0, kb1);
+    for (int u = unit0; u < p.num_units; u += unit_step) {
+      int mt, nt, kb0, kb1, blk0, nblk;
+      decode_unit<WB>(p, u, mt, nt, kb0, kb1, blk0, nblk);
       unsigned long long ce = te ? clock64() : 0ull;
-      if (!mbar_wait(&accfull[acc], accphase, s_abort, p.err,
-                     KERR_WAIT_EPILOGUE))
-        goto epi_done;
-      if (te) {
-        const unsigned long long c1 = clock64();
-        e_wait += c1 - ce;
-        ce = c1;
-      }
-      if (tr && warp == 2 + kDeqWarps && lane == 0 && t == unit0)
-        tr[TR_FIRST_ACC] = clock64();
-      tc_fence_after();
-      // Pair layout: lanes (2i, 2i+1) own features (n, n+1); the even lane
-      // writes even tokens, the odd lane odd tokens.
-      const int nrow = nt * kWT + rank * C::kBM + q * 32;
-      const int n_pair = nrow + (int)(lane & ~1u);
-      const int odd = (int)(lane & 1u);
-      float csx = 1.0f;
-      if constexpr (MODE == MODE_I8) {
-        const int nn = nrow + (int)lane;
-        csx = nn < p.N ? p.sw[nn] : 0.0f;
-      }
-      float2 ebias = make_float2(0.0f, 0.0f), egate = make_float2(0.0f, 0.0f);
-      if (n_pair < p.N) {
-        if (p.bias != nullptr) {
-          const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(p.bias + n_pair);
-          ebias = make_float2(__bfloat162float(bb.x), __bfloat162float(bb.y));
-        }
-        if constexpr (EPI == EPI_GATED_RES) egate = *reinterpret_cast<const float2*>(p.gate + n_pair);
-      }
-      constexpr int kChunks = TN / 32;
-      const int c_last = ((kChunks - 1 - egrp) / 2) * 2 + egrp;
 #pragma unroll 1
-      for (int c = egrp; c < kChunks; c += 2) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + (uint32_t)(acc * TN + c * 32), v);
-        tmem_wait_ld();
-        if (c == c_last) {
+      for (int g = 0; g < WB; ++g) {
+        const int slot = acc * WB + g;   // accumulator g of the set
+        if (!mbar_wait(&accfull[slot], accphase, s_abort, p.err,
+                       KERR_WAIT_EPILOGUE))
+          goto epi_done;
+        if (te) {
+          const unsigned long long c1 = clock64();
+          e_wait += c1 - ce;
+          ce = c1;
+        }
+        if (te && u == unit0 && g == 0) tr[TR_FIRST_ACC] = clock64();
+        tc_fence_after();
+        if (g >= nblk) {
+          // a half unit's unused accumulator: hand it straight back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
             if constexpr (PAIR) {
-              mbar_arrive_cluster(mapa_shared(smem_u32(&accempty[acc]), 0));
+              mbar_arrive_cluster(mapa_shared(smem_u32(&accempty[slot]), 0));
             } else {
-              mbar_arrive(&accempty[acc]);
+              mbar_arrive(&accempty[slot]);
             }
-          }
-        }
-        float f[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if constexpr (MODE == MODE_I8) {
-            f[i] = (float)(int)v[i] * csx;
-          } else {
-            f[i] = __uint_as_float(v[i]);
-          }
-        }
-        const int j0 = mt * TN + c * 32;
-        if (!PAIR && p.splits > 1) {
-          // K-split partial: park it in this CTA's shared memory as
-          // red[token][feature] f32 (the pipeline buffers are idle now);
-          // the cluster reduces it after the role loops.
-          float* red = reinterpret_cast<float*>(s_x);
-          const int nl = q * 32 + (int)lane;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float val = f[i];
-            if constexpr (MODE == MODE_I8) {
-              const int j = j0 + i;
-              val *= j < p.M ? p.sx[j] : 0.0f;
-            }
-            red[(c * 32 + i) * C::kBM + nl] = val;
           }
           continue;
         }
-        // The residual of this chunk's 16 sites, all loaded before any
-        // store (one memory latency per chunk, not one per token).
-        uint32_t res[16];
-        if constexpr (EPI == EPI_GATED_RES) {
+        // Pair layout: lanes (2i, 2i+1) own features (n, n+1); the even lane
+        // writes even tokens, the odd lane odd tokens.
+        const int nrow = nt * kWT + (blk0 + g) * kBlk + rank * C::kBM + q * 32;
+        const int n_pair = nrow + (int)(lane & ~1u);
+        const int odd = (int)(lane & 1u);
+        float csx = 1.0f;
+        if constexpr (MODE == MODE_I8) {
+          const int nn = nrow + (int)lane;
+          csx = nn < p.N ? p.sw[nn] : 0.0f;
+        }
+        float2 ebias = make_float2(0.0f, 0.0f), egate = make_float2(0.0f, 0.0f);
+        if (n_pair < p.N) {
+          if (p.bias != nullptr) {
+            const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(p.bias + n_pair);
+            ebias = make_float2(__bfloat162float(bb.x), __bfloat162float(bb.y));
+          }
+          if constexpr (EPI == EPI_GATED_RES) egate = *reinterpret_cast<const float2*>(p.gate + n_pair);
+        }
+        // One 32-column chunk of the accumulator, from registers to y.
+        auto emit = [&](const uint32_t (&v)[32], int c) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if constexpr (MODE == MODE_I8) {
+              f[i] = (float)(int)v[i] * csx;
+            } else {
+              f[i] = __uint_as_float(v[i]);
+            }
+          }
+          const int j0 = mt * TN + c * 32;
+          if (!PAIR && p.splits > 1) {
+            // K-split partial: park it in this CTA's shared memory as
+            // red[token][feature] f32 (the pipeline buffers are idle now);
+            // the cluster reduces it after the role loops.
+            float* red = reinterpret_cast<float*>(s_x);
+            const int nl = q * 32 + (int)lane;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float val = f[i];
+              if constexpr (MODE == MODE_I8) {
+                const int j = j0 + i;
+                val *= j < p.M ? p.sx[j] : 0.0f;
+              }
+              red[(c * 32 + i) * C::kBM + nl] = val;
+            }
+            return;
+          }
+          // The residual of this chunk's 16 sites, all loaded before any
+          // store (one memory latency per chunk, not one per token).
+          uint32_t res[16];
+          if constexpr (EPI == EPI_GATED_RES) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int j = j0 + 2 * k + odd;
+              res[k] = (j < p.M && n_pair < p.N)
+                           ? *reinterpret_cast<const uint32_t*>(p.y + (size_t)j * p.ldy + n_pair)
+                           : 0u;
+            }
+          }
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
+            // even lane keeps token 2k, odd lane keeps token 2k+1
+            const float send = odd ? f[2 * k] : f[2 * k + 1];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            float a = odd ? recv : f[2 * k];           // feature n_pair
+            float b = odd ? f[2 * k + 1] : recv;       // feature n_pair + 1
             const int j = j0 + 2 * k + odd;
-            res[k] = (j < p.M && n_pair < p.N)
-                         ? *reinterpret_cast<const uint32_t*>(p.y + (size_t)j * p.ldy + n_pair)
-                         : 0u;
+            if constexpr (MODE == MODE_I8) {
+              const float sj = j < p.M ? p.sx[j] : 0.0f;
+              a *= sj;
+              b *= sj;
+            }
+            if (j < p.M && n_pair < p.N) {
+              const uint32_t o = epi_pair<EPI>(a, b, p.bias != nullptr, ebias, egate,
+                                               EPI == EPI_GATED_RES ? res[k] : 0u);
+              *reinterpret_cast<uint32_t*>(p.y + (size_t)j * p.ldy + n_pair) = o;
+            }
+          }
+        };
+        auto release = [&]() {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (PAIR) {
+              mbar_arrive_cluster(mapa_shared(smem_u32(&accempty[slot]), 0));
+            } else {
+              mbar_arrive(&accempty[slot]);
+            }
+          }
+        };
+        constexpr int kChunks = TN / 32;
+        constexpr int kPer = kChunks / kEG;   // chunks this warp drains per accumulator
+        static_assert(kChunks % kEG == 0, "chunks split evenly over the groups");
+        // Pull every chunk out of TMEM first and hand the accumulator back
+        // before the first store, so the MMA waits for the loads only --
+        // where the held chunks fit the register budget without spilling
+        // (not beside a gated residual's loads or the int8 rescale).
+        constexpr bool kHold = kPer <= 2 && MODE == MODE_BF16 && EPI != EPI_GATED_RES;
+        if constexpr (kHold) {
+          uint32_t v[kPer][32];
+#pragma unroll
+          for (int h = 0; h < kPer; ++h)
+            tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + (egrp + h * kEG) * 32), v[h]);
+          tmem_wait_ld();
+          release();
+#pragma unroll
+          for (int h = 0; h < kPer; ++h) emit(v[h], egrp + h * kEG);
+        } else {
+#pragma unroll 1
+          for (int h = 0; h < kPer; ++h) {
+            const int c = egrp + h * kEG;
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + c * 32), v);
+            tmem_wait_ld();
+            if (h == kPer - 1) release();
+            emit(v, c);
           }
         }
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          // even lane keeps token 2k, odd lane keeps token 2k+1
-          const float send = odd ? f[2 * k] : f[2 * k + 1];
-          const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-          float a = odd ? recv : f[2 * k];           // feature n_pair
-          float b = odd ? f[2 * k + 1] : recv;       // feature n_pair + 1
-          const int j = j0 + 2 * k + odd;
-          if constexpr (MODE == MODE_I8) {
-            const float sj = j < p.M ? p.sx[j] : 0.0f;
-            a *= sj;
-            b *= sj;
-          }
-          if (j < p.M && n_pair < p.N) {
-            const uint32_t o = epi_pair<EPI>(a, b, p.bias != nullptr, ebias, egate,
-                                             EPI == EPI_GATED_RES ? res[k] : 0u);
-            *reinterpret_cast<uint32_t*>(p.y + (size_t)j * p.ldy + n_pair) = o;
-          }
+        if (te) {
+          const unsigned long long c1 = clock64();
+          e_work += c1 - ce;
+          ce = c1;
         }
       }
-      if (te) e_work += clock64() - ce;
       if (++acc == C::kNAcc) {
         acc = 0;
         accphase ^= 1;
@@ -727,10 +820,10 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* gaddr,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MODE, int TN, int EPI, bool PAIR>
+template <int MODE, int TN, int EPI, bool PAIR, int WB>
 int launch_t(const GemmLaunch& L, cudaStream_t stream)
 {
-  using C = GemmCfg<MODE, TN, PAIR>;
+  using C = GemmCfg<MODE, TN, PAIR, WB>;
   CUtensorMap tx, tw, tsz;
   memset(&tsz, 0, sizeof(tsz));
   GemmParams p = L.p;
@@ -784,15 +877,34 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
                    (uint64_t)L.ld_ext * 2, 64, C::kXRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
   }
-  auto kern = gemm_tc_kernel<MODE, TN, EPI, PAIR>;
+  auto kern = gemm_tc_kernel<MODE, TN, EPI, PAIR, WB>;
   static std::atomic<unsigned long long> attr_done{0};
   if (!smem_limit_once(kern, C::kSmemBytes, attr_done)) return -2;
+  // Tail split (two weight blocks per CTA): when the tiles past the last
+  // full wave of pairs fit the pairs twice over, they run as half units of
+  // one weight block each, so the last wave takes half a tile's time
+  // instead of a whole one (e.g. 256 tiles on 74 pairs: 3.5 tile times,
+  // not 4).
+  static const bool tail_split = [] {
+    const char* e = getenv("LTX25_TAIL_SPLIT");   // A/B: 0 = whole tiles only
+    return !(e != nullptr && e[0] == '0');
+  }();
+  p.full_units = p.num_tiles;
+  p.num_units = p.num_tiles;
+  if (WB == 2 && tail_split) {
+    const int pairs = L.num_sms / 2;
+    const int rem = p.num_tiles % pairs;
+    if (rem > 0 && 2 * rem <= pairs) {
+      p.full_units = p.num_tiles - rem;
+      p.num_units = p.full_units + 2 * rem;
+    }
+  }
   int cluster = 1;
   int grid = p.num_tiles < L.num_sms ? p.num_tiles : L.num_sms;
   if (PAIR) {
-    // One cluster of two CTAs per output tile, persistent over tiles.
+    // One cluster of two CTAs per work unit, persistent over units.
     if (p.splits != 1) return -5;
-    const int pairs = p.num_tiles < L.num_sms / 2 ? p.num_tiles : L.num_sms / 2;
+    const int pairs = p.num_units < L.num_sms / 2 ? p.num_units : L.num_sms / 2;
     grid = 2 * pairs;
     cluster = 2;
   } else if (p.splits > 1) {
@@ -806,13 +918,13 @@ int launch_t(const GemmLaunch& L, cudaStream_t stream)
   return launched() == 0 ? 0 : -3;
 }
 
-template <int MODE, int TN, bool PAIR>
+template <int MODE, int TN, bool PAIR, int WB = 1>
 int launch_epi(const GemmLaunch& L, cudaStream_t stream)
 {
   switch (L.epi) {
-    case EPI_STORE: return launch_t<MODE, TN, EPI_STORE, PAIR>(L, stream);
-    case EPI_GELU: return launch_t<MODE, TN, EPI_GELU, PAIR>(L, stream);
-    case EPI_GATED_RES: return launch_t<MODE, TN, EPI_GATED_RES, PAIR>(L, stream);
+    case EPI_STORE: return launch_t<MODE, TN, EPI_STORE, PAIR, WB>(L, stream);
+    case EPI_GELU: return launch_t<MODE, TN, EPI_GELU, PAIR, WB>(L, stream);
+    case EPI_GATED_RES: return launch_t<MODE, TN, EPI_GATED_RES, PAIR, WB>(L, stream);
   }
   return -4;
 }
@@ -820,6 +932,10 @@ int launch_epi(const GemmLaunch& L, cudaStream_t stream)
 template <int MODE>
 int launch_tn(const GemmLaunch& L, cudaStream_t stream)
 {
+  if constexpr (MODE == MODE_BF16) {
+    if (L.pair && L.wb == 2) return L.tn == 256 ? launch_epi<MODE, 256, true, 2>(L, stream) : -4;
+  }
+  if (L.wb != 1) return -4;
   if constexpr (MODE == MODE_W8G64 || MODE == MODE_BF16) {
     if (L.pair) return L.tn == 256 ? launch_epi<MODE, 256, true>(L, stream) : -4;
   } else {

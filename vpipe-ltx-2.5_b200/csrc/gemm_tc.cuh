@@ -23,15 +23,21 @@
 // Warp roles (576 threads):
 //   warp 0       TMA producer (one elected lane)
 //   warp 1       TMEM allocator + MMA issuer (one elected lane)
-//   warps 2-9    dequant (MODE_W8G64 only): two groups of four, one warp per
-//                TMEM lane quarter (warp % 4), alternating k-blocks
-//   warps 10-17  epilogue: two groups of four, alternating 32-column chunks;
+//   warps 2-9    dequant (MODE_W8G64): two groups of four, one warp per
+//                TMEM lane quarter (warp % 4), alternating k-blocks; on
+//                the dense path (MODE_BF16) these eight join the epilogue
+//   warps 10-17  epilogue: groups of four (two, or four with warps 2-9),
+//                alternating 32-column chunks;
 //                TMEM -> registers -> bias/act/residual -> global
 //
 // Large token counts run as CTA PAIRS (cta_group::2, a cluster of two):
 // one M = 256 MMA spans 256 weight rows, each CTA dequantizing its 128 into
 // its own TMEM and holding half of the 256-token activation tile, so each
 // SM streams half the activation bytes per FLOP of a single-CTA tile.
+// A dense pair may also hold TWO weight blocks per CTA (WB = 2: 512 weight
+// rows x 256 tokens per pair, both accumulators filling all 512 TMEM
+// columns): each activation stage then feeds two MMAs, so an SM takes in
+// 48 KB per 2 x 128x256x64 MMA instead of 32 KB per one.
 //
 // K is split across CTAs (`splits` > 1, at most 8) for the small-M,
 // bandwidth-bound shapes.  The splits of one output tile are launched as
@@ -68,6 +74,12 @@ struct GemmParams {
   // 0 or == kblocks: no extension.
   int kblocks_main;
   int num_tiles;           // m_tiles * n_tiles * splits
+  // Work units of the persistent loop.  Units below full_units are whole
+  // tiles; with two weight blocks per CTA the tiles past full_units (the
+  // last, partial wave) run as two half units of one weight block each,
+  // unit full_units + 2 h + b taking block b of tile full_units + h.
+  // Without a tail split both equal num_tiles.
+  int full_units, num_units;
   int ldy;                 // row stride of y, elements
   const __nv_bfloat16* bias;   // [N] or null
   const float* gate;           // [N] f32, EPI_GATED_RES only
@@ -97,32 +109,45 @@ enum TraceSlot : int {
   TR_EPI_WAIT, TR_EPI_WORK
 };
 
-template <int MODE, int TN, bool PAIR = false>
+template <int MODE, int TN, bool PAIR = false, int WB = 1>
 struct GemmCfg {
-  static constexpr int kBM = 128;                       // weight rows / CTA
+  static constexpr int kBM = 128;                       // weight rows / block
+  // Weight blocks of kBM rows per CTA: a dense pair may hold two, so one
+  // activation stage feeds two M = 256 MMAs (512 weight rows per pair).
+  static constexpr int kWB = WB;
   // Activation rows per CTA: a pair splits the TN-token tile between its
   // two CTAs (each holds half of the MMA's B operand).
   static constexpr int kXRows = PAIR ? TN / 2 : TN;
   static constexpr int kXStage = kXRows * 128;           // 128 B of K per row
-  static constexpr int kWStage = MODE == MODE_W8G64 ? kBM * 64 : kBM * 128;
+  static constexpr int kWStage = MODE == MODE_W8G64 ? kBM * 64 : WB * kBM * 128;
   static constexpr int kSZStage = MODE == MODE_W8G64 ? kBM * 4 : 0;
   static constexpr int kStageBytes = kXStage + kWStage + kSZStage;
   static constexpr int kStages =
       (224 * 1024) / kStageBytes > 8 ? 8 : (224 * 1024) / kStageBytes;
+  // Accumulator sets in TMEM (double buffering across tiles); a set is WB
+  // accumulators of TN columns.
   static constexpr int kNAcc =
-      MODE == MODE_W8G64 ? (2 * TN + 4 * 32 <= 512 ? 2 : 1) : 2;
-  static constexpr int kASlotsRaw = (512 - kNAcc * TN) / 32;
+      MODE == MODE_W8G64 ? (2 * TN + 4 * 32 <= 512 ? 2 : 1) : (WB == 2 ? 1 : 2);
+  static constexpr int kASlotsRaw = (512 - kNAcc * WB * TN) / 32;
   static constexpr int kASlots =
       MODE == MODE_W8G64 ? (kASlotsRaw > 8 ? 8 : kASlotsRaw) : 0;
-  static constexpr int kACol0 = kNAcc * TN;              // first A column
+  static constexpr int kACol0 = kNAcc * WB * TN;         // first A column
   static constexpr int kKPerStage = MODE == MODE_I8 ? 128 : 64;  // elements
   static constexpr int kThreads = 576;   // 18 warps, see the role table
+  // Epilogue warps: on the dense path the eight dequant warps join them
+  // (the int8 path keeps eight: its rescale needs the registers).
+  static constexpr int kEpiWarps = MODE == MODE_BF16 ? 16 : 8;
+  static constexpr int kEpiWarp0 = 18 - kEpiWarps;
   static constexpr int kNumBars =
       3 * kStages + 2 * (kASlots > 0 ? kASlots : 1) + 2 * 2 + 1;
   static constexpr int kSmemBytes =
       1024 + kStages * kStageBytes + kNumBars * 8 + 64;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "MMA N");
-  static_assert(kNAcc * TN + kASlots * 32 <= 512, "TMEM budget");
+  static_assert(WB == 1 || (WB == 2 && PAIR && MODE == MODE_BF16 && TN == 256),
+                "two weight blocks: dense 256-token pairs only");
+  static_assert(kNAcc * WB <= 2, "accumulator barriers");
+  static_assert(TN / 32 >= kEpiWarps / 4, "every epilogue group drains a chunk");
+  static_assert(kNAcc * WB * TN + kASlots * 32 <= 512, "TMEM budget");
   static_assert(MODE != MODE_W8G64 || kASlots >= 2, "A pipeline depth");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };

@@ -25,7 +25,9 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType,
 struct GemmLaunch {
   int mode = MODE_W8G64;   // GemmMode
   int tn = 256;            // token tile: 128 or 256
-  bool pair = false;       // cta_group::2 pairs (MODE_W8G64, tn 256)
+  bool pair = false;       // cta_group::2 pairs (MODE_W8G64 / MODE_BF16, tn 256)
+  int wb = 1;              // weight blocks per CTA: 2 for dense pairs only
+                           // (512 weight rows per tile, n_tiles = N / 512)
   int epi = EPI_STORE;     // EpiMode
   int num_sms = 148;
   const void* x = nullptr; // bf16 [M][ldx] (int8 for MODE_I8)

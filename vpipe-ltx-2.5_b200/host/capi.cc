@@ -543,9 +543,9 @@ int ltx_set_tile_plan(ltx_ctx* ctx, int force_pair, int force_tn, int force_spli
 {
   return guarded([&]() -> int {
     if (ctx == nullptr) return LTX_E_NULL;
-    if (force_pair < -1 || force_pair > 1 || !(force_tn == -1 || force_tn == 128 || force_tn == 256) ||
+    if (force_pair < -1 || force_pair > 2 || !(force_tn == -1 || force_tn == 128 || force_tn == 256) ||
         force_splits < -1 || force_splits == 0 || force_splits > 8)
-      return fail(ctx, LTX_E_SHAPE, "set_tile_plan: pair -1/0/1, tn -1/128/256, splits -1 or 1..8");
+      return fail(ctx, LTX_E_SHAPE, "set_tile_plan: pair -1/0/1/2, tn -1/128/256, splits -1 or 1..8");
     ltx25::PlanKnobs k;
     k.pair = force_pair;
     k.tn = force_tn;

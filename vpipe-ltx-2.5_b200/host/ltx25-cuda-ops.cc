@@ -29,6 +29,7 @@ bool aligned(const void* p, size_t a)
 struct Plan {
   int tn = 256;
   bool pair = false;
+  int wb = 1;          // weight blocks per CTA (2: 512 weight rows per pair tile)
   int splits = 1;
   int m_tiles = 1, n_tiles = 1, kblocks = 1;
 };
@@ -38,6 +39,12 @@ struct Plan {
 // text shapes (M <= 128 / small tile counts) split K until the grid covers
 // the SMs, because those shapes are bound by reading the weight, not by
 // the tensor pipe.
+// Dense pairs hold two weight blocks per CTA unless LTX25_PAIR_WB=1.
+const bool g_wb2_default = [] {
+  const char* e = std::getenv("LTX25_PAIR_WB");
+  return !(e != nullptr && e[0] == '1');
+}();
+
 Plan plan_gemm(int mode, int M, int N, int K, int sms, const PlanKnobs& kn)
 {
   Plan p;
@@ -56,10 +63,16 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms, const PlanKnobs& kn)
              M > 128 && N % 256 == 0;
   }
   if (p.pair) p.tn = 256;
+  // Two weight blocks per CTA: one activation stage feeds two MMAs, 48 KB
+  // per 2 x 128x256x64 MMA taken in by each SM instead of 32 KB per one.
+  if ((kn.pair == 2 || (kn.pair < 0 && g_wb2_default)) && p.pair && mode == ltx::MODE_BF16 &&
+      N % 512 == 0)
+    p.wb = 2;
   if (kn.tn >= 0) {
     if (!p.pair && (kn.tn == 128 || kn.tn == 256)) p.tn = kn.tn;
   }
-  p.n_tiles = (N + (p.pair ? 255 : 127)) / (p.pair ? 256 : 128);
+  const int wrows = (p.pair ? 256 : 128) * p.wb;   // weight rows per tile
+  p.n_tiles = (N + wrows - 1) / wrows;
   p.m_tiles = (M + p.tn - 1) / p.tn;
   const int tiles = p.m_tiles * p.n_tiles;
   p.splits = 1;
@@ -117,7 +130,10 @@ CudaOps::~CudaOps()
 bool CudaOps::init(int device, std::string* err)
 {  // the tile plan's A/B overrides start from the environment, read here
   // once (LTX25_FORCE_PAIR, LTX25_FORCE_TN, LTX25_FORCE_SPLITS)
-  if (const char* e = std::getenv("LTX25_FORCE_PAIR")) _knobs.pair = std::atoi(e) != 0 ? 1 : 0;
+  if (const char* e = std::getenv("LTX25_FORCE_PAIR")) {
+    const int v = std::atoi(e);
+    _knobs.pair = v == 2 ? 2 : v != 0 ? 1 : 0;
+  }
   if (const char* e = std::getenv("LTX25_FORCE_TN")) _knobs.tn = std::atoi(e);
   if (const char* e = std::getenv("LTX25_FORCE_SPLITS")) _knobs.splits = std::atoi(e);
 
@@ -247,6 +263,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   L.mode = mode;
   L.tn = pl.tn;
   L.pair = pl.pair;
+  L.wb = pl.wb;
   L.epi = epi;
   L.num_sms = _sms;
   L.x = x;

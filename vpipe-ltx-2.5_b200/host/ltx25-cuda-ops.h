@@ -64,7 +64,7 @@ enum class Route { Fused = 0, DequantOnce = 1, Auto = 2 };
 // src/ltx25-metal-ops.h:793-795): CTA pairs on/off, the token tile, the
 // K split.  -1 = the planner's own choice.
 struct PlanKnobs {
-  int pair = -1, tn = -1, splits = -1;
+  int pair = -1, tn = -1, splits = -1;   // pair: -1 auto, 0, 1, 2 (two weight blocks)
 };
 
 class CudaOps {
