@@ -74,17 +74,20 @@ def test_tc_attention_writes_only_its_rows(ctx):
     assert float(((out.float() - want).norm() / want.norm()).item()) < BAR
 
 
+@pytest.mark.parametrize("mode", ["tc", "mma"])
 @pytest.mark.parametrize("tq,tk,heads,gated", [(126, 126, 32, True), (126, 256, 32, True),
-                                               (100, 77, 3, False), (1, 5, 1, True)])
-def test_tc_attention_64_unsplit(tq, tk, heads, gated):
-    """The unsplit 64-wide attentions (the audio stream's) through the
-    tcgen05 kernel, the path LTX25_ATTN64=tc selects (by default they run
-    the warp-MMA kernel), on a context created with the switch set."""
+                                               (8160, 126, 32, True), (100, 77, 3, False),
+                                               (1, 5, 1, True)])
+def test_attention_64_unsplit(tq, tk, heads, gated, mode):
+    """The unsplit 64-wide attentions (the audio stream's, and the video
+    queries over the audio keys) through each kernel LTX25_ATTN64 selects:
+    tcgen05 and warp MMA (the default), on a context created with the switch
+    set."""
     import os
     import torch
     import ltx25_b200 as L
     old = os.environ.get("LTX25_ATTN64")
-    os.environ["LTX25_ATTN64"] = "tc"
+    os.environ["LTX25_ATTN64"] = mode
     c = L.Context(0)
     try:
         g = torch.Generator(device="cuda")

@@ -128,14 +128,23 @@ CudaOps::~CudaOps()
 }
 
 bool CudaOps::init(int device, std::string* err)
-{  // the tile plan's A/B overrides start from the environment, read here
-  // once (LTX25_FORCE_PAIR, LTX25_FORCE_TN, LTX25_FORCE_SPLITS)
+{  // the tile plan's and the attention's A/B overrides start from the
+  // environment, read here once (LTX25_FORCE_PAIR, LTX25_FORCE_TN,
+  // LTX25_FORCE_SPLITS, LTX25_ATTN, LTX25_ATTN64)
   if (const char* e = std::getenv("LTX25_FORCE_PAIR")) {
     const int v = std::atoi(e);
     _knobs.pair = v == 2 ? 2 : v != 0 ? 1 : 0;
   }
   if (const char* e = std::getenv("LTX25_FORCE_TN")) _knobs.tn = std::atoi(e);
   if (const char* e = std::getenv("LTX25_FORCE_SPLITS")) _knobs.splits = std::atoi(e);
+  // attention kernel choice (A/B switches): LTX25_ATTN=mma runs every
+  // attention on the warp-MMA kernel.  The unsplit 64-wide attentions (126-256
+  // keys: the audio stream's, and the video queries over the audio keys) run
+  // the warp-MMA kernel; LTX25_ATTN64=tc selects the tcgen05 one, measured
+  // slower on all of them (8160 x 126: 74 vs 60 us; 126 x 126: 26 vs 19 us)
+  // and, on the side stream beside the video GEMMs, 5 % slower a block.
+  if (const char* e = std::getenv("LTX25_ATTN")) _attn_mode = std::strcmp(e, "mma") == 0 ? 0 : 1;
+  if (const char* e = std::getenv("LTX25_ATTN64")) _attn64_tc = std::strcmp(e, "tc") == 0;
 
   int n = 0;
   if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount", err)) return false;
@@ -709,16 +718,6 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
                         int ldg, int tq, int tk, int heads, int head_dim,
                         std::string* err, int layer)
 {
-  if (_attn_mode < 0) {
-    const char* e = getenv("LTX25_ATTN");
-    _attn_mode = (e != nullptr && strcmp(e, "mma") == 0) ? 0 : 1;
-    // The unsplit 64-wide attentions (the audio stream's, 126-256 keys) run
-    // the warp-MMA kernel: on the side stream beside the video GEMMs the
-    // tcgen05 kernel (its V^T copy, its shared memory and tensor memory)
-    // measured 5 % slower a block.  LTX25_ATTN64=tc selects it.
-    const char* e64 = getenv("LTX25_ATTN64");
-    _attn64_mma = !(e64 != nullptr && strcmp(e64, "tc") == 0);
-  }
   int rc;
   const bool on_side = _aux != nullptr && s == _aux;
   const int splits = ltx::attention_tc_splits(tq, tk, heads);
@@ -726,7 +725,7 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
   // unsplit 64-wide ones too with LTX25_ATTN64=tc); the key-split form needs
   // the main stream's partials scratch
   const bool tc = _attn_mode == 1 && !(on_side && splits > 1) &&
-                  (head_dim == 128 || (head_dim == 64 && (splits > 1 || !_attn64_mma)));
+                  (head_dim == 128 || (head_dim == 64 && (splits > 1 || _attn64_tc)));
   if (sage_for(layer, head_dim)) {
     if (!reserve_sage(tq, tk, heads, head_dim, err)) return false;
     rc = ltx::launch_sage_tc(q, ldq, k, ldk, v, ldv, _sb, o, ldo, gate, ldg, tq, tk, heads,

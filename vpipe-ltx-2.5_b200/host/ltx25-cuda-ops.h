@@ -268,8 +268,8 @@ private:
   float* _part = nullptr;          // attention: split-KV partials
   size_t _part_elems = 0;
   ltx::SageBuffers _sb;            // sage tier: int8 Q/K, scales, key mean
-  int _attn_mode = -1;             // LTX25_ATTN: 0 = always warp-MMA
-  bool _attn64_mma = true;         // 64-wide unsplit -> warp-MMA (LTX25_ATTN64=tc: tcgen05)
+  int _attn_mode = 1;              // LTX25_ATTN=mma: 0 = always warp-MMA
+  bool _attn64_tc = false;         // 64-wide unsplit on tcgen05 (LTX25_ATTN64=tc), else warp-MMA
   int* _err_word = nullptr;
   std::unique_ptr<Comm> _comm;
   std::unique_ptr<Comm> _comm_side;
