@@ -8,9 +8,11 @@ sequence parallel: each keeps them whole and runs half the video tokens),
 and run a block and a 2-block stack on the same replicated inputs.  Tensor
 parallel runs with the residual sharded by token rows (the default when the
 tokens split evenly) and, in tp_allreduce, with x whole on every rank and the
-products all-reduced, and in tp_chunked with the feed-forward as two token
+products all-reduced, in tp_chunked with the feed-forward as two token
 chunks whose collectives overlap the other chunk's GEMMs (the default from 8
-ranks).  Checked: both ranks end with the same x; it matches the
+ranks), and in tp_scatter with the row-split products reduce-scattered by
+the GEMM itself (each row's partial stored into its owner's receive slot over
+peer memory, then summed by the owner).  Checked: both ranks end with the same x; it matches the
 oracle at the block bars of tests/test_block_gpu.py and the one-GPU device
 block within bf16.  Skipped with fewer than 2 GPUs.  NVLS is off in the
 workers, and a worker that does not finish in time is killed by PID.
@@ -106,6 +108,10 @@ def _worker(rank, world, uid, out_dir, mode):
         # the row-sharded feed-forward as two token chunks whose collectives
         # overlap the other chunk's GEMMs (the default from 8 ranks)
         os.environ["LTX25_TP_FF_CHUNKS"] = "1"
+    # the fused reduce-scatter (the row-split GEMMs store each row's partial
+    # into its owner's receive slot over peer memory) is the default; the
+    # other row-sharded modes run the NCCL reduce-scatter
+    os.environ["LTX25_TP_SCATTER"] = "1" if mode.startswith("tp_scatter") else "0"
     import torch
     import ltx25_b200 as L
     torch.cuda.set_device(rank)
@@ -118,7 +124,8 @@ def _worker(rank, world, uid, out_dir, mode):
 
 
 @pytest.mark.parametrize("mode", ["tp", "sp", "tp_lora", "sp_lora", "tp_allreduce",
-                                  "tp_chunked", "tp_chunked_lora"])
+                                  "tp_chunked", "tp_chunked_lora", "tp_scatter",
+                                  "tp_scatter_lora"])
 def test_two_gpu_block_and_stack(ctx, tmp_path, mode):
     import torch
     import torch.multiprocessing as mp

@@ -436,7 +436,7 @@ __global__ void gated_residual_kernel(__nv_bfloat16* __restrict__ x, int ldx,
                                       const __nv_bfloat16* __restrict__ part,
                                       const __nv_bfloat16* __restrict__ bias,
                                       const float* __restrict__ gate, int rows,
-                                      int dim)
+                                      int dim, int nslot, size_t slot_stride)
 {
   pdl_wait();
   pdl_trigger();
@@ -449,6 +449,13 @@ __global__ void gated_residual_kernel(__nv_bfloat16* __restrict__ x, int ldx,
     float xv[8], pv[8];
     load8(x + (size_t)r * ldx + k, xv);
     load8(part + (size_t)r * dim + k, pv);
+    // further partials (one per source rank), summed in slot order
+    for (int sl = 1; sl < nslot; ++sl) {
+      float qv[8];
+      load8(part + sl * slot_stride + (size_t)r * dim + k, qv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pv[j] += qv[j];
+    }
     float bv[8];
     if (bias != nullptr) {
       load8(bias + k, bv);
@@ -866,14 +873,14 @@ int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,
 
 int launch_gated_residual(__nv_bfloat16* x, int ldx, const __nv_bfloat16* part,
                           const __nv_bfloat16* bias, const float* gate, int rows,
-                          int dim, cudaStream_t s)
+                          int dim, cudaStream_t s, int nslot, size_t slot_stride)
 {
   if (rows <= 0) return 0;
-  if (dim % 8 != 0 || ldx % 8 != 0) return -2;
+  if (dim % 8 != 0 || ldx % 8 != 0 || nslot < 1 || slot_stride % 8 != 0) return -2;
   const size_t total = (size_t)rows * (dim / 8);
   size_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
-  launch_k(gated_residual_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, x, ldx, part, bias, gate, rows, dim);
+  launch_k(gated_residual_kernel, dim3((unsigned)grid), dim3(256), 0, s, 1, x, ldx, part, bias, gate, rows, dim, nslot, slot_stride);
   return launched();
 }
 

@@ -75,9 +75,12 @@ int launch_row_sumsq(const __nv_bfloat16* in, int ldi, int rows, int cols,
                      float* out, cudaStream_t s);
 
 // x[r] += gate * (part[r] + bias) (part [rows][dim] dense, bias may be null).
+// With nslot > 1, part holds nslot such partials slot_stride elements apart
+// (one per source rank) and their sum, taken in slot order in f32, stands for
+// part[r].
 int launch_gated_residual(__nv_bfloat16* x, int ldx, const __nv_bfloat16* part,
                           const __nv_bfloat16* bias, const float* gate, int rows,
-                          int dim, cudaStream_t s);
+                          int dim, cudaStream_t s, int nslot = 1, size_t slot_stride = 0);
 
 // Non-causal attention, token-major q [tq][ldq], k/v [tk][ld], head h at
 // columns [h*D, (h+1)*D); o [tq][ldo]; optional gate logits [tq][ldg]

@@ -87,6 +87,14 @@ struct GemmParams {
   const float* sx;             // MODE_I8: [M] token scales
   const float* sw;             // MODE_I8: [N] channel scales
   int* err;                    // device error word (0 = ok)
+  // Row scatter (the fused tensor-parallel reduce-scatter), EPI_STORE, one
+  // K split: when scatter_rows > 0, token row j is stored at
+  // ys[j / scatter_rows] + (scatter_slot * scatter_rows + j % scatter_rows) * ldy
+  // instead of y + j * ldy -- the receive slot of the rank that owns row j,
+  // which may be another GPU's memory mapped into this one (plain stores over
+  // NVLink), followed by a system-scope fence before the kernel ends.
+  __nv_bfloat16* ys[8];
+  int scatter_rows, scatter_slot;
   int group_m;                 // raster: token tiles per weight sweep (0 = 8)
   int krot;                    // 1: rotate each tile's K start (one token tile)
   // Diagnostics (null = off): kTraceSlots u64 per CTA for the first

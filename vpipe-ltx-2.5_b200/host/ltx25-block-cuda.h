@@ -252,6 +252,9 @@ private:
                  const __nv_bfloat16* bias, __nv_bfloat16* x, int n, int d,
                  const float* gate, std::string* err, const LoraSite* lora = nullptr,
                  int n_all = 0);
+  // The fused reduce-scatter's availability for a row-split product over
+  // n_all rows of width d on the current communicator.
+  bool scatter_ok_(int n_all, int d) const;
   // All-gather this rank's n rows (in place at rank * n * d) of a
   // [world * n][d] buffer on the current stream's communicator.
   bool gather_rows_(cudaStream_t s, __nv_bfloat16* buf, int n, int d, std::string* err) const;
@@ -264,6 +267,7 @@ private:
   int _tp_rank = 0, _tp_world = 1;
   bool _tp_rows = true;          // tensor parallel: shard the residual by rows
   bool _tp_ff_chunks = false;    // ... and run the feed-forward in two chunks
+  bool _tp_scatter = false;      // ... and fuse the row-split products' reduce-scatter
   bool _sp = false;              // sequence parallel (weights whole)
   int _sp_rank = 0, _sp_world = 1;
   std::map<std::string, Staged> _staged;

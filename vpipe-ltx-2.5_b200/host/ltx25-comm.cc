@@ -7,6 +7,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 namespace ltx25 {
 
@@ -90,7 +91,81 @@ bool Comm::unique_id(void* out, std::string* err)
 
 Comm::~Comm()
 {
+  release_buffers_();
+  if (_token != nullptr) cudaFree(_token);
   if (_comm != nullptr && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(_comm));
+}
+
+void Comm::release_buffers_()
+{
+  for (int r = 0; r < _world && r < 8; ++r) {
+    if (_peer[r] == nullptr) continue;
+    if (r == _rank)
+      cudaFree(_peer[r]);
+    else
+      cudaIpcCloseMemHandle(_peer[r]);
+    _peer[r] = nullptr;
+  }
+  _share_bytes = 0;
+}
+
+bool Comm::share_buffers(size_t bytes, cudaStream_t s, std::string* err)
+{
+  if (_comm == nullptr || bytes <= _share_bytes) return true;
+  if (_world > 8) {
+    if (err) *err = "peer buffers: at most 8 ranks";
+    return false;
+  }
+  auto cuda = [&](cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return true;
+    if (err) *err = std::string(what) + ": " + cudaGetErrorString(e);
+    return false;
+  };
+  // Everything issued before (the previous buffers' last readers and
+  // writers on every rank) is done once this returns.
+  if (_share_bytes > 0 && !(barrier(s, err) && cuda(cudaStreamSynchronize(s), "sync")))
+    return false;
+  release_buffers_();
+  bytes = (bytes + 255) & ~size_t(255);
+  void* mine = nullptr;
+  cudaIpcMemHandle_t h;
+  if (!cuda(cudaMalloc(&mine, 2 * bytes), "cudaMalloc(peer buffers)")) return false;
+  _peer[_rank] = mine;
+  char* hall = nullptr;   // [world][64] handles, all-gathered
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  bool ok = cuda(cudaIpcGetMemHandle(&h, mine), "cudaIpcGetMemHandle") &&
+            cuda(cudaMalloc(&hall, (size_t)_world * 64), "cudaMalloc(handles)") &&
+            cuda(cudaMemcpyAsync(hall + (size_t)_rank * 64, &h, 64, cudaMemcpyHostToDevice, s),
+                 "handle upload") &&
+            nccl_ok(nccl().all_gather(hall + (size_t)_rank * 64, hall, 64, ncclInt8,
+                                      static_cast<ncclComm_t>(_comm), s),
+                    "ncclAllGather(handles)", err);
+  std::vector<char> host((size_t)_world * 64);
+  ok = ok && cuda(cudaMemcpyAsync(host.data(), hall, host.size(), cudaMemcpyDeviceToHost, s),
+                  "handle download") &&
+       cuda(cudaStreamSynchronize(s), "sync");
+  if (hall != nullptr) cudaFree(hall);
+  for (int r = 0; ok && r < _world; ++r) {
+    if (r == _rank) continue;
+    cudaIpcMemHandle_t hr;
+    memcpy(&hr, host.data() + (size_t)r * 64, 64);
+    ok = cuda(cudaIpcOpenMemHandle(&_peer[r], hr, cudaIpcMemLazyEnablePeerAccess),
+              "cudaIpcOpenMemHandle");
+  }
+  if (!ok) {
+    release_buffers_();
+    return false;
+  }
+  _share_bytes = bytes;
+  return true;
+}
+
+bool Comm::barrier(cudaStream_t s, std::string* err) const
+{
+  if (_comm == nullptr) return true;
+  return nccl_ok(nccl().all_reduce(_token, _token, 1, ncclFloat32, ncclSum,
+                                   static_cast<ncclComm_t>(_comm), s),
+                 "ncclAllReduce(barrier)", err);
 }
 
 bool Comm::init(int device, int rank, int world, const void* id, std::string* err)
@@ -115,6 +190,12 @@ bool Comm::init(int device, int rank, int world, const void* id, std::string* er
   _comm = c;
   _rank = rank;
   _world = world;
+  _device = device;
+  if (cudaMalloc(&_token, sizeof(float)) != cudaSuccess ||
+      cudaMemset(_token, 0, sizeof(float)) != cudaSuccess) {
+    if (err) *err = "tp: cudaMalloc(barrier word) failed";
+    return false;
+  }
   return true;
 }
 
@@ -142,6 +223,12 @@ bool Comm::split(Comm* out, std::string* err) const
   out->_comm = c;
   out->_rank = _rank;
   out->_world = _world;
+  out->_device = _device;
+  if (cudaMalloc(&out->_token, sizeof(float)) != cudaSuccess ||
+      cudaMemset(out->_token, 0, sizeof(float)) != cudaSuccess) {
+    if (err) *err = "comm split: cudaMalloc(barrier word) failed";
+    return false;
+  }
   return true;
 }
 

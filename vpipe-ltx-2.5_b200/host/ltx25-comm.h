@@ -45,12 +45,38 @@ public:
   // collectives issued on another stream.
   bool split(Comm* out, std::string* err) const;
 
+  // Peer-mapped receive buffers for the fused reduce-scatter: every rank
+  // allocates two buffers of `bytes` and maps every other rank's through
+  // CUDA IPC, so a kernel here can store into any rank's buffers over
+  // NVLink.  Collective (every rank, same bytes, same order); a no-op when
+  // the buffers are already that large.  Up to 8 ranks.
+  bool share_buffers(size_t bytes, cudaStream_t s, std::string* err);
+  size_t shared_bytes() const { return _share_bytes; }
+  // Which of the two buffers the next fused reduce-scatter uses: they
+  // alternate, so a call's writers never meet the previous call's readers
+  // (every rank makes the same calls in the same order).
+  int next_buffer() const { return _flip ^= 1; }
+  // Rank r's buffer `which` (0 or 1), as mapped in this process.
+  void* peer_buffer(int r, int which) const
+  {
+    return static_cast<char*>(_peer[r]) + (size_t)which * _share_bytes;
+  }
+  // An ordering point for the group on `s`: returns once every rank's work
+  // issued on its stream before it has completed (a 4-byte all-reduce).
+  bool barrier(cudaStream_t s, std::string* err) const;
+
   int rank() const { return _rank; }
   int world() const { return _world; }
 
 private:
+  void release_buffers_();
+
   void* _comm = nullptr;
-  int _rank = 0, _world = 1;
+  int _rank = 0, _world = 1, _device = -1;
+  void* _peer[8] = {};            // [rank]: this rank's own at _peer[_rank]
+  size_t _share_bytes = 0;        // bytes of one of the two buffers
+  float* _token = nullptr;        // the barrier's 4 bytes
+  mutable int _flip = 1;          // the buffer of the last fused reduce-scatter
 };
 
 }  // namespace ltx25

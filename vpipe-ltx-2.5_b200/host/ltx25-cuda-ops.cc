@@ -262,12 +262,21 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
                     const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy,
                     int M, int K, int N, int epi, const float* gate,
                     const float* sx, const float* sw, std::string* err,
-                    const LoraExt* ext)
+                    const LoraExt* ext, const RowScatter* scatter)
 {
   // An extension adds ceil(r / 64) K blocks after the main K.
   const int ext_k = (ext != nullptr) ? ext->r : 0;
   const int ext_kb = (ext_k + 63) / 64;
-  const Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms, _knobs);
+  Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms, _knobs);
+  if (scatter != nullptr) {
+    // scattered rows are stored by the tile epilogue itself: one K split
+    if (epi != ltx::EPI_STORE || scatter->rows <= 0 || scatter->slot < 0 ||
+        (M + scatter->rows - 1) / scatter->rows > 8) {
+      if (err) *err = "row scatter: store epilogue, rows > 0, at most 8 owners";
+      return false;
+    }
+    pl.splits = 1;
+  }
   ltx::GemmLaunch L;
   L.mode = mode;
   L.tn = pl.tn;
@@ -304,6 +313,11 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.err = _err_word;
   p.trace = _trace;
   p.trace_ctas = _trace_ctas;
+  if (scatter != nullptr) {
+    for (int o = 0; o < 8; ++o) p.ys[o] = scatter->dst[o];
+    p.scatter_rows = scatter->rows;
+    p.scatter_slot = scatter->slot;
+  }
   const int rc = ltx::gemm_launch(L, s);
   if (rc != 0) {
     if (err)
@@ -317,7 +331,8 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
 bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
                      const QWeight& w, const __nv_bfloat16* bias,
                      __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
-                     const float* gate, std::string* err, const LoraExt* lora)
+                     const float* gate, std::string* err, const LoraExt* lora,
+                     const RowScatter* sc)
 {
   if (x == nullptr || y == nullptr) {
     if (err) *err = "linear: null x or y";
@@ -365,11 +380,11 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
       wb = _deq;
     }
     return gemm_(s, ltx::MODE_BF16, x, ldx, wb, nullptr, bias, y, ldy, M, K, N, epi, gate,
-                 nullptr, nullptr, err, lora);
+                 nullptr, nullptr, err, lora, sc);
   }
   if (!w.quantized) {
     return gemm_(s, ltx::MODE_BF16, x, ldx, w.w, nullptr, bias, y, ldy, M, K,
-                 N, epi, gate, nullptr, nullptr, err);
+                 N, epi, gate, nullptr, nullptr, err, nullptr, sc);
   }
   if (i8_takes(M, K, N)) {
     if (!prepare_i8(const_cast<QWeight&>(w), s, err)) return false;
@@ -379,7 +394,7 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
       return false;
     }
     return gemm_(s, ltx::MODE_I8, _xq, K, w.wq, nullptr, bias, y, ldy, M, K,
-                 N, epi, gate, _sx, w.sw, err);
+                 N, epi, gate, _sx, w.sw, err, nullptr, sc);
   }
   if (_route == Route::DequantOnce || (_route == Route::Auto && M >= LTX_DEQUANT_MIN_M)) {
     if (!ensure_(0, (size_t)N * K * 2, err)) return false;
@@ -388,10 +403,10 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
       return false;
     }
     return gemm_(s, ltx::MODE_BF16, x, ldx, _deq, nullptr, bias, y, ldy, M,
-                 K, N, epi, gate, nullptr, nullptr, err);
+                 K, N, epi, gate, nullptr, nullptr, err, nullptr, sc);
   }
   return gemm_(s, ltx::MODE_W8G64, x, ldx, w.codes, w.sz, bias, y, ldy, M, K,
-               N, epi, gate, nullptr, nullptr, err);
+               N, epi, gate, nullptr, nullptr, err, nullptr, sc);
 }
 
 __nv_bfloat16* CudaOps::lora_rbuf(size_t elems, std::string* err)

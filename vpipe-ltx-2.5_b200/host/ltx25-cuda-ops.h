@@ -48,6 +48,16 @@ struct LoraExt {
   __nv_bfloat16* rbuf = nullptr;      // [M][r] scratch: x.A^T
 };
 
+// Where a linear's output rows go under the fused tensor-parallel
+// reduce-scatter: row j to dst[j / rows] + (slot * rows + j % rows) * ldy,
+// the receive slot of the rank owning row j (up to 8 ranks; dst entries may
+// be other GPUs' memory mapped into this process).
+struct RowScatter {
+  __nv_bfloat16* dst[8] = {};
+  int rows = 0;   // rows per owner
+  int slot = 0;   // this rank's slot in every owner's buffer
+};
+
 // One module's uploaded adapter pair (src/ltx25-lora.h:48-56): a [r8][k]
 // with the scale folded in, b [n][r8], the rank padded to r8 (a multiple of
 // 8, so every row is 16-byte aligned for TMA) with zero rows / columns.
@@ -86,7 +96,8 @@ public:
   bool linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
               const QWeight& w, const __nv_bfloat16* bias, __nv_bfloat16* y,
               int ldy, int M, int K, int N, int epi,
-              const float* gate, std::string* err, const LoraExt* lora = nullptr);
+              const float* gate, std::string* err, const LoraExt* lora = nullptr,
+              const RowScatter* scatter = nullptr);
 
   // Ltx25Dit's patchify (src/ltx25-dit.cc:1509-1540): x[T][dim] =
   // latent . W^T + bias (+ adapter), then `prefix` [dim] added to rows
@@ -157,6 +168,12 @@ public:
     _sequence = sequence;
   }
   const Comm* comm() const { return _comm.get(); }
+  // Grow the tensor-parallel communicator's peer-mapped buffers to `bytes`
+  // each (collective over the group; see Comm::share_buffers).
+  bool share_peer_buffers(size_t bytes, std::string* err)
+  {
+    return _comm == nullptr || _comm->share_buffers(bytes, nullptr, err);
+  }
   // The communicator for collectives on the side stream (null: none).
   const Comm* side_comm() const { return _comm_side.get(); }
   bool sequence_parallel() const { return _comm != nullptr && _sequence; }
@@ -223,7 +240,8 @@ private:
              const void* wptr, const uint32_t* sz, const __nv_bfloat16* bias,
              __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
              const float* gate, const float* sx, const float* sw,
-             std::string* err, const LoraExt* ext = nullptr);
+             std::string* err, const LoraExt* ext = nullptr,
+             const RowScatter* scatter = nullptr);
   // f32 ones [n] (the gate of lora_add's accumulate), grown on demand
   const float* ones_(int n, cudaStream_t s, std::string* err);
 public:
