@@ -64,10 +64,12 @@ __device__ __forceinline__ int kb_at(const GemmParams& p, int i, int n_tile, int
   return kb0 + j;
 }
 
-// Row j of the output: y's row, or under a row scatter its owner's slot.
+// Row j of the output: y's row, or under a row scatter (store epilogue
+// only: the host refuses it with the others) its owner's slot.
+template <int EPI>
 __device__ __forceinline__ __nv_bfloat16* out_row(const GemmParams& p, int j)
 {
-  if (p.scatter_rows > 0) {
+  if (EPI == EPI_STORE && p.scatter_rows > 0) {
     const int o = j / p.scatter_rows;
     return p.ys[o] + ((size_t)p.scatter_slot * p.scatter_rows + (j - o * p.scatter_rows)) * p.ldy;
   }
@@ -642,7 +644,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
             for (int k = 0; k < 16; ++k) {
               const int j = j0 + 2 * k + odd;
               res[k] = (j < p.M && n_pair < p.N)
-                           ? *reinterpret_cast<const uint32_t*>(out_row(p, j) + n_pair)
+                           ? *reinterpret_cast<const uint32_t*>(out_row<EPI>(p, j) + n_pair)
                            : 0u;
             }
           }
@@ -662,7 +664,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
             if (j < p.M && n_pair < p.N) {
               const uint32_t o = epi_pair<EPI>(a, b, p.bias != nullptr, ebias, egate,
                                                EPI == EPI_GATED_RES ? res[k] : 0u);
-              *reinterpret_cast<uint32_t*>(out_row(p, j) + n_pair) = o;
+              *reinterpret_cast<uint32_t*>(out_row<EPI>(p, j) + n_pair) = o;
             }
           }
         };
@@ -719,7 +721,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
   epi_done:
     // scattered rows may sit in another GPU's memory: make them visible
     // there before the kernel's completion is
-    if (p.scatter_rows > 0) __threadfence_system();
+    if (EPI == EPI_STORE && p.scatter_rows > 0) __threadfence_system();
     if (te) {
       tr[TR_EPI_WAIT] = e_wait;
       tr[TR_EPI_WORK] = e_work;
@@ -763,7 +765,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
           sum.w += v[sp].w;
         }
       }
-      __nv_bfloat16* yrow = out_row(p, j);
+      __nv_bfloat16* yrow = out_row<EPI>(p, j);
       auto site = [&](float a, float b, int nn) {
         float2 bias = make_float2(0.0f, 0.0f), g = make_float2(0.0f, 0.0f);
         uint32_t res = 0u;

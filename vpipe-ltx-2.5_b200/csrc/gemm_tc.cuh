@@ -83,18 +83,13 @@ struct GemmParams {
   int ldy;                 // row stride of y, elements
   const __nv_bfloat16* bias;   // [N] or null
   const float* gate;           // [N] f32, EPI_GATED_RES only
-  __nv_bfloat16* y;            // [M][ldy]
+  union {
+    __nv_bfloat16* y;               // [M][ldy]
+    __nv_bfloat16* const* ys;       // row scatter: see scatter_rows
+  };
   const float* sx;             // MODE_I8: [M] token scales
   const float* sw;             // MODE_I8: [N] channel scales
   int* err;                    // device error word (0 = ok)
-  // Row scatter (the fused tensor-parallel reduce-scatter), EPI_STORE, one
-  // K split: when scatter_rows > 0, token row j is stored at
-  // ys[j / scatter_rows] + (scatter_slot * scatter_rows + j % scatter_rows) * ldy
-  // instead of y + j * ldy -- the receive slot of the rank that owns row j,
-  // which may be another GPU's memory mapped into this one (plain stores over
-  // NVLink), followed by a system-scope fence before the kernel ends.
-  __nv_bfloat16* ys[8];
-  int scatter_rows, scatter_slot;
   int group_m;                 // raster: token tiles per weight sweep (0 = 8)
   int krot;                    // 1: rotate each tile's K start (one token tile)
   // Diagnostics (null = off): kTraceSlots u64 per CTA for the first
@@ -102,6 +97,14 @@ struct GemmParams {
   // cumulative wait cycles per barrier kind.
   unsigned long long* trace;
   int trace_ctas;
+  // Row scatter (the fused tensor-parallel reduce-scatter), EPI_STORE, one
+  // K split: when scatter_rows > 0, token row j is stored at
+  // ys[j / scatter_rows] + (scatter_slot * scatter_rows + j % scatter_rows) * ldy
+  // instead of y + j * ldy -- the receive slot of the rank that owns row j,
+  // which may be another GPU's memory mapped into this one (plain stores over
+  // NVLink), followed by a system-scope fence before the kernel ends.  `ys`
+  // (a device array of the owners' buffers) takes the place of y.
+  int scatter_rows, scatter_slot;
 };
 
 constexpr int kTraceSlots = 24;

@@ -789,11 +789,11 @@ bool CudaBlock::out_proj_(cudaStream_t s, const __nv_bfloat16* in, int k,
     // order, adding the bias and the gated residual in the same pass.
     const int which = _ccur->next_buffer();
     RowScatter sc;
-    for (int o = 0; o < _tp_world; ++o)
-      sc.dst[o] = static_cast<__nv_bfloat16*>(_ccur->peer_buffer(o, which));
+    sc.dst = _ccur->peer_table(which);
+    sc.owners = _tp_world;
     sc.rows = n;
     sc.slot = _tp_rank;
-    __nv_bfloat16* mine = sc.dst[_tp_rank];
+    __nv_bfloat16* mine = static_cast<__nv_bfloat16*>(_ccur->peer_buffer(_tp_rank, which));
     if (!_ops->linear(s, in, k, w, nullptr, mine, d, n_all, k, d, ltx::EPI_STORE, nullptr, err,
                       ext, &sc) ||
         !_ccur->barrier(s, err))

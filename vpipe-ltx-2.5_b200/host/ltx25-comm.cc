@@ -92,6 +92,7 @@ bool Comm::unique_id(void* out, std::string* err)
 Comm::~Comm()
 {
   release_buffers_();
+  if (_table != nullptr) cudaFree(_table);
   if (_token != nullptr) cudaFree(_token);
   if (_comm != nullptr && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(_comm));
 }
@@ -157,6 +158,16 @@ bool Comm::share_buffers(size_t bytes, cudaStream_t s, std::string* err)
     return false;
   }
   _share_bytes = bytes;
+  __nv_bfloat16* tbl[16] = {};
+  for (int w = 0; w < 2; ++w)
+    for (int r = 0; r < _world; ++r)
+      tbl[w * 8 + r] = static_cast<__nv_bfloat16*>(peer_buffer(r, w));
+  if ((_table == nullptr &&
+       !cuda(cudaMalloc(&_table, sizeof tbl), "cudaMalloc(peer table)")) ||
+      !cuda(cudaMemcpy(_table, tbl, sizeof tbl, cudaMemcpyHostToDevice), "peer table upload")) {
+    release_buffers_();
+    return false;
+  }
   return true;
 }
 

@@ -4,6 +4,7 @@
 // that copy).  The reference has no counterpart: it runs on one Apple GPU.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -56,6 +57,8 @@ public:
   // alternate, so a call's writers never meet the previous call's readers
   // (every rank makes the same calls in the same order).
   int next_buffer() const { return _flip ^= 1; }
+  // Buffer `which` of every rank (world entries), as a device array.
+  __nv_bfloat16* const* peer_table(int which) const { return _table + (size_t)which * 8; }
   // Rank r's buffer `which` (0 or 1), as mapped in this process.
   void* peer_buffer(int r, int which) const
   {
@@ -76,6 +79,7 @@ private:
   void* _peer[8] = {};            // [rank]: this rank's own at _peer[_rank]
   size_t _share_bytes = 0;        // bytes of one of the two buffers
   float* _token = nullptr;        // the barrier's 4 bytes
+  __nv_bfloat16** _table = nullptr;   // device [2][8]: every rank's buffers
   mutable int _flip = 1;          // the buffer of the last fused reduce-scatter
 };
 

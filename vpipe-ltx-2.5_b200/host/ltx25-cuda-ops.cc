@@ -270,9 +270,9 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms, _knobs);
   if (scatter != nullptr) {
     // scattered rows are stored by the tile epilogue itself: one K split
-    if (epi != ltx::EPI_STORE || scatter->rows <= 0 || scatter->slot < 0 ||
-        (M + scatter->rows - 1) / scatter->rows > 8) {
-      if (err) *err = "row scatter: store epilogue, rows > 0, at most 8 owners";
+    if (epi != ltx::EPI_STORE || scatter->dst == nullptr || scatter->rows <= 0 ||
+        scatter->slot < 0 || (M + scatter->rows - 1) / scatter->rows > scatter->owners) {
+      if (err) *err = "row scatter: store epilogue, an owner for every row";
       return false;
     }
     pl.splits = 1;
@@ -314,7 +314,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.trace = _trace;
   p.trace_ctas = _trace_ctas;
   if (scatter != nullptr) {
-    for (int o = 0; o < 8; ++o) p.ys[o] = scatter->dst[o];
+    p.ys = scatter->dst;
     p.scatter_rows = scatter->rows;
     p.scatter_slot = scatter->slot;
   }

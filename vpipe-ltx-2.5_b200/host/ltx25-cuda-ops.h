@@ -50,12 +50,14 @@ struct LoraExt {
 
 // Where a linear's output rows go under the fused tensor-parallel
 // reduce-scatter: row j to dst[j / rows] + (slot * rows + j % rows) * ldy,
-// the receive slot of the rank owning row j (up to 8 ranks; dst entries may
-// be other GPUs' memory mapped into this process).
+// the receive slot of the rank owning row j (up to 8 ranks; the owners'
+// buffers may be other GPUs' memory mapped into this process).  `dst` is a
+// device array of the owners' buffers (what the kernel reads).
 struct RowScatter {
-  __nv_bfloat16* dst[8] = {};
-  int rows = 0;   // rows per owner
-  int slot = 0;   // this rank's slot in every owner's buffer
+  __nv_bfloat16* const* dst = nullptr;
+  int owners = 0;  // entries of dst
+  int rows = 0;    // rows per owner
+  int slot = 0;    // this rank's slot in every owner's buffer
 };
 
 // One module's uploaded adapter pair (src/ltx25-lora.h:48-56): a [r8][k]
