@@ -2,6 +2,7 @@
 // gemm_tc.cuh.
 #include <cstdio>
 #include <cstdlib>
+#include <type_traits>
 
 #include "gemm_tc.cuh"
 #include "block_ops.h"
@@ -566,6 +567,47 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
 #pragma unroll 1
       for (int g = 0; g < WB; ++g) {
         const int slot = acc * WB + g;   // accumulator g of the set
+        // Pair layout: lanes (2i, 2i+1) own features (n, n+1); the even lane
+        // writes even tokens, the odd lane odd tokens.
+        const int nrow = nt * kWT + (blk0 + g) * kBlk + rank * C::kBM + q * 32;
+        const int n_pair = nrow + (int)(lane & ~1u);
+        const int odd = (int)(lane & 1u);
+        float csx = 1.0f;
+        if constexpr (MODE == MODE_I8) {
+          const int nn = nrow + (int)lane;
+          csx = nn < p.N ? p.sw[nn] : 0.0f;
+        }
+        float2 ebias = make_float2(0.0f, 0.0f), egate = make_float2(0.0f, 0.0f);
+        if (n_pair < p.N) {
+          if (p.bias != nullptr) {
+            const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(p.bias + n_pair);
+            ebias = make_float2(__bfloat162float(bb.x), __bfloat162float(bb.y));
+          }
+          if constexpr (EPI == EPI_GATED_RES) egate = *reinterpret_cast<const float2*>(p.gate + n_pair);
+        }
+        // The gated residual of a token chunk's 16 sites, all loaded before
+        // any store (one memory latency per chunk, not one per token).
+        auto load_res = [&](int c, uint32_t (&res)[16]) {
+          if constexpr (EPI == EPI_GATED_RES) {
+            if (!PAIR && p.splits > 1) return;   // the cluster reduction adds it
+            const int j0 = mt * TN + c * 32;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int j = j0 + 2 * k + odd;
+              res[k] = (j < p.M && n_pair < p.N)
+                           ? *reinterpret_cast<const uint32_t*>(out_row<EPI>(p, j) + n_pair)
+                           : 0u;
+            }
+          }
+        };
+        // On two-block pairs (no second accumulator set to hide the drain
+        // behind) the first chunk's residual is fetched while the
+        // accumulator fills, so nothing but the TMEM loads stands between
+        // the accumulator becoming full and its release (elsewhere the
+        // registers it holds over the wait would spill).
+        constexpr bool kPrefetch = EPI == EPI_GATED_RES && PAIR && WB == 2;
+        uint32_t res0[16];
+        if constexpr (kPrefetch) load_res(egrp, res0);
         if (!mbar_wait(&accfull[slot], accphase, s_abort, p.err,
                        KERR_WAIT_EPILOGUE))
           goto epi_done;
@@ -589,26 +631,9 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
           }
           continue;
         }
-        // Pair layout: lanes (2i, 2i+1) own features (n, n+1); the even lane
-        // writes even tokens, the odd lane odd tokens.
-        const int nrow = nt * kWT + (blk0 + g) * kBlk + rank * C::kBM + q * 32;
-        const int n_pair = nrow + (int)(lane & ~1u);
-        const int odd = (int)(lane & 1u);
-        float csx = 1.0f;
-        if constexpr (MODE == MODE_I8) {
-          const int nn = nrow + (int)lane;
-          csx = nn < p.N ? p.sw[nn] : 0.0f;
-        }
-        float2 ebias = make_float2(0.0f, 0.0f), egate = make_float2(0.0f, 0.0f);
-        if (n_pair < p.N) {
-          if (p.bias != nullptr) {
-            const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(p.bias + n_pair);
-            ebias = make_float2(__bfloat162float(bb.x), __bfloat162float(bb.y));
-          }
-          if constexpr (EPI == EPI_GATED_RES) egate = *reinterpret_cast<const float2*>(p.gate + n_pair);
-        }
         // One 32-column chunk of the accumulator, from registers to y.
-        auto emit = [&](const uint32_t (&v)[32], int c) {
+        // `pre`: std::true_type when rpre already holds the chunk's residual.
+        auto emit = [&](const uint32_t (&v)[32], int c, const uint32_t (&rpre)[16], auto pre) {
           float f[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -636,16 +661,13 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
             }
             return;
           }
-          // The residual of this chunk's 16 sites, all loaded before any
-          // store (one memory latency per chunk, not one per token).
           uint32_t res[16];
           if constexpr (EPI == EPI_GATED_RES) {
+            if constexpr (decltype(pre)::value) {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              const int j = j0 + 2 * k + odd;
-              res[k] = (j < p.M && n_pair < p.N)
-                           ? *reinterpret_cast<const uint32_t*>(out_row<EPI>(p, j) + n_pair)
-                           : 0u;
+              for (int k = 0; k < 16; ++k) res[k] = rpre[k];
+            } else {
+              load_res(c, res);
             }
           }
 #pragma unroll
@@ -695,7 +717,24 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
           tmem_wait_ld();
           release();
 #pragma unroll
-          for (int h = 0; h < kPer; ++h) emit(v[h], egrp + h * kEG);
+          for (int h = 0; h < kPer; ++h) emit(v[h], egrp + h * kEG, res0, std::false_type{});
+        } else if constexpr (kPrefetch) {
+          {
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + egrp * 32), v);
+            tmem_wait_ld();
+            if (kPer == 1) release();
+            emit(v, egrp, res0, std::true_type{});
+          }
+#pragma unroll 1
+          for (int h = 1; h < kPer; ++h) {
+            const int c = egrp + h * kEG;
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + c * 32), v);
+            tmem_wait_ld();
+            if (h == kPer - 1) release();
+            emit(v, c, res0, std::false_type{});
+          }
         } else {
 #pragma unroll 1
           for (int h = 0; h < kPer; ++h) {
@@ -704,7 +743,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
             tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + c * 32), v);
             tmem_wait_ld();
             if (h == kPer - 1) release();
-            emit(v, c);
+            emit(v, c, res0, std::false_type{});
           }
         }
         if (te) {

@@ -45,7 +45,7 @@ const bool g_wb2_default = [] {
   return !(e != nullptr && e[0] == '1');
 }();
 
-Plan plan_gemm(int mode, int M, int N, int K, int sms, const PlanKnobs& kn)
+Plan plan_gemm(int mode, int M, int N, int K, int epi, int sms, const PlanKnobs& kn)
 {
   Plan p;
   const int kpb = mode == ltx::MODE_I8 ? 128 : 64;
@@ -58,6 +58,12 @@ Plan plan_gemm(int mode, int M, int N, int K, int sms, const PlanKnobs& kn)
   // cross-CTA hand-off of dequantized A slots), so opt-in there.
   p.pair = mode == ltx::MODE_BF16 && M >= 1024 && N % 256 == 0 &&
            ((M + 255) / 256) * (N / 256) >= sms / 2;
+  // ... except a gated residual over a short K: with at most 32 k-blocks a
+  // tile's main loop is not much longer than that epilogue (residual loads
+  // included), which single CTAs hide behind their second accumulator and
+  // a two-block pair cannot (a2v out, 8160 x 2048 -> 4096: 132-144 us single
+  // against 148-161 paired, same box, arms interleaved).
+  if (epi == ltx::EPI_GATED_RES && K <= 2048) p.pair = false;
   if (kn.pair >= 0) {
     p.pair = (mode == ltx::MODE_W8G64 || mode == ltx::MODE_BF16) && kn.pair != 0 &&
              M > 128 && N % 256 == 0;
@@ -267,7 +273,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   // An extension adds ceil(r / 64) K blocks after the main K.
   const int ext_k = (ext != nullptr) ? ext->r : 0;
   const int ext_kb = (ext_k + 63) / 64;
-  Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, _sms, _knobs);
+  Plan pl = plan_gemm(mode, M, N, K + 64 * ext_kb, epi, _sms, _knobs);
   if (scatter != nullptr) {
     // scattered rows are stored by the tile epilogue itself: one K split
     if (epi != ltx::EPI_STORE || scatter->dst == nullptr || scatter->rows <= 0 ||
