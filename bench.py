@@ -1540,8 +1540,8 @@ def run_cublas_ab(args):
     """The dense tcgen05 GEMM (gemm_tc_kernel<MODE_BF16>, the expand-once
     route's second half) against cuBLAS (torch.matmul, a library GEMM) on
     the six M=8160 sweep shapes with the same bf16 operands, arms
-    interleaved step by step so clocks and power fall on both alike.  The
-    comparison DESIGN's dense-GEMM figures quote."""
+    interleaved step by step so clocks and power fall on both alike: how
+    close the hand-written dense GEMM comes to the library one."""
     import numpy as np
     import torch
     import ltx25_b200 as L
@@ -1623,8 +1623,8 @@ def run_gemm_trace(args):
     the sweep, one uncontended long-K shape, and the video FFN-up shape on
     the fused route (single CTAs and CTA pairs).  Prints per-CTA medians:
     phase stamps from entry, and per-k-block cycles of the MMA issuer's span
-    and of each role's waits.  L2 flushed before every traced call.  The
-    evidence behind the small-M and fused-kernel analysis in DESIGN."""
+    and of each role's waits.  L2 flushed before every traced call: where
+    the small-M and fused kernels spend their cycles."""
     import numpy as np
     import torch
     import ltx25_b200 as L
