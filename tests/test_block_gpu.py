@@ -194,6 +194,52 @@ def test_block_real_widths(ctx):
     blk.close()
 
 
+@pytest.mark.parametrize("grid", [(4, 12, 22), (4, 16, 24)])
+def test_block_long_video_vt_out(ctx, grid):
+    """A video long enough (1056 tokens: the fused w8g64 projections; 1536:
+    the expand-once route) that the self-attention's and the v2a attention's
+    V^T come straight from the K/V projection's epilogue: the oracle's bars,
+    and the same bits as a context that runs the V^T copy kernel instead
+    (LTX25_VT_OUT=0), both without K splits (the V^T output form has none; the
+    planner would split some of these GEMMs otherwise)."""
+    import os
+    import torch
+    import ltx25_b200 as L
+    cfg = dict(vdim=256, vheads=2, adim=128, aheads=2, vt=grid[0] * grid[1] * grid[2], at=7,
+               tt=5)
+    blk, ow, ins = build(ctx, cfg, seed=31, grid=grid)
+    res = run_and_compare(blk, ow, ins, cfg, "joint")
+    print(res)
+    ctx.set_tile_plan(splits=1)
+    try:
+        dv, da = to_dev(ins["video"]), to_dev(ins["audio"])
+        blk.forward(dv, da)
+        torch.cuda.synchronize()
+        fused = (host(dv["x"]), host(da["x"]))
+    finally:
+        ctx.set_tile_plan()
+    blk.close()
+    old = os.environ.get("LTX25_VT_OUT")
+    os.environ["LTX25_VT_OUT"] = "0"
+    c2 = L.Context(0)
+    try:
+        blk2, _, _ = build(c2, cfg, seed=31, grid=grid)
+        c2.set_tile_plan(splits=1)
+        dv, da = to_dev(ins["video"]), to_dev(ins["audio"])
+        blk2.forward(dv, da)
+        torch.cuda.synchronize()
+        c2.check()
+        assert np.array_equal(host(dv["x"]), fused[0])
+        assert np.array_equal(host(da["x"]), fused[1])
+        blk2.close()
+    finally:
+        c2.close()
+        if old is None:
+            os.environ.pop("LTX25_VT_OUT", None)
+        else:
+            os.environ["LTX25_VT_OUT"] = old
+
+
 def test_block_is_not_vacuous(ctx):
     """Negative control: perturb one adaLN table on the GPU side only and the
     comparison must fail."""

@@ -1398,7 +1398,7 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
                         size_t vt_elems, __nv_bfloat16* o, int ldo,
                         const __nv_bfloat16* gate, int ldg, int tq, int tk, int heads,
                         int head_dim, int* err, cudaStream_t s, float* part,
-                        size_t part_elems)
+                        size_t part_elems, bool vt_ready)
 {
   if (tq <= 0 || tk <= 0 || heads <= 0) return 0;
   if (head_dim != 128 && head_dim != 64) return -2;
@@ -1409,7 +1409,14 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
   const int D = head_dim;
   const int cols = heads * D;
   CUtensorMap tq_map, tk_map, tv_map;
-  if (prepare_vt(v, ldv, tk, cols, D, vt, &tv_map, s) != 0) return -1;
+  if (vt_ready) {
+    // V^T written by its producer ([cols][ldvt], keys contiguous)
+    const uint64_t ldvt = ((uint64_t)tk + 7) / 8 * 8;
+    if (!aligned16(vt) || !fa_encode(&tv_map, vt, (uint64_t)tk, (uint64_t)cols, ldvt * 2, 64, D))
+      return -1;
+  } else if (prepare_vt(v, ldv, tk, cols, D, vt, &tv_map, s) != 0) {
+    return -1;
+  }
   if (!fa_encode(&tq_map, q, (uint64_t)cols, (uint64_t)tq, (uint64_t)ldq * 2, 64, kFaBQ) ||
       !fa_encode(&tk_map, k, (uint64_t)cols, (uint64_t)tk, (uint64_t)ldk * 2, 64, kFaBK))
     return -1;

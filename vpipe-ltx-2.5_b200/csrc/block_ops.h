@@ -105,7 +105,7 @@ int launch_attention_tc(const __nv_bfloat16* q, int ldq, const __nv_bfloat16* k,
                         size_t vt_elems, __nv_bfloat16* o, int ldo,
                         const __nv_bfloat16* gate, int ldg, int tq, int tk, int heads,
                         int head_dim, int* err, cudaStream_t s, float* part = nullptr,
-                        size_t part_elems = 0);
+                        size_t part_elems = 0, bool vt_ready = false);
 
 // The sage tier (int8 QK^T, one scale per 128-token block, K smoothed by
 // its per-channel mean; P V in bf16): scratch sizes in elements and the

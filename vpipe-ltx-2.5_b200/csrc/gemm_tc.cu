@@ -70,9 +70,10 @@ __device__ __forceinline__ int kb_at(const GemmParams& p, int i, int n_tile, int
 template <int EPI>
 __device__ __forceinline__ __nv_bfloat16* out_row(const GemmParams& p, int j)
 {
-  if (EPI == EPI_STORE && p.scatter_rows > 0) {
-    const int o = j / p.scatter_rows;
-    return p.ys[o] + ((size_t)p.scatter_slot * p.scatter_rows + (j - o * p.scatter_rows)) * p.ldy;
+  if (EPI == EPI_STORE && p.scatter > 0) {
+    const int rows = scatter_rows(p);
+    const int o = j / rows;
+    return p.ys[o] + ((size_t)scatter_slot(p) * rows + (j - o * rows)) * p.ldy;
   }
   return p.y + (size_t)j * p.ldy;
 }
@@ -690,6 +691,35 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
             }
           }
         };
+        // V^T: this lane's feature over a chunk's 32 tokens, 64 contiguous
+        // bytes (the warp's 32 features all lie at or past vt_col0, a
+        // multiple of 32).
+        auto emit_vt = [&](const uint32_t (&v)[32], int c) {
+          const int n = nrow + (int)lane;
+          const int j0 = mt * TN + c * 32;
+          if (n >= p.N) return;
+          const float bn = p.bias != nullptr ? __bfloat162float(p.bias[n]) : 0.0f;
+          __nv_bfloat16* dst = p.vt + (size_t)(n - vt_col0(p)) * vt_ld(p) + j0;
+          if (j0 + 32 <= p.M) {
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(
+                    __uint_as_float(v[8 * q4 + 2 * e]) + bn, __uint_as_float(v[8 * q4 + 2 * e + 1]) + bn);
+                w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+              *reinterpret_cast<uint4*>(dst + 8 * q4) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (j0 + i < p.M) dst[i] = __float2bfloat16_rn(__uint_as_float(v[i]) + bn);
+          }
+        };
+        constexpr bool kVt = EPI == EPI_STORE && MODE != MODE_I8;
+        const bool vt_warp = kVt && p.vt_spec != 0 && nrow >= vt_col0(p);
         auto release = [&]() {
           tc_fence_before();
           __syncwarp();
@@ -709,7 +739,18 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
         // where the held chunks fit the register budget without spilling
         // (not beside a gated residual's loads or the int8 rescale).
         constexpr bool kHold = kPer <= 2 && MODE == MODE_BF16 && EPI != EPI_GATED_RES;
-        if constexpr (kHold) {
+        if (kHold && vt_warp) {
+          // V^T warps stream their chunks (light stores, no exchange)
+#pragma unroll 1
+          for (int h = 0; h < kPer; ++h) {
+            const int c = egrp + h * kEG;
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + c * 32), v);
+            tmem_wait_ld();
+            if (h == kPer - 1) release();
+            emit_vt(v, c);
+          }
+        } else if constexpr (kHold) {
           uint32_t v[kPer][32];
 #pragma unroll
           for (int h = 0; h < kPer; ++h)
@@ -743,7 +784,11 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
             tmem_ld32(tmem + lane_base + (uint32_t)(slot * TN + c * 32), v);
             tmem_wait_ld();
             if (h == kPer - 1) release();
-            emit(v, c, res0, std::false_type{});
+            if (vt_warp) {
+              emit_vt(v, c);
+            } else {
+              emit(v, c, res0, std::false_type{});
+            }
           }
         }
         if (te) {
@@ -760,7 +805,7 @@ __global__ void __launch_bounds__(GemmCfg<MODE, TN, PAIR, WB>::kThreads, 1)
   epi_done:
     // scattered rows may sit in another GPU's memory: make them visible
     // there before the kernel's completion is
-    if (EPI == EPI_STORE && p.scatter_rows > 0) __threadfence_system();
+    if (EPI == EPI_STORE && p.scatter > 0) __threadfence_system();
     if (te) {
       tr[TR_EPI_WAIT] = e_wait;
       tr[TR_EPI_WORK] = e_work;

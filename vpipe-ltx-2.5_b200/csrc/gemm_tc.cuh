@@ -88,7 +88,13 @@ struct GemmParams {
     __nv_bfloat16* const* ys;       // row scatter: see scatter_rows
   };
   const float* sx;             // MODE_I8: [M] token scales
-  const float* sw;             // MODE_I8: [N] channel scales
+  union {
+    const float* sw;             // MODE_I8: [N] channel scales
+    // The other modes, EPI_STORE, one K split: columns n >= vt_col0 are
+    // written TRANSPOSED, vt[(n - vt_col0) * ldvt + j] (an attention's V^T,
+    // keys contiguous), and not to y; null = off.  vt_col0 % 32 == 0.
+    __nv_bfloat16* vt;
+  };
   int* err;                    // device error word (0 = ok)
   int group_m;                 // raster: token tiles per weight sweep (0 = 8)
   int krot;                    // 1: rotate each tile's K start (one token tile)
@@ -98,14 +104,24 @@ struct GemmParams {
   unsigned long long* trace;
   int trace_ctas;
   // Row scatter (the fused tensor-parallel reduce-scatter), EPI_STORE, one
-  // K split: when scatter_rows > 0, token row j is stored at
-  // ys[j / scatter_rows] + (scatter_slot * scatter_rows + j % scatter_rows) * ldy
-  // instead of y + j * ldy -- the receive slot of the rank that owns row j,
-  // which may be another GPU's memory mapped into this one (plain stores over
-  // NVLink), followed by a system-scope fence before the kernel ends.  `ys`
-  // (a device array of the owners' buffers) takes the place of y.
-  int scatter_rows, scatter_slot;
+  // K split, packed as rows * 8 + slot (0 = off; slot < 8): token row j is
+  // stored at ys[j / rows] + (slot * rows + j % rows) * ldy instead of
+  // y + j * ldy -- the receive slot of the rank that owns row j, which may be
+  // another GPU's memory mapped into this one (plain stores over NVLink),
+  // followed by a system-scope fence before the kernel ends.  `ys` (a device
+  // array of the owners' buffers) takes the place of y.
+  int scatter;
+  // Transposed columns (see vt), packed as (vt_col0 / 32) << 20 | ldvt / 8
+  // (0 = off).  Both switches fit the 8 bytes added to this block: a larger
+  // parameter block made ptxas spill in the gated-residual variants, which
+  // use neither.
+  int vt_spec;
 };
+
+__host__ __device__ inline int scatter_rows(const GemmParams& p) { return p.scatter >> 3; }
+__host__ __device__ inline int scatter_slot(const GemmParams& p) { return p.scatter & 7; }
+__host__ __device__ inline int vt_col0(const GemmParams& p) { return (p.vt_spec >> 20) * 32; }
+__host__ __device__ inline int vt_ld(const GemmParams& p) { return (p.vt_spec & 0xFFFFF) * 8; }
 
 constexpr int kTraceSlots = 24;
 enum TraceSlot : int {

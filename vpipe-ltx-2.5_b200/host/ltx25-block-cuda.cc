@@ -633,9 +633,25 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
   const __nv_bfloat16 *qraw, *kraw, *vraw;
   int ldq, ldkv;
   LoraExt lx;
+  // Long key sequences (the video keys: 8160) whose attention reads V^T (the
+  // tcgen05 path) take V^T straight from the K/V projection's epilogue, which
+  // writes those columns transposed into the attention's scratch instead of
+  // next to K; the V^T copy kernel then does not run.  Shorter K/V
+  // projections (the text's 256 tokens) run K-split GEMMs, which that
+  // output form excludes.
+  VtOut vo;
+  const VtOut* vop = nullptr;
+  if (tkv >= 1024 && _ops->attention_reads_vt(s, tq, tkv, a.heads, a.head_dim, _layer) &&
+      !_ops->i8_takes(a.self ? tq : tkv, a.self ? a.qdim : a.kvdim, a.self ? 3 * I : 2 * I)) {
+    vo.vt = _ops->vt_scratch(tkv, I, err);
+    if (vo.vt == nullptr) return false;
+    vo.col0 = a.self ? 2 * I : I;
+    vo.ld = (tkv + 7) / 8 * 8;
+    vop = &vo;
+  }
   if (a.self) {
     if (!_ops->linear(s, xq, a.qdim, a.qkv, a.qkv_b, _cur->qkv, 3 * I, tq, a.qdim,
-                      3 * I, ltx::EPI_STORE, nullptr, err, lx_(a.l_qkv, &lx)))
+                      3 * I, ltx::EPI_STORE, nullptr, err, lx_(a.l_qkv, &lx), nullptr, vop))
       return false;
     qraw = _cur->qkv;
     kraw = _cur->qkv + I;
@@ -645,7 +661,8 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     if (!_ops->linear(s, xq, a.qdim, a.q, a.qkv_b, _cur->qkv, I, tq, a.qdim, I,
                       ltx::EPI_STORE, nullptr, err, lx_(a.l_q, &lx)) ||
         !_ops->linear(s, xkv, a.kvdim, a.kv, a.kv_b, _cur->kvp, 2 * I, tkv,
-                      a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err, lx_(a.l_kv, &lx)))
+                      a.kvdim, 2 * I, ltx::EPI_STORE, nullptr, err, lx_(a.l_kv, &lx), nullptr,
+                      vop))
       return false;
     qraw = _cur->qkv;
     kraw = _cur->kvp;
@@ -679,7 +696,7 @@ bool CudaBlock::attend_(cudaStream_t s, const CudaAttn& a,
     glog = _cur->glog;
   }
   if (!_ops->attention(s, _cur->qn, I, _cur->kn, I, vraw, ldkv, out, I, glog, a.heads, tq,
-                       tkv, a.heads, a.head_dim, err, _layer))
+                       tkv, a.heads, a.head_dim, err, _layer, vop != nullptr ? vo.vt : nullptr))
     return false;
   return true;
 }

@@ -151,6 +151,9 @@ bool CudaOps::init(int device, std::string* err)
   // and, on the side stream beside the video GEMMs, 5 % slower a block.
   if (const char* e = std::getenv("LTX25_ATTN")) _attn_mode = std::strcmp(e, "mma") == 0 ? 0 : 1;
   if (const char* e = std::getenv("LTX25_ATTN64")) _attn64_tc = std::strcmp(e, "tc") == 0;
+  // V^T from the K/V projection's epilogue (on by default; LTX25_VT_OUT=0
+  // keeps the V^T copy kernel)
+  if (const char* e = std::getenv("LTX25_VT_OUT")) _vt_out = e[0] != '0';
 
   int n = 0;
   if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount", err)) return false;
@@ -268,7 +271,7 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
                     const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy,
                     int M, int K, int N, int epi, const float* gate,
                     const float* sx, const float* sw, std::string* err,
-                    const LoraExt* ext, const RowScatter* scatter)
+                    const LoraExt* ext, const RowScatter* scatter, const VtOut* vto)
 {
   // An extension adds ceil(r / 64) K blocks after the main K.
   const int ext_k = (ext != nullptr) ? ext->r : 0;
@@ -279,6 +282,16 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
     if (epi != ltx::EPI_STORE || scatter->dst == nullptr || scatter->rows <= 0 ||
         scatter->slot < 0 || (M + scatter->rows - 1) / scatter->rows > scatter->owners) {
       if (err) *err = "row scatter: store epilogue, an owner for every row";
+      return false;
+    }
+    pl.splits = 1;
+  }
+  if (vto != nullptr) {
+    // transposed columns are stored by the tile epilogue itself: one K split
+    if (mode == ltx::MODE_I8 || epi != ltx::EPI_STORE || scatter != nullptr ||
+        vto->vt == nullptr || !aligned(vto->vt, 16) || vto->col0 < 0 || vto->col0 % 32 != 0 ||
+        vto->col0 / 32 >= 2048 || vto->ld <= 0 || vto->ld % 8 != 0 || vto->ld / 8 >= (1 << 20)) {
+      if (err) *err = "V^T output: store epilogue, no int8 tier, col0 % 32, ld % 8, aligned";
       return false;
     }
     pl.splits = 1;
@@ -321,8 +334,11 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.trace_ctas = _trace_ctas;
   if (scatter != nullptr) {
     p.ys = scatter->dst;
-    p.scatter_rows = scatter->rows;
-    p.scatter_slot = scatter->slot;
+    p.scatter = scatter->rows * 8 + scatter->slot;
+  }
+  if (vto != nullptr) {
+    p.vt = vto->vt;
+    p.vt_spec = ((vto->col0 / 32) << 20) | (vto->ld / 8);
   }
   const int rc = ltx::gemm_launch(L, s);
   if (rc != 0) {
@@ -338,7 +354,7 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
                      const QWeight& w, const __nv_bfloat16* bias,
                      __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
                      const float* gate, std::string* err, const LoraExt* lora,
-                     const RowScatter* sc)
+                     const RowScatter* sc, const VtOut* vto)
 {
   if (x == nullptr || y == nullptr) {
     if (err) *err = "linear: null x or y";
@@ -386,13 +402,17 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
       wb = _deq;
     }
     return gemm_(s, ltx::MODE_BF16, x, ldx, wb, nullptr, bias, y, ldy, M, K, N, epi, gate,
-                 nullptr, nullptr, err, lora, sc);
+                 nullptr, nullptr, err, lora, sc, vto);
   }
   if (!w.quantized) {
     return gemm_(s, ltx::MODE_BF16, x, ldx, w.w, nullptr, bias, y, ldy, M, K,
-                 N, epi, gate, nullptr, nullptr, err, nullptr, sc);
+                 N, epi, gate, nullptr, nullptr, err, nullptr, sc, vto);
   }
   if (i8_takes(M, K, N)) {
+    if (vto != nullptr) {
+      if (err) *err = "linear: V^T output is not on the int8 tier";
+      return false;
+    }
     if (!prepare_i8(const_cast<QWeight&>(w), s, err)) return false;
     if (!ensure_((size_t)M * K, 0, err)) return false;
     if (ltx::launch_quant_rows_i8(x, M, K, ldx, K, _xq, _sx, s) != 0) {
@@ -409,10 +429,10 @@ bool CudaOps::linear(cudaStream_t s, const __nv_bfloat16* x, int ldx,
       return false;
     }
     return gemm_(s, ltx::MODE_BF16, x, ldx, _deq, nullptr, bias, y, ldy, M,
-                 K, N, epi, gate, nullptr, nullptr, err, nullptr, sc);
+                 K, N, epi, gate, nullptr, nullptr, err, nullptr, sc, vto);
   }
   return gemm_(s, ltx::MODE_W8G64, x, ldx, w.codes, w.sz, bias, y, ldy, M, K,
-               N, epi, gate, nullptr, nullptr, err, nullptr, sc);
+               N, epi, gate, nullptr, nullptr, err, nullptr, sc, vto);
 }
 
 __nv_bfloat16* CudaOps::lora_rbuf(size_t elems, std::string* err)
@@ -733,11 +753,25 @@ bool CudaOps::reserve_split(int tq, int tk, int heads, int head_dim, std::string
   return true;
 }
 
+bool CudaOps::attention_reads_vt(cudaStream_t s, int tq, int tk, int heads, int head_dim,
+                                 int layer) const
+{
+  const bool on_side = _aux != nullptr && s == _aux;
+  const int splits = ltx::attention_tc_splits(tq, tk, heads);
+  return _vt_out && !on_side && _attn_mode == 1 && !sage_for(layer, head_dim) &&
+         (head_dim == 128 || (head_dim == 64 && (splits > 1 || _attn64_tc)));
+}
+
+__nv_bfloat16* CudaOps::vt_scratch(int tk, int width, std::string* err)
+{
+  return reserve_attention(tk, width, err) ? _vt : nullptr;
+}
+
 bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
                         const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v,
                         int ldv, __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate,
                         int ldg, int tq, int tk, int heads, int head_dim,
-                        std::string* err, int layer)
+                        std::string* err, int layer, const __nv_bfloat16* vt_ready)
 {
   int rc;
   const bool on_side = _aux != nullptr && s == _aux;
@@ -747,7 +781,13 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
   // the main stream's partials scratch
   const bool tc = _attn_mode == 1 && !(on_side && splits > 1) &&
                   (head_dim == 128 || (head_dim == 64 && (splits > 1 || _attn64_tc)));
-  if (sage_for(layer, head_dim)) {
+  const bool sage = sage_for(layer, head_dim);
+  if (vt_ready != nullptr && (sage || !tc || on_side)) {
+    // the producer left V out of its buffer: only the path that reads V^T may run
+    if (err) *err = "attention: a ready V^T was given to a path that reads V";
+    return false;
+  }
+  if (sage) {
     if (!reserve_sage(tq, tk, heads, head_dim, err)) return false;
     rc = ltx::launch_sage_tc(q, ldq, k, ldk, v, ldv, _sb, o, ldo, gate, ldg, tq, tk, heads,
                              head_dim, _err_word, s);
@@ -765,12 +805,13 @@ bool CudaOps::attention(cudaStream_t s, const __nv_bfloat16* q, int ldq,
     } else {
       if (!reserve_attention(tk, heads * head_dim, err)) return false;
       if (!reserve_split(tq, tk, heads, head_dim, err)) return false;
-      vt = _vt;
-      vt_elems = _vt_elems;
+      vt = vt_ready != nullptr ? const_cast<__nv_bfloat16*>(vt_ready) : _vt;
+      vt_elems = vt_ready != nullptr ? ltx::attention_tc_scratch(tk, heads, head_dim) : _vt_elems;
     }
     rc = ltx::launch_attention_tc(q, ldq, k, ldk, v, ldv, vt, vt_elems, o, ldo, gate, ldg,
                                   tq, tk, heads, head_dim, _err_word, s,
-                                  side ? nullptr : _part, side ? 0 : _part_elems);
+                                  side ? nullptr : _part, side ? 0 : _part_elems,
+                                  vt_ready != nullptr);
   } else {
     rc = ltx::launch_attention(q, ldq, k, ldk, v, ldv, o, ldo, gate, ldg, tq, tk, heads,
                                head_dim, s);

@@ -60,6 +60,15 @@ struct RowScatter {
   int slot = 0;    // this rank's slot in every owner's buffer
 };
 
+// A linear's columns [col0, N) written TRANSPOSED, vt[(n - col0) * ld + j]
+// (an attention's V^T, keys contiguous), instead of to y: col0 % 32 == 0,
+// ld % 8 == 0, vt 16-byte aligned; not on the int8 tier.
+struct VtOut {
+  __nv_bfloat16* vt = nullptr;
+  int col0 = 0;
+  int ld = 0;
+};
+
 // One module's uploaded adapter pair (src/ltx25-lora.h:48-56): a [r8][k]
 // with the scale folded in, b [n][r8], the rank padded to r8 (a multiple of
 // 8, so every row is 16-byte aligned for TMA) with zero rows / columns.
@@ -99,7 +108,7 @@ public:
               const QWeight& w, const __nv_bfloat16* bias, __nv_bfloat16* y,
               int ldy, int M, int K, int N, int epi,
               const float* gate, std::string* err, const LoraExt* lora = nullptr,
-              const RowScatter* scatter = nullptr);
+              const RowScatter* scatter = nullptr, const VtOut* vto = nullptr);
 
   // Ltx25Dit's patchify (src/ltx25-dit.cc:1509-1540): x[T][dim] =
   // latent . W^T + bias (+ adapter), then `prefix` [dim] added to rows
@@ -200,7 +209,15 @@ public:
                  const __nv_bfloat16* k, int ldk, const __nv_bfloat16* v, int ldv,
                  __nv_bfloat16* o, int ldo, const __nv_bfloat16* gate, int ldg,
                  int tq, int tk, int heads, int head_dim, std::string* err,
-                 int layer = -1);
+                 int layer = -1, const __nv_bfloat16* vt_ready = nullptr);
+  // Whether attention() with these arguments reads V through the main
+  // stream's V^T scratch (the tcgen05 path), so that a producer should
+  // write V^T there itself (vt_scratch, VtOut) and pass it as vt_ready;
+  // false under LTX25_VT_OUT=0.
+  bool attention_reads_vt(cudaStream_t s, int tq, int tk, int heads, int head_dim,
+                          int layer = -1) const;
+  // That scratch, grown to tk keys x width columns ([width][round8(tk)]).
+  __nv_bfloat16* vt_scratch(int tk, int width, std::string* err);
   // MetalOps::sage_takes (src/ltx25-metal-ops.cc:897-905): the widths the
   // int8 twin exists for, while the tier is on.
   bool sage_takes(int head_dim) const
@@ -243,7 +260,7 @@ private:
              __nv_bfloat16* y, int ldy, int M, int K, int N, int epi,
              const float* gate, const float* sx, const float* sw,
              std::string* err, const LoraExt* ext = nullptr,
-             const RowScatter* scatter = nullptr);
+             const RowScatter* scatter = nullptr, const VtOut* vto = nullptr);
   // f32 ones [n] (the gate of lora_add's accumulate), grown on demand
   const float* ones_(int n, cudaStream_t s, std::string* err);
 public:
@@ -290,6 +307,7 @@ private:
   ltx::SageBuffers _sb;            // sage tier: int8 Q/K, scales, key mean
   int _attn_mode = 1;              // LTX25_ATTN=mma: 0 = always warp-MMA
   bool _attn64_tc = false;         // 64-wide unsplit on tcgen05 (LTX25_ATTN64=tc), else warp-MMA
+  bool _vt_out = true;             // V^T from the K/V projection (LTX25_VT_OUT=0: copy kernel)
   int* _err_word = nullptr;
   std::unique_ptr<Comm> _comm;
   std::unique_ptr<Comm> _comm_side;
