@@ -37,7 +37,16 @@
 // A dense pair may also hold TWO weight blocks per CTA (WB = 2: 512 weight
 // rows x 256 tokens per pair, both accumulators filling all 512 TMEM
 // columns): each activation stage then feeds two MMAs, so an SM takes in
-// 48 KB per 2 x 128x256x64 MMA instead of 32 KB per one.
+// 48 KB per 2 x 128x256x64 MMA instead of 32 KB per one.  Without a second
+// accumulator set, the epilogue pulls its chunks out of TMEM and releases
+// the accumulator before storing (or, for the gated residual, prefetches
+// the first chunk's residual during the wait), and the tiles of a last,
+// partial wave run as half tiles of one weight block each.
+//
+// Besides y, the store epilogue has two output forms: a ROW SCATTER (each
+// token row to the receive slot of the tensor-parallel rank that owns it,
+// possibly another GPU's memory: the reduce-scatter fused into the GEMM)
+// and TRANSPOSED columns (an attention's V^T written by the K/V projection).
 //
 // K is split across CTAs (`splits` > 1, at most 8) for the small-M,
 // bandwidth-bound shapes.  The splits of one output tile are launched as
