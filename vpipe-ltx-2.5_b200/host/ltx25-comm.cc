@@ -93,8 +93,24 @@ Comm::~Comm()
 {
   release_buffers_();
   if (_table != nullptr) cudaFree(_table);
-  if (_token != nullptr) cudaFree(_token);
+  if (_token != nullptr) cudaFree(_token);   // _vote and _hbuf share its allocation
   if (_comm != nullptr && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(_comm));
+}
+
+bool Comm::alloc_words_()
+{
+  // the barrier word, the vote word and the [8][64] handle exchange in one
+  // allocation
+  void* p = nullptr;
+  if (cudaMalloc(&p, 256 + 8 * 64) != cudaSuccess) return false;
+  if (cudaMemset(p, 0, 256 + 8 * 64) != cudaSuccess) {
+    cudaFree(p);
+    return false;
+  }
+  _token = static_cast<float*>(p);
+  _vote = _token + 1;
+  _hbuf = static_cast<char*>(p) + 256;
+  return true;
 }
 
 void Comm::release_buffers_()
@@ -113,61 +129,72 @@ void Comm::release_buffers_()
 bool Comm::share_buffers(size_t bytes, cudaStream_t s, std::string* err)
 {
   if (_comm == nullptr || bytes <= _share_bytes) return true;
-  if (_world > 8) {
-    if (err) *err = "peer buffers: at most 8 ranks";
-    return false;
-  }
+  if (_world > 8) return true;   // unavailable: the NCCL reduce-scatter stays
   auto cuda = [&](cudaError_t e, const char* what) {
     if (e == cudaSuccess) return true;
     if (err) *err = std::string(what) + ": " + cudaGetErrorString(e);
     return false;
   };
+  const ncclComm_t c = static_cast<ncclComm_t>(_comm);
   // Everything issued before (the previous buffers' last readers and
   // writers on every rank) is done once this returns.
   if (_share_bytes > 0 && !(barrier(s, err) && cuda(cudaStreamSynchronize(s), "sync")))
     return false;
   release_buffers_();
   bytes = (bytes + 255) & ~size_t(255);
-  void* mine = nullptr;
-  cudaIpcMemHandle_t h;
-  if (!cuda(cudaMalloc(&mine, 2 * bytes), "cudaMalloc(peer buffers)")) return false;
-  _peer[_rank] = mine;
-  char* hall = nullptr;   // [world][64] handles, all-gathered
+  // Every rank takes both collectives below whatever happens locally, so
+  // that a rank whose allocation or mapping fails cannot leave the others
+  // waiting: a failed rank publishes an empty handle, and the ranks then
+  // agree (a sum of failures) to use the buffers or none.
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
-  bool ok = cuda(cudaIpcGetMemHandle(&h, mine), "cudaIpcGetMemHandle") &&
-            cuda(cudaMalloc(&hall, (size_t)_world * 64), "cudaMalloc(handles)") &&
-            cuda(cudaMemcpyAsync(hall + (size_t)_rank * 64, &h, 64, cudaMemcpyHostToDevice, s),
-                 "handle upload") &&
-            nccl_ok(nccl().all_gather(hall + (size_t)_rank * 64, hall, 64, ncclInt8,
-                                      static_cast<ncclComm_t>(_comm), s),
-                    "ncclAllGather(handles)", err);
+  cudaIpcMemHandle_t h;
+  memset(&h, 0, sizeof h);
+  void* mine = nullptr;
+  bool local_ok = cudaMalloc(&mine, 2 * bytes) == cudaSuccess;
+  if (local_ok) _peer[_rank] = mine;
+  local_ok = local_ok && cudaIpcGetMemHandle(&h, mine) == cudaSuccess;
+  if (!local_ok) memset(&h, 0, sizeof h);
   std::vector<char> host((size_t)_world * 64);
-  ok = ok && cuda(cudaMemcpyAsync(host.data(), hall, host.size(), cudaMemcpyDeviceToHost, s),
-                  "handle download") &&
-       cuda(cudaStreamSynchronize(s), "sync");
-  if (hall != nullptr) cudaFree(hall);
-  for (int r = 0; ok && r < _world; ++r) {
+  if (!(cuda(cudaMemcpy(_hbuf + (size_t)_rank * 64, &h, 64, cudaMemcpyHostToDevice),
+             "handle upload") &&
+        nccl_ok(nccl().all_gather(_hbuf + (size_t)_rank * 64, _hbuf, 64, ncclInt8, c, s),
+                "ncclAllGather(handles)", err) &&
+        cuda(cudaStreamSynchronize(s), "sync") &&
+        cuda(cudaMemcpy(host.data(), _hbuf, host.size(), cudaMemcpyDeviceToHost),
+             "handle download"))) {
+    release_buffers_();
+    return false;
+  }
+  for (int r = 0; local_ok && r < _world; ++r) {
     if (r == _rank) continue;
     cudaIpcMemHandle_t hr;
     memcpy(&hr, host.data() + (size_t)r * 64, 64);
-    ok = cuda(cudaIpcOpenMemHandle(&_peer[r], hr, cudaIpcMemLazyEnablePeerAccess),
-              "cudaIpcOpenMemHandle");
+    local_ok = cudaIpcOpenMemHandle(&_peer[r], hr, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    if (!local_ok) _peer[r] = nullptr;
   }
-  if (!ok) {
+  __nv_bfloat16* tbl[16] = {};
+  for (int w = 0; local_ok && w < 2; ++w)
+    for (int r = 0; r < _world; ++r)
+      tbl[w * 8 + r] = static_cast<__nv_bfloat16*>(_peer[r]) + (size_t)w * (bytes / 2);
+  local_ok = local_ok && (_table != nullptr || cudaMalloc(&_table, sizeof tbl) == cudaSuccess) &&
+             cudaMemcpy(_table, tbl, sizeof tbl, cudaMemcpyHostToDevice) == cudaSuccess;
+  cudaGetLastError();   // a failed IPC call above is this rank's vote, not an error
+  float fails = local_ok ? 0.0f : 1.0f;
+  if (!(cuda(cudaMemcpy(_vote, &fails, sizeof fails, cudaMemcpyHostToDevice), "vote upload") &&
+        nccl_ok(nccl().all_reduce(_vote, _vote, 1, ncclFloat32, ncclSum, c, s),
+                "ncclAllReduce(vote)", err) &&
+        cuda(cudaStreamSynchronize(s), "sync") &&
+        cuda(cudaMemcpy(&fails, _vote, sizeof fails, cudaMemcpyDeviceToHost), "vote download"))) {
     release_buffers_();
     return false;
+  }
+  if (fails > 0.0f) {
+    // some rank cannot map its peers (no peer access on this node): every
+    // rank drops the buffers and keeps the NCCL reduce-scatter
+    release_buffers_();
+    return true;
   }
   _share_bytes = bytes;
-  __nv_bfloat16* tbl[16] = {};
-  for (int w = 0; w < 2; ++w)
-    for (int r = 0; r < _world; ++r)
-      tbl[w * 8 + r] = static_cast<__nv_bfloat16*>(peer_buffer(r, w));
-  if ((_table == nullptr &&
-       !cuda(cudaMalloc(&_table, sizeof tbl), "cudaMalloc(peer table)")) ||
-      !cuda(cudaMemcpy(_table, tbl, sizeof tbl, cudaMemcpyHostToDevice), "peer table upload")) {
-    release_buffers_();
-    return false;
-  }
   return true;
 }
 
@@ -202,9 +229,8 @@ bool Comm::init(int device, int rank, int world, const void* id, std::string* er
   _rank = rank;
   _world = world;
   _device = device;
-  if (cudaMalloc(&_token, sizeof(float)) != cudaSuccess ||
-      cudaMemset(_token, 0, sizeof(float)) != cudaSuccess) {
-    if (err) *err = "tp: cudaMalloc(barrier word) failed";
+  if (!alloc_words_()) {
+    if (err) *err = "tp: cudaMalloc(communicator words) failed";
     return false;
   }
   return true;
@@ -235,9 +261,8 @@ bool Comm::split(Comm* out, std::string* err) const
   out->_rank = _rank;
   out->_world = _world;
   out->_device = _device;
-  if (cudaMalloc(&out->_token, sizeof(float)) != cudaSuccess ||
-      cudaMemset(out->_token, 0, sizeof(float)) != cudaSuccess) {
-    if (err) *err = "comm split: cudaMalloc(barrier word) failed";
+  if (!out->alloc_words_()) {
+    if (err) *err = "comm split: cudaMalloc(communicator words) failed";
     return false;
   }
   return true;

@@ -50,7 +50,10 @@ public:
   // allocates two buffers of `bytes` and maps every other rank's through
   // CUDA IPC, so a kernel here can store into any rank's buffers over
   // NVLink.  Collective (every rank, same bytes, same order); a no-op when
-  // the buffers are already that large.  Up to 8 ranks.
+  // the buffers are already that large.  When any rank cannot allocate or
+  // map them (no peer access, more than 8 ranks) every rank ends without
+  // buffers (shared_bytes() == 0) and true; false only when the
+  // communicator itself fails.
   bool share_buffers(size_t bytes, cudaStream_t s, std::string* err);
   size_t shared_bytes() const { return _share_bytes; }
   // Which of the two buffers the next fused reduce-scatter uses: they
@@ -73,12 +76,15 @@ public:
 
 private:
   void release_buffers_();
+  bool alloc_words_();
 
   void* _comm = nullptr;
   int _rank = 0, _world = 1, _device = -1;
   void* _peer[8] = {};            // [rank]: this rank's own at _peer[_rank]
   size_t _share_bytes = 0;        // bytes of one of the two buffers
   float* _token = nullptr;        // the barrier's 4 bytes
+  float* _vote = nullptr;         // share_buffers' agreement word
+  char* _hbuf = nullptr;          // share_buffers' [8][64] IPC handle exchange
   __nv_bfloat16** _table = nullptr;   // device [2][8]: every rank's buffers
   mutable int _flip = 1;          // the buffer of the last fused reduce-scatter
 };
