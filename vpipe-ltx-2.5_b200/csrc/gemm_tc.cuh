@@ -127,6 +127,10 @@ struct GemmParams {
   int vt_spec;
 };
 
+// The packed switches: rows < 2^28 and slot < 8; col0 % 32 == 0 and
+// col0 < 65536, ld % 8 == 0 and ld < 2^23 (the host checks the ranges).
+__host__ __device__ inline int pack_scatter(int rows, int slot) { return rows * 8 + slot; }
+__host__ __device__ inline int pack_vt(int col0, int ld) { return ((col0 / 32) << 20) | (ld / 8); }
 __host__ __device__ inline int scatter_rows(const GemmParams& p) { return p.scatter >> 3; }
 __host__ __device__ inline int scatter_slot(const GemmParams& p) { return p.scatter & 7; }
 __host__ __device__ inline int vt_col0(const GemmParams& p) { return (p.vt_spec >> 20) * 32; }

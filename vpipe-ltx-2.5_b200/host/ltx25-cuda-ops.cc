@@ -280,7 +280,8 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   if (scatter != nullptr) {
     // scattered rows are stored by the tile epilogue itself: one K split
     if (epi != ltx::EPI_STORE || scatter->dst == nullptr || scatter->rows <= 0 ||
-        scatter->slot < 0 || (M + scatter->rows - 1) / scatter->rows > scatter->owners) {
+        scatter->rows >= (1 << 28) || scatter->slot < 0 || scatter->slot >= 8 ||
+        (M + scatter->rows - 1) / scatter->rows > scatter->owners) {
       if (err) *err = "row scatter: store epilogue, an owner for every row";
       return false;
     }
@@ -334,11 +335,11 @@ bool CudaOps::gemm_(cudaStream_t s, int mode, const void* x, int ldx,
   p.trace_ctas = _trace_ctas;
   if (scatter != nullptr) {
     p.ys = scatter->dst;
-    p.scatter = scatter->rows * 8 + scatter->slot;
+    p.scatter = ltx::pack_scatter(scatter->rows, scatter->slot);
   }
   if (vto != nullptr) {
     p.vt = vto->vt;
-    p.vt_spec = ((vto->col0 / 32) << 20) | (vto->ld / 8);
+    p.vt_spec = ltx::pack_vt(vto->col0, vto->ld);
   }
   const int rc = ltx::gemm_launch(L, s);
   if (rc != 0) {
